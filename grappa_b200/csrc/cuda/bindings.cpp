@@ -1,0 +1,518 @@
+// torch bindings of the sm_100a kernels (module grappa_b200._cuda).  Every entry
+// point checks device, dtype and contiguity and launches on the current stream.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <optional>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "peer.h"
+
+namespace d = grappa::dev;
+using at::Tensor;
+using OptT = std::optional<Tensor>;
+
+namespace {
+
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void check_cuda(const Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+}
+
+template <typename T>
+T* ptr(const Tensor& t, at::ScalarType st, const char* name) {
+  check_cuda(t, name);
+  TORCH_CHECK(t.scalar_type() == st, name, " has dtype ", t.scalar_type(), ", expected ", st);
+  return reinterpret_cast<T*>(t.data_ptr());
+}
+
+template <typename T>
+T* optr(const OptT& t, at::ScalarType st, const char* name) {
+  if (!t.has_value() || !t->defined()) return nullptr;
+  return ptr<T>(*t, st, name);
+}
+
+// 2-D operand whose rows may be strided (row stride = stride(0)) but whose
+// columns are contiguous
+template <typename T>
+T* ptr2d(const Tensor& t, at::ScalarType st, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.dim() == 2 && t.stride(1) == 1, name, " must be 2-D with contiguous rows");
+  TORCH_CHECK(t.scalar_type() == st, name, " has dtype ", t.scalar_type(), ", expected ", st);
+  return reinterpret_cast<T*>(t.data_ptr());
+}
+
+int num_sms() {
+  static int n = 0;
+  if (!n) n = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
+  return n;
+}
+
+// --------------------------------------------------------------------------- S1 / S2
+void sample_hop(Tensor indptr, Tensor indices, Tensor dst_nid, OptT n_dst_dev, int64_t n_dst, OptT frontier,
+                int64_t fanout, bool replace, Tensor counters, int64_t hop, OptT gideg, OptT cov_accum,
+                Tensor out_indptr, Tensor out_nbr, Tensor n_edges_out, Tensor scan_scratch, Tensor err,
+                int64_t cap_dst) {
+  c10::cuda::CUDAGuard g(indptr.device());
+  d::SampleHopArgs a;
+  a.indptr = ptr<int64_t>(indptr, at::kLong, "indptr");
+  a.indices = ptr<int32_t>(indices, at::kInt, "indices");
+  a.n_graph_nodes = indptr.numel() - 1;
+  a.dst_nid = ptr<int32_t>(dst_nid, at::kInt, "dst_nid");
+  a.n_dst_ptr = optr<int32_t>(n_dst_dev, at::kInt, "n_dst_dev");
+  a.n_dst = static_cast<int32_t>(n_dst);
+  a.frontier = optr<uint8_t>(frontier, at::kByte, "frontier");
+  a.fanout = static_cast<int32_t>(fanout);
+  a.replace = replace;
+  a.counters = ptr<int64_t>(counters, at::kLong, "counters");
+  a.hop = static_cast<int32_t>(hop);
+  a.gideg = optr<int64_t>(gideg, at::kLong, "gideg");
+  a.cov_accum = optr<float>(cov_accum, at::kFloat, "cov_accum");
+  a.out_indptr = ptr<int32_t>(out_indptr, at::kInt, "out_indptr");
+  a.out_nbr = ptr<int32_t>(out_nbr, at::kInt, "out_nbr");
+  a.cap_edges = static_cast<int32_t>(out_nbr.numel());
+  a.n_edges_out = ptr<int32_t>(n_edges_out, at::kInt, "n_edges_out");
+  a.scan_scratch = reinterpret_cast<unsigned long long*>(ptr<int64_t>(scan_scratch, at::kLong, "scan_scratch"));
+  a.err = ptr<int32_t>(err, at::kInt, "err");
+  TORCH_CHECK(out_indptr.numel() >= cap_dst + 1, "out_indptr too small");
+  TORCH_CHECK(dst_nid.numel() >= cap_dst, "dst_nid smaller than cap_dst");
+  TORCH_CHECK(!a.frontier || frontier->numel() >= cap_dst, "frontier smaller than cap_dst");
+  TORCH_CHECK(!a.gideg || gideg->numel() >= cap_dst, "gideg smaller than cap_dst");
+  TORCH_CHECK(scan_scratch.numel() >= d::sample_scan_scratch_words(static_cast<int>(cap_dst)), "scan_scratch too small");
+  d::launch_sample_hop(a, static_cast<int>(cap_dst), stream());
+}
+
+int64_t sample_scratch_words(int64_t cap_dst) { return d::sample_scan_scratch_words(static_cast<int>(cap_dst)); }
+int64_t compact_scratch_words(int64_t cap_e) { return d::compact_scan_scratch_words(static_cast<int>(cap_e)); }
+
+void compact(Tensor dst_nid, Tensor n_dst_dev, Tensor nbr, Tensor n_edges_dev, Tensor map, Tensor src_nid,
+             Tensor src_sampled, Tensor indices, Tensor n_src_out, Tensor scan_scratch, Tensor err, int64_t cap_dst,
+             int64_t cap_edges, Tensor counters, int64_t slot) {
+  c10::cuda::CUDAGuard g(dst_nid.device());
+  TORCH_CHECK(slot >= 0 && slot < 16, "slot must be in [0, 16)");
+  TORCH_CHECK(counters.numel() >= 6, "counters needs 6 entries");
+  d::CompactArgs a;
+  a.dst_nid = ptr<int32_t>(dst_nid, at::kInt, "dst_nid");
+  a.n_dst_ptr = ptr<int32_t>(n_dst_dev, at::kInt, "n_dst_dev");
+  a.nbr = ptr<int32_t>(nbr, at::kInt, "nbr");
+  a.n_edges_ptr = ptr<int32_t>(n_edges_dev, at::kInt, "n_edges_dev");
+  a.map = reinterpret_cast<unsigned long long*>(ptr<int64_t>(map, at::kLong, "map"));
+  a.n_graph_nodes = map.numel();
+  a.src_nid = ptr<int32_t>(src_nid, at::kInt, "src_nid");
+  a.src_sampled = ptr<uint8_t>(src_sampled, at::kByte, "src_sampled");
+  a.indices = ptr<int32_t>(indices, at::kInt, "indices");
+  a.n_src_out = ptr<int32_t>(n_src_out, at::kInt, "n_src_out");
+  a.cap_src = static_cast<int32_t>(std::min(src_nid.numel(), src_sampled.numel()));
+  a.scan_scratch = reinterpret_cast<unsigned long long*>(ptr<int64_t>(scan_scratch, at::kLong, "scan_scratch"));
+  a.err = ptr<int32_t>(err, at::kInt, "err");
+  TORCH_CHECK(nbr.numel() >= cap_edges && indices.numel() >= cap_edges, "edge buffers smaller than cap_edges");
+  TORCH_CHECK(dst_nid.numel() >= cap_dst && a.cap_src >= cap_dst, "dst/src buffers smaller than cap_dst");
+  TORCH_CHECK(scan_scratch.numel() >= d::compact_scan_scratch_words(static_cast<int>(cap_edges)), "scan_scratch too small");
+  const int64_t* gen = ptr<int64_t>(counters, at::kLong, "counters") + 4;
+  d::launch_compact(a, static_cast<int>(cap_dst), static_cast<int>(cap_edges), gen, static_cast<int>(slot), num_sms(),
+                    stream());
+}
+
+// --------------------------------------------------------------------------- GEMM
+void gemm(Tensor A, bool a_mn, Tensor B, bool b_mn, int64_t M_cap, OptT M_dev, int64_t N, int64_t K_cap, OptT K_dev,
+          int64_t splits, Tensor C, int64_t mode, OptT bias, int64_t act, double dropout_p, OptT counters, int64_t salt,
+          OptT labels, int64_t n_classes, OptT dlogits, OptT loss_sum, OptT correct, OptT pred_out, OptT n_rows_dev,
+          OptT dbias, Tensor err, int64_t bn) {
+  c10::cuda::CUDAGuard g(A.device());
+  d::GemmProblem p;
+  p.A = ptr2d<at::BFloat16>(A, at::kBFloat16, "A");
+  p.a_rows = A.size(0);
+  p.a_cols = A.size(1);
+  p.lda = A.stride(0);
+  p.a_mn = a_mn;
+  p.B = ptr2d<at::BFloat16>(B, at::kBFloat16, "B");
+  p.b_rows = B.size(0);
+  p.b_cols = B.size(1);
+  p.ldb = B.stride(0);
+  p.b_mn = b_mn;
+  d::GemmArgs a;
+  a.M_cap = static_cast<int32_t>(M_cap);
+  a.M_dev = optr<int32_t>(M_dev, at::kInt, "M_dev");
+  a.N = static_cast<int32_t>(N);
+  a.K_cap = static_cast<int32_t>(K_cap);
+  a.K_dev = optr<int32_t>(K_dev, at::kInt, "K_dev");
+  a.splits = static_cast<int32_t>(splits);
+  a.c_mode = static_cast<int32_t>(mode);
+  if (mode == d::kStoreBf16) {
+    a.C = ptr2d<at::BFloat16>(C, at::kBFloat16, "C");
+    a.ldc = C.stride(0);
+  } else if (mode != d::kCrossEntropy) {
+    a.C = ptr2d<float>(C, at::kFloat, "C");
+    a.ldc = C.stride(0);
+  }
+  a.bias = optr<float>(bias, at::kFloat, "bias");
+  a.act = static_cast<int32_t>(act);
+  a.dropout_p = static_cast<float>(dropout_p);
+  a.counters = optr<int64_t>(counters, at::kLong, "counters");
+  a.dropout_salt = static_cast<uint32_t>(salt);
+  TORCH_CHECK(dropout_p == 0.0 || a.counters, "dropout needs the step counters");
+  TORCH_CHECK(dropout_p == 0.0 || a.ldc % 4 == 0, "dropout needs ldc % 4 == 0");
+  a.labels = optr<int32_t>(labels, at::kInt, "labels");
+  a.n_classes = static_cast<int32_t>(n_classes);
+  if (dlogits.has_value()) {
+    a.dlogits = reinterpret_cast<__nv_bfloat16*>(ptr2d<at::BFloat16>(*dlogits, at::kBFloat16, "dlogits"));
+    a.ld_dl = dlogits->stride(0);
+  }
+  a.loss_sum = optr<float>(loss_sum, at::kFloat, "loss_sum");
+  a.correct = optr<int32_t>(correct, at::kInt, "correct");
+  a.pred_out = optr<int32_t>(pred_out, at::kInt, "pred_out");
+  a.n_rows_dev = optr<int32_t>(n_rows_dev, at::kInt, "n_rows_dev");
+  a.dbias = optr<float>(dbias, at::kFloat, "dbias");
+  a.err = ptr<int32_t>(err, at::kInt, "err");
+  if (mode == d::kCrossEntropy)
+    TORCH_CHECK(a.labels && a.dlogits && a.loss_sum && a.correct, "cross-entropy epilogue needs labels/dlogits/loss/correct");
+  d::launch_gemm(p, a, static_cast<int>(bn), stream());
+}
+
+// --------------------------------------------------------------------------- aggregation
+void aggregate(Tensor indptr, Tensor indices, OptT n_dst_dev, int64_t n_dst, int64_t cap_dst, Tensor src, OptT src_map,
+               int64_t dim, int64_t mode, OptT edge_w, OptT src_norm, OptT dst_norm, Tensor out, int64_t agg_col,
+               int64_t self_col, double self_scale, int64_t zero_tail_rows, Tensor err) {
+  c10::cuda::CUDAGuard g(src.device());
+  d::AggArgs a;
+  a.indptr = ptr<int32_t>(indptr, at::kInt, "indptr");
+  a.indices = ptr<int32_t>(indices, at::kInt, "indices");
+  a.n_dst_ptr = optr<int32_t>(n_dst_dev, at::kInt, "n_dst_dev");
+  a.n_dst = static_cast<int32_t>(n_dst);
+  a.src = reinterpret_cast<const __nv_bfloat16*>(ptr2d<at::BFloat16>(src, at::kBFloat16, "src"));
+  a.src_stride = src.stride(0);
+  a.src_map = optr<int32_t>(src_map, at::kInt, "src_map");
+  a.dim = static_cast<int32_t>(dim);
+  a.mode = static_cast<int32_t>(mode);
+  a.edge_w = optr<float>(edge_w, at::kFloat, "edge_w");
+  a.src_norm = optr<float>(src_norm, at::kFloat, "src_norm");
+  a.dst_norm = optr<float>(dst_norm, at::kFloat, "dst_norm");
+  a.out = reinterpret_cast<__nv_bfloat16*>(ptr2d<at::BFloat16>(out, at::kBFloat16, "out"));
+  a.out_stride = out.stride(0);
+  a.agg_col = static_cast<int32_t>(agg_col);
+  a.self_col = static_cast<int32_t>(self_col);
+  a.self_scale = static_cast<float>(self_scale);
+  a.zero_tail_rows = static_cast<int32_t>(zero_tail_rows);
+  a.err = ptr<int32_t>(err, at::kInt, "err");
+  TORCH_CHECK(mode != d::kAggGcn || a.src_norm, "GCN aggregation needs src_norm");
+  TORCH_CHECK(mode != d::kAggWeighted || a.edge_w, "weighted aggregation needs edge_w");
+  TORCH_CHECK(agg_col + dim <= out.size(1) && (self_col < 0 || self_col + dim <= out.size(1)), "output too narrow");
+  TORCH_CHECK(dim <= src.size(1), "dim larger than the source rows");
+  TORCH_CHECK(out.size(0) >= cap_dst, "output has fewer rows than cap_dst");
+  d::launch_aggregate(a, static_cast<int>(cap_dst), stream());
+}
+
+void aggregate_bwd(Tensor indptr, Tensor indices, OptT n_dst_dev, int64_t n_dst, int64_t cap_dst, Tensor dout,
+                   int64_t agg_col, int64_t self_col, double self_scale, int64_t dim, int64_t mode, OptT edge_w,
+                   OptT src_norm, OptT dst_norm, Tensor dsrc, Tensor err) {
+  c10::cuda::CUDAGuard g(dout.device());
+  d::AggBwdArgs a;
+  a.indptr = ptr<int32_t>(indptr, at::kInt, "indptr");
+  a.indices = ptr<int32_t>(indices, at::kInt, "indices");
+  a.n_dst_ptr = optr<int32_t>(n_dst_dev, at::kInt, "n_dst_dev");
+  a.n_dst = static_cast<int32_t>(n_dst);
+  a.dout = reinterpret_cast<const __nv_bfloat16*>(ptr2d<at::BFloat16>(dout, at::kBFloat16, "dout"));
+  a.dout_stride = dout.stride(0);
+  a.agg_col = static_cast<int32_t>(agg_col);
+  a.self_col = static_cast<int32_t>(self_col);
+  a.self_scale = static_cast<float>(self_scale);
+  a.dim = static_cast<int32_t>(dim);
+  a.mode = static_cast<int32_t>(mode);
+  a.edge_w = optr<float>(edge_w, at::kFloat, "edge_w");
+  a.src_norm = optr<float>(src_norm, at::kFloat, "src_norm");
+  a.dst_norm = optr<float>(dst_norm, at::kFloat, "dst_norm");
+  a.dsrc = ptr2d<float>(dsrc, at::kFloat, "dsrc");
+  a.dsrc_stride = dsrc.stride(0);
+  a.err = ptr<int32_t>(err, at::kInt, "err");
+  TORCH_CHECK(dim <= dsrc.size(1), "dsrc too narrow");
+  d::launch_aggregate_bwd(a, static_cast<int>(cap_dst), stream());
+}
+
+void src_norm(Tensor indices, Tensor n_edges_dev, int64_t cap_edges, OptT n_src_dev, int64_t cap_src, Tensor deg_scratch,
+              Tensor out) {
+  c10::cuda::CUDAGuard g(indices.device());
+  d::launch_src_norm(ptr<int32_t>(indices, at::kInt, "indices"), ptr<int32_t>(n_edges_dev, at::kInt, "n_edges"),
+                     static_cast<int>(cap_edges), optr<int32_t>(n_src_dev, at::kInt, "n_src"), static_cast<int>(cap_src),
+                     ptr<float>(deg_scratch, at::kFloat, "deg_scratch"), ptr<float>(out, at::kFloat, "out"), stream());
+}
+
+void act_bwd(Tensor dh, OptT h, Tensor dy, OptT n_dev, int64_t n, int64_t dim, double scale, OptT dbias,
+             int64_t cap_rows) {
+  c10::cuda::CUDAGuard g(dh.device());
+  d::ActBwdArgs a;
+  a.dh = ptr2d<float>(dh, at::kFloat, "dh");
+  a.dh_stride = dh.stride(0);
+  if (h.has_value()) {
+    a.h = reinterpret_cast<const __nv_bfloat16*>(ptr2d<at::BFloat16>(*h, at::kBFloat16, "h"));
+    a.h_stride = h->stride(0);
+  }
+  a.dy = reinterpret_cast<__nv_bfloat16*>(ptr2d<at::BFloat16>(dy, at::kBFloat16, "dy"));
+  a.dy_stride = dy.stride(0);
+  a.n_ptr = optr<int32_t>(n_dev, at::kInt, "n_dev");
+  a.n = static_cast<int32_t>(n);
+  a.dim = static_cast<int32_t>(dim);
+  a.scale = static_cast<float>(scale);
+  a.dbias = optr<float>(dbias, at::kFloat, "dbias");
+  a.cap_rows = static_cast<int32_t>(std::min(dy.size(0), dh.size(0)));
+  if (cap_rows > 0) a.cap_rows = std::min<int32_t>(a.cap_rows, static_cast<int32_t>(cap_rows));
+  d::launch_act_bwd(a, stream());
+}
+
+// --------------------------------------------------------------------------- gathers / generators
+void gather_rows(Tensor table, Tensor ids, OptT n_dev, int64_t n, int64_t cap, int64_t dim, Tensor out) {
+  c10::cuda::CUDAGuard g(table.device());
+  TORCH_CHECK(table.is_cuda() && table.dim() == 2 && table.stride(1) == 1, "table must be a 2-D CUDA tensor");
+  TORCH_CHECK(table.scalar_type() == at::kBFloat16 || table.scalar_type() == at::kFloat, "table must be bf16 or fp32");
+  d::launch_gather_rows_bf16(table.data_ptr(), table.scalar_type() == at::kFloat, table.stride(0), static_cast<int32_t>(dim),
+                             ptr<int32_t>(ids, at::kInt, "ids"), optr<int32_t>(n_dev, at::kInt, "n_dev"),
+                             static_cast<int32_t>(n), static_cast<int>(cap),
+                             reinterpret_cast<__nv_bfloat16*>(ptr2d<at::BFloat16>(out, at::kBFloat16, "out")),
+                             out.stride(0), stream());
+}
+
+void gather_scalar(Tensor table, Tensor ids, OptT n_dev, int64_t n, int64_t cap, Tensor out) {
+  c10::cuda::CUDAGuard g(table.device());
+  if (table.scalar_type() == at::kInt)
+    d::launch_gather_i32(ptr<int32_t>(table, at::kInt, "table"), ptr<int32_t>(ids, at::kInt, "ids"),
+                         optr<int32_t>(n_dev, at::kInt, "n_dev"), static_cast<int>(n), static_cast<int>(cap),
+                         ptr<int32_t>(out, at::kInt, "out"), stream());
+  else
+    d::launch_gather_i64(ptr<int64_t>(table, at::kLong, "table"), ptr<int32_t>(ids, at::kInt, "ids"),
+                         optr<int32_t>(n_dev, at::kInt, "n_dev"), static_cast<int>(n), static_cast<int>(cap),
+                         ptr<int64_t>(out, at::kLong, "out"), stream());
+}
+
+void rmat_candidates(int64_t n, int64_t scale, double a, double b, double c, int64_t seed, int64_t e0, Tensor keys) {
+  c10::cuda::CUDAGuard g(keys.device());
+  d::launch_rmat_candidates(n, static_cast<int>(scale), a, b, c, static_cast<uint64_t>(seed), e0, keys.numel(),
+                            ptr<int64_t>(keys, at::kLong, "keys"), stream());
+}
+
+void shuffle_keys(Tensor ids, int64_t seed, int64_t epoch, Tensor keys) {
+  c10::cuda::CUDAGuard g(ids.device());
+  d::launch_shuffle_keys(ptr<int64_t>(ids, at::kLong, "ids"), ids.numel(), static_cast<uint64_t>(seed),
+                         static_cast<uint64_t>(epoch), ptr<int64_t>(keys, at::kLong, "keys"), stream());
+}
+
+void normal_fill(Tensor out, int64_t seed) {
+  c10::cuda::CUDAGuard g(out.device());
+  d::launch_normal_fill(ptr<float>(out, at::kFloat, "out"), out.numel(), static_cast<uint64_t>(seed), stream());
+}
+
+void dropout_mask(Tensor mask, int64_t ld, double p, Tensor counters, int64_t salt) {
+  c10::cuda::CUDAGuard g(mask.device());
+  d::launch_dropout_mask(ptr<uint8_t>(mask, at::kByte, "mask"), mask.size(0), mask.size(1), ld, static_cast<float>(p),
+                         ptr<int64_t>(counters, at::kLong, "counters"), static_cast<uint32_t>(salt), stream());
+}
+
+// --------------------------------------------------------------------------- optimizer
+void adam(Tensor param, Tensor m, Tensor v, Tensor grad, OptT param_bf16, double lr, double b1, double b2, double eps,
+          double wd, Tensor counters, double grad_scale, OptT grad_scale_dev, bool clear_grad) {
+  c10::cuda::CUDAGuard g(param.device());
+  d::AdamArgs a;
+  a.param = ptr<float>(param, at::kFloat, "param");
+  a.m = ptr<float>(m, at::kFloat, "m");
+  a.v = ptr<float>(v, at::kFloat, "v");
+  a.grad = ptr<float>(grad, at::kFloat, "grad");
+  if (param_bf16.has_value())
+    a.param_bf16 = reinterpret_cast<__nv_bfloat16*>(ptr<at::BFloat16>(*param_bf16, at::kBFloat16, "param_bf16"));
+  a.n = param.numel();
+  TORCH_CHECK(m.numel() == a.n && v.numel() == a.n && grad.numel() == a.n, "adam buffers differ in size");
+  TORCH_CHECK(!a.param_bf16 || param_bf16->numel() == a.n, "param_bf16 differs in size");
+  a.lr = static_cast<float>(lr);
+  a.beta1 = static_cast<float>(b1);
+  a.beta2 = static_cast<float>(b2);
+  a.eps = static_cast<float>(eps);
+  a.weight_decay = static_cast<float>(wd);
+  TORCH_CHECK(counters.numel() >= 6, "counters needs 6 entries");
+  a.step = ptr<int64_t>(counters, at::kLong, "counters") + 5;
+  a.grad_scale = static_cast<float>(grad_scale);
+  a.grad_scale_dev = optr<float>(grad_scale_dev, at::kFloat, "grad_scale_dev");
+  a.clear_grad = clear_grad;
+  d::launch_adam(a, stream());
+}
+
+void zero_(Tensor t) {
+  c10::cuda::CUDAGuard g(t.device());
+  check_cuda(t, "t");
+  GB_CUDA_CHECK(cudaMemsetAsync(t.data_ptr(), 0, t.numel() * t.element_size(), stream()));
+}
+
+void step_end(Tensor counters) {
+  c10::cuda::CUDAGuard g(counters.device());
+  TORCH_CHECK(counters.numel() >= 6, "counters needs 6 entries");
+  d::launch_step_end(ptr<int64_t>(counters, at::kLong, "counters"), stream());
+}
+
+// --------------------------------------------------------------------------- peer memory
+Tensor tensor_from_ptr(int64_t p, std::vector<int64_t> sizes, at::ScalarType dtype, int64_t device) {
+  auto opts = at::TensorOptions().dtype(dtype).device(at::kCUDA, device);
+  return at::from_blob(reinterpret_cast<void*>(p), sizes, [](void*) {}, opts);
+}
+
+template <typename T>
+T* as_ptr(int64_t p) {
+  return reinterpret_cast<T*>(p);
+}
+
+void allreduce_adam(int64_t rank, int64_t world, Tensor grad, int64_t chunk, std::vector<int64_t> send_local,
+                    std::vector<int64_t> send_peer, int64_t flags_local, std::vector<int64_t> flags_peer, OptT cov,
+                    Tensor counters, OptT param, OptT m, OptT v, OptT param_bf16, double lr, double b1, double b2,
+                    double eps, double wd, bool do_adam, OptT grad_out, Tensor err, int64_t grid, int64_t timeout_ns) {
+  c10::cuda::CUDAGuard g(grad.device());
+  namespace pe = grappa::peer;
+  TORCH_CHECK(world >= 1 && world <= pe::kMaxRanks, "world out of range");
+  TORCH_CHECK(send_local.size() == 2 && send_peer.size() == static_cast<size_t>(2 * world) &&
+                  flags_peer.size() == static_cast<size_t>(world),
+              "peer pointer lists have the wrong length");
+  pe::ArAdamArgs a;
+  a.rank = static_cast<int32_t>(rank);
+  a.world = static_cast<int32_t>(world);
+  a.grad = ptr<float>(grad, at::kFloat, "grad");
+  a.n = grad.numel();
+  a.chunk = static_cast<int32_t>(chunk);
+  a.send_local[0] = as_ptr<float>(send_local[0]);
+  a.send_local[1] = as_ptr<float>(send_local[1]);
+  for (int p = 0; p < world; ++p) {
+    a.send_peer[p][0] = as_ptr<const float>(send_peer[2 * p]);
+    a.send_peer[p][1] = as_ptr<const float>(send_peer[2 * p + 1]);
+    a.flags_peer[p] = as_ptr<uint32_t>(flags_peer[p]);
+  }
+  a.flags_local = as_ptr<uint32_t>(flags_local);
+  a.cov = optr<float>(cov, at::kFloat, "cov");
+  TORCH_CHECK(counters.numel() >= 6, "counters needs 6 entries");
+  a.counters = ptr<int64_t>(counters, at::kLong, "counters");
+  a.do_adam = do_adam;
+  if (do_adam) {
+    TORCH_CHECK(param.has_value() && m.has_value() && v.has_value(), "Adam needs param, m and v");
+    a.param = ptr<float>(*param, at::kFloat, "param");
+    a.m = ptr<float>(*m, at::kFloat, "m");
+    a.v = ptr<float>(*v, at::kFloat, "v");
+    TORCH_CHECK(param->numel() == a.n && m->numel() == a.n && v->numel() == a.n, "Adam buffers differ in size");
+    if (param_bf16.has_value())
+      a.param_bf16 = reinterpret_cast<__nv_bfloat16*>(ptr<at::BFloat16>(*param_bf16, at::kBFloat16, "param_bf16"));
+  } else {
+    TORCH_CHECK(grad_out.has_value() && grad_out->numel() == a.n, "grad_out of the gradient's size is needed");
+    a.grad_out = ptr<float>(*grad_out, at::kFloat, "grad_out");
+  }
+  a.lr = static_cast<float>(lr);
+  a.beta1 = static_cast<float>(b1);
+  a.beta2 = static_cast<float>(b2);
+  a.eps = static_cast<float>(eps);
+  a.weight_decay = static_cast<float>(wd);
+  a.err = ptr<int32_t>(err, at::kInt, "err");
+  a.timeout_ns = timeout_ns;
+  pe::launch_allreduce_adam(a, static_cast<int>(grid), stream());
+}
+
+void pull_rows(std::vector<int64_t> tables, int64_t table_stride, int64_t elem_bytes, int64_t row_bytes, Tensor gids,
+               OptT n_dev, int64_t n, Tensor prefix, int64_t out, int64_t out_stride, int64_t out_row0, int64_t cap) {
+  c10::cuda::CUDAGuard g(gids.device());
+  namespace pe = grappa::peer;
+  pe::PullRowsArgs a;
+  TORCH_CHECK(tables.size() >= 1 && tables.size() <= static_cast<size_t>(pe::kMaxRanks), "bad table list");
+  for (size_t i = 0; i < tables.size(); ++i) a.tables[i] = as_ptr<const void>(tables[i]);
+  a.world = static_cast<int32_t>(tables.size());
+  a.table_stride = table_stride;
+  a.elem_bytes = static_cast<int32_t>(elem_bytes);
+  a.row_bytes = static_cast<int32_t>(row_bytes);
+  a.gids = ptr<int64_t>(gids, at::kLong, "gids");
+  a.n_ptr = optr<int32_t>(n_dev, at::kInt, "n_dev");
+  a.n = n;
+  a.prefix = ptr<int64_t>(prefix, at::kLong, "prefix");
+  TORCH_CHECK(prefix.numel() == a.world + 1, "prefix needs world + 1 entries");
+  a.out = as_ptr<void>(out);
+  a.out_stride = out_stride;
+  a.out_row0 = out_row0;
+  pe::launch_pull_rows(a, cap, stream());
+}
+
+void peer_copy(int64_t dst, int64_t src, int64_t bytes) {
+  grappa::peer::launch_copy(as_ptr<void>(dst), as_ptr<const void>(src), bytes, stream());
+}
+
+void mark_ids(int64_t ids, OptT n_dev, int64_t n, Tensor mark) {
+  c10::cuda::CUDAGuard g(mark.device());
+  grappa::peer::launch_mark(as_ptr<const int32_t>(ids), optr<int32_t>(n_dev, at::kInt, "n_dev"), n,
+                            ptr<uint8_t>(mark, at::kByte, "mark"), stream());
+}
+
+void iota_map(Tensor map, int64_t g0, int64_t count, int64_t base, OptT clear_mark) {
+  c10::cuda::CUDAGuard g(map.device());
+  TORCH_CHECK(g0 >= 0 && g0 + count <= map.numel(), "iota_map range outside the map");
+  grappa::peer::launch_iota_map(ptr<int32_t>(map, at::kInt, "map"), g0, count, static_cast<int32_t>(base),
+                                optr<uint8_t>(clear_mark, at::kByte, "clear_mark"), stream());
+}
+
+void mark_compact(Tensor mark, Tensor out_ids, Tensor map, int64_t base, Tensor n_out, Tensor scratch, Tensor err) {
+  c10::cuda::CUDAGuard g(mark.device());
+  TORCH_CHECK(map.numel() >= mark.numel(), "map smaller than mark");
+  TORCH_CHECK(scratch.numel() >= grappa::peer::mark_compact_scratch_words(mark.numel()), "scratch too small");
+  grappa::peer::launch_mark_compact(ptr<uint8_t>(mark, at::kByte, "mark"), mark.numel(),
+                                    ptr<int64_t>(out_ids, at::kLong, "out_ids"), ptr<int32_t>(map, at::kInt, "map"),
+                                    static_cast<int32_t>(base), ptr<int32_t>(n_out, at::kInt, "n_out"),
+                                    reinterpret_cast<unsigned long long*>(ptr<int64_t>(scratch, at::kLong, "scratch")),
+                                    out_ids.numel(), ptr<int32_t>(err, at::kInt, "err"), stream());
+}
+
+void csr_merge(int64_t indptr_a, int64_t indices_a, int64_t n_a, int64_t indptr_b, int64_t indices_b, int64_t n_b,
+               Tensor map, Tensor indptr_out, Tensor indices_out, Tensor err) {
+  c10::cuda::CUDAGuard g(map.device());
+  grappa::peer::CsrMergeArgs a;
+  a.indptr_a = as_ptr<const int64_t>(indptr_a);
+  a.indices_a = as_ptr<const int32_t>(indices_a);
+  a.n_a = n_a;
+  a.indptr_b = as_ptr<const int64_t>(indptr_b);
+  a.indices_b = as_ptr<const int32_t>(indices_b);
+  a.n_b = n_b;
+  a.map = ptr<int32_t>(map, at::kInt, "map");
+  a.indptr_out = ptr<int64_t>(indptr_out, at::kLong, "indptr_out");
+  a.indices_out = ptr<int32_t>(indices_out, at::kInt, "indices_out");
+  a.cap_edges = indices_out.numel();
+  a.n_rows_total = indptr_out.numel() - 1;
+  a.err = ptr<int32_t>(err, at::kInt, "err");
+  TORCH_CHECK(a.n_rows_total >= n_a + n_b, "indptr_out too short");
+  grappa::peer::launch_csr_merge(a, stream());
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "grappa_b200 sm_100a kernels";
+  m.def("sample_hop", &sample_hop);
+  m.def("sample_scratch_words", &sample_scratch_words);
+  m.def("compact", &compact);
+  m.def("compact_scratch_words", &compact_scratch_words);
+  m.def("gemm", &gemm);
+  m.def("aggregate", &aggregate);
+  m.def("aggregate_bwd", &aggregate_bwd);
+  m.def("src_norm", &src_norm);
+  m.def("act_bwd", &act_bwd);
+  m.def("gather_rows", &gather_rows);
+  m.def("gather_scalar", &gather_scalar);
+  m.def("rmat_candidates", &rmat_candidates);
+  m.def("shuffle_keys", &shuffle_keys);
+  m.def("normal_fill", &normal_fill);
+  m.def("dropout_mask", &dropout_mask);
+  m.def("adam", &adam);
+  m.def("zero_", &zero_);
+  m.def("step_end", &step_end);
+  m.def("peer_alloc", [](int64_t bytes) { return reinterpret_cast<int64_t>(grappa::peer::alloc(bytes)); });
+  m.def("peer_free", [](int64_t p) { grappa::peer::release(reinterpret_cast<void*>(p)); });
+  m.def("ipc_handle", [](int64_t p) { return py::bytes(grappa::peer::ipc_handle(reinterpret_cast<void*>(p))); });
+  m.def("ipc_open", [](py::bytes h) { return reinterpret_cast<int64_t>(grappa::peer::ipc_open(std::string(h))); });
+  m.def("ipc_close", [](int64_t p) { grappa::peer::ipc_close(reinterpret_cast<void*>(p)); });
+  m.def("tensor_from_ptr", &tensor_from_ptr);
+  m.def("allreduce_adam", &allreduce_adam);
+  m.def("pull_rows", &pull_rows);
+  m.def("peer_copy", &peer_copy);
+  m.def("mark_ids", &mark_ids);
+  m.def("iota_map", &iota_map);
+  m.def("mark_compact", &mark_compact);
+  m.def("mark_compact_scratch_words", [](int64_t n) { return grappa::peer::mark_compact_scratch_words(n); });
+  m.def("csr_merge", &csr_merge);
+}

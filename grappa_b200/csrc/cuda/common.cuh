@@ -1,0 +1,175 @@
+// Shared device helpers for the sm_100a kernels.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <stdexcept>
+#include <string>
+
+#define GB_CUDA_CHECK(expr)                                                                  \
+  do {                                                                                       \
+    cudaError_t _e = (expr);                                                                 \
+    if (_e != cudaSuccess)                                                                   \
+      throw std::runtime_error(std::string("CUDA error ") + cudaGetErrorString(_e) + " at " + \
+                               __FILE__ + ":" + std::to_string(__LINE__));                  \
+  } while (0)
+
+#define GB_LAUNCH_CHECK() GB_CUDA_CHECK(cudaGetLastError())
+
+namespace grappa {
+namespace dev {
+
+// Error bits a kernel sets in the device error word instead of trapping.
+enum : int32_t {
+  kErrScanTimeout = 1 << 0,    // a look-back wait ran out of iterations
+  kErrCapacity = 1 << 1,       // an output did not fit its buffer; writes were dropped
+  kErrBadIndex = 1 << 2,       // an index was outside its table
+  kErrPeerTimeout = 1 << 3,    // a wait on a peer GPU's flag ran out of time
+  kErrMmaTimeout = 1 << 4,     // a wait on a tensor-core/TMA barrier ran out of time
+};
+
+__device__ __forceinline__ void set_error(int32_t* err, int32_t bit) {
+  if (err) atomicOr(err, bit);
+}
+
+__device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31u; }
+__device__ __forceinline__ uint32_t lanemask_lt() {
+  uint32_t m;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
+}
+
+__device__ __forceinline__ void st_release_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+template <typename T>
+__device__ __forceinline__ T warp_inclusive_scan(T v) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    T n = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane_id() >= static_cast<uint32_t>(o)) v += n;
+  }
+  return v;
+}
+
+template <typename T>
+__device__ __forceinline__ T warp_sum(T v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Block-wide exclusive scan of one value per thread; returns the exclusive
+// prefix and writes the block total to *total.  smem needs kThreads/32 entries.
+template <int kThreads, typename T>
+__device__ __forceinline__ T block_exclusive_scan(T v, T* smem, T* total) {
+  constexpr int kWarps = kThreads / 32;
+  const int w = threadIdx.x >> 5;
+  T inc = warp_inclusive_scan(v);
+  if (lane_id() == 31) smem[w] = inc;
+  __syncthreads();
+  if (w == 0) {
+    T s = lane_id() < kWarps ? smem[lane_id()] : T(0);
+    s = warp_inclusive_scan(s);
+    if (lane_id() < kWarps) smem[lane_id()] = s;
+  }
+  __syncthreads();
+  const T warp_prefix = w > 0 ? smem[w - 1] : T(0);
+  *total = smem[kWarps - 1];
+  __syncthreads();
+  return warp_prefix + inc - v;
+}
+
+// Decoupled look-back (D. Merrill, M. Garland, "Single-pass Parallel Prefix Scan
+// with Decoupled Look-back", NVIDIA TR NVR-2016-002).  scratch[0] is the tile
+// ticket; scratch[1 + t] the status word of tile t: bits 63..62 = flag
+// (1 aggregate, 2 inclusive prefix), bits 61..0 = value.  The caller zeroes the
+// scratch before the launch.  Waits are bounded: after kSpinLimit polls the tile
+// records kErrScanTimeout and proceeds with what it has.
+struct LookBack {
+  static constexpr unsigned long long kAgg = 1ull << 62;
+  static constexpr unsigned long long kPre = 2ull << 62;
+  static constexpr unsigned long long kMask = (1ull << 62) - 1;
+  static constexpr int kSpinLimit = 1 << 20;
+
+  __device__ static int ticket(unsigned long long* scratch, int* smem_slot) {
+    if (threadIdx.x == 0) *smem_slot = static_cast<int>(atomicAdd(scratch, 1ull));
+    __syncthreads();
+    return *smem_slot;
+  }
+
+  // Called by all lanes of warp 0.  Returns the exclusive prefix of tile t.
+  __device__ static long long exclusive_prefix(unsigned long long* scratch, int t, long long agg,
+                                               int32_t* err) {
+    unsigned long long* status = scratch + 1;
+    if (t == 0) {
+      if (lane_id() == 0) st_release_u64(status, kPre | (static_cast<unsigned long long>(agg) & kMask));
+      return 0;
+    }
+    if (lane_id() == 0) st_release_u64(status + t, kAgg | (static_cast<unsigned long long>(agg) & kMask));
+    long long prefix = 0;
+    int j = t - 1;
+    while (j >= 0) {
+      const int idx = j - static_cast<int>(lane_id());
+      unsigned long long s = kPre;  // lanes past tile 0 act as a zero prefix
+      if (idx >= 0) {
+        int spins = 0;
+        s = ld_acquire_u64(status + idx);
+        while ((s >> 62) == 0) {
+          if (++spins > kSpinLimit) {
+            set_error(err, kErrScanTimeout);
+            s = kPre;
+            break;
+          }
+          if (spins > 64) __nanosleep(32);
+          s = ld_acquire_u64(status + idx);
+        }
+      }
+      const uint32_t pre_mask = __ballot_sync(0xffffffffu, (s >> 62) == 2);
+      const int first_pre = pre_mask ? __ffs(pre_mask) - 1 : 32;  // nearest prefix lane
+      long long v = (static_cast<int>(lane_id()) <= first_pre && idx >= 0) ? static_cast<long long>(s & kMask) : 0;
+      prefix += warp_sum(v);
+      if (pre_mask) break;
+      j -= 32;
+    }
+    if (lane_id() == 0)
+      st_release_u64(status + t, kPre | (static_cast<unsigned long long>(prefix + agg) & kMask));
+    return prefix;
+  }
+};
+
+// bf16x8 <-> float helpers for 16-byte vector access.
+__device__ __forceinline__ void bf16x8_to_f32(const uint4& u, float* f) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __bfloat1622float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+__device__ __forceinline__ uint4 f32_to_bf16x8(const float* f) {
+  uint4 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+  return u;
+}
+
+__host__ __device__ __forceinline__ int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+}  // namespace dev
+}  // namespace grappa

@@ -1,0 +1,154 @@
+// S2: block compaction (the GPU equivalent of DGL's to_block as used by
+// t10n/dgl_dsg/compliant.py:32-49): the block's src nodes are its dst nodes, in
+// order, followed by the sampled neighbours that are not dst nodes, in order of
+// first appearance in the edge list; every edge gets the local index of its
+// source; src_sampled marks the src nodes that were sampled as a neighbour (the
+// frontier of the next hop, csrc/python/py_graph.cc:140-190).
+//
+// Instead of a hash table the kernels use a dense map over the graph's node ids
+// (8 bytes per node, resident in HBM and mostly in the 126 MB L2): entry =
+// (tag << 32) | position.  Tags decrease from call to call, so an atomicMin with
+// the current tag always wins over anything left by an earlier call and the map
+// is never cleared.
+//   K1  map[dst[i]] = min(., tag|i);  map[nbr[e]] = min(., tag|(n_dst+e))
+//   K2  edge e is a first appearance iff map[nbr[e]] == tag|(n_dst+e); decoupled
+//       look-back scan of those flags gives new local ids n_dst + rank;
+//       map[nbr[e]] = tag|lid, src_nid[lid] = nbr[e]
+//   K3  indices[e] = low32(map[nbr[e]]); src_sampled[indices[e]] = 1
+// A first-appearance test in K2 can never see a rewritten entry as its own value:
+// a rewritten entry holds a local id <= n_dst + e0 < n_dst + e for any later e.
+#include "common.cuh"
+#include "kernels.h"
+
+#include <algorithm>
+
+namespace grappa {
+namespace dev {
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kItems = 4;  // edges per thread in K2
+constexpr int kTile = kThreads * kItems;
+
+// Tag of this call: derived on the device from the generation counter so that a
+// captured CUDA graph keeps drawing fresh tags on every replay.
+__device__ __forceinline__ unsigned long long tag_word(const int64_t* gen, int slot) {
+  const uint32_t tag = 0xFFFFFFFFu - static_cast<uint32_t>(static_cast<uint64_t>(*gen) * 16u + static_cast<uint32_t>(slot));
+  return static_cast<unsigned long long>(tag) << 32;
+}
+
+__global__ void __launch_bounds__(kThreads) compact_k1(CompactArgs a, const int64_t* gen, int slot) {
+  const int n_dst = *a.n_dst_ptr;
+  const int n_e = *a.n_edges_ptr;
+  const unsigned long long tw = tag_word(gen, slot);
+  const long long total = static_cast<long long>(n_dst) + n_e;
+  for (long long j = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; j < total;
+       j += static_cast<long long>(gridDim.x) * blockDim.x) {
+    int32_t id;
+    if (j < n_dst) {
+      id = a.dst_nid[j];
+      a.src_nid[j] = id;
+      a.src_sampled[j] = 0;
+    } else {
+      id = a.nbr[j - n_dst];
+    }
+    if (id < 0 || id >= a.n_graph_nodes) {
+      set_error(a.err, kErrBadIndex);
+      continue;
+    }
+    atomicMin(a.map + id, tw | static_cast<unsigned long long>(j));
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) compact_k2(CompactArgs a, const int64_t* gen, int slot) {
+  __shared__ long long s_scan[kThreads / 32];
+  __shared__ int s_tile;
+  __shared__ long long s_prefix;
+  const int tile = LookBack::ticket(a.scan_scratch, &s_tile);
+  const int n_dst = *a.n_dst_ptr;
+  const int n_e = *a.n_edges_ptr;
+  const unsigned long long tw = tag_word(gen, slot);
+  const int e0 = tile * kTile + threadIdx.x * kItems;
+  int32_t ids[kItems];
+  bool fresh[kItems];
+  int cnt = 0;
+#pragma unroll
+  for (int q = 0; q < kItems; ++q) {
+    const int e = e0 + q;
+    fresh[q] = false;
+    ids[q] = -1;
+    if (e < n_e) {
+      ids[q] = a.nbr[e];
+      if (ids[q] >= 0 && ids[q] < a.n_graph_nodes) {
+        const unsigned long long m = a.map[ids[q]];
+        fresh[q] = m == (tw | static_cast<unsigned long long>(n_dst + e));
+      }
+      cnt += fresh[q];
+    }
+  }
+  long long total;
+  const long long excl = block_exclusive_scan<kThreads, long long>(cnt, s_scan, &total);
+  if ((threadIdx.x >> 5) == 0) {
+    const long long p = LookBack::exclusive_prefix(a.scan_scratch, tile, total, a.err);
+    if (lane_id() == 0) s_prefix = p;
+  }
+  __syncthreads();
+  long long lid = static_cast<long long>(n_dst) + s_prefix + excl;
+#pragma unroll
+  for (int q = 0; q < kItems; ++q) {
+    if (!fresh[q]) continue;
+    if (lid < a.cap_src) {
+      a.map[ids[q]] = tw | static_cast<unsigned long long>(lid);
+      a.src_nid[lid] = ids[q];
+      a.src_sampled[lid] = 0;
+    } else {
+      set_error(a.err, kErrCapacity);
+    }
+    ++lid;
+  }
+  const int last_tile = n_e > 0 ? (n_e - 1) / kTile : 0;
+  if (tile == last_tile && threadIdx.x == 0) {
+    long long ns = static_cast<long long>(n_dst) + s_prefix + total;
+    if (ns > a.cap_src) ns = a.cap_src;
+    *a.n_src_out = static_cast<int32_t>(ns);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) compact_k3(CompactArgs a) {
+  const int n_e = *a.n_edges_ptr;
+  for (long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < n_e;
+       e += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int32_t id = a.nbr[e];
+    int32_t lid = 0;
+    if (id >= 0 && id < a.n_graph_nodes) lid = static_cast<int32_t>(a.map[id] & 0xffffffffull);
+    if (lid >= a.cap_src || lid < 0) lid = 0;
+    a.indices[e] = lid;
+    a.src_sampled[lid] = 1;
+  }
+}
+
+}  // namespace
+
+int compact_scan_scratch_words(int cap_edges) {
+  return static_cast<int>(ceil_div(cap_edges > 0 ? cap_edges : 1, kTile)) + 1;
+}
+
+void launch_compact(const CompactArgs& a, int cap_dst, int cap_edges, const int64_t* gen, int slot, int num_sms,
+                    cudaStream_t stream) {
+  const int grid_stride = num_sms * 8;
+  const long long work1 = static_cast<long long>(cap_dst) + cap_edges;
+  const int g1 = static_cast<int>(std::min<long long>(grid_stride, ceil_div(work1 > 0 ? work1 : 1, kThreads)));
+  compact_k1<<<g1, kThreads, 0, stream>>>(a, gen, slot);
+  GB_LAUNCH_CHECK();
+  const int tiles = static_cast<int>(ceil_div(cap_edges > 0 ? cap_edges : 1, kTile));
+  GB_CUDA_CHECK(cudaMemsetAsync(a.scan_scratch, 0, sizeof(unsigned long long) * (tiles + 1), stream));
+  compact_k2<<<tiles, kThreads, 0, stream>>>(a, gen, slot);
+  GB_LAUNCH_CHECK();
+  const int g3 = static_cast<int>(std::min<long long>(grid_stride, ceil_div(cap_edges > 0 ? cap_edges : 1, kThreads)));
+  compact_k3<<<g3, kThreads, 0, stream>>>(a);
+  GB_LAUNCH_CHECK();
+}
+
+}  // namespace dev
+}  // namespace grappa

@@ -1,0 +1,209 @@
+// Argument blocks and launchers of the sm_100a kernels (no torch types here; the
+// torch bindings live in bindings.cpp).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace grappa {
+namespace dev {
+
+// ---------------------------------------------------------------- sampling (S1)
+struct SampleHopArgs {
+  const int64_t* indptr = nullptr;   // graph CSC by dst, [n_graph_nodes + 1]
+  const int32_t* indices = nullptr;  // graph sources
+  int64_t n_graph_nodes = 0;
+  const int32_t* dst_nid = nullptr;  // block destinations (graph ids)
+  const int32_t* n_dst_ptr = nullptr;  // device count, or null to use n_dst
+  int32_t n_dst = 0;
+  const uint8_t* frontier = nullptr;   // null: every dst samples
+  int32_t fanout = 0;                  // < 0: all neighbours
+  bool replace = false;
+  const int64_t* counters = nullptr;   // device [seed, epoch, step, ...]
+  int32_t hop = 0;
+  const int64_t* gideg = nullptr;      // per dst global in-degree (seed hop) or null
+  float* cov_accum = nullptr;          // device [sum, count]
+  int32_t* out_indptr = nullptr;       // [cap_dst + 1]
+  int32_t* out_nbr = nullptr;          // [cap_edges]
+  int32_t cap_edges = 0;
+  int32_t* n_edges_out = nullptr;
+  unsigned long long* scan_scratch = nullptr;
+  int32_t* err = nullptr;
+};
+void launch_sample_hop(const SampleHopArgs& a, int cap_dst, cudaStream_t stream);
+int sample_scan_scratch_words(int cap_dst);
+
+// ---------------------------------------------------------------- compaction (S2)
+struct CompactArgs {
+  const int32_t* dst_nid = nullptr;
+  const int32_t* n_dst_ptr = nullptr;
+  const int32_t* nbr = nullptr;
+  const int32_t* n_edges_ptr = nullptr;
+  unsigned long long* map = nullptr;  // dense [n_graph_nodes]
+  int64_t n_graph_nodes = 0;
+  int32_t* src_nid = nullptr;         // [cap_src]
+  uint8_t* src_sampled = nullptr;     // [cap_src]
+  int32_t* indices = nullptr;         // [cap_edges]
+  int32_t* n_src_out = nullptr;
+  int32_t cap_src = 0;
+  unsigned long long* scan_scratch = nullptr;
+  int32_t* err = nullptr;
+};
+// gen: device generation counter; tags are derived on the device from (*gen, slot)
+// so that a captured graph keeps drawing fresh tags (slot < 16 per generation).
+void launch_compact(const CompactArgs& a, int cap_dst, int cap_edges, const int64_t* gen, int slot, int num_sms,
+                    cudaStream_t stream);
+int compact_scan_scratch_words(int cap_edges);
+
+// ---------------------------------------------------------------- GEMM
+enum GemmMode : int { kStoreBf16 = 0, kStoreF32 = 1, kAtomicF32 = 2, kCrossEntropy = 3 };
+
+struct GemmProblem {
+  // physical row-major shapes; K-major A is [M][K], MN-major A is [K][M]
+  const void* A = nullptr;
+  int64_t a_rows = 0, a_cols = 0, lda = 0;
+  bool a_mn = false;
+  const void* B = nullptr;
+  int64_t b_rows = 0, b_cols = 0, ldb = 0;
+  bool b_mn = false;
+};
+
+struct GemmArgs {
+  int32_t M_cap = 0;
+  const int32_t* M_dev = nullptr;
+  int32_t N = 0;
+  int32_t K_cap = 0;
+  const int32_t* K_dev = nullptr;
+  int32_t splits = 1;
+  void* C = nullptr;
+  int64_t ldc = 0;
+  int32_t c_mode = kStoreBf16;
+  const float* bias = nullptr;
+  int32_t act = 0;  // 1: ReLU
+  float dropout_p = 0.f;
+  const int64_t* counters = nullptr;
+  uint32_t dropout_salt = 0;
+  // cross-entropy epilogue
+  const int32_t* labels = nullptr;
+  int32_t n_classes = 0;
+  __nv_bfloat16* dlogits = nullptr;
+  int64_t ld_dl = 0;
+  float* loss_sum = nullptr;
+  int32_t* correct = nullptr;
+  int32_t* pred_out = nullptr;
+  const int32_t* n_rows_dev = nullptr;
+  float* dbias = nullptr;              // cross-entropy epilogue: += column sums of the gradient
+  int32_t* err = nullptr;
+};
+void launch_gemm(const GemmProblem& p, GemmArgs a, int bn, cudaStream_t stream);
+
+// ---------------------------------------------------------------- aggregation (K-SpMM)
+enum AggMode : int { kAggMean = 0, kAggSum = 1, kAggGcn = 2, kAggWeighted = 3 };
+
+struct AggArgs {
+  const int32_t* indptr = nullptr;   // block CSR by dst [n_dst + 1]
+  const int32_t* indices = nullptr;  // local src index per edge
+  const int32_t* n_dst_ptr = nullptr;
+  int32_t n_dst = 0;
+  const __nv_bfloat16* src = nullptr;  // source rows
+  int64_t src_stride = 0;
+  const int32_t* src_map = nullptr;  // local src -> row of src (null: identity)
+  int32_t dim = 0;                   // feature width (multiple of 8)
+  int32_t mode = kAggMean;
+  const float* edge_w = nullptr;     // kAggWeighted
+  const float* src_norm = nullptr;   // kAggGcn: per local src
+  const float* dst_norm = nullptr;   // kAggGcn: per dst (null: computed from the block in-degree)
+  __nv_bfloat16* out = nullptr;
+  int64_t out_stride = 0;
+  int32_t agg_col = 0;               // column of the aggregate in out
+  int32_t self_col = -1;             // >= 0: also copy the dst row here
+  float self_scale = 0.f;            // != 0: out_agg += self_scale * self (GIN)
+  int32_t zero_tail_rows = 0;        // write zeros in rows [n_dst, roundup(n_dst, this))
+  int32_t* err = nullptr;
+};
+void launch_aggregate(const AggArgs& a, int cap_dst, cudaStream_t stream);
+
+struct AggBwdArgs {
+  const int32_t* indptr = nullptr;
+  const int32_t* indices = nullptr;
+  const int32_t* n_dst_ptr = nullptr;
+  int32_t n_dst = 0;
+  const __nv_bfloat16* dout = nullptr;  // gradient of the aggregation output
+  int64_t dout_stride = 0;
+  int32_t agg_col = 0;
+  int32_t self_col = -1;                // >= 0: add this gradient block to the dst rows
+  float self_scale = 0.f;               // GIN: the aggregate's gradient also flows to self
+  int32_t dim = 0;
+  int32_t mode = kAggMean;
+  const float* edge_w = nullptr;
+  const float* src_norm = nullptr;
+  const float* dst_norm = nullptr;
+  float* dsrc = nullptr;                // fp32 accumulation [n_src][dim], must start at 0
+  int64_t dsrc_stride = 0;
+  int32_t* err = nullptr;
+};
+void launch_aggregate_bwd(const AggBwdArgs& a, int cap_dst, cudaStream_t stream);
+
+// GCN normalisation: out-degree of every local src of a block (clamped >= 1) ^ -1/2
+void launch_src_norm(const int32_t* indices, const int32_t* n_edges_ptr, int cap_edges, const int32_t* n_src_ptr,
+                     int cap_src, float* deg_scratch, float* src_norm, cudaStream_t stream);
+
+// ---------------------------------------------------------------- elementwise / misc
+// dY = (h != 0) ? dh * scale : 0  (ReLU + dropout backward from the stored output),
+// fp32 dh read and cleared (so the accumulation buffer starts at 0 next time);
+// rows [n, roundup(n, 64)) of dY are zeroed for the split-K GEMM; the column sums of
+// dY are added to dbias.
+struct ActBwdArgs {
+  float* dh = nullptr;
+  int64_t dh_stride = 0;
+  const __nv_bfloat16* h = nullptr;  // forward output (null: identity activation)
+  int64_t h_stride = 0;
+  __nv_bfloat16* dy = nullptr;
+  int64_t dy_stride = 0;
+  const int32_t* n_ptr = nullptr;
+  int32_t n = 0;
+  int32_t dim = 0;
+  float scale = 1.f;
+  float* dbias = nullptr;
+  int32_t cap_rows = 0;
+};
+void launch_act_bwd(const ActBwdArgs& a, cudaStream_t stream);
+
+void launch_gather_rows_bf16(const void* table, bool table_f32, int64_t table_stride, int32_t dim,
+                             const int32_t* ids, const int32_t* n_ptr, int32_t n, int cap,
+                             __nv_bfloat16* out, int64_t out_stride, cudaStream_t stream);
+void launch_gather_i32(const int32_t* table, const int32_t* ids, const int32_t* n_ptr, int n, int cap,
+                       int32_t* out, cudaStream_t stream);
+void launch_gather_i64(const int64_t* table, const int32_t* ids, const int32_t* n_ptr, int n, int cap,
+                       int64_t* out, cudaStream_t stream);
+
+void launch_rmat_candidates(int64_t n, int scale, double a, double b, double c, uint64_t seed, int64_t e_begin,
+                            int64_t count, int64_t* keys, cudaStream_t stream);
+void launch_shuffle_keys(const int64_t* ids, int64_t n, uint64_t seed, uint64_t epoch, int64_t* keys,
+                         cudaStream_t stream);
+void launch_normal_fill(float* out, int64_t n, uint64_t seed, cudaStream_t stream);
+void launch_dropout_mask(uint8_t* mask, int64_t rows, int64_t cols, int64_t ld, float p, const int64_t* counters,
+                         uint32_t salt, cudaStream_t stream);
+
+// ---------------------------------------------------------------- optimizer
+struct AdamArgs {
+  float* param = nullptr;     // fp32 master weights
+  float* m = nullptr;
+  float* v = nullptr;
+  float* grad = nullptr;
+  bool clear_grad = true;     // zero the gradient after reading it
+  __nv_bfloat16* param_bf16 = nullptr;  // working copy (may be null)
+  int64_t n = 0;
+  float lr = 1e-3f, beta1 = 0.9f, beta2 = 0.999f, eps = 1e-8f, weight_decay = 0.f;
+  const int64_t* step = nullptr;  // device count of completed optimizer steps
+  float grad_scale = 1.f;
+  const float* grad_scale_dev = nullptr;  // multiplies grad_scale when given
+};
+void launch_adam(const AdamArgs& a, cudaStream_t stream);
+
+// counters = [seed, epoch, step_in_epoch, global_step, gen, adam_t]: advance the step
+void launch_step_end(int64_t* counters, cudaStream_t stream);
+
+}  // namespace dev
+}  // namespace grappa

@@ -1,0 +1,282 @@
+// Element-wise and gather kernels of the training step, the synthetic-data
+// generators, and the fused Adam update.
+#include "common.cuh"
+#include "grappa/rng.h"
+#include "kernels.h"
+
+#include <algorithm>
+
+namespace grappa {
+namespace dev {
+
+namespace {
+
+int sm_count() {
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  return sms;
+}
+
+int grid_1d(int64_t n, int threads, int per_sm = 8) {
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ceil_div(n > 0 ? n : 1, threads), int64_t(sm_count()) * per_sm)));
+}
+
+// ---------------------------------------------------------------- act_bwd
+__global__ void act_bwd_kernel(ActBwdArgs a, int chunks) {
+  extern __shared__ float s_col[];  // [blockDim.x * 8]
+  const int n = a.n_ptr ? *a.n_ptr : a.n;
+  const int rpb = blockDim.x / chunks;
+  const int c = threadIdx.x % chunks;
+  const int r_in = threadIdx.x / chunks;
+  const int tail = static_cast<int>(ceil_div(n, 64) * 64);
+  const int rows_end = std::min(tail, a.cap_rows > 0 ? a.cap_rows : tail);
+  float colsum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int r = blockIdx.x * rpb + r_in; r < rows_end; r += gridDim.x * rpb) {
+    float g[8];
+    if (r < n) {
+      float* dh = a.dh + static_cast<int64_t>(r) * a.dh_stride + c * 8;
+      const float4 d0 = *reinterpret_cast<float4*>(dh);
+      const float4 d1 = *reinterpret_cast<float4*>(dh + 4);
+      *reinterpret_cast<float4*>(dh) = make_float4(0.f, 0.f, 0.f, 0.f);
+      *reinterpret_cast<float4*>(dh + 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+      g[0] = d0.x; g[1] = d0.y; g[2] = d0.z; g[3] = d0.w;
+      g[4] = d1.x; g[5] = d1.y; g[6] = d1.z; g[7] = d1.w;
+      if (a.h) {
+        float hv[8];
+        bf16x8_to_f32(*reinterpret_cast<const uint4*>(a.h + static_cast<int64_t>(r) * a.h_stride + c * 8), hv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) g[j] = hv[j] != 0.f ? g[j] * a.scale : 0.f;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) g[j] *= a.scale;
+      }
+      // the bias gradient uses the bf16-rounded value that the GEMMs consume
+      const uint4 packed = f32_to_bf16x8(g);
+      bf16x8_to_f32(packed, g);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) colsum[j] += g[j];
+      *reinterpret_cast<uint4*>(a.dy + static_cast<int64_t>(r) * a.dy_stride + c * 8) = packed;
+    } else {
+      *reinterpret_cast<uint4*>(a.dy + static_cast<int64_t>(r) * a.dy_stride + c * 8) = make_uint4(0, 0, 0, 0);
+    }
+  }
+  if (!a.dbias) return;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) s_col[threadIdx.x * 8 + j] = colsum[j];
+  __syncthreads();
+  for (int t = threadIdx.x; t < chunks * 8; t += blockDim.x) {
+    const int cc = t / 8, j = t % 8;
+    float s = 0.f;
+    for (int q = 0; q < rpb; ++q) s += s_col[(q * chunks + cc) * 8 + j];
+    if (s != 0.f) atomicAdd(a.dbias + cc * 8 + j, s);
+  }
+}
+
+// ---------------------------------------------------------------- gathers
+template <bool F32>
+__global__ void gather_rows_kernel(const void* table, int64_t ts, int dim, const int32_t* ids, const int32_t* n_ptr,
+                                   int n_static, __nv_bfloat16* out, int64_t os) {
+  const int n = n_ptr ? *n_ptr : n_static;
+  const int chunks = dim >> 3;
+  const int lane = threadIdx.x & 31;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  for (int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < n; r += warps) {
+    const int64_t src = ids[r];
+    for (int c = lane; c < chunks; c += 32) {
+      uint4 v;
+      if (F32) {
+        const float* t = reinterpret_cast<const float*>(table) + src * ts + c * 8;
+        const float4 x = *reinterpret_cast<const float4*>(t);
+        const float4 y = *reinterpret_cast<const float4*>(t + 4);
+        const float f[8] = {x.x, x.y, x.z, x.w, y.x, y.y, y.z, y.w};
+        v = f32_to_bf16x8(f);
+      } else {
+        v = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(table) + src * ts + c * 8);
+      }
+      *reinterpret_cast<uint4*>(out + r * os + c * 8) = v;
+    }
+  }
+}
+
+template <typename T>
+__global__ void gather_scalar_kernel(const T* table, const int32_t* ids, const int32_t* n_ptr, int n_static, T* out) {
+  const int n = n_ptr ? *n_ptr : n_static;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) out[i] = table[ids[i]];
+}
+
+// ---------------------------------------------------------------- generators
+__global__ void rmat_kernel(int64_t n, int scale, uint64_t ta, uint64_t tb, uint64_t tc, uint64_t key, int64_t e0,
+                            int64_t count, int64_t* keys) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < count;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint64_t e = static_cast<uint64_t>(e0 + i);
+    uint64_t u = 0, v = 0;
+    U4 r{0, 0, 0, 0};
+    for (int l = 0; l < scale; ++l) {
+      if ((l & 3) == 0) r = index_draw4(key, e, static_cast<uint32_t>(l >> 2));
+      const uint64_t x = u4_word(r, l & 3);
+      const uint64_t bu = x >= tb ? 1u : 0u;
+      const uint64_t bv = ((x >= ta && x < tb) || x >= tc) ? 1u : 0u;
+      u = (u << 1) | bu;
+      v = (v << 1) | bv;
+    }
+    int64_t out = -1;
+    if (u < static_cast<uint64_t>(n) && v < static_cast<uint64_t>(n) && u != v) {
+      const uint64_t lo = u < v ? u : v, hi = u < v ? v : u;
+      out = static_cast<int64_t>(lo * static_cast<uint64_t>(n) + hi);
+    }
+    keys[i] = out;
+  }
+}
+
+__global__ void shuffle_keys_kernel(const int64_t* ids, int64_t n, uint64_t k, int64_t* keys) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    keys[i] = static_cast<int64_t>(mix64(static_cast<uint64_t>(ids[i]) ^ k) >> 1);
+}
+
+// Box-Muller transform of Philox uniforms (standard normal samples).
+__global__ void normal_kernel(float* out, int64_t n, uint64_t key) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; 2 * i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const U4 r = index_draw4(key, static_cast<uint64_t>(i), 7u);
+    const float u1 = (static_cast<float>(r.x >> 8) + 0.5f) * (1.0f / 16777216.0f);
+    const float u2 = static_cast<float>(r.y >> 8) * (1.0f / 16777216.0f);
+    const float rad = sqrtf(-2.0f * logf(u1));
+    float s, c;
+    sincospif(2.0f * u2, &s, &c);
+    out[2 * i] = rad * c;
+    if (2 * i + 1 < n) out[2 * i + 1] = rad * s;
+  }
+}
+
+__global__ void dropout_mask_kernel(uint8_t* mask, int64_t rows, int64_t cols, int64_t ld, uint32_t thr,
+                                    const int64_t* counters, uint32_t salt) {
+  const uint64_t key = hop_key(static_cast<uint64_t>(counters[0]) ^ 0xD80Full, static_cast<uint64_t>(counters[1]),
+                               static_cast<uint64_t>(counters[2]), salt);
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < rows * cols;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / cols, c = i % cols;
+    const uint64_t idx = static_cast<uint64_t>(r) * static_cast<uint64_t>(ld) + static_cast<uint64_t>(c);
+    const U4 w = index_draw4(key, idx >> 2, 0);
+    mask[i] = u4_word(w, static_cast<int>(idx & 3)) >= thr ? 1 : 0;
+  }
+}
+
+// ---------------------------------------------------------------- Adam
+// Same update as torch.optim.Adam (no amsgrad): m = b1 m + (1-b1) g,
+// v = b2 v + (1-b2) g^2, p -= lr/bc1 * m / (sqrt(v)/sqrt(bc2) + eps).
+__global__ void adam_kernel(AdamArgs a) {
+  const float t = static_cast<float>(*a.step + 1);
+  const float bc1 = 1.f - powf(a.beta1, t);
+  const float bc2 = 1.f - powf(a.beta2, t);
+  const float step_size = a.lr / bc1;
+  const float inv_sqrt_bc2 = rsqrtf(bc2);
+  const float gs = a.grad_scale * (a.grad_scale_dev ? *a.grad_scale_dev : 1.f);
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < a.n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float g = a.grad[i] * gs;
+    if (a.clear_grad) a.grad[i] = 0.f;
+    float p = a.param[i];
+    if (a.weight_decay != 0.f) g += a.weight_decay * p;
+    const float m = a.beta1 * a.m[i] + (1.f - a.beta1) * g;
+    const float v = a.beta2 * a.v[i] + (1.f - a.beta2) * g * g;
+    a.m[i] = m;
+    a.v[i] = v;
+    p -= step_size * m / (sqrtf(v) * inv_sqrt_bc2 + a.eps);
+    a.param[i] = p;
+    if (a.param_bf16) a.param_bf16[i] = __float2bfloat16_rn(p);
+  }
+}
+
+// counters = [seed, epoch, step_in_epoch, global_step, gen, adam_t]
+__global__ void step_end_kernel(int64_t* counters) {
+  counters[2] += 1;
+  counters[3] += 1;
+  counters[4] += 1;
+  counters[5] += 1;
+}
+
+}  // namespace
+
+void launch_act_bwd(const ActBwdArgs& a, cudaStream_t stream) {
+  if (a.dim % 8 != 0) throw std::invalid_argument("act_bwd: dim must be a multiple of 8");
+  const int chunks = a.dim / 8;
+  if (chunks > 256) throw std::invalid_argument("act_bwd: dim too large");
+  const int rpb = std::max(1, 256 / chunks);
+  const int threads = chunks * rpb;
+  const int rows = a.cap_rows > 0 ? a.cap_rows : a.n;
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ceil_div(rows, rpb), int64_t(sm_count()) * 8)));
+  act_bwd_kernel<<<grid, threads, threads * 8 * sizeof(float), stream>>>(a, chunks);
+  GB_LAUNCH_CHECK();
+}
+
+void launch_gather_rows_bf16(const void* table, bool table_f32, int64_t table_stride, int32_t dim, const int32_t* ids,
+                             const int32_t* n_ptr, int32_t n, int cap, __nv_bfloat16* out, int64_t out_stride,
+                             cudaStream_t stream) {
+  if (dim % 8 != 0) throw std::invalid_argument("gather: dim must be a multiple of 8");
+  const int grid = grid_1d(static_cast<int64_t>(cap) * 32, 256, 16);
+  if (table_f32)
+    gather_rows_kernel<true><<<grid, 256, 0, stream>>>(table, table_stride, dim, ids, n_ptr, n, out, out_stride);
+  else
+    gather_rows_kernel<false><<<grid, 256, 0, stream>>>(table, table_stride, dim, ids, n_ptr, n, out, out_stride);
+  GB_LAUNCH_CHECK();
+}
+
+void launch_gather_i32(const int32_t* table, const int32_t* ids, const int32_t* n_ptr, int n, int cap, int32_t* out,
+                       cudaStream_t stream) {
+  gather_scalar_kernel<int32_t><<<grid_1d(cap, 256), 256, 0, stream>>>(table, ids, n_ptr, n, out);
+  GB_LAUNCH_CHECK();
+}
+void launch_gather_i64(const int64_t* table, const int32_t* ids, const int32_t* n_ptr, int n, int cap, int64_t* out,
+                       cudaStream_t stream) {
+  gather_scalar_kernel<int64_t><<<grid_1d(cap, 256), 256, 0, stream>>>(table, ids, n_ptr, n, out);
+  GB_LAUNCH_CHECK();
+}
+
+void launch_rmat_candidates(int64_t n, int scale, double a, double b, double c, uint64_t seed, int64_t e_begin,
+                            int64_t count, int64_t* keys, cudaStream_t stream) {
+  const uint64_t ta = static_cast<uint64_t>(a * 4294967296.0);
+  const uint64_t tb = static_cast<uint64_t>((a + b) * 4294967296.0);
+  const uint64_t tc = static_cast<uint64_t>((a + b + c) * 4294967296.0);
+  rmat_kernel<<<grid_1d(count, 256, 32), 256, 0, stream>>>(n, scale, ta, tb, tc, mix64(seed ^ 0x524D4154ull), e_begin,
+                                                          count, keys);
+  GB_LAUNCH_CHECK();
+}
+
+void launch_shuffle_keys(const int64_t* ids, int64_t n, uint64_t seed, uint64_t epoch, int64_t* keys,
+                         cudaStream_t stream) {
+  const uint64_t k = mix64(mix64(seed ^ 0x5348554646ull) ^ epoch);
+  shuffle_keys_kernel<<<grid_1d(n, 256, 16), 256, 0, stream>>>(ids, n, k, keys);
+  GB_LAUNCH_CHECK();
+}
+
+void launch_normal_fill(float* out, int64_t n, uint64_t seed, cudaStream_t stream) {
+  normal_kernel<<<grid_1d((n + 1) / 2, 256, 32), 256, 0, stream>>>(out, n, mix64(seed ^ 0x4E4F524Dull));
+  GB_LAUNCH_CHECK();
+}
+
+void launch_dropout_mask(uint8_t* mask, int64_t rows, int64_t cols, int64_t ld, float p, const int64_t* counters,
+                         uint32_t salt, cudaStream_t stream) {
+  const uint32_t thr = static_cast<uint32_t>(static_cast<double>(p) * 4294967296.0);
+  dropout_mask_kernel<<<grid_1d(rows * cols, 256, 16), 256, 0, stream>>>(mask, rows, cols, ld, thr, counters, salt);
+  GB_LAUNCH_CHECK();
+}
+
+void launch_adam(const AdamArgs& a, cudaStream_t stream) {
+  adam_kernel<<<grid_1d(a.n, 256, 4), 256, 0, stream>>>(a);
+  GB_LAUNCH_CHECK();
+}
+
+void launch_step_end(int64_t* counters, cudaStream_t stream) {
+  step_end_kernel<<<1, 1, 0, stream>>>(counters);
+  GB_LAUNCH_CHECK();
+}
+
+}  // namespace dev
+}  // namespace grappa

@@ -1,0 +1,354 @@
+// Peer-memory kernels (see peer.h).
+//
+// K-AR, the fused coverage-corrected all-reduce + Adam (one-shot).  The reference
+// scales each rank's gradient bucket by its coverage weight c_r / W and sums the
+// buckets with an NCCL all-reduce, then runs torch.optim.Adam
+// (t10n/grad.py:6-24, experiments/grappa/train/t10n_train.py:159-162,248).  Here
+// one persistent kernel does all of it.  The gradient is cut into chunks; CTA j
+// of every rank owns the same chunks, so no grid-wide synchronisation is needed:
+//   1. publish: send[parity][chunk] = grad[chunk] * c_r / W (local store), grad = 0;
+//      then __threadfence_system and a st.release.sys of the step tag into flag
+//      [rank][chunk] of every peer
+//   2. wait: ld.acquire.sys polls of this rank's flags [p][chunk] for all p until
+//      they reach the tag (bounded by a %globaltimer deadline; on expiry the CTA
+//      records kErrPeerTimeout and stops reducing, so the GPU is never held)
+//   3. reduce: g = sum_p send_p[parity][chunk] with 16-byte P2P loads over NVLink,
+//      summed in rank order so that every rank computes bit-identical parameters;
+//      then the Adam update of the chunk writes the fp32 master weights, the
+//      moments and the bf16 working copy.
+// The send slots alternate with the step parity: a rank can only start publishing
+// step t+2 after every peer has published step t+1, which each peer does only after
+// it finished reading step t, so a slot is never overwritten while it is read.
+// Flags are compared with >= (wrap-safe), since a peer may already have published
+// the next step's tag for a chunk that this CTA has not polled yet.
+#include "common.cuh"
+#include "peer.h"
+
+#include <algorithm>
+
+namespace grappa {
+namespace peer {
+
+using dev::ceil_div;
+
+void* alloc(int64_t bytes) {
+  void* p = nullptr;
+  GB_CUDA_CHECK(cudaMalloc(&p, static_cast<size_t>(bytes > 0 ? bytes : 16)));
+  GB_CUDA_CHECK(cudaMemset(p, 0, static_cast<size_t>(bytes > 0 ? bytes : 16)));
+  return p;
+}
+void release(void* p) {
+  if (p) GB_CUDA_CHECK(cudaFree(p));
+}
+std::string ipc_handle(void* p) {
+  cudaIpcMemHandle_t h;
+  GB_CUDA_CHECK(cudaIpcGetMemHandle(&h, p));
+  return std::string(reinterpret_cast<const char*>(&h), sizeof(h));
+}
+void* ipc_open(const std::string& handle) {
+  if (handle.size() != sizeof(cudaIpcMemHandle_t)) throw std::invalid_argument("bad IPC handle size");
+  cudaIpcMemHandle_t h;
+  std::copy(handle.begin(), handle.end(), reinterpret_cast<char*>(&h));
+  void* p = nullptr;
+  GB_CUDA_CHECK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  return p;
+}
+void ipc_close(void* p) {
+  if (p) GB_CUDA_CHECK(cudaIpcCloseMemHandle(p));
+}
+
+namespace {
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void adam_update(const ArAdamArgs& a, int64_t i, float g, float step_size, float inv_sqrt_bc2) {
+  float p = a.param[i];
+  if (a.weight_decay != 0.f) g += a.weight_decay * p;
+  const float m = a.beta1 * a.m[i] + (1.f - a.beta1) * g;
+  const float v = a.beta2 * a.v[i] + (1.f - a.beta2) * g * g;
+  a.m[i] = m;
+  a.v[i] = v;
+  p -= step_size * m / (sqrtf(v) * inv_sqrt_bc2 + a.eps);
+  a.param[i] = p;
+  if (a.param_bf16) a.param_bf16[i] = __float2bfloat16_rn(p);
+}
+
+__global__ void __launch_bounds__(256) ar_adam_kernel(ArAdamArgs a) {
+  const int64_t n_chunks = ceil_div(a.n, a.chunk);
+  const int64_t step = a.counters[3];
+  const int parity = static_cast<int>(step & 1);
+  const uint32_t tag = static_cast<uint32_t>(step + 1);
+  float scale = 1.f / static_cast<float>(a.world);
+  if (a.cov) {
+    const float cn = a.cov[1];
+    scale = (cn > 0.f ? a.cov[0] / cn : 0.f) / static_cast<float>(a.world);
+  }
+  const float t = static_cast<float>(a.counters[5] + 1);
+  const float bc1 = 1.f - powf(a.beta1, t);
+  const float bc2 = 1.f - powf(a.beta2, t);
+  const float step_size = a.lr / bc1;
+  const float inv_sqrt_bc2 = rsqrtf(bc2);
+  float* send = a.send_local[parity];
+  __shared__ int s_timeout;  // sticky: after a timeout the CTA stops reducing
+  if (threadIdx.x == 0) s_timeout = 0;
+
+  for (int64_t j = blockIdx.x; j < n_chunks; j += gridDim.x) {
+    const int64_t lo = j * a.chunk;
+    const int64_t hi = min(a.n, lo + a.chunk);
+    // 1. publish
+    for (int64_t i = lo + threadIdx.x * 4; i < hi; i += blockDim.x * 4) {
+      if (i + 3 < hi) {
+        float4 g = *reinterpret_cast<float4*>(a.grad + i);
+        *reinterpret_cast<float4*>(a.grad + i) = make_float4(0.f, 0.f, 0.f, 0.f);
+        g.x *= scale; g.y *= scale; g.z *= scale; g.w *= scale;
+        *reinterpret_cast<float4*>(send + i) = g;
+      } else {
+        for (int64_t k = i; k < hi; ++k) {
+          send[k] = a.grad[k] * scale;
+          a.grad[k] = 0.f;
+        }
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      for (int p = 0; p < a.world; ++p) st_release_sys(a.flags_peer[p] + a.rank * n_chunks + j, tag);
+    }
+    // 2. wait for every rank's copy of this chunk
+    if (threadIdx.x < a.world) {
+      const uint32_t* f = a.flags_local + threadIdx.x * n_chunks + j;
+      if (static_cast<int32_t>(ld_acquire_sys(f) - tag) < 0) {
+        const uint64_t t0 = dev::globaltimer_ns();
+        uint32_t polls = 0;
+        while (static_cast<int32_t>(ld_acquire_sys(f) - tag) < 0) {
+          if ((++polls & 63u) == 0) {
+            if (dev::globaltimer_ns() - t0 > static_cast<uint64_t>(a.timeout_ns)) {
+              dev::set_error(a.err, dev::kErrPeerTimeout);
+              s_timeout = 1;
+              break;
+            }
+            __nanosleep(64);
+          }
+        }
+      }
+    }
+    __syncthreads();
+    if (s_timeout) continue;
+    // 3. reduce (rank order) + Adam
+    for (int64_t i = lo + threadIdx.x * 4; i < hi; i += blockDim.x * 4) {
+      if (i + 3 < hi) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int p = 0; p < a.world; ++p) {
+          const float4 x = *reinterpret_cast<const float4*>(a.send_peer[p][parity] + i);
+          acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
+        }
+        if (a.do_adam) {
+          adam_update(a, i, acc.x, step_size, inv_sqrt_bc2);
+          adam_update(a, i + 1, acc.y, step_size, inv_sqrt_bc2);
+          adam_update(a, i + 2, acc.z, step_size, inv_sqrt_bc2);
+          adam_update(a, i + 3, acc.w, step_size, inv_sqrt_bc2);
+        } else {
+          *reinterpret_cast<float4*>(a.grad_out + i) = acc;
+        }
+      } else {
+        for (int64_t k = i; k < hi; ++k) {
+          float acc = 0.f;
+          for (int p = 0; p < a.world; ++p) acc += a.send_peer[p][parity][k];
+          if (a.do_adam) adam_update(a, k, acc, step_size, inv_sqrt_bc2);
+          else a.grad_out[k] = acc;
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- repartition
+__global__ void pull_rows_kernel(PullRowsArgs a) {
+  const int64_t n = a.n_ptr ? *a.n_ptr : a.n;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  const int chunks = a.row_bytes >> 4;
+  for (int64_t r = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; r < n; r += warps) {
+    const int64_t g = a.gids[r];
+    int p = 0;
+    while (p + 1 < a.world && g >= a.prefix[p + 1]) ++p;
+    const int64_t row = g - a.prefix[p];
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(a.tables[p]) + row * a.table_stride * a.elem_bytes;
+    uint8_t* dst = reinterpret_cast<uint8_t*>(a.out) + (a.out_row0 + r) * a.out_stride * a.elem_bytes;
+    for (int c = lane; c < chunks; c += 32)
+      reinterpret_cast<uint4*>(dst)[c] = reinterpret_cast<const uint4*>(src)[c];
+  }
+}
+
+__global__ void copy_kernel(uint4* dst, const uint4* src, int64_t n16) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n16;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    dst[i] = src[i];
+}
+
+__global__ void mark_kernel(const int32_t* ids, const int32_t* n_ptr, int64_t n_static, uint8_t* mark) {
+  const int64_t n = n_ptr ? *n_ptr : n_static;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    mark[ids[i]] = 1;
+}
+
+__global__ void iota_map_kernel(int32_t* map, int64_t g0, int64_t count, int32_t base, uint8_t* clear_mark) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    map[g0 + i] = base + static_cast<int32_t>(i);
+    if (clear_mark) clear_mark[g0 + i] = 0;
+  }
+}
+
+constexpr int kMcThreads = 256;
+constexpr int kMcItems = 16;
+constexpr int kMcTile = kMcThreads * kMcItems;
+
+__global__ void __launch_bounds__(kMcThreads) mark_compact_kernel(uint8_t* mark, int64_t n_global, int64_t* out_ids,
+                                                                   int32_t* map, int32_t base, int32_t* n_out,
+                                                                   unsigned long long* scratch, int64_t cap_out,
+                                                                   int32_t* err) {
+  __shared__ long long s_scan[kMcThreads / 32];
+  __shared__ int s_tile;
+  __shared__ long long s_prefix;
+  const int tile = dev::LookBack::ticket(scratch, &s_tile);
+  const int64_t g0 = static_cast<int64_t>(tile) * kMcTile + threadIdx.x * kMcItems;
+  uint32_t bits = 0;
+  int cnt = 0;
+#pragma unroll
+  for (int q = 0; q < kMcItems; ++q) {
+    const int64_t g = g0 + q;
+    if (g < n_global && mark[g]) {
+      bits |= 1u << q;
+      ++cnt;
+    }
+  }
+  long long total;
+  const long long excl = dev::block_exclusive_scan<kMcThreads, long long>(cnt, s_scan, &total);
+  if ((threadIdx.x >> 5) == 0) {
+    const long long p = dev::LookBack::exclusive_prefix(scratch, tile, total, err);
+    if (dev::lane_id() == 0) s_prefix = p;
+  }
+  __syncthreads();
+  long long k = s_prefix + excl;
+#pragma unroll
+  for (int q = 0; q < kMcItems; ++q) {
+    if (!(bits & (1u << q))) continue;
+    const int64_t g = g0 + q;
+    mark[g] = 0;
+    if (k < cap_out) {
+      out_ids[k] = g;
+      map[g] = base + static_cast<int32_t>(k);
+    } else {
+      dev::set_error(err, dev::kErrCapacity);
+    }
+    ++k;
+  }
+  const int64_t last = n_global > 0 ? (n_global - 1) / kMcTile : 0;
+  if (tile == last && threadIdx.x == 0) {
+    const long long tot = s_prefix + total;
+    *n_out = static_cast<int32_t>(tot < cap_out ? tot : cap_out);
+  }
+}
+
+__global__ void csr_merge_kernel(CsrMergeArgs a) {
+  const int64_t ea0 = a.indptr_a[0], ea = a.indptr_a[a.n_a] - ea0;
+  const int64_t eb0 = a.n_b > 0 ? a.indptr_b[0] : 0;
+  const int64_t eb = a.n_b > 0 ? a.indptr_b[a.n_b] - eb0 : 0;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  if (tid == 0 && ea + eb > a.cap_edges) dev::set_error(a.err, dev::kErrCapacity);
+  for (int64_t v = tid; v <= a.n_rows_total; v += stride) {
+    int64_t o;
+    if (v <= a.n_a) o = a.indptr_a[v] - ea0;
+    else if (v <= a.n_a + a.n_b) o = ea + (a.indptr_b[v - a.n_a] - eb0);
+    else o = ea + eb;
+    a.indptr_out[v] = o < a.cap_edges ? o : a.cap_edges;
+  }
+  for (int64_t e = tid; e < ea + eb && e < a.cap_edges; e += stride) {
+    const int32_t g = e < ea ? a.indices_a[ea0 + e] : a.indices_b[eb0 + (e - ea)];
+    a.indices_out[e] = a.map[g];
+  }
+}
+
+int sm_count() {
+  static int s = 0;
+  if (!s) {
+    int d = 0;
+    cudaGetDevice(&d);
+    cudaDeviceGetAttribute(&s, cudaDevAttrMultiProcessorCount, d);
+    if (s <= 0) s = 148;
+  }
+  return s;
+}
+
+int grid_for(int64_t n, int threads, int per_sm = 8) {
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ceil_div(n > 0 ? n : 1, threads), int64_t(sm_count()) * per_sm)));
+}
+
+}  // namespace
+
+void launch_allreduce_adam(const ArAdamArgs& a, int grid, cudaStream_t stream) {
+  if (a.world < 1 || a.world > kMaxRanks) throw std::invalid_argument("world size out of range");
+  if (a.chunk % 4 != 0) throw std::invalid_argument("chunk must be a multiple of 4");
+  const int64_t n_chunks = ceil_div(a.n, a.chunk);
+  // at most one CTA per SM so that all CTAs are resident while they wait on peers
+  if (grid <= 0) grid = static_cast<int>(std::min<int64_t>(n_chunks, sm_count()));
+  grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({static_cast<int64_t>(grid), n_chunks,
+                                                                   static_cast<int64_t>(sm_count())})));
+  ar_adam_kernel<<<grid, 256, 0, stream>>>(a);
+  GB_LAUNCH_CHECK();
+}
+
+void launch_pull_rows(const PullRowsArgs& a, int64_t cap, cudaStream_t stream) {
+  if (a.row_bytes % 16 != 0) throw std::invalid_argument("pull_rows: row bytes must be a multiple of 16");
+  pull_rows_kernel<<<grid_for(cap * 32, 256, 16), 256, 0, stream>>>(a);
+  GB_LAUNCH_CHECK();
+}
+
+void launch_copy(void* dst, const void* src, int64_t bytes, cudaStream_t stream) {
+  if (bytes % 16 != 0) throw std::invalid_argument("copy: bytes must be a multiple of 16");
+  const int64_t n16 = bytes / 16;
+  if (n16 == 0) return;
+  copy_kernel<<<grid_for(n16, 256, 16), 256, 0, stream>>>(reinterpret_cast<uint4*>(dst), reinterpret_cast<const uint4*>(src), n16);
+  GB_LAUNCH_CHECK();
+}
+
+void launch_mark(const int32_t* ids, const int32_t* n_ptr, int64_t n, uint8_t* mark, cudaStream_t stream) {
+  if (n <= 0 && !n_ptr) return;
+  mark_kernel<<<grid_for(n, 256), 256, 0, stream>>>(ids, n_ptr, n, mark);
+  GB_LAUNCH_CHECK();
+}
+
+void launch_iota_map(int32_t* map, int64_t g0, int64_t count, int32_t base, uint8_t* clear_mark, cudaStream_t stream) {
+  if (count <= 0) return;
+  iota_map_kernel<<<grid_for(count, 256), 256, 0, stream>>>(map, g0, count, base, clear_mark);
+  GB_LAUNCH_CHECK();
+}
+
+int64_t mark_compact_scratch_words(int64_t n_global) { return ceil_div(n_global > 0 ? n_global : 1, kMcTile) + 1; }
+
+void launch_mark_compact(uint8_t* mark, int64_t n_global, int64_t* out_ids, int32_t* map, int32_t base, int32_t* n_out,
+                         unsigned long long* scan_scratch, int64_t cap_out, int32_t* err, cudaStream_t stream) {
+  const int64_t tiles = ceil_div(n_global > 0 ? n_global : 1, kMcTile);
+  GB_CUDA_CHECK(cudaMemsetAsync(scan_scratch, 0, sizeof(unsigned long long) * (tiles + 1), stream));
+  mark_compact_kernel<<<static_cast<unsigned>(tiles), kMcThreads, 0, stream>>>(mark, n_global, out_ids, map, base, n_out,
+                                                                             scan_scratch, cap_out, err);
+  GB_LAUNCH_CHECK();
+}
+
+void launch_csr_merge(const CsrMergeArgs& a, cudaStream_t stream) {
+  csr_merge_kernel<<<grid_for(std::max<int64_t>(a.cap_edges, a.n_rows_total + 1), 256, 16), 256, 0, stream>>>(a);
+  GB_LAUNCH_CHECK();
+}
+
+}  // namespace peer
+}  // namespace grappa

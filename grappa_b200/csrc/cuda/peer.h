@@ -1,0 +1,98 @@
+// Peer-memory data plane over NVLink 5 / NVSwitch: IPC-exported buffers, the
+// fused coverage-weighted gradient all-reduce + Adam kernel, and the repartition
+// pull kernels.  No TMA copy touches peer memory here: every remote access is an
+// ordinary ld/st.global through an IPC mapping.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+
+namespace grappa {
+namespace peer {
+
+constexpr int kMaxRanks = 8;
+
+// ---- buffers
+void* alloc(int64_t bytes);                       // cudaMalloc'd, zeroed
+void release(void* p);
+std::string ipc_handle(void* p);                  // 64-byte cudaIpcMemHandle_t
+void* ipc_open(const std::string& handle);        // maps a peer's buffer
+void ipc_close(void* p);
+
+// ---- fused all-reduce + Adam
+struct ArAdamArgs {
+  int32_t rank = 0, world = 1;
+  float* grad = nullptr;                 // local fp32 gradient, cleared after it is read
+  int64_t n = 0;
+  int32_t chunk = 4096;                  // elements per flag
+  float* send_local[2] = {nullptr, nullptr};          // this rank's two send slots
+  const float* send_peer[kMaxRanks][2] = {};          // every rank's send slots (self included)
+  uint32_t* flags_local = nullptr;                    // [world][n_chunks], written by peers
+  uint32_t* flags_peer[kMaxRanks] = {};               // every rank's flag array
+  const float* cov = nullptr;            // [sum, count] of this rank's coverage ratios (null: weight 1)
+  const int64_t* counters = nullptr;     // [seed, epoch, step, global_step, gen, adam_t]
+  // Adam
+  float* param = nullptr;
+  float* m = nullptr;
+  float* v = nullptr;
+  __nv_bfloat16* param_bf16 = nullptr;
+  float lr = 1e-3f, beta1 = 0.9f, beta2 = 0.999f, eps = 1e-8f, weight_decay = 0.f;
+  bool do_adam = true;                   // false: write the reduced gradient to grad_out
+  float* grad_out = nullptr;
+  int32_t* err = nullptr;
+  int64_t timeout_ns = 10000000000ll;
+};
+void launch_allreduce_adam(const ArAdamArgs& a, int grid, cudaStream_t stream);
+
+// ---- repartition (pull over peer memory)
+struct PullRowsArgs {
+  const void* tables[kMaxRanks] = {};    // per-rank row tables (peer mappings)
+  int64_t table_stride = 0;              // elements
+  int32_t elem_bytes = 2;
+  int32_t row_bytes = 0;                 // bytes copied per row (multiple of 16)
+  const int64_t* gids = nullptr;         // global ids of the rows to fetch
+  const int32_t* n_ptr = nullptr;
+  int64_t n = 0;
+  const int64_t* prefix = nullptr;       // device [world + 1] global id ranges
+  int32_t world = 1;
+  void* out = nullptr;
+  int64_t out_stride = 0;                // elements
+  int64_t out_row0 = 0;                  // first output row
+};
+void launch_pull_rows(const PullRowsArgs& a, int64_t cap, cudaStream_t stream);
+
+// contiguous copy (peer -> local), 16-byte vectors
+void launch_copy(void* dst, const void* src, int64_t bytes, cudaStream_t stream);
+
+// mark[g] = 1 for g in ids (global ids)
+void launch_mark(const int32_t* ids, const int32_t* n_ptr, int64_t n, uint8_t* mark, cudaStream_t stream);
+// fill map[g] = base + (g - g0) for g in [g0, g0 + count) and clear mark there
+void launch_iota_map(int32_t* map, int64_t g0, int64_t count, int32_t base, uint8_t* clear_mark, cudaStream_t stream);
+// compact the marked global ids in increasing order: out[k] = g, map[g] = base + k, *n_out = count;
+// the marks are cleared as they are consumed
+void launch_mark_compact(uint8_t* mark, int64_t n_global, int64_t* out_ids, int32_t* map, int32_t base,
+                         int32_t* n_out, unsigned long long* scan_scratch, int64_t cap_out, int32_t* err,
+                         cudaStream_t stream);
+int64_t mark_compact_scratch_words(int64_t n_global);
+// working CSR: rows [0, n_a) from graph A, [n_a, n_a + n_b) from graph B (peer), sources translated
+// through map (global -> working); rows after n_a + n_b are empty.
+struct CsrMergeArgs {
+  const int64_t* indptr_a = nullptr;
+  const int32_t* indices_a = nullptr;
+  int64_t n_a = 0;
+  const int64_t* indptr_b = nullptr;
+  const int32_t* indices_b = nullptr;
+  int64_t n_b = 0;
+  const int32_t* map = nullptr;
+  int64_t* indptr_out = nullptr;
+  int32_t* indices_out = nullptr;
+  int64_t cap_edges = 0;
+  int64_t n_rows_total = 0;              // rows of indptr_out - 1
+  int32_t* err = nullptr;
+};
+void launch_csr_merge(const CsrMergeArgs& a, cudaStream_t stream);
+
+}  // namespace peer
+}  // namespace grappa
