@@ -1,0 +1,242 @@
+"""Benchmark: seconds per epoch of mini-batch GraphSAGE on the ogbn-products-shaped graph.
+
+Workload (the headline configuration): 3-layer GraphSAGE (mean), hidden 256, bf16
+compute with fp32 master weights, fanout [15,10,5], 1024 seeds per GPU per batch,
+Adam lr 3e-3, dropout 0.5, repartition every 10 epochs; seeded RMAT graph
+(0.57,0.19,0.19,0.05) with 2,449,029 nodes and 61,859,140 undirected edges
+(123.7M directed), 100-dim N(0,1) features, 47 teacher classes, 8% train split;
+one hash partition per GPU.  Random-init weights, synthetic data.
+
+A "step" of this benchmark is one training epoch (the metric is s/epoch): every
+rank runs all of its ceil(n_train_local / 1024) mini-batches, all ranks the same
+number.  The device-timed value brackets K epochs with CUDA events after W
+warm-up epochs (barrier + synchronize on both sides, max over ranks).  The
+end-to-end value runs the same number of epochs through the public API with the
+seeds fed from pinned host memory and every step's loss copied back to the host,
+timed by the host clock.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W]
+    python -m torch.distributed.run --nproc-per-node N bench.py --gpus N ...
+    python bench.py --impl reference ...
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+BASELINE_S_PER_EPOCH = None  # no epoch time of the reference is published for this config
+
+
+def _clock_sampler(stop, samples, index):
+    cmd = ["nvidia-smi", f"--id={index}",
+           "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+           "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+           "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+           "--format=csv,noheader,nounits", "-lms", "200"]
+    try:
+        p = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+    except OSError:
+        return
+    try:
+        while not stop.is_set():
+            line = p.stdout.readline()
+            if not line:
+                break
+            samples.append(line.strip())
+    finally:
+        p.terminate()
+        try:
+            p.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            p.kill()
+
+
+def _summarise_clocks(samples):
+    mhz, mx, reasons = [], None, set()
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    for s in samples:
+        f = [x.strip() for x in s.split(",")]
+        if len(f) < 8:
+            continue
+        try:
+            mhz.append(float(f[0]))
+            mx = float(f[1])
+        except ValueError:
+            continue
+        for name, val in zip(names, f[4:8]):
+            if val.lower().startswith("active"):
+                reasons.add(name)
+    mhz.sort()
+    med = mhz[len(mhz) // 2] if mhz else None
+    return {"sm_mhz": med, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(mhz)}
+
+
+REFERENCE_UNAVAILABLE = (
+    "reference does not install offline: pip install of the reference fails at its CMake configure step "
+    "(third_party modules parallel-hashmap, easylogging and pcg_cpp are not in the repository; libnuma, "
+    "libunwind and DGL 1.x are not installed)")
+
+
+def run_reference(args):
+    ref = os.path.join(os.path.dirname(os.path.abspath(__file__)), "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "t10n")):
+        print(json.dumps({"impl": "reference", "unavailable": REFERENCE_UNAVAILABLE}))
+        return 0
+    print(json.dumps({"impl": "reference", "unavailable": REFERENCE_UNAVAILABLE + "; DGL is absent"}))
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10, help="timed epochs")
+    ap.add_argument("--warmup", type=int, default=3, help="warm-up epochs")
+    ap.add_argument("--impl", default="grappa", choices=["grappa", "reference"])
+    ap.add_argument("--config", default="ogbpr")
+    ap.add_argument("--no-graph", action="store_true", help="disable CUDA graph capture")
+    ap.add_argument("--no-fused-ar", action="store_true", help="use the NCCL gradient path")
+    ap.add_argument("--skip-e2e", action="store_true")
+    ap.add_argument("--eval", action="store_true", help="report validation/test accuracy after training")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+    import torch.nn.functional as F
+
+    from grappa_b200.dataset import synthetic as S
+    from grappa_b200.graph_store import partition_from_global
+    from grappa_b200.models import SAGE
+    from grappa_b200.parallel.comm import Comm, init_distributed
+    from grappa_b200.trainer import MiniBatchTrainer
+
+    rank, world = init_distributed("nccl" if args.gpus > 1 else None)
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    comm = Comm()
+
+    spec = S.SPECS[args.config]
+    t0 = time.time()
+    graph = S.build(spec, device)
+    own = partition_from_global(graph, world, rank, device, part_seed=spec.seed)
+    del graph
+    torch.cuda.empty_cache()
+    t_setup = time.time() - t0
+
+    torch.manual_seed(1234)
+    model = SAGE(spec.feat_dim, 256, spec.n_classes, 3, F.relu, 0.5)
+    trainer = MiniBatchTrainer(model, own, [15, 10, 5], 1024, lr=3e-3, repart_every=10, comm=comm, seed=7,
+                               fused_allreduce=not args.no_fused_ar, use_cuda_graph=not args.no_graph)
+    trainer.warmup()
+    launches_per_step = trainer.engine.launches_per_step
+    for e in range(args.warmup):
+        trainer.train_epoch(e)
+    torch.cuda.synchronize()
+    trainer.engine.check_errors()
+
+    def max_over_ranks(x):
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-timed epochs
+    stop, samples = threading.Event(), []
+    th = threading.Thread(target=_clock_sampler, args=(stop, samples, local), daemon=True)
+    th.start()
+    e0 = args.warmup
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for e in range(e0, e0 + args.steps):
+        trainer.train_epoch(e)
+    ev1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms_dev = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
+    stop.set()
+    th.join(timeout=10)
+    clocks = _summarise_clocks(samples)
+    trainer.engine.check_errors()
+
+    # ---- end to end through the public API (pinned host seeds in, loss out, host clock)
+    e2e = None
+    e1 = e0 + args.steps
+    if not args.skip_e2e:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        loss = None
+        for e in range(e1, e1 + args.steps):
+            loss = trainer.train_epoch(e, host_feed=True)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        s_e2e = max_over_ranks((time.perf_counter() - t0) / args.steps)
+        e2e = {"value": round(s_e2e, 6), "unit": "s/epoch",
+               "h2d_bytes_per_step": trainer.batch_size * 4 + 4, "d2h_bytes_per_step": 4,
+               "last_mean_loss": None if loss is None else round(loss, 5)}
+        trainer.engine.check_errors()
+
+    acc = None
+    if args.eval:
+        acc = {"val_acc": round(trainer.evaluate(own.val_mask), 4),
+               "test_acc": round(trainer.evaluate(own.test_mask), 4),
+               "epochs_trained": e1 + (0 if args.skip_e2e else args.steps)}
+
+    out = {
+        "metric": "s/epoch (device-timed, max over ranks) @1/2/4/8 GPU, SAGE 2.45M-node; test acc",
+        "value": round(ms_dev / 1000.0, 6),
+        "unit": "s/epoch",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_dev, 4),
+        "higher_is_better": False,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded RMAT graph, N(0,1) features, teacher labels; random-init weights)",
+        "config": {
+            "model": "GraphSAGE-mean 3 layers, hidden 256, fanout [15,10,5], dropout 0.5, Adam lr 3e-3",
+            "graph": f"RMAT {spec.n_nodes} nodes / {2 * spec.n_edges} directed edges, {spec.feat_dim}-dim, "
+                     f"{spec.n_classes} classes, 8% train",
+            "global_batch": trainer.batch_size * world,
+            "seq_len": None,
+            "seeds_per_gpu_per_batch": trainer.batch_size,
+            "mini_batches_per_epoch": trainer.n_batches,
+            "parallelism": f"partition-parallel x{world} (one hash partition per GPU; coverage-weighted gradient "
+                           f"all-reduce{' + Adam fused over NVLink peer memory' if world > 1 and not args.no_fused_ar else ''})",
+            "repart_every": 10,
+            "l2": "inputs larger than L2 (feature table and CSR about 1 GB per GPU); no flush",
+            "step": "one benchmark step = one epoch",
+            "setup_s": round(t_setup, 2),
+        },
+        "clocks": clocks,
+        "e2e": e2e,
+        "gpu_launches": int(launches_per_step * trainer.n_batches * args.steps + args.steps),
+    }
+    if acc:
+        out["accuracy"] = acc
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    trainer.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

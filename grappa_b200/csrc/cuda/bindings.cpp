@@ -6,7 +6,7 @@
 
 #include <optional>
 
-#include "common.cuh"
+#include "cuda_check.h"
 #include "kernels.h"
 #include "peer.h"
 

@@ -8,15 +8,7 @@
 #include <stdexcept>
 #include <string>
 
-#define GB_CUDA_CHECK(expr)                                                                  \
-  do {                                                                                       \
-    cudaError_t _e = (expr);                                                                 \
-    if (_e != cudaSuccess)                                                                   \
-      throw std::runtime_error(std::string("CUDA error ") + cudaGetErrorString(_e) + " at " + \
-                               __FILE__ + ":" + std::to_string(__LINE__));                  \
-  } while (0)
-
-#define GB_LAUNCH_CHECK() GB_CUDA_CHECK(cudaGetLastError())
+#include "cuda_check.h"
 
 namespace grappa {
 namespace dev {
