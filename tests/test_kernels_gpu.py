@@ -1,0 +1,325 @@
+"""GPU numerics tests of the sm_100a kernels: each one is compared with a plain
+PyTorch fp32 reference of the same op (or, for sampling, with the exact-replay
+CPU oracle of the host engine)."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from grappa_b200 import _native
+from grappa_b200.block import Block
+from grappa_b200.ops import ref
+from grappa_b200.sampler_gpu import GpuNeighborSampler, new_counters
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def cu():
+    return _native.cuda()
+
+
+def host_graph(n=2000, m=30000, seed=0):
+    rng = np.random.default_rng(seed)
+    u = rng.integers(0, n, m)
+    v = rng.integers(0, n, m)
+    v[: m // 5] = rng.integers(0, 8, m // 5)  # hubs
+    u2 = np.concatenate([u, v, np.arange(n)])
+    v2 = np.concatenate([v, u, np.arange(n)])
+    g = _native.host().graph.HostGraph(u2, v2, n)
+    ip = torch.from_numpy(g.indptr()).to(DEV)
+    ix = torch.from_numpy(g.indices()).to(torch.int32).to(DEV)
+    return g, ip, ix, n
+
+
+def err_tensor():
+    return torch.zeros(1, dtype=torch.int32, device=DEV)
+
+
+# ----------------------------------------------------------------------------- sampling
+def _compare_blocks(gpu_blocks, ref_blocks):
+    for h, rb in enumerate(ref_blocks):
+        b = gpu_blocks[len(gpu_blocks) - 1 - h]
+        assert b.n_dst == rb["n_dst"] and b.n_src == rb["n_src"], (h, b, rb["n_dst"], rb["n_src"])
+        np.testing.assert_array_equal(b.indptr.cpu().numpy(), rb["indptr"])
+        np.testing.assert_array_equal(b.indices.cpu().numpy(), rb["indices"])
+        np.testing.assert_array_equal(b.srcdata["_ID"].cpu().numpy(), rb["src_nid"])
+        np.testing.assert_array_equal(b.src_sampled.cpu().numpy(), rb["src_sampled"])
+
+
+def test_sampler_matches_cpu_oracle_exactly():
+    g, ip, ix, n = host_graph()
+    fan = [15, 10, 5]
+    seeds = np.arange(0, 1536, 6, dtype=np.int64)
+    sm = GpuNeighborSampler(fan, 256, n, DEV)
+    counters = new_counters(11, DEV)
+    gideg_all = torch.full((n,), 30, dtype=torch.int64, device=DEV)
+    for step in range(3):  # three calls: exercises the tagged map across generations
+        counters[1], counters[2] = 2, step
+        cov = torch.zeros(2, device=DEV)
+        sm.load_seeds(torch.from_numpy(seeds))
+        sm.sample(ip, ix, counters, gideg=gideg_all, cov=cov)
+        cu().step_end(counters)  # advances the generation of the compaction tags
+        torch.cuda.synchronize()
+        assert sm.err.item() == 0
+        rb, cs, cn = _native.host().graph.sample_batch(g, fan, seeds, np.full(len(seeds), 30), 11, 2, step, False)
+        _compare_blocks(sm.blocks(), rb)
+        assert abs(cov[0].item() - cs) < 1e-2 and cov[1].item() == cn
+
+
+def test_sampler_partial_batch_and_frontier():
+    g, ip, ix, n = host_graph(seed=1)
+    fan = [3, 4]
+    seeds = np.array([5, 17, 100, 3, 1999, 0, 7], dtype=np.int64)
+    sm = GpuNeighborSampler(fan, 64, n, DEV)
+    counters = new_counters(3, DEV)
+    sm.load_seeds(torch.from_numpy(seeds))
+    sm.sample(ip, ix, counters)
+    torch.cuda.synchronize()
+    rb, _, _ = _native.host().graph.sample_batch(g, fan, seeds, None, 3, 0, 0, False)
+    _compare_blocks(sm.blocks(), rb)
+
+
+# ----------------------------------------------------------------------------- GEMM
+def bf(x):
+    return x.to(torch.bfloat16)
+
+
+def run_gemm(A, a_mn, B, b_mn, M_cap, M_dev, N, K_cap, K_dev, splits, C, mode, bias=None, act=0, p=0.0,
+             counters=None, salt=0, labels=None, n_classes=0, dl=None, loss=None, correct=None, n_rows=None,
+             dbias=None, bn=256):
+    err = err_tensor()
+    cu().gemm(A, a_mn, B, b_mn, M_cap, M_dev, N, K_cap, K_dev, splits, C, mode, bias, act, p, counters, salt,
+              labels, n_classes, dl, loss, correct, None, n_rows, dbias, err, bn)
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    return C
+
+
+@pytest.mark.parametrize("M,K,N,bn", [(300, 208, 256, 256), (1000, 512, 48, 48), (129, 64, 64, 64),
+                                      (257, 200, 128, 128), (5000, 512, 256, 256)])
+def test_gemm_kmajor_bias_relu(M, K, N, bn):
+    torch.manual_seed(0)
+    cap = (M + 127) // 128 * 128 + 128
+    A = bf(torch.randn(cap, K, device=DEV))
+    B = bf(torch.randn(N, K, device=DEV) / math.sqrt(K))
+    bias = torch.randn(N, device=DEV)
+    C = torch.full((cap, N), 7.0, device=DEV, dtype=torch.bfloat16)
+    Mdev = torch.tensor([M], dtype=torch.int32, device=DEV)
+    run_gemm(A, False, B, False, cap, Mdev, N, K, None, 1, C, 0, bias=bias, act=1, bn=bn)
+    want = torch.relu(A[:M].float() @ B.float().t() + bias)
+    torch.testing.assert_close(C[:M].float(), want, rtol=2e-2, atol=2e-2)
+    assert bool((C[M:] == 7).all())
+
+
+def test_gemm_dropout_matches_host_mask():
+    torch.manual_seed(1)
+    M, K, N, p = 256, 128, 256, 0.5
+    A = bf(torch.randn(M, K, device=DEV))
+    B = bf(torch.randn(N, K, device=DEV) / math.sqrt(K))
+    bias = torch.zeros(N, device=DEV)
+    C = torch.zeros((M, N), device=DEV, dtype=torch.bfloat16)
+    counters = new_counters(21, DEV)
+    counters[1], counters[2] = 4, 9
+    run_gemm(A, False, B, False, M, None, N, K, None, 1, C, 0, bias=bias, act=1, p=p, counters=counters, salt=2)
+    mask = torch.from_numpy(_native.host().dropout_mask(21, 4, 9, 2, M, N, N, p)).view(M, N).to(DEV).float()
+    want = torch.relu(A.float() @ B.float().t()) * mask / (1 - p)
+    torch.testing.assert_close(C.float(), want, rtol=2e-2, atol=3e-2)
+
+
+@pytest.mark.parametrize("Mo,Kx,R,live,splits", [(48, 208, 700, 650, 3), (256, 512, 4096, 4000, 8),
+                                                 (256, 208, 130, 100, 1)])
+def test_gemm_dw_mn_major_split_k(Mo, Kx, R, live, splits):
+    torch.manual_seed(2)
+    dY = bf(torch.randn(R, Mo, device=DEV))
+    dY[live:] = 0
+    X = bf(torch.randn(R, Kx, device=DEV))
+    C = torch.zeros((Mo, Kx), device=DEV, dtype=torch.float32)
+    Kdev = torch.tensor([live], dtype=torch.int32, device=DEV)
+    run_gemm(dY, True, X, True, Mo, None, Kx, R, Kdev, splits, C, 2, bn=256)
+    want = dY[:live].float().t() @ X[:live].float()
+    torch.testing.assert_close(C, want, rtol=1e-2, atol=5e-2)
+
+
+@pytest.mark.parametrize("R,live,No,Kx", [(700, 650, 48, 512), (300, 300, 256, 512), (128, 77, 256, 208)])
+def test_gemm_dx_mn_major_b(R, live, No, Kx):
+    torch.manual_seed(3)
+    dY = bf(torch.randn(R, No, device=DEV))
+    W = bf(torch.randn(No, Kx, device=DEV) / math.sqrt(No))
+    C = torch.full((R, Kx), 3.0, device=DEV, dtype=torch.bfloat16)
+    Mdev = torch.tensor([live], dtype=torch.int32, device=DEV)
+    run_gemm(dY, False, W, True, R, Mdev, Kx, No, None, 1, C, 0, bn=256)
+    want = dY[:live].float() @ W.float()
+    torch.testing.assert_close(C[:live].float(), want, rtol=2e-2, atol=2e-2)
+
+
+def test_gemm_cross_entropy_epilogue():
+    torch.manual_seed(4)
+    M, cap, K, N, n_cls = 1000, 1152, 512, 48, 47
+    X = bf(torch.randn(cap, K, device=DEV))
+    W = bf(torch.randn(N, K, device=DEV) / math.sqrt(K))
+    W[n_cls:] = 0
+    bias = torch.randn(N, device=DEV) * 0.1
+    labels = torch.randint(0, n_cls, (cap,), dtype=torch.int32, device=DEV)
+    dl = torch.full((cap, N), 5.0, device=DEV, dtype=torch.bfloat16)
+    loss = torch.zeros(1, device=DEV)
+    correct = torch.zeros(1, dtype=torch.int32, device=DEV)
+    dbias = torch.zeros(N, device=DEV)
+    n_rows = torch.tensor([M], dtype=torch.int32, device=DEV)
+    dummy = torch.zeros((1, 1), device=DEV)
+    run_gemm(X, False, W, False, cap, n_rows, N, K, None, 1, dummy, 3, bias=bias, labels=labels, n_classes=n_cls,
+             dl=dl, loss=loss, correct=correct, n_rows=n_rows, dbias=dbias, bn=48)
+    logits = (X[:M].float() @ W.float().t() + bias)[:, :n_cls].requires_grad_(True)
+    ce = torch.nn.functional.cross_entropy(logits, labels[:M].long())
+    ce.backward()
+    assert abs(loss.item() - ce.item()) < 2e-2 * max(1.0, ce.item())
+    torch.testing.assert_close(dl[:M, :n_cls].float(), logits.grad, rtol=3e-2, atol=2e-5)
+    assert bool((dl[:M, n_cls:] == 0).all())
+    assert bool((dl[M:(M + 63) // 64 * 64] == 0).all())
+    assert abs(correct.item() - int((logits.argmax(1) == labels[:M].long()).sum())) <= 3
+    torch.testing.assert_close(dbias[:n_cls], logits.grad.sum(0), rtol=5e-2, atol=5e-4)
+
+
+# ----------------------------------------------------------------------------- aggregation
+def random_block(n_dst, n_src, max_deg, seed):
+    g = torch.Generator().manual_seed(seed)
+    deg = torch.randint(0, max_deg + 1, (n_dst,), generator=g)
+    indptr = torch.zeros(n_dst + 1, dtype=torch.int32)
+    indptr[1:] = torch.cumsum(deg, 0)
+    indices = torch.randint(0, n_src, (int(indptr[-1]),), generator=g, dtype=torch.int32)
+    src = torch.arange(n_src, dtype=torch.int32)
+    return Block(indptr, indices, src, n_dst, n_src)
+
+
+@pytest.mark.parametrize("mode,dim", [("mean", 104), ("mean", 256), ("sum", 64), ("gcn", 256), ("weighted", 600)])
+def test_aggregate_forward(mode, dim):
+    b = random_block(300, 1000, 20, 5)
+    torch.manual_seed(5)
+    h = bf(torch.randn(1000, dim))
+    modes = {"mean": 0, "sum": 1, "gcn": 2, "weighted": 3}
+    ew = torch.rand(b.num_edges()) if mode == "weighted" else None
+    snorm = ref.gcn_src_norm(b) if mode == "gcn" else None
+    out = torch.zeros((300, 2 * dim), dtype=torch.bfloat16, device=DEV)
+    err = err_tensor()
+    n_dev = torch.tensor([300], dtype=torch.int32, device=DEV)
+    cu().aggregate(b.indptr.to(DEV), b.indices.to(DEV), n_dev, 0, 300, h.to(DEV), None, dim, modes[mode],
+                   None if ew is None else ew.to(DEV), None if snorm is None else snorm.to(DEV), None, out, dim, 0,
+                   0.0, 0, err)
+    torch.cuda.synchronize()
+    want = ref.aggregate(b, h.float(), mode, edge_weight=ew, src_norm=snorm)
+    torch.testing.assert_close(out[:, dim:].float().cpu(), want, rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(out[:, :dim].float().cpu(), h[:300].float())
+
+
+def test_aggregate_through_src_map():
+    b = random_block(200, 500, 12, 6)
+    table = bf(torch.randn(5000, 104))
+    src_map = torch.randperm(5000)[:500].to(torch.int32)
+    out = torch.zeros((256, 208), dtype=torch.bfloat16, device=DEV)
+    err = err_tensor()
+    n_dev = torch.tensor([200], dtype=torch.int32, device=DEV)
+    cu().aggregate(b.indptr.to(DEV), b.indices.to(DEV), n_dev, 0, 256, table.to(DEV), src_map.to(DEV), 104, 0,
+                   None, None, None, out, 104, 0, 0.0, 0, err)
+    torch.cuda.synchronize()
+    h = table[src_map.long()].float()
+    torch.testing.assert_close(out[:200, 104:].float().cpu(), ref.aggregate(b, h, "mean"), rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(out[:200, :104].float().cpu(), h[:200])
+
+
+@pytest.mark.parametrize("mode,dim", [("mean", 256), ("sum", 64), ("gcn", 128), ("weighted", 104)])
+def test_aggregate_backward(mode, dim):
+    b = random_block(300, 900, 16, 7)
+    torch.manual_seed(7)
+    h = torch.randn(900, dim, requires_grad=True)
+    modes = {"mean": 0, "sum": 1, "gcn": 2, "weighted": 3}
+    ew = torch.rand(b.num_edges()) if mode == "weighted" else None
+    snorm = ref.gcn_src_norm(b) if mode == "gcn" else None
+    out = torch.cat([h[:300], ref.aggregate(b, h, mode, edge_weight=ew, src_norm=snorm)], 1)
+    dout = bf(torch.randn(300, 2 * dim))
+    out.backward(dout.float())
+    dsrc = torch.zeros((900, dim), device=DEV)
+    err = err_tensor()
+    n_dev = torch.tensor([300], dtype=torch.int32, device=DEV)
+    cu().aggregate_bwd(b.indptr.to(DEV), b.indices.to(DEV), n_dev, 0, 300, dout.to(DEV), dim, 0, 0.0, dim,
+                       modes[mode], None if ew is None else ew.to(DEV), None if snorm is None else snorm.to(DEV), None,
+                       dsrc, err)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(dsrc.cpu(), h.grad, rtol=1e-3, atol=1e-3)
+
+
+def test_act_bwd_mask_bias_and_clear():
+    torch.manual_seed(8)
+    R, n, dim = 700, 613, 256
+    dh = torch.randn(R, dim, device=DEV)
+    dh_copy = dh.clone()
+    h = bf(torch.relu(torch.randn(R, dim, device=DEV)))
+    dy = torch.full((R, dim), 9.0, device=DEV, dtype=torch.bfloat16)
+    dbias = torch.zeros(dim, device=DEV)
+    n_dev = torch.tensor([n], dtype=torch.int32, device=DEV)
+    cu().act_bwd(dh, h, dy, n_dev, 0, dim, 2.0, dbias, R)
+    torch.cuda.synchronize()
+    want = torch.where(h[:n] != 0, dh_copy[:n] * 2.0, torch.zeros_like(dh_copy[:n]))
+    torch.testing.assert_close(dy[:n].float(), want, rtol=1e-2, atol=1e-2)
+    assert bool((dy[n:(n + 63) // 64 * 64] == 0).all())
+    assert bool((dh[:n] == 0).all())
+    torch.testing.assert_close(dbias, bf(want).float().sum(0), rtol=1e-4, atol=1e-3)
+
+
+def test_gather_rows():
+    table = torch.randn(3000, 104, device=DEV)
+    ids = torch.randint(0, 3000, (500,), dtype=torch.int32, device=DEV)
+    out = torch.zeros((512, 104), dtype=torch.bfloat16, device=DEV)
+    cu().gather_rows(table, ids, None, 500, 512, 104, out)
+    torch.testing.assert_close(out[:500].float(), bf(table[ids.long()]).float())
+
+
+# ----------------------------------------------------------------------------- optimizer
+def test_adam_matches_torch():
+    torch.manual_seed(9)
+    n = 10000
+    p0 = torch.randn(n)
+    p_ref = torch.nn.Parameter(p0.clone())
+    opt = torch.optim.Adam([p_ref], lr=3e-3)
+    param, m, v = p0.clone().to(DEV), torch.zeros(n, device=DEV), torch.zeros(n, device=DEV)
+    wbf = torch.zeros(n, dtype=torch.bfloat16, device=DEV)
+    counters = new_counters(0, DEV)
+    for _ in range(3):
+        g = torch.randn(n)
+        p_ref.grad = g.clone()
+        opt.step()
+        grad = g.to(DEV)
+        cu().adam(param, m, v, grad, wbf, 3e-3, 0.9, 0.999, 1e-8, 0.0, counters, 1.0, None, True)
+        cu().step_end(counters)
+        torch.cuda.synchronize()
+        assert bool((grad == 0).all())
+    torch.testing.assert_close(param.cpu(), p_ref.detach(), rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(wbf.float().cpu(), bf(p_ref.detach()).float())
+
+
+def test_fused_allreduce_adam_single_rank():
+    from grappa_b200.engine import FusedAllReduceAdam
+    from grappa_b200.parallel.comm import Comm
+
+    torch.manual_seed(10)
+    n = 50000
+    p0 = torch.randn(n)
+    p_ref = torch.nn.Parameter(p0.clone())
+    opt = torch.optim.Adam([p_ref], lr=1e-2)
+    ar = FusedAllReduceAdam(Comm(), n, chunk=4096)
+    param, m, v = p0.clone().to(DEV), torch.zeros(n, device=DEV), torch.zeros(n, device=DEV)
+    counters = new_counters(0, DEV)
+    err = err_tensor()
+    cov = torch.tensor([16.0, 20.0], device=DEV)  # c_r = 0.8
+    for _ in range(4):
+        g = torch.randn(n)
+        p_ref.grad = g * 0.8
+        opt.step()
+        grad = g.to(DEV)
+        ar.step(grad, cov, counters, param, m, v, None, 1e-2, 0.9, 0.999, 1e-8, err)
+        cu().step_end(counters)
+        torch.cuda.synchronize()
+        assert err.item() == 0
+    torch.testing.assert_close(param.cpu(), p_ref.detach(), rtol=1e-5, atol=1e-6)
+    ar.close()
