@@ -190,3 +190,80 @@ int sample_scan_scratch_words(int cap_dst) {
 
 }  // namespace dev
 }  // namespace grappa
+
+// ---------------------------------------------------------------------------------------
+// Allocation-free entry point (declared and documented in sample_noalloc.h; it has no
+// counterpart in the reference).  Same kernel as launch_sample_hop; the look-back scan
+// scratch is the file-scope device array below instead of a caller-allocated buffer.
+#include <mutex>
+
+#include "sample_noalloc.h"
+
+namespace {
+constexpr int kNoAllocScratchWords = kGrappaNoAllocMaxDst / 256 + 1;  // tile statuses + ticket
+constexpr int kNoAllocMaxDevices = 128;
+std::mutex g_noalloc_mu;
+unsigned long long* g_noalloc_dev_ptr[kNoAllocMaxDevices] = {};
+}  // namespace
+
+// The scratch: every GPU that loads this library holds these 32 KiB until exit.  In host
+// code the name is only a stand-in; its device address comes from cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned long long g_noalloc_scan_scratch[kNoAllocScratchWords];
+
+extern "C" __attribute__((visibility("default"))) int grappa_sample_hop_noalloc_max_dst(void) {
+  return kGrappaNoAllocMaxDst;
+}
+
+extern "C" __attribute__((visibility("default"))) int grappa_sample_hop_noalloc(
+    const int64_t* indptr, const int32_t* indices, int64_t n_graph_nodes, const int32_t* dst_nid, int32_t n_dst,
+    const uint8_t* frontier, int32_t fanout, int32_t replace, const int64_t* counters, int32_t hop,
+    const int64_t* gideg, float* cov_accum, int32_t* out_indptr, int32_t* out_nbr, int32_t cap_edges,
+    int32_t* n_edges_out, int32_t* err, void* stream) {
+  static_assert(grappa::dev::kThreads == 256, "scratch sizing assumes 256-node tiles");
+  if (n_dst < 0 || n_dst > kGrappaNoAllocMaxDst) return GRAPPA_NOALLOC_TOO_MANY_DST;
+  if (!indptr || !indices || !dst_nid || !counters || !out_indptr || !n_edges_out || n_graph_nodes < 0 ||
+      cap_edges < 0 || (cap_edges > 0 && !out_nbr))
+    return GRAPPA_NOALLOC_BAD_ARGUMENT;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return GRAPPA_NOALLOC_SETUP_FAILED;
+  unsigned long long* scratch = nullptr;
+  {
+    // once per device, with that device current: the device address of the array
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_dev_ptr[dev]) {
+      void* p = nullptr;
+      if (cudaGetSymbolAddress(&p, g_noalloc_scan_scratch) != cudaSuccess || p == nullptr)
+        return GRAPPA_NOALLOC_SETUP_FAILED;
+      g_noalloc_dev_ptr[dev] = static_cast<unsigned long long*>(p);
+    }
+    scratch = g_noalloc_dev_ptr[dev];
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int tiles = static_cast<int>(grappa::dev::ceil_div(n_dst > 0 ? n_dst : 1, 256));
+  // the array keeps the previous call's contents: the scan needs it zeroed
+  if (cudaMemsetAsync(scratch, 0, sizeof(unsigned long long) * (tiles + 1), s) != cudaSuccess)
+    return GRAPPA_NOALLOC_LAUNCH_FAILED;
+  grappa::dev::SampleHopArgs a;
+  a.indptr = indptr;
+  a.indices = indices;
+  a.n_graph_nodes = n_graph_nodes;
+  a.dst_nid = dst_nid;
+  a.n_dst_ptr = nullptr;
+  a.n_dst = n_dst;
+  a.frontier = frontier;
+  a.fanout = fanout;
+  a.replace = replace != 0;
+  a.counters = counters;
+  a.hop = hop;
+  a.gideg = gideg;
+  a.cov_accum = cov_accum;
+  a.out_indptr = out_indptr;
+  a.out_nbr = out_nbr;
+  a.cap_edges = cap_edges;
+  a.n_edges_out = n_edges_out;
+  a.scan_scratch = scratch;
+  a.err = err;
+  grappa::dev::sample_hop_kernel<<<tiles, 256, 0, s>>>(a);
+  if (cudaGetLastError() != cudaSuccess) return GRAPPA_NOALLOC_LAUNCH_FAILED;
+  return GRAPPA_NOALLOC_OK;
+}
