@@ -159,13 +159,15 @@ struct Smem {
   static constexpr int kBRows = BN <= 64 ? 64 : BN;  // MN-major B needs 64-wide chunks
   static constexpr int kBBytes = kBRows * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = (200 * 1024) / kStageBytes > 6 ? 6 : (200 * 1024) / kStageBytes;
+  // ~96 KB of ring per CTA: two CTAs fit on an SM, so one CTA's epilogue overlaps the
+  // other's loads and MMAs (each CTA holds at most 256 of the SM's 512 TMEM columns)
+  static constexpr int kStages = (96 * 1024) / kStageBytes > 6 ? 6 : (96 * 1024) / kStageBytes;
   static constexpr int kTmemCols = BN <= 32 ? 32 : (BN <= 64 ? 64 : (BN <= 128 ? 128 : 256));
   static constexpr int kBytes = kStages * kStageBytes + 1024 /*align*/;
 };
 
 template <int BN, bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs a) {
   using S = Smem<BN>;
   constexpr int kStages = S::kStages;
@@ -283,6 +285,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t trow = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
     if (a.c_mode == kCrossEntropy) {
+     if constexpr (BN <= 64) {  // only narrow tiles carry the whole row in registers
       // BN >= n_classes; the whole row is in this thread's registers
       float v[BN];
 #pragma unroll
@@ -352,6 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (arg == y) atomicAdd(a.correct, 1);
         if (a.pred_out) a.pred_out[m] = arg;
       }
+     }
     } else {
       const uint64_t key = a.counters ? hop_key(static_cast<uint64_t>(a.counters[0]) ^ 0xD80Full,
                                                 static_cast<uint64_t>(a.counters[1]),

@@ -25,6 +25,9 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
+// destination nodes per CTA: 8 warps share 64 nodes, so that enough warps are in
+// flight to hide the dependent indptr -> indices loads of every node
+constexpr int kTileNodes = 64;
 constexpr int kSmemAcc = 64;  // accepted offsets kept in shared memory up to this fanout
 
 __device__ __forceinline__ uint64_t step_key(const int64_t* counters, int hop) {
@@ -66,9 +69,9 @@ __device__ void warp_pick_distinct(uint64_t key, uint64_t nid, uint32_t d, uint3
 
 __global__ void __launch_bounds__(kThreads) sample_hop_kernel(SampleHopArgs a) {
   __shared__ long long s_scan[kWarps];
-  __shared__ long long s_off[kThreads];
-  __shared__ int32_t s_pick[kThreads];
-  __shared__ int32_t s_nid[kThreads];
+  __shared__ long long s_off[kTileNodes];
+  __shared__ int32_t s_pick[kTileNodes];
+  __shared__ int32_t s_nid[kTileNodes];
   __shared__ int32_t s_acc[kWarps][kSmemAcc];
   __shared__ int s_tile;
   __shared__ long long s_prefix;
@@ -76,8 +79,8 @@ __global__ void __launch_bounds__(kThreads) sample_hop_kernel(SampleHopArgs a) {
 
   const int tile = LookBack::ticket(a.scan_scratch, &s_tile);
   const int n_dst = a.n_dst_ptr ? *a.n_dst_ptr : a.n_dst;
-  const int i = tile * kThreads + threadIdx.x;
-  const bool valid = i < n_dst;
+  const int i = tile * kTileNodes + threadIdx.x;
+  const bool valid = threadIdx.x < kTileNodes && i < n_dst;
   int32_t nid = -1;
   int64_t deg = 0;
   int32_t pick = 0;
@@ -126,13 +129,15 @@ __global__ void __launch_bounds__(kThreads) sample_hop_kernel(SampleHopArgs a) {
   }
   __syncthreads();
   const long long off = s_prefix + excl;
-  s_off[threadIdx.x] = off;
-  s_pick[threadIdx.x] = pick;
-  s_nid[threadIdx.x] = nid;
+  if (threadIdx.x < kTileNodes) {
+    s_off[threadIdx.x] = off;
+    s_pick[threadIdx.x] = pick;
+    s_nid[threadIdx.x] = nid;
+  }
   if (valid) a.out_indptr[i] = static_cast<int32_t>(off < a.cap_edges ? off : a.cap_edges);
   const long long tile_end = s_prefix + total;
   // the tile holding the last destination (or tile 0 when there is none) writes the total
-  const int last_tile = n_dst > 0 ? (n_dst - 1) / kThreads : 0;
+  const int last_tile = n_dst > 0 ? (n_dst - 1) / kTileNodes : 0;
   if (tile == last_tile && threadIdx.x == 0) {
     if (tile_end > a.cap_edges) set_error(a.err, kErrCapacity);
     const int32_t tot = static_cast<int32_t>(tile_end > a.cap_edges ? a.cap_edges : tile_end);
@@ -145,7 +150,7 @@ __global__ void __launch_bounds__(kThreads) sample_hop_kernel(SampleHopArgs a) {
   const uint64_t key = step_key(a.counters, a.hop);
   const int w = threadIdx.x >> 5;
   const uint32_t lane = lane_id();
-  for (int r = w; r < kThreads; r += kWarps) {
+  for (int r = w; r < kTileNodes; r += kWarps) {
     const int32_t k = s_pick[r];
     if (k == 0) continue;
     const long long o = s_off[r];
@@ -178,14 +183,14 @@ __global__ void __launch_bounds__(kThreads) sample_hop_kernel(SampleHopArgs a) {
 }  // namespace
 
 void launch_sample_hop(const SampleHopArgs& a, int cap_dst, cudaStream_t stream) {
-  const int tiles = static_cast<int>(ceil_div(cap_dst > 0 ? cap_dst : 1, kThreads));
+  const int tiles = static_cast<int>(ceil_div(cap_dst > 0 ? cap_dst : 1, kTileNodes));
   GB_CUDA_CHECK(cudaMemsetAsync(a.scan_scratch, 0, sizeof(unsigned long long) * (tiles + 1), stream));
   sample_hop_kernel<<<tiles, kThreads, 0, stream>>>(a);
   GB_LAUNCH_CHECK();
 }
 
 int sample_scan_scratch_words(int cap_dst) {
-  return static_cast<int>(ceil_div(cap_dst > 0 ? cap_dst : 1, kThreads)) + 1;
+  return static_cast<int>(ceil_div(cap_dst > 0 ? cap_dst : 1, kTileNodes)) + 1;
 }
 
 }  // namespace dev
@@ -200,13 +205,13 @@ int sample_scan_scratch_words(int cap_dst) {
 #include "sample_noalloc.h"
 
 namespace {
-constexpr int kNoAllocScratchWords = kGrappaNoAllocMaxDst / 256 + 1;  // tile statuses + ticket
+constexpr int kNoAllocScratchWords = kGrappaNoAllocMaxDst / grappa::dev::kTileNodes + 1;  // tile statuses + ticket
 constexpr int kNoAllocMaxDevices = 128;
 std::mutex g_noalloc_mu;
 unsigned long long* g_noalloc_dev_ptr[kNoAllocMaxDevices] = {};
 }  // namespace
 
-// The scratch: every GPU that loads this library holds these 32 KiB until exit.  In host
+// The scratch: every GPU that loads this library holds these 128 KiB until exit.  In host
 // code the name is only a stand-in; its device address comes from cudaGetSymbolAddress.
 static __device__ __align__(256) unsigned long long g_noalloc_scan_scratch[kNoAllocScratchWords];
 
@@ -219,7 +224,6 @@ extern "C" __attribute__((visibility("default"))) int grappa_sample_hop_noalloc(
     const uint8_t* frontier, int32_t fanout, int32_t replace, const int64_t* counters, int32_t hop,
     const int64_t* gideg, float* cov_accum, int32_t* out_indptr, int32_t* out_nbr, int32_t cap_edges,
     int32_t* n_edges_out, int32_t* err, void* stream) {
-  static_assert(grappa::dev::kThreads == 256, "scratch sizing assumes 256-node tiles");
   if (n_dst < 0 || n_dst > kGrappaNoAllocMaxDst) return GRAPPA_NOALLOC_TOO_MANY_DST;
   if (!indptr || !indices || !dst_nid || !counters || !out_indptr || !n_edges_out || n_graph_nodes < 0 ||
       cap_edges < 0 || (cap_edges > 0 && !out_nbr))
@@ -239,7 +243,7 @@ extern "C" __attribute__((visibility("default"))) int grappa_sample_hop_noalloc(
     scratch = g_noalloc_dev_ptr[dev];
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int tiles = static_cast<int>(grappa::dev::ceil_div(n_dst > 0 ? n_dst : 1, 256));
+  const int tiles = static_cast<int>(grappa::dev::ceil_div(n_dst > 0 ? n_dst : 1, grappa::dev::kTileNodes));
   // the array keeps the previous call's contents: the scan needs it zeroed
   if (cudaMemsetAsync(scratch, 0, sizeof(unsigned long long) * (tiles + 1), s) != cudaSuccess)
     return GRAPPA_NOALLOC_LAUNCH_FAILED;
@@ -263,7 +267,7 @@ extern "C" __attribute__((visibility("default"))) int grappa_sample_hop_noalloc(
   a.n_edges_out = n_edges_out;
   a.scan_scratch = scratch;
   a.err = err;
-  grappa::dev::sample_hop_kernel<<<tiles, 256, 0, s>>>(a);
+  grappa::dev::sample_hop_kernel<<<tiles, grappa::dev::kThreads, 0, s>>>(a);
   if (cudaGetLastError() != cudaSuccess) return GRAPPA_NOALLOC_LAUNCH_FAILED;
   return GRAPPA_NOALLOC_OK;
 }

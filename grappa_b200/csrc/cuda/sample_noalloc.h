@@ -13,7 +13,7 @@
 // Limits and behaviour:
 //   * at most kGrappaNoAllocMaxDst (1,048,576) destination nodes per call; larger
 //     requests are rejected with GRAPPA_NOALLOC_TOO_MANY_DST before anything runs;
-//   * the scratch array (32 KiB) is held by every GPU that loads the library until
+//   * the scratch array (128 KiB) is held by every GPU that loads the library until
 //     the process exits;
 //   * the first call on a device looks up the array's device address
 //     (cudaGetSymbolAddress) with that device current; make that first call before

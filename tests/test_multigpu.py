@@ -1,0 +1,186 @@
+"""Multi-GPU tests (2 ranks, one process per GPU, NCCL for bootstrap only):
+the fused coverage-weighted all-reduce + Adam over peer memory, the peer-memory
+repartition, and a short partition-parallel training run."""
+import os
+import socket
+import traceback
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+WORLD = 2
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _run(fn, port, *args):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_entry, args=(r, port, fn, q) + args) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    results = {}
+    for _ in range(WORLD):
+        r, ok, payload = q.get(timeout=600)
+        results[r] = (ok, payload)
+    for p in procs:
+        p.join(timeout=120)
+    for r, (ok, payload) in sorted(results.items()):
+        assert ok, f"rank {r} failed:\n{payload}"
+    return {r: payload for r, (ok, payload) in results.items()}
+
+
+def _entry(rank, port, fn, q, *args):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(WORLD),
+                          LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+        torch.cuda.set_device(rank)
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        out = fn(rank)
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, True, out))
+    except Exception:
+        q.put((rank, False, traceback.format_exc()))
+
+
+def _ar_body(rank):
+    from grappa_b200.engine import FusedAllReduceAdam
+    from grappa_b200.parallel.comm import Comm
+    from grappa_b200.sampler_gpu import new_counters
+
+    dev = torch.device("cuda", rank)
+    n = 300001
+    comm = Comm()
+    ar = FusedAllReduceAdam(comm, n, chunk=4096)
+    counters = new_counters(0, dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    out = torch.zeros(n, device=dev)
+    results = []
+    for step in range(3):
+        g = torch.Generator(device="cpu").manual_seed(100 * step + rank)
+        grad = torch.randn(n, generator=g).to(dev)
+        c = 0.5 + 0.25 * rank  # coverage weight of this rank
+        cov = torch.tensor([c * 8.0, 8.0], device=dev)
+        ar.reduce(grad, cov, counters, out, err)
+        counters[3] += 1  # next step (flags and send-slot parity)
+        torch.cuda.synchronize()
+        assert err.item() == 0
+        want = torch.zeros(n)
+        for r in range(WORLD):
+            gr = torch.randn(n, generator=torch.Generator(device="cpu").manual_seed(100 * step + r))
+            want += (0.5 + 0.25 * r) * gr / WORLD
+        results.append(float((out.cpu() - want).abs().max()))
+    ar.close()
+    return results
+
+
+def test_fused_allreduce_two_ranks():
+    res = _run(_ar_body, _free_port())
+    for r in range(WORLD):
+        assert max(res[r]) < 1e-5, res
+
+
+def _repart_body(rank):
+    from grappa_b200.dataset import synthetic as S
+    from grappa_b200.graph_store import PartitionStore, partition_from_global
+    from grappa_b200.parallel.comm import Comm
+
+    dev = torch.device("cuda", rank)
+    g = S.build(S.SPECS["tiny"], dev)
+    own = partition_from_global(g, WORLD, rank, dev, part_seed=7)
+    store = PartitionStore(own, Comm())
+    nbr = (rank + 1) % WORLD
+    w = store.repartition(nbr)
+    torch.cuda.synchronize()
+    store.check_errors()
+    # CPU reconstruction of the working graph from the global graph
+    n = g.n_nodes
+    pid = torch.from_numpy(__import__("grappa_b200").host().c_dist.random_assign_pid(n, WORLD, 7))
+    order = torch.argsort(pid * n + torch.arange(n))
+    new_id = torch.empty(n, dtype=torch.int64)
+    new_id[order] = torch.arange(n)
+    u = new_id[g.u.cpu()]
+    v = new_id[g.v.cpu()]
+    prefix = own.prefix
+    lo_r, hi_r, lo_q, hi_q = prefix[rank], prefix[rank + 1], prefix[nbr], prefix[nbr + 1]
+    n_r, n_q = hi_r - lo_r, hi_q - lo_q
+    halo = int(w.n_halo_dev.item())
+    ids = torch.empty(n_r + n_q + halo, dtype=torch.int64)
+    ids[:n_r] = torch.arange(lo_r, hi_r)
+    ids[n_r:n_r + n_q] = torch.arange(lo_q, hi_q)
+    ids[n_r + n_q:] = store._halo_ids[:halo].cpu()
+    # every in-edge of own and neighbour nodes (plus their self-loops) must be in the working CSR
+    ip = w.indptr.cpu()
+    ix = w.indices.cpu().long()
+    checked = 0
+    for wv in list(range(0, n_r, max(1, n_r // 50))) + list(range(n_r, n_r + n_q, max(1, n_q // 50))):
+        gv = int(ids[wv])
+        want = set(u[v == gv].tolist()) | {gv}
+        got = set(ids[ix[ip[wv]:ip[wv + 1]]].tolist())
+        assert got == want, (wv, gv)
+        checked += 1
+    # halo rows: sources outside both partitions, sorted, features pulled from their owners
+    hal = ids[n_r + n_q:]
+    assert bool((hal[1:] > hal[:-1]).all())
+    assert bool((((hal < lo_r) | (hal >= hi_r)) & ((hal < lo_q) | (hal >= hi_q))).all())
+    feat_all = torch.zeros((n, w.feat.shape[1]))
+    feat_all[new_id, : g.spec.feat_dim] = g.feat.cpu()
+    wf = w.feat[: n_r + n_q + halo].float().cpu()
+    torch.testing.assert_close(wf, feat_all[ids].to(torch.bfloat16).float())
+    store.close()
+    return checked
+
+
+def test_repartition_two_ranks():
+    res = _run(_repart_body, _free_port())
+    assert all(v > 10 for v in res.values())
+
+
+def _train_body(rank):
+    import torch.nn.functional as F
+
+    from grappa_b200.dataset import synthetic as S
+    from grappa_b200.graph_store import partition_from_global
+    from grappa_b200.models import SAGE
+    from grappa_b200.parallel.comm import Comm
+    from grappa_b200.trainer import MiniBatchTrainer
+
+    dev = torch.device("cuda", rank)
+    g = S.build(S.SPECS["tiny"], dev)
+    own = partition_from_global(g, WORLD, rank, dev, part_seed=3)
+    torch.manual_seed(0)
+    model = SAGE(g.spec.feat_dim, 64, g.spec.n_classes, 3, F.relu, 0.5)
+    tr = MiniBatchTrainer(model, own, [10, 10, 5], 128, comm=Comm(), seed=2, repart_every=2)
+    tr.warmup()
+    losses = []
+    for e in range(5):  # crosses two repartitions
+        losses.append(tr.train_epoch(e, host_feed=True))
+    torch.cuda.synchronize()
+    tr.engine.check_errors()
+    flat = tr.engine.flat.cpu().clone()
+    acc = tr.evaluate(own.val_mask)
+    tr.close()
+    return {"losses": losses, "flat_sum": float(flat.double().sum()), "flat_head": flat[:64].tolist(), "acc": acc}
+
+
+def test_partition_parallel_training_two_ranks():
+    res = _run(_train_body, _free_port())
+    a, b = res[0], res[1]
+    # the fused all-reduce + Adam keeps the replicas bit-identical
+    assert a["flat_head"] == b["flat_head"] and a["flat_sum"] == b["flat_sum"]
+    assert a["losses"][-1] < a["losses"][0]
+    assert a["acc"] == b["acc"]
