@@ -145,6 +145,73 @@ Block sample_hop(const CSC& g, const int64_t* dst_nid, const uint8_t* frontier, 
   return b;
 }
 
+Block random_walk_topk(const CSC& g, const int64_t* seeds, int64_t n_seeds, int length,
+                       double restart_prob, int num_walks, int num_neighbors, uint64_t key,
+                       std::vector<float>* weights) {
+  const uint32_t thr = restart_prob >= 1.0 ? 0xFFFFFFFFu : static_cast<uint32_t>(restart_prob * 4294967296.0);
+  std::vector<std::vector<std::pair<int64_t, int64_t>>> top(n_seeds);
+#pragma omp parallel for schedule(dynamic, 16)
+  for (int64_t i = 0; i < n_seeds; ++i) {
+    std::vector<int64_t> visits;
+    visits.reserve(static_cast<size_t>(num_walks) * length);
+    const int64_t s0 = seeds[i];
+    for (int j = 0; j < num_walks; ++j) {
+      int64_t cur = s0;
+      const uint64_t w = static_cast<uint64_t>(i) * num_walks + j;
+      for (int t = 0; t < length; ++t) {
+        if (cur < 0 || cur >= g.n_nodes) break;
+        const U4 r = index_draw4(key, w, static_cast<uint32_t>(t));
+        if (r.x < thr) break;
+        const int64_t d = g.degree(cur);
+        if (d == 0) break;
+        cur = g.indices[g.indptr[cur] + draw_below(r.y, static_cast<uint32_t>(d))];
+        visits.push_back(cur);
+      }
+    }
+    std::sort(visits.begin(), visits.end());
+    auto& tp = top[i];
+    for (size_t a = 0; a < visits.size();) {
+      size_t b = a;
+      while (b < visits.size() && visits[b] == visits[a]) ++b;
+      tp.emplace_back(static_cast<int64_t>(b - a), visits[a]);
+      a = b;
+    }
+    // most visited first; ties by smaller id (ids are ascending already)
+    std::stable_sort(tp.begin(), tp.end(), [](const auto& x, const auto& y) { return x.first > y.first; });
+    if (static_cast<int64_t>(tp.size()) > num_neighbors) tp.resize(num_neighbors);
+  }
+  Block b;
+  b.n_dst = n_seeds;
+  b.indptr.assign(n_seeds + 1, 0);
+  for (int64_t i = 0; i < n_seeds; ++i) b.indptr[i + 1] = b.indptr[i] + static_cast<int64_t>(top[i].size());
+  const int64_t n_e = b.indptr[n_seeds];
+  std::unordered_map<int64_t, int64_t> lid;
+  lid.reserve(static_cast<size_t>((n_seeds + n_e) * 1.3) + 16);
+  b.src_nid.assign(seeds, seeds + n_seeds);
+  for (int64_t i = 0; i < n_seeds; ++i) lid.emplace(seeds[i], i);
+  b.indices.resize(n_e);
+  if (weights) weights->resize(n_e);
+  for (int64_t i = 0; i < n_seeds; ++i)
+    for (size_t k = 0; k < top[i].size(); ++k) {
+      const int64_t e = b.indptr[i] + static_cast<int64_t>(k);
+      const int64_t nid = top[i][k].second;
+      auto it = lid.find(nid);
+      if (it == lid.end()) {
+        const int64_t id = static_cast<int64_t>(b.src_nid.size());
+        lid.emplace(nid, id);
+        b.src_nid.push_back(nid);
+        b.indices[e] = id;
+      } else {
+        b.indices[e] = it->second;
+      }
+      if (weights) (*weights)[e] = static_cast<float>(top[i][k].first);
+    }
+  b.n_src = static_cast<int64_t>(b.src_nid.size());
+  b.src_sampled.assign(b.n_src, 0);
+  for (int64_t j = 0; j < n_e; ++j) b.src_sampled[b.indices[j]] = 1;
+  return b;
+}
+
 void rmat_candidates(int64_t n, int scale, double a, double b, double c, uint64_t seed,
                      int64_t e_begin, int64_t e_end, int64_t* keys) {
   const uint64_t ta = static_cast<uint64_t>(a * 4294967296.0);

@@ -56,6 +56,19 @@ Block sample_hop(const CSC& g, const int64_t* dst_nid, const uint8_t* frontier, 
                  int64_t fanout, uint64_t key, const int64_t* gideg, double* cov_sum,
                  double* cov_n);
 
+// PinSAGE neighbourhood (the random-walk neighbour sampler DGL provides to the
+// reference, t10n/dgl_dsg/sampler.py:323-366): every seed starts num_walks walks
+// over in-edges; before each of at most `length` steps a walk stops with
+// probability restart_prob (and at a node without in-edges).  Every node a walk
+// visits after its start is counted for the seed; the num_neighbors most visited
+// (ties: smaller id first) become the seed's neighbours, their counts the edge
+// weights.  Walker w = i * num_walks + j, step t draws index_draw4(key, w, t):
+// word x decides the stop (x < restart_prob * 2^32), word y the in-neighbour
+// (draw_below(y, deg)).  Same rule on the GPU.
+Block random_walk_topk(const CSC& g, const int64_t* seeds, int64_t n_seeds, int length,
+                       double restart_prob, int num_walks, int num_neighbors, uint64_t key,
+                       std::vector<float>* weights);
+
 // Coverage ratio of one seed (shared definition with the GPU sampler).
 inline float coverage_ratio(int64_t local_deg, int64_t global_deg) {
   const int64_t up = local_deg - 1 < 0 ? 0 : local_deg - 1;

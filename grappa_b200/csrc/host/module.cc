@@ -361,6 +361,23 @@ PYBIND11_MODULE(_C, m) {
         return py::make_tuple(to_py(std::move(u)), to_py(std::move(v)));
       },
       py::arg("graph"), py::arg("seeds"), py::arg("fanout"), py::arg("key") = 0);
+  mg.def(
+      "random_walk_topk",
+      [](HostGraph& g, arr<int64_t> seeds, int length, double restart_prob, int num_walks, int num_neighbors,
+         uint64_t key) {
+        std::vector<float> w;
+        Block b;
+        {
+          py::gil_scoped_release rel;
+          b = grappa::host::random_walk_topk(g.csc, seeds.data(), static_cast<int64_t>(seeds.size()), length,
+                                             restart_prob, num_walks, num_neighbors, key, &w);
+        }
+        py::dict d = block_to_py(b);
+        d["weights"] = to_py(std::move(w));
+        return d;
+      },
+      py::arg("graph"), py::arg("seeds"), py::arg("length"), py::arg("restart_prob") = 0.5,
+      py::arg("num_walks") = 4, py::arg("num_neighbors") = 5, py::arg("key") = 0);
   mg.def("pick_offsets", [](uint64_t key, uint64_t nid, uint32_t d, uint32_t k) {
     std::vector<int64_t> out(k);
     grappa::host::pick_offsets(key, nid, d, k, out.data());

@@ -1,0 +1,94 @@
+"""Sequential (single-process) chunk builder (reference: t10n/dataset/chunk_seq.py:27-150).
+
+Reads a dataset in the pre-partition layout (``t10n.json`` + ``*.bin.npy``, see
+grappa_b200.dataset.synthetic.to_t10n_layout), assigns nodes to partitions and
+writes the partition chunks with the C++ writer (grappa_b200._C.c_seq).
+
+Partition methods: ``hash`` / ``random`` (seeded hash of the node id) and
+``lp`` (label-propagation refinement of the hash assignment that keeps the
+partitions balanced; the reference's ``metis`` needs DGL's METIS binding, which
+is not part of this framework — ``metis`` is accepted as an alias of ``lp``).
+"""
+import json
+import os
+import pathlib
+
+import numpy as np
+import torch
+
+from grappa_b200 import _native
+from grappa_b200.dataset.meta import t10n_chunk_path
+
+
+def assign_partitions(u, v, n, n_part, method="hash", seed=0, rounds=4):
+    if n_part == 1:
+        return np.zeros(n, dtype=np.int64)
+    pid = _native.host().c_dist.random_assign_pid(n, n_part, seed)
+    if method in ("hash", "random"):
+        return pid
+    if method not in ("lp", "metis"):
+        raise ValueError(f"unknown partition method {method}")
+    return label_propagation(u, v, n, n_part, pid, rounds)
+
+
+def label_propagation(u, v, n, n_part, pid, rounds=4, slack=1.05):
+    """Move nodes to the partition most of their neighbours are in, subject to a size cap."""
+    pid = torch.from_numpy(pid.copy())
+    uu, vv = torch.from_numpy(u), torch.from_numpy(v)
+    cap = int(slack * n / n_part) + 1
+    for _ in range(rounds):
+        votes = torch.zeros((n, n_part), dtype=torch.int32)
+        votes.index_put_((vv, pid[uu]), torch.ones(vv.numel(), dtype=torch.int32), accumulate=True)
+        best = votes.argmax(1)
+        gain = votes.gather(1, best.unsqueeze(1)).squeeze(1) - votes.gather(1, pid.unsqueeze(1)).squeeze(1)
+        order = torch.argsort(gain, descending=True)
+        sizes = torch.bincount(pid, minlength=n_part)
+        moved = 0
+        for node in order[gain[order] > 0].tolist():
+            a, b = int(pid[node]), int(best[node])
+            if sizes[b] < cap:
+                sizes[a] -= 1
+                sizes[b] += 1
+                pid[node] = b
+                moved += 1
+        if moved == 0:
+            break
+    return pid.numpy()
+
+
+def build_chunks_seq(dest_path, dataset_name, src_path, part_method, n_part, seed=0):
+    with open(os.path.join(src_path, "t10n.json")) as f:
+        cfg = json.load(f)
+    out = os.path.join(dest_path, t10n_chunk_path(dataset_name, part_method, n_part))
+    if os.path.exists(out):
+        raise FileExistsError(f"please delete {out} first")
+    pathlib.Path(out).mkdir(parents=True)
+    edges = np.load(cfg["edge_file_bin"])
+    n, m, dim = int(cfg["num_nodes"]), int(cfg["num_edges"]), int(cfg["feat_dim"])
+    u, v = edges[:m].astype(np.int64), edges[m:].astype(np.int64)
+    pid = assign_partitions(u, v, n, n_part, part_method, seed)
+    c = _native.host().c_seq
+    stats = c.build(out, n, m, dim, n_part, u, v, pid)
+    c.split_node_feat(out, n, dim, n_part, np.load(cfg["node_feats_file_bin"]).astype(np.float32))
+    c.split_node_data(out, n, n_part, np.load(cfg["node_label_file"]).astype(np.float32),
+                      np.load(cfg["train_mask_file_bin"]).astype(np.int8),
+                      np.load(cfg["val_mask_file_bin"]).astype(np.int8),
+                      np.load(cfg["test_mask_file_bin"]).astype(np.int8))
+    return out, stats
+
+
+def build_chunks_from_graph(graph, dest_path, n_part, part_method="hash", seed=0):
+    """Write the chunk layout of an in-memory SyntheticGraph (no intermediate files)."""
+    name = graph.spec.name
+    out = os.path.join(dest_path, t10n_chunk_path(name, part_method, n_part))
+    pathlib.Path(out).mkdir(parents=True, exist_ok=True)
+    n = graph.n_nodes
+    u = graph.u.cpu().numpy().astype(np.int64)
+    v = graph.v.cpu().numpy().astype(np.int64)
+    pid = assign_partitions(u, v, n, n_part, part_method, seed)
+    c = _native.host().c_seq
+    stats = c.build(out, n, len(u), graph.spec.feat_dim, n_part, u, v, pid)
+    c.split_node_feat(out, n, graph.spec.feat_dim, n_part, graph.feat.cpu().numpy().astype(np.float32))
+    c.split_node_data(out, n, n_part, graph.label.cpu().numpy().astype(np.float32),
+                      graph.train_mask.cpu().numpy(), graph.val_mask.cpu().numpy(), graph.test_mask.cpu().numpy())
+    return out, stats
