@@ -176,9 +176,16 @@ void gemm(Tensor A, bool a_mn, Tensor B, bool b_mn, int64_t M_cap, OptT M_dev, i
 // --------------------------------------------------------------------------- aggregation
 void aggregate(Tensor indptr, Tensor indices, OptT n_dst_dev, int64_t n_dst, int64_t cap_dst, Tensor src, OptT src_map,
                int64_t dim, int64_t mode, OptT edge_w, OptT src_norm, OptT dst_norm, Tensor out, int64_t agg_col,
-               int64_t self_col, double self_scale, int64_t zero_tail_rows, Tensor err) {
+               int64_t self_col, double self_scale, int64_t zero_tail_rows, Tensor err, OptT bias, int64_t act,
+               double dropout_p, OptT counters, int64_t dropout_salt) {
   c10::cuda::CUDAGuard g(src.device());
   d::AggArgs a;
+  a.bias = optr<float>(bias, at::kFloat, "bias");
+  a.act = static_cast<int32_t>(act);
+  a.dropout_p = static_cast<float>(dropout_p);
+  a.counters = optr<int64_t>(counters, at::kLong, "counters");
+  a.dropout_salt = static_cast<uint32_t>(dropout_salt);
+  TORCH_CHECK(!a.bias || bias->numel() >= dim, "bias shorter than dim");
   a.indptr = ptr<int32_t>(indptr, at::kInt, "indptr");
   a.indices = ptr<int32_t>(indices, at::kInt, "indices");
   a.n_dst_ptr = optr<int32_t>(n_dst_dev, at::kInt, "n_dst_dev");
@@ -479,6 +486,259 @@ void csr_merge(int64_t indptr_a, int64_t indices_a, int64_t n_a, int64_t indptr_
   grappa::peer::launch_csr_merge(a, stream());
 }
 
+
+// --------------------------------------------------------------------------- nn.cu
+void cross_entropy(Tensor logits, int64_t n_classes, Tensor labels, OptT n_rows_dev, int64_t cap_rows, OptT row_mask,
+                   OptT n_sel_dev, Tensor dlogits, OptT dbias, Tensor loss_sum, Tensor correct) {
+  c10::cuda::CUDAGuard g(logits.device());
+  d::CeArgs a;
+  a.logits = reinterpret_cast<const __nv_bfloat16*>(ptr2d<at::BFloat16>(logits, at::kBFloat16, "logits"));
+  a.ld = logits.stride(0);
+  a.n_classes = static_cast<int32_t>(n_classes);
+  a.labels = ptr<int32_t>(labels, at::kInt, "labels");
+  a.n_rows_ptr = optr<int32_t>(n_rows_dev, at::kInt, "n_rows_dev");
+  a.cap_rows = static_cast<int32_t>(cap_rows);
+  a.row_mask = optr<uint8_t>(row_mask, at::kByte, "row_mask");
+  a.n_sel_ptr = optr<int32_t>(n_sel_dev, at::kInt, "n_sel_dev");
+  a.dlogits = reinterpret_cast<__nv_bfloat16*>(ptr2d<at::BFloat16>(dlogits, at::kBFloat16, "dlogits"));
+  a.ld_dl = dlogits.stride(0);
+  a.dbias = optr<float>(dbias, at::kFloat, "dbias");
+  a.loss_sum = ptr<float>(loss_sum, at::kFloat, "loss_sum");
+  a.correct = ptr<int32_t>(correct, at::kInt, "correct");
+  TORCH_CHECK(logits.size(0) >= cap_rows && dlogits.size(0) >= cap_rows, "logits rows < cap_rows");
+  TORCH_CHECK(labels.numel() >= cap_rows, "labels shorter than cap_rows");
+  TORCH_CHECK(dlogits.size(1) >= n_classes && logits.size(1) >= n_classes, "fewer columns than classes");
+  d::launch_cross_entropy(a, stream());
+}
+
+void batchnorm_fwd(Tensor x, int64_t dim, OptT n_dev, int64_t cap, Tensor sums, Tensor gamma, Tensor beta,
+                   Tensor running_mean, Tensor running_var, OptT num_batches, double momentum, double eps,
+                   bool training, int64_t act, Tensor y) {
+  c10::cuda::CUDAGuard g(x.device());
+  d::BnArgs a;
+  a.x = reinterpret_cast<const __nv_bfloat16*>(ptr2d<at::BFloat16>(x, at::kBFloat16, "x"));
+  a.ldx = x.stride(0);
+  a.dim = static_cast<int32_t>(dim);
+  a.n_ptr = optr<int32_t>(n_dev, at::kInt, "n_dev");
+  a.cap = static_cast<int32_t>(cap);
+  a.sums = ptr<float>(sums, at::kFloat, "sums");
+  a.gamma = gamma.data_ptr<float>();
+  a.beta = beta.data_ptr<float>();
+  a.running_mean = running_mean.data_ptr<float>();
+  a.running_var = running_var.data_ptr<float>();
+  a.stat_dim = static_cast<int32_t>(std::min(running_mean.numel(), running_var.numel()));
+  a.num_batches = optr<int64_t>(num_batches, at::kLong, "num_batches");
+  a.momentum = static_cast<float>(momentum);
+  a.eps = static_cast<float>(eps);
+  a.training = training;
+  a.act = static_cast<int32_t>(act);
+  a.y = reinterpret_cast<__nv_bfloat16*>(ptr2d<at::BFloat16>(y, at::kBFloat16, "y"));
+  a.ldy = y.stride(0);
+  TORCH_CHECK(sums.numel() >= 2 * dim && gamma.numel() >= dim && beta.numel() >= dim, "batchnorm: short parameters");
+  TORCH_CHECK(x.size(0) >= cap && y.size(0) >= cap, "batchnorm: fewer rows than cap");
+  d::launch_batchnorm_fwd(a, stream());
+}
+
+void batchnorm_bwd(Tensor x, OptT y, Tensor dy, bool clear_dy, int64_t dim, OptT n_dev, int64_t cap, Tensor sums,
+                   Tensor bsums, Tensor gamma, OptT dgamma, OptT dbeta, double eps, Tensor dx) {
+  c10::cuda::CUDAGuard g(x.device());
+  d::BnBwdArgs a;
+  a.x = reinterpret_cast<const __nv_bfloat16*>(ptr2d<at::BFloat16>(x, at::kBFloat16, "x"));
+  a.ldx = x.stride(0);
+  if (y.has_value() && y->defined()) {
+    a.y = reinterpret_cast<const __nv_bfloat16*>(ptr2d<at::BFloat16>(*y, at::kBFloat16, "y"));
+    a.ldy = y->stride(0);
+  }
+  if (dy.scalar_type() == at::kBFloat16) {
+    a.dy_bf16 = reinterpret_cast<const __nv_bfloat16*>(ptr2d<at::BFloat16>(dy, at::kBFloat16, "dy"));
+  } else {
+    a.dy = ptr2d<float>(dy, at::kFloat, "dy");
+  }
+  a.lddy = dy.stride(0);
+  a.clear_dy = clear_dy;
+  a.dim = static_cast<int32_t>(dim);
+  a.n_ptr = optr<int32_t>(n_dev, at::kInt, "n_dev");
+  a.cap = static_cast<int32_t>(cap);
+  a.sums = ptr<float>(sums, at::kFloat, "sums");
+  a.bsums = ptr<float>(bsums, at::kFloat, "bsums");
+  a.gamma = gamma.data_ptr<float>();
+  a.dgamma = dgamma.has_value() ? dgamma->data_ptr<float>() : nullptr;
+  a.dbeta = dbeta.has_value() ? dbeta->data_ptr<float>() : nullptr;
+  a.eps = static_cast<float>(eps);
+  a.dx = reinterpret_cast<__nv_bfloat16*>(ptr2d<at::BFloat16>(dx, at::kBFloat16, "dx"));
+  a.lddx = dx.stride(0);
+  d::launch_batchnorm_bwd(a, stream());
+}
+
+void l2norm_fwd(Tensor z, int64_t dim, OptT n_dev, int64_t cap, Tensor y, Tensor norms) {
+  c10::cuda::CUDAGuard g(z.device());
+  d::launch_l2norm_fwd(reinterpret_cast<const __nv_bfloat16*>(ptr2d<at::BFloat16>(z, at::kBFloat16, "z")), z.stride(0),
+                       static_cast<int32_t>(dim), optr<int32_t>(n_dev, at::kInt, "n_dev"), static_cast<int>(cap),
+                       reinterpret_cast<__nv_bfloat16*>(ptr2d<at::BFloat16>(y, at::kBFloat16, "y")), y.stride(0),
+                       ptr<float>(norms, at::kFloat, "norms"), stream());
+}
+
+void l2norm_bwd(Tensor y, Tensor dy, Tensor norms, int64_t dim, OptT n_dev, int64_t cap, Tensor dz) {
+  c10::cuda::CUDAGuard g(y.device());
+  float* dyf = nullptr;
+  const __nv_bfloat16* dyb = nullptr;
+  if (dy.scalar_type() == at::kBFloat16) dyb = reinterpret_cast<const __nv_bfloat16*>(ptr2d<at::BFloat16>(dy, at::kBFloat16, "dy"));
+  else dyf = ptr2d<float>(dy, at::kFloat, "dy");
+  d::launch_l2norm_bwd(reinterpret_cast<const __nv_bfloat16*>(ptr2d<at::BFloat16>(y, at::kBFloat16, "y")), y.stride(0),
+                       dyf, dyb, dy.stride(0), ptr<float>(norms, at::kFloat, "norms"), static_cast<int32_t>(dim),
+                       optr<int32_t>(n_dev, at::kInt, "n_dev"), static_cast<int>(cap), ptr2d<float>(dz, at::kFloat, "dz"),
+                       dz.stride(0), stream());
+}
+
+void add_bf16_rows(Tensor dst, Tensor src, int64_t dim, OptT n_dev, int64_t cap) {
+  c10::cuda::CUDAGuard g(dst.device());
+  d::launch_add_bf16_rows(ptr2d<float>(dst, at::kFloat, "dst"), dst.stride(0),
+                          reinterpret_cast<const __nv_bfloat16*>(ptr2d<at::BFloat16>(src, at::kBFloat16, "src")),
+                          src.stride(0), static_cast<int32_t>(dim), optr<int32_t>(n_dev, at::kInt, "n_dev"),
+                          static_cast<int>(cap), stream());
+}
+
+void dropout_rows(Tensor in, Tensor out, int64_t dim, int64_t ld_mask, OptT n_dev, int64_t cap, double p,
+                  Tensor counters, int64_t salt) {
+  c10::cuda::CUDAGuard g(in.device());
+  d::launch_dropout_rows(reinterpret_cast<const __nv_bfloat16*>(ptr2d<at::BFloat16>(in, at::kBFloat16, "in")),
+                         in.stride(0), reinterpret_cast<__nv_bfloat16*>(ptr2d<at::BFloat16>(out, at::kBFloat16, "out")),
+                         out.stride(0), static_cast<int32_t>(dim), ld_mask, optr<int32_t>(n_dev, at::kInt, "n_dev"),
+                         static_cast<int>(cap), static_cast<float>(p), ptr<int64_t>(counters, at::kLong, "counters"),
+                         static_cast<uint32_t>(salt), stream());
+}
+
+void dropout_grad(Tensor gr, int64_t dim, int64_t ld_mask, OptT n_dev, int64_t cap, double p, Tensor counters,
+                  int64_t salt) {
+  c10::cuda::CUDAGuard g(gr.device());
+  d::launch_dropout_grad(ptr2d<float>(gr, at::kFloat, "g"), gr.stride(0), static_cast<int32_t>(dim), ld_mask,
+                         optr<int32_t>(n_dev, at::kInt, "n_dev"), static_cast<int>(cap), static_cast<float>(p),
+                         ptr<int64_t>(counters, at::kLong, "counters"), static_cast<uint32_t>(salt), stream());
+}
+
+void f32_to_bf16_rows(Tensor src, Tensor dst, int64_t dim, OptT n_dev, int64_t cap, bool clear, int64_t zero_tail_rows) {
+  c10::cuda::CUDAGuard g(src.device());
+  TORCH_CHECK(src.size(0) >= cap && dst.size(0) >= cap, "f32_to_bf16_rows: fewer rows than cap");
+  d::launch_f32_to_bf16_rows(ptr2d<float>(src, at::kFloat, "src"), src.stride(0),
+                             reinterpret_cast<__nv_bfloat16*>(ptr2d<at::BFloat16>(dst, at::kBFloat16, "dst")),
+                             dst.stride(0), static_cast<int32_t>(dim), optr<int32_t>(n_dev, at::kInt, "n_dev"),
+                             static_cast<int>(cap), clear, static_cast<int32_t>(zero_tail_rows), stream());
+}
+
+// --------------------------------------------------------------------------- gat.cu
+d::GatArgs gat_args(Tensor indptr, Tensor indices, OptT n_dst_dev, int64_t cap_dst, OptT n_src_dev, int64_t cap_src,
+                    int64_t heads, int64_t feat, Tensor z, Tensor attn_l, Tensor attn_r, Tensor el, Tensor er,
+                    Tensor smax, Tensor ssum, double slope) {
+  d::GatArgs a;
+  a.indptr = ptr<int32_t>(indptr, at::kInt, "indptr");
+  a.indices = ptr<int32_t>(indices, at::kInt, "indices");
+  a.n_dst_ptr = optr<int32_t>(n_dst_dev, at::kInt, "n_dst_dev");
+  a.cap_dst = static_cast<int32_t>(cap_dst);
+  a.n_src_ptr = optr<int32_t>(n_src_dev, at::kInt, "n_src_dev");
+  a.cap_src = static_cast<int32_t>(cap_src);
+  a.heads = static_cast<int32_t>(heads);
+  a.feat = static_cast<int32_t>(feat);
+  a.z = reinterpret_cast<const __nv_bfloat16*>(ptr2d<at::BFloat16>(z, at::kBFloat16, "z"));
+  a.ldz = z.stride(0);
+  a.attn_l = attn_l.data_ptr<float>();
+  a.attn_r = attn_r.data_ptr<float>();
+  a.el = ptr<float>(el, at::kFloat, "el");
+  a.er = ptr<float>(er, at::kFloat, "er");
+  a.smax = ptr<float>(smax, at::kFloat, "smax");
+  a.ssum = ptr<float>(ssum, at::kFloat, "ssum");
+  a.slope = static_cast<float>(slope);
+  TORCH_CHECK(z.size(0) >= cap_src && z.size(1) >= heads * feat, "gat: z too small");
+  TORCH_CHECK(el.numel() >= cap_src * heads && er.numel() >= cap_dst * heads, "gat: score buffers too small");
+  TORCH_CHECK(smax.numel() >= cap_dst * heads && ssum.numel() >= cap_dst * heads, "gat: softmax buffers too small");
+  TORCH_CHECK(attn_l.is_cuda() && attn_r.is_cuda() && attn_l.scalar_type() == at::kFloat, "gat: attention vectors");
+  return a;
+}
+
+void gat_scores(Tensor indptr, Tensor indices, OptT n_dst_dev, int64_t cap_dst, OptT n_src_dev, int64_t cap_src,
+                int64_t heads, int64_t feat, Tensor z, Tensor attn_l, Tensor attn_r, Tensor el, Tensor er, Tensor smax,
+                Tensor ssum, double slope) {
+  c10::cuda::CUDAGuard g(z.device());
+  auto a = gat_args(indptr, indices, n_dst_dev, cap_dst, n_src_dev, cap_src, heads, feat, z, attn_l, attn_r, el, er,
+                    smax, ssum, slope);
+  d::launch_gat_scores(a, stream());
+}
+
+void gat_fwd(Tensor indptr, Tensor indices, OptT n_dst_dev, int64_t cap_dst, OptT n_src_dev, int64_t cap_src,
+             int64_t heads, int64_t feat, Tensor z, Tensor attn_l, Tensor attn_r, Tensor el, Tensor er, Tensor smax,
+             Tensor ssum, double slope, Tensor bias, bool mean_heads, int64_t act, double dropout_p, OptT counters,
+             int64_t dropout_salt, Tensor out) {
+  c10::cuda::CUDAGuard g(z.device());
+  auto a = gat_args(indptr, indices, n_dst_dev, cap_dst, n_src_dev, cap_src, heads, feat, z, attn_l, attn_r, el, er,
+                    smax, ssum, slope);
+  a.bias = bias.data_ptr<float>();
+  a.mean_heads = mean_heads;
+  a.act = static_cast<int32_t>(act);
+  a.dropout_p = static_cast<float>(dropout_p);
+  a.counters = optr<int64_t>(counters, at::kLong, "counters");
+  a.dropout_salt = static_cast<uint32_t>(dropout_salt);
+  a.out = reinterpret_cast<__nv_bfloat16*>(ptr2d<at::BFloat16>(out, at::kBFloat16, "out"));
+  a.ldo = out.stride(0);
+  TORCH_CHECK(out.size(0) >= cap_dst && out.size(1) >= (mean_heads ? feat : heads * feat), "gat: out too small");
+  d::launch_gat_fwd(a, stream());
+}
+
+void gat_bwd(Tensor indptr, Tensor indices, OptT n_dst_dev, int64_t cap_dst, OptT n_src_dev, int64_t cap_src,
+             int64_t heads, int64_t feat, Tensor z, Tensor attn_l, Tensor attn_r, Tensor el, Tensor er, Tensor smax,
+             Tensor ssum, double slope, bool mean_heads, Tensor dout, Tensor edge_scratch, Tensor del, Tensor der,
+             Tensor dz, OptT dbias, OptT dattn_l, OptT dattn_r, Tensor dz_bf16, Tensor err) {
+  c10::cuda::CUDAGuard g(z.device());
+  auto a = gat_args(indptr, indices, n_dst_dev, cap_dst, n_src_dev, cap_src, heads, feat, z, attn_l, attn_r, el, er,
+                    smax, ssum, slope);
+  a.mean_heads = mean_heads;
+  a.dout = reinterpret_cast<const __nv_bfloat16*>(ptr2d<at::BFloat16>(dout, at::kBFloat16, "dout"));
+  a.lddo = dout.stride(0);
+  a.edge_scratch = ptr<float>(edge_scratch, at::kFloat, "edge_scratch");
+  a.del = ptr<float>(del, at::kFloat, "del");
+  a.der = ptr<float>(der, at::kFloat, "der");
+  a.dz = ptr2d<float>(dz, at::kFloat, "dz");
+  a.lddz = dz.stride(0);
+  a.dbias = dbias.has_value() ? dbias->data_ptr<float>() : nullptr;
+  a.dattn_l = dattn_l.has_value() ? dattn_l->data_ptr<float>() : nullptr;
+  a.dattn_r = dattn_r.has_value() ? dattn_r->data_ptr<float>() : nullptr;
+  a.dz_bf16 = reinterpret_cast<__nv_bfloat16*>(ptr2d<at::BFloat16>(dz_bf16, at::kBFloat16, "dz_bf16"));
+  a.lddzb = dz_bf16.stride(0);
+  a.err = ptr<int32_t>(err, at::kInt, "err");
+  TORCH_CHECK(edge_scratch.numel() >= static_cast<int64_t>(indices.numel()) * heads, "gat: edge scratch too small");
+  TORCH_CHECK(dz.size(0) >= cap_src && dz_bf16.size(0) >= cap_src, "gat: gradient buffers too small");
+  d::launch_gat_bwd(a, stream());
+}
+
+
+void walk_hop(Tensor indptr, Tensor indices, Tensor dst_nid, OptT n_dst_dev, int64_t n_dst, int64_t length,
+              double restart_prob, int64_t num_walks, int64_t num_neighbors, Tensor counters, int64_t hop,
+              Tensor out_indptr, Tensor out_nbr, Tensor out_w, Tensor n_edges_out, Tensor scan_scratch, Tensor err,
+              int64_t cap_dst) {
+  c10::cuda::CUDAGuard g(indptr.device());
+  d::WalkHopArgs a;
+  a.indptr = ptr<int64_t>(indptr, at::kLong, "indptr");
+  a.indices = ptr<int32_t>(indices, at::kInt, "indices");
+  a.n_graph_nodes = indptr.numel() - 1;
+  a.dst_nid = ptr<int32_t>(dst_nid, at::kInt, "dst_nid");
+  a.n_dst_ptr = optr<int32_t>(n_dst_dev, at::kInt, "n_dst_dev");
+  a.n_dst = static_cast<int32_t>(n_dst);
+  a.length = static_cast<int32_t>(length);
+  a.restart_thr = restart_prob >= 1.0 ? 0xFFFFFFFFu : static_cast<uint32_t>(restart_prob * 4294967296.0);
+  a.num_walks = static_cast<int32_t>(num_walks);
+  a.num_neighbors = static_cast<int32_t>(num_neighbors);
+  a.counters = ptr<int64_t>(counters, at::kLong, "counters");
+  a.hop = static_cast<int32_t>(hop);
+  a.out_indptr = ptr<int32_t>(out_indptr, at::kInt, "out_indptr");
+  a.out_nbr = ptr<int32_t>(out_nbr, at::kInt, "out_nbr");
+  a.out_w = ptr<float>(out_w, at::kFloat, "out_w");
+  a.cap_edges = static_cast<int32_t>(std::min(out_nbr.numel(), out_w.numel()));
+  a.n_edges_out = ptr<int32_t>(n_edges_out, at::kInt, "n_edges_out");
+  a.scan_scratch = reinterpret_cast<unsigned long long*>(ptr<int64_t>(scan_scratch, at::kLong, "scan_scratch"));
+  a.err = ptr<int32_t>(err, at::kInt, "err");
+  TORCH_CHECK(out_indptr.numel() >= cap_dst + 1 && dst_nid.numel() >= cap_dst, "walk_hop: buffers smaller than cap_dst");
+  TORCH_CHECK(scan_scratch.numel() >= d::walk_scan_scratch_words(static_cast<int>(cap_dst)), "scan_scratch too small");
+  d::launch_walk_hop(a, static_cast<int>(cap_dst), stream());
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -488,7 +748,25 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("compact", &compact);
   m.def("compact_scratch_words", &compact_scratch_words);
   m.def("gemm", &gemm);
-  m.def("aggregate", &aggregate);
+  m.def("aggregate", &aggregate, py::arg("indptr"), py::arg("indices"), py::arg("n_dst_dev"), py::arg("n_dst"),
+        py::arg("cap_dst"), py::arg("src"), py::arg("src_map"), py::arg("dim"), py::arg("mode"), py::arg("edge_w"),
+        py::arg("src_norm"), py::arg("dst_norm"), py::arg("out"), py::arg("agg_col"), py::arg("self_col"),
+        py::arg("self_scale"), py::arg("zero_tail_rows"), py::arg("err"), py::arg("bias") = py::none(),
+        py::arg("act") = 0, py::arg("dropout_p") = 0.0, py::arg("counters") = py::none(), py::arg("dropout_salt") = 0);
+  m.def("cross_entropy", &cross_entropy);
+  m.def("walk_hop", &walk_hop);
+  m.def("walk_scratch_words", [](int64_t cap) { return d::walk_scan_scratch_words(static_cast<int>(cap)); });
+  m.def("batchnorm_fwd", &batchnorm_fwd);
+  m.def("batchnorm_bwd", &batchnorm_bwd);
+  m.def("l2norm_fwd", &l2norm_fwd);
+  m.def("l2norm_bwd", &l2norm_bwd);
+  m.def("add_bf16_rows", &add_bf16_rows);
+  m.def("dropout_rows", &dropout_rows);
+  m.def("dropout_grad", &dropout_grad);
+  m.def("f32_to_bf16_rows", &f32_to_bf16_rows);
+  m.def("gat_scores", &gat_scores);
+  m.def("gat_fwd", &gat_fwd);
+  m.def("gat_bwd", &gat_bwd);
   m.def("aggregate_bwd", &aggregate_bwd);
   m.def("src_norm", &src_norm);
   m.def("act_bwd", &act_bwd);

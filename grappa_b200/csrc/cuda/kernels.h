@@ -34,6 +34,31 @@ struct SampleHopArgs {
 void launch_sample_hop(const SampleHopArgs& a, int cap_dst, cudaStream_t stream);
 int sample_scan_scratch_words(int cap_dst);
 
+// PinSAGE hop: random walks with restart + top-k visited (walk.cu)
+struct WalkHopArgs {
+  const int64_t* indptr = nullptr;
+  const int32_t* indices = nullptr;
+  int64_t n_graph_nodes = 0;
+  const int32_t* dst_nid = nullptr;
+  const int32_t* n_dst_ptr = nullptr;
+  int32_t n_dst = 0;
+  int32_t length = 0;              // steps per walk
+  uint32_t restart_thr = 0;        // stop when the draw is below this (restart_prob * 2^32)
+  int32_t num_walks = 0;
+  int32_t num_neighbors = 0;
+  const int64_t* counters = nullptr;
+  int32_t hop = 0;
+  int32_t* out_indptr = nullptr;
+  int32_t* out_nbr = nullptr;
+  float* out_w = nullptr;
+  int32_t cap_edges = 0;
+  int32_t* n_edges_out = nullptr;
+  unsigned long long* scan_scratch = nullptr;
+  int32_t* err = nullptr;
+};
+void launch_walk_hop(const WalkHopArgs& a, int cap_dst, cudaStream_t stream);
+int walk_scan_scratch_words(int cap_dst);
+
 // ---------------------------------------------------------------- compaction (S2)
 struct CompactArgs {
   const int32_t* dst_nid = nullptr;
@@ -119,7 +144,16 @@ struct AggArgs {
   int32_t agg_col = 0;               // column of the aggregate in out
   int32_t self_col = -1;             // >= 0: also copy the dst row here
   float self_scale = 0.f;            // != 0: out_agg += self_scale * self (GIN)
-  int32_t zero_tail_rows = 0;        // write zeros in rows [n_dst, roundup(n_dst, this))
+  int32_t zero_tail_rows = 0;        // write zeros in rows [n_dst, roundup(n_dst, this)) below cap_rows
+  int32_t cap_rows = 0;              // rows of the output buffer (set by the launcher)
+  // optional epilogue on the aggregate (GraphConv with the projection applied first):
+  // out = dropout(act(agg + bias)); the dropout mask of element (r, c) is the Philox
+  // draw of index r * out_stride + c (c counted from agg_col), as in the GEMM epilogue
+  const float* bias = nullptr;
+  int32_t act = 0;                   // 1: ReLU
+  float dropout_p = 0.f;
+  const int64_t* counters = nullptr;
+  uint32_t dropout_salt = 0;
   int32_t* err = nullptr;
 };
 void launch_aggregate(const AggArgs& a, int cap_dst, cudaStream_t stream);
@@ -201,6 +235,154 @@ struct AdamArgs {
   const float* grad_scale_dev = nullptr;  // multiplies grad_scale when given
 };
 void launch_adam(const AdamArgs& a, cudaStream_t stream);
+
+// ---------------------------------------------------------------- loss / normalisation (nn.cu)
+// Softmax cross-entropy over bf16 logits rows (one warp per row): loss, gradient
+// (softmax - onehot) / n_sel, correct count and the bias gradient (column sums).
+// Rows with row_mask == 0 (or >= *n_rows_ptr) get a zero gradient; rows up to
+// roundup(n, zero_tail_rows) are written so split-K reductions see zeros.
+struct CeArgs {
+  const __nv_bfloat16* logits = nullptr;
+  int64_t ld = 0;
+  int32_t n_classes = 0;
+  const int32_t* labels = nullptr;
+  const int32_t* n_rows_ptr = nullptr;
+  int32_t cap_rows = 0;
+  const uint8_t* row_mask = nullptr;
+  const int32_t* n_sel_ptr = nullptr;  // denominator of the mean (null: the row count)
+  __nv_bfloat16* dlogits = nullptr;
+  int64_t ld_dl = 0;
+  float* dbias = nullptr;
+  float* loss_sum = nullptr;
+  int32_t* correct = nullptr;
+  int32_t zero_tail_rows = 64;
+};
+void launch_cross_entropy(const CeArgs& a, cudaStream_t stream);
+
+// BatchNorm1d over the live rows (training: batch statistics, biased variance for
+// the normalisation, unbiased for the running estimate; eval: running estimates),
+// optionally followed by ReLU.  sums[2 * dim] must be zero before the forward and is
+// kept for the backward.
+struct BnArgs {
+  const __nv_bfloat16* x = nullptr;
+  int64_t ldx = 0;
+  int32_t dim = 0;
+  const int32_t* n_ptr = nullptr;
+  int32_t cap = 0;
+  float* sums = nullptr;
+  const float* gamma = nullptr;
+  const float* beta = nullptr;
+  float* running_mean = nullptr;     // [stat_dim] (columns past it are padding)
+  float* running_var = nullptr;
+  int32_t stat_dim = 0;
+  int64_t* num_batches = nullptr;
+  float momentum = 0.1f, eps = 1e-5f;
+  bool training = true;
+  int32_t act = 1;
+  __nv_bfloat16* y = nullptr;
+  int64_t ldy = 0;
+  int32_t zero_tail_rows = 64;
+};
+void launch_batchnorm_fwd(const BnArgs& a, cudaStream_t stream);
+// Backward of (ReLU o BatchNorm): dy is fp32 (cleared after reading when clear_dy),
+// dx written as bf16; dgamma / dbeta accumulated (+=).  bsums[2 * dim] zero before.
+struct BnBwdArgs {
+  const __nv_bfloat16* x = nullptr;
+  int64_t ldx = 0;
+  const __nv_bfloat16* y = nullptr;   // forward output (ReLU mask); null: no activation
+  int64_t ldy = 0;
+  float* dy = nullptr;
+  const __nv_bfloat16* dy_bf16 = nullptr;  // alternative bf16 gradient (e.g. from the loss)
+  int64_t lddy = 0;
+  bool clear_dy = true;
+  int32_t dim = 0;
+  const int32_t* n_ptr = nullptr;
+  int32_t cap = 0;
+  const float* sums = nullptr;
+  float* bsums = nullptr;
+  const float* gamma = nullptr;
+  float* dgamma = nullptr;
+  float* dbeta = nullptr;
+  float eps = 1e-5f;
+  __nv_bfloat16* dx = nullptr;
+  int64_t lddx = 0;
+  int32_t zero_tail_rows = 64;
+};
+void launch_batchnorm_bwd(const BnBwdArgs& a, cudaStream_t stream);
+
+// Row L2 normalisation (PinSAGE): y = z / |z| (|z| == 0 -> 1); norms kept for the
+// backward, dz = (dy - y (y . dy)) / |z| with dy fp32 (cleared after reading) or bf16,
+// dz fp32.
+void launch_l2norm_fwd(const __nv_bfloat16* z, int64_t ldz, int32_t dim, const int32_t* n_ptr, int cap,
+                       __nv_bfloat16* y, int64_t ldy, float* norms, cudaStream_t stream);
+void launch_l2norm_bwd(const __nv_bfloat16* y, int64_t ldy, float* dy, const __nv_bfloat16* dy_bf16, int64_t lddy,
+                       const float* norms, int32_t dim, const int32_t* n_ptr, int cap, float* dz, int64_t lddz,
+                       cudaStream_t stream);
+// dst[r, :dim] += src[r, :dim] for r < *n_ptr (fp32 += bf16)
+void launch_add_bf16_rows(float* dst, int64_t ldd, const __nv_bfloat16* src, int64_t lds, int32_t dim,
+                          const int32_t* n_ptr, int cap, cudaStream_t stream);
+
+// Dropout on a bf16 matrix: out = in * keep / (1 - p) with the Philox mask of index
+// r * ld_mask + c (the GEMM epilogue's rule); grad variant scales an fp32 gradient
+// in place with the same mask.  Rows >= *n_ptr are written as zeros (out) / skipped.
+void launch_dropout_rows(const __nv_bfloat16* in, int64_t ldi, __nv_bfloat16* out, int64_t ldo, int32_t dim,
+                         int64_t ld_mask, const int32_t* n_ptr, int cap, float p, const int64_t* counters,
+                         uint32_t salt, cudaStream_t stream);
+void launch_dropout_grad(float* g, int64_t ldg, int32_t dim, int64_t ld_mask, const int32_t* n_ptr, int cap, float p,
+                         const int64_t* counters, uint32_t salt, cudaStream_t stream);
+// fp32 -> bf16 rows (clears the fp32 source when clear), rows past *n_ptr zeroed
+// up to roundup(n, zero_tail_rows)
+void launch_f32_to_bf16_rows(float* src, int64_t lds, __nv_bfloat16* dst, int64_t ldd, int32_t dim,
+                             const int32_t* n_ptr, int cap, bool clear, int32_t zero_tail_rows, cudaStream_t stream);
+
+// ---------------------------------------------------------------- GAT (gat.cu)
+// Attention logits of every source row: el[u, h] = z_u[h] . a_l[h] and, for the
+// first n_dst rows, er[v, h] = z_v[h] . a_r[h] (z: bf16 [n_src, H*F]).
+struct GatArgs {
+  const int32_t* indptr = nullptr;
+  const int32_t* indices = nullptr;
+  const int32_t* n_dst_ptr = nullptr;
+  const int32_t* n_src_ptr = nullptr;
+  int32_t cap_dst = 0, cap_src = 0;
+  int32_t heads = 0, feat = 0;        // H, F (H * F <= 1024, F % 8 == 0)
+  const __nv_bfloat16* z = nullptr;
+  int64_t ldz = 0;
+  const float* attn_l = nullptr;      // [H * F]
+  const float* attn_r = nullptr;
+  const float* bias = nullptr;        // [H * F]
+  float* el = nullptr;                // [cap_src, H]
+  float* er = nullptr;                // [cap_dst, H]
+  float* smax = nullptr;              // [cap_dst, H] softmax max, kept for the backward
+  float* ssum = nullptr;              // [cap_dst, H] softmax denominator
+  float slope = 0.2f;
+  // forward output: hidden layers write act(out) flattened [n_dst, H*F] with dropout;
+  // the last layer writes the mean over heads [n_dst, F]
+  bool mean_heads = false;
+  int32_t act = 1;
+  float dropout_p = 0.f;
+  const int64_t* counters = nullptr;
+  uint32_t dropout_salt = 0;
+  __nv_bfloat16* out = nullptr;
+  int64_t ldo = 0;
+  // backward
+  const __nv_bfloat16* dout = nullptr;  // [n_dst, H*F] (or [n_dst, F] with mean_heads)
+  int64_t lddo = 0;
+  float* edge_scratch = nullptr;        // [cap_edges, H]
+  float* del = nullptr;                 // [cap_src, H] (zero before)
+  float* der = nullptr;                 // [cap_dst, H]
+  float* dz = nullptr;                  // fp32 [cap_src, H*F] (zero before)
+  int64_t lddz = 0;
+  float* dbias = nullptr;
+  float* dattn_l = nullptr;
+  float* dattn_r = nullptr;
+  __nv_bfloat16* dz_bf16 = nullptr;     // GEMM operand of the backward projections
+  int64_t lddzb = 0;
+  int32_t zero_tail_rows = 64;
+  int32_t* err = nullptr;
+};
+void launch_gat_scores(const GatArgs& a, cudaStream_t stream);
+void launch_gat_fwd(const GatArgs& a, cudaStream_t stream);
+void launch_gat_bwd(const GatArgs& a, cudaStream_t stream);
 
 // counters = [seed, epoch, step_in_epoch, global_step, gen, adam_t]: advance the step
 void launch_step_end(int64_t* counters, cudaStream_t stream);

@@ -16,9 +16,13 @@
 // which lets the first layer aggregate straight from the resident feature table
 // (no gathered copy of the input features is materialised).
 //
+// An optional epilogue adds a bias, applies ReLU and dropout to the aggregate
+// (GraphConv when the projection runs before the aggregation).
+//
 // Backward: dsrc[src_e] += coef_e * dagg_v with vector fp32 reductions
 // (red.global.add.v4.f32), plus the gradient of the self block to the dst rows.
 #include "common.cuh"
+#include "grappa/rng.h"
 #include "kernels.h"
 
 #include <algorithm>
@@ -51,7 +55,7 @@ __global__ void __launch_bounds__(kThreads) aggregate_kernel(AggArgs a) {
   const int sub = lane % lpe;
   const int warps_total = (gridDim.x * kThreads) >> 5;
   const int wg = (blockIdx.x * kThreads + threadIdx.x) >> 5;
-  const int tail = a.zero_tail_rows > 0 ? static_cast<int>(ceil_div(n_dst, a.zero_tail_rows) * a.zero_tail_rows) : n_dst;
+  const int tail = a.zero_tail_rows > 0 ? min(a.cap_rows, static_cast<int>(ceil_div(n_dst, a.zero_tail_rows) * a.zero_tail_rows)) : n_dst;
   for (int row = wg; row < tail; row += warps_total) {
     if (row >= n_dst) {
       // zero rows past the count so that a split-K reduction over this buffer sees zeros
@@ -133,6 +137,15 @@ __global__ void __launch_bounds__(kThreads) aggregate_kernel(AggArgs a) {
     else if (a.mode == kAggWeighted) scale = 1.f / fmaxf(wsum, 1.f);
     if (g == 0) {
       const int64_t rs = a.src_map ? a.src_map[row] : row;
+      uint64_t key = 0;
+      uint32_t thr = 0;
+      float keep_scale = 1.f;
+      if (a.dropout_p > 0.f) {
+        key = hop_key(static_cast<uint64_t>(a.counters[0]) ^ 0xD80Full, static_cast<uint64_t>(a.counters[1]),
+                      static_cast<uint64_t>(a.counters[2]), a.dropout_salt);
+        thr = static_cast<uint32_t>(static_cast<double>(a.dropout_p) * 4294967296.0);
+        keep_scale = 1.f / (1.f - a.dropout_p);
+      }
 #pragma unroll
       for (int q = 0; q < CPL; ++q) {
         const int c = sub + q * lpe;
@@ -149,6 +162,28 @@ __global__ void __launch_bounds__(kThreads) aggregate_kernel(AggArgs a) {
 #pragma unroll
             for (int j = 0; j < 8; ++j) o[j] += a.self_scale * fs[j];
           }
+        }
+        if (a.bias) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] += a.bias[c * 8 + j];
+        }
+        if (a.act == 1) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] = fmaxf(o[j], 0.f);
+        }
+        if (a.dropout_p > 0.f) {
+          const uint64_t base = static_cast<uint64_t>(row) * static_cast<uint64_t>(a.out_stride) +
+                                static_cast<uint64_t>(a.agg_col + c * 8);
+          const U4 r0 = index_draw4(key, base >> 2, 0);
+          const U4 r1 = index_draw4(key, (base >> 2) + 1, 0);
+          o[0] = r0.x >= thr ? o[0] * keep_scale : 0.f;
+          o[1] = r0.y >= thr ? o[1] * keep_scale : 0.f;
+          o[2] = r0.z >= thr ? o[2] * keep_scale : 0.f;
+          o[3] = r0.w >= thr ? o[3] * keep_scale : 0.f;
+          o[4] = r1.x >= thr ? o[4] * keep_scale : 0.f;
+          o[5] = r1.y >= thr ? o[5] * keep_scale : 0.f;
+          o[6] = r1.z >= thr ? o[6] * keep_scale : 0.f;
+          o[7] = r1.w >= thr ? o[7] * keep_scale : 0.f;
         }
         *reinterpret_cast<uint4*>(a.out + row * a.out_stride + a.agg_col + c * 8) = f32_to_bf16x8(o);
       }
@@ -262,10 +297,13 @@ int grid_for_rows(int cap_rows) {
 
 }  // namespace
 
-void launch_aggregate(const AggArgs& a, int cap_dst, cudaStream_t stream) {
+void launch_aggregate(const AggArgs& args, int cap_dst, cudaStream_t stream) {
+  AggArgs a = args;
+  a.cap_rows = cap_dst;
   if (a.dim % 8 != 0) throw std::invalid_argument("aggregate: dim must be a multiple of 8");
   if (a.src_stride % 8 != 0 || a.out_stride % 8 != 0 || a.agg_col % 8 != 0 || (a.self_col >= 0 && a.self_col % 8 != 0))
     throw std::invalid_argument("aggregate: strides and column offsets must be multiples of 8 elements");
+  if (a.dropout_p > 0.f && !a.counters) throw std::invalid_argument("aggregate: dropout needs the step counters");
   const int rows = a.zero_tail_rows > 0 ? static_cast<int>(ceil_div(cap_dst, a.zero_tail_rows) * a.zero_tail_rows) : cap_dst;
   const int grid = grid_for_rows(rows);
   const int chunks = a.dim / 8;

@@ -1,25 +1,31 @@
-"""Mini-batch training engine on the sm_100a kernels.
+"""Mini-batch and full-graph training engines on the sm_100a kernels.
 
-One training step of a sampled-block GNN, entirely on the device:
+One training step of a block GNN, entirely on the device:
 
   for hop h = 0..L-1 (seed hop first, fanouts reversed as in the reference):
-      S1  sample_hop      pick counts + look-back scan + Philox picks (+ coverage of the seeds)
-      S2  compact         dst-first relabelling with a dense tagged id map (3 kernels)
-  layer l = 0..L-1 (input layer first, on hop h = L-1-l):
-      K-SpMM  aggregate   [h_dst | mean h_src] (layer 0 reads the resident feature table
-                          through the block's source ids, so no gathered copy is made)
-      K-GEMM  tcgen05     [h_dst | agg] . [W_self | W_neigh]^T + b, ReLU, dropout (hidden)
-                          or the fused softmax cross-entropy + its gradient (last layer)
-  backward, last layer first:
-      K-GEMM  dW += dY^T X  (split-K, fp32 reductions straight into the flat gradient)
-      K-GEMM  dX  = dY W    (MN-major operand, no transposes)
-      K-SpMM  transpose aggregation into fp32 accumulators
-      act_bwd ReLU/dropout mask from the stored activation, bias gradient, clears the accumulator
-  K-AR   coverage-weighted all-reduce + Adam over NVLink peer memory (W > 1), or Adam (W = 1)
+      S1  sample_hop / walk_hop  pick counts + look-back scan + Philox picks (or the
+                                 PinSAGE random walks + top-k visited)
+      S2  compact                dst-first relabelling with a dense tagged id map
+  layer l = 0..L-1 (input layer first, on hop h = L-1-l): the model's layer kernels
+  backward, last layer first: the transposed kernels, fp32 reductions
+  K-AR   coverage-weighted all-reduce + Adam over NVLink peer memory (W > 1), or Adam
+
+Layer programs (kernels in grappa_b200/csrc/cuda):
+  SAGE     aggregate [h_dst | mean h_src] -> tcgen05 GEMM (+bias, ReLU, dropout; or the
+           fused softmax cross-entropy of the last layer)
+  GCN      in <= out: aggregate (sym. norm) -> GEMM;  in > out: GEMM over the source
+           rows -> aggregate with the bias/ReLU/dropout epilogue (DGL's order)
+  GIN      aggregate (sum + self) -> GEMM -> BatchNorm+ReLU -> GEMM -> BatchNorm+ReLU
+  GAT      GEMM over the source rows -> attention logits -> fused edge softmax +
+           weighted sum (+ReLU, dropout; head mean on the last layer)
+  PinSAGE  dropout -> GEMM (+bias, ReLU) over the sources -> weighted mean over the
+           random-walk neighbours -> [agg | h_dst] -> GEMM (+bias, ReLU) -> L2 norm
 
 Every buffer is allocated once at its capacity (batch size times the fanout
 products); the kernels read the live sizes from device counters, so the step has
 no host synchronisation and is captured once into a CUDA graph and replayed.
+Full-graph training uses the same engines with ``FullGraphBlocks`` (the working
+graph as a fixed block for every layer) in place of the sampler.
 """
 import math
 
@@ -27,17 +33,19 @@ import torch
 
 from grappa_b200 import _native
 from grappa_b200.models.flat import pad8
-from grappa_b200.sampler_gpu import C_ADAM, C_EPOCH, C_SEED, C_STEP, GpuNeighborSampler, new_counters
+from grappa_b200.sampler_gpu import C_EPOCH, C_STEP, GpuNeighborSampler, new_counters
 
 GEMM_STORE_BF16, GEMM_STORE_F32, GEMM_ATOMIC_F32, GEMM_CROSS_ENTROPY = 0, 1, 2, 3
 AGG_MEAN, AGG_SUM, AGG_GCN, AGG_WEIGHTED = 0, 1, 2, 3
 
 # kernels launched by each binding (memsets excluded)
 KERNELS_PER_CALL = {
-    "sample_hop": 1, "compact": 3, "gemm": 1, "aggregate": 1, "aggregate_bwd": 1, "act_bwd": 1,
+    "sample_hop": 1, "walk_hop": 1, "compact": 3, "gemm": 1, "aggregate": 1, "aggregate_bwd": 1, "act_bwd": 1,
     "gather_scalar": 1, "gather_rows": 1, "adam": 1, "allreduce_adam": 1, "step_end": 1, "src_norm": 2,
     "pull_rows": 1, "csr_merge": 1, "mark_ids": 1, "iota_map": 1, "mark_compact": 1, "peer_copy": 1,
-    "shuffle_keys": 1,
+    "shuffle_keys": 1, "cross_entropy": 1, "batchnorm_fwd": 2, "batchnorm_bwd": 2, "l2norm_fwd": 1,
+    "l2norm_bwd": 1, "dropout_rows": 1, "dropout_grad": 1, "f32_to_bf16_rows": 1, "add_bf16_rows": 1,
+    "gat_scores": 1, "gat_fwd": 1, "gat_bwd": 2,
 }
 
 
@@ -61,9 +69,9 @@ class LaunchCounter:
         return wrapped
 
 
-def bn_for(n):
-    """Tile width of the GEMM for an output width n (K-major operands)."""
-    if n == 48:
+def bn_for(n, mn_major=False):
+    """Tile width of the GEMM for an output width n (48 only with K-major B)."""
+    if n == 48 and not mn_major:
         return 48
     if n <= 64:
         return 64
@@ -80,13 +88,99 @@ def split_k(rows, n_tiles, sms=148, min_kblocks=8):
     return max(1, min(by_work, by_sms))
 
 
-class SageEngine:
-    """GraphSAGE (mean) mini-batch training on one rank's working graph."""
+# ---------------------------------------------------------------------- block sources
+class FullGraphBlocks:
+    """The working graph's own + neighbour rows as one fixed block used by every layer
+    (isolated full-graph training, reference experiments/grappa/train/
+    t10n_fullgraph_train.py:163-205): dst = src = rows [0, n), edges = in-edges among
+    them.  Same interface as GpuNeighborSampler; ``sample`` does nothing."""
+
+    def __init__(self, indptr, indices, n_layers, device, labels, train_rows):
+        dev = torch.device(device)
+        self.L = int(n_layers)
+        n = int(indptr.numel() - 1)
+        self.n = n
+        self.B = n
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.cnt = torch.tensor([n] + [int(indices.numel()), n, 0] * self.L, **i32)
+        self.seeds = torch.arange(n, **i32)
+        ip = indptr.to(dev, torch.int32).contiguous()
+        ix = indices.to(dev, torch.int32).contiguous()
+        self.indptr = [ip] * self.L
+        self.indices = [ix] * self.L
+        self.src = [self.seeds] * self.L
+        self.cap_dst = [n] * self.L
+        self.cap_src = [n] * self.L
+        self.cap_e = [max(1, int(ix.numel()))] * self.L
+        self.w = [None] * self.L
+        self.labels = labels.to(dev, torch.int32).contiguous()
+        self.row_mask = train_rows.to(dev, torch.uint8).contiguous()
+        self.n_sel = torch.tensor([int(self.row_mask.sum())], **i32)
+        self.full_graph = True
+
+    def n_seeds(self):
+        return self.cnt[0:1]
+
+    def n_edges(self, h):
+        return self.cnt[1 + 3 * h:2 + 3 * h]
+
+    def n_src(self, h):
+        return self.cnt[2 + 3 * h:3 + 3 * h]
+
+    def n_dst(self, h):
+        return self.n_seeds() if h == 0 else self.n_src(h - 1)
+
+    def sample(self, *args, **kwargs):
+        return None
+
+
+class GpuWalkSampler(GpuNeighborSampler):
+    """PinSAGE sampler on the GPU: per hop walk_hop (random walks + top-k visited,
+    grappa_b200/csrc/cuda/walk.cu) then the S2 compaction; the visit counts are the
+    edge weights ``w[h]`` in the block's edge order."""
+
+    def __init__(self, n_layers, batch_size, n_nodes_cap, device, cu=None, length=None, restart_prob=0.5,
+                 num_walks=4, num_neighbors=5):
+        super().__init__([num_neighbors] * int(n_layers), batch_size, n_nodes_cap, device, cu=cu)
+        self.length = int(length if length is not None else n_layers)
+        self.restart_prob = float(restart_prob)
+        self.num_walks = int(num_walks)
+        self.num_neighbors = int(num_neighbors)
+        self.w = [torch.zeros(self.cap_e[h], dtype=torch.float32, device=self.device) for h in range(self.L)]
+        self.wscr = [torch.zeros(self.cu.walk_scratch_words(self.cap_dst[h]), dtype=torch.int64, device=self.device)
+                     for h in range(self.L)]
+
+    def sample(self, indptr, indices, counters, gideg=None, cov=None, err=None):
+        cu = self.cu
+        err = self.err if err is None else err
+        for h in range(self.L):
+            dst = self.dst(h)
+            cu.walk_hop(indptr, indices, dst, self.n_dst(h), 0, self.length, self.restart_prob, self.num_walks,
+                        self.num_neighbors, counters, h, self.indptr[h], self.nbr[h], self.w[h], self.n_edges(h),
+                        self.wscr[h], err, self.cap_dst[h])
+            cu.compact(dst, self.n_dst(h), self.nbr[h], self.n_edges(h), self.map, self.src[h], self.sampled[h],
+                       self.indices[h], self.n_src(h), self.cscr[h], err, self.cap_dst[h], self.cap_e[h], counters, h)
+
+    def blocks(self):
+        out = super().blocks()
+        cnt = self.cnt.cpu().tolist()
+        for b, h in zip(out, range(self.L - 1, -1, -1)):
+            b.edata["weights"] = self.w[h][: cnt[1 + 3 * h]].clone()
+        return out
+
+
+# ---------------------------------------------------------------------- engines
+class BlockEngine:
+    """Shared parts: parameters (flat fp32 master, bf16 working copy, gradient, Adam
+    moments), device counters, the block source, the optimizer step, CUDA-graph
+    capture.  Subclasses implement ``_alloc_layers``, ``_forward`` and ``_backward``."""
+
+    model_name = None
 
     def __init__(self, model, n_nodes_cap, fanouts, batch_size, device, lr=3e-3, comm=None, seed=0,
-                 fused_allreduce=True, use_cuda_graph=True, betas=(0.9, 0.999), eps=1e-8):
-        if getattr(model, "name", None) != "sage":
-            raise ValueError("SageEngine trains GraphSAGE models")
+                 fused_allreduce=True, use_cuda_graph=True, betas=(0.9, 0.999), eps=1e-8, blocks=None):
+        if getattr(model, "name", None) != self.model_name:
+            raise ValueError(f"{type(self).__name__} trains {self.model_name} models")
         self.cu = LaunchCounter(_native.cuda())
         self.launches_per_step = 0
         self.model = model
@@ -94,19 +188,17 @@ class SageEngine:
         self.world = 1 if comm is None else comm.world
         self.rank = 0 if comm is None else comm.rank
         self.fanouts = [int(f) for f in fanouts]
-        self.L = len(self.fanouts)
-        if self.L != model.n_layers:
+        self.L = len(model.layers)
+        if blocks is None and len(self.fanouts) != self.L:
             raise ValueError("one fanout per layer")
-        self.B = int(batch_size)
         self.lr, self.betas, self.eps = float(lr), betas, float(eps)
-        self.p = float(model.dropout_p)
+        self.p = float(getattr(model, "dropout_p", 0.0))
         self.device = torch.device(device)
         self.seed = int(seed)
         self.use_cuda_graph = use_cuda_graph
         self.fused_allreduce = fused_allreduce and self.world > 1
         dev = self.device
 
-        # parameters: flat fp32 master, bf16 working copy, gradient, Adam moments
         model.place(dev)
         self.flat = model.flat
         self.wbf = self.flat.to(torch.bfloat16)
@@ -114,7 +206,6 @@ class SageEngine:
         self.m = torch.zeros_like(self.flat)
         self.v = torch.zeros_like(self.flat)
 
-        # device scalars
         self.counters = new_counters(self.seed, dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
         self.fstats = torch.zeros(4, dtype=torch.float32, device=dev)  # cov_sum, cov_n, loss_sum, spare
@@ -122,42 +213,86 @@ class SageEngine:
         self._ce_dummy = torch.zeros((1, 1), dtype=torch.float32, device=dev)
         self.allreduce = FusedAllReduceAdam(comm, self.flat.numel()) if self.fused_allreduce else None
 
-        self.sm = GpuNeighborSampler(self.fanouts, self.B, n_nodes_cap, dev, cu=self.cu)
+        if blocks is None:
+            self.sm = self._make_sampler(int(batch_size), int(n_nodes_cap), dev)
+        else:
+            self.sm = blocks
+        self.full_graph = getattr(self.sm, "full_graph", False)
+        self._cov_one = torch.ones(2, dtype=torch.float32, device=dev)
+        self.B = self.sm.B
         self.seeds = self.sm.seeds
         self.seed_label = torch.zeros(self.B, dtype=torch.int32, device=dev)
+        self.n_classes = model.n_classes
+        self.lay = []
         self._alloc_layers()
         self._working = None
         self._graph = None
 
-    # ------------------------------------------------------------------ buffers
-    def _alloc_layers(self):
-        dev = self.device
-        L, model = self.L, self.model
-        self.lay = []
-        for l, layer in enumerate(model.layers):
-            h = L - 1 - l
-            ip, op = pad8(layer.in_feats), pad8(layer.out_feats)
-            K = 2 * ip
-            rows = self.sm.cap_dst[h]
-            seg_w = model.segment(layer.seg_w)
-            seg_b = model.segment(layer.seg_b)
-            spec = dict(h=h, ip=ip, op=op, K=K, rows=rows,
-                        W=seg_w.view(self.wbf), bias=seg_b.view(self.flat)[0],
-                        gW=seg_w.view(self.grad), gb=seg_b.view(self.grad)[0],
-                        X=torch.zeros((rows, K), dtype=torch.bfloat16, device=dev),
-                        dY=torch.zeros((rows, op), dtype=torch.bfloat16, device=dev))
-            if l < L - 1:
-                spec["H"] = torch.zeros((rows, op), dtype=torch.bfloat16, device=dev)
-                spec["dH"] = torch.zeros((rows, op), dtype=torch.float32, device=dev)
-            if l > 0:
-                spec["dX"] = torch.zeros((rows, K), dtype=torch.bfloat16, device=dev)
-            self.lay.append(spec)
-        self.n_classes = model.n_classes
+    def _make_sampler(self, batch_size, n_nodes_cap, dev):
+        return GpuNeighborSampler(self.fanouts, batch_size, n_nodes_cap, dev, cu=self.cu)
 
-    # ------------------------------------------------------------------ graph binding
+    def set_blocks(self, blocks):
+        """Replace a fixed block source (full-graph training after a repartition) and
+        re-size the layer buffers; parameters and optimizer state are kept."""
+        self.sm = blocks
+        self.full_graph = getattr(blocks, "full_graph", False)
+        self.B = blocks.B
+        self.seeds = blocks.seeds
+        self.seed_label = torch.zeros(self.B, dtype=torch.int32, device=self.device)
+        self.lay = []
+        self._alloc_layers()
+        self._graph = None
+
+    # ------------------------------------------------------------------ helpers
+    def _seg(self, name, buf=None):
+        return self.model.segment(name).view(self.flat if buf is None else buf)
+
+    def _n_dst(self, h):
+        return self.sm.n_dst(h)
+
+    def _input(self, l):
+        """(rows, src_map) that layer l aggregates from."""
+        h = self.L - 1 - l
+        if l == 0:
+            return self._working.feat, (None if self.full_graph else self.sm.src[h])
+        return self.lay[l - 1]["H"], None
+
+    def _gathered_input(self, l, s):
+        """Source rows of layer l as a contiguous GEMM operand."""
+        h = self.L - 1 - l
+        if l > 0:
+            return self.lay[l - 1]["H"]
+        if self.full_graph:
+            return self._working.feat
+        self.cu.gather_rows(self._working.feat, self.sm.src[h], self.sm.n_src(h), 0, self.sm.cap_src[h], s["ip"],
+                            s["Xg"])
+        return s["Xg"]
+
+    def _labels_rows(self):
+        if self.full_graph:
+            return self.sm.labels, self.sm.row_mask, self.sm.n_sel
+        return self.seed_label, None, None
+
+    def _ce(self, logits, C, dl, dbias, h):
+        labels, mask, n_sel = self._labels_rows()
+        self.cu.cross_entropy(logits, C, labels, self._n_dst(h), self.sm.cap_dst[h], mask, n_sel, dl, dbias,
+                              self.fstats[2:3], self.istats[0:1])
+
+    def _gemm(self, A, a_mn, B, b_mn, M_cap, M_dev, N, K_cap, K_dev, splits, C, mode, bias=None, act=0, p=0.0,
+              salt=0, bn=None):
+        bn = bn or bn_for(N, b_mn)
+        self.cu.gemm(A, a_mn, B, b_mn, M_cap, M_dev, N, K_cap, K_dev, splits, C, mode, bias, act, p,
+                     self.counters if p > 0 else None, salt, None, 0, None, None, None, None, None, None, self.err, bn)
+
+    def _dw(self, A, B, M, N, K_cap, K_dev, gW):
+        """gW[M, N] += A^T B with A [K, M], B [K, N] (both MN-major), split-K over rows."""
+        n_tiles = math.ceil(M / 128) * math.ceil(N / 256)
+        self._gemm(A, True, B, True, M, None, N, K_cap, K_dev, split_k(K_cap, n_tiles), gW, GEMM_ATOMIC_F32, bn=256)
+
+    # ------------------------------------------------------------------ binding
     def bind_working(self, working, labels, gideg):
         """Point the engine at a working graph (after a repartition)."""
-        if working.indptr.numel() - 1 > self.sm.n_nodes_cap:
+        if not self.full_graph and working.indptr.numel() - 1 > self.sm.n_nodes_cap:
             raise ValueError("working graph larger than the engine's node capacity")
         self._working = working
         self.labels = labels
@@ -169,72 +304,36 @@ class SageEngine:
         self.counters[C_STEP] = 0
 
     # ------------------------------------------------------------------ the step
-    def _n_dst(self, h):
-        return self.sm.n_dst(h)
+    def _cov(self):
+        """[coverage sum, count] of the step: the sampler's for mini-batches; a fixed 1/1
+        for full-graph training (every in-edge of the partition is present)."""
+        return self._cov_one if self.full_graph else self.fstats[0:2]
 
     def _sample(self):
+        if self.full_graph:
+            return
         w = self._working
         self.cu.gather_scalar(self.labels, self.sm.seeds, self.sm.n_seeds(), 0, self.B, self.seed_label)
         self.sm.sample(w.indptr, w.indices, self.counters, gideg=self.gideg, cov=self.fstats[0:2], err=self.err)
 
     def _forward(self, training=True):
-        cu, w, sm = self.cu, self._working, self.sm
-        L = self.L
-        for l, s in enumerate(self.lay):
-            h = s["h"]
-            if l == 0:
-                src, src_map = w.feat, sm.src[h]
-            else:
-                src, src_map = self.lay[l - 1]["H"], None
-            cu.aggregate(sm.indptr[h], sm.indices[h], self._n_dst(h), 0, sm.cap_dst[h], src, src_map,
-                         s["ip"], AGG_MEAN, None, None, None, s["X"], s["ip"], 0, 0.0, 0, self.err)
-            bn = bn_for(s["op"])
-            if l < L - 1:
-                cu.gemm(s["X"], False, s["W"], False, s["rows"], self._n_dst(h), s["op"], s["K"], None, 1,
-                        s["H"], GEMM_STORE_BF16, s["bias"], 1, self.p if training else 0.0,
-                        self.counters, l, None, 0, None, None, None, None, None, None, self.err, bn)
-            else:
-                cu.gemm(s["X"], False, s["W"], False, s["rows"], self._n_dst(h), s["op"], s["K"], None, 1,
-                        self._ce_dummy, GEMM_CROSS_ENTROPY, s["bias"], 0, 0.0, None, 0, self.seed_label,
-                        self.n_classes, s["dY"], self.fstats[2:3], self.istats[0:1], None, self.sm.n_seeds(),
-                        s["gb"] if training else None, self.err, bn)
+        raise NotImplementedError
 
     def _backward(self):
-        cu, sm = self.cu, self.sm
-        L = self.L
-        scale = 1.0 / (1.0 - self.p) if self.p > 0 else 1.0
-        for l in range(L - 1, -1, -1):
-            s = self.lay[l]
-            h = s["h"]
-            n_tiles = math.ceil(s["op"] / 128) * math.ceil(s["K"] / 256)
-            # dW += dY^T X (split-K over the block's rows, fp32 reductions into the gradient)
-            cu.gemm(s["dY"], True, s["X"], True, s["op"], None, s["K"], s["rows"], self._n_dst(h),
-                    split_k(s["rows"], n_tiles), s["gW"], GEMM_ATOMIC_F32, None, 0, 0.0, None, 0, None, 0,
-                    None, None, None, None, None, None, self.err, 256)
-            if l == 0:
-                break
-            # dX = dY W (W read MN-major)
-            cu.gemm(s["dY"], False, s["W"], True, s["rows"], self._n_dst(h), s["K"], s["op"], None, 1, s["dX"],
-                    GEMM_STORE_BF16, None, 0, 0.0, None, 0, None, 0, None, None, None, None, None, None, self.err,
-                    256)
-            prev = self.lay[l - 1]
-            # transpose aggregation: d(self) -> dst rows, d(agg) -> sources
-            cu.aggregate_bwd(sm.indptr[h], sm.indices[h], self._n_dst(h), 0, sm.cap_dst[h], s["dX"],
-                             s["ip"], 0, 0.0, s["ip"], AGG_MEAN, None, None, None, prev["dH"], self.err)
-            cu.act_bwd(prev["dH"], prev["H"], prev["dY"], self._n_dst(prev["h"]), 0, prev["op"], scale, prev["gb"],
-                       prev["rows"])
+        raise NotImplementedError
 
     def _update(self):
         cu = self.cu
         b1, b2 = self.betas
         if self.fused_allreduce:
-            self.allreduce.step(self.grad, self.fstats[0:2], self.counters, self.flat, self.m, self.v, self.wbf,
+            self.allreduce.step(self.grad, self._cov(), self.counters, self.flat, self.m, self.v, self.wbf,
                                 self.lr, b1, b2, self.eps, self.err, cu=cu)
         elif self.world > 1:
             # the reference's path (t10n/grad.py:6-24): scale by c_r / W, NCCL SUM all-reduce, Adam
             import torch.distributed as dist
 
-            c = self.fstats[0:1] / self.fstats[1:2].clamp(min=1.0)
+            cov = self._cov()
+            c = cov[0:1] / cov[1:2].clamp(min=1.0)
             self.grad.mul_(c / self.world)
             dist.all_reduce(self.grad)
             cu.adam(self.flat, self.m, self.v, self.grad, self.wbf, self.lr, b1, b2, self.eps, 0.0, self.counters,
@@ -267,6 +366,8 @@ class SageEngine:
         """Copy this step's seeds ([B] int32) and seed count ([1] int32) into the static
         buffers.  Both may live in device memory or in pinned host memory; they are
         plain copies (no kernels) and must stay unchanged until the step has run."""
+        if self.full_graph:
+            return
         self.seeds.copy_(seeds, non_blocking=True)
         self.sm.cnt[0:1].copy_(count, non_blocking=True)
 
@@ -288,7 +389,7 @@ class SageEngine:
             self.capture()
 
     def predict(self, seeds, count):
-        """Forward only (dropout off) for the given seeds; returns (correct, loss) on the device."""
+        """Forward only (eval mode) for the given seeds; returns (correct, loss) on the device."""
         self.load_seeds(seeds, count)
         self.cu.zero_(self.fstats)
         self.cu.zero_(self.istats)
@@ -300,6 +401,488 @@ class SageEngine:
         e = int(self.err.item())
         if e:
             raise RuntimeError(f"device error word {e:#x} (bits: grappa_b200/csrc/cuda/common.cuh kErr*)")
+
+    # checkpoint helpers --------------------------------------------------------------
+    def optimizer_state_dict(self):
+        """torch.optim.Adam-compatible state of the fused optimizer (one entry per
+        model parameter, views of the flat moments)."""
+        state, ids = {}, []
+        t = torch.tensor(float(self.counters[5].item()))
+        for i, (name, p) in enumerate(self.model.named_parameters()):
+            mv = self._param_view(p, self.m)
+            vv = self._param_view(p, self.v)
+            state[i] = {"step": t.clone(), "exp_avg": mv.detach().clone().cpu(), "exp_avg_sq": vv.detach().clone().cpu()}
+            ids.append(i)
+        b1, b2 = self.betas
+        group = {"lr": self.lr, "betas": (b1, b2), "eps": self.eps, "weight_decay": 0, "amsgrad": False,
+                 "maximize": False, "foreach": None, "capturable": False, "differentiable": False, "fused": None,
+                 "params": ids}
+        return {"state": state, "param_groups": [group]}
+
+    def _param_view(self, p, buf):
+        off = (p.data_ptr() - self.flat.data_ptr()) // 4
+        return torch.as_strided(buf, p.shape, p.stride(), off)
+
+    def load_optimizer_state_dict(self, sd):
+        with torch.no_grad():
+            for i, (name, p) in enumerate(self.model.named_parameters()):
+                st = sd["state"].get(i)
+                if st is None:
+                    continue
+                self._param_view(p, self.m).copy_(st["exp_avg"])
+                self._param_view(p, self.v).copy_(st["exp_avg_sq"])
+                self.counters[5] = int(float(st["step"]))
+            self.wbf.copy_(self.flat)
+
+
+class SageEngine(BlockEngine):
+    """GraphSAGE (mean): [h_dst | mean h_src] . [W_self | W_neigh]^T + b in one GEMM."""
+
+    model_name = "sage"
+
+    def _alloc_layers(self):
+        dev = self.device
+        for l, layer in enumerate(self.model.layers):
+            h = self.L - 1 - l
+            ip, op = pad8(layer.in_feats), pad8(layer.out_feats)
+            K = 2 * ip
+            rows = self.sm.cap_dst[h]
+            spec = dict(h=h, ip=ip, op=op, K=K, rows=rows,
+                        W=self._seg(layer.seg_w, self.wbf), bias=self._seg(layer.seg_b)[0],
+                        gW=self._seg(layer.seg_w, self.grad), gb=self._seg(layer.seg_b, self.grad)[0],
+                        X=torch.zeros((rows, K), dtype=torch.bfloat16, device=dev),
+                        dY=torch.zeros((rows, op), dtype=torch.bfloat16, device=dev))
+            if l < self.L - 1:
+                spec["H"] = torch.zeros((rows, op), dtype=torch.bfloat16, device=dev)
+                spec["dH"] = torch.zeros((rows, op), dtype=torch.float32, device=dev)
+            else:
+                spec["ce_fused"] = op <= 64
+                if not spec["ce_fused"]:
+                    spec["logits"] = torch.zeros((rows, op), dtype=torch.bfloat16, device=dev)
+            if l > 0:
+                spec["dX"] = torch.zeros((rows, K), dtype=torch.bfloat16, device=dev)
+            self.lay.append(spec)
+
+    def _forward(self, training=True):
+        cu, sm = self.cu, self.sm
+        L = self.L
+        for l, s in enumerate(self.lay):
+            h = s["h"]
+            src, src_map = self._input(l)
+            cu.aggregate(sm.indptr[h], sm.indices[h], self._n_dst(h), 0, sm.cap_dst[h], src, src_map,
+                         s["ip"], AGG_MEAN, None, None, None, s["X"], s["ip"], 0, 0.0, 0, self.err)
+            if l < L - 1:
+                self._gemm(s["X"], False, s["W"], False, s["rows"], self._n_dst(h), s["op"], s["K"], None, 1,
+                           s["H"], GEMM_STORE_BF16, s["bias"], 1, self.p if training else 0.0, l)
+            elif s["ce_fused"]:
+                labels, _, _ = self._labels_rows()
+                cu.gemm(s["X"], False, s["W"], False, s["rows"], self._n_dst(h), s["op"], s["K"], None, 1,
+                        self._ce_dummy, GEMM_CROSS_ENTROPY, s["bias"], 0, 0.0, None, 0, labels,
+                        self.n_classes, s["dY"], self.fstats[2:3], self.istats[0:1], None, self._n_dst(h),
+                        s["gb"] if training else None, self.err, bn_for(s["op"]))
+            else:
+                self._gemm(s["X"], False, s["W"], False, s["rows"], self._n_dst(h), s["op"], s["K"], None, 1,
+                           s["logits"], GEMM_STORE_BF16, s["bias"])
+                self._ce(s["logits"], self.n_classes, s["dY"], s["gb"] if training else None, h)
+
+    def _backward(self):
+        cu, sm = self.cu, self.sm
+        scale = 1.0 / (1.0 - self.p) if self.p > 0 else 1.0
+        for l in range(self.L - 1, -1, -1):
+            s = self.lay[l]
+            h = s["h"]
+            n_tiles = math.ceil(s["op"] / 128) * math.ceil(s["K"] / 256)
+            # dW += dY^T X (split-K over the block's rows, fp32 reductions into the gradient)
+            self._gemm(s["dY"], True, s["X"], True, s["op"], None, s["K"], s["rows"], self._n_dst(h),
+                       split_k(s["rows"], n_tiles), s["gW"], GEMM_ATOMIC_F32, bn=256)
+            if l == 0:
+                break
+            # dX = dY W (W read MN-major)
+            self._gemm(s["dY"], False, s["W"], True, s["rows"], self._n_dst(h), s["K"], s["op"], None, 1, s["dX"],
+                       GEMM_STORE_BF16, bn=256)
+            prev = self.lay[l - 1]
+            # transpose aggregation: d(self) -> dst rows, d(agg) -> sources
+            cu.aggregate_bwd(sm.indptr[h], sm.indices[h], self._n_dst(h), 0, sm.cap_dst[h], s["dX"],
+                             s["ip"], 0, 0.0, s["ip"], AGG_MEAN, None, None, None, prev["dH"], self.err)
+            cu.act_bwd(prev["dH"], prev["H"], prev["dY"], self._n_dst(prev["h"]), 0, prev["op"], scale, prev["gb"],
+                       prev["rows"])
+
+
+class GcnEngine(BlockEngine):
+    """GCN (GraphConv norm='both'): D_dst^-1/2 A D_src^-1/2 h W + b.  The projection
+    runs first when it narrows the rows (in > out), as DGL does."""
+
+    model_name = "gcn"
+
+    def _alloc_layers(self):
+        dev = self.device
+        z = dict(dtype=torch.bfloat16, device=dev)
+        for l, layer in enumerate(self.model.layers):
+            h = self.L - 1 - l
+            ip, op = pad8(layer.in_feats), pad8(layer.out_feats)
+            rows, srows = self.sm.cap_dst[h], self.sm.cap_src[h]
+            last = l == self.L - 1
+            s = dict(h=h, ip=ip, op=op, rows=rows, srows=srows, last=last, first_proj=layer.in_feats > layer.out_feats,
+                     W=self._seg(layer.seg_w, self.wbf), bias=self._seg(layer.seg_b)[0],
+                     gW=self._seg(layer.seg_w, self.grad), gb=self._seg(layer.seg_b, self.grad)[0],
+                     snorm=torch.zeros(srows, dtype=torch.float32, device=dev),
+                     degs=torch.zeros(srows, dtype=torch.float32, device=dev),
+                     dY=torch.zeros((rows, op), **z))
+            s["H"] = torch.zeros((rows, op), **z)  # hidden output, or the logits of the last layer
+            if not last:
+                s["dH"] = torch.zeros((rows, op), dtype=torch.float32, device=dev)
+            if s["first_proj"]:
+                if l == 0 and not self.full_graph:
+                    s["Xg"] = torch.zeros((srows, ip), **z)
+                s["Z"] = torch.zeros((srows, op), **z)
+                s["dZ32"] = torch.zeros((srows, op), dtype=torch.float32, device=dev)
+                s["dZ"] = torch.zeros((srows, op), **z)
+            else:
+                s["X"] = torch.zeros((rows, ip), **z)
+                if l > 0:
+                    s["dX"] = torch.zeros((rows, ip), **z)
+            self.lay.append(s)
+
+    def _forward(self, training=True):
+        cu, sm = self.cu, self.sm
+        for l, s in enumerate(self.lay):
+            h = s["h"]
+            p = self.p if (training and not s["last"]) else 0.0
+            act = 0 if s["last"] else 1
+            cu.src_norm(sm.indices[h], sm.n_edges(h), sm.cap_e[h], sm.n_src(h), sm.cap_src[h], s["degs"], s["snorm"])
+            if s["first_proj"]:
+                A = self._gathered_input(l, s)
+                self._gemm(A, False, s["W"], True, s["srows"], sm.n_src(h), s["op"], s["ip"], None, 1, s["Z"],
+                           GEMM_STORE_BF16)
+                cu.aggregate(sm.indptr[h], sm.indices[h], self._n_dst(h), 0, sm.cap_dst[h], s["Z"], None, s["op"],
+                             AGG_GCN, None, s["snorm"], None, s["H"], 0, -1, 0.0, 64, self.err, bias=s["bias"],
+                             act=act, dropout_p=p, counters=self.counters if p > 0 else None, dropout_salt=l)
+            else:
+                src, src_map = self._input(l)
+                cu.aggregate(sm.indptr[h], sm.indices[h], self._n_dst(h), 0, sm.cap_dst[h], src, src_map, s["ip"],
+                             AGG_GCN, None, s["snorm"], None, s["X"], 0, -1, 0.0, 64, self.err)
+                self._gemm(s["X"], False, s["W"], True, s["rows"], self._n_dst(h), s["op"], s["ip"], None, 1, s["H"],
+                           GEMM_STORE_BF16, s["bias"], act, p, l)
+            if s["last"]:
+                self._ce(s["H"], self.n_classes, s["dY"], s["gb"] if training else None, h)
+
+    def _backward(self):
+        cu, sm = self.cu, self.sm
+        scale = 1.0 / (1.0 - self.p) if self.p > 0 else 1.0
+        for l in range(self.L - 1, -1, -1):
+            s = self.lay[l]
+            h = s["h"]
+            if not s["last"]:
+                cu.act_bwd(s["dH"], s["H"], s["dY"], self._n_dst(h), 0, s["op"], scale, s["gb"], s["rows"])
+            prev = self.lay[l - 1] if l > 0 else None
+            if s["first_proj"]:
+                cu.aggregate_bwd(sm.indptr[h], sm.indices[h], self._n_dst(h), 0, sm.cap_dst[h], s["dY"], 0, -1, 0.0,
+                                 s["op"], AGG_GCN, None, s["snorm"], None, s["dZ32"], self.err)
+                cu.f32_to_bf16_rows(s["dZ32"], s["dZ"], s["op"], sm.n_src(h), s["srows"], True, 64)
+                A = s["Xg"] if "Xg" in s else (self._working.feat if l == 0 else prev["H"])
+                self._dw(A, s["dZ"], s["ip"], s["op"], s["srows"], sm.n_src(h), s["gW"])
+                if prev is not None:
+                    self._gemm(s["dZ"], False, s["W"], False, s["srows"], sm.n_src(h), s["ip"], s["op"], None, 1,
+                               prev["dH"], GEMM_STORE_F32)
+            else:
+                self._dw(s["X"], s["dY"], s["ip"], s["op"], s["rows"], self._n_dst(h), s["gW"])
+                if prev is not None:
+                    self._gemm(s["dY"], False, s["W"], False, s["rows"], self._n_dst(h), s["ip"], s["op"], None, 1,
+                               s["dX"], GEMM_STORE_BF16)
+                    cu.aggregate_bwd(sm.indptr[h], sm.indices[h], self._n_dst(h), 0, sm.cap_dst[h], s["dX"], 0, -1,
+                                     0.0, s["ip"], AGG_GCN, None, s["snorm"], None, prev["dH"], self.err)
+
+
+class GinEngine(BlockEngine):
+    """GIN: MLP((1 + eps) h_dst + sum h_src) with Linear -> BatchNorm+ReLU -> Linear,
+    then the model's BatchNorm+ReLU (training-mode batch statistics)."""
+
+    model_name = "gin"
+
+    def _alloc_layers(self):
+        dev = self.device
+        z = dict(dtype=torch.bfloat16, device=dev)
+        f32 = dict(dtype=torch.float32, device=dev)
+        m = self.model
+        for l, conv in enumerate(m.layers):
+            h = self.L - 1 - l
+            mlp = conv.apply_func
+            lin0, lin1 = mlp.linears
+            ip, hp, op = pad8(lin0.in_features), pad8(lin0.out_features), pad8(lin1.out_features)
+            rows = self.sm.cap_dst[h]
+            bn_mlp, bn_out = mlp.batch_norm, m.batch_norms[l]
+            seg_bn_out = f"batch_norms.{l}"
+            s = dict(h=h, ip=ip, hp=hp, op=op, rows=rows, last=l == self.L - 1, eps=float(conv.eps.item()),
+                     W0=self._seg(mlp.seg_w0, self.wbf), W1=self._seg(mlp.seg_w1, self.wbf),
+                     gW0=self._seg(mlp.seg_w0, self.grad), gW1=self._seg(mlp.seg_w1, self.grad),
+                     g_mlp=self._seg(mlp.seg_bn)[0], b_mlp=self._seg(mlp.seg_bn)[1],
+                     dg_mlp=self._seg(mlp.seg_bn, self.grad)[0], db_mlp=self._seg(mlp.seg_bn, self.grad)[1],
+                     g_out=self._seg(seg_bn_out)[0], b_out=self._seg(seg_bn_out)[1],
+                     dg_out=self._seg(seg_bn_out, self.grad)[0], db_out=self._seg(seg_bn_out, self.grad)[1],
+                     bn_mlp=bn_mlp, bn_out=bn_out,
+                     X=torch.zeros((rows, ip), **z), T0=torch.zeros((rows, hp), **z), U=torch.zeros((rows, hp), **z),
+                     T1=torch.zeros((rows, op), **z), H=torch.zeros((rows, op), **z),
+                     s_mlp=torch.zeros(2 * hp, **f32), s_out=torch.zeros(2 * op, **f32),
+                     bs_mlp=torch.zeros(2 * hp, **f32), bs_out=torch.zeros(2 * op, **f32),
+                     dU=torch.zeros((rows, hp), **f32), dT0=torch.zeros((rows, hp), **z),
+                     dT1=torch.zeros((rows, op), **z))
+            if s["last"]:
+                s["dl"] = torch.zeros((rows, op), **z)
+            else:
+                s["dH"] = torch.zeros((rows, op), **f32)
+            if l > 0:
+                s["dX"] = torch.zeros((rows, ip), **z)
+            self.lay.append(s)
+
+    def _bn(self, x, dim, n, cap, sums, gamma, beta, mod, training, y):
+        cu = self.cu
+        if training:
+            cu.zero_(sums)
+        cu.batchnorm_fwd(x, dim, n, cap, sums, gamma, beta, mod.running_mean, mod.running_var,
+                         mod.num_batches_tracked if training else None, mod.momentum, mod.eps, training, 1, y)
+
+    def _forward(self, training=True):
+        cu, sm = self.cu, self.sm
+        for l, s in enumerate(self.lay):
+            h = s["h"]
+            n = self._n_dst(h)
+            src, src_map = self._input(l)
+            cu.aggregate(sm.indptr[h], sm.indices[h], n, 0, sm.cap_dst[h], src, src_map, s["ip"], AGG_SUM, None,
+                         None, None, s["X"], 0, -1, 1.0 + s["eps"], 64, self.err)
+            self._gemm(s["X"], False, s["W0"], False, s["rows"], n, s["hp"], s["ip"], None, 1, s["T0"],
+                       GEMM_STORE_BF16)
+            self._bn(s["T0"], s["hp"], n, s["rows"], s["s_mlp"], s["g_mlp"], s["b_mlp"], s["bn_mlp"], training, s["U"])
+            self._gemm(s["U"], False, s["W1"], False, s["rows"], n, s["op"], s["hp"], None, 1, s["T1"],
+                       GEMM_STORE_BF16)
+            self._bn(s["T1"], s["op"], n, s["rows"], s["s_out"], s["g_out"], s["b_out"], s["bn_out"], training, s["H"])
+            if s["last"]:
+                self._ce(s["H"], self.n_classes, s["dl"], None, h)
+
+    def _backward(self):
+        cu, sm = self.cu, self.sm
+        for l in range(self.L - 1, -1, -1):
+            s = self.lay[l]
+            h = s["h"]
+            n = self._n_dst(h)
+            dy = s["dl"] if s["last"] else s["dH"]
+            cu.zero_(s["bs_out"])
+            cu.batchnorm_bwd(s["T1"], s["H"], dy, True, s["op"], n, s["rows"], s["s_out"], s["bs_out"], s["g_out"],
+                             s["dg_out"], s["db_out"], s["bn_out"].eps, s["dT1"])
+            self._dw(s["dT1"], s["U"], s["op"], s["hp"], s["rows"], n, s["gW1"])
+            self._gemm(s["dT1"], False, s["W1"], True, s["rows"], n, s["hp"], s["op"], None, 1, s["dU"],
+                       GEMM_STORE_F32)
+            cu.zero_(s["bs_mlp"])
+            cu.batchnorm_bwd(s["T0"], s["U"], s["dU"], True, s["hp"], n, s["rows"], s["s_mlp"], s["bs_mlp"],
+                             s["g_mlp"], s["dg_mlp"], s["db_mlp"], s["bn_mlp"].eps, s["dT0"])
+            self._dw(s["dT0"], s["X"], s["hp"], s["ip"], s["rows"], n, s["gW0"])
+            if l == 0:
+                break
+            prev = self.lay[l - 1]
+            self._gemm(s["dT0"], False, s["W0"], True, s["rows"], n, s["ip"], s["hp"], None, 1, s["dX"],
+                       GEMM_STORE_BF16)
+            cu.aggregate_bwd(sm.indptr[h], sm.indices[h], n, 0, sm.cap_dst[h], s["dX"], 0, -1, 1.0 + s["eps"],
+                             s["ip"], AGG_SUM, None, None, None, prev["dH"], self.err)
+
+
+class GatEngine(BlockEngine):
+    """GAT: z = fc(h_src) (GEMM) -> attention logits -> fused edge softmax + weighted sum
+    (+bias; ReLU + dropout on hidden layers, mean over heads on the last)."""
+
+    model_name = "gat"
+
+    def _alloc_layers(self):
+        dev = self.device
+        z = dict(dtype=torch.bfloat16, device=dev)
+        f32 = dict(dtype=torch.float32, device=dev)
+        for l, layer in enumerate(self.model.layers):
+            h = self.L - 1 - l
+            H, F = layer.num_heads, layer.out_feats
+            HF = H * F
+            ip, hfp = pad8(layer.in_feats), pad8(HF)
+            rows, srows, ecap = self.sm.cap_dst[h], self.sm.cap_src[h], self.sm.cap_e[h]
+            last = l == self.L - 1
+            A = self._seg(layer.seg_a)
+            gA = self._seg(layer.seg_a, self.grad)
+            s = dict(h=h, H=H, F=F, HF=HF, ip=ip, hfp=hfp, rows=rows, srows=srows, last=last,
+                     W=self._seg(layer.seg_w, self.wbf), gW=self._seg(layer.seg_w, self.grad),
+                     al=A[0], ar=A[1], gal=gA[0], gar=gA[1],
+                     bias=self._seg(layer.seg_b)[0], gb=self._seg(layer.seg_b, self.grad)[0],
+                     Z=torch.zeros((srows, hfp), **z), el=torch.zeros(srows * H, **f32),
+                     er=torch.zeros(rows * H, **f32), smax=torch.zeros(rows * H, **f32),
+                     ssum=torch.zeros(rows * H, **f32), escr=torch.zeros(ecap * H, **f32),
+                     del_=torch.zeros(srows * H, **f32), der=torch.zeros(rows * H, **f32),
+                     dz=torch.zeros((srows, hfp), **f32), dzb=torch.zeros((srows, hfp), **z))
+            if l == 0 and not self.full_graph:
+                s["Xg"] = torch.zeros((srows, ip), **z)
+            if last:
+                s["fo"] = pad8(F)
+                s["H_out"] = torch.zeros((rows, s["fo"]), **z)
+                s["dl"] = torch.zeros((rows, s["fo"]), **z)
+            else:
+                s["H_out"] = torch.zeros((rows, hfp), **z)
+                s["dY"] = torch.zeros((rows, hfp), **z)
+                s["dH"] = torch.zeros((rows, hfp), **f32)
+            self.lay.append(s)
+
+    def _A(self, l, s):
+        if l > 0:
+            return self.lay[l - 1]["H_out"]
+        return s["Xg"] if "Xg" in s else self._working.feat
+
+    def _forward(self, training=True):
+        cu, sm = self.cu, self.sm
+        for l, s in enumerate(self.lay):
+            h = s["h"]
+            if l == 0:
+                A = self._gathered_input(0, s) if "Xg" in s else self._working.feat
+            else:
+                A = self.lay[l - 1]["H_out"]
+            self._gemm(A, False, s["W"], False, s["srows"], sm.n_src(h), s["HF"], s["ip"], None, 1, s["Z"],
+                       GEMM_STORE_BF16)
+            args = (sm.indptr[h], sm.indices[h], self._n_dst(h), s["rows"], sm.n_src(h), s["srows"], s["H"], s["F"],
+                    s["Z"], s["al"], s["ar"], s["el"], s["er"], s["smax"], s["ssum"], 0.2)
+            cu.gat_scores(*args)
+            p = self.p if (training and not s["last"]) else 0.0
+            cu.gat_fwd(*args, s["bias"], s["last"], 0 if s["last"] else 1, p, self.counters if p > 0 else None,
+                       l, s["H_out"])
+            if s["last"]:
+                self._ce(s["H_out"], self.n_classes, s["dl"], None, h)
+
+    def _backward(self):
+        cu, sm = self.cu, self.sm
+        scale = 1.0 / (1.0 - self.p) if self.p > 0 else 1.0
+        for l in range(self.L - 1, -1, -1):
+            s = self.lay[l]
+            h = s["h"]
+            if s["last"]:
+                dout = s["dl"]
+            else:
+                cu.act_bwd(s["dH"], s["H_out"], s["dY"], self._n_dst(h), 0, s["hfp"], scale, None, s["rows"])
+                dout = s["dY"]
+            cu.gat_bwd(sm.indptr[h], sm.indices[h], self._n_dst(h), s["rows"], sm.n_src(h), s["srows"], s["H"],
+                       s["F"], s["Z"], s["al"], s["ar"], s["el"], s["er"], s["smax"], s["ssum"], 0.2, s["last"], dout,
+                       s["escr"], s["del_"], s["der"], s["dz"], s["gb"], s["gal"], s["gar"], s["dzb"], self.err)
+            A = self._A(l, s)
+            self._dw(s["dzb"], A, s["HF"], s["ip"], s["srows"], sm.n_src(h), s["gW"])
+            if l > 0:
+                prev = self.lay[l - 1]
+                self._gemm(s["dzb"], False, s["W"], True, s["srows"], sm.n_src(h), s["ip"], s["HF"], None, 1,
+                           prev["dH"], GEMM_STORE_F32)
+
+
+class PinSageEngine(BlockEngine):
+    """PinSAGE (WeightedSAGEConv): n = ReLU(Q drop(h_src) + q); n_v = sum w n_u / max(sum w, 1);
+    z = ReLU(W drop([n_v | h_dst]) + b); out = z / |z|, on random-walk blocks."""
+
+    model_name = "pinsage"
+
+    def __init__(self, *args, walk_length=None, restart_prob=0.5, num_walks=4, num_neighbors=5, **kw):
+        self._walk = dict(length=walk_length, restart_prob=restart_prob, num_walks=num_walks,
+                          num_neighbors=num_neighbors)
+        super().__init__(*args, **kw)
+
+    def _make_sampler(self, batch_size, n_nodes_cap, dev):
+        wk = self._walk
+        return GpuWalkSampler(self.L, batch_size, n_nodes_cap, dev, cu=self.cu,
+                              length=wk["length"] if wk["length"] is not None else self.L,
+                              restart_prob=wk["restart_prob"], num_walks=wk["num_walks"],
+                              num_neighbors=wk["num_neighbors"])
+
+    def _alloc_layers(self):
+        dev = self.device
+        z = dict(dtype=torch.bfloat16, device=dev)
+        f32 = dict(dtype=torch.float32, device=dev)
+        for l, layer in enumerate(self.model.layers):
+            h = self.L - 1 - l
+            if layer.hidden_dims % 8 != 0:
+                raise ValueError("PinSAGE engine: hidden width must be a multiple of 8")
+            ip, hid, op = pad8(layer.input_dims), layer.hidden_dims, pad8(layer.output_dims)
+            kw = pad8(hid + layer.input_dims)
+            rows, srows = self.sm.cap_dst[h], self.sm.cap_src[h]
+            last = l == self.L - 1
+            s = dict(h=h, ip=ip, hid=hid, op=op, kw=kw, rows=rows, srows=srows, last=last,
+                     Q=self._seg(layer.seg_q, self.wbf), gQ=self._seg(layer.seg_q, self.grad),
+                     qb=self._seg(layer.seg_qb)[0], gqb=self._seg(layer.seg_qb, self.grad)[0],
+                     W=self._seg(layer.seg_w, self.wbf), gW=self._seg(layer.seg_w, self.grad),
+                     wb=self._seg(layer.seg_wb)[0], gwb=self._seg(layer.seg_wb, self.grad)[0],
+                     Hd=torch.zeros((srows, ip), **z), N=torch.zeros((srows, hid), **z),
+                     X=torch.zeros((rows, kw), **z), Z=torch.zeros((rows, op), **z), H=torch.zeros((rows, op), **z),
+                     norms=torch.zeros(rows, **f32), dZ32=torch.zeros((rows, op), **f32),
+                     dZ=torch.zeros((rows, op), **z), dX=torch.zeros((rows, kw), **z),
+                     dN32=torch.zeros((srows, hid), **f32), dN=torch.zeros((srows, hid), **z))
+            if l == 0 and not self.full_graph:
+                s["Xg"] = torch.zeros((srows, ip), **z)
+            if last:
+                s["dl"] = torch.zeros((rows, op), **z)
+            else:
+                s["dH"] = torch.zeros((rows, op), **f32)
+            self.lay.append(s)
+
+    def _A(self, l, s):
+        if l > 0:
+            return self.lay[l - 1]["H"]
+        return s["Xg"] if "Xg" in s else self._working.feat
+
+    def _forward(self, training=True):
+        cu, sm = self.cu, self.sm
+        p = self.p if training else 0.0
+        for l, s in enumerate(self.lay):
+            h = s["h"]
+            n = self._n_dst(h)
+            A = self._gathered_input(l, s) if l == 0 else self._A(l, s)
+            cu.dropout_rows(A, s["Hd"], s["ip"], s["ip"], sm.n_src(h), s["srows"], p, self.counters, 8 * l + 1)
+            self._gemm(s["Hd"], False, s["Q"], False, s["srows"], sm.n_src(h), s["hid"], s["ip"], None, 1, s["N"],
+                       GEMM_STORE_BF16, s["qb"], 1)
+            cu.aggregate(sm.indptr[h], sm.indices[h], n, 0, sm.cap_dst[h], s["N"], None, s["hid"], AGG_WEIGHTED,
+                         sm.w[h], None, None, s["X"], 0, -1, 0.0, 64, self.err, dropout_p=p,
+                         counters=self.counters if p > 0 else None, dropout_salt=8 * l + 2)
+            cu.dropout_rows(A, s["X"][:, s["hid"]:s["hid"] + s["ip"]], s["ip"], s["kw"], n, s["rows"], p,
+                            self.counters, 8 * l + 3)
+            self._gemm(s["X"], False, s["W"], False, s["rows"], n, s["op"], s["kw"], None, 1, s["Z"],
+                       GEMM_STORE_BF16, s["wb"], 1)
+            cu.l2norm_fwd(s["Z"], s["op"], n, s["rows"], s["H"], s["norms"])
+            if s["last"]:
+                self._ce(s["H"], self.n_classes, s["dl"], None, h)
+
+    def _backward(self):
+        cu, sm = self.cu, self.sm
+        p = self.p
+        for l in range(self.L - 1, -1, -1):
+            s = self.lay[l]
+            h = s["h"]
+            n = self._n_dst(h)
+            cu.l2norm_bwd(s["H"], s["dl"] if s["last"] else s["dH"], s["norms"], s["op"], n, s["rows"], s["dZ32"])
+            cu.act_bwd(s["dZ32"], s["Z"], s["dZ"], n, 0, s["op"], 1.0, s["gwb"], s["rows"])
+            self._dw(s["dZ"], s["X"], s["op"], s["kw"], s["rows"], n, s["gW"])
+            self._gemm(s["dZ"], False, s["W"], True, s["rows"], n, s["kw"], s["op"], None, 1, s["dX"],
+                       GEMM_STORE_BF16)
+            hid, ip = s["hid"], s["ip"]
+            dnv, dhd = s["dX"][:, :hid], s["dX"][:, hid:hid + ip]
+            cu.dropout_rows(dnv, dnv, hid, s["kw"], n, s["rows"], p, self.counters, 8 * l + 2)
+            cu.aggregate_bwd(sm.indptr[h], sm.indices[h], n, 0, sm.cap_dst[h], s["dX"], 0, -1, 0.0, hid,
+                             AGG_WEIGHTED, sm.w[h], None, None, s["dN32"], self.err)
+            cu.act_bwd(s["dN32"], s["N"], s["dN"], sm.n_src(h), 0, hid, 1.0, s["gqb"], s["srows"])
+            self._dw(s["dN"], s["Hd"], hid, ip, s["srows"], sm.n_src(h), s["gQ"])
+            if l == 0:
+                continue
+            prev = self.lay[l - 1]
+            cu.dropout_rows(dhd, dhd, ip, s["kw"], n, s["rows"], p, self.counters, 8 * l + 3)
+            self._gemm(s["dN"], False, s["Q"], True, s["srows"], sm.n_src(h), ip, hid, None, 1, prev["dH"],
+                       GEMM_STORE_F32)
+            cu.dropout_grad(prev["dH"], ip, ip, sm.n_src(h), s["srows"], p, self.counters, 8 * l + 1)
+            cu.add_bf16_rows(prev["dH"], dhd, ip, n, s["rows"])
+
+
+ENGINES = {"sage": SageEngine, "gcn": GcnEngine, "gin": GinEngine, "gat": GatEngine, "pinsage": PinSageEngine}
+
+
+def make_engine(model, *args, **kwargs):
+    """The engine class of ``model.name`` (sage, gcn, gin, gat, pinsage)."""
+    try:
+        cls = ENGINES[model.name]
+    except KeyError:
+        raise ValueError(f"no GPU engine for model {getattr(model, 'name', None)}") from None
+    return cls(model, *args, **kwargs)
 
 
 class FusedAllReduceAdam:

@@ -217,3 +217,51 @@ def next_neighbor(nbr_idx, rank, world):
     if nbr_idx == rank:
         nbr_idx = (nbr_idx + 1) % world
     return nbr_idx
+
+
+def partition_from_chunks(data_path, graph_name, part_method, n_part, rank, feat_dim, device,
+                          feat_dtype=torch.bfloat16):
+    """This rank's OwnPartition read from a chunked dataset (the reference's on-disk layout,
+    grappa_b200.dataset.io_dist): the intra-partition edges p{rank}.u/v (with their
+    self-loops) plus every bridge b{j}_{rank} into the partition form the complete
+    in-edge CSR of the own nodes; features, labels and masks come from the p{rank}.* files.
+    The global in-degree is the in-edge count without the self-loop."""
+    import numpy as np
+
+    from grappa_b200.dataset.io_dist import ChunkIO
+    from grappa_b200.dataset.meta import t10n_chunk_path
+
+    device = torch.device(device)
+    io = ChunkIO(f"{data_path}/{t10n_chunk_path(graph_name, part_method, n_part)}", n_part, feat_dim)
+    prefix = io.prefix
+    lo, hi = prefix[rank], prefix[rank + 1]
+    n = hi - lo
+    us = [io.part(rank, "u") + lo]
+    vs = [io.part(rank, "v")]
+    for j in range(n_part):
+        if j == rank:
+            continue
+        bu, bv = io.bridge(j, rank)
+        if bu is not None:
+            us.append(bu + prefix[j])
+            vs.append(bv)
+    u = torch.from_numpy(np.concatenate(us)).to(device)
+    v = torch.from_numpy(np.concatenate(vs)).to(device)
+    N = prefix[-1]
+    key, _ = torch.sort(v * N + u)
+    indices = (key % N).to(torch.int32)
+    vv = key // N
+    deg = torch.bincount(vv, minlength=n)
+    indptr = torch.zeros(n + 1, dtype=torch.int64, device=device)
+    indptr[1:] = torch.cumsum(deg, 0)
+    loops = torch.bincount(vv[(key % N) == vv + lo], minlength=n)
+    gideg = (deg - loops).to(torch.int64)
+    del key, vv, u, v
+    ext = indices[(indices < lo) | (indices >= hi)]
+    ext_src = torch.unique(ext).to(torch.int32)
+    feat = torch.zeros((n, pad8(feat_dim)), dtype=feat_dtype, device=device)
+    feat[:, :feat_dim] = torch.from_numpy(io.part(rank, "nfeat")).to(device).to(feat_dtype)
+    label = torch.from_numpy(io.part(rank, "label")).to(device).to(torch.int32)
+    masks = [torch.from_numpy(io.part(rank, k)).to(device) for k in ("train", "valid", "test")]
+    return OwnPartition(rank, n_part, prefix, indptr, indices, feat, label, masks[0], masks[1], masks[2], gideg,
+                        ext_src, feat_dim=feat_dim)

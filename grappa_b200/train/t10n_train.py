@@ -175,43 +175,47 @@ def run_gpu(args):
     torch.manual_seed(args.seed)
     model = get_model(args.model, meta.n_dim, meta.n_label, num_hidden=args.num_hidden, num_layers=args.num_layers,
                       dropout=args.dropout)
-    ckpt_epoch = resume_from_ckpt(model, None, args.resume_path)
+    ckpt = None
+    if args.resume_path:
+        ckpt = torch.load(args.resume_path, weights_only=False)
+        model.load_state_dict(ckpt["state_dict"])
     own = partition_from_chunks(args.data_path, args.graph_name, args.part_method, args.n_part, rank, meta.n_dim,
                                 device)
     comm = Comm() if world > 1 else None
     fanouts = [int(f) for f in args.fan_out.split(",")]
     trainer = MiniBatchTrainer(model, own, fanouts, args.batch_size, lr=args.lr, repart_every=args.repart_every,
                                comm=comm, seed=args.seed)
+    if ckpt is not None:
+        trainer.engine.load_optimizer_state_dict(ckpt["optimizer_state_dict"])
+    first = int(ckpt["epoch"]) + 1 if ckpt is not None else 0
+    trainer.warmup()
     best = {"val_acc": 0.0, "state_dict": None}
     epoch_loss = []
-    epoch = ckpt_epoch
-    for epoch in range(ckpt_epoch + 1, args.num_epochs):
+    epoch = first - 1
+    for epoch in range(first, args.num_epochs):
         tic = time.time()
-        loss = trainer.train_epoch(epoch)
+        loss = trainer.train_epoch(epoch, host_feed=True)
         toc = time.time()
         epoch_loss.append(float(loss))
-        n_seed = int(trainer.train_ids.numel())
-        rank_print("epoch_|epoch|{:04d}|part|{:04d}|epoch_seconds|{:.4f}|sampling|{:.4f}|f_fetch|{:.4f}|pcie|{:.4f}|"
-                   "forward|{:.4f}|backward|{:.4f}|update|{:.4f}|account|{:.4f}|n_seed|{:012d}|n_input|{:012d}".format(
-                       epoch, rank, toc - tic, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0, n_seed, 0))
+        rank_print("epoch_|epoch|{:04d}|part|{:04d}|epoch_seconds|{:.4f}|loss|{:.4f}|n_seed|{:012d}".format(
+            epoch, rank, toc - tic, float(loss), int(trainer.train_ids.numel())))
         if epoch != 0 and (epoch + 1) % args.eval_every == 0:
-            acc = trainer.evaluate()
-            val_acc = acc["val"]
+            val_acc = trainer.evaluate(own.val_mask)
             rank_print(f"epoch={epoch}, val_acc={val_acc}")
             if val_acc >= best["val_acc"]:
                 best["val_acc"] = val_acc
-                best["state_dict"] = deepcopy(trainer.state_dict())
+                best["state_dict"] = model.state_dict_contiguous()
     summary = {"epochs": epoch + 1, "loss": epoch_loss, "val_acc": 0.0, "test_acc": 0.0, "train_acc": 0.0}
     if best["state_dict"] is not None:
         t0 = time.time()
         trainer.load_state_dict(best["state_dict"])
-        acc = trainer.evaluate()
-        rank_print("infer_|epoch|{:04d}|part|{:04d}|val_acc|{:.4f}|test_acc|{:.4f}|train_acc|{:.4f}|time_sec|{:.4f}|"
-                   "val:{:.1f}|test:{:.1f}|train:{:.1f}".format(epoch, rank, acc["val"], acc["test"], acc["train"],
-                                                                 time.time() - t0, acc["n_val"], acc["n_test"],
-                                                                 acc["n_train"]))
+        acc = {k: trainer.evaluate(m) for k, m in (("val", own.val_mask), ("test", own.test_mask),
+                                                   ("train", own.train_mask))}
+        rank_print("infer_|epoch|{:04d}|part|{:04d}|val_acc|{:.4f}|test_acc|{:.4f}|train_acc|{:.4f}|time_sec|{:.4f}"
+                   .format(epoch, rank, acc["val"], acc["test"], acc["train"], time.time() - t0))
         summary.update(val_acc=acc["val"], test_acc=acc["test"], train_acc=acc["train"])
-    save_to_ckpt(args, epoch, rank, model, trainer.optimizer_state_dict(), epoch_loss[-1] if epoch_loss else 0.0)
+    save_to_ckpt(args, epoch, rank, model, trainer.engine.optimizer_state_dict(),
+                 epoch_loss[-1] if epoch_loss else 0.0)
     trainer.close()
     return summary
 

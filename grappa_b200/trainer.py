@@ -20,7 +20,7 @@ import time
 import torch
 
 from grappa_b200.dataset.synthetic import shuffle_keys
-from grappa_b200.engine import SageEngine
+from grappa_b200.engine import make_engine
 from grappa_b200.graph_store import PartitionStore, next_neighbor
 
 
@@ -47,7 +47,7 @@ class MiniBatchTrainer:
             nb = int(comm.all_reduce_max([nb])[0])
         self.n_batches = nb
         self.batch_size = max(1, math.ceil(n_local / nb))  # reference: adjust_bs
-        self.engine = SageEngine(model, self.store.cap_nodes, fanouts, self.batch_size, self.device, lr=lr,
+        self.engine = make_engine(model, self.store.cap_nodes, fanouts, self.batch_size, self.device, lr=lr,
                                  comm=comm, seed=seed, fused_allreduce=fused_allreduce,
                                  use_cuda_graph=use_cuda_graph)
         self._maybe_repartition(0)
@@ -134,6 +134,128 @@ class MiniBatchTrainer:
         if self.comm is not None and self.comm.world > 1:
             correct, total = self.comm.all_reduce_sum([correct, total])
         return correct / max(total, 1.0)
+
+    def load_state_dict(self, state_dict):
+        """Load model weights into the flat master buffer and refresh the bf16 working copy."""
+        self.model.load_state_dict(state_dict)
+        with torch.no_grad():
+            self.engine.wbf.copy_(self.engine.flat)
+
+    def close(self):
+        self.engine._graph = None
+        if self.engine.allreduce is not None:
+            self.engine.allreduce.close()
+        self.store.close()
+
+
+def full_graph_blocks(working, n_layers, own):
+    """FullGraphBlocks of the working graph's own + neighbour rows: the in-edges whose
+    source is one of those rows (halo sources dropped, as the reference's isolated
+    full-graph partition holds only the two chunks, t10n/dataloader.py:492-502).
+    Labels and the training mask exist for the own rows only."""
+    from grappa_b200.engine import FullGraphBlocks
+
+    n = int(working.n_own + working.n_nbr)
+    dev = working.indices.device
+    ip = working.indptr[: n + 1].to(torch.int64)
+    E = int(ip[-1].item())
+    ind = working.indices[:E].to(torch.int64)
+    keep = ind < n
+    deg = (ip[1:] - ip[:-1])
+    row = torch.repeat_interleave(torch.arange(n, device=dev), deg)
+    cnt = torch.bincount(row[keep], minlength=n)
+    new_ip = torch.zeros(n + 1, dtype=torch.int64, device=dev)
+    new_ip[1:] = torch.cumsum(cnt, 0)
+    labels = torch.zeros(n, dtype=torch.int32, device=dev)
+    labels[: working.n_own] = own.label
+    train = torch.zeros(n, dtype=torch.uint8, device=dev)
+    train[: working.n_own] = own.train_mask.to(torch.uint8)
+    return FullGraphBlocks(new_ip, ind[keep], n_layers, dev, labels, train)
+
+
+class FullGraphTrainer:
+    """Isolated full-graph training of one partition (reference:
+    experiments/grappa/train/t10n_fullgraph_train.py:142-254): every epoch is one step
+    over the whole working graph (own + neighbour partition), loss on the own training
+    nodes, coverage-corrected gradient aggregation across ranks (coverage 1: every
+    in-edge among the partition's rows is present), repartitioned every
+    ``repart_every`` epochs.  The reference computes the loss on every own node
+    (training, validation and test); here only the training nodes contribute."""
+
+    def __init__(self, model, own, lr=3e-3, repart_every=10, comm=None, seed=0, fused_allreduce=True,
+                 use_cuda_graph=True):
+        from grappa_b200.engine import make_engine
+
+        self.model, self.own, self.comm = model, own, comm
+        self.rank, self.world = own.rank, own.world
+        self.repart_every = max(1, int(repart_every))
+        self.device = own.indices.device
+        self.store = PartitionStore(own, comm)
+        self.nbr_idx = self.rank
+        self._last_repart = None
+        self.repart_seconds = []
+        if self.world > 1:
+            self.nbr_idx = next_neighbor(self.nbr_idx, self.rank, self.world)
+        w = self.store.repartition(self.nbr_idx)
+        blocks = full_graph_blocks(w, len(model.layers), own)
+        self.engine = make_engine(model, self.store.cap_nodes, [], 0, self.device, lr=lr, comm=comm, seed=seed,
+                                  fused_allreduce=fused_allreduce, use_cuda_graph=use_cuda_graph, blocks=blocks)
+        self.engine.bind_working(w, own.label, own.gideg)
+        self._last_repart = 0
+        self._warm = False
+
+    def _maybe_repartition(self, epoch):
+        if self.world == 1 or epoch % self.repart_every != 0 or epoch == self._last_repart:
+            return
+        t0 = time.perf_counter()
+        self.nbr_idx = next_neighbor(self.nbr_idx, self.rank, self.world)
+        w = self.store.repartition(self.nbr_idx)
+        self.engine.set_blocks(full_graph_blocks(w, len(self.model.layers), self.own))
+        self.engine.bind_working(w, self.own.label, self.own.gideg)
+        self._last_repart = epoch
+        self._warm = False
+        self.repart_seconds.append(time.perf_counter() - t0)
+
+    def warmup(self):
+        if self._warm:
+            return
+        self.engine.set_epoch(0)
+        self.engine.step()
+        torch.cuda.synchronize(self.device)
+        self.engine.check_errors()
+        self.engine.prepare()
+        self._warm = True
+
+    def train_epoch(self, epoch, read_loss=True):
+        self._maybe_repartition(epoch)
+        if not self._warm:
+            self.warmup()
+        self.engine.set_epoch(epoch)
+        self.engine.step()
+        if read_loss:
+            return float(self.engine.fstats[2].item())
+        return None
+
+    def evaluate(self, mask):
+        """Accuracy (forward without dropout) on the own rows selected by ``mask``, summed over ranks."""
+        sm = self.engine.sm
+        keep_mask, keep_sel = sm.row_mask, sm.n_sel
+        m = torch.zeros_like(keep_mask)
+        m[: self.own.n_nodes] = mask.to(torch.uint8)
+        sm.row_mask = m
+        sm.n_sel = torch.tensor([int(m.sum())], dtype=torch.int32, device=self.device)
+        c, _ = self.engine.predict(None, None)
+        correct, total = float(c.item()), float(sm.n_sel.item())
+        sm.row_mask, sm.n_sel = keep_mask, keep_sel
+        if self.comm is not None and self.comm.world > 1:
+            correct, total = self.comm.all_reduce_sum([correct, total])
+        return correct / max(total, 1.0)
+
+    def load_state_dict(self, state_dict):
+        """Load model weights into the flat master buffer and refresh the bf16 working copy."""
+        self.model.load_state_dict(state_dict)
+        with torch.no_grad():
+            self.engine.wbf.copy_(self.engine.flat)
 
     def close(self):
         self.engine._graph = None

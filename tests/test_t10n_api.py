@@ -190,3 +190,20 @@ def test_cli_trains_on_cpu_ranks(tiny_chunks, tmp_path, model):
     ck = torch.load(os.path.join(str(tmp_path), "epoch_003.pt"), weights_only=False)
     assert set(ck) == {"epoch", "state_dict", "optimizer_state_dict", "loss"}
     assert ck["epoch"] == 3
+
+
+def test_partition_from_chunks_matches_global(tiny_chunks):
+    from grappa_b200.graph_store import partition_from_chunks, partition_from_global
+
+    g = tiny_chunks.graph
+    for r in range(WORLD):
+        a = partition_from_chunks(tiny_chunks.root, "tiny", "hash", WORLD, r, 32, "cpu")
+        b = partition_from_global(g, WORLD, r, "cpu")
+        assert a.prefix == b.prefix
+        assert torch.equal(a.indptr, b.indptr)
+        assert torch.equal(a.indices, b.indices)
+        assert torch.equal(a.feat, b.feat)
+        assert torch.equal(a.label, b.label)
+        assert torch.equal(a.gideg, b.gideg)
+        assert torch.equal(a.ext_src, b.ext_src)
+        assert torch.equal(a.train_mask.to(torch.int8), b.train_mask.to(torch.int8))
