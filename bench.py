@@ -18,6 +18,11 @@ timed by the host clock.
     python bench.py [--gpus N] [--steps K] [--warmup W]
     python -m torch.distributed.run --nproc-per-node N bench.py --gpus N ...
     python bench.py --impl reference ...
+
+Other workloads of the same framework (not the headline number):
+    --workload gcn_full   full-graph 3-layer GCN, hidden 256, reddit-shaped graph
+    --workload gat        3-layer GAT 4x64, fanout [10,10,10], ogbn-papers100M-shaped graph
+    --workload gin | pinsage   3-layer GIN / PinSAGE, hidden 256, ogbn-products-shaped graph
 """
 import argparse
 import json
@@ -89,13 +94,29 @@ def run_reference(args):
     return 0
 
 
+WORKLOADS = {
+    "sage": dict(model="sage", graph="ogbpr", hidden=256, fanouts=[15, 10, 5], repart=10,
+                 desc="GraphSAGE-mean 3 layers, hidden 256, fanout [15,10,5], dropout 0.5, Adam lr 3e-3"),
+    "gcn_full": dict(model="gcn", graph="reddit", hidden=256, full_graph=True, repart=10,
+                     desc="full-graph GCN 3 layers, hidden 256, symmetric norm, dropout 0.5, Adam lr 3e-3"),
+    "gat": dict(model="gat", graph="ogbpa", hidden=64, heads=4, fanouts=[10, 10, 10], repart=5,
+                desc="GAT 3 layers, 4 heads x 64, fanout [10,10,10], dropout 0.5, Adam lr 3e-3"),
+    "gin": dict(model="gin", graph="ogbpr", hidden=256, fanouts=[15, 10, 5], repart=10,
+                desc="GIN 3 layers, hidden 256, fanout [15,10,5], Adam lr 3e-3"),
+    "pinsage": dict(model="pinsage", graph="ogbpr", hidden=256, fanouts=[5, 5, 5], repart=10,
+                    desc="PinSAGE 3 layers, hidden 256, 4 walks x 3 steps, top-5, dropout 0.5, Adam lr 3e-3"),
+}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10, help="timed epochs")
     ap.add_argument("--warmup", type=int, default=3, help="warm-up epochs")
     ap.add_argument("--impl", default="grappa", choices=["grappa", "reference"])
-    ap.add_argument("--config", default="ogbpr")
+    ap.add_argument("--config", default=None, help="graph spec (default: the workload's)")
+    ap.add_argument("--workload", default="sage", choices=["sage", "gcn_full", "gat", "gin", "pinsage"])
+    ap.add_argument("--batch", type=int, default=1024, help="seeds per GPU per mini-batch")
     ap.add_argument("--no-graph", action="store_true", help="disable CUDA graph capture")
     ap.add_argument("--no-fused-ar", action="store_true", help="use the NCCL gradient path")
     ap.add_argument("--skip-e2e", action="store_true")
@@ -110,9 +131,13 @@ def main():
 
     from grappa_b200.dataset import synthetic as S
     from grappa_b200.graph_store import partition_from_global
-    from grappa_b200.models import SAGE
+    from grappa_b200.models import get_model
     from grappa_b200.parallel.comm import Comm, init_distributed
-    from grappa_b200.trainer import MiniBatchTrainer
+    from grappa_b200.trainer import FullGraphTrainer, MiniBatchTrainer
+
+    wl = WORKLOADS[args.workload]
+    if args.config is None:
+        args.config = wl["graph"]
 
     rank, world = init_distributed("nccl" if args.gpus > 1 else None)
     if world != args.gpus:
@@ -131,13 +156,24 @@ def main():
     t_setup = time.time() - t0
 
     torch.manual_seed(1234)
-    model = SAGE(spec.feat_dim, 256, spec.n_classes, 3, F.relu, 0.5)
-    trainer = MiniBatchTrainer(model, own, [15, 10, 5], 1024, lr=3e-3, repart_every=10, comm=comm, seed=7,
-                               fused_allreduce=not args.no_fused_ar, use_cuda_graph=not args.no_graph)
+    model = get_model(wl["model"], spec.feat_dim, spec.n_classes, num_hidden=wl["hidden"], num_layers=3,
+                      dropout=0.5, n_heads=wl.get("heads", 4))
+    full = wl.get("full_graph", False)
+    if full:
+        trainer = FullGraphTrainer(model, own, lr=3e-3, repart_every=wl["repart"], comm=comm, seed=7,
+                                   fused_allreduce=not args.no_fused_ar, use_cuda_graph=not args.no_graph)
+        trainer.n_batches, trainer.batch_size = 1, int(trainer.engine.sm.n)
+    else:
+        trainer = MiniBatchTrainer(model, own, wl["fanouts"], args.batch, lr=3e-3, repart_every=wl["repart"],
+                                   comm=comm, seed=7, fused_allreduce=not args.no_fused_ar,
+                                   use_cuda_graph=not args.no_graph)
     trainer.warmup()
     launches_per_step = trainer.engine.launches_per_step
+    def run_epoch(e):
+        return trainer.train_epoch(e, read_loss=False) if full else trainer.train_epoch(e)
+
     for e in range(args.warmup):
-        trainer.train_epoch(e)
+        run_epoch(e)
     torch.cuda.synchronize()
     trainer.engine.check_errors()
 
@@ -158,7 +194,7 @@ def main():
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
     for e in range(e0, e0 + args.steps):
-        trainer.train_epoch(e)
+        run_epoch(e)
     ev1.record()
     torch.cuda.synchronize()
     if world > 1:
@@ -179,13 +215,14 @@ def main():
         t0 = time.perf_counter()
         loss = None
         for e in range(e1, e1 + args.steps):
-            loss = trainer.train_epoch(e, host_feed=True)
+            loss = trainer.train_epoch(e) if full else trainer.train_epoch(e, host_feed=True)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         s_e2e = max_over_ranks((time.perf_counter() - t0) / args.steps)
         e2e = {"value": round(s_e2e, 6), "unit": "s/epoch",
-               "h2d_bytes_per_step": trainer.batch_size * 4 + 4, "d2h_bytes_per_step": 4,
+               "h2d_bytes_per_step": 0 if full else (trainer.batch_size * 4 + 4) * trainer.n_batches,
+               "d2h_bytes_per_step": 4 if full else 4 * trainer.n_batches,
                "last_mean_loss": None if loss is None else round(loss, 5)}
         trainer.engine.check_errors()
 
@@ -209,16 +246,16 @@ def main():
         "dtype": "bf16",
         "data": "synthetic (seeded RMAT graph, N(0,1) features, teacher labels; random-init weights)",
         "config": {
-            "model": "GraphSAGE-mean 3 layers, hidden 256, fanout [15,10,5], dropout 0.5, Adam lr 3e-3",
+            "model": wl["desc"],
             "graph": f"RMAT {spec.n_nodes} nodes / {2 * spec.n_edges} directed edges, {spec.feat_dim}-dim, "
-                     f"{spec.n_classes} classes, 8% train",
+                     f"{spec.n_classes} classes, {spec.train_frac:.1%} train",
             "global_batch": trainer.batch_size * world,
             "seq_len": None,
             "seeds_per_gpu_per_batch": trainer.batch_size,
             "mini_batches_per_epoch": trainer.n_batches,
             "parallelism": f"partition-parallel x{world} (one hash partition per GPU; coverage-weighted gradient "
                            f"all-reduce{' + Adam fused over NVLink peer memory' if world > 1 and not args.no_fused_ar else ''})",
-            "repart_every": 10,
+            "repart_every": wl["repart"],
             "l2": "inputs larger than L2 (feature table and CSR about 1 GB per GPU); no flush",
             "step": "one benchmark step = one epoch",
             "setup_s": round(t_setup, 2),
@@ -229,6 +266,8 @@ def main():
     }
     if acc:
         out["accuracy"] = acc
+    if args.workload != "sage":
+        out["workload"] = args.workload
     if rank == 0:
         print(json.dumps(out), flush=True)
     trainer.close()

@@ -1,0 +1,204 @@
+"""Numerics of the row-wise network kernels (nn.cu, gat.cu) against plain PyTorch
+fp32 references of the same ops, on bf16-exact inputs."""
+import pytest
+import torch
+import torch.nn.functional as F
+
+from grappa_b200 import _native
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+
+
+def cu():
+    return _native.cuda()
+
+
+def bf(x):
+    return x.to(torch.bfloat16)
+
+
+def test_cross_entropy_kernel():
+    torch.manual_seed(0)
+    n, cap, C, ld = 300, 320, 47, 48
+    logits = bf(torch.randn(cap, ld, device=DEV) * 3)
+    labels = torch.randint(0, C, (cap,), dtype=torch.int32, device=DEV)
+    mask = (torch.rand(cap, device=DEV) > 0.3).to(torch.uint8)
+    n_rows = torch.tensor([n], dtype=torch.int32, device=DEV)
+    n_sel = torch.tensor([int(mask[:n].sum())], dtype=torch.int32, device=DEV)
+    dl = torch.full((cap, ld), 7.0, dtype=torch.bfloat16, device=DEV)
+    dbias = torch.zeros(ld, device=DEV)
+    loss = torch.zeros(1, device=DEV)
+    correct = torch.zeros(1, dtype=torch.int32, device=DEV)
+    cu().cross_entropy(logits, C, labels, n_rows, cap, mask, n_sel, dl, dbias, loss, correct)
+    torch.cuda.synchronize()
+    sel = mask[:n].bool()
+    x = logits[:n, :C].float().requires_grad_(True)
+    ref = F.cross_entropy(x[sel], labels[:n][sel].long(), reduction="sum") / float(n_sel)
+    ref.backward()
+    assert abs(float(loss) - float(ref)) < 1e-3 * max(1.0, float(ref))
+    torch.testing.assert_close(dl[:n, :C].float(), x.grad, atol=2e-3, rtol=1e-2)
+    assert torch.all(dl[n:320] == 0) and torch.all(dl[:n, C:] == 0)
+    torch.testing.assert_close(dbias[:C], x.grad.sum(0), atol=2e-3, rtol=2e-2)
+    pred = logits[:n, :C].float().argmax(1)
+    assert int(correct) == int(((pred == labels[:n].long()) & sel).sum())
+
+
+@pytest.mark.parametrize("act", [0, 1])
+def test_batchnorm_kernels(act):
+    torch.manual_seed(1)
+    n, cap, dim, C = 500, 576, 64, 60  # C < dim: padded columns
+    x = bf(torch.randn(cap, dim, device=DEV) * 2 + 0.5)
+    gamma = torch.randn(dim, device=DEV)
+    beta = torch.randn(dim, device=DEV)
+    gamma[C:] = 0
+    beta[C:] = 0
+    rm = torch.zeros(C, device=DEV)
+    rv = torch.ones(C, device=DEV)
+    nb = torch.zeros((), dtype=torch.int64, device=DEV)
+    sums = torch.zeros(2 * dim, device=DEV)
+    y = torch.zeros(cap, dim, dtype=torch.bfloat16, device=DEV)
+    nd = torch.tensor([n], dtype=torch.int32, device=DEV)
+    cu().batchnorm_fwd(x, dim, nd, cap, sums, gamma, beta, rm, rv, nb, 0.1, 1e-5, True, act, y)
+    xr = x[:n, :C].float().requires_grad_(True)
+    bn = torch.nn.BatchNorm1d(C).to(DEV)
+    with torch.no_grad():
+        bn.weight.copy_(gamma[:C])
+        bn.bias.copy_(beta[:C])
+    yr = bn(xr)
+    if act:
+        yr = F.relu(yr)
+    torch.testing.assert_close(y[:n, :C].float(), yr, atol=2e-2, rtol=1e-2)
+    torch.testing.assert_close(rm, bn.running_mean, atol=1e-4, rtol=1e-3)
+    torch.testing.assert_close(rv, bn.running_var, atol=1e-4, rtol=1e-3)
+    assert int(nb) == 1
+    # backward
+    gy = torch.randn(n, C, device=DEV)
+    dy = torch.zeros(cap, dim, device=DEV)
+    dy[:n, :C] = gy
+    bsums = torch.zeros(2 * dim, device=DEV)
+    dgamma = torch.zeros(dim, device=DEV)
+    dbeta = torch.zeros(dim, device=DEV)
+    dx = torch.zeros(cap, dim, dtype=torch.bfloat16, device=DEV)
+    cu().batchnorm_bwd(x, y if act else None, dy, True, dim, nd, cap, sums, bsums, gamma, dgamma, dbeta, 1e-5, dx)
+    torch.cuda.synchronize()
+    # the ReLU mask of the kernel is its own bf16 output; use the same mask in the reference
+    yr.backward(gy * (y[:n, :C].float() != 0) if act else gy)
+    torch.testing.assert_close(dx[:n, :C].float(), xr.grad, atol=3e-2, rtol=2e-2)
+    torch.testing.assert_close(dgamma[:C], bn.weight.grad, atol=5e-2, rtol=2e-2)
+    torch.testing.assert_close(dbeta[:C], bn.bias.grad, atol=5e-2, rtol=2e-2)
+    assert torch.all(dy == 0)
+    assert torch.all(dx[n:576] == 0)
+
+
+def test_l2norm_kernels():
+    torch.manual_seed(2)
+    n, cap, dim = 200, 256, 48
+    z = bf(torch.relu(torch.randn(cap, dim, device=DEV)))
+    z[5] = 0  # zero row: norm 1
+    y = torch.zeros(cap, dim, dtype=torch.bfloat16, device=DEV)
+    norms = torch.zeros(cap, device=DEV)
+    nd = torch.tensor([n], dtype=torch.int32, device=DEV)
+    cu().l2norm_fwd(z, dim, nd, cap, y, norms)
+    zr = z[:n].float().requires_grad_(True)
+    nr = zr.norm(2, 1, keepdim=True)
+    nr = torch.where(nr == 0, torch.ones_like(nr), nr)
+    yr = zr / nr
+    torch.testing.assert_close(y[:n].float(), yr, atol=1e-2, rtol=1e-2)
+    g = torch.randn(n, dim, device=DEV)
+    dy = torch.zeros(cap, dim, device=DEV)
+    dy[:n] = g
+    dz = torch.zeros(cap, dim, device=DEV)
+    cu().l2norm_bwd(y, dy, norms, dim, nd, cap, dz)
+    torch.cuda.synchronize()
+    yr.backward(g)
+    torch.testing.assert_close(dz[:n], zr.grad, atol=2e-2, rtol=2e-2)
+    assert torch.all(dy == 0)
+
+
+def test_dropout_rows_matches_mask():
+    n, cap, dim, ld = 100, 128, 64, 80
+    x = bf(torch.randn(cap, ld, device=DEV))
+    out = torch.zeros(cap, ld, dtype=torch.bfloat16, device=DEV)
+    counters = torch.tensor([3, 1, 4, 0, 0, 0], dtype=torch.int64, device=DEV)
+    nd = torch.tensor([n], dtype=torch.int32, device=DEV)
+    cu().dropout_rows(x[:, :dim], out[:, :dim], dim, ld, nd, cap, 0.5, counters, 9)
+    torch.cuda.synchronize()
+    mask = torch.from_numpy(_native.host().dropout_mask(3, 1, 4, 9, n, dim, ld, 0.5)).view(n, dim).to(DEV)
+    ref = x[:n, :dim].float() * mask.float() * 2.0
+    torch.testing.assert_close(out[:n, :dim].float(), ref, atol=1e-2, rtol=1e-2)
+    assert torch.all(out[n:, :dim] == 0)
+    g = torch.randn(cap, dim, device=DEV)
+    g0 = g.clone()
+    cu().dropout_grad(g, dim, ld, nd, cap, 0.5, counters, 9)
+    torch.testing.assert_close(g[:n], g0[:n] * mask.float() * 2.0)
+
+
+def _gat_ref(indptr, indices, n_dst, z, al, ar, bias, H, F_, slope, mean_heads):
+    deg = indptr[1:] - indptr[:-1]
+    v = torch.repeat_interleave(torch.arange(n_dst, device=z.device), deg[:n_dst])
+    u = indices[: int(indptr[n_dst])].long()
+    zz = z.view(z.shape[0], H, F_)
+    el = (zz * al.view(1, H, F_)).sum(-1)
+    er = (zz[:n_dst] * ar.view(1, H, F_)).sum(-1)
+    e = F.leaky_relu(el[u] + er[v], slope)
+    m = torch.full((n_dst, H), -float("inf"), device=z.device).index_reduce_(0, v, e, "amax")
+    a = torch.exp(e - m[v])
+    s = torch.zeros(n_dst, H, device=z.device).index_add_(0, v, a)
+    a = a / s[v]
+    out = torch.zeros(n_dst, H, F_, device=z.device).index_add_(0, v, zz[u] * a.unsqueeze(-1))
+    out = out + bias.view(1, H, F_)
+    return out.mean(1) if mean_heads else out.flatten(1)
+
+
+@pytest.mark.parametrize("H,F_,mean_heads", [(4, 16, False), (4, 12, True), (2, 20, True)])
+def test_gat_kernels(H, F_, mean_heads):
+    torch.manual_seed(3)
+    n_dst, n_src = 70, 300
+    deg = torch.randint(0, 9, (n_dst,))
+    indptr = torch.zeros(n_dst + 1, dtype=torch.int32)
+    indptr[1:] = torch.cumsum(deg, 0)
+    E = int(indptr[-1])
+    indices = torch.randint(0, n_src, (E,), dtype=torch.int32)
+    indptr, indices = indptr.to(DEV), indices.to(DEV)
+    HF = H * F_
+    hfp = (HF + 7) // 8 * 8
+    z = torch.zeros(n_src, hfp, dtype=torch.bfloat16, device=DEV)
+    z[:, :HF] = bf(torch.randn(n_src, HF, device=DEV))
+    al = torch.randn(HF, device=DEV) * 0.3
+    ar = torch.randn(HF, device=DEV) * 0.3
+    bias = torch.randn(HF, device=DEV) * 0.1
+    f32 = dict(dtype=torch.float32, device=DEV)
+    el, er = torch.zeros(n_src * H, **f32), torch.zeros(n_dst * H, **f32)
+    smax, ssum = torch.zeros(n_dst * H, **f32), torch.zeros(n_dst * H, **f32)
+    fo = (F_ + 7) // 8 * 8 if mean_heads else hfp
+    out = torch.zeros(n_dst, fo, dtype=torch.bfloat16, device=DEV)
+    nd = torch.tensor([n_dst], dtype=torch.int32, device=DEV)
+    ns = torch.tensor([n_src], dtype=torch.int32, device=DEV)
+    args = (indptr, indices, nd, n_dst, ns, n_src, H, F_, z, al, ar, el, er, smax, ssum, 0.2)
+    cu().gat_scores(*args)
+    cu().gat_fwd(*args, bias, mean_heads, 0, 0.0, None, 0, out)
+    zf = z[:, :HF].float().requires_grad_(True)
+    alr, arr, br = al.clone().requires_grad_(True), ar.clone().requires_grad_(True), bias.clone().requires_grad_(True)
+    ref = _gat_ref(indptr, indices, n_dst, zf, alr, arr, br, H, F_, 0.2, mean_heads)
+    w = F_ if mean_heads else HF
+    torch.testing.assert_close(out[:, :w].float(), ref, atol=2e-2, rtol=2e-2)
+    # backward
+    g = bf(torch.randn(n_dst, fo, device=DEV))
+    if mean_heads:
+        g[:, F_:] = 0
+    escr = torch.zeros(max(E, 1) * H, **f32)
+    dl_, dr_ = torch.zeros(n_src * H, **f32), torch.zeros(n_dst * H, **f32)
+    dz = torch.zeros(n_src, hfp, **f32)
+    dzb = torch.zeros(n_src + 64, hfp, dtype=torch.bfloat16, device=DEV)
+    db, dal, dar = torch.zeros(HF, **f32), torch.zeros(HF, **f32), torch.zeros(HF, **f32)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    cu().gat_bwd(*args, mean_heads, g, escr, dl_, dr_, dz, db, dal, dar, dzb, err)
+    torch.cuda.synchronize()
+    ref.backward(g[:, :w].float())
+    torch.testing.assert_close(dzb[:n_src, :HF].float(), zf.grad, atol=3e-2, rtol=3e-2)
+    torch.testing.assert_close(db, br.grad, atol=3e-2, rtol=3e-2)
+    torch.testing.assert_close(dal, alr.grad, atol=5e-2, rtol=3e-2)
+    torch.testing.assert_close(dar, arr.grad, atol=5e-2, rtol=3e-2)
+    assert torch.all(dz == 0) and torch.all(dl_ == 0)
+    assert int(err) == 0
