@@ -369,7 +369,8 @@ T* as_ptr(int64_t p) {
 void allreduce_adam(int64_t rank, int64_t world, Tensor grad, int64_t chunk, std::vector<int64_t> send_local,
                     std::vector<int64_t> send_peer, int64_t flags_local, std::vector<int64_t> flags_peer, OptT cov,
                     Tensor counters, OptT param, OptT m, OptT v, OptT param_bf16, double lr, double b1, double b2,
-                    double eps, double wd, bool do_adam, OptT grad_out, Tensor err, int64_t grid, int64_t timeout_ns) {
+                    double eps, double wd, bool do_adam, OptT grad_out, Tensor err, int64_t grid, int64_t timeout_ns,
+                    int64_t flags2_local, std::vector<int64_t> flags2_peer) {
   c10::cuda::CUDAGuard g(grad.device());
   namespace pe = grappa::peer;
   TORCH_CHECK(world >= 1 && world <= pe::kMaxRanks, "world out of range");
@@ -412,6 +413,12 @@ void allreduce_adam(int64_t rank, int64_t world, Tensor grad, int64_t chunk, std
   a.eps = static_cast<float>(eps);
   a.weight_decay = static_cast<float>(wd);
   a.err = ptr<int32_t>(err, at::kInt, "err");
+  if (flags2_local != 0) {
+    TORCH_CHECK(flags2_peer.size() == static_cast<size_t>(world), "flags2_peer has the wrong length");
+    a.two_shot = true;
+    a.flags2_local = as_ptr<uint32_t>(flags2_local);
+    for (int p = 0; p < world; ++p) a.flags2_peer[p] = as_ptr<uint32_t>(flags2_peer[p]);
+  }
   a.timeout_ns = timeout_ns;
   pe::launch_allreduce_adam(a, static_cast<int>(grid), stream());
 }
@@ -440,6 +447,38 @@ void pull_rows(std::vector<int64_t> tables, int64_t table_stride, int64_t elem_b
 
 void peer_copy(int64_t dst, int64_t src, int64_t bytes) {
   grappa::peer::launch_copy(as_ptr<void>(dst), as_ptr<const void>(src), bytes, stream());
+}
+
+void a2a_pull(std::vector<int64_t> src, std::vector<int64_t> src_off, std::vector<int64_t> len,
+              std::vector<int64_t> dst_off, int64_t dst) {
+  namespace pe = grappa::peer;
+  const size_t w = src.size();
+  TORCH_CHECK(w >= 1 && w <= static_cast<size_t>(pe::kMaxRanks) && src_off.size() == w && len.size() == w &&
+                  dst_off.size() == w,
+              "a2a_pull: one entry per rank");
+  pe::A2aArgs a;
+  a.world = static_cast<int32_t>(w);
+  for (size_t p = 0; p < w; ++p) {
+    a.src[p] = as_ptr<const uint8_t>(src[p]);
+    a.src_off[p] = src_off[p];
+    a.len[p] = len[p];
+    a.dst_off[p] = dst_off[p];
+  }
+  a.dst = as_ptr<uint8_t>(dst);
+  pe::launch_a2a_pull(a, stream());
+}
+
+void peer_barrier(int64_t rank, int64_t world, int64_t flags_local, std::vector<int64_t> flags_peer, Tensor epoch,
+                  int64_t timeout_ns, Tensor err) {
+  c10::cuda::CUDAGuard g(epoch.device());
+  namespace pe = grappa::peer;
+  TORCH_CHECK(world >= 1 && world <= pe::kMaxRanks && flags_peer.size() == static_cast<size_t>(world),
+              "peer_barrier: one flag array per rank");
+  uint32_t* fp[pe::kMaxRanks] = {};
+  for (int p = 0; p < world; ++p) fp[p] = as_ptr<uint32_t>(flags_peer[p]);
+  pe::launch_peer_barrier(static_cast<int32_t>(rank), static_cast<int32_t>(world), as_ptr<uint32_t>(flags_local), fp,
+                          ptr<int64_t>(epoch, at::kLong, "epoch"), timeout_ns, ptr<int32_t>(err, at::kInt, "err"),
+                          stream());
 }
 
 void mark_ids(int64_t ids, OptT n_dev, int64_t n, Tensor mark) {
@@ -785,9 +824,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_open", [](py::bytes h) { return reinterpret_cast<int64_t>(grappa::peer::ipc_open(std::string(h))); });
   m.def("ipc_close", [](int64_t p) { grappa::peer::ipc_close(reinterpret_cast<void*>(p)); });
   m.def("tensor_from_ptr", &tensor_from_ptr);
-  m.def("allreduce_adam", &allreduce_adam);
+  m.def("allreduce_adam", &allreduce_adam, py::arg("rank"), py::arg("world"), py::arg("grad"), py::arg("chunk"),
+        py::arg("send_local"), py::arg("send_peer"), py::arg("flags_local"), py::arg("flags_peer"), py::arg("cov"),
+        py::arg("counters"), py::arg("param"), py::arg("m"), py::arg("v"), py::arg("param_bf16"), py::arg("lr"),
+        py::arg("b1"), py::arg("b2"), py::arg("eps"), py::arg("wd"), py::arg("do_adam"), py::arg("grad_out"),
+        py::arg("err"), py::arg("grid"), py::arg("timeout_ns"), py::arg("flags2_local") = 0,
+        py::arg("flags2_peer") = std::vector<int64_t>{});
   m.def("pull_rows", &pull_rows);
   m.def("peer_copy", &peer_copy);
+  m.def("a2a_pull", &a2a_pull);
+  m.def("peer_barrier", &peer_barrier);
   m.def("mark_ids", &mark_ids);
   m.def("iota_map", &iota_map);
   m.def("mark_compact", &mark_compact);

@@ -1,6 +1,6 @@
 // Peer-memory kernels (see peer.h).
 //
-// K-AR, the fused coverage-corrected all-reduce + Adam (one-shot).  The reference
+// K-AR, the fused coverage-corrected all-reduce + Adam (one-shot or two-shot).  The reference
 // scales each rank's gradient bucket by its coverage weight c_r / W and sums the
 // buckets with an NCCL all-reduce, then runs torch.optim.Adam
 // (t10n/grad.py:6-24, experiments/grappa/train/t10n_train.py:159-162,248).  Here
@@ -16,6 +16,10 @@
 //      summed in rank order so that every rank computes bit-identical parameters;
 //      then the Adam update of the chunk writes the fp32 master weights, the
 //      moments and the bf16 working copy.
+// Two-shot (large buffers, W > 2): only the owner of chunk j (j % W) waits for and
+// sums the W copies, stores the sum in its own send slot and raises flags2[j] at
+// every rank; every rank then reads the sum from the owner and runs Adam.  Every
+// rank moves 2 (W-1)/W of the buffer over NVLink instead of W-1 times it.
 // The send slots alternate with the step parity: a rank can only start publishing
 // step t+2 after every peer has published step t+1, which each peer does only after
 // it finished reading step t, so a slot is never overwritten while it is read.
@@ -80,6 +84,29 @@ __device__ __forceinline__ void adam_update(const ArAdamArgs& a, int64_t i, floa
   if (a.param_bf16) a.param_bf16[i] = __float2bfloat16_rn(p);
 }
 
+// Bounded wait until *f reaches tag (wrap-safe); false on timeout (error recorded).
+__device__ __forceinline__ bool wait_flag(const uint32_t* f, uint32_t tag, const ArAdamArgs& a) {
+  if (static_cast<int32_t>(ld_acquire_sys(f) - tag) >= 0) return true;
+  const uint64_t t0 = dev::globaltimer_ns();
+  uint32_t polls = 0;
+  while (static_cast<int32_t>(ld_acquire_sys(f) - tag) < 0) {
+    if ((++polls & 63u) == 0) {
+      if (dev::globaltimer_ns() - t0 > static_cast<uint64_t>(a.timeout_ns)) {
+        dev::set_error(a.err, dev::kErrPeerTimeout);
+        return false;
+      }
+      __nanosleep(64);
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void finish_chunk(const ArAdamArgs& a, int64_t i, float g, float step_size,
+                                             float inv_sqrt_bc2) {
+  if (a.do_adam) adam_update(a, i, g, step_size, inv_sqrt_bc2);
+  else a.grad_out[i] = g;
+}
+
 __global__ void __launch_bounds__(256) ar_adam_kernel(ArAdamArgs a) {
   const int64_t n_chunks = ceil_div(a.n, a.chunk);
   const int64_t step = a.counters[3];
@@ -102,6 +129,7 @@ __global__ void __launch_bounds__(256) ar_adam_kernel(ArAdamArgs a) {
   for (int64_t j = blockIdx.x; j < n_chunks; j += gridDim.x) {
     const int64_t lo = j * a.chunk;
     const int64_t hi = min(a.n, lo + a.chunk);
+    const int owner = a.two_shot ? static_cast<int>(j % a.world) : -1;
     // 1. publish
     for (int64_t i = lo + threadIdx.x * 4; i < hi; i += blockDim.x * 4) {
       if (i + 3 < hi) {
@@ -119,51 +147,64 @@ __global__ void __launch_bounds__(256) ar_adam_kernel(ArAdamArgs a) {
     __syncthreads();
     if (threadIdx.x == 0) {
       __threadfence_system();
-      for (int p = 0; p < a.world; ++p) st_release_sys(a.flags_peer[p] + a.rank * n_chunks + j, tag);
+      if (a.two_shot) {
+        st_release_sys(a.flags_peer[owner] + a.rank * n_chunks + j, tag);
+      } else {
+        for (int p = 0; p < a.world; ++p) st_release_sys(a.flags_peer[p] + a.rank * n_chunks + j, tag);
+      }
     }
-    // 2. wait for every rank's copy of this chunk
-    if (threadIdx.x < a.world) {
-      const uint32_t* f = a.flags_local + threadIdx.x * n_chunks + j;
-      if (static_cast<int32_t>(ld_acquire_sys(f) - tag) < 0) {
-        const uint64_t t0 = dev::globaltimer_ns();
-        uint32_t polls = 0;
-        while (static_cast<int32_t>(ld_acquire_sys(f) - tag) < 0) {
-          if ((++polls & 63u) == 0) {
-            if (dev::globaltimer_ns() - t0 > static_cast<uint64_t>(a.timeout_ns)) {
-              dev::set_error(a.err, dev::kErrPeerTimeout);
-              s_timeout = 1;
-              break;
-            }
-            __nanosleep(64);
+    if (!a.two_shot || owner == a.rank) {
+      // 2. wait for every rank's copy of this chunk
+      if (threadIdx.x < a.world && !wait_flag(a.flags_local + threadIdx.x * n_chunks + j, tag, a)) s_timeout = 1;
+      __syncthreads();
+      if (s_timeout) continue;
+      // 3. reduce in rank order (bit-identical on every rank); one-shot: + Adam;
+      //    two-shot owner: store the sum in the own send slot for the other ranks
+      for (int64_t i = lo + threadIdx.x * 4; i < hi; i += blockDim.x * 4) {
+        if (i + 3 < hi) {
+          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int p = 0; p < a.world; ++p) {
+            const float4 x = *reinterpret_cast<const float4*>(a.send_peer[p][parity] + i);
+            acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
+          }
+          if (a.two_shot) {
+            *reinterpret_cast<float4*>(send + i) = acc;
+          } else {
+            finish_chunk(a, i, acc.x, step_size, inv_sqrt_bc2);
+            finish_chunk(a, i + 1, acc.y, step_size, inv_sqrt_bc2);
+            finish_chunk(a, i + 2, acc.z, step_size, inv_sqrt_bc2);
+            finish_chunk(a, i + 3, acc.w, step_size, inv_sqrt_bc2);
+          }
+        } else {
+          for (int64_t k = i; k < hi; ++k) {
+            float acc = 0.f;
+            for (int p = 0; p < a.world; ++p) acc += a.send_peer[p][parity][k];
+            if (a.two_shot) send[k] = acc;
+            else finish_chunk(a, k, acc, step_size, inv_sqrt_bc2);
           }
         }
       }
+      if (!a.two_shot) continue;
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        __threadfence_system();
+        for (int p = 0; p < a.world; ++p) st_release_sys(a.flags2_peer[p] + j, tag);
+      }
     }
+    // 4. two-shot: read the owner's sum, Adam
+    if (threadIdx.x == 0 && !wait_flag(a.flags2_local + j, tag, a)) s_timeout = 1;
     __syncthreads();
     if (s_timeout) continue;
-    // 3. reduce (rank order) + Adam
+    const float* red = a.send_peer[owner][parity];
     for (int64_t i = lo + threadIdx.x * 4; i < hi; i += blockDim.x * 4) {
       if (i + 3 < hi) {
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int p = 0; p < a.world; ++p) {
-          const float4 x = *reinterpret_cast<const float4*>(a.send_peer[p][parity] + i);
-          acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
-        }
-        if (a.do_adam) {
-          adam_update(a, i, acc.x, step_size, inv_sqrt_bc2);
-          adam_update(a, i + 1, acc.y, step_size, inv_sqrt_bc2);
-          adam_update(a, i + 2, acc.z, step_size, inv_sqrt_bc2);
-          adam_update(a, i + 3, acc.w, step_size, inv_sqrt_bc2);
-        } else {
-          *reinterpret_cast<float4*>(a.grad_out + i) = acc;
-        }
+        const float4 x = *reinterpret_cast<const float4*>(red + i);
+        finish_chunk(a, i, x.x, step_size, inv_sqrt_bc2);
+        finish_chunk(a, i + 1, x.y, step_size, inv_sqrt_bc2);
+        finish_chunk(a, i + 2, x.z, step_size, inv_sqrt_bc2);
+        finish_chunk(a, i + 3, x.w, step_size, inv_sqrt_bc2);
       } else {
-        for (int64_t k = i; k < hi; ++k) {
-          float acc = 0.f;
-          for (int p = 0; p < a.world; ++p) acc += a.send_peer[p][parity][k];
-          if (a.do_adam) adam_update(a, k, acc, step_size, inv_sqrt_bc2);
-          else a.grad_out[k] = acc;
-        }
+        for (int64_t k = i; k < hi; ++k) finish_chunk(a, k, red[k], step_size, inv_sqrt_bc2);
       }
     }
   }
@@ -191,6 +232,54 @@ __global__ void copy_kernel(uint4* dst, const uint4* src, int64_t n16) {
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n16;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x)
     dst[i] = src[i];
+}
+
+__global__ void a2a_pull_kernel(A2aArgs a) {
+  int64_t pre[kMaxRanks + 1];
+  pre[0] = 0;
+  for (int p = 0; p < a.world; ++p) pre[p + 1] = pre[p] + (a.len[p] >> 4);
+  const int64_t total = pre[a.world];
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    int p = 0;
+    while (i >= pre[p + 1]) ++p;
+    const int64_t k = i - pre[p];
+    const uint4* s = reinterpret_cast<const uint4*>(a.src[p] + a.src_off[p]);
+    uint4* d = reinterpret_cast<uint4*>(a.dst + a.dst_off[p]);
+    d[k] = s[k];
+  }
+}
+
+struct BarrierArgs {
+  uint32_t* flags_local;
+  uint32_t* flags_peer[kMaxRanks];
+  int64_t* epoch;
+  int64_t timeout_ns;
+  int32_t* err;
+  int32_t rank, world;
+};
+
+__global__ void peer_barrier_kernel(BarrierArgs a) {
+  const uint32_t tag = static_cast<uint32_t>(*a.epoch + 1);
+  const int p = threadIdx.x;
+  if (p < a.world) st_release_sys(a.flags_peer[p] + a.rank, tag);
+  __syncthreads();
+  if (p < a.world) {
+    const uint32_t* f = a.flags_local + p;
+    const uint64_t t0 = dev::globaltimer_ns();
+    uint32_t polls = 0;
+    while (static_cast<int32_t>(ld_acquire_sys(f) - tag) < 0) {
+      if ((++polls & 63u) == 0) {
+        if (dev::globaltimer_ns() - t0 > static_cast<uint64_t>(a.timeout_ns)) {
+          dev::set_error(a.err, dev::kErrPeerTimeout);
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+  }
+  __syncthreads();
+  if (p == 0) *a.epoch = tag;
 }
 
 __global__ void mark_kernel(const int32_t* ids, const int32_t* n_ptr, int64_t n_static, uint8_t* mark) {
@@ -299,6 +388,7 @@ int grid_for(int64_t n, int threads, int per_sm = 8) {
 void launch_allreduce_adam(const ArAdamArgs& a, int grid, cudaStream_t stream) {
   if (a.world < 1 || a.world > kMaxRanks) throw std::invalid_argument("world size out of range");
   if (a.chunk % 4 != 0) throw std::invalid_argument("chunk must be a multiple of 4");
+  if (a.two_shot && !a.flags2_local) throw std::invalid_argument("two-shot needs the second flag array");
   const int64_t n_chunks = ceil_div(a.n, a.chunk);
   // at most one CTA per SM so that all CTAs are resident while they wait on peers
   if (grid <= 0) grid = static_cast<int>(std::min<int64_t>(n_chunks, sm_count()));
@@ -319,6 +409,33 @@ void launch_copy(void* dst, const void* src, int64_t bytes, cudaStream_t stream)
   const int64_t n16 = bytes / 16;
   if (n16 == 0) return;
   copy_kernel<<<grid_for(n16, 256, 16), 256, 0, stream>>>(reinterpret_cast<uint4*>(dst), reinterpret_cast<const uint4*>(src), n16);
+  GB_LAUNCH_CHECK();
+}
+
+void launch_a2a_pull(const A2aArgs& a, cudaStream_t stream) {
+  if (a.world < 1 || a.world > kMaxRanks) throw std::invalid_argument("a2a: world out of range");
+  int64_t total = 0;
+  for (int p = 0; p < a.world; ++p) {
+    if ((a.len[p] | a.src_off[p] | a.dst_off[p]) & 15) throw std::invalid_argument("a2a: 16-byte alignment");
+    total += a.len[p] >> 4;
+  }
+  if (total == 0) return;
+  a2a_pull_kernel<<<grid_for(total, 256, 16), 256, 0, stream>>>(a);
+  GB_LAUNCH_CHECK();
+}
+
+void launch_peer_barrier(int32_t rank, int32_t world, uint32_t* flags_local, uint32_t* const* flags_peer,
+                         int64_t* epoch, int64_t timeout_ns, int32_t* err, cudaStream_t stream) {
+  if (world < 1 || world > kMaxRanks) throw std::invalid_argument("barrier: world out of range");
+  BarrierArgs a;
+  a.flags_local = flags_local;
+  for (int p = 0; p < world; ++p) a.flags_peer[p] = flags_peer[p];
+  a.epoch = epoch;
+  a.timeout_ns = timeout_ns;
+  a.err = err;
+  a.rank = rank;
+  a.world = world;
+  peer_barrier_kernel<<<1, 32, 0, stream>>>(a);
   GB_LAUNCH_CHECK();
 }
 

@@ -43,6 +43,13 @@ struct ArAdamArgs {
   float* grad_out = nullptr;
   int32_t* err = nullptr;
   int64_t timeout_ns = 10000000000ll;
+  // two-shot: chunk j is reduced by rank j % world (reads W-1 peers' copies), which
+  // stores the sum in its own send slot and raises flags2[j] at every rank; every
+  // rank then reads the sums from the owners (2 (W-1)/W of the bytes per rank
+  // instead of W-1 times them for the one-shot)
+  bool two_shot = false;
+  uint32_t* flags2_local = nullptr;                   // [n_chunks], written by the owners
+  uint32_t* flags2_peer[kMaxRanks] = {};
 };
 void launch_allreduce_adam(const ArAdamArgs& a, int grid, cudaStream_t stream);
 
@@ -65,6 +72,26 @@ void launch_pull_rows(const PullRowsArgs& a, int64_t cap, cudaStream_t stream);
 
 // contiguous copy (peer -> local), 16-byte vectors
 void launch_copy(void* dst, const void* src, int64_t bytes, cudaStream_t stream);
+
+// Pull all-to-all: this rank copies, from every rank p, the byte range
+// [src_off[p], src_off[p] + len[p]) of p's (peer-mapped) send buffer into its own
+// receive buffer at dst_off[p].  One launch for all peers, 16-byte P2P loads
+// (all offsets and lengths multiples of 16).
+struct A2aArgs {
+  const uint8_t* src[kMaxRanks] = {};
+  int64_t src_off[kMaxRanks] = {};
+  int64_t len[kMaxRanks] = {};
+  int64_t dst_off[kMaxRanks] = {};
+  uint8_t* dst = nullptr;
+  int32_t world = 1;
+};
+void launch_a2a_pull(const A2aArgs& a, cudaStream_t stream);
+
+// Device-side barrier across ranks: raise this rank's flag at every peer with the
+// next tag (*epoch + 1, kept in device memory), wait (bounded by timeout_ns, then
+// kErrPeerTimeout) until every peer's flag here reached it.  flags_local[world].
+void launch_peer_barrier(int32_t rank, int32_t world, uint32_t* flags_local, uint32_t* const* flags_peer,
+                         int64_t* epoch, int64_t timeout_ns, int32_t* err, cudaStream_t stream);
 
 // mark[g] = 1 for g in ids (global ids)
 void launch_mark(const int32_t* ids, const int32_t* n_ptr, int64_t n, uint8_t* mark, cudaStream_t stream);

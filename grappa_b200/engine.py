@@ -42,7 +42,7 @@ AGG_MEAN, AGG_SUM, AGG_GCN, AGG_WEIGHTED = 0, 1, 2, 3
 KERNELS_PER_CALL = {
     "sample_hop": 1, "walk_hop": 1, "compact": 3, "gemm": 1, "aggregate": 1, "aggregate_bwd": 1, "act_bwd": 1,
     "gather_scalar": 1, "gather_rows": 1, "adam": 1, "allreduce_adam": 1, "step_end": 1, "src_norm": 2,
-    "pull_rows": 1, "csr_merge": 1, "mark_ids": 1, "iota_map": 1, "mark_compact": 1, "peer_copy": 1,
+    "pull_rows": 1, "csr_merge": 1, "mark_ids": 1, "iota_map": 1, "mark_compact": 1, "peer_copy": 1, "a2a_pull": 1, "peer_barrier": 1,
     "shuffle_keys": 1, "cross_entropy": 1, "batchnorm_fwd": 2, "batchnorm_bwd": 2, "l2norm_fwd": 1,
     "l2norm_bwd": 1, "dropout_rows": 1, "dropout_grad": 1, "f32_to_bf16_rows": 1, "add_bf16_rows": 1,
     "gat_scores": 1, "gat_fwd": 1, "gat_bwd": 2,
@@ -886,19 +886,32 @@ def make_engine(model, *args, **kwargs):
 
 
 class FusedAllReduceAdam:
-    """Coverage-weighted gradient all-reduce fused with Adam (peer memory, one kernel)."""
+    """Coverage-weighted gradient all-reduce fused with Adam (peer memory, one kernel).
 
-    def __init__(self, comm, n, chunk=4096, timeout_s=30.0):
+    One-shot for small buffers (every rank reads all W copies: lowest latency) and
+    two-shot for large ones at W > 2 (owner-reduce then owner-broadcast: 2 (W-1)/W of
+    the bytes per rank).  ``two_shot`` forces the choice; None picks by size."""
+
+    TWO_SHOT_BYTES = 1 << 20
+
+    def __init__(self, comm, n, chunk=None, timeout_s=30.0, two_shot=None):
         from grappa_b200.parallel.comm import PeerBuffer
 
         self.comm = comm
         self.n = int(n)
+        W = comm.world
+        if two_shot is None:
+            two_shot = W > 2 and self.n * 4 >= self.TWO_SHOT_BYTES
+        self.two_shot = bool(two_shot) and W > 1
+        if chunk is None:
+            # enough chunks to keep every SM busy, 16 KB at least, 1 MB at most
+            chunk = max(4096, min(262144, (self.n // (148 * 4)) // 4 * 4))
         self.chunk = int(chunk)
         self.n_chunks = (self.n + self.chunk - 1) // self.chunk
-        W = comm.world
         half = (self.n * 4 + 255) // 256 * 256
         flag_bytes = (W * self.n_chunks * 4 + 255) // 256 * 256
-        self.buf = PeerBuffer(comm, 2 * half + flag_bytes)
+        flag2_bytes = (self.n_chunks * 4 + 255) // 256 * 256
+        self.buf = PeerBuffer(comm, 2 * half + flag_bytes + flag2_bytes)
         me = comm.rank
         self.send_local = [self.buf.ptrs[me], self.buf.ptrs[me] + half]
         self.send_peer = []
@@ -906,6 +919,11 @@ class FusedAllReduceAdam:
             self.send_peer += [self.buf.ptrs[p], self.buf.ptrs[p] + half]
         self.flags_local = self.buf.ptrs[me] + 2 * half
         self.flags_peer = [self.buf.ptrs[p] + 2 * half for p in range(W)]
+        if self.two_shot:
+            self.flags2_local = self.buf.ptrs[me] + 2 * half + flag_bytes
+            self.flags2_peer = [self.buf.ptrs[p] + 2 * half + flag_bytes for p in range(W)]
+        else:
+            self.flags2_local, self.flags2_peer = 0, []
         self.timeout_ns = int(timeout_s * 1e9)
         torch.cuda.synchronize()
         comm.barrier()
@@ -914,13 +932,14 @@ class FusedAllReduceAdam:
         cu = cu or _native.cuda()
         cu.allreduce_adam(self.comm.rank, self.comm.world, grad, self.chunk, self.send_local, self.send_peer,
                           self.flags_local, self.flags_peer, cov, counters, param, m, v, wbf, lr, b1, b2, eps, 0.0,
-                          True, None, err, grid, self.timeout_ns)
+                          True, None, err, grid, self.timeout_ns, self.flags2_local, self.flags2_peer)
 
     def reduce(self, grad, cov, counters, out, err, grid=0):
         """All-reduce only (no Adam): out = sum_r c_r grad_r / W."""
         _native.cuda().allreduce_adam(self.comm.rank, self.comm.world, grad, self.chunk, self.send_local,
                                       self.send_peer, self.flags_local, self.flags_peer, cov, counters, None, None,
-                                      None, None, 0.0, 0.9, 0.999, 1e-8, 0.0, False, out, err, grid, self.timeout_ns)
+                                      None, None, 0.0, 0.9, 0.999, 1e-8, 0.0, False, out, err, grid, self.timeout_ns,
+                                      self.flags2_local, self.flags2_peer)
 
     def close(self):
         self.buf.close()

@@ -49,7 +49,7 @@ def _entry(rank, port, fn, q, *args):
         import datetime
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
-        out = fn(rank)
+        out = fn(rank, *args)
         dist.barrier()
         dist.destroy_process_group()
         q.put((rank, True, out))
@@ -57,7 +57,7 @@ def _entry(rank, port, fn, q, *args):
         q.put((rank, False, traceback.format_exc()))
 
 
-def _ar_body(rank):
+def _ar_body(rank, two_shot=False):
     from grappa_b200.engine import FusedAllReduceAdam
     from grappa_b200.parallel.comm import Comm
     from grappa_b200.sampler_gpu import new_counters
@@ -65,7 +65,7 @@ def _ar_body(rank):
     dev = torch.device("cuda", rank)
     n = 300001
     comm = Comm()
-    ar = FusedAllReduceAdam(comm, n, chunk=4096)
+    ar = FusedAllReduceAdam(comm, n, chunk=4096, two_shot=two_shot)
     counters = new_counters(0, dev)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     out = torch.zeros(n, device=dev)
@@ -88,8 +88,9 @@ def _ar_body(rank):
     return results
 
 
-def test_fused_allreduce_two_ranks():
-    res = _run(_ar_body, _free_port())
+@pytest.mark.parametrize("two_shot", [False, True])
+def test_fused_allreduce_two_ranks(two_shot):
+    res = _run(_ar_body, _free_port(), two_shot)
     for r in range(WORLD):
         assert max(res[r]) < 1e-5, res
 
@@ -184,3 +185,38 @@ def test_partition_parallel_training_two_ranks():
     assert a["flat_head"] == b["flat_head"] and a["flat_sum"] == b["flat_sum"]
     assert a["losses"][-1] < a["losses"][0]
     assert a["acc"] == b["acc"]
+
+
+def _train_model_body(rank, name, full):
+    from grappa_b200.dataset import synthetic as S
+    from grappa_b200.graph_store import partition_from_global
+    from grappa_b200.models import get_model
+    from grappa_b200.parallel.comm import Comm
+    from grappa_b200.trainer import FullGraphTrainer, MiniBatchTrainer
+
+    dev = torch.device("cuda", rank)
+    g = S.build(S.SPECS["tiny"], dev)
+    own = partition_from_global(g, WORLD, rank, dev, part_seed=3)
+    torch.manual_seed(0)
+    model = get_model(name, g.spec.feat_dim, g.spec.n_classes, num_hidden=32, num_layers=2, dropout=0.2, n_heads=2)
+    if full:
+        tr = FullGraphTrainer(model, own, comm=Comm(), seed=2, repart_every=2, lr=1e-2)
+    else:
+        tr = MiniBatchTrainer(model, own, [5, 5], 128, comm=Comm(), seed=2, repart_every=2, lr=1e-2)
+        tr.warmup()
+    losses = []
+    for e in range(5):
+        losses.append(tr.train_epoch(e) if full else tr.train_epoch(e, host_feed=True))
+    torch.cuda.synchronize()
+    tr.engine.check_errors()
+    flat = tr.engine.flat.cpu().clone()
+    tr.close()
+    return {"losses": losses, "flat_sum": float(flat.double().sum()), "flat_head": flat[:64].tolist()}
+
+
+@pytest.mark.parametrize("name,full", [("gcn", True), ("gat", False), ("gin", False), ("pinsage", False)])
+def test_model_families_two_ranks(name, full):
+    res = _run(_train_model_body, _free_port(), name, full)
+    a, b = res[0], res[1]
+    assert a["flat_head"] == b["flat_head"] and a["flat_sum"] == b["flat_sum"]
+    assert all(np.isfinite(a["losses"]))

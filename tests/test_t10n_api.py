@@ -207,3 +207,18 @@ def test_partition_from_chunks_matches_global(tiny_chunks):
         assert torch.equal(a.gideg, b.gideg)
         assert torch.equal(a.ext_src, b.ext_src)
         assert torch.equal(a.train_mask.to(torch.int8), b.train_mask.to(torch.int8))
+
+
+def _full_cli_body(rank, a):
+    sys.argv = ["t10n_fullgraph_train", "--data_path", a["root"], "--graph_name", "tiny", "--part_method", "hash",
+                "--n_part", str(WORLD), "--model", "gcn", "--num_hidden", "16", "--num_layers", "2", "--num_epochs",
+                "6", "--lr", "0.02", "--repart_every", "3", "--log_every", "2", "--tag_id", "t", "--dropout", "0.0"]
+    from grappa_b200.train import t10n_fullgraph_train as fg
+
+    return fg.main(fg.build_parser().parse_args(), init_pg=False)
+
+
+def test_fullgraph_cli_cpu_ranks(tiny_chunks):
+    out = run_ranks(_full_cli_body, {"root": tiny_chunks.root})
+    for r in range(WORLD):
+        assert out[r]["loss"][-1] < out[r]["loss"][0]
