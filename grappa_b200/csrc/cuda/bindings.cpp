@@ -349,6 +349,13 @@ void zero_(Tensor t) {
   GB_CUDA_CHECK(cudaMemsetAsync(t.data_ptr(), 0, t.numel() * t.element_size(), stream()));
 }
 
+void sampler_counters(Tensor main, Tensor dst, int64_t step_offset) {
+  c10::cuda::CUDAGuard g(main.device());
+  TORCH_CHECK(main.numel() >= 6 && dst.numel() >= 6, "counters need 6 entries");
+  d::launch_sampler_counters(ptr<int64_t>(main, at::kLong, "main"), ptr<int64_t>(dst, at::kLong, "dst"), step_offset,
+                             stream());
+}
+
 void step_end(Tensor counters) {
   c10::cuda::CUDAGuard g(counters.device());
   TORCH_CHECK(counters.numel() >= 6, "counters needs 6 entries");
@@ -818,6 +825,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adam", &adam);
   m.def("zero_", &zero_);
   m.def("step_end", &step_end);
+  m.def("sampler_counters", &sampler_counters);
   m.def("peer_alloc", [](int64_t bytes) { return reinterpret_cast<int64_t>(grappa::peer::alloc(bytes)); });
   m.def("peer_free", [](int64_t p) { grappa::peer::release(reinterpret_cast<void*>(p)); });
   m.def("ipc_handle", [](int64_t p) { return py::bytes(grappa::peer::ipc_handle(reinterpret_cast<void*>(p))); });

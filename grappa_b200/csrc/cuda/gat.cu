@@ -47,15 +47,37 @@ int sms() {
   }
   return s;
 }
-int grid_warps(int rows) {
+int grid_warps(int rows, int per_sm = 16) {
   const int64_t want = ceil_div(rows > 0 ? rows : 1, kThreads / 32);
-  return static_cast<int>(std::min<int64_t>(want, static_cast<int64_t>(sms()) * 16));
+  return static_cast<int>(std::min<int64_t>(want, static_cast<int64_t>(sms()) * per_sm));
 }
 
 __device__ __forceinline__ void red_add_v4f(float* p, float a, float b, float c, float d) {
   asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
 }
 __device__ __forceinline__ float leaky(float x, float s) { return x > 0.f ? x : x * s; }
+
+// Column sums of per-lane partials (lane owns columns (lane + 32 q) * 8 + j, the
+// same in every warp) over the block's warps in shared memory, then one atomic per
+// column per block: the column gradients (bias, attention vectors) would otherwise
+// take one contended atomic per warp and column.  Called by every thread.
+template <int CPL>
+__device__ void block_col_atomic(const float (&v)[CPL][8], float* dst, int HF) {
+  __shared__ float s[kThreads / 32][1024];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int q = 0; q < CPL; ++q)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s[w][(lane + 32 * q) * 8 + j] = v[q][j];
+  __syncthreads();
+  for (int c = threadIdx.x; c < HF; c += blockDim.x) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < kThreads / 32; ++k) t += s[k][c];
+    if (t != 0.f) atomicAdd(dst + c, t);
+  }
+  __syncthreads();
+}
 
 // ------------------------------------------------------------------ scores
 template <int CPL>
@@ -331,15 +353,7 @@ __global__ void __launch_bounds__(kThreads) gat_bwd_edge_kernel(GatArgs a) {
     }
     if (lane < H) a.der[static_cast<int64_t>(v) * H + lane] = der_acc;
   }
-  if (a.dbias) {
-#pragma unroll
-    for (int q = 0; q < CPL; ++q) {
-      const int c0 = (lane + 32 * q) * 8;
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (c0 + j < HF && bsum[q][j] != 0.f) atomicAdd(a.dbias + c0 + j, bsum[q][j]);
-    }
-  }
+  if (a.dbias) block_col_atomic<CPL>(bsum, a.dbias, HF);
 }
 
 // ------------------------------------------------------------------ backward, per source
@@ -403,16 +417,8 @@ __global__ void __launch_bounds__(kThreads) gat_bwd_node_kernel(GatArgs a) {
       *reinterpret_cast<uint4*>(a.dz_bf16 + static_cast<int64_t>(u) * a.lddzb + c0) = f32_to_bf16x8(o);
     }
   }
-#pragma unroll
-  for (int q = 0; q < CPL; ++q) {
-    const int c0 = (lane + 32 * q) * 8;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      if (c0 + j >= HF) break;
-      if (a.dattn_l && gl[q][j] != 0.f) atomicAdd(a.dattn_l + c0 + j, gl[q][j]);
-      if (a.dattn_r && gr[q][j] != 0.f) atomicAdd(a.dattn_r + c0 + j, gr[q][j]);
-    }
-  }
+  if (a.dattn_l) block_col_atomic<CPL>(gl, a.dattn_l, HF);
+  if (a.dattn_r) block_col_atomic<CPL>(gr, a.dattn_r, HF);
 }
 
 int cpl_for(int hf) { return (hf + 255) / 256; }
@@ -451,8 +457,8 @@ void launch_gat_fwd(const GatArgs& a, cudaStream_t stream) {
 void launch_gat_bwd(const GatArgs& a, cudaStream_t stream) {
   check(a);
   if (a.lddz % 4 != 0 || a.lddzb % 8 != 0) throw std::invalid_argument("gat: gradient strides");
-  GAT_DISPATCH(gat_bwd_edge_kernel, grid_warps(a.cap_dst), 0);
-  GAT_DISPATCH(gat_bwd_node_kernel, grid_warps(a.cap_src), 0);
+  GAT_DISPATCH(gat_bwd_edge_kernel, grid_warps(a.cap_dst, 4), 0);
+  GAT_DISPATCH(gat_bwd_node_kernel, grid_warps(a.cap_src, 4), 0);
 }
 
 }  // namespace dev

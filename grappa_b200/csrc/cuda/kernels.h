@@ -386,6 +386,9 @@ void launch_gat_bwd(const GatArgs& a, cudaStream_t stream);
 
 // counters = [seed, epoch, step_in_epoch, global_step, gen, adam_t]: advance the step
 void launch_step_end(int64_t* counters, cudaStream_t stream);
+// The counters a sampler draws with for the step step_offset ahead of the main
+// counters (seed, epoch, step + offset), with its own compaction generation (+1).
+void launch_sampler_counters(const int64_t* main, int64_t* dst, int64_t step_offset, cudaStream_t stream);
 
 }  // namespace dev
 }  // namespace grappa

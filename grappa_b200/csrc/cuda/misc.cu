@@ -195,6 +195,15 @@ __global__ void adam_kernel(AdamArgs a) {
 }
 
 // counters = [seed, epoch, step_in_epoch, global_step, gen, adam_t]
+__global__ void sampler_counters_kernel(const int64_t* main, int64_t* dst, int64_t step_offset) {
+  dst[0] = main[0];
+  dst[1] = main[1];
+  dst[2] = main[2] + step_offset;
+  dst[3] = main[3] + step_offset;
+  dst[4] += 1;  // the sampler's own compaction generation
+  dst[5] = main[5];
+}
+
 __global__ void step_end_kernel(int64_t* counters) {
   counters[2] += 1;
   counters[3] += 1;
@@ -270,6 +279,11 @@ void launch_dropout_mask(uint8_t* mask, int64_t rows, int64_t cols, int64_t ld, 
 
 void launch_adam(const AdamArgs& a, cudaStream_t stream) {
   adam_kernel<<<grid_1d(a.n, 256, 4), 256, 0, stream>>>(a);
+  GB_LAUNCH_CHECK();
+}
+
+void launch_sampler_counters(const int64_t* main, int64_t* dst, int64_t step_offset, cudaStream_t stream) {
+  sampler_counters_kernel<<<1, 1, 0, stream>>>(main, dst, step_offset);
   GB_LAUNCH_CHECK();
 }
 

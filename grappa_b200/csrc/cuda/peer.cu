@@ -1,6 +1,8 @@
 // Peer-memory kernels (see peer.h).
 //
-// K-AR, the fused coverage-corrected all-reduce + Adam (one-shot or two-shot).  The reference
+// K-AR, the fused coverage-corrected all-reduce + Adam (one-shot or two-shot).
+// One CTA of 1024 threads per SM at most, so that every CTA is resident while
+// it waits on peers.  The reference
 // scales each rank's gradient bucket by its coverage weight c_r / W and sums the
 // buckets with an NCCL all-reduce, then runs torch.optim.Adam
 // (t10n/grad.py:6-24, experiments/grappa/train/t10n_train.py:159-162,248).  Here
@@ -101,13 +103,44 @@ __device__ __forceinline__ bool wait_flag(const uint32_t* f, uint32_t tag, const
   return true;
 }
 
-__device__ __forceinline__ void finish_chunk(const ArAdamArgs& a, int64_t i, float g, float step_size,
-                                             float inv_sqrt_bc2) {
+__device__ __forceinline__ void finish4(const ArAdamArgs& a, int64_t i, float4 g, float step_size,
+                                        float inv_sqrt_bc2) {
+  if (!a.do_adam) {
+    *reinterpret_cast<float4*>(a.grad_out + i) = g;
+    return;
+  }
+  float4 p = *reinterpret_cast<const float4*>(a.param + i);
+  float4 m = *reinterpret_cast<const float4*>(a.m + i);
+  float4 v = *reinterpret_cast<const float4*>(a.v + i);
+  float* pp = &p.x;
+  float* mp = &m.x;
+  float* vp = &v.x;
+  const float* gp = &g.x;
+  __nv_bfloat16 w[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    float gk = gp[k];
+    if (a.weight_decay != 0.f) gk += a.weight_decay * pp[k];
+    mp[k] = a.beta1 * mp[k] + (1.f - a.beta1) * gk;
+    vp[k] = a.beta2 * vp[k] + (1.f - a.beta2) * gk * gk;
+    pp[k] -= step_size * mp[k] / (sqrtf(vp[k]) * inv_sqrt_bc2 + a.eps);
+    w[k] = __float2bfloat16_rn(pp[k]);
+  }
+  *reinterpret_cast<float4*>(a.param + i) = p;
+  *reinterpret_cast<float4*>(a.m + i) = m;
+  *reinterpret_cast<float4*>(a.v + i) = v;
+  if (a.param_bf16) *reinterpret_cast<uint2*>(a.param_bf16 + i) = *reinterpret_cast<uint2*>(w);
+}
+
+__device__ __forceinline__ void finish1(const ArAdamArgs& a, int64_t i, float g, float step_size, float inv_sqrt_bc2) {
   if (a.do_adam) adam_update(a, i, g, step_size, inv_sqrt_bc2);
   else a.grad_out[i] = g;
 }
 
-__global__ void __launch_bounds__(256) ar_adam_kernel(ArAdamArgs a) {
+// Work split: CTA b owns chunks b, b + G, b + 2G, ... (G = grid, the same on every
+// rank).  It first publishes all of them, then waits for and reduces each, so the
+// flag round trips over NVLink overlap with the other chunks' traffic.
+__global__ void __launch_bounds__(1024) ar_adam_kernel(ArAdamArgs a) {
   const int64_t n_chunks = ceil_div(a.n, a.chunk);
   const int64_t step = a.counters[3];
   const int parity = static_cast<int>(step & 1);
@@ -123,15 +156,15 @@ __global__ void __launch_bounds__(256) ar_adam_kernel(ArAdamArgs a) {
   const float step_size = a.lr / bc1;
   const float inv_sqrt_bc2 = rsqrtf(bc2);
   float* send = a.send_local[parity];
-  __shared__ int s_timeout;  // sticky: after a timeout the CTA stops reducing
+  const int64_t vec_stride = static_cast<int64_t>(blockDim.x) * 4;
+  __shared__ int s_timeout;  // sticky: after a timeout the CTA stops waiting and reducing
   if (threadIdx.x == 0) s_timeout = 0;
 
+  // 1. publish every owned chunk: send = grad * c_r / W, grad = 0; flag the readers
   for (int64_t j = blockIdx.x; j < n_chunks; j += gridDim.x) {
     const int64_t lo = j * a.chunk;
     const int64_t hi = min(a.n, lo + a.chunk);
-    const int owner = a.two_shot ? static_cast<int>(j % a.world) : -1;
-    // 1. publish
-    for (int64_t i = lo + threadIdx.x * 4; i < hi; i += blockDim.x * 4) {
+    for (int64_t i = lo + threadIdx.x * 4; i < hi; i += vec_stride) {
       if (i + 3 < hi) {
         float4 g = *reinterpret_cast<float4*>(a.grad + i);
         *reinterpret_cast<float4*>(a.grad + i) = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -148,64 +181,64 @@ __global__ void __launch_bounds__(256) ar_adam_kernel(ArAdamArgs a) {
     if (threadIdx.x == 0) {
       __threadfence_system();
       if (a.two_shot) {
-        st_release_sys(a.flags_peer[owner] + a.rank * n_chunks + j, tag);
+        st_release_sys(a.flags_peer[j % a.world] + a.rank * n_chunks + j, tag);
       } else {
         for (int p = 0; p < a.world; ++p) st_release_sys(a.flags_peer[p] + a.rank * n_chunks + j, tag);
       }
     }
-    if (!a.two_shot || owner == a.rank) {
-      // 2. wait for every rank's copy of this chunk
-      if (threadIdx.x < a.world && !wait_flag(a.flags_local + threadIdx.x * n_chunks + j, tag, a)) s_timeout = 1;
-      __syncthreads();
-      if (s_timeout) continue;
-      // 3. reduce in rank order (bit-identical on every rank); one-shot: + Adam;
-      //    two-shot owner: store the sum in the own send slot for the other ranks
-      for (int64_t i = lo + threadIdx.x * 4; i < hi; i += blockDim.x * 4) {
-        if (i + 3 < hi) {
-          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-          for (int p = 0; p < a.world; ++p) {
+  }
+  // 2. wait for the W copies of each chunk this rank reduces; sum in rank order
+  //    (bit-identical on every rank).  One-shot: + Adam.  Two-shot (owner only):
+  //    store the sum in the own send slot and flag every rank.
+  for (int64_t j = blockIdx.x; j < n_chunks; j += gridDim.x) {
+    if (a.two_shot && static_cast<int>(j % a.world) != a.rank) continue;
+    if (threadIdx.x < a.world && !s_timeout && !wait_flag(a.flags_local + threadIdx.x * n_chunks + j, tag, a))
+      s_timeout = 1;
+    __syncthreads();
+    if (s_timeout) break;
+    const int64_t lo = j * a.chunk;
+    const int64_t hi = min(a.n, lo + a.chunk);
+    for (int64_t i = lo + threadIdx.x * 4; i < hi; i += vec_stride) {
+      if (i + 3 < hi) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int p = 0; p < kMaxRanks; ++p)
+          if (p < a.world) {
             const float4 x = *reinterpret_cast<const float4*>(a.send_peer[p][parity] + i);
             acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
           }
-          if (a.two_shot) {
-            *reinterpret_cast<float4*>(send + i) = acc;
-          } else {
-            finish_chunk(a, i, acc.x, step_size, inv_sqrt_bc2);
-            finish_chunk(a, i + 1, acc.y, step_size, inv_sqrt_bc2);
-            finish_chunk(a, i + 2, acc.z, step_size, inv_sqrt_bc2);
-            finish_chunk(a, i + 3, acc.w, step_size, inv_sqrt_bc2);
-          }
-        } else {
-          for (int64_t k = i; k < hi; ++k) {
-            float acc = 0.f;
-            for (int p = 0; p < a.world; ++p) acc += a.send_peer[p][parity][k];
-            if (a.two_shot) send[k] = acc;
-            else finish_chunk(a, k, acc, step_size, inv_sqrt_bc2);
-          }
+        if (a.two_shot) *reinterpret_cast<float4*>(send + i) = acc;
+        else finish4(a, i, acc, step_size, inv_sqrt_bc2);
+      } else {
+        for (int64_t k = i; k < hi; ++k) {
+          float acc = 0.f;
+          for (int p = 0; p < a.world; ++p) acc += a.send_peer[p][parity][k];
+          if (a.two_shot) send[k] = acc;
+          else finish1(a, k, acc, step_size, inv_sqrt_bc2);
         }
       }
-      if (!a.two_shot) continue;
+    }
+    if (a.two_shot) {
       __syncthreads();
       if (threadIdx.x == 0) {
         __threadfence_system();
         for (int p = 0; p < a.world; ++p) st_release_sys(a.flags2_peer[p] + j, tag);
       }
     }
-    // 4. two-shot: read the owner's sum, Adam
-    if (threadIdx.x == 0 && !wait_flag(a.flags2_local + j, tag, a)) s_timeout = 1;
+  }
+  if (!a.two_shot) return;
+  // 3. two-shot: read every chunk's sum from its owner, Adam
+  for (int64_t j = blockIdx.x; j < n_chunks; j += gridDim.x) {
+    if (threadIdx.x == 0 && !s_timeout && !wait_flag(a.flags2_local + j, tag, a)) s_timeout = 1;
     __syncthreads();
-    if (s_timeout) continue;
-    const float* red = a.send_peer[owner][parity];
-    for (int64_t i = lo + threadIdx.x * 4; i < hi; i += blockDim.x * 4) {
-      if (i + 3 < hi) {
-        const float4 x = *reinterpret_cast<const float4*>(red + i);
-        finish_chunk(a, i, x.x, step_size, inv_sqrt_bc2);
-        finish_chunk(a, i + 1, x.y, step_size, inv_sqrt_bc2);
-        finish_chunk(a, i + 2, x.z, step_size, inv_sqrt_bc2);
-        finish_chunk(a, i + 3, x.w, step_size, inv_sqrt_bc2);
-      } else {
-        for (int64_t k = i; k < hi; ++k) finish_chunk(a, k, red[k], step_size, inv_sqrt_bc2);
-      }
+    if (s_timeout) break;
+    const float* red = a.send_peer[j % a.world][parity];
+    const int64_t lo = j * a.chunk;
+    const int64_t hi = min(a.n, lo + a.chunk);
+    for (int64_t i = lo + threadIdx.x * 4; i < hi; i += vec_stride) {
+      if (i + 3 < hi) finish4(a, i, *reinterpret_cast<const float4*>(red + i), step_size, inv_sqrt_bc2);
+      else
+        for (int64_t k = i; k < hi; ++k) finish1(a, k, red[k], step_size, inv_sqrt_bc2);
     }
   }
 }
@@ -394,7 +427,7 @@ void launch_allreduce_adam(const ArAdamArgs& a, int grid, cudaStream_t stream) {
   if (grid <= 0) grid = static_cast<int>(std::min<int64_t>(n_chunks, sm_count()));
   grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({static_cast<int64_t>(grid), n_chunks,
                                                                    static_cast<int64_t>(sm_count())})));
-  ar_adam_kernel<<<grid, 256, 0, stream>>>(a);
+  ar_adam_kernel<<<grid, 1024, 0, stream>>>(a);
   GB_LAUNCH_CHECK();
 }
 

@@ -45,7 +45,7 @@ KERNELS_PER_CALL = {
     "pull_rows": 1, "csr_merge": 1, "mark_ids": 1, "iota_map": 1, "mark_compact": 1, "peer_copy": 1, "a2a_pull": 1, "peer_barrier": 1,
     "shuffle_keys": 1, "cross_entropy": 1, "batchnorm_fwd": 2, "batchnorm_bwd": 2, "l2norm_fwd": 1,
     "l2norm_bwd": 1, "dropout_rows": 1, "dropout_grad": 1, "f32_to_bf16_rows": 1, "add_bf16_rows": 1,
-    "gat_scores": 1, "gat_fwd": 1, "gat_bwd": 2,
+    "gat_scores": 1, "gat_fwd": 1, "gat_bwd": 2, "sampler_counters": 1,
 }
 
 
@@ -78,6 +78,19 @@ def bn_for(n, mn_major=False):
     if n <= 128:
         return 128
     return 256
+
+
+def gemm_bn(M_cap, N, mn_major=False, sms=148):
+    """Tile width for an M_cap x N output: the widest tile (fewest B re-reads, longest
+    rows per epilogue thread) that still gives about two CTAs per SM, assuming a third
+    of the row capacity is live (block sizes are a fraction of their capacity)."""
+    bn = bn_for(N, mn_major)
+    if bn == 48:
+        return bn
+    mt = math.ceil(max(1, M_cap // 3) / 128)
+    while bn > 64 and mt * math.ceil(N / bn) < 2 * sms:
+        bn //= 2
+    return bn
 
 
 def split_k(rows, n_tiles, sms=148, min_kblocks=8):
@@ -178,7 +191,8 @@ class BlockEngine:
     model_name = None
 
     def __init__(self, model, n_nodes_cap, fanouts, batch_size, device, lr=3e-3, comm=None, seed=0,
-                 fused_allreduce=True, use_cuda_graph=True, betas=(0.9, 0.999), eps=1e-8, blocks=None):
+                 fused_allreduce=True, use_cuda_graph=True, betas=(0.9, 0.999), eps=1e-8, blocks=None,
+                 overlap_sampling=True):
         if getattr(model, "name", None) != self.model_name:
             raise ValueError(f"{type(self).__name__} trains {self.model_name} models")
         self.cu = LaunchCounter(_native.cuda())
@@ -213,20 +227,40 @@ class BlockEngine:
         self._ce_dummy = torch.zeros((1, 1), dtype=torch.float32, device=dev)
         self.allreduce = FusedAllReduceAdam(comm, self.flat.numel()) if self.fused_allreduce else None
 
+        # block sources: with CUDA graphs two samplers alternate, so that the next
+        # step's sampling (a side stream inside the step graph) overlaps this step's
+        # layers; the eager path uses the first one only
         if blocks is None:
-            self.sm = self._make_sampler(int(batch_size), int(n_nodes_cap), dev)
+            n = 2 if (use_cuda_graph and overlap_sampling) else 1
+            samplers = [self._make_sampler(int(batch_size), int(n_nodes_cap), dev) for _ in range(n)]
         else:
-            self.sm = blocks
-        self.full_graph = getattr(self.sm, "full_graph", False)
+            samplers = [blocks]
         self._cov_one = torch.ones(2, dtype=torch.float32, device=dev)
-        self.B = self.sm.B
-        self.seeds = self.sm.seeds
-        self.seed_label = torch.zeros(self.B, dtype=torch.int32, device=dev)
         self.n_classes = model.n_classes
+        self._working = None
+        self._set_samplers(samplers)
+
+    def _set_samplers(self, samplers):
+        dev = self.device
+        self.samplers = samplers
+        self.full_graph = getattr(samplers[0], "full_graph", False)
+        self.B = samplers[0].B
+        self.scnt = [new_counters(self.seed, dev) for _ in samplers]      # per-sampler draw counters
+        self.covs = [torch.zeros(2, dtype=torch.float32, device=dev) for _ in samplers]
+        self.seed_labels = [torch.zeros(self.B, dtype=torch.int32, device=dev) for _ in samplers]
+        self._select(0)
         self.lay = []
         self._alloc_layers()
-        self._working = None
         self._graph = None
+        self._graphs = {}
+
+    def _select(self, p):
+        """Make sampler p the one whose blocks the layers run on."""
+        self.p_cur = p
+        self.sm = self.samplers[p]
+        self.seeds = self.sm.seeds
+        self.seed_label = self.seed_labels[p]
+        self.cov_cur = self.covs[p]
 
     def _make_sampler(self, batch_size, n_nodes_cap, dev):
         return GpuNeighborSampler(self.fanouts, batch_size, n_nodes_cap, dev, cu=self.cu)
@@ -234,14 +268,7 @@ class BlockEngine:
     def set_blocks(self, blocks):
         """Replace a fixed block source (full-graph training after a repartition) and
         re-size the layer buffers; parameters and optimizer state are kept."""
-        self.sm = blocks
-        self.full_graph = getattr(blocks, "full_graph", False)
-        self.B = blocks.B
-        self.seeds = blocks.seeds
-        self.seed_label = torch.zeros(self.B, dtype=torch.int32, device=self.device)
-        self.lay = []
-        self._alloc_layers()
-        self._graph = None
+        self._set_samplers([blocks])
 
     # ------------------------------------------------------------------ helpers
     def _seg(self, name, buf=None):
@@ -280,7 +307,7 @@ class BlockEngine:
 
     def _gemm(self, A, a_mn, B, b_mn, M_cap, M_dev, N, K_cap, K_dev, splits, C, mode, bias=None, act=0, p=0.0,
               salt=0, bn=None):
-        bn = bn or bn_for(N, b_mn)
+        bn = bn or gemm_bn(M_cap, N, b_mn)
         self.cu.gemm(A, a_mn, B, b_mn, M_cap, M_dev, N, K_cap, K_dev, splits, C, mode, bias, act, p,
                      self.counters if p > 0 else None, salt, None, 0, None, None, None, None, None, None, self.err, bn)
 
@@ -298,6 +325,7 @@ class BlockEngine:
         self.labels = labels
         self.gideg = gideg
         self._graph = None  # pointers may have changed: capture again
+        self._graphs = {}
 
     def set_epoch(self, epoch):
         self.counters[C_EPOCH] = int(epoch)
@@ -307,14 +335,23 @@ class BlockEngine:
     def _cov(self):
         """[coverage sum, count] of the step: the sampler's for mini-batches; a fixed 1/1
         for full-graph training (every in-edge of the partition is present)."""
-        return self._cov_one if self.full_graph else self.fstats[0:2]
+        return self._cov_one if self.full_graph else self.cov_cur
 
-    def _sample(self):
+    def _sample_into(self, q, step_offset):
+        """Sample the blocks of the step ``step_offset`` ahead of the main counters into
+        sampler q (its own draw counters, coverage and seed labels)."""
         if self.full_graph:
             return
         w = self._working
-        self.cu.gather_scalar(self.labels, self.sm.seeds, self.sm.n_seeds(), 0, self.B, self.seed_label)
-        self.sm.sample(w.indptr, w.indices, self.counters, gideg=self.gideg, cov=self.fstats[0:2], err=self.err)
+        sm = self.samplers[q]
+        cu = self.cu
+        cu.sampler_counters(self.counters, self.scnt[q], step_offset)
+        cu.zero_(self.covs[q])
+        cu.gather_scalar(self.labels, sm.seeds, sm.n_seeds(), 0, self.B, self.seed_labels[q])
+        sm.sample(w.indptr, w.indices, self.scnt[q], gideg=self.gideg, cov=self.covs[q], err=self.err)
+
+    def _sample(self):
+        self._sample_into(self.p_cur, 0)
 
     def _forward(self, training=True):
         raise NotImplementedError
@@ -351,16 +388,85 @@ class BlockEngine:
         self._update()
         self.cu.step_end(self.counters)
 
-    def capture(self):
-        """Capture the step into a CUDA graph (after one eager step has run)."""
+    def _capture(self, body):
         s = torch.cuda.Stream(device=self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         g = torch.cuda.CUDAGraph()
         with torch.cuda.stream(s):
             with torch.cuda.graph(g, stream=s):
-                self._step_body()
+                body()
         torch.cuda.current_stream(self.device).wait_stream(s)
-        self._graph = g
+        return g
+
+    def capture(self):
+        """Capture the single-sampler step into a CUDA graph (after one eager step has run)."""
+        self._select(0)
+        self._graph = self._capture(self._step_body)
+
+    def _overlapped_step_body(self, p, prefetch):
+        """Layers of the step on sampler p; with ``prefetch`` the next step is sampled
+        into the other sampler on a side stream that joins before the counters advance."""
+        self._select(p)
+        main = torch.cuda.current_stream(self.device)
+        self.cu.zero_(self.fstats)
+        self.cu.zero_(self.istats)
+        if prefetch:
+            side = torch.cuda.Stream(device=self.device)
+            side.wait_stream(main)
+            with torch.cuda.stream(side):
+                self._sample_into(1 - p, 1)
+        self._forward(True)
+        self._backward()
+        self._update()
+        if prefetch:
+            main.wait_stream(side)
+        self.cu.step_end(self.counters)
+
+    def _graph_for(self, key):
+        g = self._graphs.get(key)
+        if g is None:
+            torch.cuda.synchronize(self.device)
+            if key[0] == "sample":
+                p = key[1]
+
+                def body():
+                    self._select(p)
+                    self._sample_into(p, 0)
+
+                g = self._capture(body)
+            else:
+                g = self._capture(lambda: self._overlapped_step_body(key[1], key[2]))
+            self._graphs[key] = g
+        return g
+
+    def _load_into(self, q, seeds, count):
+        sm = self.samplers[q]
+        sm.seeds.copy_(seeds, non_blocking=True)
+        sm.cnt[0:1].copy_(count, non_blocking=True)
+
+    def run_epoch(self, seeds, counts, ring=None):
+        """Run the mini-batches ``seeds[s]`` / ``counts[s]`` of one epoch (the counters'
+        epoch must be set).  With CUDA graphs and two samplers every step graph samples
+        the next step's blocks while it computes.  ``ring[s]`` receives step s's loss."""
+        nb = int(seeds.shape[0])
+        if not (self.use_cuda_graph and len(self.samplers) > 1):
+            for s in range(nb):
+                self.step(seeds[s], counts[s])
+                if ring is not None:
+                    ring[s:s + 1].copy_(self.fstats[2:3], non_blocking=True)
+            return
+        p = 0
+        self._load_into(p, seeds[0], counts[0])
+        self._graph_for(("sample", p)).replay()
+        for s in range(nb):
+            nxt = s + 1 < nb
+            if nxt:
+                self._load_into(1 - p, seeds[s + 1], counts[s + 1])
+            self._graph_for(("step", p, nxt)).replay()
+            if ring is not None:
+                ring[s:s + 1].copy_(self.fstats[2:3], non_blocking=True)
+            p ^= 1
+        self._select(0)
 
     def load_seeds(self, seeds, count):
         """Copy this step's seeds ([B] int32) and seed count ([1] int32) into the static
@@ -372,6 +478,7 @@ class BlockEngine:
         self.sm.cnt[0:1].copy_(count, non_blocking=True)
 
     def step(self, seeds=None, count=None):
+        self._select(0)
         if seeds is not None:
             self.load_seeds(seeds, count)
         if self.use_cuda_graph and self._graph is not None:
@@ -390,6 +497,7 @@ class BlockEngine:
 
     def predict(self, seeds, count):
         """Forward only (eval mode) for the given seeds; returns (correct, loss) on the device."""
+        self._select(0)
         self.load_seeds(seeds, count)
         self.cu.zero_(self.fstats)
         self.cu.zero_(self.istats)
@@ -499,7 +607,7 @@ class SageEngine(BlockEngine):
                 break
             # dX = dY W (W read MN-major)
             self._gemm(s["dY"], False, s["W"], True, s["rows"], self._n_dst(h), s["K"], s["op"], None, 1, s["dX"],
-                       GEMM_STORE_BF16, bn=256)
+                       GEMM_STORE_BF16)
             prev = self.lay[l - 1]
             # transpose aggregation: d(self) -> dst rows, d(agg) -> sources
             cu.aggregate_bwd(sm.indptr[h], sm.indices[h], self._n_dst(h), 0, sm.cap_dst[h], s["dX"],

@@ -10,9 +10,11 @@
       nccl     all_to_all_single of the same bytes
 
 Times are CUDA-event device times of the collective alone, after warm-up, the max
-over ranks.  The roofline time is the bytes that must cross NVLink per GPU and
-direction divided by the measured 770 GB/s peer bandwidth: 2 (W-1)/W * S for an
-all-reduce of S bytes, (W-1)/W of the sent bytes for the all-to-all.
+over ranks.  The roofline time is the slower of the bytes that must cross NVLink
+per GPU and direction at the measured 770 GB/s peer bandwidth (2 (W-1)/W * S for
+an all-reduce of S bytes, the remote part of the sent bytes for the all-to-all)
+and, for the all-reduce fused with Adam, the local HBM bytes of the update at the
+measured 6.56 TB/s.
 
     python -m torch.distributed.run --nproc-per-node W --master-addr 127.0.0.1 \\
         -m grappa_b200.parallel.bench_collectives [--part a|b|ab] [--max-bytes N]
@@ -26,6 +28,7 @@ import torch
 import torch.distributed as dist
 
 LINK_GBS = 770.0  # measured peer copy bandwidth per direction per GPU
+HBM_GBS = 6555.8  # measured HBM copy bandwidth of this GPU type
 
 
 def _max_over_ranks(x, dev):
@@ -92,7 +95,14 @@ def bench_allreduce(comm, dev, sizes, iters_for):
             cu.step_end(counters)
 
         row["nccl_ms"] = _time(run_nccl, iters, 3, dev)
-        roof_ms = 2.0 * (W - 1) / W * n * 4 / (LINK_GBS * 1e9) * 1e3
+        link_ms = 2.0 * (W - 1) / W * n * 4 / (LINK_GBS * 1e9) * 1e3
+        # local HBM bytes per element: publish (grad read + clear, send write) 12, the
+        # peers' reads of this rank's copy 4 (W-1), Adam (param, m, v read and write,
+        # bf16 copy) 26, the reduced value 4
+        hbm_ms = (42.0 + 4.0 * (W - 1)) * n / (HBM_GBS * 1e9) * 1e3
+        roof_ms = max(link_ms, hbm_ms)
+        row["roofline_link_ms"] = link_ms
+        row["roofline_hbm_ms"] = hbm_ms
         row["roofline_ms"] = roof_ms
         best = min(v for k, v in row.items() if k.startswith("fused") and k.endswith("_ms"))
         row["fused_best_ms"] = best

@@ -106,12 +106,9 @@ class MiniBatchTrainer:
             self.engine.prepare()
         seeds, counts = self.epoch_seeds(epoch, on_host=host_feed)
         self.engine.set_epoch(epoch)
+        # device -> host read of every step's loss (pinned, asynchronous)
         ring = torch.zeros(self.n_batches, dtype=torch.float32).pin_memory() if host_feed else None
-        for s in range(self.n_batches):
-            self.engine.step(seeds[s], counts[s])
-            if host_feed:
-                # device -> host read of the step's loss (pinned, asynchronous)
-                ring[s:s + 1].copy_(self.engine.fstats[2:3], non_blocking=True)
+        self.engine.run_epoch(seeds, counts, ring)
         if host_feed:
             torch.cuda.current_stream(self.device).synchronize()
             self.last_losses = ring
