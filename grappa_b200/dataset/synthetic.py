@@ -218,7 +218,7 @@ def to_t10n_layout(graph, out_dir):
         "num_nodes": n,
         "num_edges": int(u.numel()),
         "feat_dim": graph.spec.feat_dim,
-        "num_classes": graph.spec.n_classes,
+        "num_labels": graph.spec.n_classes,
         "edge_file_bin": os.path.join(out_dir, "edge_index.bin.npy"),
         "node_feats_file_bin": os.path.join(out_dir, "node_feat.bin.npy"),
         "node_label_file": os.path.join(out_dir, "node_label.bin.npy"),

@@ -222,3 +222,51 @@ def test_fullgraph_cli_cpu_ranks(tiny_chunks):
     out = run_ranks(_full_cli_body, {"root": tiny_chunks.root})
     for r in range(WORLD):
         assert out[r]["loss"][-1] < out[r]["loss"][0]
+
+
+def test_t10n_alias_and_converters(tmp_path, tiny_chunks):
+    import importlib
+
+    import t10n  # noqa: F401
+    from t10n._C.graph import HostGraph
+    from t10n.dataset.meta import name_to_meta
+    from t10n.sampler import HostBatchSamplerWithCounter
+    from t10n.dgl_dsg.sampler import PinSAGESampler, to_dgl_batch
+
+    assert importlib.import_module("t10n.dataloader").IsolatedDataloader is not None
+    assert name_to_meta("tiny").n_dim == 32
+    from grappa_b200.dataset.dgl_to_t10n import convert, write_t10n
+
+    g = tiny_chunks.graph
+    # npz round trip through the converter
+    npz = tmp_path / "g.npz"
+    np.savez(npz, edge_index=np.stack([g.u.numpy(), g.v.numpy()]), feat=g.feat.numpy(), label=g.label.numpy(),
+             train_mask=g.train_mask.numpy(), val_mask=g.val_mask.numpy(), test_mask=g.test_mask.numpy())
+    cfg = convert(str(npz), str(tmp_path / "out"), "tiny")
+    assert cfg["num_edges"] == g.u.numel() + g.n_nodes and cfg["num_labels"] == 8
+    e = np.load(cfg["edge_file_bin"])
+    assert e.shape[0] == 2 * cfg["num_edges"]
+    hg = HostGraph(g.u.numpy(), g.v.numpy(), g.n_nodes)
+    s = HostBatchSamplerWithCounter(hg, torch.arange(100), [3, 3], batch_size=50, target_nodes_gideg=torch.ones(100,
+                                    dtype=torch.int64))
+    n = sum(1 for _ in s)
+    assert n == 2
+    inp, out, blocks = PinSAGESampler(hg, 2).sample_blocks(None, torch.arange(10))
+    assert blocks[-1].n_dst == 10 and "weights" in blocks[-1].edata
+    u = torch.tensor([5, 6, 7]); v = torch.tensor([1, 1, 2])
+    src, dst, b = to_dgl_batch(torch.tensor([1, 2]), [u, v])
+    assert b[0].n_dst == 2 and b[0].num_edges() == 3
+
+
+def test_launcher_sweep_and_table(tmp_path):
+    from grappa_b200 import launch
+
+    out = launch.main(["--dry_run", "--models", "sage,gcn", "--layers_fanouts", "2:10,5;3:15,10,5", "--runs", "2",
+                       "--log_dir", str(tmp_path)])
+    assert out == 0
+    log = tmp_path / "t10n_hash_rmat16k_sage_2_1_R1_0.txt"
+    log.write_text("rank0 infer_|epoch|0009|part|0000|val_acc|0.8000|test_acc|0.7500|train_acc|0.9\n")
+    (tmp_path / "t10n_hash_rmat16k_gcn_3_1_R1_0.txt").write_text(
+        "rank0 infer_|epoch|0009|part|0000|val_acc|0.7|test_acc|0.6100|train_acc|0.8\n")
+    table = launch.result_table(str(tmp_path))
+    assert "| sage_2 | 0.75 |" in table and "| gcn_3 | 0.61 |" in table
