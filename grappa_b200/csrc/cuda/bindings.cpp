@@ -145,6 +145,7 @@ void gemm(Tensor A, bool a_mn, Tensor B, bool b_mn, int64_t M_cap, OptT M_dev, i
   if (mode == d::kStoreBf16) {
     a.C = ptr2d<at::BFloat16>(C, at::kBFloat16, "C");
     a.ldc = C.stride(0);
+    a.c_rows = C.size(0);
   } else if (mode != d::kCrossEntropy) {
     a.C = ptr2d<float>(C, at::kFloat, "C");
     a.ldc = C.stride(0);

@@ -53,7 +53,9 @@ int grid_warps(int rows, int per_sm = 16) {
 }
 
 __device__ __forceinline__ void red_add_v4f(float* p, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+  // no "memory" clobber: the reduced buffer is not read in the same launch, and a
+  // compiler barrier here would serialise the edge loop's loads behind every reduction
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d));
 }
 __device__ __forceinline__ float leaky(float x, float s) { return x > 0.f ? x : x * s; }
 
@@ -87,6 +89,43 @@ __global__ void __launch_bounds__(kThreads) gat_scores_kernel(GatArgs a) {
   const int HF = a.heads * a.feat;
   const int lane = threadIdx.x & 31;
   const int warps_total = (gridDim.x * kThreads) >> 5;
+  // fast path: heads of F % 8 == 0 columns with F / 8 lanes per head (a power of two
+  // below 32): every 8-column chunk lies in one head, reduced by a segmented shuffle
+  const int g = a.feat / 8;
+  const bool seg = a.feat % 8 == 0 && g < 32 && (g & (g - 1)) == 0;
+  if (seg) {
+    for (int r = (blockIdx.x * kThreads + threadIdx.x) >> 5; r < n_src; r += warps_total) {
+      const bool is_dst = r < n_dst;
+#pragma unroll
+      for (int q = 0; q < CPL; ++q) {
+        const int c0 = (lane + 32 * q) * 8;
+        float sl = 0.f, sr = 0.f;
+        if (c0 < HF) {
+          float f[8], al[8], ar[8];
+          bf16x8_to_f32(*reinterpret_cast<const uint4*>(a.z + static_cast<int64_t>(r) * a.ldz + c0), f);
+          *reinterpret_cast<float4*>(al) = __ldg(reinterpret_cast<const float4*>(a.attn_l + c0));
+          *reinterpret_cast<float4*>(al + 4) = __ldg(reinterpret_cast<const float4*>(a.attn_l + c0 + 4));
+          *reinterpret_cast<float4*>(ar) = __ldg(reinterpret_cast<const float4*>(a.attn_r + c0));
+          *reinterpret_cast<float4*>(ar + 4) = __ldg(reinterpret_cast<const float4*>(a.attn_r + c0 + 4));
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            sl += f[j] * al[j];
+            sr += f[j] * ar[j];
+          }
+        }
+        for (int off = 1; off < g; off <<= 1) {
+          sl += __shfl_xor_sync(0xffffffffu, sl, off);
+          sr += __shfl_xor_sync(0xffffffffu, sr, off);
+        }
+        if (c0 < HF && (lane & (g - 1)) == 0) {
+          const int h = c0 / a.feat;
+          a.el[static_cast<int64_t>(r) * a.heads + h] = sl;
+          if (is_dst) a.er[static_cast<int64_t>(r) * a.heads + h] = sr;
+        }
+      }
+    }
+    return;
+  }
   for (int r = (blockIdx.x * kThreads + threadIdx.x) >> 5; r < n_src; r += warps_total) {
     float pl[kMaxHeads], pr[kMaxHeads];
 #pragma unroll
@@ -393,22 +432,44 @@ __global__ void __launch_bounds__(kThreads) gat_bwd_node_kernel(GatArgs a) {
       if (c0 >= a.lddzb) continue;
       float o[8];
       if (c0 < HF) {
-        float zf[8];
+        // all loads of the chunk first (16-byte vectors), then the arithmetic, then the
+        // stores: no load waits behind a store that might alias it
+        float zf[8], dv[8], al[8], ar[8];
         bf16x8_to_f32(*reinterpret_cast<const uint4*>(a.z + static_cast<int64_t>(u) * a.ldz + c0), zf);
         float* d = a.dz + static_cast<int64_t>(u) * a.lddz + c0;
+        const bool full = c0 + 8 <= HF;
+        if (full) {
+          *reinterpret_cast<float4*>(dv) = *reinterpret_cast<const float4*>(d);
+          *reinterpret_cast<float4*>(dv + 4) = *reinterpret_cast<const float4*>(d + 4);
+          *reinterpret_cast<float4*>(al) = __ldg(reinterpret_cast<const float4*>(a.attn_l + c0));
+          *reinterpret_cast<float4*>(al + 4) = __ldg(reinterpret_cast<const float4*>(a.attn_l + c0 + 4));
+          *reinterpret_cast<float4*>(ar) = __ldg(reinterpret_cast<const float4*>(a.attn_r + c0));
+          *reinterpret_cast<float4*>(ar + 4) = __ldg(reinterpret_cast<const float4*>(a.attn_r + c0 + 4));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const bool in = c0 + j < HF;
+            dv[j] = in ? d[j] : 0.f;
+            al[j] = in ? a.attn_l[c0 + j] : 0.f;
+            ar[j] = in ? a.attn_r[c0 + j] : 0.f;
+          }
+        }
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const int c = c0 + j;
-          if (c >= HF) {
-            o[j] = 0.f;
-            continue;
-          }
           const bool first = c / F == ha;
           const float cl = first ? dla : dlb, cr = first ? dra : drb;
-          o[j] = d[j] + cl * a.attn_l[c] + cr * a.attn_r[c];
-          d[j] = 0.f;
-          gl[q][j] += cl * zf[j];
-          gr[q][j] += cr * zf[j];
+          o[j] = c < HF ? dv[j] + cl * al[j] + cr * ar[j] : 0.f;
+          if (c < HF) {
+            gl[q][j] += cl * zf[j];
+            gr[q][j] += cr * zf[j];
+          }
+        }
+        if (full) {
+          *reinterpret_cast<float4*>(d) = make_float4(0.f, 0.f, 0.f, 0.f);
+          *reinterpret_cast<float4*>(d + 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+        } else {
+          for (int j = 0; j < 8 && c0 + j < HF; ++j) d[j] = 0.f;
         }
       } else {
 #pragma unroll

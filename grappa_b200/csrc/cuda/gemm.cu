@@ -91,6 +91,14 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// TMA store of one [box rows][64 cols] bf16 panel from 128B-swizzled shared memory.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* smem_src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(smem_u32(smem_src))
+               : "memory");
+}
+
 __device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(ncols)
                : "memory");
@@ -168,9 +176,11 @@ struct Smem {
 
 template <int BN, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 2)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs a) {
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmC, GemmArgs a) {
   using S = Smem<BN>;
   constexpr int kStages = S::kStages;
+  constexpr bool kTmaStore = BN % 64 == 0 && 4 * 32 * BN * 2 <= kStages * S::kStageBytes;
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t full_bar[kStages], empty_bar[kStages], tmem_bar;
   __shared__ uint32_t tmem_slot;
@@ -356,6 +366,70 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (a.pred_out) a.pred_out[m] = arg;
       }
      }
+    } else if (kTmaStore && a.c_mode == kStoreBf16) {
+      // bf16 tile through shared memory and TMA stores: each epilogue warp stages its
+      // 32 rows as 64-column panels in the 128B-swizzled layout of the store's tensor
+      // map (reusing the drained operand ring) and one lane stores them
+      const uint64_t key = a.counters ? hop_key(static_cast<uint64_t>(a.counters[0]) ^ 0xD80Full,
+                                                static_cast<uint64_t>(a.counters[1]),
+                                                static_cast<uint64_t>(a.counters[2]), a.dropout_salt)
+                                      : 0ull;
+      const float keep_scale = a.dropout_p > 0.f ? 1.0f / (1.0f - a.dropout_p) : 1.0f;
+      const uint32_t thr = static_cast<uint32_t>(static_cast<double>(a.dropout_p) * 4294967296.0);
+      uint8_t* stage = smem + quarter * (32 * BN * 2);
+      const bool live = m < M;
+      // a 32-row slab that crosses the live row count stores its live rows directly,
+      // so that rows >= M are never written
+      const bool slab_full = m0 + quarter * 32 + 32 <= M;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        float v[32];
+        tmem_ld32(trow + c, v);
+        const int nc = n0 + c;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          float x = v[j];
+          if (a.bias && nc + j < a.N) x += a.bias[nc + j];
+          if (a.act == 1) x = fmaxf(x, 0.f);
+          v[j] = live ? x : 0.f;
+        }
+        if (a.dropout_p > 0.f && live) {
+          const uint64_t base = static_cast<uint64_t>(m) * static_cast<uint64_t>(a.ldc) + static_cast<uint64_t>(nc);
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            const U4 r = index_draw4(key, (base + j) >> 2, 0);
+            v[j] = r.x >= thr ? v[j] * keep_scale : 0.f;
+            v[j + 1] = r.y >= thr ? v[j + 1] * keep_scale : 0.f;
+            v[j + 2] = r.z >= thr ? v[j + 2] * keep_scale : 0.f;
+            v[j + 3] = r.w >= thr ? v[j + 3] * keep_scale : 0.f;
+          }
+        }
+        if (slab_full) {
+          uint8_t* panel = stage + (c >> 6) * 4096 + lane * 128;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int k = ((c & 63) >> 3) + q;
+            *reinterpret_cast<uint4*>(panel + ((k ^ (lane & 7)) << 4)) = f32_to_bf16x8(v + 8 * q);
+          }
+        } else if (live && ok && nc < a.N) {
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.C) + static_cast<int64_t>(m) * a.ldc + nc;
+          if (nc + 32 <= a.ldc) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) *reinterpret_cast<uint4*>(dst + j) = f32_to_bf16x8(v + j);
+          } else {
+            for (int j = 0; j < 32 && nc + j < a.ldc; ++j) dst[j] = __float2bfloat16_rn(v[j]);
+          }
+        }
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0 && ok && slab_full) {
+        for (int p = 0; p < BN / 64; ++p)
+          if (n0 + p * 64 < a.N) tma_store_2d(&tmC, stage + p * 4096, n0 + p * 64, m0 + quarter * 32);
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+      }
+      __syncwarp();
     } else {
       const uint64_t key = a.counters ? hop_key(static_cast<uint64_t>(a.counters[0]) ^ 0xD80Full,
                                                 static_cast<uint64_t>(a.counters[1]),
@@ -466,6 +540,12 @@ void launch_t(const GemmProblem& p, const GemmArgs& a, dim3 grid, cudaStream_t s
   // A: K-major -> [M rows][K cols]; MN-major -> [K rows][M cols]
   const CUtensorMap ma = A_MN ? make_map(p.A, p.a_rows, p.a_cols, p.lda, BK) : make_map(p.A, p.a_rows, p.a_cols, p.lda, BM);
   const CUtensorMap mb = B_MN ? make_map(p.B, p.b_rows, p.b_cols, p.ldb, BK) : make_map(p.B, p.b_rows, p.b_cols, p.ldb, BN);
+  // output map for the TMA-store epilogue (bf16 C of c_rows x N; otherwise an unused copy of A's)
+  CUtensorMap mc = ma;
+  if (a.c_mode == kStoreBf16 && BN % 64 == 0) {
+    if (a.c_rows <= 0) throw std::invalid_argument("bf16 GEMM output needs its row count");
+    mc = make_map(a.C, a.c_rows, a.N, a.ldc, 32);
+  }
   auto kern = gemm_kernel<BN, A_MN, B_MN>;
   static int attr_device = -1;
   int dev = 0;
@@ -474,7 +554,7 @@ void launch_t(const GemmProblem& p, const GemmArgs& a, dim3 grid, cudaStream_t s
     GB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes));
     attr_device = dev;
   }
-  kern<<<grid, kThreads, S::kBytes, stream>>>(ma, mb, a);
+  kern<<<grid, kThreads, S::kBytes, stream>>>(ma, mb, mc, a);
   GB_LAUNCH_CHECK();
 }
 

@@ -120,6 +120,7 @@ struct GemmArgs {
   const int32_t* n_rows_dev = nullptr;
   float* dbias = nullptr;              // cross-entropy epilogue: += column sums of the gradient
   int32_t* err = nullptr;
+  int64_t c_rows = 0;                  // rows of C (bf16 stores go through a TMA store of that extent)
 };
 void launch_gemm(const GemmProblem& p, GemmArgs a, int bn, cudaStream_t stream);
 

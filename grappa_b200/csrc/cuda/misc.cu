@@ -220,7 +220,10 @@ void launch_act_bwd(const ActBwdArgs& a, cudaStream_t stream) {
   const int rpb = std::max(1, 256 / chunks);
   const int threads = chunks * rpb;
   const int rows = a.cap_rows > 0 ? a.cap_rows : a.n;
-  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ceil_div(rows, rpb), int64_t(sm_count()) * 8)));
+  // with a bias gradient every block ends with one atomic per column: keep the grid
+  // at a few blocks per SM so that those atomics do not queue up on the same words
+  const int per_sm = a.dbias ? 3 : 8;
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ceil_div(rows, rpb), int64_t(sm_count()) * per_sm)));
   act_bwd_kernel<<<grid, threads, threads * 8 * sizeof(float), stream>>>(a, chunks);
   GB_LAUNCH_CHECK();
 }

@@ -35,7 +35,8 @@ namespace {
 constexpr int kThreads = 256;
 
 __device__ __forceinline__ void red_add_v4f(float* p, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+  // no "memory" clobber: dsrc is not read in the same launch (see aggregate_bwd_kernel)
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d));
 }
 
 __host__ __device__ __forceinline__ int next_pow2(int x) {
@@ -75,7 +76,40 @@ __global__ void __launch_bounds__(kThreads) aggregate_kernel(AggArgs a) {
       for (int j = 0; j < 8; ++j) acc[q][j] = 0.f;
     float wsum = 0.f;
     int e = beg + g;
-    // two edges per group per iteration for memory-level parallelism
+    // four, then two edges per group per iteration for memory-level parallelism
+    for (; e + 3 * groups < end; e += 4 * groups) {
+      int u[4];
+      float w[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        u[t] = a.indices[e + t * groups];
+        w[t] = 1.f;
+        if (a.mode == kAggWeighted) w[t] = a.edge_w[e + t * groups];
+      }
+      int64_t rr[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        rr[t] = a.src_map ? a.src_map[u[t]] : u[t];
+        if (a.mode == kAggGcn) w[t] = a.src_norm[u[t]];
+        wsum += w[t];
+      }
+#pragma unroll
+      for (int q = 0; q < CPL; ++q) {
+        const int c = sub + q * lpe;
+        if (c < chunks) {
+          uint4 x[4];
+#pragma unroll
+          for (int t = 0; t < 4; ++t) x[t] = *reinterpret_cast<const uint4*>(a.src + rr[t] * a.src_stride + c * 8);
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            float f[8];
+            bf16x8_to_f32(x[t], f);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[q][j] += w[t] * f[j];
+          }
+        }
+      }
+    }
     for (; e + groups < end; e += 2 * groups) {
       const int u0 = a.indices[e], u1 = a.indices[e + groups];
       const int64_t r0 = a.src_map ? a.src_map[u0] : u0;

@@ -312,9 +312,27 @@ class BlockEngine:
                      self.counters if p > 0 else None, salt, None, 0, None, None, None, None, None, None, self.err, bn)
 
     def _dw(self, A, B, M, N, K_cap, K_dev, gW):
-        """gW[M, N] += A^T B with A [K, M], B [K, N] (both MN-major), split-K over rows."""
+        """gW[M, N] += A^T B with A [K, M], B [K, N] (both MN-major), split-K over rows.
+        Runs on the auxiliary stream (forked here, joined before the optimizer step), so
+        the weight gradients overlap the input-gradient chain of the backward pass."""
         n_tiles = math.ceil(M / 128) * math.ceil(N / 256)
-        self._gemm(A, True, B, True, M, None, N, K_cap, K_dev, split_k(K_cap, n_tiles), gW, GEMM_ATOMIC_F32, bn=256)
+        main = torch.cuda.current_stream(self.device)
+        aux = self._aux_stream()
+        aux.wait_stream(main)
+        with torch.cuda.stream(aux):
+            self._gemm(A, True, B, True, M, None, N, K_cap, K_dev, split_k(K_cap, n_tiles), gW, GEMM_ATOMIC_F32,
+                       bn=256)
+        self._aux_used = True
+
+    def _aux_stream(self):
+        if getattr(self, "_aux", None) is None:
+            self._aux = torch.cuda.Stream(device=self.device)
+        return self._aux
+
+    def _join_aux(self):
+        if getattr(self, "_aux_used", False):
+            torch.cuda.current_stream(self.device).wait_stream(self._aux)
+            self._aux_used = False
 
     # ------------------------------------------------------------------ binding
     def bind_working(self, working, labels, gideg):
@@ -360,6 +378,7 @@ class BlockEngine:
         raise NotImplementedError
 
     def _update(self):
+        self._join_aux()
         cu = self.cu
         b1, b2 = self.betas
         if self.fused_allreduce:
@@ -505,6 +524,31 @@ class BlockEngine:
         self._forward(training=False)
         return self.istats[0:1], self.fstats[2:3]
 
+    def time_phases(self, seeds, counts, n_steps=None):
+        """Device time per phase of eager steps (CUDA events on the launching stream,
+        one synchronisation at the end): {'sample', 'forward', 'backward', 'update'} in
+        ms per step, averaged over the steps.  NVTX ranges mark the same phases."""
+        import torch.cuda.nvtx as nvtx
+
+        n = int(seeds.shape[0]) if n_steps is None else int(n_steps)
+        names = ("sample", "forward", "backward", "update")
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(n)]
+        self._select(0)
+        for s in range(n):
+            self.load_seeds(seeds[s % seeds.shape[0]], counts[s % counts.shape[0]])
+            self.cu.zero_(self.fstats)
+            self.cu.zero_(self.istats)
+            e = ev[s]
+            e[0].record()
+            for k, fn in enumerate((self._sample, lambda: self._forward(True), self._backward, self._update)):
+                nvtx.range_push(names[k])
+                fn()
+                nvtx.range_pop()
+                e[k + 1].record()
+            self.cu.step_end(self.counters)
+        torch.cuda.synchronize(self.device)
+        return {name: sum(ev[s][k].elapsed_time(ev[s][k + 1]) for s in range(n)) / n for k, name in enumerate(names)}
+
     def check_errors(self):
         e = int(self.err.item())
         if e:
@@ -599,10 +643,8 @@ class SageEngine(BlockEngine):
         for l in range(self.L - 1, -1, -1):
             s = self.lay[l]
             h = s["h"]
-            n_tiles = math.ceil(s["op"] / 128) * math.ceil(s["K"] / 256)
             # dW += dY^T X (split-K over the block's rows, fp32 reductions into the gradient)
-            self._gemm(s["dY"], True, s["X"], True, s["op"], None, s["K"], s["rows"], self._n_dst(h),
-                       split_k(s["rows"], n_tiles), s["gW"], GEMM_ATOMIC_F32, bn=256)
+            self._dw(s["dY"], s["X"], s["op"], s["K"], s["rows"], self._n_dst(h), s["gW"])
             if l == 0:
                 break
             # dX = dY W (W read MN-major)

@@ -1,0 +1,61 @@
+"""Profiling entry point: one mini-batch training step of a model inside an NVTX
+range named ``prof_step`` (after one eager warm-up step), for kernel captures such as
+
+    ncu --set full --clock-control none --nvtx --nvtx-include "prof_step/" \\
+        -o prof python -m grappa_b200.utils.profile_step --workload sage
+
+and, with ``--phases N``, the CUDA-event device time of each step phase (sample,
+forward, backward, update) averaged over N eager steps.  Workloads: 3-layer models
+on the ogbn-products-shaped synthetic graph (``--config`` picks another spec),
+1024 seeds per batch, one GPU.
+"""
+import argparse
+import json
+
+import torch
+
+from grappa_b200.dataset import synthetic as S
+from grappa_b200.graph_store import partition_from_global
+from grappa_b200.models import get_model
+from grappa_b200.trainer import MiniBatchTrainer
+
+WORKLOADS = {"sage": ("sage", 256, [15, 10, 5]), "gcn": ("gcn", 256, [15, 10, 5]), "gin": ("gin", 256, [15, 10, 5]),
+             "gat": ("gat", 64, [10, 10, 10]), "pinsage": ("pinsage", 256, [5, 5, 5])}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--workload", default="sage", choices=sorted(WORKLOADS))
+    ap.add_argument("--config", default="ogbpr")
+    ap.add_argument("--batch", type=int, default=1024)
+    ap.add_argument("--phases", type=int, default=0, help="time the phases of this many eager steps")
+    a = ap.parse_args()
+    name, hidden, fanouts = WORKLOADS[a.workload]
+    dev = torch.device("cuda", 0)
+    spec = S.SPECS[a.config]
+    g = S.build(spec, dev)
+    own = partition_from_global(g, 1, 0, dev, part_seed=spec.seed)
+    del g
+    torch.cuda.empty_cache()
+    torch.manual_seed(0)
+    model = get_model(name, spec.feat_dim, spec.n_classes, num_hidden=hidden, num_layers=3, dropout=0.5, n_heads=4)
+    tr = MiniBatchTrainer(model, own, fanouts, a.batch, comm=None, seed=3, use_cuda_graph=False)
+    eng = tr.engine
+    seeds, counts = tr.epoch_seeds(0, on_host=False)
+    eng.set_epoch(0)
+    eng.step(seeds[0], counts[0])
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("prof_step")
+    eng.step(seeds[1], counts[1])
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    eng.check_errors()
+    out = {"workload": a.workload, "launches_per_step": eng.launches_per_step, "block_counts": eng.sm.cnt.tolist()}
+    if a.phases:
+        out["phase_ms"] = eng.time_phases(seeds, counts, a.phases)
+    print(json.dumps(out))
+    tr.close()
+
+
+if __name__ == "__main__":
+    main()
