@@ -100,7 +100,11 @@ class MiniBatchTrainer:
 
     def train_epoch(self, epoch, host_feed=False):
         """Run one epoch.  With ``host_feed`` the seeds come from pinned host memory and
-        every step's loss is copied back; returns the mean loss then (else None)."""
+        every step's loss is copied back; returns the mean loss then (else None).
+        With a ``watchdog`` (grappa_b200.parallel.watchdog.Heartbeat) set, a peer that
+        left the job raises PeerFailure here, before any collective of the epoch."""
+        if getattr(self, "watchdog", None) is not None:
+            self.watchdog.check()
         self._maybe_repartition(epoch)
         if self._warm:
             self.engine.prepare()
