@@ -149,11 +149,15 @@ def main():
 
     spec = S.SPECS[args.config]
     t0 = time.time()
-    graph = S.build(spec, device)
-    own = partition_from_global(graph, world, rank, device, part_seed=spec.seed)
-    del graph
+    if spec.n_nodes >= S.LEAN_MIN_NODES:
+        own = S.build_partition(spec, world, rank, device)
+    else:
+        graph = S.build(spec, device)
+        own = partition_from_global(graph, world, rank, device, part_seed=spec.seed)
+        del graph
     torch.cuda.empty_cache()
     t_setup = time.time() - t0
+    own_gb = sum(t.numel() * t.element_size() for t in (own.indptr, own.indices, own.feat)) / 1e9
 
     torch.manual_seed(1234)
     model = get_model(wl["model"], spec.feat_dim, spec.n_classes, num_hidden=wl["hidden"], num_layers=3,
@@ -256,7 +260,7 @@ def main():
             "parallelism": f"partition-parallel x{world} (one hash partition per GPU; coverage-weighted gradient "
                            f"all-reduce{' + Adam fused over NVLink peer memory' if world > 1 and not args.no_fused_ar else ''})",
             "repart_every": wl["repart"],
-            "l2": "inputs larger than L2 (feature table and CSR about 1 GB per GPU); no flush",
+            "l2": f"inputs larger than L2 (feature table and CSR {own_gb:.1f} GB on GPU 0); no flush",
             "step": "one benchmark step = one epoch",
             "setup_s": round(t_setup, 2),
         },

@@ -311,6 +311,14 @@ void normal_fill(Tensor out, int64_t seed) {
   d::launch_normal_fill(ptr<float>(out, at::kFloat, "out"), out.numel(), static_cast<uint64_t>(seed), stream());
 }
 
+void normal_rows(Tensor out, int64_t row0, int64_t d, int64_t seed) {
+  c10::cuda::CUDAGuard g(out.device());
+  TORCH_CHECK(out.dim() == 2 && out.size(1) >= d, "normal_rows: out must be [rows, >= d]");
+  d::launch_normal_rows_bf16(reinterpret_cast<__nv_bfloat16*>(ptr2d<at::BFloat16>(out, at::kBFloat16, "out")),
+                             out.stride(0), row0, out.size(0), static_cast<int>(d), static_cast<uint64_t>(seed),
+                             stream());
+}
+
 void dropout_mask(Tensor mask, int64_t ld, double p, Tensor counters, int64_t salt) {
   c10::cuda::CUDAGuard g(mask.device());
   d::launch_dropout_mask(ptr<uint8_t>(mask, at::kByte, "mask"), mask.size(0), mask.size(1), ld, static_cast<float>(p),
@@ -822,6 +830,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmat_candidates", &rmat_candidates);
   m.def("shuffle_keys", &shuffle_keys);
   m.def("normal_fill", &normal_fill);
+  m.def("normal_rows", &normal_rows);
   m.def("dropout_mask", &dropout_mask);
   m.def("adam", &adam);
   m.def("zero_", &zero_);

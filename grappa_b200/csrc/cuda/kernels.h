@@ -218,6 +218,8 @@ void launch_rmat_candidates(int64_t n, int scale, double a, double b, double c, 
 void launch_shuffle_keys(const int64_t* ids, int64_t n, uint64_t seed, uint64_t epoch, int64_t* keys,
                          cudaStream_t stream);
 void launch_normal_fill(float* out, int64_t n, uint64_t seed, cudaStream_t stream);
+void launch_normal_rows_bf16(__nv_bfloat16* out, int64_t ld, int64_t row0, int64_t rows, int d, uint64_t seed,
+                             cudaStream_t stream);
 void launch_dropout_mask(uint8_t* mask, int64_t rows, int64_t cols, int64_t ld, float p, const int64_t* counters,
                          uint32_t salt, cudaStream_t stream);
 

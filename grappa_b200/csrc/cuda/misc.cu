@@ -155,6 +155,31 @@ __global__ void normal_kernel(float* out, int64_t n, uint64_t key) {
   }
 }
 
+// Rows [row0, row0 + rows) of the [*, d] matrix whose flat element i is the normal
+// value of index i (the stream of normal_kernel), as bf16 rows of stride ld (columns
+// past d zeroed).  d is even, so a Box-Muller pair never straddles two rows.
+__global__ void normal_rows_kernel(__nv_bfloat16* out, int64_t ld, int64_t row0, int64_t rows, int d,
+                                   uint64_t key) {
+  const int64_t pairs_per_row = d / 2;
+  const int64_t total = rows * pairs_per_row;
+  for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = t / pairs_per_row;
+    const int c = static_cast<int>(t % pairs_per_row) * 2;
+    const uint64_t pair = static_cast<uint64_t>(((row0 + r) * d + c) >> 1);
+    const U4 q = index_draw4(key, pair, 7u);
+    const float u1 = (static_cast<float>(q.x >> 8) + 0.5f) * (1.0f / 16777216.0f);
+    const float u2 = static_cast<float>(q.y >> 8) * (1.0f / 16777216.0f);
+    const float rad = sqrtf(-2.0f * logf(u1));
+    float sn, cs;
+    sincospif(2.0f * u2, &sn, &cs);
+    __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(out + r * ld + c);
+    *o = __floats2bfloat162_rn(rad * cs, rad * sn);
+    if (c + 2 == d)
+      for (int64_t z = d; z < ld; ++z) out[r * ld + z] = __float2bfloat16_rn(0.f);
+  }
+}
+
 __global__ void dropout_mask_kernel(uint8_t* mask, int64_t rows, int64_t cols, int64_t ld, uint32_t thr,
                                     const int64_t* counters, uint32_t salt) {
   const uint64_t key = hop_key(static_cast<uint64_t>(counters[0]) ^ 0xD80Full, static_cast<uint64_t>(counters[1]),
@@ -270,6 +295,14 @@ void launch_shuffle_keys(const int64_t* ids, int64_t n, uint64_t seed, uint64_t 
 
 void launch_normal_fill(float* out, int64_t n, uint64_t seed, cudaStream_t stream) {
   normal_kernel<<<grid_1d((n + 1) / 2, 256, 32), 256, 0, stream>>>(out, n, mix64(seed ^ 0x4E4F524Dull));
+  GB_LAUNCH_CHECK();
+}
+
+void launch_normal_rows_bf16(__nv_bfloat16* out, int64_t ld, int64_t row0, int64_t rows, int d, uint64_t seed,
+                             cudaStream_t stream) {
+  if (d % 2 != 0) throw std::invalid_argument("normal_rows: d must be even");
+  normal_rows_kernel<<<grid_1d(rows * (d / 2), 256, 32), 256, 0, stream>>>(out, ld, row0, rows, d,
+                                                                          mix64(seed ^ 0x4E4F524Dull));
   GB_LAUNCH_CHECK();
 }
 

@@ -231,3 +231,181 @@ def to_t10n_layout(graph, out_dir):
     with open(os.path.join(out_dir, "t10n.json"), "w") as f:
         json.dump(cfg, f, indent=1)
     return cfg
+
+
+# ---------------------------------------------------------------------------------------
+# Memory-lean build of one rank's partition (graphs of 10^8 nodes / 10^9 edges).
+#
+# ``build`` keeps fp32 features and both edge directions as int64 (about 170 GB for the
+# ogbn-papers100M shape); this path never holds more than the CSC, the bf16 features and
+# two [n, hidden] teacher buffers:
+#   * the undirected RMAT edges are turned straight into a CSC by destination (with one
+#     self-loop per node), sources ascending per row -- the same graph as ``build``;
+#   * features are generated row-wise in bf16 from the same N(0,1) stream (element i of
+#     the flattened [n, d] matrix is the same Philox draw as in ``build``);
+#   * the 2-hop mean teacher runs in bf16 with the mean-aggregation kernel, using
+#     A (A X W1) W2 = (A (A X W1)) W2 to keep the widest buffer at the hidden width;
+#   * partitions are contiguous ranges of the (already hash-permuted) node ids, a
+#     balanced random hash partition that needs no relabelling: rank r owns
+#     [r n / W, (r + 1) n / W), and its in-edge CSR is a slice of the global CSC.
+# ---------------------------------------------------------------------------------------
+def lean_prefix(n, world):
+    return [r * n // world for r in range(world + 1)]
+
+
+def _csc_with_loops(spec, device):
+    n = spec.n_nodes
+    keys = rmat_undirected(spec, device)
+    perm = node_permutation(n, spec.seed, device)
+    m = keys.numel()
+    # directed edges (src, dst) of both directions plus the loops, keyed dst * n + src
+    dkey = torch.empty(2 * m + n, dtype=torch.int64, device=device)
+    step = 1 << 27
+    for s in range(0, m, step):
+        k = keys[s:s + step]
+        a = perm[k // n]
+        b = perm[k % n]
+        dkey[s:s + k.numel()] = b * n + a
+        dkey[m + s:m + s + k.numel()] = a * n + b
+        del k, a, b
+    del keys, perm
+    ids = torch.arange(n, dtype=torch.int64, device=device)
+    dkey[2 * m:] = ids * (n + 1)
+    del ids
+    dkey, _ = torch.sort(dkey)
+    indices = torch.empty(dkey.numel(), dtype=torch.int32, device=device)
+    deg = torch.zeros(n, dtype=torch.int64, device=device)
+    for s in range(0, dkey.numel(), step):
+        k = dkey[s:s + step]
+        indices[s:s + k.numel()] = (k % n).to(torch.int32)
+        deg += torch.bincount(k // n, minlength=n)
+        del k
+    del dkey
+    indptr = torch.zeros(n + 1, dtype=torch.int64, device=device)
+    indptr[1:] = torch.cumsum(deg, 0)
+    return indptr, indices
+
+
+def normal_rows(n_rows, row0, d, ld, seed, device):
+    """Rows [row0, row0 + n_rows) of the [*, d] N(0,1) matrix of ``normal(. * d, seed)`` as
+    bf16 rows of width ld (columns past d are zero)."""
+    device = torch.device(device)
+    out = torch.zeros((n_rows, ld), dtype=torch.bfloat16, device=device)
+    if n_rows == 0:
+        return out
+    if device.type == "cuda":
+        _native.cuda().normal_rows(out, int(row0), int(d), int(seed))
+        return out
+    flat = torch.from_numpy(_native.host().normal((row0 + n_rows) * d, int(seed)))
+    out[:, :d] = flat[row0 * d:].view(n_rows, d).to(torch.bfloat16)
+    return out
+
+
+def _mean_agg_bf16(indptr, indices, h, out, max_edges=1 << 30):
+    """out[v] = mean_{u in in(v)} h[u] (bf16 rows, dst-chunked so that edge offsets fit in int32)."""
+    n = indptr.numel() - 1
+    dim = h.shape[1]
+    if h.is_cuda:
+        cu = _native.cuda()
+        err = torch.zeros(1, dtype=torch.int32, device=h.device)
+        ip = indptr.cpu()
+        s = 0
+        while s < n:
+            e = int(torch.searchsorted(ip, ip[s] + max_edges, right=True)) - 1
+            e = max(s + 1, min(n, e))
+            e0, e1 = int(ip[s]), int(ip[e])
+            local = (indptr[s:e + 1] - e0).to(torch.int32)
+            cu.aggregate(local, indices[e0:e1], None, e - s, e - s, h, None, dim, 0, None, None, None, out[s:e], 0,
+                         -1, 0.0, 0, err, None, 0, 0.0, None, 0)
+            s = e
+        torch.cuda.synchronize(h.device)
+        if int(err.item()):
+            raise RuntimeError(f"aggregation error word {int(err.item()):#x} in the teacher")
+        return out
+    res = _mean_agg(indptr, indices, h.float())
+    out.copy_(res.to(out.dtype))
+    return out
+
+
+def _teacher_labels(spec, indptr, indices, feat, device, row_chunk=1 << 22):
+    n, d = spec.n_nodes, spec.feat_dim
+    g = torch.Generator(device="cpu").manual_seed(spec.seed ^ 0x7EAC)
+    w1 = (torch.randn(d, spec.teacher_hidden, generator=g) / math.sqrt(d)).to(device)
+    w2 = (torch.randn(spec.teacher_hidden, spec.n_classes, generator=g) / math.sqrt(spec.teacher_hidden)).to(device)
+    hid = spec.teacher_hidden
+    z = torch.zeros((n, hid), dtype=torch.bfloat16, device=device)
+    for s in range(0, n, row_chunk):
+        z[s:s + row_chunk] = (feat[s:s + row_chunk, :d].float() @ w1).to(torch.bfloat16)
+    h1 = torch.zeros_like(z)
+    _mean_agg_bf16(indptr, indices, z, h1)
+    h1.relu_()
+    _mean_agg_bf16(indptr, indices, h1, z)  # z <- A relu(A X W1)
+    del h1
+    s1 = torch.zeros(spec.n_classes, dtype=torch.float64, device=device)
+    s2 = torch.zeros_like(s1)
+    for s in range(0, n, row_chunk):
+        lg = z[s:s + row_chunk].float() @ w2
+        s1 += lg.sum(0, dtype=torch.float64)
+        s2 += (lg.double() ** 2).sum(0)
+    mean = s1 / n
+    std = ((s2 - n * mean ** 2) / max(1, n - 1)).clamp(min=0).sqrt().clamp(min=1e-6)
+    label = torch.empty(n, dtype=torch.int32, device=device)
+    for s in range(0, n, row_chunk):
+        lg = z[s:s + row_chunk].float() @ w2
+        label[s:s + row_chunk] = torch.argmax((lg - mean.float()) / std.float(), dim=1).to(torch.int32)
+    return label
+
+
+def _split_masks(spec, lo, hi, device):
+    n = spec.n_nodes
+    order = torch.argsort(shuffle_keys(torch.arange(n, dtype=torch.int64, device=device), spec.seed ^ 0x5B1, 0))
+    n_tr = int(round(spec.train_frac * n))
+    n_va = int(round(spec.val_frac * n))
+    split = torch.empty(n, dtype=torch.int8, device=device)  # 0 train, 1 val, 2 test
+    split[order[:n_tr]] = 0
+    split[order[n_tr:n_tr + n_va]] = 1
+    split[order[n_tr + n_va:]] = 2
+    del order
+    own = split[lo:hi]
+    return [(own == k).to(torch.int8) for k in range(3)]
+
+
+def build_partition(spec, world, rank, device):
+    """Rank ``rank``'s OwnPartition of ``spec``'s graph, built without the global fp32
+    arrays of ``build`` (see the notes above).  Every rank builds the global CSC and the
+    teacher on its own device and keeps its slice."""
+    from grappa_b200.graph_store import OwnPartition
+    from grappa_b200.models.flat import pad8
+
+    if isinstance(spec, str):
+        spec = SPECS[spec]
+    device = torch.device(device)
+    n, d = spec.n_nodes, spec.feat_dim
+    prefix = lean_prefix(n, world)
+    lo, hi = prefix[rank], prefix[rank + 1]
+    indptr, indices = _csc_with_loops(spec, device)
+    feat = normal_rows(n, 0, d, pad8(d), spec.seed ^ 0xFEA7, device)
+    label = _teacher_labels(spec, indptr, indices, feat, device)
+    gideg = (indptr[1:] - indptr[:-1] - 1)[lo:hi].clone()
+    if world > 1:
+        e0, e1 = int(indptr[lo]), int(indptr[hi])
+        own_indptr = indptr[lo:hi + 1] - e0
+        own_indices = indices[e0:e1].clone()
+        del indptr, indices
+        own_feat = feat[lo:hi].clone()
+        del feat
+        label = label[lo:hi].clone()
+    else:
+        own_indptr, own_indices, own_feat = indptr, indices, feat
+    tr, va, te = _split_masks(spec, lo, hi, device)
+    ext = own_indices[(own_indices < lo) | (own_indices >= hi)]
+    ext_src = torch.unique(ext).to(torch.int32)
+    del ext
+    if device.type == "cuda":
+        torch.cuda.empty_cache()
+    return OwnPartition(rank, world, prefix, own_indptr, own_indices, own_feat, label, tr, va, te, gideg, ext_src,
+                        feat_dim=d)
+
+
+# graphs above this size are built per partition by ``build_partition``
+LEAN_MIN_NODES = 20_000_000
