@@ -763,6 +763,47 @@ void gat_bwd(Tensor indptr, Tensor indices, OptT n_dst_dev, int64_t cap_dst, Opt
   d::launch_gat_bwd(a, stream());
 }
 
+void gat_bwd_input(Tensor indptr, Tensor indices, OptT n_dst_dev, int64_t cap_dst, OptT n_src_dev, int64_t cap_src,
+                   int64_t heads, int64_t feat, Tensor z, Tensor attn_l, Tensor attn_r, Tensor el, Tensor er,
+                   Tensor smax, Tensor ssum, double slope, Tensor dout, Tensor edge_scratch, Tensor del, Tensor der,
+                   OptT dbias, OptT dattn_l, OptT dattn_r, Tensor x, int64_t in_dim, Tensor y, Tensor xl, Tensor xr,
+                   Tensor err) {
+  c10::cuda::CUDAGuard g(z.device());
+  auto a = gat_args(indptr, indices, n_dst_dev, cap_dst, n_src_dev, cap_src, heads, feat, z, attn_l, attn_r, el, er,
+                    smax, ssum, slope);
+  a.dout = reinterpret_cast<const __nv_bfloat16*>(ptr2d<at::BFloat16>(dout, at::kBFloat16, "dout"));
+  a.lddo = dout.stride(0);
+  a.edge_scratch = ptr<float>(edge_scratch, at::kFloat, "edge_scratch");
+  a.del = ptr<float>(del, at::kFloat, "del");
+  a.der = ptr<float>(der, at::kFloat, "der");
+  a.dbias = dbias.has_value() ? dbias->data_ptr<float>() : nullptr;
+  a.dattn_l = dattn_l.has_value() ? dattn_l->data_ptr<float>() : nullptr;
+  a.dattn_r = dattn_r.has_value() ? dattn_r->data_ptr<float>() : nullptr;
+  a.x = reinterpret_cast<const __nv_bfloat16*>(ptr2d<at::BFloat16>(x, at::kBFloat16, "x"));
+  a.ldx = x.stride(0);
+  a.in_dim = static_cast<int32_t>(in_dim);
+  a.y = reinterpret_cast<__nv_bfloat16*>(ptr2d<at::BFloat16>(y, at::kBFloat16, "y"));
+  a.ldy = y.stride(0);
+  a.xl = ptr<float>(xl, at::kFloat, "xl");
+  a.xr = ptr<float>(xr, at::kFloat, "xr");
+  a.err = ptr<int32_t>(err, at::kInt, "err");
+  TORCH_CHECK(edge_scratch.numel() >= static_cast<int64_t>(indices.numel()) * heads, "gat: edge scratch too small");
+  TORCH_CHECK(x.size(0) >= cap_src && x.size(1) >= in_dim, "gat: x too small");
+  TORCH_CHECK(y.size(0) >= cap_dst && y.size(1) >= heads * in_dim, "gat: y too small");
+  TORCH_CHECK(xl.numel() >= heads * in_dim && xr.numel() >= heads * in_dim, "gat: xl / xr too small");
+  d::launch_gat_bwd_input(a, stream());
+}
+
+void gat_dw_combine(Tensor T, Tensor xl, Tensor xr, Tensor attn_l, Tensor attn_r, int64_t heads, int64_t feat,
+                    int64_t in_dim, Tensor dw) {
+  c10::cuda::CUDAGuard g(T.device());
+  TORCH_CHECK(T.size(0) >= heads * feat && T.size(1) >= heads * in_dim, "gat_dw_combine: T too small");
+  TORCH_CHECK(dw.size(0) >= heads * feat && dw.size(1) >= in_dim, "gat_dw_combine: dw too small");
+  d::launch_gat_dw_combine(ptr2d<float>(T, at::kFloat, "T"), T.stride(0), ptr<float>(xl, at::kFloat, "xl"),
+                           ptr<float>(xr, at::kFloat, "xr"), attn_l.data_ptr<float>(), attn_r.data_ptr<float>(),
+                           static_cast<int>(heads), static_cast<int>(feat), static_cast<int>(in_dim),
+                           ptr2d<float>(dw, at::kFloat, "dw"), dw.stride(0), stream());
+}
 
 void walk_hop(Tensor indptr, Tensor indices, Tensor dst_nid, OptT n_dst_dev, int64_t n_dst, int64_t length,
               double restart_prob, int64_t num_walks, int64_t num_neighbors, Tensor counters, int64_t hop,
@@ -822,6 +863,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gat_scores", &gat_scores);
   m.def("gat_fwd", &gat_fwd);
   m.def("gat_bwd", &gat_bwd);
+  m.def("gat_bwd_input", &gat_bwd_input);
+  m.def("gat_dw_combine", &gat_dw_combine);
   m.def("aggregate_bwd", &aggregate_bwd);
   m.def("src_norm", &src_norm);
   m.def("act_bwd", &act_bwd);

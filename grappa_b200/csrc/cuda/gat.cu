@@ -23,6 +23,15 @@
 //   del[u,h] += de, der[v,h] += de, dz_u[h] += a_uvh dout_v[h]   (fp32 reductions)
 //   dz_u[h] += del[u,h] a_l[h] + der[u,h] a_r[h];  da_l += del z;  da_r += der z
 // dz is staged to bf16 for the dW / dX GEMMs and the fp32 accumulators are cleared.
+//
+// Input layer (no dX wanted): dz is only needed for dW = dz^T x, and
+//   dW[hF+f, k] = sum_v dout_v[hF+f] y_v[h, k] + a_l[hF+f] xl[h, k] + a_r[hF+f] xr[h, k]
+// with y_v[h] = sum_u a_uvh x_u (an attention-weighted sum of the layer's INPUT rows,
+// per destination), xl[h] = sum_u del[u,h] x_u and xr[h] = sum_{u<n_dst} der[u,h] x_u.
+// The edge kernel then writes y (n_dst rows of H * in) instead of scattering the
+// H*F-wide dz over the sources with fp32 reductions, the node kernel reduces xl/xr,
+// a GEMM forms dout^T y and gat_dw_combine adds its diagonal head blocks and the two
+// rank-1 terms into dW.
 #include <algorithm>
 
 #include "common.cuh"
@@ -63,9 +72,16 @@ __device__ __forceinline__ float leaky(float x, float s) { return x > 0.f ? x : 
 // same in every warp) over the block's warps in shared memory, then one atomic per
 // column per block: the column gradients (bias, attention vectors) would otherwise
 // take one contended atomic per warp and column.  Called by every thread.
+// One shared scratch per kernel for every block_col_atomic instantiation (a static
+// __shared__ array inside the template would be allocated once per instantiation).
+__device__ __forceinline__ float (*col_scratch())[1024] {
+  __shared__ float s[kThreads / 32][1024];
+  return s;
+}
+
 template <int CPL>
 __device__ void block_col_atomic(const float (&v)[CPL][8], float* dst, int HF) {
-  __shared__ float s[kThreads / 32][1024];
+  float (*s)[1024] = col_scratch();
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
 #pragma unroll
   for (int q = 0; q < CPL; ++q)
@@ -285,13 +301,113 @@ __global__ void __launch_bounds__(kThreads) gat_fwd_kernel(GatArgs a) {
 }
 
 // ------------------------------------------------------------------ backward, per destination
-template <int CPL>
-__global__ void __launch_bounds__(kThreads) gat_bwd_edge_kernel(GatArgs a) {
+// SEG: every 8-column chunk lies in one head and a head spans a power-of-two group of
+// lanes (F a power of two in [8, 256]): the per-head dot products of an edge are then
+// a butterfly inside each lane group (log2(F / 8) shuffles) instead of H full warp
+// reductions, and no per-element head arithmetic is needed.  Otherwise the generic
+// path handles chunks that straddle two heads.
+struct HeadMap {
+  int h0[4];      // head of chunk q (CPL <= 4)
+  int lph;        // lanes per head (SEG)
+  int src_q, src_lane;  // lane h (< H): chunk and lane where the sum of head h ends up
+};
+
+template <int CPL, bool SEG>
+__device__ __forceinline__ HeadMap head_map(int lane, int H, int F) {
+  HeadMap m;
+#pragma unroll
+  for (int q = 0; q < CPL; ++q) m.h0[q] = min((lane + 32 * q) * 8 / F, H - 1);
+  m.lph = SEG ? F / 8 : 32;
+  const int chunk = SEG ? lane * (F / 8) : 0;  // first chunk of head `lane`
+  m.src_q = chunk / 32;
+  m.src_lane = chunk % 32;
+  return m;
+}
+
+// da of one edge for head `lane` (lanes >= H get 0): sum over the head's columns of
+// go * z, z given as the lane's bf16 chunks.
+template <int CPL, bool SEG>
+__device__ __forceinline__ float edge_head_dot(const float (&go)[CPL][8], const uint4 (&zv)[CPL], const HeadMap& m,
+                                               int lane, int H, int F, int HF) {
+  if constexpr (SEG) {
+    float part[CPL];
+#pragma unroll
+    for (int q = 0; q < CPL; ++q) {
+      float f[8];
+      bf16x8_to_f32(zv[q], f);
+      float t = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) t = fmaf(go[q][j], f[j], t);
+      part[q] = t;
+    }
+    for (int off = 1; off < m.lph; off <<= 1)
+#pragma unroll
+      for (int q = 0; q < CPL; ++q) part[q] += __shfl_xor_sync(0xffffffffu, part[q], off);
+    float da = 0.f;
+#pragma unroll
+    for (int q = 0; q < CPL; ++q) {
+      const float t = __shfl_sync(0xffffffffu, part[q], m.src_lane);
+      if (q == m.src_q) da = t;
+    }
+    return lane < H ? da : 0.f;
+  } else {
+    float p[kMaxHeads];
+#pragma unroll
+    for (int h = 0; h < kMaxHeads; ++h) p[h] = 0.f;
+#pragma unroll
+    for (int q = 0; q < CPL; ++q) {
+      const int c0 = (lane + 32 * q) * 8;
+      if (c0 >= HF) continue;
+      float f[8];
+      bf16x8_to_f32(zv[q], f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int h = (c0 + j) / F;
+        const float t = go[q][j] * f[j];
+#pragma unroll
+        for (int hh = 0; hh < kMaxHeads; ++hh)
+          if (hh == h) p[hh] += t;
+      }
+    }
+    float da_mine = 0.f;
+#pragma unroll
+    for (int h = 0; h < kMaxHeads; ++h) {
+      if (h >= H) break;
+      const float t = warp_sum(p[h]);
+      if (lane == h) da_mine = t;
+    }
+    return da_mine;
+  }
+}
+
+// resident blocks per SM the edge kernel is compiled for: two (128 registers: four
+// edges' rows in flight per warp), one for wide heads x features
+template <int CPL, int CPLY>
+constexpr int bwd_min_blocks() { return CPL + CPLY <= 3 ? 2 : 1; }
+
+template <int CPL, int CPLY, bool SEG>
+__global__ void __launch_bounds__(kThreads, bwd_min_blocks<CPL, CPLY>()) gat_bwd_edge_kernel(GatArgs a) {
   const int n_dst = a.n_dst_ptr ? min(*a.n_dst_ptr, a.cap_dst) : a.cap_dst;
   const int H = a.heads, F = a.feat, HF = H * F;
+  const int IN = a.in_dim, HIN = H * a.in_dim;  // input-layer mode (CPLY > 0)
   const int lane = threadIdx.x & 31;
   const int warps_total = (gridDim.x * kThreads) >> 5;
   const float inv_h = a.mean_heads ? 1.f / static_cast<float>(H) : 1.f;
+  const HeadMap hm = head_map<CPL, SEG>(lane, H, F);
+  constexpr int NY = CPLY > 0 ? CPLY : 1;
+  constexpr int EU = CPL == 1 && NY <= 2 ? 4 : 2;  // edges per pass-A iteration
+  int hy[NY], ky[NY];  // head and input column of the lane's y chunks
+#pragma unroll
+  for (int q = 0; q < NY; ++q) {
+    const int c0 = (lane + 32 * q) * 8;
+    hy[q] = CPLY > 0 ? min(c0 / max(IN, 1), H - 1) : 0;
+    ky[q] = c0 - hy[q] * IN;
+  }
+  float y[NY][8];
+#pragma unroll
+  for (int q = 0; q < NY; ++q)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) y[q][j] = 0.f;
   float bsum[CPL][8];
 #pragma unroll
   for (int q = 0; q < CPL; ++q)
@@ -300,22 +416,28 @@ __global__ void __launch_bounds__(kThreads) gat_bwd_edge_kernel(GatArgs a) {
   for (int v = (blockIdx.x * kThreads + threadIdx.x) >> 5; v < n_dst; v += warps_total) {
     const int beg = a.indptr[v], end = a.indptr[v + 1];
     float go[CPL][8];
-    int h0[CPL];
 #pragma unroll
     for (int q = 0; q < CPL; ++q) {
       const int c0 = (lane + 32 * q) * 8;
-      h0[q] = min(c0 / F, H - 1);
+      if (!a.mean_heads && c0 + 8 <= HF) {
+        float t[8];
+        bf16x8_to_f32(*reinterpret_cast<const uint4*>(a.dout + static_cast<int64_t>(v) * a.lddo + c0), t);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int c = c0 + j;
-        float g = 0.f;
-        if (c < HF) {
-          const int col = a.mean_heads ? c % F : c;
-          g = __bfloat162float(a.dout[static_cast<int64_t>(v) * a.lddo + col]) * inv_h;
+        for (int j = 0; j < 8; ++j) go[q][j] = t[j];
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int c = c0 + j;
+          float g = 0.f;
+          if (c < HF) {
+            const int col = a.mean_heads ? c % F : c;
+            g = __bfloat162float(a.dout[static_cast<int64_t>(v) * a.lddo + col]) * inv_h;
+          }
+          go[q][j] = g;
         }
-        go[q][j] = g;
-        bsum[q][j] += g;
       }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) bsum[q][j] += go[q][j];
     }
     float m = 0.f, s = 1.f, er_h = 0.f;
     if (lane < H) {
@@ -323,163 +445,344 @@ __global__ void __launch_bounds__(kThreads) gat_bwd_edge_kernel(GatArgs a) {
       s = a.ssum[static_cast<int64_t>(v) * H + lane];
       er_h = a.er[static_cast<int64_t>(v) * H + lane];
     }
-    // pass A: da per edge and head, S_h = sum a da
+    const float inv_s = 1.f / s;
+    // The in-edges are taken 32 at a time: one coalesced load of their source ids,
+    // broadcast by shuffles, so no row load waits behind an index load.
+    // pass A: da per edge and head, S_h = sum a da, EU edges per iteration with all
+    // their row loads issued together; in input-layer mode also y_v = sum a x_u
     float S = 0.f;
-    for (int e = beg; e < end; ++e) {
-      const int u = a.indices[e];
-      float p[kMaxHeads];
+    for (int cb = beg; cb < end; cb += 32) {
+      const int cnt = min(32, end - cb);
+      const int my_idx = lane < cnt ? a.indices[cb + lane] : 0;
+      for (int k = 0; k < cnt; k += EU) {
+        int uu[EU];
+        float elv[EU];
+        uint4 zv[EU][CPL];
 #pragma unroll
-      for (int h = 0; h < kMaxHeads; ++h) p[h] = 0.f;
+        for (int t = 0; t < EU; ++t) {
+          uu[t] = __shfl_sync(0xffffffffu, my_idx, min(k + t, 31));
+          const bool ok = k + t < cnt;
+          elv[t] = 0.f;
+          if (ok && lane < H) elv[t] = a.el[static_cast<int64_t>(uu[t]) * H + lane];
 #pragma unroll
-      for (int q = 0; q < CPL; ++q) {
-        const int c0 = (lane + 32 * q) * 8;
-        if (c0 >= HF) continue;
-        float f[8];
-        bf16x8_to_f32(*reinterpret_cast<const uint4*>(a.z + static_cast<int64_t>(u) * a.ldz + c0), f);
+          for (int q = 0; q < CPL; ++q) {
+            const int c0 = (lane + 32 * q) * 8;
+            zv[t][q] = make_uint4(0, 0, 0, 0);
+            if (ok && c0 < HF) zv[t][q] = *reinterpret_cast<const uint4*>(a.z + static_cast<int64_t>(uu[t]) * a.ldz + c0);
+          }
+        }
+        uint4 xv[CPLY > 0 ? EU : 1][NY];
+        if constexpr (CPLY > 0) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int h = (c0 + j) / F;
-          const float t = go[q][j] * f[j];
+          for (int t = 0; t < EU; ++t)
 #pragma unroll
-          for (int hh = 0; hh < kMaxHeads; ++hh)
-            if (hh == h) p[hh] += t;
+            for (int q = 0; q < CPLY; ++q) {
+              const int c0 = (lane + 32 * q) * 8;
+              xv[t][q] = make_uint4(0, 0, 0, 0);
+              if (k + t < cnt && c0 < HIN)
+                xv[t][q] = *reinterpret_cast<const uint4*>(a.x + static_cast<int64_t>(uu[t]) * a.ldx + ky[q]);
+            }
+        }
+        float alv[EU];
+#pragma unroll
+        for (int t = 0; t < EU; ++t) {
+          const float da = edge_head_dot<CPL, SEG>(go, zv[t], hm, lane, H, F, HF);
+          alv[t] = 0.f;
+          if (lane < H && k + t < cnt) {
+            alv[t] = __expf(leaky(elv[t] + er_h, a.slope) - m) * inv_s;
+            a.edge_scratch[static_cast<int64_t>(cb + k + t) * H + lane] = da;
+            S += alv[t] * da;
+          }
+        }
+        if constexpr (CPLY > 0) {
+          // y_v[h, k] += a_uvh x_u[k]; an 8-column chunk of the [H, IN] row lies in one head
+#pragma unroll
+          for (int q = 0; q < CPLY; ++q) {
+            const int c0 = (lane + 32 * q) * 8;
+            float at[EU];
+#pragma unroll
+            for (int t = 0; t < EU; ++t) at[t] = __shfl_sync(0xffffffffu, alv[t], hy[q]);
+            if (c0 >= HIN) continue;
+#pragma unroll
+            for (int t = 0; t < EU; ++t) {
+              float f[8];
+              bf16x8_to_f32(xv[t][q], f);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) y[q][j] = fmaf(at[t], f[j], y[q][j]);
+            }
+          }
         }
       }
-      float da_mine = 0.f;
-#pragma unroll
-      for (int h = 0; h < kMaxHeads; ++h) {
-        if (h >= H) break;
-        const float t = warp_sum(p[h]);
-        if (lane == h) da_mine = t;
-      }
-      if (lane < H) {
-        const float x = leaky(a.el[static_cast<int64_t>(u) * H + lane] + er_h, a.slope);
-        const float al = __expf(x - m) / s;
-        a.edge_scratch[static_cast<int64_t>(e) * H + lane] = da_mine;
-        S += al * da_mine;
-      }
     }
-    // pass B: score gradients and the transposed weighted sum
+    // pass B: score gradients and (dz mode) the transposed weighted sum.  Lane l
+    // fetches the el row and the pass-A da values of edge l of the chunk (one round
+    // trip for up to 32 edges); lane h takes those of head h by shuffles.
     float der_acc = 0.f;
-    for (int e = beg; e < end; ++e) {
-      const int u = a.indices[e];
-      float al = 0.f;
-      if (lane < H) {
-        const float x = leaky(a.el[static_cast<int64_t>(u) * H + lane] + er_h, a.slope);
-        al = __expf(x - m) / s;
-        const float de = al * (a.edge_scratch[static_cast<int64_t>(e) * H + lane] - S);
-        const float dx = x > 0.f ? de : de * a.slope;
-        atomicAdd(a.del + static_cast<int64_t>(u) * H + lane, dx);
-        der_acc += dx;
-      }
+    for (int cb = beg; cb < end; cb += 32) {
+      const int cnt = min(32, end - cb);
+      const int my_idx = lane < cnt ? a.indices[cb + lane] : 0;
+      float elc[kMaxHeads], dac[kMaxHeads];
 #pragma unroll
-      for (int q = 0; q < CPL; ++q) {
-        const int c0 = (lane + 32 * q) * 8;
-        const float a0 = __shfl_sync(0xffffffffu, al, h0[q]);
-        const float a1 = __shfl_sync(0xffffffffu, al, min(h0[q] + 1, H - 1));
-        if (c0 >= HF) continue;
-        float t[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) t[j] = ((c0 + j) / F == h0[q] ? a0 : a1) * go[q][j];
-        float* d = a.dz + static_cast<int64_t>(u) * a.lddz + c0;
-        if (c0 + 8 <= HF) {
-          red_add_v4f(d, t[0], t[1], t[2], t[3]);
-          red_add_v4f(d + 4, t[4], t[5], t[6], t[7]);
+      for (int h = 0; h < kMaxHeads; ++h) elc[h] = dac[h] = 0.f;
+      if (lane < cnt) {
+        if (H == 4) {
+          const float4 e4 = *reinterpret_cast<const float4*>(a.el + static_cast<int64_t>(my_idx) * 4);
+          const float4 d4 = *reinterpret_cast<const float4*>(a.edge_scratch + static_cast<int64_t>(cb + lane) * 4);
+          elc[0] = e4.x; elc[1] = e4.y; elc[2] = e4.z; elc[3] = e4.w;
+          dac[0] = d4.x; dac[1] = d4.y; dac[2] = d4.z; dac[3] = d4.w;
         } else {
-          for (int j = 0; j < 8 && c0 + j < HF; ++j) atomicAdd(d + j, t[j]);
+#pragma unroll
+          for (int h = 0; h < kMaxHeads; ++h)
+            if (h < H) {
+              elc[h] = a.el[static_cast<int64_t>(my_idx) * H + h];
+              dac[h] = a.edge_scratch[static_cast<int64_t>(cb + lane) * H + h];
+            }
+        }
+      }
+      for (int k = 0; k < cnt; ++k) {
+        const int u = __shfl_sync(0xffffffffu, my_idx, k);
+        float el_m = 0.f, da_m = 0.f;
+#pragma unroll
+        for (int h = 0; h < kMaxHeads; ++h) {
+          if (h >= H) break;
+          const float t1 = __shfl_sync(0xffffffffu, elc[h], k);
+          const float t2 = __shfl_sync(0xffffffffu, dac[h], k);
+          if (lane == h) {
+            el_m = t1;
+            da_m = t2;
+          }
+        }
+        float al = 0.f;
+        if (lane < H) {
+          const float x = leaky(el_m + er_h, a.slope);
+          al = __expf(x - m) * inv_s;
+          const float de = al * (da_m - S);
+          const float dx = x > 0.f ? de : de * a.slope;
+          atomicAdd(a.del + static_cast<int64_t>(u) * H + lane, dx);
+          der_acc += dx;
+        }
+        if constexpr (CPLY == 0) {
+#pragma unroll
+          for (int q = 0; q < CPL; ++q) {
+            const int c0 = (lane + 32 * q) * 8;
+            const float a0 = __shfl_sync(0xffffffffu, al, hm.h0[q]);
+            float a1 = a0;
+            if constexpr (!SEG) a1 = __shfl_sync(0xffffffffu, al, min(hm.h0[q] + 1, H - 1));
+            if (c0 >= HF) continue;
+            float tv[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) tv[j] = (SEG || (c0 + j) / F == hm.h0[q] ? a0 : a1) * go[q][j];
+            float* d = a.dz + static_cast<int64_t>(u) * a.lddz + c0;
+            if (c0 + 8 <= HF) {
+              red_add_v4f(d, tv[0], tv[1], tv[2], tv[3]);
+              red_add_v4f(d + 4, tv[4], tv[5], tv[6], tv[7]);
+            } else {
+              for (int j = 0; j < 8 && c0 + j < HF; ++j) atomicAdd(d + j, tv[j]);
+            }
+          }
         }
       }
     }
     if (lane < H) a.der[static_cast<int64_t>(v) * H + lane] = der_acc;
+    if constexpr (CPLY > 0) {
+#pragma unroll
+      for (int q = 0; q < CPLY; ++q) {
+        const int c0 = (lane + 32 * q) * 8;
+        if (c0 < HIN)
+          *reinterpret_cast<uint4*>(a.y + static_cast<int64_t>(v) * a.ldy + c0) = f32_to_bf16x8(y[q]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) y[q][j] = 0.f;
+      }
+    }
   }
   if (a.dbias) block_col_atomic<CPL>(bsum, a.dbias, HF);
 }
 
 // ------------------------------------------------------------------ backward, per source
-template <int CPL>
-__global__ void __launch_bounds__(kThreads) gat_bwd_node_kernel(GatArgs a) {
+// A streaming pass over the source rows, kNodeRows rows per warp iteration with every
+// load of the iteration issued before the first use (the kernel is latency-bound:
+// a few KB per warp in flight is what keeps HBM busy).  dz mode: dz_u += del a_l +
+// der a_r, staged to bf16 and cleared; input-layer mode (CPLY > 0): the xl / xr row
+// reductions instead.  Both: the attention-vector gradients da_l += del z,
+// da_r += der z.  del is cleared for the next step after its rows are consumed.
+constexpr int kNodeRows = 4;
+
+template <int CPL, int CPLY, bool SEG>
+__global__ void __launch_bounds__(kThreads, 1) gat_bwd_node_kernel(GatArgs a) {
   const int n_src = a.n_src_ptr ? min(*a.n_src_ptr, a.cap_src) : a.cap_src;
   const int n_dst = a.n_dst_ptr ? min(*a.n_dst_ptr, a.cap_dst) : a.cap_dst;
   const int H = a.heads, F = a.feat, HF = H * F;
+  const int IN = a.in_dim, HIN = H * a.in_dim;
   const int lane = threadIdx.x & 31;
   const int warps_total = (gridDim.x * kThreads) >> 5;
-  const int rows_end = a.zero_tail_rows > 0 ? min(a.cap_src, static_cast<int>(ceil_div(n_src, a.zero_tail_rows) * a.zero_tail_rows)) : n_src;
-  float gl[CPL][8], gr[CPL][8];
+  const HeadMap hm = head_map<CPL, SEG>(lane, H, F);
+  constexpr bool DZ = CPLY == 0;
+  constexpr int NY = CPLY > 0 ? CPLY : 1;
+  constexpr int R = kNodeRows;
+  const int rows_end =
+      DZ && a.zero_tail_rows > 0
+          ? min(a.cap_src, static_cast<int>(ceil_div(n_src, a.zero_tail_rows) * a.zero_tail_rows))
+          : n_src;
+  int hy[NY], ky[NY];
+#pragma unroll
+  for (int q = 0; q < NY; ++q) {
+    const int c0 = (lane + 32 * q) * 8;
+    hy[q] = CPLY > 0 ? min(c0 / max(IN, 1), H - 1) : 0;
+    ky[q] = c0 - hy[q] * IN;
+  }
+  float gl[CPL][8], gr[CPL][8], xl[NY][8], xr[NY][8];
 #pragma unroll
   for (int q = 0; q < CPL; ++q)
 #pragma unroll
     for (int j = 0; j < 8; ++j) gl[q][j] = gr[q][j] = 0.f;
-  for (int u = (blockIdx.x * kThreads + threadIdx.x) >> 5; u < rows_end; u += warps_total) {
-    if (u >= n_src) {
-      for (int c = lane * 8; c < a.lddzb; c += 256)
-        *reinterpret_cast<uint4*>(a.dz_bf16 + static_cast<int64_t>(u) * a.lddzb + c) = make_uint4(0, 0, 0, 0);
-      continue;
-    }
-    float dl = 0.f, dr = 0.f;
-    if (lane < H) {
-      float* pl = a.del + static_cast<int64_t>(u) * H + lane;
-      dl = *pl;
-      *pl = 0.f;
-      if (u < n_dst) dr = a.der[static_cast<int64_t>(u) * H + lane];
-    }
 #pragma unroll
-    for (int q = 0; q < CPL; ++q) {
-      const int c0 = (lane + 32 * q) * 8;
-      const int ha = min(c0 / F, H - 1);
-      const int hb = min(ha + 1, H - 1);
-      const float dla = __shfl_sync(0xffffffffu, dl, ha), dlb = __shfl_sync(0xffffffffu, dl, hb);
-      const float dra = __shfl_sync(0xffffffffu, dr, ha), drb = __shfl_sync(0xffffffffu, dr, hb);
-      if (c0 >= a.lddzb) continue;
-      float o[8];
-      if (c0 < HF) {
-        // all loads of the chunk first (16-byte vectors), then the arithmetic, then the
-        // stores: no load waits behind a store that might alias it
-        float zf[8], dv[8], al[8], ar[8];
-        bf16x8_to_f32(*reinterpret_cast<const uint4*>(a.z + static_cast<int64_t>(u) * a.ldz + c0), zf);
-        float* d = a.dz + static_cast<int64_t>(u) * a.lddz + c0;
-        const bool full = c0 + 8 <= HF;
-        if (full) {
-          *reinterpret_cast<float4*>(dv) = *reinterpret_cast<const float4*>(d);
-          *reinterpret_cast<float4*>(dv + 4) = *reinterpret_cast<const float4*>(d + 4);
-          *reinterpret_cast<float4*>(al) = __ldg(reinterpret_cast<const float4*>(a.attn_l + c0));
-          *reinterpret_cast<float4*>(al + 4) = __ldg(reinterpret_cast<const float4*>(a.attn_l + c0 + 4));
-          *reinterpret_cast<float4*>(ar) = __ldg(reinterpret_cast<const float4*>(a.attn_r + c0));
-          *reinterpret_cast<float4*>(ar + 4) = __ldg(reinterpret_cast<const float4*>(a.attn_r + c0 + 4));
-        } else {
+  for (int q = 0; q < NY; ++q)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) xl[q][j] = xr[q][j] = 0.f;
+  const int first = (blockIdx.x * kThreads + threadIdx.x) >> 5;
+  for (int u0 = R * first; u0 < rows_end; u0 += R * warps_total) {
+    // ---- loads of the R rows
+    float dl[R], dr[R];
+    uint4 zv[R][CPL];
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+      const int u = u0 + i;
+      dl[i] = dr[i] = 0.f;
+      if (lane < H && u < n_src) {
+        dl[i] = a.del[static_cast<int64_t>(u) * H + lane];
+        if (u < n_dst) dr[i] = a.der[static_cast<int64_t>(u) * H + lane];
+      }
+#pragma unroll
+      for (int q = 0; q < CPL; ++q) {
+        const int c0 = (lane + 32 * q) * 8;
+        zv[i][q] = make_uint4(0, 0, 0, 0);
+        if (u < n_src && c0 < HF)
+          zv[i][q] = *reinterpret_cast<const uint4*>(a.z + static_cast<int64_t>(u) * a.ldz + c0);
+      }
+    }
+    float4 dv[DZ ? R : 1][CPL][2];
+    uint4 xv[DZ ? 1 : R][NY];
+    if constexpr (DZ) {
+#pragma unroll
+      for (int i = 0; i < R; ++i)
+#pragma unroll
+        for (int q = 0; q < CPL; ++q) {
+          const int c0 = (lane + 32 * q) * 8;
+          const float* d = a.dz + static_cast<int64_t>(u0 + i) * a.lddz + c0;
+          dv[i][q][0] = dv[i][q][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (u0 + i < n_src && c0 < HF) {
+            if (c0 + 8 <= HF) {
+              dv[i][q][0] = *reinterpret_cast<const float4*>(d);
+              dv[i][q][1] = *reinterpret_cast<const float4*>(d + 4);
+            } else {
+              float t[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+              for (int j = 0; j < 8 && c0 + j < HF; ++j) t[j] = d[j];
+              dv[i][q][0] = make_float4(t[0], t[1], t[2], t[3]);
+              dv[i][q][1] = make_float4(t[4], t[5], t[6], t[7]);
+            }
+          }
+        }
+    } else {
+#pragma unroll
+      for (int i = 0; i < R; ++i)
+#pragma unroll
+        for (int q = 0; q < NY; ++q) {
+          const int c0 = (lane + 32 * q) * 8;
+          xv[i][q] = make_uint4(0, 0, 0, 0);
+          if (u0 + i < n_src && c0 < HIN)
+            xv[i][q] = *reinterpret_cast<const uint4*>(a.x + static_cast<int64_t>(u0 + i) * a.ldx + ky[q]);
+        }
+    }
+    // ---- arithmetic and stores
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+      const int u = u0 + i;
+#pragma unroll
+      for (int q = 0; q < CPL; ++q) {
+        const int c0 = (lane + 32 * q) * 8;
+        const int ha = hm.h0[q];
+        const float dla = __shfl_sync(0xffffffffu, dl[i], ha), dra = __shfl_sync(0xffffffffu, dr[i], ha);
+        float dlb = dla, drb = dra;
+        if constexpr (!SEG) {
+          const int hb = min(ha + 1, H - 1);
+          dlb = __shfl_sync(0xffffffffu, dl[i], hb);
+          drb = __shfl_sync(0xffffffffu, dr[i], hb);
+        }
+        if (u >= rows_end) continue;
+        if (DZ && c0 >= a.lddzb) continue;
+        float o[8];
+        if (u < n_src && c0 < HF) {
+          float zf[8];
+          bf16x8_to_f32(zv[i][q], zf);
+          float dvf[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          if constexpr (DZ) {
+            *reinterpret_cast<float4*>(dvf) = dv[i][q][0];
+            *reinterpret_cast<float4*>(dvf + 4) = dv[i][q][1];
+          }
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            const bool in = c0 + j < HF;
-            dv[j] = in ? d[j] : 0.f;
-            al[j] = in ? a.attn_l[c0 + j] : 0.f;
-            ar[j] = in ? a.attn_r[c0 + j] : 0.f;
+            const bool fa = SEG || (c0 + j) / F == ha;
+            const float cl = fa ? dla : dlb, cr = fa ? dra : drb;
+            gl[q][j] = fmaf(cl, zf[j], gl[q][j]);
+            gr[q][j] = fmaf(cr, zf[j], gr[q][j]);
+            if constexpr (DZ) {
+              const bool in = c0 + j < HF;
+              o[j] = in ? dvf[j] + cl * __ldg(a.attn_l + min(c0 + j, HF - 1)) +
+                              cr * __ldg(a.attn_r + min(c0 + j, HF - 1))
+                        : 0.f;
+            }
           }
-        }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int c = c0 + j;
-          const bool first = c / F == ha;
-          const float cl = first ? dla : dlb, cr = first ? dra : drb;
-          o[j] = c < HF ? dv[j] + cl * al[j] + cr * ar[j] : 0.f;
-          if (c < HF) {
-            gl[q][j] += cl * zf[j];
-            gr[q][j] += cr * zf[j];
+          if constexpr (DZ) {
+            float* d = a.dz + static_cast<int64_t>(u) * a.lddz + c0;
+            if (c0 + 8 <= HF) {
+              *reinterpret_cast<float4*>(d) = make_float4(0.f, 0.f, 0.f, 0.f);
+              *reinterpret_cast<float4*>(d + 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+            } else {
+              for (int j = 0; j < 8 && c0 + j < HF; ++j) d[j] = 0.f;
+            }
           }
-        }
-        if (full) {
-          *reinterpret_cast<float4*>(d) = make_float4(0.f, 0.f, 0.f, 0.f);
-          *reinterpret_cast<float4*>(d + 4) = make_float4(0.f, 0.f, 0.f, 0.f);
         } else {
-          for (int j = 0; j < 8 && c0 + j < HF; ++j) d[j] = 0.f;
-        }
-      } else {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) o[j] = 0.f;
+          for (int j = 0; j < 8; ++j) o[j] = 0.f;
+        }
+        if constexpr (DZ) *reinterpret_cast<uint4*>(a.dz_bf16 + static_cast<int64_t>(u) * a.lddzb + c0) = f32_to_bf16x8(o);
       }
-      *reinterpret_cast<uint4*>(a.dz_bf16 + static_cast<int64_t>(u) * a.lddzb + c0) = f32_to_bf16x8(o);
+      if constexpr (!DZ) {
+#pragma unroll
+        for (int q = 0; q < NY; ++q) {
+          const int c0 = (lane + 32 * q) * 8;
+          const float dlq = __shfl_sync(0xffffffffu, dl[i], hy[q]), drq = __shfl_sync(0xffffffffu, dr[i], hy[q]);
+          if (u >= n_src || c0 >= HIN) continue;
+          float f[8];
+          bf16x8_to_f32(xv[i][q], f);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            xl[q][j] = fmaf(dlq, f[j], xl[q][j]);
+            xr[q][j] = fmaf(drq, f[j], xr[q][j]);
+          }
+        }
+      }
+      if (lane < H && u < n_src) a.del[static_cast<int64_t>(u) * H + lane] = 0.f;
     }
   }
   if (a.dattn_l) block_col_atomic<CPL>(gl, a.dattn_l, HF);
   if (a.dattn_r) block_col_atomic<CPL>(gr, a.dattn_r, HF);
+  if constexpr (!DZ) {
+    block_col_atomic<NY>(xl, a.xl, HIN);
+    block_col_atomic<NY>(xr, a.xr, HIN);
+  }
+}
+
+// dW[r, k] += T[r, h * IN + k] + a_l[r] xl[h, k] + a_r[r] xr[h, k], h = r / F
+__global__ void gat_dw_combine_kernel(const float* T, int64_t ldt, const float* xl, const float* xr,
+                                      const float* attn_l, const float* attn_r, int H, int F, int IN, float* dw,
+                                      int64_t ldw) {
+  const int total = H * F * IN;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int r = i / IN, k = i % IN, h = r / F;
+    dw[static_cast<int64_t>(r) * ldw + k] +=
+        T[static_cast<int64_t>(r) * ldt + h * IN + k] + attn_l[r] * xl[h * IN + k] + attn_r[r] * xr[h * IN + k];
+  }
 }
 
 int cpl_for(int hf) { return (hf + 255) / 256; }
@@ -515,11 +818,55 @@ void launch_gat_fwd(const GatArgs& a, cudaStream_t stream) {
   GAT_DISPATCH(gat_fwd_kernel, grid_warps(a.cap_dst), smem);
 }
 
+bool seg_heads(int F) { return F >= 8 && F <= 256 && (F & (F - 1)) == 0; }
+
+template <int CPL, int CPLY, bool SEG>
+void gat_bwd_pair(const GatArgs& a, cudaStream_t stream) {
+  constexpr int mb = bwd_min_blocks<CPL, CPLY>();
+  gat_bwd_edge_kernel<CPL, CPLY, SEG><<<grid_warps(a.cap_dst, mb), kThreads, 0, stream>>>(a);
+  GB_LAUNCH_CHECK();
+  gat_bwd_node_kernel<CPL, CPLY, SEG><<<grid_warps(static_cast<int>(ceil_div(a.cap_src, kNodeRows)), 1), kThreads, 0, stream>>>(a);
+  GB_LAUNCH_CHECK();
+}
+
+template <int CPLY>
+void gat_bwd_cpl(const GatArgs& a, cudaStream_t stream) {
+  const int cpl = cpl_for(a.heads * a.feat);
+  const bool seg = seg_heads(a.feat);
+  if (cpl <= 1) seg ? gat_bwd_pair<1, CPLY, true>(a, stream) : gat_bwd_pair<1, CPLY, false>(a, stream);
+  else if (cpl <= 2) seg ? gat_bwd_pair<2, CPLY, true>(a, stream) : gat_bwd_pair<2, CPLY, false>(a, stream);
+  else seg ? gat_bwd_pair<4, CPLY, true>(a, stream) : gat_bwd_pair<4, CPLY, false>(a, stream);
+}
+
 void launch_gat_bwd(const GatArgs& a, cudaStream_t stream) {
   check(a);
   if (a.lddz % 4 != 0 || a.lddzb % 8 != 0) throw std::invalid_argument("gat: gradient strides");
-  GAT_DISPATCH(gat_bwd_edge_kernel, grid_warps(a.cap_dst, 4), 0);
-  GAT_DISPATCH(gat_bwd_node_kernel, grid_warps(a.cap_src, 4), 0);
+  if (!a.mean_heads && a.lddo % 8 != 0) throw std::invalid_argument("gat: dout stride % 8");
+  gat_bwd_cpl<0>(a, stream);
+}
+
+void launch_gat_bwd_input(const GatArgs& a, cudaStream_t stream) {
+  check(a);
+  if (a.mean_heads) throw std::invalid_argument("gat input-layer backward: hidden layers only");
+  if (a.in_dim <= 0 || a.in_dim % 8 != 0 || a.ldx % 8 != 0 || a.ldy % 8 != 0)
+    throw std::invalid_argument("gat input-layer backward: in_dim and strides must be multiples of 8");
+  const int hin = a.heads * a.in_dim;
+  if (hin > 1024) throw std::invalid_argument("gat input-layer backward: heads * in <= 1024");
+  if (!a.x || !a.y || !a.xl || !a.xr) throw std::invalid_argument("gat input-layer backward: x, y, xl, xr needed");
+  if (a.lddo % 8 != 0) throw std::invalid_argument("gat: dout stride % 8");
+  const int cply = cpl_for(hin);
+  if (cply <= 1) gat_bwd_cpl<1>(a, stream);
+  else if (cply <= 2) gat_bwd_cpl<2>(a, stream);
+  else gat_bwd_cpl<4>(a, stream);
+}
+
+void launch_gat_dw_combine(const float* T, int64_t ldt, const float* xl, const float* xr, const float* attn_l,
+                           const float* attn_r, int heads, int feat, int in_dim, float* dw, int64_t ldw,
+                           cudaStream_t stream) {
+  const int total = heads * feat * in_dim;
+  const int grid = std::max(1, std::min((total + 255) / 256, sms() * 4));
+  gat_dw_combine_kernel<<<grid, 256, 0, stream>>>(T, ldt, xl, xr, attn_l, attn_r, heads, feat, in_dim, dw, ldw);
+  GB_LAUNCH_CHECK();
 }
 
 }  // namespace dev

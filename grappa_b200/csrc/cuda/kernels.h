@@ -382,10 +382,22 @@ struct GatArgs {
   int64_t lddzb = 0;
   int32_t zero_tail_rows = 64;
   int32_t* err = nullptr;
+  // input-layer backward (launch_gat_bwd_input: no dz, see gat.cu)
+  const __nv_bfloat16* x = nullptr;     // [cap_src, ldx] the layer's input rows
+  int64_t ldx = 0;
+  int32_t in_dim = 0;                   // width of x used by the projection (multiple of 8)
+  __nv_bfloat16* y = nullptr;           // [cap_dst, ldy >= H * in_dim]
+  int64_t ldy = 0;
+  float* xl = nullptr;                  // [H * in_dim] (zero before)
+  float* xr = nullptr;                  // [H * in_dim] (zero before)
 };
 void launch_gat_scores(const GatArgs& a, cudaStream_t stream);
 void launch_gat_fwd(const GatArgs& a, cudaStream_t stream);
 void launch_gat_bwd(const GatArgs& a, cudaStream_t stream);
+void launch_gat_bwd_input(const GatArgs& a, cudaStream_t stream);
+void launch_gat_dw_combine(const float* T, int64_t ldt, const float* xl, const float* xr, const float* attn_l,
+                           const float* attn_r, int heads, int feat, int in_dim, float* dw, int64_t ldw,
+                           cudaStream_t stream);
 
 // counters = [seed, epoch, step_in_epoch, global_step, gen, adam_t]: advance the step
 void launch_step_end(int64_t* counters, cudaStream_t stream);

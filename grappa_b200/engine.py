@@ -28,6 +28,7 @@ Full-graph training uses the same engines with ``FullGraphBlocks`` (the working
 graph as a fixed block for every layer) in place of the sampler.
 """
 import math
+import os
 
 import torch
 
@@ -37,6 +38,9 @@ from grappa_b200.sampler_gpu import C_EPOCH, C_STEP, GpuNeighborSampler, new_cou
 
 GEMM_STORE_BF16, GEMM_STORE_F32, GEMM_ATOMIC_F32, GEMM_CROSS_ENTROPY = 0, 1, 2, 3
 AGG_MEAN, AGG_SUM, AGG_GCN, AGG_WEIGHTED = 0, 1, 2, 3
+# GAT input layer: dW from attention-weighted input rows instead of a per-source dz
+# (GRAPPA_GAT_INPUT_BWD=0 selects the dz path, for comparisons)
+GAT_INPUT_LAYER_BWD = os.environ.get("GRAPPA_GAT_INPUT_BWD", "1") != "0"
 
 # kernels launched by each binding (memsets excluded)
 KERNELS_PER_CALL = {
@@ -45,7 +49,7 @@ KERNELS_PER_CALL = {
     "pull_rows": 1, "csr_merge": 1, "mark_ids": 1, "iota_map": 1, "mark_compact": 1, "peer_copy": 1, "a2a_pull": 1, "peer_barrier": 1,
     "shuffle_keys": 1, "cross_entropy": 1, "batchnorm_fwd": 2, "batchnorm_bwd": 2, "l2norm_fwd": 1,
     "l2norm_bwd": 1, "dropout_rows": 1, "dropout_grad": 1, "f32_to_bf16_rows": 1, "add_bf16_rows": 1,
-    "gat_scores": 1, "gat_fwd": 1, "gat_bwd": 2, "sampler_counters": 1,
+    "gat_scores": 1, "gat_fwd": 1, "gat_bwd": 2, "gat_bwd_input": 2, "gat_dw_combine": 1, "sampler_counters": 1,
 }
 
 
@@ -853,15 +857,23 @@ class GatEngine(BlockEngine):
             last = l == self.L - 1
             A = self._seg(layer.seg_a)
             gA = self._seg(layer.seg_a, self.grad)
-            s = dict(h=h, H=H, F=F, HF=HF, ip=ip, hfp=hfp, rows=rows, srows=srows, last=last,
+            # input layer: dW from attention-weighted input rows, no dz (gat.cu)
+            in_fast = GAT_INPUT_LAYER_BWD and l == 0 and not last and H * ip <= 1024
+            s = dict(h=h, H=H, F=F, HF=HF, ip=ip, hfp=hfp, rows=rows, srows=srows, last=last, in_fast=in_fast,
                      W=self._seg(layer.seg_w, self.wbf), gW=self._seg(layer.seg_w, self.grad),
                      al=A[0], ar=A[1], gal=gA[0], gar=gA[1],
                      bias=self._seg(layer.seg_b)[0], gb=self._seg(layer.seg_b, self.grad)[0],
                      Z=torch.zeros((srows, hfp), **z), el=torch.zeros(srows * H, **f32),
                      er=torch.zeros(rows * H, **f32), smax=torch.zeros(rows * H, **f32),
                      ssum=torch.zeros(rows * H, **f32), escr=torch.zeros(ecap * H, **f32),
-                     del_=torch.zeros(srows * H, **f32), der=torch.zeros(rows * H, **f32),
-                     dz=torch.zeros((srows, hfp), **f32), dzb=torch.zeros((srows, hfp), **z))
+                     del_=torch.zeros(srows * H, **f32), der=torch.zeros(rows * H, **f32))
+            if in_fast:
+                s["Yin"] = torch.zeros((rows, H * ip), **z)
+                s["T"] = torch.zeros((hfp, H * ip), **f32)
+                s["xlr"] = torch.zeros(2 * H * ip, **f32)
+            else:
+                s["dz"] = torch.zeros((srows, hfp), **f32)
+                s["dzb"] = torch.zeros((srows, hfp), **z)
             if l == 0 and not self.full_graph:
                 s["Xg"] = torch.zeros((srows, ip), **z)
             if last:
@@ -909,15 +921,42 @@ class GatEngine(BlockEngine):
             else:
                 cu.act_bwd(s["dH"], s["H_out"], s["dY"], self._n_dst(h), 0, s["hfp"], scale, None, s["rows"])
                 dout = s["dY"]
+            A = self._A(l, s)
+            if s["in_fast"]:
+                self._input_layer_bwd(s, h, dout, A)
+                continue
             cu.gat_bwd(sm.indptr[h], sm.indices[h], self._n_dst(h), s["rows"], sm.n_src(h), s["srows"], s["H"],
                        s["F"], s["Z"], s["al"], s["ar"], s["el"], s["er"], s["smax"], s["ssum"], 0.2, s["last"], dout,
                        s["escr"], s["del_"], s["der"], s["dz"], s["gb"], s["gal"], s["gar"], s["dzb"], self.err)
-            A = self._A(l, s)
             self._dw(s["dzb"], A, s["HF"], s["ip"], s["srows"], sm.n_src(h), s["gW"])
             if l > 0:
                 prev = self.lay[l - 1]
                 self._gemm(s["dzb"], False, s["W"], True, s["srows"], sm.n_src(h), s["ip"], s["HF"], None, 1,
                            prev["dH"], GEMM_STORE_F32)
+
+
+    def _input_layer_bwd(self, s, h, dout, A):
+        """dW of the input layer as dout^T y plus two rank-1 terms (y = attention-weighted
+        input rows per destination), with no per-source dz: the GEMM and the combine run
+        on the auxiliary stream like the other weight gradients."""
+        cu, sm = self.cu, self.sm
+        Hh, ip = s["H"], s["ip"]
+        xl, xr = s["xlr"][:Hh * ip], s["xlr"][Hh * ip:]
+        cu.zero_(s["xlr"])
+        cu.gat_bwd_input(sm.indptr[h], sm.indices[h], self._n_dst(h), s["rows"], sm.n_src(h), s["srows"], Hh,
+                         s["F"], s["Z"], s["al"], s["ar"], s["el"], s["er"], s["smax"], s["ssum"], 0.2, dout,
+                         s["escr"], s["del_"], s["der"], s["gb"], s["gal"], s["gar"], A, ip, s["Yin"], xl, xr,
+                         self.err)
+        main = torch.cuda.current_stream(self.device)
+        aux = self._aux_stream()
+        aux.wait_stream(main)
+        n_tiles = math.ceil(s["hfp"] / 128) * math.ceil(Hh * ip / 256)
+        with torch.cuda.stream(aux):
+            cu.zero_(s["T"])
+            self._gemm(dout, True, s["Yin"], True, s["hfp"], None, Hh * ip, s["rows"], self._n_dst(h),
+                       split_k(s["rows"], n_tiles), s["T"], GEMM_ATOMIC_F32, bn=256)
+            cu.gat_dw_combine(s["T"], xl, xr, s["al"], s["ar"], Hh, s["F"], ip, s["gW"])
+        self._aux_used = True
 
 
 class PinSageEngine(BlockEngine):

@@ -14,7 +14,7 @@ t10n/infer.py:106-108).  Accuracy
 counts are all-reduced: [train_ok, valid_ok, test_ok, train_n, valid_n, test_n].
 
 Layers run on the tensors' device: the PyTorch path on CPU tensors, the sm_100a
-layer kernels (grappa_b200.engine.infer_layer) on CUDA tensors.
+layer kernels (grappa_b200.infer_gpu.infer_layer) on CUDA tensors.
 """
 import gc
 
@@ -45,7 +45,7 @@ def apply_layer(model, layer_i, block, h):
     """One layer of ``model`` plus its inter-layer activation (eval mode: no dropout)."""
     last = layer_i == len(model.layers) - 1
     if h.is_cuda:
-        from grappa_b200.engine import infer_layer
+        from grappa_b200.infer_gpu import infer_layer
 
         return infer_layer(model, layer_i, block, h)
     layer = model.layers[layer_i]

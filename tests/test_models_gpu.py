@@ -47,6 +47,7 @@ CASES = [
     ("gcn", dict(num_hidden=16, num_layers=2), [10, 5]),       # projection-first on gathered inputs
     ("gin", dict(num_hidden=64, num_layers=3), [10, 10, 5]),
     ("gat", dict(num_hidden=16, num_layers=3, n_heads=4), [10, 10, 5]),
+    ("gat", dict(num_hidden=24, num_layers=2, n_heads=3), [10, 5]),  # heads straddling 8-column chunks
     ("pinsage", dict(num_hidden=64, num_layers=3), None),
 ]
 
@@ -80,6 +81,13 @@ def test_engine_step_matches_cpu_model(tiny, name, kw, fanouts):
     # percent per layer towards the input (BatchNorm kernels alone: test_nn_kernels_gpu.py)
     tol = 0.15 if name == "gin" else 6e-2
     assert rel < tol, f"{name}: gradient relative error {rel:.3e}"
+    if name == "gat":
+        # the input layer's weight and attention gradients take their own kernel path
+        for seg_name in ("layers.0.W", "layers.0.A", "layers.0.b"):
+            seg = model.segment(seg_name)
+            a, b = seg.view(grad_gpu), seg.view(flat_grad.detach())
+            r = (a - b).norm() / b.norm().clamp(min=1e-12)
+            assert r < 6e-2, f"gat {seg_name}: gradient relative error {r:.3e}"
     if name == "gin":
         # BatchNorm running statistics follow the batch statistics
         for a, b in zip(model.batch_norms, cpu_model.batch_norms):
