@@ -33,6 +33,9 @@
 // kErrMmaTimeout, drains what it issued (again bounded), frees its TMEM and exits.
 #include <cuda.h>
 
+#include <algorithm>
+#include <cstdlib>
+
 #include "common.cuh"
 #include "grappa/rng.h"
 #include "kernels.h"
@@ -159,6 +162,145 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
 __device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
   asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
                : "memory");
+}
+
+// Epilogue of one 128 x BN accumulator tile for the store and atomic modes: warp
+// `quarter` drains TMEM lanes 32 * quarter + (0..31), i.e. rows m0 + 32 * quarter +
+// lane, columns [c_begin, c_end) (multiples of 64 on the TMA-store path); `trow` is
+// that warp's TMEM address of the tile, `stage` its 32 x (c_end - c_begin) bf16
+// staging panels for the TMA store (kTmaStore), `ok` false after an aborted wait.
+template <int BN, bool kTmaStore>
+__device__ __forceinline__ void store_tile(const GemmArgs& a, const CUtensorMap* tmC, uint32_t trow, int m0, int n0,
+                                           int M, int quarter, int lane, uint8_t* stage, bool ok, int c_begin = 0,
+                                           int c_end = BN) {
+  const int m = m0 + quarter * 32 + lane;
+  if (kTmaStore && a.c_mode == kStoreBf16) {
+    // bf16 tile through shared memory and TMA stores: each epilogue warp stages its
+    // 32 rows as 64-column panels in the 128B-swizzled layout of the store's tensor
+    // map (`stage`: 32 rows x BN bf16) and one lane stores them
+    const uint64_t key = a.counters ? hop_key(static_cast<uint64_t>(a.counters[0]) ^ 0xD80Full,
+                                              static_cast<uint64_t>(a.counters[1]),
+                                              static_cast<uint64_t>(a.counters[2]), a.dropout_salt)
+                                    : 0ull;
+    const float keep_scale = a.dropout_p > 0.f ? 1.0f / (1.0f - a.dropout_p) : 1.0f;
+    const uint32_t thr = static_cast<uint32_t>(static_cast<double>(a.dropout_p) * 4294967296.0);
+    const bool live = m < M;
+    // a 32-row slab that crosses the live row count stores its live rows directly,
+    // so that rows >= M are never written
+    const bool slab_full = m0 + quarter * 32 + 32 <= M;
+#pragma unroll 1
+    for (int c = c_begin; c < c_end; c += 32) {
+      float v[32];
+      tmem_ld32(trow + c, v);
+      const int nc = n0 + c;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        float x = v[j];
+        if (a.bias && nc + j < a.N) x += a.bias[nc + j];
+        if (a.act == 1) x = fmaxf(x, 0.f);
+        v[j] = live ? x : 0.f;
+      }
+      if (a.dropout_p > 0.f && live) {
+        const uint64_t base = static_cast<uint64_t>(m) * static_cast<uint64_t>(a.ldc) + static_cast<uint64_t>(nc);
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          const U4 r = index_draw4(key, (base + j) >> 2, 0);
+          v[j] = r.x >= thr ? v[j] * keep_scale : 0.f;
+          v[j + 1] = r.y >= thr ? v[j + 1] * keep_scale : 0.f;
+          v[j + 2] = r.z >= thr ? v[j + 2] * keep_scale : 0.f;
+          v[j + 3] = r.w >= thr ? v[j + 3] * keep_scale : 0.f;
+        }
+      }
+      if (slab_full) {
+        uint8_t* panel = stage + ((c - c_begin) >> 6) * 4096 + lane * 128;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int k = ((c & 63) >> 3) + q;
+          *reinterpret_cast<uint4*>(panel + ((k ^ (lane & 7)) << 4)) = f32_to_bf16x8(v + 8 * q);
+        }
+      } else if (live && ok && nc < a.N) {
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.C) + static_cast<int64_t>(m) * a.ldc + nc;
+        if (nc + 32 <= a.ldc) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) *reinterpret_cast<uint4*>(dst + j) = f32_to_bf16x8(v + j);
+        } else {
+          for (int j = 0; j < 32 && nc + j < a.ldc; ++j) dst[j] = __float2bfloat16_rn(v[j]);
+        }
+      }
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+    if (lane == 0 && ok && slab_full) {
+      for (int p = 0; p < (c_end - c_begin) / 64; ++p)
+        if (n0 + c_begin + p * 64 < a.N)
+          tma_store_2d(tmC, stage + p * 4096, n0 + c_begin + p * 64, m0 + quarter * 32);
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      // the staging panels may be rewritten once the store has read them
+      asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+    }
+    __syncwarp();
+  } else {
+    const uint64_t key = a.counters ? hop_key(static_cast<uint64_t>(a.counters[0]) ^ 0xD80Full,
+                                              static_cast<uint64_t>(a.counters[1]),
+                                              static_cast<uint64_t>(a.counters[2]), a.dropout_salt)
+                                    : 0ull;
+    const float keep_scale = a.dropout_p > 0.f ? 1.0f / (1.0f - a.dropout_p) : 1.0f;
+    const uint32_t thr = static_cast<uint32_t>(static_cast<double>(a.dropout_p) * 4294967296.0);
+#pragma unroll 1
+    for (int c = c_begin; c < c_end; c += 32) {
+      float v[32];
+      tmem_ld32(trow + c, v);
+      if (!ok || m >= M) continue;
+      const int nc = n0 + c;
+      if (nc >= a.N) continue;
+      if (a.c_mode == kAtomicF32) {
+        float* dst = reinterpret_cast<float*>(a.C) + static_cast<int64_t>(m) * a.ldc + nc;
+        if (nc + 32 <= a.N) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) red_add_v4(dst + j, v[j], v[j + 1], v[j + 2], v[j + 3]);
+        } else {
+          for (int j = 0; j < 32 && nc + j < a.N; ++j) atomicAdd(dst + j, v[j]);
+        }
+        continue;
+      }
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        float x = v[j];
+        if (a.bias && nc + j < a.N) x += a.bias[nc + j];
+        if (a.act == 1) x = fmaxf(x, 0.f);
+        v[j] = x;
+      }
+      if (a.dropout_p > 0.f) {
+        const uint64_t base = static_cast<uint64_t>(m) * static_cast<uint64_t>(a.ldc) + static_cast<uint64_t>(nc);
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          // one Philox call covers 4 consecutive elements (base + j is a multiple of 4)
+          const U4 r = index_draw4(key, (base + j) >> 2, 0);
+          v[j] = r.x >= thr ? v[j] * keep_scale : 0.f;
+          v[j + 1] = r.y >= thr ? v[j + 1] * keep_scale : 0.f;
+          v[j + 2] = r.z >= thr ? v[j + 2] * keep_scale : 0.f;
+          v[j + 3] = r.w >= thr ? v[j + 3] * keep_scale : 0.f;
+        }
+      }
+      if (a.c_mode == kStoreBf16) {
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.C) + static_cast<int64_t>(m) * a.ldc + nc;
+        if (nc + 32 <= a.ldc) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) *reinterpret_cast<uint4*>(dst + j) = f32_to_bf16x8(v + j);
+        } else {
+          for (int j = 0; j < 32 && nc + j < a.ldc; ++j) dst[j] = __float2bfloat16_rn(v[j]);
+        }
+      } else {
+        float* dst = reinterpret_cast<float*>(a.C) + static_cast<int64_t>(m) * a.ldc + nc;
+        if (nc + 32 <= a.ldc) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        } else {
+          for (int j = 0; j < 32 && nc + j < a.ldc; ++j) dst[j] = v[j];
+        }
+      }
+    }
+    }
 }
 
 template <int BN>
@@ -366,133 +508,223 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (a.pred_out) a.pred_out[m] = arg;
       }
      }
-    } else if (kTmaStore && a.c_mode == kStoreBf16) {
-      // bf16 tile through shared memory and TMA stores: each epilogue warp stages its
-      // 32 rows as 64-column panels in the 128B-swizzled layout of the store's tensor
-      // map (reusing the drained operand ring) and one lane stores them
-      const uint64_t key = a.counters ? hop_key(static_cast<uint64_t>(a.counters[0]) ^ 0xD80Full,
-                                                static_cast<uint64_t>(a.counters[1]),
-                                                static_cast<uint64_t>(a.counters[2]), a.dropout_salt)
-                                      : 0ull;
-      const float keep_scale = a.dropout_p > 0.f ? 1.0f / (1.0f - a.dropout_p) : 1.0f;
-      const uint32_t thr = static_cast<uint32_t>(static_cast<double>(a.dropout_p) * 4294967296.0);
-      uint8_t* stage = smem + quarter * (32 * BN * 2);
-      const bool live = m < M;
-      // a 32-row slab that crosses the live row count stores its live rows directly,
-      // so that rows >= M are never written
-      const bool slab_full = m0 + quarter * 32 + 32 <= M;
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        float v[32];
-        tmem_ld32(trow + c, v);
-        const int nc = n0 + c;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          float x = v[j];
-          if (a.bias && nc + j < a.N) x += a.bias[nc + j];
-          if (a.act == 1) x = fmaxf(x, 0.f);
-          v[j] = live ? x : 0.f;
-        }
-        if (a.dropout_p > 0.f && live) {
-          const uint64_t base = static_cast<uint64_t>(m) * static_cast<uint64_t>(a.ldc) + static_cast<uint64_t>(nc);
-#pragma unroll
-          for (int j = 0; j < 32; j += 4) {
-            const U4 r = index_draw4(key, (base + j) >> 2, 0);
-            v[j] = r.x >= thr ? v[j] * keep_scale : 0.f;
-            v[j + 1] = r.y >= thr ? v[j + 1] * keep_scale : 0.f;
-            v[j + 2] = r.z >= thr ? v[j + 2] * keep_scale : 0.f;
-            v[j + 3] = r.w >= thr ? v[j + 3] * keep_scale : 0.f;
-          }
-        }
-        if (slab_full) {
-          uint8_t* panel = stage + (c >> 6) * 4096 + lane * 128;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int k = ((c & 63) >> 3) + q;
-            *reinterpret_cast<uint4*>(panel + ((k ^ (lane & 7)) << 4)) = f32_to_bf16x8(v + 8 * q);
-          }
-        } else if (live && ok && nc < a.N) {
-          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.C) + static_cast<int64_t>(m) * a.ldc + nc;
-          if (nc + 32 <= a.ldc) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 8) *reinterpret_cast<uint4*>(dst + j) = f32_to_bf16x8(v + j);
-          } else {
-            for (int j = 0; j < 32 && nc + j < a.ldc; ++j) dst[j] = __float2bfloat16_rn(v[j]);
-          }
-        }
-      }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      __syncwarp();
-      if (lane == 0 && ok && slab_full) {
-        for (int p = 0; p < BN / 64; ++p)
-          if (n0 + p * 64 < a.N) tma_store_2d(&tmC, stage + p * 4096, n0 + p * 64, m0 + quarter * 32);
-        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-        asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
-      }
-      __syncwarp();
     } else {
-      const uint64_t key = a.counters ? hop_key(static_cast<uint64_t>(a.counters[0]) ^ 0xD80Full,
-                                                static_cast<uint64_t>(a.counters[1]),
-                                                static_cast<uint64_t>(a.counters[2]), a.dropout_salt)
-                                      : 0ull;
-      const float keep_scale = a.dropout_p > 0.f ? 1.0f / (1.0f - a.dropout_p) : 1.0f;
-      const uint32_t thr = static_cast<uint32_t>(static_cast<double>(a.dropout_p) * 4294967296.0);
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        float v[32];
-        tmem_ld32(trow + c, v);
-        if (!ok || m >= M) continue;
-        const int nc = n0 + c;
-        if (nc >= a.N) continue;
-        if (a.c_mode == kAtomicF32) {
-          float* dst = reinterpret_cast<float*>(a.C) + static_cast<int64_t>(m) * a.ldc + nc;
-          if (nc + 32 <= a.N) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) red_add_v4(dst + j, v[j], v[j + 1], v[j + 2], v[j + 3]);
-          } else {
-            for (int j = 0; j < 32 && nc + j < a.N; ++j) atomicAdd(dst + j, v[j]);
+      store_tile<BN, kTmaStore>(a, &tmC, trow, m0, n0, M, quarter, lane, smem + quarter * (32 * BN * 2), ok);
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  }
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    tmem_dealloc(tmem_base, S::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------- persistent variant
+// One CTA per SM walks the output tiles t = blockIdx.x, blockIdx.x + grid, ... (tile
+// order: N fastest, then M, then the split), so that the producer streams the
+// operands of the next tile while the epilogue warps drain the previous one.  The
+// accumulator is double-buffered in TMEM (2 x BN columns): the MMA thread fills
+// buffer lt & 1 of local tile lt while the epilogue reads the other; acc_full[b] is
+// committed by the MMA thread, acc_empty[b] is arrived by every epilogue warp.
+// The ring of k-block stages continues across tiles.  Store and atomic modes only
+// (the cross-entropy epilogue stays with the one-tile kernel).
+template <int BN>
+struct PSmem {
+  static constexpr int kABytes = BM * BK * 2;
+  static constexpr int kBRows = BN <= 64 ? 64 : BN;
+  static constexpr int kBBytes = kBRows * BK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStageArea = BN % 64 == 0 ? 4 * 32 * BN * 2 : 0;  // TMA-store panels
+  static constexpr int kRingBudget = 218 * 1024 - kStageArea;
+  static constexpr int kStages = kRingBudget / kStageBytes > 8 ? 8 : kRingBudget / kStageBytes;
+  static constexpr int kAccCols = BN <= 32 ? 32 : (BN <= 64 ? 64 : (BN <= 128 ? 128 : 256));
+  static constexpr int kTmemCols = 2 * kAccCols;
+  static constexpr int kBytes = kStages * kStageBytes + kStageArea + 1024 /*align*/;
+  static_assert(kStages >= 2, "persistent GEMM: ring too small");
+};
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+struct TileIdx {
+  int m0, n0, kb0, kb1;
+};
+__device__ __forceinline__ TileIdx decode_tile(int t, int n_tiles, int m_tiles, int BNv, int kb_total, int kb_per) {
+  TileIdx r;
+  const int nt = t % n_tiles;
+  const int rest = t / n_tiles;
+  r.m0 = (rest % m_tiles) * BM;
+  r.n0 = nt * BNv;
+  r.kb0 = (rest / m_tiles) * kb_per;
+  r.kb1 = min(kb_total, r.kb0 + kb_per);
+  return r;
+}
+
+// epilogue warps of the persistent kernel: two per TMEM lane quarter (each drains half
+// the columns) for tiles of 128 columns and more, one otherwise
+template <int BN>
+__host__ __device__ constexpr int p_epi_warps() { return BN % 128 == 0 ? 8 : 4; }
+template <int BN>
+__host__ __device__ constexpr int p_threads() { return 64 + 32 * p_epi_warps<BN>(); }
+
+template <int BN, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(p_threads<BN>(), 1)
+    gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                           const __grid_constant__ CUtensorMap tmC, GemmArgs a) {
+  using S = PSmem<BN>;
+  constexpr int kStages = S::kStages;
+  constexpr bool kTmaStore = BN % 64 == 0;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint64_t full_bar[kStages], empty_bar[kStages], acc_full[2], acc_empty[2];
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+
+  const int M = a.M_dev ? min(*a.M_dev, a.M_cap) : a.M_cap;
+  const int K = a.K_dev ? min(*a.K_dev, a.K_cap) : a.K_cap;
+  const int kb_total = (K + BK - 1) / BK;
+  const int kb_per = (kb_total + a.splits - 1) / a.splits;
+  const int m_tiles = (M + BM - 1) / BM;
+  const int n_tiles = (a.N + BN - 1) / BN;
+  const int tiles = m_tiles * n_tiles * a.splits;
+
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stage_area = smem + kStages * S::kStageBytes;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], p_epi_warps<BN>());
+    }
+    abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) tmem_alloc(&tmem_slot, S::kTmemCols);
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem_base = tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool stop = false;
+      for (int t = blockIdx.x; t < tiles && !stop; t += gridDim.x) {
+        const TileIdx ti = decode_tile(t, n_tiles, m_tiles, BN, kb_total, kb_per);
+        for (int kb = ti.kb0; kb < ti.kb1; ++kb, ++it) {
+          const int s = static_cast<int>(it % kStages);
+          const uint32_t ph = (it / kStages) & 1u;
+          if (it >= static_cast<uint32_t>(kStages) && !mbar_wait(&empty_bar[s], ph ^ 1u, &abort_flag)) {
+            set_error(a.err, kErrMmaTimeout);
+            abort_flag = 1;
+            stop = true;
+            break;
           }
-          continue;
-        }
+          uint8_t* sa = smem + s * S::kStageBytes;
+          uint8_t* sb = sa + S::kABytes;
+          const int kc = kb * BK;
+          mbar_expect_tx(&full_bar[s], S::kABytes + (B_MN ? (BN <= 64 ? 64 : BN) : BN) * BK * 2);
+          if (A_MN) {
+            tma_load_2d(sa, &tmA, &full_bar[s], ti.m0, kc);
+            tma_load_2d(sa + 64 * BK * 2, &tmA, &full_bar[s], ti.m0 + 64, kc);
+          } else {
+            tma_load_2d(sa, &tmA, &full_bar[s], kc, ti.m0);
+          }
+          if (B_MN) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          float x = v[j];
-          if (a.bias && nc + j < a.N) x += a.bias[nc + j];
-          if (a.act == 1) x = fmaxf(x, 0.f);
-          v[j] = x;
-        }
-        if (a.dropout_p > 0.f) {
-          const uint64_t base = static_cast<uint64_t>(m) * static_cast<uint64_t>(a.ldc) + static_cast<uint64_t>(nc);
-#pragma unroll
-          for (int j = 0; j < 32; j += 4) {
-            // one Philox call covers 4 consecutive elements (base + j is a multiple of 4)
-            const U4 r = index_draw4(key, (base + j) >> 2, 0);
-            v[j] = r.x >= thr ? v[j] * keep_scale : 0.f;
-            v[j + 1] = r.y >= thr ? v[j + 1] * keep_scale : 0.f;
-            v[j + 2] = r.z >= thr ? v[j + 2] * keep_scale : 0.f;
-            v[j + 3] = r.w >= thr ? v[j + 3] * keep_scale : 0.f;
+            for (int c = 0; c < (BN + 63) / 64; ++c)
+              tma_load_2d(sb + c * 64 * BK * 2, &tmB, &full_bar[s], ti.n0 + c * 64, kc);
+          } else {
+            tma_load_2d(sb, &tmB, &full_bar[s], kc, ti.n0);
           }
         }
-        if (a.c_mode == kStoreBf16) {
-          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.C) + static_cast<int64_t>(m) * a.ldc + nc;
-          if (nc + 32 <= a.ldc) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 8) *reinterpret_cast<uint4*>(dst + j) = f32_to_bf16x8(v + j);
-          } else {
-            for (int j = 0; j < 32 && nc + j < a.ldc; ++j) dst[j] = __float2bfloat16_rn(v[j]);
-          }
-        } else {
-          float* dst = reinterpret_cast<float*>(a.C) + static_cast<int64_t>(m) * a.ldc + nc;
-          if (nc + 32 <= a.ldc) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-          } else {
-            for (int j = 0; j < 32 && nc + j < a.ldc; ++j) dst[j] = v[j];
+      }
+      // on abort, wait (bounded) until the loads still in flight (the last kStages
+      // issued at most) have landed
+      if (abort_flag) {
+        const uint32_t first = it > static_cast<uint32_t>(kStages) ? it - kStages : 0u;
+        for (uint32_t i = first; i < it; ++i) {
+          const int s = static_cast<int>(i % kStages);
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(&full_bar[s], (i / kStages) & 1u) && globaltimer_ns() - t0 < kWaitNs) {
           }
         }
       }
     }
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc(BM, BN, A_MN, B_MN);
+      uint32_t it = 0;
+      int lt = 0;
+      bool stop = false;
+      for (int t = blockIdx.x; t < tiles && !stop; t += gridDim.x) {
+        const TileIdx ti = decode_tile(t, n_tiles, m_tiles, BN, kb_total, kb_per);
+        if (ti.kb1 <= ti.kb0) continue;
+        const int b = lt & 1;
+        if (lt >= 2 && !mbar_wait(&acc_empty[b], ((lt >> 1) - 1) & 1u, &abort_flag)) {
+          set_error(a.err, kErrMmaTimeout);
+          abort_flag = 1;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * S::kAccCols);
+        for (int kb = ti.kb0; kb < ti.kb1; ++kb, ++it) {
+          const int s = static_cast<int>(it % kStages);
+          if (!mbar_wait(&full_bar[s], (it / kStages) & 1u, &abort_flag)) {
+            set_error(a.err, kErrMmaTimeout);
+            abort_flag = 1;
+            stop = true;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t sa = smem_u32(smem + s * S::kStageBytes);
+          const uint32_t sb = sa + S::kABytes;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t da = A_MN ? umma_desc(sa + kk * 2048, 64 * BK * 2, 1024) : umma_desc(sa + kk * 32, 16, 1024);
+            const uint64_t db = B_MN ? umma_desc(sb + kk * 2048, 64 * BK * 2, 1024) : umma_desc(sb + kk * 32, 16, 1024);
+            umma_f16(d_tmem, da, db, idesc, (kb > ti.kb0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty_bar[s]);
+        }
+        if (stop) break;
+        umma_commit(&acc_full[b]);
+        ++lt;
+      }
+    }
+  } else {
+    // epilogue warps 2 .. 2 + p_epi_warps - 1
+    constexpr int kEpi = p_epi_warps<BN>();
+    constexpr int kCols = BN / (kEpi / 4);  // columns per epilogue warp
+    const int quarter = warp & 3;
+    const int part = (warp - 2) / 4;
+    uint8_t* stage = stage_area + (warp - 2) * (32 * kCols * 2);
+    int lt = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+      const TileIdx ti = decode_tile(t, n_tiles, m_tiles, BN, kb_total, kb_per);
+      if (ti.kb1 <= ti.kb0) continue;
+      const int b = lt & 1;
+      if (!mbar_wait(&acc_full[b], (lt >> 1) & 1u, &abort_flag)) {
+        if (lane == 0) set_error(a.err, kErrMmaTimeout);
+        abort_flag = 1;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t trow = tmem_base + static_cast<uint32_t>(b * S::kAccCols) + (static_cast<uint32_t>(quarter * 32) << 16);
+      store_tile<BN, kTmaStore>(a, &tmC, trow, ti.m0, ti.n0, M, quarter, lane, stage, true, part * kCols,
+                                (part + 1) * kCols);
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
+      ++lt;
+    }
   }
   __syncthreads();
   if (warp == 1) {
@@ -534,6 +766,27 @@ CUtensorMap make_map(const void* ptr, int64_t rows, int64_t cols, int64_t ld, in
   return m;
 }
 
+int sm_count() {
+  static int sms = 0;
+  if (!sms) {
+    int d = 0;
+    cudaGetDevice(&d);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, d);
+    if (sms <= 0) sms = 148;
+  }
+  return sms;
+}
+
+// GRAPPA_GEMM_PERSISTENT=0 selects the one-tile-per-CTA kernel (for comparisons)
+bool persistent_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("GRAPPA_GEMM_PERSISTENT");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
 template <int BN, bool A_MN, bool B_MN>
 void launch_t(const GemmProblem& p, const GemmArgs& a, dim3 grid, cudaStream_t stream) {
   using S = Smem<BN>;
@@ -546,10 +799,24 @@ void launch_t(const GemmProblem& p, const GemmArgs& a, dim3 grid, cudaStream_t s
     if (a.c_rows <= 0) throw std::invalid_argument("bf16 GEMM output needs its row count");
     mc = make_map(a.C, a.c_rows, a.N, a.ldc, 32);
   }
-  auto kern = gemm_kernel<BN, A_MN, B_MN>;
-  static int attr_device = -1;
   int dev = 0;
   GB_CUDA_CHECK(cudaGetDevice(&dev));
+  if (a.c_mode != kCrossEntropy && persistent_enabled()) {
+    using P = PSmem<BN>;
+    auto kern = gemm_persistent_kernel<BN, A_MN, B_MN>;
+    static int attr_device_p = -1;
+    if (attr_device_p != dev) {
+      GB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, P::kBytes));
+      attr_device_p = dev;
+    }
+    const int64_t tiles = static_cast<int64_t>(grid.x) * grid.y * grid.z;
+    const unsigned g = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(tiles, sm_count())));
+    kern<<<g, p_threads<BN>(), P::kBytes, stream>>>(ma, mb, mc, a);
+    GB_LAUNCH_CHECK();
+    return;
+  }
+  auto kern = gemm_kernel<BN, A_MN, B_MN>;
+  static int attr_device = -1;
   if (attr_device != dev) {
     GB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes));
     attr_device = dev;

@@ -103,20 +103,24 @@ __device__ __forceinline__ bool wait_flag(const uint32_t* f, uint32_t tag, const
   return true;
 }
 
-__device__ __forceinline__ void finish4(const ArAdamArgs& a, int64_t i, float4 g, float step_size,
-                                        float inv_sqrt_bc2) {
-  if (!a.do_adam) {
-    *reinterpret_cast<float4*>(a.grad_out + i) = g;
-    return;
-  }
-  float4 p = *reinterpret_cast<const float4*>(a.param + i);
-  float4 m = *reinterpret_cast<const float4*>(a.m + i);
-  float4 v = *reinterpret_cast<const float4*>(a.v + i);
+__device__ __forceinline__ void finish1(const ArAdamArgs& a, int64_t i, float g, float step_size, float inv_sqrt_bc2) {
+  if (a.do_adam) adam_update(a, i, g, step_size, inv_sqrt_bc2);
+  else a.grad_out[i] = g;
+}
+
+// Groups of kArU float4 positions per thread (stride = the CTA's vector width): every
+// load of a group is issued before the first use, so a thread keeps kArU 16-byte
+// requests in flight per peer instead of one (the kernel is bound by the latency of
+// NVLink reads, not by their bandwidth, at one request per thread).
+constexpr int kArU = 4;
+constexpr int kArThreads = 512;  // one CTA per SM; 128 registers for the kArU groups
+
+__device__ __forceinline__ void adam4(const ArAdamArgs& a, float4& p, float4& m, float4& v, const float4& g,
+                                      float step_size, float inv_sqrt_bc2, __nv_bfloat16 (&w)[4]) {
   float* pp = &p.x;
   float* mp = &m.x;
   float* vp = &v.x;
   const float* gp = &g.x;
-  __nv_bfloat16 w[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     float gk = gp[k];
@@ -126,21 +130,49 @@ __device__ __forceinline__ void finish4(const ArAdamArgs& a, int64_t i, float4 g
     pp[k] -= step_size * mp[k] / (sqrtf(vp[k]) * inv_sqrt_bc2 + a.eps);
     w[k] = __float2bfloat16_rn(pp[k]);
   }
-  *reinterpret_cast<float4*>(a.param + i) = p;
-  *reinterpret_cast<float4*>(a.m + i) = m;
-  *reinterpret_cast<float4*>(a.v + i) = v;
-  if (a.param_bf16) *reinterpret_cast<uint2*>(a.param_bf16 + i) = *reinterpret_cast<uint2*>(w);
 }
 
-__device__ __forceinline__ void finish1(const ArAdamArgs& a, int64_t i, float g, float step_size, float inv_sqrt_bc2) {
-  if (a.do_adam) adam_update(a, i, g, step_size, inv_sqrt_bc2);
-  else a.grad_out[i] = g;
+// Adam (or the plain sum) for the full float4 positions i0 + u * stride < hi - 3.
+__device__ __forceinline__ void finish_group(const ArAdamArgs& a, int64_t i0, int64_t stride, int64_t hi,
+                                             const float4 (&g)[kArU], float step_size, float inv_sqrt_bc2) {
+  if (!a.do_adam) {
+#pragma unroll
+    for (int u = 0; u < kArU; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i + 3 < hi) *reinterpret_cast<float4*>(a.grad_out + i) = g[u];
+    }
+    return;
+  }
+  float4 p[kArU], m[kArU], v[kArU];
+#pragma unroll
+  for (int u = 0; u < kArU; ++u) {
+    const int64_t i = i0 + u * stride;
+    if (i + 3 < hi) {
+      p[u] = *reinterpret_cast<const float4*>(a.param + i);
+      m[u] = *reinterpret_cast<const float4*>(a.m + i);
+      v[u] = *reinterpret_cast<const float4*>(a.v + i);
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < kArU; ++u) {
+    const int64_t i = i0 + u * stride;
+    if (i + 3 >= hi) continue;
+    __nv_bfloat16 w[4];
+    adam4(a, p[u], m[u], v[u], g[u], step_size, inv_sqrt_bc2, w);
+    *reinterpret_cast<float4*>(a.param + i) = p[u];
+    *reinterpret_cast<float4*>(a.m + i) = m[u];
+    *reinterpret_cast<float4*>(a.v + i) = v[u];
+    if (a.param_bf16) *reinterpret_cast<uint2*>(a.param_bf16 + i) = *reinterpret_cast<uint2*>(w);
+  }
 }
+
+// The ragged end of a chunk (positions whose float4 would cross hi), element by element.
+__device__ __forceinline__ bool ragged(int64_t i, int64_t hi) { return i < hi && i + 3 >= hi; }
 
 // Work split: CTA b owns chunks b, b + G, b + 2G, ... (G = grid, the same on every
 // rank).  It first publishes all of them, then waits for and reduces each, so the
 // flag round trips over NVLink overlap with the other chunks' traffic.
-__global__ void __launch_bounds__(1024) ar_adam_kernel(ArAdamArgs a) {
+__global__ void __launch_bounds__(kArThreads) ar_adam_kernel(ArAdamArgs a) {
   const int64_t n_chunks = ceil_div(a.n, a.chunk);
   const int64_t step = a.counters[3];
   const int parity = static_cast<int>(step & 1);
@@ -157,6 +189,7 @@ __global__ void __launch_bounds__(1024) ar_adam_kernel(ArAdamArgs a) {
   const float inv_sqrt_bc2 = rsqrtf(bc2);
   float* send = a.send_local[parity];
   const int64_t vec_stride = static_cast<int64_t>(blockDim.x) * 4;
+  const int64_t group_stride = vec_stride * kArU;
   __shared__ int s_timeout;  // sticky: after a timeout the CTA stops waiting and reducing
   if (threadIdx.x == 0) s_timeout = 0;
 
@@ -164,16 +197,25 @@ __global__ void __launch_bounds__(1024) ar_adam_kernel(ArAdamArgs a) {
   for (int64_t j = blockIdx.x; j < n_chunks; j += gridDim.x) {
     const int64_t lo = j * a.chunk;
     const int64_t hi = min(a.n, lo + a.chunk);
-    for (int64_t i = lo + threadIdx.x * 4; i < hi; i += vec_stride) {
-      if (i + 3 < hi) {
-        float4 g = *reinterpret_cast<float4*>(a.grad + i);
-        *reinterpret_cast<float4*>(a.grad + i) = make_float4(0.f, 0.f, 0.f, 0.f);
-        g.x *= scale; g.y *= scale; g.z *= scale; g.w *= scale;
-        *reinterpret_cast<float4*>(send + i) = g;
-      } else {
-        for (int64_t k = i; k < hi; ++k) {
-          send[k] = a.grad[k] * scale;
-          a.grad[k] = 0.f;
+    for (int64_t i0 = lo + threadIdx.x * 4; i0 < hi; i0 += group_stride) {
+      float4 g[kArU];
+#pragma unroll
+      for (int u = 0; u < kArU; ++u) {
+        const int64_t i = i0 + u * vec_stride;
+        if (i + 3 < hi) g[u] = *reinterpret_cast<const float4*>(a.grad + i);
+      }
+#pragma unroll
+      for (int u = 0; u < kArU; ++u) {
+        const int64_t i = i0 + u * vec_stride;
+        if (i + 3 < hi) {
+          *reinterpret_cast<float4*>(a.grad + i) = make_float4(0.f, 0.f, 0.f, 0.f);
+          *reinterpret_cast<float4*>(send + i) = make_float4(g[u].x * scale, g[u].y * scale, g[u].z * scale,
+                                                             g[u].w * scale);
+        } else if (ragged(i, hi)) {
+          for (int64_t k = i; k < hi; ++k) {
+            send[k] = a.grad[k] * scale;
+            a.grad[k] = 0.f;
+          }
         }
       }
     }
@@ -198,23 +240,46 @@ __global__ void __launch_bounds__(1024) ar_adam_kernel(ArAdamArgs a) {
     if (s_timeout) break;
     const int64_t lo = j * a.chunk;
     const int64_t hi = min(a.n, lo + a.chunk);
-    for (int64_t i = lo + threadIdx.x * 4; i < hi; i += vec_stride) {
-      if (i + 3 < hi) {
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int64_t i0 = lo + threadIdx.x * 4; i0 < hi; i0 += group_stride) {
+      float4 acc[kArU];
 #pragma unroll
-        for (int p = 0; p < kMaxRanks; ++p)
-          if (p < a.world) {
-            const float4 x = *reinterpret_cast<const float4*>(a.send_peer[p][parity] + i);
-            acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
+      for (int u = 0; u < kArU; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int p = 0; p < kMaxRanks; ++p) {
+        if (p >= a.world) break;
+        const float* src = a.send_peer[p][parity];
+        float4 x[kArU];
+#pragma unroll
+        for (int u = 0; u < kArU; ++u) {
+          const int64_t i = i0 + u * vec_stride;
+          if (i + 3 < hi) x[u] = *reinterpret_cast<const float4*>(src + i);
+        }
+#pragma unroll
+        for (int u = 0; u < kArU; ++u) {
+          const int64_t i = i0 + u * vec_stride;
+          if (i + 3 < hi) {
+            acc[u].x += x[u].x; acc[u].y += x[u].y; acc[u].z += x[u].z; acc[u].w += x[u].w;
           }
-        if (a.two_shot) *reinterpret_cast<float4*>(send + i) = acc;
-        else finish4(a, i, acc, step_size, inv_sqrt_bc2);
+        }
+      }
+      if (a.two_shot) {
+#pragma unroll
+        for (int u = 0; u < kArU; ++u) {
+          const int64_t i = i0 + u * vec_stride;
+          if (i + 3 < hi) *reinterpret_cast<float4*>(send + i) = acc[u];
+        }
       } else {
+        finish_group(a, i0, vec_stride, hi, acc, step_size, inv_sqrt_bc2);
+      }
+#pragma unroll
+      for (int u = 0; u < kArU; ++u) {
+        const int64_t i = i0 + u * vec_stride;
+        if (!ragged(i, hi)) continue;
         for (int64_t k = i; k < hi; ++k) {
-          float acc = 0.f;
-          for (int p = 0; p < a.world; ++p) acc += a.send_peer[p][parity][k];
-          if (a.two_shot) send[k] = acc;
-          else finish1(a, k, acc, step_size, inv_sqrt_bc2);
+          float s1 = 0.f;
+          for (int p = 0; p < a.world; ++p) s1 += a.send_peer[p][parity][k];
+          if (a.two_shot) send[k] = s1;
+          else finish1(a, k, s1, step_size, inv_sqrt_bc2);
         }
       }
     }
@@ -235,10 +300,20 @@ __global__ void __launch_bounds__(1024) ar_adam_kernel(ArAdamArgs a) {
     const float* red = a.send_peer[j % a.world][parity];
     const int64_t lo = j * a.chunk;
     const int64_t hi = min(a.n, lo + a.chunk);
-    for (int64_t i = lo + threadIdx.x * 4; i < hi; i += vec_stride) {
-      if (i + 3 < hi) finish4(a, i, *reinterpret_cast<const float4*>(red + i), step_size, inv_sqrt_bc2);
-      else
-        for (int64_t k = i; k < hi; ++k) finish1(a, k, red[k], step_size, inv_sqrt_bc2);
+    for (int64_t i0 = lo + threadIdx.x * 4; i0 < hi; i0 += group_stride) {
+      float4 g[kArU];
+#pragma unroll
+      for (int u = 0; u < kArU; ++u) {
+        const int64_t i = i0 + u * vec_stride;
+        if (i + 3 < hi) g[u] = *reinterpret_cast<const float4*>(red + i);
+      }
+      finish_group(a, i0, vec_stride, hi, g, step_size, inv_sqrt_bc2);
+#pragma unroll
+      for (int u = 0; u < kArU; ++u) {
+        const int64_t i = i0 + u * vec_stride;
+        if (ragged(i, hi))
+          for (int64_t k = i; k < hi; ++k) finish1(a, k, red[k], step_size, inv_sqrt_bc2);
+      }
     }
   }
 }
@@ -442,7 +517,7 @@ void launch_allreduce_adam(const ArAdamArgs& a, int grid, cudaStream_t stream) {
   if (grid <= 0) grid = static_cast<int>(std::min<int64_t>(n_chunks, sm_count()));
   grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({static_cast<int64_t>(grid), n_chunks,
                                                                    static_cast<int64_t>(sm_count())})));
-  ar_adam_kernel<<<grid, 1024, 0, stream>>>(a);
+  ar_adam_kernel<<<grid, kArThreads, 0, stream>>>(a);
   GB_LAUNCH_CHECK();
 }
 

@@ -72,6 +72,43 @@ class MiniBatchTrainer:
         counts.copy_(torch.tensor([[max(0, min(B, n - s * B))] for s in range(nb)], dtype=torch.int32))
         return seeds, counts
 
+    # ------------------------------------------------------------------ host feed
+    def _host_buffers(self, slot):
+        """Two pinned [n_batches, B] seed / [n_batches, 1] count buffers (epochs alternate
+        between them) and the pinned per-step loss ring, allocated once."""
+        if getattr(self, "_pinned", None) is None:
+            nb, B = self.n_batches, self.batch_size
+            self._pinned = [(torch.zeros((nb, B), dtype=torch.int32).pin_memory(),
+                             torch.zeros((nb, 1), dtype=torch.int32).pin_memory()) for _ in range(2)]
+            self._ring = torch.zeros(nb, dtype=torch.float32).pin_memory()
+            self._train_ids_host = self.train_ids.cpu()
+            B_, n = self.batch_size, self._train_ids_host.numel()
+            self._host_counts = torch.tensor([[max(0, min(B_, n - s * B_))] for s in range(nb)], dtype=torch.int32)
+        return self._pinned[slot]
+
+    def _fill_host_seeds(self, epoch):
+        """The epoch's shuffled seeds (the same order as ``epoch_seeds``) in its pinned slot."""
+        seeds, counts = self._host_buffers(epoch & 1)
+        ids = self._train_ids_host
+        perm = ids[torch.argsort(shuffle_keys(ids, self.seed, epoch), stable=True)].to(torch.int32)
+        seeds.view(-1)[:perm.numel()].copy_(perm)
+        counts.copy_(self._host_counts)
+        return seeds, counts
+
+    def _host_seeds(self, epoch):
+        fut = getattr(self, "_prefetched", {}).pop(epoch, None)
+        return fut.result() if fut is not None else self._fill_host_seeds(epoch)
+
+    def _prefetch_host_seeds(self, epoch):
+        """Shuffle the next epoch's seeds on a host thread while this epoch runs on the
+        device (its pinned slot is not the one the current epoch's copies read)."""
+        if getattr(self, "_pool", None) is None:
+            from concurrent.futures import ThreadPoolExecutor
+
+            self._pool = ThreadPoolExecutor(max_workers=1)
+            self._prefetched = {}
+        self._prefetched[epoch] = self._pool.submit(self._fill_host_seeds, epoch)
+
     def _maybe_repartition(self, epoch):
         first = self._last_repart is None
         if not first and (epoch % self.repart_every != 0 or epoch == self._last_repart):
@@ -108,15 +145,19 @@ class MiniBatchTrainer:
         self._maybe_repartition(epoch)
         if self._warm:
             self.engine.prepare()
-        seeds, counts = self.epoch_seeds(epoch, on_host=host_feed)
+        if host_feed:
+            seeds, counts = self._host_seeds(epoch)
+        else:
+            seeds, counts = self.epoch_seeds(epoch, on_host=False)
         self.engine.set_epoch(epoch)
         # device -> host read of every step's loss (pinned, asynchronous)
-        ring = torch.zeros(self.n_batches, dtype=torch.float32).pin_memory() if host_feed else None
+        ring = self._ring if host_feed else None
         self.engine.run_epoch(seeds, counts, ring)
         if host_feed:
+            self._prefetch_host_seeds(epoch + 1)
             torch.cuda.current_stream(self.device).synchronize()
-            self.last_losses = ring
-            return float(ring.mean())
+            self.last_losses = ring.clone()
+            return float(self.last_losses.mean())
         return None
 
     def evaluate(self, mask, fanouts=None):
@@ -143,6 +184,9 @@ class MiniBatchTrainer:
             self.engine.wbf.copy_(self.engine.flat)
 
     def close(self):
+        if getattr(self, "_pool", None) is not None:
+            self._pool.shutdown(wait=True)
+            self._pool = None
         self.engine._graph = None
         if self.engine.allreduce is not None:
             self.engine.allreduce.close()

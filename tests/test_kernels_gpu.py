@@ -99,7 +99,9 @@ def run_gemm(A, a_mn, B, b_mn, M_cap, M_dev, N, K_cap, K_dev, splits, C, mode, b
 
 
 @pytest.mark.parametrize("M,K,N,bn", [(300, 208, 256, 256), (1000, 512, 48, 48), (129, 64, 64, 64),
-                                      (257, 200, 128, 128), (5000, 512, 256, 256)])
+                                      (257, 200, 128, 128), (5000, 512, 256, 256),
+                                      # many tiles per persistent CTA, both TMEM buffers in turn
+                                      (40001, 256, 256, 64), (70000, 128, 512, 256), (9000, 64, 48, 48)])
 def test_gemm_kmajor_bias_relu(M, K, N, bn):
     torch.manual_seed(0)
     cap = (M + 127) // 128 * 128 + 128
@@ -130,7 +132,7 @@ def test_gemm_dropout_matches_host_mask():
 
 
 @pytest.mark.parametrize("Mo,Kx,R,live,splits", [(48, 208, 700, 650, 3), (256, 512, 4096, 4000, 8),
-                                                 (256, 208, 130, 100, 1)])
+                                                 (256, 208, 130, 100, 1), (1024, 1024, 8192, 8000, 4)])
 def test_gemm_dw_mn_major_split_k(Mo, Kx, R, live, splits):
     torch.manual_seed(2)
     dY = bf(torch.randn(R, Mo, device=DEV))
