@@ -5,7 +5,10 @@ range named ``prof_step`` (after one eager warm-up step), for kernel captures su
         -o prof python -m grappa_b200.utils.profile_step --workload sage
 
 and, with ``--phases N``, the CUDA-event device time of each step phase (sample,
-forward, backward, update) averaged over N eager steps.  Workloads: 3-layer models
+forward, backward, update) averaged over N eager steps; with ``--graphs N`` the
+device time of N replays of each captured graph: sampling alone, the step without
+and with the next step's sampling on its side stream (the overlap that the
+training loop uses).  Workloads: 3-layer models
 on the ogbn-products-shaped synthetic graph (``--config`` picks another spec),
 1024 seeds per batch, one GPU.
 """
@@ -29,6 +32,7 @@ def main():
     ap.add_argument("--config", default="ogbpr")
     ap.add_argument("--batch", type=int, default=1024)
     ap.add_argument("--phases", type=int, default=0, help="time the phases of this many eager steps")
+    ap.add_argument("--graphs", type=int, default=0, help="time this many replays of each step graph")
     a = ap.parse_args()
     name, hidden, fanouts = WORKLOADS[a.workload]
     dev = torch.device("cuda", 0)
@@ -53,8 +57,37 @@ def main():
     out = {"workload": a.workload, "launches_per_step": eng.launches_per_step, "block_counts": eng.sm.cnt.tolist()}
     if a.phases:
         out["phase_ms"] = eng.time_phases(seeds, counts, a.phases)
-    print(json.dumps(out))
     tr.close()
+    if a.graphs:
+        out["graph_ms"] = time_graphs(model, own, fanouts, a.batch, a.graphs)
+    print(json.dumps(out))
+
+
+def time_graphs(model, own, fanouts, batch, n):
+    tr = MiniBatchTrainer(model, own, fanouts, batch, comm=None, seed=3, use_cuda_graph=True)
+    tr.warmup()
+    eng = tr.engine
+    seeds, counts = tr.epoch_seeds(0, on_host=False)
+    eng.set_epoch(0)
+    eng._load_into(0, seeds[0], counts[0])
+    eng._load_into(1, seeds[1], counts[1])
+    res = {}
+    for name, key in (("sample", ("sample", 0)), ("step_compute_only", ("step", 0, False)),
+                      ("step_with_next_sampling", ("step", 0, True))):
+        g = eng._graph_for(key)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        for _ in range(n):
+            g.replay()
+        a1.record()
+        torch.cuda.synchronize()
+        res[name] = a0.elapsed_time(a1) / n
+    eng.check_errors()
+    tr.close()
+    return res
 
 
 if __name__ == "__main__":
