@@ -68,6 +68,9 @@ __global__ void __launch_bounds__(kThreads) compact_k2(CompactArgs a, const int6
   const int tile = LookBack::ticket(a.scan_scratch, &s_tile);
   const int n_dst = *a.n_dst_ptr;
   const int n_e = *a.n_edges_ptr;
+  // capacity-sized grid: tiles past the last live one leave before the scan
+  const int last_tile = n_e > 0 ? (n_e - 1) / kTile : 0;
+  if (tile > last_tile) return;
   const unsigned long long tw = tag_word(gen, slot);
   const int e0 = tile * kTile + threadIdx.x * kItems;
   int32_t ids[kItems];
@@ -107,7 +110,6 @@ __global__ void __launch_bounds__(kThreads) compact_k2(CompactArgs a, const int6
     }
     ++lid;
   }
-  const int last_tile = n_e > 0 ? (n_e - 1) / kTile : 0;
   if (tile == last_tile && threadIdx.x == 0) {
     long long ns = static_cast<long long>(n_dst) + s_prefix + total;
     if (ns > a.cap_src) ns = a.cap_src;

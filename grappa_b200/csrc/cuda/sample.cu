@@ -79,6 +79,10 @@ __global__ void __launch_bounds__(kThreads) sample_hop_kernel(SampleHopArgs a) {
 
   const int tile = LookBack::ticket(a.scan_scratch, &s_tile);
   const int n_dst = a.n_dst_ptr ? *a.n_dst_ptr : a.n_dst;
+  // the grid is sized by the capacity; tiles past the last live one take no part in
+  // the scan (no live tile waits on them), so they leave at once
+  const int last_tile = n_dst > 0 ? (n_dst - 1) / kTileNodes : 0;
+  if (tile > last_tile) return;
   const int i = tile * kTileNodes + threadIdx.x;
   const bool valid = threadIdx.x < kTileNodes && i < n_dst;
   int32_t nid = -1;
@@ -137,7 +141,6 @@ __global__ void __launch_bounds__(kThreads) sample_hop_kernel(SampleHopArgs a) {
   if (valid) a.out_indptr[i] = static_cast<int32_t>(off < a.cap_edges ? off : a.cap_edges);
   const long long tile_end = s_prefix + total;
   // the tile holding the last destination (or tile 0 when there is none) writes the total
-  const int last_tile = n_dst > 0 ? (n_dst - 1) / kTileNodes : 0;
   if (tile == last_tile && threadIdx.x == 0) {
     if (tile_end > a.cap_edges) set_error(a.err, kErrCapacity);
     const int32_t tot = static_cast<int32_t>(tile_end > a.cap_edges ? a.cap_edges : tile_end);

@@ -40,6 +40,9 @@ __global__ void __launch_bounds__(kThreads) walk_hop_kernel(WalkHopArgs a) {
 
   const int tile = LookBack::ticket(a.scan_scratch, &s_tile);
   const int n_dst = a.n_dst_ptr ? *a.n_dst_ptr : a.n_dst;
+  // capacity-sized grid: tiles past the last live one leave before the scan
+  const int last_tile = n_dst > 0 ? (n_dst - 1) / kTileNodes : 0;
+  if (tile > last_tile) return;
   const int w = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint64_t key = hop_key(static_cast<uint64_t>(a.counters[0]), static_cast<uint64_t>(a.counters[1]),
@@ -111,7 +114,6 @@ __global__ void __launch_bounds__(kThreads) walk_hop_kernel(WalkHopArgs a) {
       }
     }
   }
-  const int last_tile = n_dst > 0 ? (n_dst - 1) / kTileNodes : 0;
   if (tile == last_tile && threadIdx.x == 0) {
     const long long tile_end = s_prefix + total;
     if (tile_end > a.cap_edges) set_error(a.err, kErrCapacity);
