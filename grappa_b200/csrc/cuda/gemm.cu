@@ -548,6 +548,8 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+constexpr int kMinSplitKb = 8;
+
 struct TileIdx {
   int m0, n0, kb0, kb1;
 };
@@ -584,10 +586,15 @@ __global__ void __launch_bounds__(p_threads<BN>(), 1)
   const int M = a.M_dev ? min(*a.M_dev, a.M_cap) : a.M_cap;
   const int K = a.K_dev ? min(*a.K_dev, a.K_cap) : a.K_cap;
   const int kb_total = (K + BK - 1) / BK;
-  const int kb_per = (kb_total + a.splits - 1) / a.splits;
+  // the host sizes the split count by the capacity of the reduction dimension; with
+  // the live length known here, keep at least kMinSplitKb k-blocks per split, so that
+  // the fp32 reductions of the split-K epilogue (one per output element and split)
+  // do not outweigh the MMAs
+  const int splits = max(1, min(a.splits, kb_total / kMinSplitKb));
+  const int kb_per = (kb_total + splits - 1) / splits;
   const int m_tiles = (M + BM - 1) / BM;
   const int n_tiles = (a.N + BN - 1) / BN;
-  const int tiles = m_tiles * n_tiles * a.splits;
+  const int tiles = m_tiles * n_tiles * splits;
 
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stage_area = smem + kStages * S::kStageBytes;

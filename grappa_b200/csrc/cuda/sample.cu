@@ -23,10 +23,10 @@ namespace dev {
 
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
-// destination nodes per CTA: 8 warps share 64 nodes, so that enough warps are in
-// flight to hide the dependent indptr -> indices loads of every node
+// destination nodes per CTA: 16 warps share 64 nodes (four each), so that enough
+// warps are in flight to hide the dependent index gathers of every node
 constexpr int kTileNodes = 64;
 constexpr int kSmemAcc = 64;  // accepted offsets kept in shared memory up to this fanout
 
@@ -72,6 +72,8 @@ __global__ void __launch_bounds__(kThreads) sample_hop_kernel(SampleHopArgs a) {
   __shared__ long long s_off[kTileNodes];
   __shared__ int32_t s_pick[kTileNodes];
   __shared__ int32_t s_nid[kTileNodes];
+  __shared__ long long s_beg[kTileNodes];
+  __shared__ long long s_deg[kTileNodes];
   __shared__ int32_t s_acc[kWarps][kSmemAcc];
   __shared__ int s_tile;
   __shared__ long long s_prefix;
@@ -86,14 +88,15 @@ __global__ void __launch_bounds__(kThreads) sample_hop_kernel(SampleHopArgs a) {
   const int i = tile * kTileNodes + threadIdx.x;
   const bool valid = threadIdx.x < kTileNodes && i < n_dst;
   int32_t nid = -1;
-  int64_t deg = 0;
+  int64_t deg = 0, beg = 0;
   int32_t pick = 0;
   float cov = 0.f, covn = 0.f;
   if (valid) {
     nid = a.dst_nid[i];
     const bool f = a.frontier ? a.frontier[i] != 0 : true;
     if (nid >= 0 && nid < a.n_graph_nodes) {
-      deg = a.indptr[nid + 1] - a.indptr[nid];
+      beg = a.indptr[nid];
+      deg = a.indptr[nid + 1] - beg;
       if (f) {
         if (a.replace)
           pick = deg == 0 ? 0 : (a.fanout < 0 ? static_cast<int32_t>(deg) : a.fanout);
@@ -137,6 +140,8 @@ __global__ void __launch_bounds__(kThreads) sample_hop_kernel(SampleHopArgs a) {
     s_off[threadIdx.x] = off;
     s_pick[threadIdx.x] = pick;
     s_nid[threadIdx.x] = nid;
+    s_beg[threadIdx.x] = beg;
+    s_deg[threadIdx.x] = deg;
   }
   if (valid) a.out_indptr[i] = static_cast<int32_t>(off < a.cap_edges ? off : a.cap_edges);
   const long long tile_end = s_prefix + total;
@@ -162,8 +167,8 @@ __global__ void __launch_bounds__(kThreads) sample_hop_kernel(SampleHopArgs a) {
       continue;
     }
     const int32_t v = s_nid[r];
-    const int64_t beg = a.indptr[v];
-    const int64_t d = a.indptr[v + 1] - beg;
+    const int64_t beg = s_beg[r];  // the node's CSR range, read once in the count phase
+    const int64_t d = s_deg[r];
     int32_t* out = a.out_nbr + o;
     if (!a.replace && k == d) {
       for (int j = lane; j < k; j += 32) out[j] = a.indices[beg + j];

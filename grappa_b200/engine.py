@@ -346,8 +346,15 @@ class BlockEngine:
         self._working = working
         self.labels = labels
         self.gideg = gideg
-        self._graph = None  # pointers may have changed: capture again
-        self._graphs = {}
+        # the captured graphs hold these pointers and sizes; the partition store rebuilds
+        # the working graph in place, so a repartition usually keeps them all and the
+        # graphs stay valid
+        sig = tuple((t.data_ptr(), tuple(t.shape)) if t is not None else None
+                    for t in (working.indptr, working.indices, working.feat, labels, gideg))
+        if sig != getattr(self, "_working_sig", None):
+            self._graph = None  # pointers changed: capture again
+            self._graphs = {}
+        self._working_sig = sig
 
     def set_epoch(self, epoch):
         self.counters[C_EPOCH] = int(epoch)

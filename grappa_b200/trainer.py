@@ -66,7 +66,14 @@ class MiniBatchTrainer:
             ids = self.train_ids
             perm = ids[torch.argsort(shuffle_keys(ids, self.seed, epoch), stable=True)].to(torch.int32)
             seeds = torch.zeros((nb, B), dtype=torch.int32, device=self.device)
-            counts = torch.zeros((nb, 1), dtype=torch.int32, device=self.device)
+            # the per-batch counts never change: uploaded once (a pageable host -> device
+            # copy every epoch would wait for the previous epoch's work to drain)
+            if getattr(self, "_dev_counts", None) is None:
+                n = perm.numel()
+                self._dev_counts = torch.tensor([[max(0, min(B, n - s * B))] for s in range(nb)],
+                                                dtype=torch.int32).to(self.device)
+            seeds.view(-1)[:perm.numel()].copy_(perm)
+            return seeds, self._dev_counts
         n = perm.numel()
         seeds.view(-1)[:n].copy_(perm)
         counts.copy_(torch.tensor([[max(0, min(B, n - s * B))] for s in range(nb)], dtype=torch.int32))

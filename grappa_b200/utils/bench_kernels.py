@@ -60,6 +60,36 @@ def gemm_case(M, K, N, bn=None, p=0.0):
             "ours_frac_of_bf16_peak": flops / (t_ours * 1e-3) / 1e12 / BF16_TFLOPS}
 
 
+def dw_case(live, cap, M, N):
+    """Split-K weight gradient gW[M, N] += dY^T X over the live rows of capacity-sized
+    operands (dY [cap, M], X [cap, N], both MN-major), as in the training step."""
+    from grappa_b200.engine import split_k
+
+    cu = _native.cuda()
+    dev = torch.device("cuda", 0)
+    dY = torch.zeros(cap, M, device=dev, dtype=torch.bfloat16)
+    X = torch.zeros(cap, N, device=dev, dtype=torch.bfloat16)
+    dY[:live] = torch.randn(live, M, device=dev).to(torch.bfloat16)
+    X[:live] = torch.randn(live, N, device=dev).to(torch.bfloat16)
+    gW = torch.zeros(M, N, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    kdev = torch.tensor([live], dtype=torch.int32, device=dev)
+    n_tiles = math.ceil(M / 128) * math.ceil(N / 256)
+    splits = split_k(cap, n_tiles)
+
+    def ours():
+        cu.gemm(dY, True, X, True, M, None, N, cap, kdev, splits, gW, 2, None, 0, 0.0, None, 0, None, 0, None, None,
+                None, None, None, None, err, 256)
+
+    def torch_ref():
+        gW.add_(dY[:live].t() @ X[:live])
+
+    t_ours, t_ref = _time(ours), _time(torch_ref)
+    assert int(err.item()) == 0
+    return {"bench": "gemm_dw_split_k", "live_rows": live, "cap_rows": cap, "M": M, "N": N, "splits_host": splits,
+            "ours_ms": t_ours, "torch_ms": t_ref}
+
+
 def aggregate_case(n_dst, n_src, deg, dim):
     cu = _native.cuda()
     dev = torch.device("cuda", 0)
@@ -86,6 +116,8 @@ def main():
     rows = [gemm_case(int(20853 * s), 208, 256), gemm_case(int(20853 * s), 208, 256, p=0.5),
             gemm_case(int(3250 * s), 512, 256), gemm_case(int(139058 * s), 104, 256),
             gemm_case(65536, 256, 256), gemm_case(131072, 1024, 1024)]
+    rows += [dw_case(int(20853 * s), int(180224 * s), 256, 208), dw_case(int(3250 * s), int(16384 * s), 256, 512),
+             dw_case(int(1021 * s), int(1024 * s), 48, 512)]
     rows += [aggregate_case(int(20853 * s), int(133975 * s), 14, 104), aggregate_case(int(3250 * s), int(20853 * s), 8, 256)]
     for r in rows:
         print(json.dumps(r), flush=True)
