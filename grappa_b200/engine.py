@@ -1086,9 +1086,14 @@ class FusedAllReduceAdam:
 
     One-shot for small buffers (every rank reads all W copies: lowest latency) and
     two-shot for large ones at W > 2 (owner-reduce then owner-broadcast: 2 (W-1)/W of
-    the bytes per rank).  ``two_shot`` forces the choice; None picks by size."""
+    the bytes per rank).  ``two_shot`` forces the choice; None picks by size: on four
+    B200s one-shot is faster up to 4 MB (37 vs 48 us at 1 MB) and even at 16 MB, two-shot
+    from 64 MB (405 vs 471 us); with eight ranks one-shot reads twice the peer bytes,
+    so the crossover is taken four times lower."""
 
-    TWO_SHOT_BYTES = 1 << 20
+    @staticmethod
+    def two_shot_bytes(world):
+        return (16 << 20) if world <= 4 else (4 << 20)
 
     def __init__(self, comm, n, chunk=None, timeout_s=30.0, two_shot=None):
         from grappa_b200.parallel.comm import PeerBuffer
@@ -1097,7 +1102,7 @@ class FusedAllReduceAdam:
         self.n = int(n)
         W = comm.world
         if two_shot is None:
-            two_shot = W > 2 and self.n * 4 >= self.TWO_SHOT_BYTES
+            two_shot = W > 2 and self.n * 4 >= self.two_shot_bytes(W)
         self.two_shot = bool(two_shot) and W > 1
         if chunk is None:
             # enough chunks to keep every SM busy, 16 KB at least, 1 MB at most
