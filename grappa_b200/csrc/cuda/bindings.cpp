@@ -466,7 +466,7 @@ void peer_copy(int64_t dst, int64_t src, int64_t bytes) {
 }
 
 void a2a_pull(std::vector<int64_t> src, std::vector<int64_t> src_off, std::vector<int64_t> len,
-              std::vector<int64_t> dst_off, int64_t dst) {
+              std::vector<int64_t> dst_off, int64_t dst, int64_t first) {
   namespace pe = grappa::peer;
   const size_t w = src.size();
   TORCH_CHECK(w >= 1 && w <= static_cast<size_t>(pe::kMaxRanks) && src_off.size() == w && len.size() == w &&
@@ -481,6 +481,8 @@ void a2a_pull(std::vector<int64_t> src, std::vector<int64_t> src_off, std::vecto
     a.dst_off[p] = dst_off[p];
   }
   a.dst = as_ptr<uint8_t>(dst);
+  TORCH_CHECK(first >= 0 && first < static_cast<int64_t>(w), "a2a_pull: first segment out of range");
+  a.first = static_cast<int32_t>(first);
   pe::launch_a2a_pull(a, stream());
 }
 
@@ -893,7 +895,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("flags2_peer") = std::vector<int64_t>{});
   m.def("pull_rows", &pull_rows);
   m.def("peer_copy", &peer_copy);
-  m.def("a2a_pull", &a2a_pull);
+  m.def("a2a_pull", &a2a_pull, py::arg("src"), py::arg("src_off"), py::arg("len"), py::arg("dst_off"), py::arg("dst"),
+        py::arg("first") = 0);
   m.def("peer_barrier", &peer_barrier);
   m.def("mark_ids", &mark_ids);
   m.def("iota_map", &iota_map);

@@ -346,9 +346,14 @@ __global__ void copy_kernel(uint4* dst, const uint4* src, int64_t n16) {
 // so that the NVLink round trips are hidden without a large grid.
 __global__ void a2a_pull_kernel(A2aArgs a) {
   constexpr int kUnroll = 8;
+  // segments in pull order: peer (first + j) % world is the j-th
   int64_t pre[kMaxRanks + 1];
+  int seg[kMaxRanks];
   pre[0] = 0;
-  for (int p = 0; p < a.world; ++p) pre[p + 1] = pre[p] + (a.len[p] >> 4);
+  for (int j = 0; j < a.world; ++j) {
+    seg[j] = (a.first + j) % a.world;
+    pre[j + 1] = pre[j] + (a.len[seg[j]] >> 4);
+  }
   const int64_t total = pre[a.world];
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; base < total;
@@ -360,9 +365,10 @@ __global__ void a2a_pull_kernel(A2aArgs a) {
       const int64_t i = base + u * stride;
       d[u] = nullptr;
       if (i < total) {
-        int p = 0;
-        while (i >= pre[p + 1]) ++p;
-        const int64_t k = i - pre[p];
+        int j = 0;
+        while (i >= pre[j + 1]) ++j;
+        const int64_t k = i - pre[j];
+        const int p = seg[j];
         v[u] = reinterpret_cast<const uint4*>(a.src[p] + a.src_off[p])[k];
         d[u] = reinterpret_cast<uint4*>(a.dst + a.dst_off[p]) + k;
       }

@@ -84,6 +84,10 @@ struct A2aArgs {
   int64_t dst_off[kMaxRanks] = {};
   uint8_t* dst = nullptr;
   int32_t world = 1;
+  // segment the pull starts with; the others follow in rotation.  With first =
+  // (rank + 1) % world every rank reads a different peer at any one time, so that
+  // no rank's outbound NVLink serves all readers at once while the others idle.
+  int32_t first = 0;
 };
 void launch_a2a_pull(const A2aArgs& a, cudaStream_t stream);
 

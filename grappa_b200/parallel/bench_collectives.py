@@ -156,7 +156,7 @@ def bench_alltoall(comm, dev, edge_counts, iters):
 
         def run_pull():
             cu.peer_barrier(r, W, flags.local, fl, epoch, int(10e9), err)
-            cu.a2a_pull(list(sbuf.ptrs), src_off, recv_sizes, dst_off, recv.data_ptr())
+            cu.a2a_pull(list(sbuf.ptrs), src_off, recv_sizes, dst_off, recv.data_ptr(), (r + 1) % W)
             cu.peer_barrier(r, W, flags.local, fl, epoch, int(10e9), err)
 
         row = {"bench": "repartition_alltoall", "world": W, "edges_per_gpu": E, "bytes_sent_per_gpu": send_total}
