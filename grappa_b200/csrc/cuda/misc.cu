@@ -27,6 +27,30 @@ int grid_1d(int64_t n, int threads, int per_sm = 8) {
 }
 
 // ---------------------------------------------------------------- act_bwd
+// One row chunk of act_bwd: g = dh * scale, masked by h > 0 when h is given (ReLU),
+// rounded to bf16 (the value the GEMMs consume), accumulated into colsum.
+__device__ __forceinline__ uint4 act_bwd_chunk(const ActBwdArgs& a, const float4& d0, const float4& d1, const uint4& hv,
+                                              float (&colsum)[8]) {
+  float g[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+  if (a.h) {
+    float h[8];
+    bf16x8_to_f32(hv, h);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) g[j] = h[j] != 0.f ? g[j] * a.scale : 0.f;
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) g[j] *= a.scale;
+  }
+  const uint4 packed = f32_to_bf16x8(g);
+  bf16x8_to_f32(packed, g);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) colsum[j] += g[j];
+  return packed;
+}
+
+// Two rows per iteration with both rows' loads issued first: the kernel streams dH
+// (fp32, cleared for the next step), H and dY once and is bound by the latency of
+// those loads at one row in flight per thread.
 __global__ void act_bwd_kernel(ActBwdArgs a, int chunks) {
   extern __shared__ float s_col[];  // [blockDim.x * 8]
   const int n = a.n_ptr ? *a.n_ptr : a.n;
@@ -34,35 +58,35 @@ __global__ void act_bwd_kernel(ActBwdArgs a, int chunks) {
   const int c = threadIdx.x % chunks;
   const int r_in = threadIdx.x / chunks;
   const int tail = static_cast<int>(ceil_div(n, 64) * 64);
-  const int rows_end = std::min(tail, a.cap_rows > 0 ? a.cap_rows : tail);
+  const int rows_end = min(tail, a.cap_rows > 0 ? a.cap_rows : tail);
+  const int rstride = gridDim.x * rpb;
   float colsum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  for (int r = blockIdx.x * rpb + r_in; r < rows_end; r += gridDim.x * rpb) {
-    float g[8];
-    if (r < n) {
-      float* dh = a.dh + static_cast<int64_t>(r) * a.dh_stride + c * 8;
-      const float4 d0 = *reinterpret_cast<float4*>(dh);
-      const float4 d1 = *reinterpret_cast<float4*>(dh + 4);
-      *reinterpret_cast<float4*>(dh) = make_float4(0.f, 0.f, 0.f, 0.f);
-      *reinterpret_cast<float4*>(dh + 4) = make_float4(0.f, 0.f, 0.f, 0.f);
-      g[0] = d0.x; g[1] = d0.y; g[2] = d0.z; g[3] = d0.w;
-      g[4] = d1.x; g[5] = d1.y; g[6] = d1.z; g[7] = d1.w;
-      if (a.h) {
-        float hv[8];
-        bf16x8_to_f32(*reinterpret_cast<const uint4*>(a.h + static_cast<int64_t>(r) * a.h_stride + c * 8), hv);
+  for (int r0 = blockIdx.x * rpb + r_in; r0 < rows_end; r0 += 2 * rstride) {
+    const int rr[2] = {r0, r0 + rstride};
+    float4 d[2][2];
+    uint4 hv[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
 #pragma unroll
-        for (int j = 0; j < 8; ++j) g[j] = hv[j] != 0.f ? g[j] * a.scale : 0.f;
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) g[j] *= a.scale;
+    for (int k = 0; k < 2; ++k) {
+      d[k][0] = d[k][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (rr[k] < n) {
+        const float* dh = a.dh + static_cast<int64_t>(rr[k]) * a.dh_stride + c * 8;
+        d[k][0] = *reinterpret_cast<const float4*>(dh);
+        d[k][1] = *reinterpret_cast<const float4*>(dh + 4);
+        if (a.h) hv[k] = *reinterpret_cast<const uint4*>(a.h + static_cast<int64_t>(rr[k]) * a.h_stride + c * 8);
       }
-      // the bias gradient uses the bf16-rounded value that the GEMMs consume
-      const uint4 packed = f32_to_bf16x8(g);
-      bf16x8_to_f32(packed, g);
+    }
 #pragma unroll
-      for (int j = 0; j < 8; ++j) colsum[j] += g[j];
-      *reinterpret_cast<uint4*>(a.dy + static_cast<int64_t>(r) * a.dy_stride + c * 8) = packed;
-    } else {
-      *reinterpret_cast<uint4*>(a.dy + static_cast<int64_t>(r) * a.dy_stride + c * 8) = make_uint4(0, 0, 0, 0);
+    for (int k = 0; k < 2; ++k) {
+      const int r = rr[k];
+      if (r >= rows_end) continue;
+      uint4 out = make_uint4(0, 0, 0, 0);
+      if (r < n) {
+        float* dh = a.dh + static_cast<int64_t>(r) * a.dh_stride + c * 8;
+        *reinterpret_cast<float4*>(dh) = make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(dh + 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+        out = act_bwd_chunk(a, d[k][0], d[k][1], hv[k], colsum);
+      }
+      *reinterpret_cast<uint4*>(a.dy + static_cast<int64_t>(r) * a.dy_stride + c * 8) = out;
     }
   }
   if (!a.dbias) return;
@@ -196,6 +220,20 @@ __global__ void dropout_mask_kernel(uint8_t* mask, int64_t rows, int64_t cols, i
 // ---------------------------------------------------------------- Adam
 // Same update as torch.optim.Adam (no amsgrad): m = b1 m + (1-b1) g,
 // v = b2 v + (1-b2) g^2, p -= lr/bc1 * m / (sqrt(v)/sqrt(bc2) + eps).
+__device__ __forceinline__ float adam_elem(const AdamArgs& a, float g, float& p, float& m, float& v, float step_size,
+                                           float inv_sqrt_bc2) {
+  if (a.weight_decay != 0.f) g += a.weight_decay * p;
+  m = a.beta1 * m + (1.f - a.beta1) * g;
+  v = a.beta2 * v + (1.f - a.beta2) * g * g;
+  p -= step_size * m / (sqrtf(v) * inv_sqrt_bc2 + a.eps);
+  return p;
+}
+
+// VEC: four elements per thread with 16-byte loads, all issued before the
+// arithmetic (the update is one streaming pass over g, p, m and v); the elements
+// past the last multiple of four, and buffers that are not 16-byte aligned, take the
+// scalar path.
+template <bool VEC>
 __global__ void adam_kernel(AdamArgs a) {
   const float t = static_cast<float>(*a.step + 1);
   const float bc1 = 1.f - powf(a.beta1, t);
@@ -203,17 +241,39 @@ __global__ void adam_kernel(AdamArgs a) {
   const float step_size = a.lr / bc1;
   const float inv_sqrt_bc2 = rsqrtf(bc2);
   const float gs = a.grad_scale * (a.grad_scale_dev ? *a.grad_scale_dev : 1.f);
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < a.n;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    float g = a.grad[i] * gs;
+  const int64_t tid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  const int64_t nthreads = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  int64_t scalar_from = 0;
+  if (VEC) {
+    const int64_t n4 = a.n / 4;
+    scalar_from = n4 * 4;
+    for (int64_t q = tid; q < n4; q += nthreads) {
+      float4 g = reinterpret_cast<const float4*>(a.grad)[q];
+      float4 p = reinterpret_cast<const float4*>(a.param)[q];
+      float4 m = reinterpret_cast<const float4*>(a.m)[q];
+      float4 v = reinterpret_cast<const float4*>(a.v)[q];
+      if (a.clear_grad) reinterpret_cast<float4*>(a.grad)[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+      adam_elem(a, g.x * gs, p.x, m.x, v.x, step_size, inv_sqrt_bc2);
+      adam_elem(a, g.y * gs, p.y, m.y, v.y, step_size, inv_sqrt_bc2);
+      adam_elem(a, g.z * gs, p.z, m.z, v.z, step_size, inv_sqrt_bc2);
+      adam_elem(a, g.w * gs, p.w, m.w, v.w, step_size, inv_sqrt_bc2);
+      reinterpret_cast<float4*>(a.param)[q] = p;
+      reinterpret_cast<float4*>(a.m)[q] = m;
+      reinterpret_cast<float4*>(a.v)[q] = v;
+      if (a.param_bf16) {
+        __nv_bfloat16 w[4] = {__float2bfloat16_rn(p.x), __float2bfloat16_rn(p.y), __float2bfloat16_rn(p.z),
+                              __float2bfloat16_rn(p.w)};
+        reinterpret_cast<uint2*>(a.param_bf16)[q] = *reinterpret_cast<uint2*>(w);
+      }
+    }
+  }
+  for (int64_t i = scalar_from + tid; i < a.n; i += nthreads) {
+    const float g = a.grad[i] * gs;
     if (a.clear_grad) a.grad[i] = 0.f;
-    float p = a.param[i];
-    if (a.weight_decay != 0.f) g += a.weight_decay * p;
-    const float m = a.beta1 * a.m[i] + (1.f - a.beta1) * g;
-    const float v = a.beta2 * a.v[i] + (1.f - a.beta2) * g * g;
+    float p = a.param[i], m = a.m[i], v = a.v[i];
+    adam_elem(a, g, p, m, v, step_size, inv_sqrt_bc2);
     a.m[i] = m;
     a.v[i] = v;
-    p -= step_size * m / (sqrtf(v) * inv_sqrt_bc2 + a.eps);
     a.param[i] = p;
     if (a.param_bf16) a.param_bf16[i] = __float2bfloat16_rn(p);
   }
@@ -314,7 +374,13 @@ void launch_dropout_mask(uint8_t* mask, int64_t rows, int64_t cols, int64_t ld, 
 }
 
 void launch_adam(const AdamArgs& a, cudaStream_t stream) {
-  adam_kernel<<<grid_1d(a.n, 256, 4), 256, 0, stream>>>(a);
+  const bool vec = ((reinterpret_cast<uintptr_t>(a.grad) | reinterpret_cast<uintptr_t>(a.param) |
+                     reinterpret_cast<uintptr_t>(a.m) | reinterpret_cast<uintptr_t>(a.v)) & 15u) == 0 &&
+                   (reinterpret_cast<uintptr_t>(a.param_bf16) & 7u) == 0;
+  if (vec)
+    adam_kernel<true><<<grid_1d((a.n + 3) / 4, 256, 4), 256, 0, stream>>>(a);
+  else
+    adam_kernel<false><<<grid_1d(a.n, 256, 4), 256, 0, stream>>>(a);
   GB_LAUNCH_CHECK();
 }
 
