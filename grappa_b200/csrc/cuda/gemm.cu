@@ -502,11 +502,15 @@ __global__ void __launch_bounds__(kThreads, 2)
           }
         }
       }
-      if (live) {
-        atomicAdd(a.loss_sum, loss * inv_n);
-        if (arg == y) atomicAdd(a.correct, 1);
-        if (a.pred_out) a.pred_out[m] = arg;
+      // loss and correct count reduced over the warp's 32 rows first: one atomic per
+      // warp instead of one per row on the same two words
+      const float lsum = warp_sum(live ? loss * inv_n : 0.f);
+      const int csum = __popc(__ballot_sync(0xffffffffu, live && arg == y));
+      if (lane == 0) {
+        if (lsum != 0.f) atomicAdd(a.loss_sum, lsum);
+        if (csum) atomicAdd(a.correct, csum);
       }
+      if (live && a.pred_out) a.pred_out[m] = arg;
      }
     } else {
       store_tile<BN, kTmaStore>(a, &tmC, trow, m0, n0, M, quarter, lane, smem + quarter * (32 * BN * 2), ok);
