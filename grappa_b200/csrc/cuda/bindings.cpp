@@ -56,7 +56,7 @@ int num_sms() {
 void sample_hop(Tensor indptr, Tensor indices, Tensor dst_nid, OptT n_dst_dev, int64_t n_dst, OptT frontier,
                 int64_t fanout, bool replace, Tensor counters, int64_t hop, OptT gideg, OptT cov_accum,
                 Tensor out_indptr, Tensor out_nbr, Tensor n_edges_out, Tensor scan_scratch, Tensor err,
-                int64_t cap_dst) {
+                int64_t cap_dst, OptT map, OptT src_nid, OptT src_sampled) {
   c10::cuda::CUDAGuard g(indptr.device());
   d::SampleHopArgs a;
   a.indptr = ptr<int64_t>(indptr, at::kLong, "indptr");
@@ -83,6 +83,15 @@ void sample_hop(Tensor indptr, Tensor indices, Tensor dst_nid, OptT n_dst_dev, i
   TORCH_CHECK(!a.frontier || frontier->numel() >= cap_dst, "frontier smaller than cap_dst");
   TORCH_CHECK(!a.gideg || gideg->numel() >= cap_dst, "gideg smaller than cap_dst");
   TORCH_CHECK(scan_scratch.numel() >= d::sample_scan_scratch_words(static_cast<int>(cap_dst)), "scan_scratch too small");
+  if (map.has_value()) {
+    TORCH_CHECK(src_nid.has_value() && src_sampled.has_value(), "fused compaction needs map, src_nid and src_sampled");
+    TORCH_CHECK(counters.numel() >= 6 && hop >= 0 && hop < 16, "fused compaction: counters[4] and hop slot");
+    a.map = reinterpret_cast<unsigned long long*>(ptr<int64_t>(*map, at::kLong, "map"));
+    a.map_nodes = map->numel();
+    a.src_nid = ptr<int32_t>(*src_nid, at::kInt, "src_nid");
+    a.src_sampled = ptr<uint8_t>(*src_sampled, at::kByte, "src_sampled");
+    TORCH_CHECK(src_nid->numel() >= cap_dst && src_sampled->numel() >= cap_dst, "src buffers smaller than cap_dst");
+  }
   d::launch_sample_hop(a, static_cast<int>(cap_dst), stream());
 }
 
@@ -91,7 +100,7 @@ int64_t compact_scratch_words(int64_t cap_e) { return d::compact_scan_scratch_wo
 
 void compact(Tensor dst_nid, Tensor n_dst_dev, Tensor nbr, Tensor n_edges_dev, Tensor map, Tensor src_nid,
              Tensor src_sampled, Tensor indices, Tensor n_src_out, Tensor scan_scratch, Tensor err, int64_t cap_dst,
-             int64_t cap_edges, Tensor counters, int64_t slot) {
+             int64_t cap_edges, Tensor counters, int64_t slot, bool k1_done) {
   c10::cuda::CUDAGuard g(dst_nid.device());
   TORCH_CHECK(slot >= 0 && slot < 16, "slot must be in [0, 16)");
   TORCH_CHECK(counters.numel() >= 6, "counters needs 6 entries");
@@ -114,7 +123,7 @@ void compact(Tensor dst_nid, Tensor n_dst_dev, Tensor nbr, Tensor n_edges_dev, T
   TORCH_CHECK(scan_scratch.numel() >= d::compact_scan_scratch_words(static_cast<int>(cap_edges)), "scan_scratch too small");
   const int64_t* gen = ptr<int64_t>(counters, at::kLong, "counters") + 4;
   d::launch_compact(a, static_cast<int>(cap_dst), static_cast<int>(cap_edges), gen, static_cast<int>(slot), num_sms(),
-                    stream());
+                    stream(), k1_done);
 }
 
 // --------------------------------------------------------------------------- GEMM
@@ -841,9 +850,16 @@ void walk_hop(Tensor indptr, Tensor indices, Tensor dst_nid, OptT n_dst_dev, int
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "grappa_b200 sm_100a kernels";
-  m.def("sample_hop", &sample_hop);
+  m.def("sample_hop", &sample_hop, py::arg("indptr"), py::arg("indices"), py::arg("dst_nid"), py::arg("n_dst_dev"),
+        py::arg("n_dst"), py::arg("frontier"), py::arg("fanout"), py::arg("replace"), py::arg("counters"),
+        py::arg("hop"), py::arg("gideg"), py::arg("cov_accum"), py::arg("out_indptr"), py::arg("out_nbr"),
+        py::arg("n_edges_out"), py::arg("scan_scratch"), py::arg("err"), py::arg("cap_dst"),
+        py::arg("map") = py::none(), py::arg("src_nid") = py::none(), py::arg("src_sampled") = py::none());
   m.def("sample_scratch_words", &sample_scratch_words);
-  m.def("compact", &compact);
+  m.def("compact", &compact, py::arg("dst_nid"), py::arg("n_dst_dev"), py::arg("nbr"), py::arg("n_edges_dev"),
+        py::arg("map"), py::arg("src_nid"), py::arg("src_sampled"), py::arg("indices"), py::arg("n_src_out"),
+        py::arg("scan_scratch"), py::arg("err"), py::arg("cap_dst"), py::arg("cap_edges"), py::arg("counters"),
+        py::arg("slot"), py::arg("k1_done") = false);
   m.def("compact_scratch_words", &compact_scratch_words);
   m.def("gemm", &gemm);
   m.def("aggregate", &aggregate, py::arg("indptr"), py::arg("indices"), py::arg("n_dst_dev"), py::arg("n_dst"),

@@ -143,6 +143,14 @@ struct LookBack {
   }
 };
 
+// Tag word of one block compaction (compact.cu): derived on the device from the
+// generation counter *gen and the hop slot, decreasing from call to call, so that a
+// captured CUDA graph draws fresh tags on every replay.
+__device__ __forceinline__ unsigned long long compact_tag_word(const int64_t* gen, int slot) {
+  const uint32_t tag = 0xFFFFFFFFu - static_cast<uint32_t>(static_cast<uint64_t>(*gen) * 16u + static_cast<uint32_t>(slot));
+  return static_cast<unsigned long long>(tag) << 32;
+}
+
 // bf16x8 <-> float helpers for 16-byte vector access.
 __device__ __forceinline__ void bf16x8_to_f32(const uint4& u, float* f) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);

@@ -15,6 +15,8 @@
 //       look-back scan of those flags gives new local ids n_dst + rank;
 //       map[nbr[e]] = tag|lid, src_nid[lid] = nbr[e]
 //   K3  indices[e] = low32(map[nbr[e]]); src_sampled[indices[e]] = 1
+// The neighbour sampler can do K1's work as it writes the block (SampleHopArgs.map):
+// the compaction then starts at K2 (k1_done).
 // A first-appearance test in K2 can never see a rewritten entry as its own value:
 // a rewritten entry holds a local id <= n_dst + e0 < n_dst + e for any later e.
 #include "common.cuh"
@@ -31,11 +33,8 @@ constexpr int kThreads = 256;
 constexpr int kItems = 4;  // edges per thread in K2
 constexpr int kTile = kThreads * kItems;
 
-// Tag of this call: derived on the device from the generation counter so that a
-// captured CUDA graph keeps drawing fresh tags on every replay.
 __device__ __forceinline__ unsigned long long tag_word(const int64_t* gen, int slot) {
-  const uint32_t tag = 0xFFFFFFFFu - static_cast<uint32_t>(static_cast<uint64_t>(*gen) * 16u + static_cast<uint32_t>(slot));
-  return static_cast<unsigned long long>(tag) << 32;
+  return compact_tag_word(gen, slot);
 }
 
 __global__ void __launch_bounds__(kThreads) compact_k1(CompactArgs a, const int64_t* gen, int slot) {
@@ -137,12 +136,14 @@ int compact_scan_scratch_words(int cap_edges) {
 }
 
 void launch_compact(const CompactArgs& a, int cap_dst, int cap_edges, const int64_t* gen, int slot, int num_sms,
-                    cudaStream_t stream) {
+                    cudaStream_t stream, bool k1_done) {
   const int grid_stride = num_sms * 8;
-  const long long work1 = static_cast<long long>(cap_dst) + cap_edges;
-  const int g1 = static_cast<int>(std::min<long long>(grid_stride, ceil_div(work1 > 0 ? work1 : 1, kThreads)));
-  compact_k1<<<g1, kThreads, 0, stream>>>(a, gen, slot);
-  GB_LAUNCH_CHECK();
+  if (!k1_done) {
+    const long long work1 = static_cast<long long>(cap_dst) + cap_edges;
+    const int g1 = static_cast<int>(std::min<long long>(grid_stride, ceil_div(work1 > 0 ? work1 : 1, kThreads)));
+    compact_k1<<<g1, kThreads, 0, stream>>>(a, gen, slot);
+    GB_LAUNCH_CHECK();
+  }
   const int tiles = static_cast<int>(ceil_div(cap_edges > 0 ? cap_edges : 1, kTile));
   GB_CUDA_CHECK(cudaMemsetAsync(a.scan_scratch, 0, sizeof(unsigned long long) * (tiles + 1), stream));
   compact_k2<<<tiles, kThreads, 0, stream>>>(a, gen, slot);

@@ -30,6 +30,14 @@ struct SampleHopArgs {
   int32_t* n_edges_out = nullptr;
   unsigned long long* scan_scratch = nullptr;
   int32_t* err = nullptr;
+  // optional: the first pass of the block compaction (compact.cu K1) fused into the
+  // hop — map[dst_nid[i]] and map[out_nbr[e]] take the atomicMin of this call's tag
+  // word (from counters[4] and slot = hop) with positions i and n_dst + e, and
+  // src_nid[i] = dst_nid[i], src_sampled[i] = 0 for the destinations
+  unsigned long long* map = nullptr;   // dense [map_nodes]
+  int64_t map_nodes = 0;
+  int32_t* src_nid = nullptr;
+  uint8_t* src_sampled = nullptr;
 };
 void launch_sample_hop(const SampleHopArgs& a, int cap_dst, cudaStream_t stream);
 int sample_scan_scratch_words(int cap_dst);
@@ -78,7 +86,7 @@ struct CompactArgs {
 // gen: device generation counter; tags are derived on the device from (*gen, slot)
 // so that a captured graph keeps drawing fresh tags (slot < 16 per generation).
 void launch_compact(const CompactArgs& a, int cap_dst, int cap_edges, const int64_t* gen, int slot, int num_sms,
-                    cudaStream_t stream);
+                    cudaStream_t stream, bool k1_done = false);
 int compact_scan_scratch_words(int cap_edges);
 
 // ---------------------------------------------------------------- GEMM

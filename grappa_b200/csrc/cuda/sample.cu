@@ -91,8 +91,14 @@ __global__ void __launch_bounds__(kThreads) sample_hop_kernel(SampleHopArgs a) {
   int64_t deg = 0, beg = 0;
   int32_t pick = 0;
   float cov = 0.f, covn = 0.f;
+  const unsigned long long tw = a.map ? compact_tag_word(a.counters + 4, a.hop) : 0ull;
   if (valid) {
     nid = a.dst_nid[i];
+    if (a.map) {  // compaction K1 for the destinations
+      a.src_nid[i] = nid;
+      a.src_sampled[i] = 0;
+      if (nid >= 0 && nid < a.map_nodes) atomicMin(a.map + nid, tw | static_cast<unsigned long long>(i));
+    }
     const bool f = a.frontier ? a.frontier[i] != 0 : true;
     if (nid >= 0 && nid < a.n_graph_nodes) {
       beg = a.indptr[nid];
@@ -170,19 +176,25 @@ __global__ void __launch_bounds__(kThreads) sample_hop_kernel(SampleHopArgs a) {
     const int64_t beg = s_beg[r];  // the node's CSR range, read once in the count phase
     const int64_t d = s_deg[r];
     int32_t* out = a.out_nbr + o;
+    // edge o + j gets neighbour u (and, fused compaction K1, map[u] its position)
+    auto emit = [&](int j, int32_t u) {
+      out[j] = u;
+      if (a.map && u >= 0 && u < a.map_nodes)
+        atomicMin(a.map + u, tw | static_cast<unsigned long long>(static_cast<long long>(n_dst) + o + j));
+    };
     if (!a.replace && k == d) {
-      for (int j = lane; j < k; j += 32) out[j] = a.indices[beg + j];
+      for (int j = lane; j < k; j += 32) emit(j, a.indices[beg + j]);
     } else if (a.replace) {
       for (int j = lane; j < k; j += 32) {
         const uint32_t off_j = a.fanout < 0 ? static_cast<uint32_t>(j)
                                             : draw_below(node_draw(key, static_cast<uint64_t>(v), j),
                                                          static_cast<uint32_t>(d));
-        out[j] = a.indices[beg + off_j];
+        emit(j, a.indices[beg + off_j]);
       }
     } else {
       int32_t* acc = k <= kSmemAcc ? s_acc[w] : out;
       warp_pick_distinct(key, static_cast<uint64_t>(v), static_cast<uint32_t>(d), static_cast<uint32_t>(k), acc);
-      for (int j = lane; j < k; j += 32) out[j] = a.indices[beg + acc[j]];
+      for (int j = lane; j < k; j += 32) emit(j, a.indices[beg + acc[j]]);
       __syncwarp();
     }
   }

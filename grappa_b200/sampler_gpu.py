@@ -102,12 +102,15 @@ class GpuNeighborSampler:
         for h in range(self.L):
             dst = self.dst(h)
             front = None if h == 0 else self.sampled[h - 1]
+            # the hop kernel also does the compaction's first pass (map entries of the
+            # block's nodes), so the compaction starts at its scan
             cu.sample_hop(indptr, indices, dst, self.n_dst(h), 0, front, self.fanouts[self.L - 1 - h], self.replace,
                           counters, h, self.seed_gideg if (h == 0 and gideg is not None) else None,
                           cov if h == 0 else None, self.indptr[h], self.nbr[h], self.n_edges(h), self.sscr[h], err,
-                          self.cap_dst[h])
+                          self.cap_dst[h], self.map, self.src[h], self.sampled[h])
             cu.compact(dst, self.n_dst(h), self.nbr[h], self.n_edges(h), self.map, self.src[h], self.sampled[h],
-                       self.indices[h], self.n_src(h), self.cscr[h], err, self.cap_dst[h], self.cap_e[h], counters, h)
+                       self.indices[h], self.n_src(h), self.cscr[h], err, self.cap_dst[h], self.cap_e[h], counters, h,
+                       True)
 
     def blocks(self):
         """Materialise the sampled blocks (input layer first) with exact sizes (host sync)."""
