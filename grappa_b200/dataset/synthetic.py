@@ -53,6 +53,10 @@ SPECS = {
     "reddit": SyntheticSpec(232965, 57307946, 602, 41, 0.66, 0.10, seed=3, name="reddit"),
     # ogbn-papers100M shape: 111,059,956 nodes, 1.6B directed edges, 128-dim, 172 classes, 1.1% train
     "ogbpa": SyntheticSpec(111059956, 807842936, 128, 172, 0.011, 0.001, seed=4, name="ogbpa"),
+    # reduced ogbn-products shape for per-kernel profiler captures: 1,000,000 nodes,
+    # 25M undirected edges (50M directed), 100-dim, 47 classes; about 0.6 GB resident,
+    # still larger than L2 so that DRAM counters keep their meaning
+    "ogbpr_small": SyntheticSpec(1000000, 25000000, 100, 47, 0.08, 0.016, seed=6, name="ogbpr_small"),
     # small graphs for tests
     "tiny": SyntheticSpec(4096, 40000, 32, 8, 0.5, 0.2, seed=5, name="tiny"),
 }

@@ -1,16 +1,27 @@
 """Profiling entry point: one mini-batch training step of a model inside an NVTX
-range named ``prof_step`` (after one eager warm-up step), for kernel captures such as
+range named ``prof_step`` (after one eager warm-up step).
 
-    ncu --set full --clock-control none --nvtx --nvtx-include "prof_step/" \\
-        -o prof python -m grappa_b200.utils.profile_step --workload sage
+Kernel captures stay small.  On the full-size graph only the one-pass launch list
+is collected:
 
-and, with ``--phases N``, the CUDA-event device time of each step phase (sample,
-forward, backward, update) averaged over N eager steps; with ``--graphs N`` the
-device time of N replays of each captured graph: sampling alone, the step without
-and with the next step's sampling on its side stream (the overlap that the
-training loop uses).  Workloads: 3-layer models
-on the ogbn-products-shaped synthetic graph (``--config`` picks another spec),
-1024 seeds per batch, one GPU.
+    ncu --metrics gpu__time_duration.sum --clock-control none --nvtx \
+        --nvtx-include "prof_step/" --csv --log-file launches.csv \
+        python -m grappa_b200.utils.profile_step --workload sage
+
+and a full section set is taken for ONE kernel, a few launches, on the reduced
+graph ``ogbpr_small`` (1M nodes, 50M directed edges, about 0.6 GB resident):
+
+    ncu --set full --clock-control none --nvtx --nvtx-include "prof_step/" \
+        -k regex:aggregate_kernel -c 1 -o prof_aggregate \
+        python -m grappa_b200.utils.profile_step --workload sage --config ogbpr_small
+
+With ``--phases N`` the CUDA-event device time of each step phase (sample,
+forward, backward, update) averaged over N eager steps is printed; with
+``--graphs N`` the device time of N replays of each captured graph: sampling
+alone, the step without and with the next step's sampling on its side stream (the
+overlap that the training loop uses).  Workloads: 3-layer models on the
+ogbn-products-shaped synthetic graph (``--config`` picks another spec), 1024 seeds
+per batch, one GPU.
 """
 import argparse
 import json
