@@ -79,18 +79,58 @@ def _summarise_clocks(samples):
     return {"sm_mhz": med, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(mhz)}
 
 
-REFERENCE_UNAVAILABLE = (
-    "reference does not install offline: pip install of the reference fails at its CMake configure step "
-    "(third_party modules parallel-hashmap, easylogging and pcg_cpp are not in the repository; libnuma, "
-    "libunwind and DGL 1.x are not installed)")
+# Outcome of the one offline install of the reference (pip install --no-index
+# --no-build-isolation --find-links /opt/wheelhouse --target baseline/_ref <reference>):
+# its setup.py runs CMake, whose configure step stops at find_package(OpenMP)
+# (cmake/openmp.cmake:1, included from CMakeLists.txt:52); the third_party CMake
+# modules it includes next (CMakeLists.txt:55,57,62) are not in the reference either.
+REFERENCE_INSTALL_OUTCOME = ("its offline pip install fails at CMake configure: 'Could NOT find OpenMP_CXX' "
+                             "(cmake/openmp.cmake:1); the third_party modules of CMakeLists.txt:55,57,62 are absent")
+
+
+def _import_reference(ref):
+    """Import the reference's package, its native module and DGL from ``ref`` the way its
+    own entry points do (t10n before torch, t10n/__init__.py:1-6).  Returns the first
+    exception text, or None when everything imports."""
+    import importlib
+    import importlib.machinery
+
+    try:
+        spec = importlib.machinery.PathFinder.find_spec("t10n", [ref])
+        if spec is None:
+            raise ModuleNotFoundError(f"No module named 't10n' under {os.path.relpath(ref)}")
+        sys.path.insert(0, ref)
+        importlib.import_module("t10n")
+        importlib.import_module("t10n._C")
+        importlib.import_module("dgl")
+    except Exception as e:  # the reference arm reports what it observed
+        return f"{type(e).__name__}: {e}"
+    return None
 
 
 def run_reference(args):
+    """The reference's own code path (mpi-dsg/grappa, experiments/grappa/train/t10n_train.py
+    with IsolatedDataloader and DDP + weighted_grad_hook).  It runs only when the
+    reference's package, its native module and DGL import from baseline/_ref; otherwise
+    the line says what failed."""
     ref = os.path.join(os.path.dirname(os.path.abspath(__file__)), "baseline", "_ref")
-    if not os.path.isdir(os.path.join(ref, "t10n")):
-        print(json.dumps({"impl": "reference", "unavailable": REFERENCE_UNAVAILABLE}))
-        return 0
-    print(json.dumps({"impl": "reference", "unavailable": REFERENCE_UNAVAILABLE + "; DGL is absent"}))
+    err = _import_reference(ref)
+    if err is None:
+        err = "the reference imports, but its training script is not part of the installed package"
+    dgl_err = None
+    if "dgl" not in err:
+        try:
+            import importlib
+
+            importlib.import_module("dgl")
+        except Exception as e:
+            dgl_err = f"{type(e).__name__}: {e}"
+    reason = f"reference not importable ({err})"
+    if dgl_err:
+        reason += f"; DGL 1.x, which every reference code path needs, is missing too ({dgl_err})"
+    reason += f"; {REFERENCE_INSTALL_OUTCOME}"
+    if int(os.environ.get("RANK", "0")) == 0:  # under torchrun every rank runs this; one line
+        print(json.dumps({"impl": "reference", "unavailable": reason}))
     return 0
 
 

@@ -449,7 +449,8 @@ void allreduce_adam(int64_t rank, int64_t world, Tensor grad, int64_t chunk, std
 }
 
 void pull_rows(std::vector<int64_t> tables, int64_t table_stride, int64_t elem_bytes, int64_t row_bytes, Tensor gids,
-               OptT n_dev, int64_t n, Tensor prefix, int64_t out, int64_t out_stride, int64_t out_row0, int64_t cap) {
+               OptT n_dev, int64_t n, Tensor prefix, int64_t out, int64_t out_stride, int64_t out_row0, int64_t cap,
+               OptT err) {
   c10::cuda::CUDAGuard g(gids.device());
   namespace pe = grappa::peer;
   pe::PullRowsArgs a;
@@ -467,6 +468,7 @@ void pull_rows(std::vector<int64_t> tables, int64_t table_stride, int64_t elem_b
   a.out = as_ptr<void>(out);
   a.out_stride = out_stride;
   a.out_row0 = out_row0;
+  a.err = optr<int32_t>(err, at::kInt, "err");
   pe::launch_pull_rows(a, cap, stream());
 }
 
@@ -909,7 +911,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("b1"), py::arg("b2"), py::arg("eps"), py::arg("wd"), py::arg("do_adam"), py::arg("grad_out"),
         py::arg("err"), py::arg("grid"), py::arg("timeout_ns"), py::arg("flags2_local") = 0,
         py::arg("flags2_peer") = std::vector<int64_t>{});
-  m.def("pull_rows", &pull_rows);
+  m.def("pull_rows", &pull_rows, py::arg("tables"), py::arg("table_stride"), py::arg("elem_bytes"),
+        py::arg("row_bytes"), py::arg("gids"), py::arg("n_dev"), py::arg("n"), py::arg("prefix"), py::arg("out"),
+        py::arg("out_stride"), py::arg("out_row0"), py::arg("cap"), py::arg("err") = py::none());
   m.def("peer_copy", &peer_copy);
   m.def("a2a_pull", &a2a_pull, py::arg("src"), py::arg("src_off"), py::arg("len"), py::arg("dst_off"), py::arg("dst"),
         py::arg("first") = 0);

@@ -320,12 +320,21 @@ __global__ void __launch_bounds__(kArThreads) ar_adam_kernel(ArAdamArgs a) {
 
 // ---------------------------------------------------------------- repartition
 __global__ void pull_rows_kernel(PullRowsArgs a) {
-  const int64_t n = a.n_ptr ? *a.n_ptr : a.n;
+  int64_t n = a.n_ptr ? *a.n_ptr : a.n;
+  if (n > a.cap) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) dev::set_error(a.err, dev::kErrCapacity);
+    n = a.cap;
+  }
   const int lane = threadIdx.x & 31;
   const int64_t warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
   const int chunks = a.row_bytes >> 4;
+  const int64_t g_lo = a.prefix[0], g_hi = a.prefix[a.world];
   for (int64_t r = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; r < n; r += warps) {
     const int64_t g = a.gids[r];
+    if (g < g_lo || g >= g_hi) {
+      if (lane == 0) dev::set_error(a.err, dev::kErrBadIndex);
+      continue;
+    }
     int p = 0;
     while (p + 1 < a.world && g >= a.prefix[p + 1]) ++p;
     const int64_t row = g - a.prefix[p];
@@ -527,8 +536,14 @@ void launch_allreduce_adam(const ArAdamArgs& a, int grid, cudaStream_t stream) {
   GB_LAUNCH_CHECK();
 }
 
-void launch_pull_rows(const PullRowsArgs& a, int64_t cap, cudaStream_t stream) {
-  if (a.row_bytes % 16 != 0) throw std::invalid_argument("pull_rows: row bytes must be a multiple of 16");
+void launch_pull_rows(const PullRowsArgs& a_in, int64_t cap, cudaStream_t stream) {
+  if (a_in.world < 1 || a_in.world > kMaxRanks) throw std::invalid_argument("pull_rows: world out of range");
+  if (a_in.row_bytes % 16 != 0) throw std::invalid_argument("pull_rows: row bytes must be a multiple of 16");
+  if (cap < 0) throw std::invalid_argument("pull_rows: negative capacity");
+  if (!a_in.n_ptr && a_in.n > cap) throw std::invalid_argument("pull_rows: more rows than the output holds");
+  PullRowsArgs a = a_in;
+  a.cap = cap;
+  if (cap == 0) return;
   pull_rows_kernel<<<grid_for(cap * 32, 256, 16), 256, 0, stream>>>(a);
   GB_LAUNCH_CHECK();
 }

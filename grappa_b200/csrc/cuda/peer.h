@@ -67,7 +67,11 @@ struct PullRowsArgs {
   void* out = nullptr;
   int64_t out_stride = 0;                // elements
   int64_t out_row0 = 0;                  // first output row
+  int64_t cap = 0;                       // rows that fit in out after out_row0; n beyond it: kErrCapacity
+  int32_t* err = nullptr;                // error word (kErrCapacity, kErrBadIndex); may be null
 };
+// A row whose global id lies outside [prefix[0], prefix[world]) is skipped and
+// raises kErrBadIndex; rows past ``cap`` are dropped and raise kErrCapacity.
 void launch_pull_rows(const PullRowsArgs& a, int64_t cap, cudaStream_t stream);
 
 // contiguous copy (peer -> local), 16-byte vectors

@@ -245,7 +245,7 @@ extern "C" __attribute__((visibility("default"))) int grappa_sample_hop_noalloc(
     const int64_t* gideg, float* cov_accum, int32_t* out_indptr, int32_t* out_nbr, int32_t cap_edges,
     int32_t* n_edges_out, int32_t* err, void* stream) {
   if (n_dst < 0 || n_dst > kGrappaNoAllocMaxDst) return GRAPPA_NOALLOC_TOO_MANY_DST;
-  if (!indptr || !indices || !dst_nid || !counters || !out_indptr || !n_edges_out || n_graph_nodes < 0 ||
+  if (!indptr || !indices || (!dst_nid && n_dst > 0) || !counters || !out_indptr || !n_edges_out || n_graph_nodes < 0 ||
       cap_edges < 0 || (cap_edges > 0 && !out_nbr))
     return GRAPPA_NOALLOC_BAD_ARGUMENT;
   int dev = -1;

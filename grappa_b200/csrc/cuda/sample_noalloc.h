@@ -40,8 +40,11 @@ extern "C" {
 // int32), for the n_dst destination nodes dst_nid; same semantics and outputs as
 // the allocating launcher (grappa_b200/csrc/cuda/sample.cu, launch_sample_hop):
 // out_indptr [n_dst + 1], out_nbr [cap_edges], *n_edges_out, coverage sums in
-// cov_accum[2] when gideg is given.  frontier, gideg and cov_accum may be null.
-// counters points to device int64 [seed, epoch, step].  stream is a cudaStream_t
+// cov_accum[2] when gideg is given.  frontier, gideg and cov_accum may be null;
+// err may be null too, which turns off error reporting (capacity overflows and
+// timeouts of the scan are then silent).
+// dst_nid may be null when n_dst is 0 (an empty batch writes out_indptr[0] = 0 and
+// *n_edges_out = 0).  counters points to device int64 [seed, epoch, step].  stream is a cudaStream_t
 // (null = the legacy default stream).  Returns a GRAPPA_NOALLOC_* code.
 int grappa_sample_hop_noalloc(const int64_t* indptr, const int32_t* indices, int64_t n_graph_nodes,
                               const int32_t* dst_nid, int32_t n_dst, const uint8_t* frontier, int32_t fanout,

@@ -194,7 +194,7 @@ class PartitionStore:
         cu.peer_copy(self._feat_w.data_ptr() + n_r * fs * esz, peer["feat"].ptrs[q], n_q * fs * esz)
         tables = [peer["feat"].ptrs[p] for p in range(self.world)]
         cu.pull_rows(tables, fs, esz, fs * esz, self._halo_ids, self._n_halo, 0, self._prefix_dev,
-                     self._feat_w.data_ptr(), fs, n_r + n_q, self._halo_ids.numel())
+                     self._feat_w.data_ptr(), fs, n_r + n_q, self._halo_ids.numel(), self.err)
         self.working = WorkingGraph(self._indptr_w, self._indices_w, self._feat_w, n_r, n_q, self._n_halo,
                                     self.cap_nodes, q)
         return self.working

@@ -16,6 +16,8 @@ def test_reference_arm_reports_unavailable():
     assert len(lines) == 1
     rec = json.loads(lines[0])
     assert rec["impl"] == "reference" and rec["unavailable"]
+    # the reason quotes the exception that the import attempt observed
+    assert "Error" in rec["unavailable"] and "t10n" in rec["unavailable"]
 
 
 def test_every_workload_has_a_metric():

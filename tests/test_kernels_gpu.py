@@ -277,6 +277,47 @@ def test_gather_rows():
     torch.testing.assert_close(out[:500].float(), bf(table[ids.long()]).float())
 
 
+def test_pull_rows_checks_ids_and_capacity():
+    """pull_rows over two local "rank" tables: rows are fetched by global id; an id outside
+    the global range is skipped with kErrBadIndex, a count above the capacity is clamped
+    with kErrCapacity (no write past the output)."""
+    t0 = torch.randn(100, 16, device=DEV).to(torch.bfloat16)
+    t1 = torch.randn(50, 16, device=DEV).to(torch.bfloat16)
+    prefix = torch.tensor([0, 100, 150], dtype=torch.int64, device=DEV)
+    gids = torch.tensor([3, 120, 99, 100, 149, 0], dtype=torch.int64, device=DEV)
+    full = torch.cat([t0, t1])
+    out = torch.zeros((8, 16), dtype=torch.bfloat16, device=DEV)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    tables = [t0.data_ptr(), t1.data_ptr()]
+    n = torch.tensor([6], dtype=torch.int32, device=DEV)
+    cu().pull_rows(tables, 16, 2, 32, gids, n, 0, prefix, out.data_ptr(), 16, 1, 7, err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    torch.testing.assert_close(out[1:7], full[gids.long()])
+    assert bool((out[0] == 0).all()) and bool((out[7] == 0).all())
+    # a bad id (-1 and 150) is skipped and flagged; the other rows still arrive
+    out.zero_()
+    bad = torch.tensor([5, -1, 150, 140], dtype=torch.int64, device=DEV)
+    cu().pull_rows(tables, 16, 2, 32, bad, torch.tensor([4], dtype=torch.int32, device=DEV), 0, prefix,
+                   out.data_ptr(), 16, 0, 8, err)
+    torch.cuda.synchronize()
+    assert int(err.item()) & (1 << 2)
+    torch.testing.assert_close(out[0], full[5])
+    torch.testing.assert_close(out[3], full[140])
+    assert bool((out[1:3] == 0).all())
+    # a device count above the capacity is clamped: rows past cap stay untouched
+    err.zero_()
+    out.zero_()
+    sentinel = torch.full((4, 16), 7.0, dtype=torch.bfloat16, device=DEV)
+    out2 = torch.cat([torch.zeros((2, 16), dtype=torch.bfloat16, device=DEV), sentinel])
+    cu().pull_rows(tables, 16, 2, 32, gids, torch.tensor([6], dtype=torch.int32, device=DEV), 0, prefix,
+                   out2.data_ptr(), 16, 0, 2, err)
+    torch.cuda.synchronize()
+    assert int(err.item()) & (1 << 1)
+    torch.testing.assert_close(out2[:2], full[gids[:2].long()])
+    assert bool((out2[2:] == 7.0).all())
+
+
 # ----------------------------------------------------------------------------- optimizer
 def test_adam_matches_torch():
     torch.manual_seed(9)

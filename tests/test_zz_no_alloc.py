@@ -47,7 +47,7 @@ def _graph(n=3000, m=40000, seed=12):
     return torch.from_numpy(g.indptr()).to(DEV), torch.from_numpy(g.indices()).to(torch.int32).to(DEV), n
 
 
-def _regular(indptr, indices, dst, fanout, counters, hop, gideg, cap_e):
+def _regular(indptr, indices, dst, fanout, counters, hop, gideg, cap_e, frontier=None, replace=False):
     n_dst = dst.numel()
     out_indptr = torch.full((n_dst + 1,), -7, dtype=torch.int32, device=DEV)
     out_nbr = torch.full((cap_e,), -7, dtype=torch.int32, device=DEV)
@@ -55,22 +55,23 @@ def _regular(indptr, indices, dst, fanout, counters, hop, gideg, cap_e):
     cov = torch.zeros(2, device=DEV)
     err = torch.zeros(1, dtype=torch.int32, device=DEV)
     scratch = torch.zeros(_native.cuda().sample_scratch_words(n_dst), dtype=torch.int64, device=DEV)
-    _native.cuda().sample_hop(indptr, indices, dst, None, n_dst, None, fanout, False, counters, hop, gideg, cov,
+    _native.cuda().sample_hop(indptr, indices, dst, None, n_dst, frontier, fanout, replace, counters, hop, gideg, cov,
                               out_indptr, out_nbr, n_e, scratch, err, n_dst)
     return out_indptr, out_nbr, n_e, cov, err
 
 
-def _noalloc(lib, indptr, indices, n, dst, fanout, counters, hop, gideg, cap_e):
+def _noalloc(lib, indptr, indices, n, dst, fanout, counters, hop, gideg, cap_e, frontier=None, replace=False,
+             with_err=True):
     n_dst = dst.numel()
     out_indptr = torch.full((n_dst + 1,), -7, dtype=torch.int32, device=DEV)
     out_nbr = torch.full((cap_e,), -7, dtype=torch.int32, device=DEV)
     n_e = torch.zeros(1, dtype=torch.int32, device=DEV)
     cov = torch.zeros(2, device=DEV)
-    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV) if with_err else None
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-    rc = lib.grappa_sample_hop_noalloc(_ptr(indptr), _ptr(indices), n, _ptr(dst), n_dst, None, fanout, 0,
-                                       _ptr(counters), hop, _ptr(gideg), _ptr(cov), _ptr(out_indptr), _ptr(out_nbr),
-                                       cap_e, _ptr(n_e), _ptr(err), stream)
+    rc = lib.grappa_sample_hop_noalloc(_ptr(indptr), _ptr(indices), n, _ptr(dst), n_dst, _ptr(frontier), fanout,
+                                       1 if replace else 0, _ptr(counters), hop, _ptr(gideg), _ptr(cov),
+                                       _ptr(out_indptr), _ptr(out_nbr), cap_e, _ptr(n_e), _ptr(err), stream)
     assert rc == 0, f"entry point returned {rc}"
     return out_indptr, out_nbr, n_e, cov, err
 
@@ -113,3 +114,36 @@ def test_noalloc_entry_rejects_oversize_batch():
                                        _ptr(counters), 0, None, None, _ptr(dummy), _ptr(dummy), 1, _ptr(dummy),
                                        _ptr(dummy), None)
     assert rc == 1  # GRAPPA_NOALLOC_TOO_MANY_DST, nothing launched
+
+
+def test_noalloc_entry_replace_frontier_empty_and_no_error_word():
+    """The other paths of the entry point against the regular launcher: sampling with
+    replacement, a partial frontier mask, an empty batch (out_indptr[0] == 0, no edges)
+    and a null error word, each twice in a row."""
+    lib = _lib()
+    indptr, indices, n = _graph(seed=5)
+    counters = new_counters(23, DEV)
+    gen = torch.Generator(device="cpu").manual_seed(3)
+    for rep in range(2):
+        counters[1], counters[2] = 2, 7 + rep
+        dst = torch.randperm(n, generator=gen)[:1500].to(torch.int32).to(DEV)
+        frontier = (torch.rand(dst.numel(), generator=gen) < 0.6).to(torch.uint8).to(DEV)
+        for replace, fr, with_err in ((True, None, True), (False, frontier, True), (True, frontier, False)):
+            cap_e = dst.numel() * 10
+            want = _regular(indptr, indices, dst, 10, counters, 1, None, cap_e, frontier=fr, replace=replace)
+            got = _noalloc(lib, indptr, indices, n, dst, 10, counters, 1, None, cap_e, frontier=fr, replace=replace,
+                           with_err=with_err)
+            torch.cuda.synchronize()
+            assert int(want[4].item()) == 0
+            if with_err:
+                assert int(got[4].item()) == 0
+            ne = int(want[2].item())
+            assert ne > 0 and int(got[2].item()) == ne
+            assert torch.equal(got[0], want[0])
+            assert torch.equal(got[1][:ne], want[1][:ne])
+        empty = torch.zeros(0, dtype=torch.int32, device=DEV)
+        got = _noalloc(lib, indptr, indices, n, empty, 10, counters, 0, None, 16)
+        torch.cuda.synchronize()
+        assert int(got[0][0].item()) == 0
+        assert int(got[2].item()) == 0
+        assert int(got[4].item()) == 0
