@@ -115,7 +115,7 @@ class FullGraphBlocks:
     t10n_fullgraph_train.py:163-205): dst = src = rows [0, n), edges = in-edges among
     them.  Same interface as GpuNeighborSampler; ``sample`` does nothing."""
 
-    def __init__(self, indptr, indices, n_layers, device, labels, train_rows):
+    def __init__(self, indptr, indices, n_layers, device, labels, train_rows, cov=None):
         dev = torch.device(device)
         self.L = int(n_layers)
         n = int(indptr.numel() - 1)
@@ -136,6 +136,9 @@ class FullGraphBlocks:
         self.labels = labels.to(dev, torch.int32).contiguous()
         self.row_mask = train_rows.to(dev, torch.uint8).contiguous()
         self.n_sel = torch.tensor([int(self.row_mask.sum())], **i32)
+        # [coverage sum, count] of the partition's training rows (weight 1 when not given)
+        self.cov = (torch.ones(2, dtype=torch.float32, device=dev) if cov is None
+                    else cov.to(dev, torch.float32).contiguous())
         self.full_graph = True
 
     def n_seeds(self):
@@ -242,7 +245,6 @@ class BlockEngine:
             samplers = [self._make_sampler(int(batch_size), int(n_nodes_cap), dev) for _ in range(n)]
         else:
             samplers = [blocks]
-        self._cov_one = torch.ones(2, dtype=torch.float32, device=dev)
         self.n_classes = model.n_classes
         self._working = None
         self._set_samplers(samplers)
@@ -365,9 +367,10 @@ class BlockEngine:
 
     # ------------------------------------------------------------------ the step
     def _cov(self):
-        """[coverage sum, count] of the step: the sampler's for mini-batches; a fixed 1/1
-        for full-graph training (every in-edge of the partition is present)."""
-        return self._cov_one if self.full_graph else self.cov_cur
+        """[coverage sum, count] of the step: the sampler's for mini-batches; the block
+        source's, computed once per repartition from the kept in-degrees, for full-graph
+        training."""
+        return self.sm.cov if self.full_graph else self.cov_cur
 
     def _sample_into(self, q, step_offset):
         """Sample the blocks of the step ``step_offset`` ahead of the main counters into

@@ -211,6 +211,53 @@ class PartitionStore:
             self._peer = None
 
 
+def working_graph_host(parts, rank, nbr):
+    """The working graph of ``rank`` with neighbour partition ``nbr`` built from every
+    rank's OwnPartition on the host (tensors on any one device): the same layout as
+    ``PartitionStore.repartition`` builds over peer memory — rows [own | nbr | halo],
+    halo = sorted global ids of the in-edge sources of own and nbr that neither owns,
+    CSR by destination in working ids, halo rows without in-edges.  This is the oracle
+    of the peer-memory path and the working graph of single-process tools."""
+    own, q = parts[rank], parts[nbr]
+    dev = own.indices.device
+    n_r, n_q = own.n_nodes, (q.n_nodes if nbr != rank else 0)
+    lo_r, lo_q = own.prefix[rank], own.prefix[nbr]
+    n_global = own.n_global
+    ext = own.ext_src.to(dev, torch.int64)
+    if nbr != rank:
+        ext = torch.cat([ext, q.ext_src.to(dev, torch.int64)])
+    ext = torch.unique(ext)
+    inside = ((ext >= lo_r) & (ext < lo_r + n_r)) | ((ext >= lo_q) & (ext < lo_q + n_q))
+    halo = ext[~inside]
+    wmap = torch.full((n_global,), -1, dtype=torch.int64, device=dev)
+    wmap[lo_r:lo_r + n_r] = torch.arange(n_r, device=dev)
+    if n_q:
+        wmap[lo_q:lo_q + n_q] = torch.arange(n_r, n_r + n_q, device=dev)
+    wmap[halo] = torch.arange(n_r + n_q, n_r + n_q + halo.numel(), device=dev)
+    n_w = n_r + n_q + int(halo.numel())
+    indptr = torch.zeros(n_w + 1, dtype=torch.int64, device=dev)
+    deg_r = own.indptr[1:] - own.indptr[:-1]
+    indptr[1:n_r + 1] = torch.cumsum(deg_r.to(dev), 0)
+    pieces = [wmap[own.indices.to(dev).long()]]
+    if n_q:
+        deg_q = (q.indptr[1:] - q.indptr[:-1]).to(dev)
+        indptr[n_r + 1:n_r + n_q + 1] = indptr[n_r] + torch.cumsum(deg_q, 0)
+        pieces.append(wmap[q.indices.to(dev).long()])
+    indptr[n_r + n_q + 1:] = indptr[n_r + n_q]
+    indices = torch.cat(pieces).to(torch.int32)
+    feats = [own.feat.to(dev)] + ([q.feat.to(dev)] if n_q else [])
+    if halo.numel():
+        owner = torch.bucketize(halo, torch.tensor(own.prefix[1:], device=dev), right=True)
+        hf = torch.zeros((halo.numel(), own.feat.shape[1]), dtype=own.feat.dtype, device=dev)
+        for p in torch.unique(owner).tolist():
+            sel = owner == p
+            hf[sel] = parts[p].feat.to(dev)[halo[sel] - own.prefix[p]]
+        feats.append(hf)
+    feat = torch.cat(feats)
+    return WorkingGraph(indptr, indices, feat, n_r, n_q,
+                        torch.tensor([int(halo.numel())], dtype=torch.int32, device=dev), n_w, nbr)
+
+
 def next_neighbor(nbr_idx, rank, world):
     """Round-robin neighbour schedule of the reference (t10n/dataloader.py:547-553)."""
     nbr_idx = (nbr_idx + 1) % world

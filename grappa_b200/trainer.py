@@ -204,7 +204,15 @@ def full_graph_blocks(working, n_layers, own):
     """FullGraphBlocks of the working graph's own + neighbour rows: the in-edges whose
     source is one of those rows (halo sources dropped, as the reference's isolated
     full-graph partition holds only the two chunks, t10n/dataloader.py:492-502).
-    Labels and the training mask exist for the own rows only."""
+    Labels and the training mask exist for the own rows only.
+
+    The coverage weight c_r of the partition is the mini-batch path's per-seed ratio
+    (csrc/graph/sampling_h.h:97-116, t10n/dataloader.py:647-663) averaged over every
+    own training node, with the kept in-degree in place of the sampled node's local
+    degree: r_v = min(1, (max(kept_v - 1, 0) + 1) / (global_indeg_v + 1)).  kept_v
+    counts v's self-loop, global_indeg_v does not.  An own node whose in-neighbours all
+    lie in the own or the neighbour partition has r_v = 1; one that lost in-edges to a
+    third partition has r_v < 1.  Computed on the device, once per repartition."""
     from grappa_b200.engine import FullGraphBlocks
 
     n = int(working.n_own + working.n_nbr)
@@ -222,15 +230,25 @@ def full_graph_blocks(working, n_layers, own):
     labels[: working.n_own] = own.label
     train = torch.zeros(n, dtype=torch.uint8, device=dev)
     train[: working.n_own] = own.train_mask.to(torch.uint8)
-    return FullGraphBlocks(new_ip, ind[keep], n_layers, dev, labels, train)
+    cov = coverage_of_rows(cnt[: working.n_own], own.gideg.to(dev), own.train_mask.to(dev))
+    return FullGraphBlocks(new_ip, ind[keep], n_layers, dev, labels, train, cov=cov)
+
+
+def coverage_of_rows(kept_deg, gideg, mask):
+    """[sum, count] of min(1, (max(kept - 1, 0) + 1) / (gideg + 1)) over the rows selected
+    by ``mask`` (float32, on the rows' device)."""
+    up = (kept_deg.to(torch.float32) - 1.0).clamp(min=0.0) + 1.0
+    r = (up / (gideg.to(torch.float32).clamp(min=0.0) + 1.0)).clamp(max=1.0)
+    sel = mask.to(torch.bool)
+    return torch.stack([r[sel].sum(), sel.sum().to(torch.float32)]).to(torch.float32)
 
 
 class FullGraphTrainer:
     """Isolated full-graph training of one partition (reference:
     experiments/grappa/train/t10n_fullgraph_train.py:142-254): every epoch is one step
     over the whole working graph (own + neighbour partition), loss on the own training
-    nodes, coverage-corrected gradient aggregation across ranks (coverage 1: every
-    in-edge among the partition's rows is present), repartitioned every
+    nodes, coverage-corrected gradient aggregation across ranks (c_r from the kept
+    in-degrees of the own training nodes, ``full_graph_blocks``), repartitioned every
     ``repart_every`` epochs.  The reference computes the loss on every own node
     (training, validation and test); here only the training nodes contribute."""
 
