@@ -7,6 +7,7 @@
 #include <optional>
 
 #include "cuda_check.h"
+#include "allreduce.h"
 #include "kernels.h"
 #include "peer.h"
 
@@ -391,62 +392,96 @@ T* as_ptr(int64_t p) {
   return reinterpret_cast<T*>(p);
 }
 
-void allreduce_adam(int64_t rank, int64_t world, Tensor grad, int64_t chunk, std::vector<int64_t> send_local,
-                    std::vector<int64_t> send_peer, int64_t flags_local, std::vector<int64_t> flags_peer, OptT cov,
-                    Tensor counters, OptT param, OptT m, OptT v, OptT param_bf16, double lr, double b1, double b2,
-                    double eps, double wd, bool do_adam, OptT grad_out, Tensor err, int64_t grid, int64_t timeout_ns,
-                    int64_t flags2_local, std::vector<int64_t> flags2_peer) {
-  c10::cuda::CUDAGuard g(grad.device());
-  namespace pe = grappa::peer;
-  TORCH_CHECK(world >= 1 && world <= pe::kMaxRanks, "world out of range");
-  TORCH_CHECK(send_local.size() == 2 && send_peer.size() == static_cast<size_t>(2 * world) &&
-                  flags_peer.size() == static_cast<size_t>(world),
-              "peer pointer lists have the wrong length");
-  pe::ArAdamArgs a;
-  a.rank = static_cast<int32_t>(rank);
-  a.world = static_cast<int32_t>(world);
-  a.grad = ptr<float>(grad, at::kFloat, "grad");
-  a.n = grad.numel();
-  a.chunk = static_cast<int32_t>(chunk);
-  a.send_local[0] = as_ptr<float>(send_local[0]);
-  a.send_local[1] = as_ptr<float>(send_local[1]);
-  for (int p = 0; p < world; ++p) {
-    a.send_peer[p][0] = as_ptr<const float>(send_peer[2 * p]);
-    a.send_peer[p][1] = as_ptr<const float>(send_peer[2 * p + 1]);
-    a.flags_peer[p] = as_ptr<uint32_t>(flags_peer[p]);
-  }
-  a.flags_local = as_ptr<uint32_t>(flags_local);
-  a.cov = optr<float>(cov, at::kFloat, "cov");
-  TORCH_CHECK(counters.numel() >= 6, "counters needs 6 entries");
-  a.counters = ptr<int64_t>(counters, at::kLong, "counters");
-  a.do_adam = do_adam;
-  if (do_adam) {
-    TORCH_CHECK(param.has_value() && m.has_value() && v.has_value(), "Adam needs param, m and v");
-    a.param = ptr<float>(*param, at::kFloat, "param");
-    a.m = ptr<float>(*m, at::kFloat, "m");
-    a.v = ptr<float>(*v, at::kFloat, "v");
-    TORCH_CHECK(param->numel() == a.n && m->numel() == a.n && v->numel() == a.n, "Adam buffers differ in size");
-    if (param_bf16.has_value())
-      a.param_bf16 = reinterpret_cast<__nv_bfloat16*>(ptr<at::BFloat16>(*param_bf16, at::kBFloat16, "param_bf16"));
-  } else {
-    TORCH_CHECK(grad_out.has_value() && grad_out->numel() == a.n, "grad_out of the gradient's size is needed");
-    a.grad_out = ptr<float>(*grad_out, at::kFloat, "grad_out");
-  }
-  a.lr = static_cast<float>(lr);
-  a.beta1 = static_cast<float>(b1);
-  a.beta2 = static_cast<float>(b2);
-  a.eps = static_cast<float>(eps);
-  a.weight_decay = static_cast<float>(wd);
-  a.err = ptr<int32_t>(err, at::kInt, "err");
-  if (flags2_local != 0) {
-    TORCH_CHECK(flags2_peer.size() == static_cast<size_t>(world), "flags2_peer has the wrong length");
-    a.two_shot = true;
-    a.flags2_local = as_ptr<uint32_t>(flags2_local);
-    for (int p = 0; p < world; ++p) a.flags2_peer[p] = as_ptr<uint32_t>(flags2_peer[p]);
-  }
-  a.timeout_ns = timeout_ns;
-  pe::launch_allreduce_adam(a, static_cast<int>(grid), stream());
+// K-AR plan: the argument block of every gradient bucket, built once; launch(k) enqueues
+// bucket k's kernel on the current stream (the step graph captures it).
+template <typename T>
+T* iptr(int64_t p) {
+  return reinterpret_cast<T*>(static_cast<uintptr_t>(p));
 }
+
+struct ArPlan {
+  std::vector<grappa::ar::Args> args;
+  std::vector<int> grids;
+  int device = -1;
+
+  int64_t add(int64_t rank, int64_t world, int64_t mode, bool grad_bf16, int64_t lo, int64_t hi, int64_t grad,
+              std::vector<int64_t> grad_peer, std::vector<int64_t> slot_local, std::vector<int64_t> slot_peer,
+              int64_t param, std::vector<int64_t> param_peer, OptT m, OptT v, OptT wbf, int64_t scale_local,
+              std::vector<int64_t> scale_peer, int64_t flags_local, std::vector<int64_t> flags_peer, OptT cov,
+              Tensor counters, double lr, double b1, double b2, double eps, double wd, bool do_adam, OptT grad_out,
+              OptT err, int64_t grid, int64_t timeout_ns) {
+    namespace ga = grappa::ar;
+    TORCH_CHECK(world >= 1 && world <= ga::kMaxRanks && rank >= 0 && rank < world, "rank/world out of range");
+    const size_t w = static_cast<size_t>(world);
+    TORCH_CHECK(flags_peer.size() == w, "one flag page per rank");
+    TORCH_CHECK(grad_peer.empty() || grad_peer.size() == w, "one gradient mapping per rank");
+    TORCH_CHECK(param_peer.empty() || param_peer.size() == w, "one parameter mapping per rank");
+    TORCH_CHECK(scale_peer.empty() || scale_peer.size() == w, "one scale mapping per rank");
+    TORCH_CHECK(slot_local.empty() || (slot_local.size() == 2 && slot_peer.size() == 2 * w), "two send slots per rank");
+    TORCH_CHECK(grid >= 1 && grid <= ga::kMaxCtas, "grid out of range");
+    TORCH_CHECK(counters.numel() >= 6, "counters needs 6 entries");
+    ga::Args a;
+    a.rank = static_cast<int32_t>(rank);
+    a.world = static_cast<int32_t>(world);
+    a.mode = static_cast<int32_t>(mode);
+    a.grad_bf16 = grad_bf16;
+    a.lo = lo;
+    a.hi = hi;
+    a.grad = iptr<void>(grad);
+    for (size_t p = 0; p < grad_peer.size(); ++p) a.grad_peer[p] = iptr<const void>(grad_peer[p]);
+    if (!slot_local.empty()) {
+      a.slot_local[0] = iptr<float>(slot_local[0]);
+      a.slot_local[1] = iptr<float>(slot_local[1]);
+      for (size_t p = 0; p < w; ++p) {
+        a.slot_peer[p][0] = iptr<const float>(slot_peer[2 * p]);
+        a.slot_peer[p][1] = iptr<const float>(slot_peer[2 * p + 1]);
+      }
+    }
+    a.param = iptr<float>(param);
+    for (size_t p = 0; p < param_peer.size(); ++p) a.param_peer[p] = iptr<const float>(param_peer[p]);
+    a.m = optr<float>(m, at::kFloat, "m");
+    a.v = optr<float>(v, at::kFloat, "v");
+    a.wbf = reinterpret_cast<__nv_bfloat16*>(optr<at::BFloat16>(wbf, at::kBFloat16, "wbf"));
+    a.scale_local = iptr<float>(scale_local);
+    for (size_t p = 0; p < scale_peer.size(); ++p) a.scale_peer[p] = iptr<const float>(scale_peer[p]);
+    a.flags_local = iptr<uint32_t>(flags_local);
+    for (size_t p = 0; p < w; ++p) a.flags_peer[p] = iptr<uint32_t>(flags_peer[p]);
+    a.cov = optr<float>(cov, at::kFloat, "cov");
+    a.counters = ptr<int64_t>(counters, at::kLong, "counters");
+    a.lr = static_cast<float>(lr);
+    a.beta1 = static_cast<float>(b1);
+    a.beta2 = static_cast<float>(b2);
+    a.eps = static_cast<float>(eps);
+    a.weight_decay = static_cast<float>(wd);
+    a.do_adam = do_adam;
+    a.grad_out = optr<float>(grad_out, at::kFloat, "grad_out");
+    a.err = optr<int32_t>(err, at::kInt, "err");
+    a.timeout_ns = timeout_ns;
+    device = counters.device().index();
+    args.push_back(a);
+    grids.push_back(static_cast<int>(grid));
+    return static_cast<int64_t>(args.size()) - 1;
+  }
+
+  // cov (optional) replaces the bound coverage tensor for this launch
+  void launch(int64_t k, OptT cov) {
+    TORCH_CHECK(k >= 0 && k < static_cast<int64_t>(args.size()), "bucket index out of range");
+    c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(device));
+    if (cov.has_value() && cov->defined()) {
+      grappa::ar::Args a = args[k];
+      a.cov = ptr<float>(*cov, at::kFloat, "cov");
+      grappa::ar::launch(a, grids[k], stream());
+    } else {
+      grappa::ar::launch(args[k], grids[k], stream());
+    }
+  }
+
+  // the learning rate of every bucket (schedules); takes effect at the next capture or
+  // eager launch
+  void set_lr(double lr) {
+    for (auto& a : args) a.lr = static_cast<float>(lr);
+  }
+};
 
 void pull_rows(std::vector<int64_t> tables, int64_t table_stride, int64_t elem_bytes, int64_t row_bytes, Tensor gids,
                OptT n_dev, int64_t n, Tensor prefix, int64_t out, int64_t out_stride, int64_t out_row0, int64_t cap,
@@ -851,6 +886,17 @@ void walk_hop(Tensor indptr, Tensor indices, Tensor dst_nid, OptT n_dst_dev, int
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  py::class_<ArPlan>(m, "ArPlan")
+      .def(py::init<>())
+      .def("add", &ArPlan::add, py::arg("rank"), py::arg("world"), py::arg("mode"), py::arg("grad_bf16"), py::arg("lo"),
+           py::arg("hi"), py::arg("grad"), py::arg("grad_peer"), py::arg("slot_local"), py::arg("slot_peer"),
+           py::arg("param"), py::arg("param_peer"), py::arg("m"), py::arg("v"), py::arg("wbf"), py::arg("scale_local"),
+           py::arg("scale_peer"), py::arg("flags_local"), py::arg("flags_peer"), py::arg("cov"), py::arg("counters"),
+           py::arg("lr"), py::arg("b1"), py::arg("b2"), py::arg("eps"), py::arg("wd"), py::arg("do_adam"),
+           py::arg("grad_out"), py::arg("err"), py::arg("grid"), py::arg("timeout_ns"))
+      .def("launch", &ArPlan::launch, py::arg("k"), py::arg("cov") = py::none())
+      .def("set_lr", &ArPlan::set_lr)
+      .def("__len__", [](const ArPlan& p) { return p.args.size(); });
   m.doc() = "grappa_b200 sm_100a kernels";
   m.def("sample_hop", &sample_hop, py::arg("indptr"), py::arg("indices"), py::arg("dst_nid"), py::arg("n_dst_dev"),
         py::arg("n_dst"), py::arg("frontier"), py::arg("fanout"), py::arg("replace"), py::arg("counters"),
@@ -905,12 +951,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_open", [](py::bytes h) { return reinterpret_cast<int64_t>(grappa::peer::ipc_open(std::string(h))); });
   m.def("ipc_close", [](int64_t p) { grappa::peer::ipc_close(reinterpret_cast<void*>(p)); });
   m.def("tensor_from_ptr", &tensor_from_ptr);
-  m.def("allreduce_adam", &allreduce_adam, py::arg("rank"), py::arg("world"), py::arg("grad"), py::arg("chunk"),
-        py::arg("send_local"), py::arg("send_peer"), py::arg("flags_local"), py::arg("flags_peer"), py::arg("cov"),
-        py::arg("counters"), py::arg("param"), py::arg("m"), py::arg("v"), py::arg("param_bf16"), py::arg("lr"),
-        py::arg("b1"), py::arg("b2"), py::arg("eps"), py::arg("wd"), py::arg("do_adam"), py::arg("grad_out"),
-        py::arg("err"), py::arg("grid"), py::arg("timeout_ns"), py::arg("flags2_local") = 0,
-        py::arg("flags2_peer") = std::vector<int64_t>{});
   m.def("pull_rows", &pull_rows, py::arg("tables"), py::arg("table_stride"), py::arg("elem_bytes"),
         py::arg("row_bytes"), py::arg("gids"), py::arg("n_dev"), py::arg("n"), py::arg("prefix"), py::arg("out"),
         py::arg("out_stride"), py::arg("out_row0"), py::arg("cap"), py::arg("err") = py::none());

@@ -1,32 +1,7 @@
-// Peer-memory kernels (see peer.h).
-//
-// K-AR, the fused coverage-corrected all-reduce + Adam (one-shot or two-shot).
-// One CTA of 1024 threads per SM at most, so that every CTA is resident while
-// it waits on peers.  The reference
-// scales each rank's gradient bucket by its coverage weight c_r / W and sums the
-// buckets with an NCCL all-reduce, then runs torch.optim.Adam
-// (t10n/grad.py:6-24, experiments/grappa/train/t10n_train.py:159-162,248).  Here
-// one persistent kernel does all of it.  The gradient is cut into chunks; CTA j
-// of every rank owns the same chunks, so no grid-wide synchronisation is needed:
-//   1. publish: send[parity][chunk] = grad[chunk] * c_r / W (local store), grad = 0;
-//      then __threadfence_system and a st.release.sys of the step tag into flag
-//      [rank][chunk] of every peer
-//   2. wait: ld.acquire.sys polls of this rank's flags [p][chunk] for all p until
-//      they reach the tag (bounded by a %globaltimer deadline; on expiry the CTA
-//      records kErrPeerTimeout and stops reducing, so the GPU is never held)
-//   3. reduce: g = sum_p send_p[parity][chunk] with 16-byte P2P loads over NVLink,
-//      summed in rank order so that every rank computes bit-identical parameters;
-//      then the Adam update of the chunk writes the fp32 master weights, the
-//      moments and the bf16 working copy.
-// Two-shot (large buffers, W > 2): only the owner of chunk j (j % W) waits for and
-// sums the W copies, stores the sum in its own send slot and raises flags2[j] at
-// every rank; every rank then reads the sum from the owner and runs Adam.  Every
-// rank moves 2 (W-1)/W of the buffer over NVLink instead of W-1 times it.
-// The send slots alternate with the step parity: a rank can only start publishing
-// step t+2 after every peer has published step t+1, which each peer does only after
-// it finished reading step t, so a slot is never overwritten while it is read.
-// Flags are compared with >= (wrap-safe), since a peer may already have published
-// the next step's tag for a chunk that this CTA has not polled yet.
+// Peer-memory kernels (see peer.h): repartition pulls (pull_rows, csr_merge,
+// mark / mark_compact), the pull all-to-all and the device barrier.  Every remote
+// access is an ordinary 16-byte ld/st.global through an IPC mapping; waits are
+// bounded by a %globaltimer deadline and report kErrPeerTimeout.
 #include "common.cuh"
 #include "peer.h"
 
@@ -72,250 +47,6 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
-}
-
-__device__ __forceinline__ void adam_update(const ArAdamArgs& a, int64_t i, float g, float step_size, float inv_sqrt_bc2) {
-  float p = a.param[i];
-  if (a.weight_decay != 0.f) g += a.weight_decay * p;
-  const float m = a.beta1 * a.m[i] + (1.f - a.beta1) * g;
-  const float v = a.beta2 * a.v[i] + (1.f - a.beta2) * g * g;
-  a.m[i] = m;
-  a.v[i] = v;
-  p -= step_size * m / (sqrtf(v) * inv_sqrt_bc2 + a.eps);
-  a.param[i] = p;
-  if (a.param_bf16) a.param_bf16[i] = __float2bfloat16_rn(p);
-}
-
-// Bounded wait until *f reaches tag (wrap-safe); false on timeout (error recorded).
-__device__ __forceinline__ bool wait_flag(const uint32_t* f, uint32_t tag, const ArAdamArgs& a) {
-  if (static_cast<int32_t>(ld_acquire_sys(f) - tag) >= 0) return true;
-  const uint64_t t0 = dev::globaltimer_ns();
-  uint32_t polls = 0;
-  while (static_cast<int32_t>(ld_acquire_sys(f) - tag) < 0) {
-    if ((++polls & 63u) == 0) {
-      if (dev::globaltimer_ns() - t0 > static_cast<uint64_t>(a.timeout_ns)) {
-        dev::set_error(a.err, dev::kErrPeerTimeout);
-        return false;
-      }
-      __nanosleep(64);
-    }
-  }
-  return true;
-}
-
-__device__ __forceinline__ void finish1(const ArAdamArgs& a, int64_t i, float g, float step_size, float inv_sqrt_bc2) {
-  if (a.do_adam) adam_update(a, i, g, step_size, inv_sqrt_bc2);
-  else a.grad_out[i] = g;
-}
-
-// Groups of kArU float4 positions per thread (stride = the CTA's vector width): every
-// load of a group is issued before the first use, so a thread keeps kArU 16-byte
-// requests in flight per peer instead of one (the kernel is bound by the latency of
-// NVLink reads, not by their bandwidth, at one request per thread).
-constexpr int kArU = 4;
-constexpr int kArThreads = 512;  // one CTA per SM; 128 registers for the kArU groups
-
-__device__ __forceinline__ void adam4(const ArAdamArgs& a, float4& p, float4& m, float4& v, const float4& g,
-                                      float step_size, float inv_sqrt_bc2, __nv_bfloat16 (&w)[4]) {
-  float* pp = &p.x;
-  float* mp = &m.x;
-  float* vp = &v.x;
-  const float* gp = &g.x;
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    float gk = gp[k];
-    if (a.weight_decay != 0.f) gk += a.weight_decay * pp[k];
-    mp[k] = a.beta1 * mp[k] + (1.f - a.beta1) * gk;
-    vp[k] = a.beta2 * vp[k] + (1.f - a.beta2) * gk * gk;
-    pp[k] -= step_size * mp[k] / (sqrtf(vp[k]) * inv_sqrt_bc2 + a.eps);
-    w[k] = __float2bfloat16_rn(pp[k]);
-  }
-}
-
-// Adam (or the plain sum) for the full float4 positions i0 + u * stride < hi - 3.
-__device__ __forceinline__ void finish_group(const ArAdamArgs& a, int64_t i0, int64_t stride, int64_t hi,
-                                             const float4 (&g)[kArU], float step_size, float inv_sqrt_bc2) {
-  if (!a.do_adam) {
-#pragma unroll
-    for (int u = 0; u < kArU; ++u) {
-      const int64_t i = i0 + u * stride;
-      if (i + 3 < hi) *reinterpret_cast<float4*>(a.grad_out + i) = g[u];
-    }
-    return;
-  }
-  float4 p[kArU], m[kArU], v[kArU];
-#pragma unroll
-  for (int u = 0; u < kArU; ++u) {
-    const int64_t i = i0 + u * stride;
-    if (i + 3 < hi) {
-      p[u] = *reinterpret_cast<const float4*>(a.param + i);
-      m[u] = *reinterpret_cast<const float4*>(a.m + i);
-      v[u] = *reinterpret_cast<const float4*>(a.v + i);
-    }
-  }
-#pragma unroll
-  for (int u = 0; u < kArU; ++u) {
-    const int64_t i = i0 + u * stride;
-    if (i + 3 >= hi) continue;
-    __nv_bfloat16 w[4];
-    adam4(a, p[u], m[u], v[u], g[u], step_size, inv_sqrt_bc2, w);
-    *reinterpret_cast<float4*>(a.param + i) = p[u];
-    *reinterpret_cast<float4*>(a.m + i) = m[u];
-    *reinterpret_cast<float4*>(a.v + i) = v[u];
-    if (a.param_bf16) *reinterpret_cast<uint2*>(a.param_bf16 + i) = *reinterpret_cast<uint2*>(w);
-  }
-}
-
-// The ragged end of a chunk (positions whose float4 would cross hi), element by element.
-__device__ __forceinline__ bool ragged(int64_t i, int64_t hi) { return i < hi && i + 3 >= hi; }
-
-// Work split: CTA b owns chunks b, b + G, b + 2G, ... (G = grid, the same on every
-// rank).  It first publishes all of them, then waits for and reduces each, so the
-// flag round trips over NVLink overlap with the other chunks' traffic.
-__global__ void __launch_bounds__(kArThreads) ar_adam_kernel(ArAdamArgs a) {
-  const int64_t n_chunks = ceil_div(a.n, a.chunk);
-  const int64_t step = a.counters[3];
-  const int parity = static_cast<int>(step & 1);
-  const uint32_t tag = static_cast<uint32_t>(step + 1);
-  float scale = 1.f / static_cast<float>(a.world);
-  if (a.cov) {
-    const float cn = a.cov[1];
-    scale = (cn > 0.f ? a.cov[0] / cn : 0.f) / static_cast<float>(a.world);
-  }
-  const float t = static_cast<float>(a.counters[5] + 1);
-  const float bc1 = 1.f - powf(a.beta1, t);
-  const float bc2 = 1.f - powf(a.beta2, t);
-  const float step_size = a.lr / bc1;
-  const float inv_sqrt_bc2 = rsqrtf(bc2);
-  float* send = a.send_local[parity];
-  const int64_t vec_stride = static_cast<int64_t>(blockDim.x) * 4;
-  const int64_t group_stride = vec_stride * kArU;
-  __shared__ int s_timeout;  // sticky: after a timeout the CTA stops waiting and reducing
-  if (threadIdx.x == 0) s_timeout = 0;
-
-  // 1. publish every owned chunk: send = grad * c_r / W, grad = 0; flag the readers
-  for (int64_t j = blockIdx.x; j < n_chunks; j += gridDim.x) {
-    const int64_t lo = j * a.chunk;
-    const int64_t hi = min(a.n, lo + a.chunk);
-    for (int64_t i0 = lo + threadIdx.x * 4; i0 < hi; i0 += group_stride) {
-      float4 g[kArU];
-#pragma unroll
-      for (int u = 0; u < kArU; ++u) {
-        const int64_t i = i0 + u * vec_stride;
-        if (i + 3 < hi) g[u] = *reinterpret_cast<const float4*>(a.grad + i);
-      }
-#pragma unroll
-      for (int u = 0; u < kArU; ++u) {
-        const int64_t i = i0 + u * vec_stride;
-        if (i + 3 < hi) {
-          *reinterpret_cast<float4*>(a.grad + i) = make_float4(0.f, 0.f, 0.f, 0.f);
-          *reinterpret_cast<float4*>(send + i) = make_float4(g[u].x * scale, g[u].y * scale, g[u].z * scale,
-                                                             g[u].w * scale);
-        } else if (ragged(i, hi)) {
-          for (int64_t k = i; k < hi; ++k) {
-            send[k] = a.grad[k] * scale;
-            a.grad[k] = 0.f;
-          }
-        }
-      }
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      __threadfence_system();
-      if (a.two_shot) {
-        st_release_sys(a.flags_peer[j % a.world] + a.rank * n_chunks + j, tag);
-      } else {
-        for (int p = 0; p < a.world; ++p) st_release_sys(a.flags_peer[p] + a.rank * n_chunks + j, tag);
-      }
-    }
-  }
-  // 2. wait for the W copies of each chunk this rank reduces; sum in rank order
-  //    (bit-identical on every rank).  One-shot: + Adam.  Two-shot (owner only):
-  //    store the sum in the own send slot and flag every rank.
-  for (int64_t j = blockIdx.x; j < n_chunks; j += gridDim.x) {
-    if (a.two_shot && static_cast<int>(j % a.world) != a.rank) continue;
-    if (threadIdx.x < a.world && !s_timeout && !wait_flag(a.flags_local + threadIdx.x * n_chunks + j, tag, a))
-      s_timeout = 1;
-    __syncthreads();
-    if (s_timeout) break;
-    const int64_t lo = j * a.chunk;
-    const int64_t hi = min(a.n, lo + a.chunk);
-    for (int64_t i0 = lo + threadIdx.x * 4; i0 < hi; i0 += group_stride) {
-      float4 acc[kArU];
-#pragma unroll
-      for (int u = 0; u < kArU; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int p = 0; p < kMaxRanks; ++p) {
-        if (p >= a.world) break;
-        const float* src = a.send_peer[p][parity];
-        float4 x[kArU];
-#pragma unroll
-        for (int u = 0; u < kArU; ++u) {
-          const int64_t i = i0 + u * vec_stride;
-          if (i + 3 < hi) x[u] = *reinterpret_cast<const float4*>(src + i);
-        }
-#pragma unroll
-        for (int u = 0; u < kArU; ++u) {
-          const int64_t i = i0 + u * vec_stride;
-          if (i + 3 < hi) {
-            acc[u].x += x[u].x; acc[u].y += x[u].y; acc[u].z += x[u].z; acc[u].w += x[u].w;
-          }
-        }
-      }
-      if (a.two_shot) {
-#pragma unroll
-        for (int u = 0; u < kArU; ++u) {
-          const int64_t i = i0 + u * vec_stride;
-          if (i + 3 < hi) *reinterpret_cast<float4*>(send + i) = acc[u];
-        }
-      } else {
-        finish_group(a, i0, vec_stride, hi, acc, step_size, inv_sqrt_bc2);
-      }
-#pragma unroll
-      for (int u = 0; u < kArU; ++u) {
-        const int64_t i = i0 + u * vec_stride;
-        if (!ragged(i, hi)) continue;
-        for (int64_t k = i; k < hi; ++k) {
-          float s1 = 0.f;
-          for (int p = 0; p < a.world; ++p) s1 += a.send_peer[p][parity][k];
-          if (a.two_shot) send[k] = s1;
-          else finish1(a, k, s1, step_size, inv_sqrt_bc2);
-        }
-      }
-    }
-    if (a.two_shot) {
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        __threadfence_system();
-        for (int p = 0; p < a.world; ++p) st_release_sys(a.flags2_peer[p] + j, tag);
-      }
-    }
-  }
-  if (!a.two_shot) return;
-  // 3. two-shot: read every chunk's sum from its owner, Adam
-  for (int64_t j = blockIdx.x; j < n_chunks; j += gridDim.x) {
-    if (threadIdx.x == 0 && !s_timeout && !wait_flag(a.flags2_local + j, tag, a)) s_timeout = 1;
-    __syncthreads();
-    if (s_timeout) break;
-    const float* red = a.send_peer[j % a.world][parity];
-    const int64_t lo = j * a.chunk;
-    const int64_t hi = min(a.n, lo + a.chunk);
-    for (int64_t i0 = lo + threadIdx.x * 4; i0 < hi; i0 += group_stride) {
-      float4 g[kArU];
-#pragma unroll
-      for (int u = 0; u < kArU; ++u) {
-        const int64_t i = i0 + u * vec_stride;
-        if (i + 3 < hi) g[u] = *reinterpret_cast<const float4*>(red + i);
-      }
-      finish_group(a, i0, vec_stride, hi, g, step_size, inv_sqrt_bc2);
-#pragma unroll
-      for (int u = 0; u < kArU; ++u) {
-        const int64_t i = i0 + u * vec_stride;
-        if (ragged(i, hi))
-          for (int64_t k = i; k < hi; ++k) finish1(a, k, red[k], step_size, inv_sqrt_bc2);
-      }
-    }
-  }
 }
 
 // ---------------------------------------------------------------- repartition
@@ -522,19 +253,6 @@ int grid_for(int64_t n, int threads, int per_sm = 8) {
 }
 
 }  // namespace
-
-void launch_allreduce_adam(const ArAdamArgs& a, int grid, cudaStream_t stream) {
-  if (a.world < 1 || a.world > kMaxRanks) throw std::invalid_argument("world size out of range");
-  if (a.chunk % 4 != 0) throw std::invalid_argument("chunk must be a multiple of 4");
-  if (a.two_shot && !a.flags2_local) throw std::invalid_argument("two-shot needs the second flag array");
-  const int64_t n_chunks = ceil_div(a.n, a.chunk);
-  // at most one CTA per SM so that all CTAs are resident while they wait on peers
-  if (grid <= 0) grid = static_cast<int>(std::min<int64_t>(n_chunks, sm_count()));
-  grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({static_cast<int64_t>(grid), n_chunks,
-                                                                   static_cast<int64_t>(sm_count())})));
-  ar_adam_kernel<<<grid, kArThreads, 0, stream>>>(a);
-  GB_LAUNCH_CHECK();
-}
 
 void launch_pull_rows(const PullRowsArgs& a_in, int64_t cap, cudaStream_t stream) {
   if (a_in.world < 1 || a_in.world > kMaxRanks) throw std::invalid_argument("pull_rows: world out of range");

@@ -1,6 +1,6 @@
 // Peer-memory data plane over NVLink 5 / NVSwitch: IPC-exported buffers, the
-// fused coverage-weighted gradient all-reduce + Adam kernel, and the repartition
-// pull kernels.  No TMA copy touches peer memory here: every remote access is an
+// repartition pull kernels, the pull all-to-all and the device barrier (the fused
+// gradient all-reduce + Adam is in allreduce.h).  No TMA copy touches peer memory here: every remote access is an
 // ordinary ld/st.global through an IPC mapping.
 #pragma once
 #include <cuda_bf16.h>
@@ -20,38 +20,6 @@ void release(void* p);
 std::string ipc_handle(void* p);                  // 64-byte cudaIpcMemHandle_t
 void* ipc_open(const std::string& handle);        // maps a peer's buffer
 void ipc_close(void* p);
-
-// ---- fused all-reduce + Adam
-struct ArAdamArgs {
-  int32_t rank = 0, world = 1;
-  float* grad = nullptr;                 // local fp32 gradient, cleared after it is read
-  int64_t n = 0;
-  int32_t chunk = 4096;                  // elements per flag
-  float* send_local[2] = {nullptr, nullptr};          // this rank's two send slots
-  const float* send_peer[kMaxRanks][2] = {};          // every rank's send slots (self included)
-  uint32_t* flags_local = nullptr;                    // [world][n_chunks], written by peers
-  uint32_t* flags_peer[kMaxRanks] = {};               // every rank's flag array
-  const float* cov = nullptr;            // [sum, count] of this rank's coverage ratios (null: weight 1)
-  const int64_t* counters = nullptr;     // [seed, epoch, step, global_step, gen, adam_t]
-  // Adam
-  float* param = nullptr;
-  float* m = nullptr;
-  float* v = nullptr;
-  __nv_bfloat16* param_bf16 = nullptr;
-  float lr = 1e-3f, beta1 = 0.9f, beta2 = 0.999f, eps = 1e-8f, weight_decay = 0.f;
-  bool do_adam = true;                   // false: write the reduced gradient to grad_out
-  float* grad_out = nullptr;
-  int32_t* err = nullptr;
-  int64_t timeout_ns = 10000000000ll;
-  // two-shot: chunk j is reduced by rank j % world (reads W-1 peers' copies), which
-  // stores the sum in its own send slot and raises flags2[j] at every rank; every
-  // rank then reads the sums from the owners (2 (W-1)/W of the bytes per rank
-  // instead of W-1 times them for the one-shot)
-  bool two_shot = false;
-  uint32_t* flags2_local = nullptr;                   // [n_chunks], written by the owners
-  uint32_t* flags2_peer[kMaxRanks] = {};
-};
-void launch_allreduce_adam(const ArAdamArgs& a, int grid, cudaStream_t stream);
 
 // ---- repartition (pull over peer memory)
 struct PullRowsArgs {

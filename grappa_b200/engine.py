@@ -45,7 +45,7 @@ GAT_INPUT_LAYER_BWD = os.environ.get("GRAPPA_GAT_INPUT_BWD", "1") != "0"
 # kernels launched by each binding (memsets excluded)
 KERNELS_PER_CALL = {
     "sample_hop": 1, "walk_hop": 1, "compact": 3, "gemm": 1, "aggregate": 1, "aggregate_bwd": 1, "act_bwd": 1,
-    "gather_scalar": 1, "gather_rows": 1, "adam": 1, "allreduce_adam": 1, "step_end": 1, "src_norm": 2,
+    "gather_scalar": 1, "gather_rows": 1, "adam": 1, "step_end": 1, "src_norm": 2,
     "pull_rows": 1, "csr_merge": 1, "mark_ids": 1, "iota_map": 1, "mark_compact": 1, "peer_copy": 1, "a2a_pull": 1, "peer_barrier": 1,
     "shuffle_keys": 1, "cross_entropy": 1, "batchnorm_fwd": 2, "batchnorm_bwd": 2, "l2norm_fwd": 1,
     "l2norm_bwd": 1, "dropout_rows": 1, "dropout_grad": 1, "f32_to_bf16_rows": 1, "add_bf16_rows": 1,
@@ -202,7 +202,7 @@ class BlockEngine:
 
     def __init__(self, model, n_nodes_cap, fanouts, batch_size, device, lr=3e-3, comm=None, seed=0,
                  fused_allreduce=True, use_cuda_graph=True, betas=(0.9, 0.999), eps=1e-8, blocks=None,
-                 overlap_sampling=True):
+                 overlap_sampling=True, overlap_allreduce=True, ar_mode=None):
         if getattr(model, "name", None) != self.model_name:
             raise ValueError(f"{type(self).__name__} trains {self.model_name} models")
         self.cu = LaunchCounter(_native.cuda())
@@ -224,9 +224,25 @@ class BlockEngine:
         dev = self.device
 
         model.place(dev)
+        self.allreduce = None
+        self._ar_by_layer = False
+        if self.fused_allreduce:
+            # gradient and fp32 master weights in peer-mapped buffers; one bucket per layer
+            # (launched as the backward pass completes the layer) when the layers' segments
+            # are contiguous, else one bucket after the backward pass
+            from grappa_b200.parallel.allreduce import FusedAllReduceAdam
+
+            buckets = model.layer_buckets(self.L) if overlap_allreduce else None
+            self._ar_by_layer = buckets is not None
+            nb = 1 if buckets is None else len(buckets)
+            modes = None if ar_mode is None else [{"one_shot": 0, "shard": 1}[ar_mode]] * nb
+            self.allreduce = FusedAllReduceAdam(comm, model.flat.numel(), buckets, modes=modes)
+            self.allreduce.adopt_params(model)
+            self.grad = self.allreduce.grad
+        else:
+            self.grad = torch.zeros_like(model.flat)
         self.flat = model.flat
         self.wbf = self.flat.to(torch.bfloat16)
-        self.grad = torch.zeros_like(self.flat)
         self.m = torch.zeros_like(self.flat)
         self.v = torch.zeros_like(self.flat)
 
@@ -235,7 +251,8 @@ class BlockEngine:
         self.fstats = torch.zeros(4, dtype=torch.float32, device=dev)  # cov_sum, cov_n, loss_sum, spare
         self.istats = torch.zeros(2, dtype=torch.int32, device=dev)   # correct, spare
         self._ce_dummy = torch.zeros((1, 1), dtype=torch.float32, device=dev)
-        self.allreduce = FusedAllReduceAdam(comm, self.flat.numel()) if self.fused_allreduce else None
+        if self.allreduce is not None:
+            self.allreduce.bind(self.counters, self.m, self.v, self.wbf, self.lr, self.betas, self.eps, self.err)
 
         # block sources: with CUDA graphs two samplers alternate, so that the next
         # step's sampling (a side stream inside the step graph) overlaps this step's
@@ -343,6 +360,35 @@ class BlockEngine:
             torch.cuda.current_stream(self.device).wait_stream(self._aux)
             self._aux_used = False
 
+    def _comm_stream(self):
+        if getattr(self, "_comm", None) is None:
+            self._comm = torch.cuda.Stream(device=self.device)
+        return self._comm
+
+    def _grad_ready(self, l):
+        """Layer l's gradient is complete and no later kernel of the backward pass reads
+        its parameters: reduce its bucket (all-reduce + Adam) on the comm stream while
+        the backward pass goes on with the layers before it (the reference's DDP buckets
+        reduced by the comm hook as autograd produces them)."""
+        if not self._ar_by_layer:
+            return
+        comm = self._comm_stream()
+        comm.wait_stream(torch.cuda.current_stream(self.device))
+        if getattr(self, "_aux", None) is not None:
+            comm.wait_stream(self._aux)
+        with torch.cuda.stream(comm):
+            self.allreduce.launch(l, self._cov())
+        self.cu.count += 1
+        self._comm_used = True
+
+    def _backward(self):
+        for l in range(self.L - 1, -1, -1):
+            self._backward_layer(l)
+            self._grad_ready(l)
+
+    def _backward_layer(self, l):
+        raise NotImplementedError
+
     # ------------------------------------------------------------------ binding
     def bind_working(self, working, labels, gideg):
         """Point the engine at a working graph (after a repartition)."""
@@ -391,16 +437,19 @@ class BlockEngine:
     def _forward(self, training=True):
         raise NotImplementedError
 
-    def _backward(self):
-        raise NotImplementedError
-
     def _update(self):
         self._join_aux()
         cu = self.cu
         b1, b2 = self.betas
         if self.fused_allreduce:
-            self.allreduce.step(self.grad, self._cov(), self.counters, self.flat, self.m, self.v, self.wbf,
-                                self.lr, b1, b2, self.eps, self.err, cu=cu)
+            if self._ar_by_layer:
+                # every bucket was launched on the comm stream during the backward pass
+                if getattr(self, "_comm_used", False):
+                    torch.cuda.current_stream(self.device).wait_stream(self._comm)
+                    self._comm_used = False
+            else:
+                self.allreduce.launch_all(self._cov())
+                self.cu.count += len(self.allreduce.buckets)
         elif self.world > 1:
             # the reference's path (t10n/grad.py:6-24): scale by c_r / W, NCCL SUM all-reduce, Adam
             import torch.distributed as dist
@@ -575,6 +624,8 @@ class BlockEngine:
     def optimizer_state_dict(self):
         """torch.optim.Adam-compatible state of the fused optimizer (one entry per
         model parameter, views of the flat moments)."""
+        if self.allreduce is not None:
+            self.allreduce.sync_moments(self.m, self.v)  # collective: sharded moments to every rank
         state, ids = {}, []
         t = torch.tensor(float(self.counters[5].item()))
         for i, (name, p) in enumerate(self.model.named_parameters()):
@@ -654,25 +705,24 @@ class SageEngine(BlockEngine):
                            s["logits"], GEMM_STORE_BF16, s["bias"])
                 self._ce(s["logits"], self.n_classes, s["dY"], s["gb"] if training else None, h)
 
-    def _backward(self):
+    def _backward_layer(self, l):
         cu, sm = self.cu, self.sm
         scale = 1.0 / (1.0 - self.p) if self.p > 0 else 1.0
-        for l in range(self.L - 1, -1, -1):
-            s = self.lay[l]
-            h = s["h"]
-            # dW += dY^T X (split-K over the block's rows, fp32 reductions into the gradient)
-            self._dw(s["dY"], s["X"], s["op"], s["K"], s["rows"], self._n_dst(h), s["gW"])
-            if l == 0:
-                break
-            # dX = dY W (W read MN-major)
-            self._gemm(s["dY"], False, s["W"], True, s["rows"], self._n_dst(h), s["K"], s["op"], None, 1, s["dX"],
-                       GEMM_STORE_BF16)
-            prev = self.lay[l - 1]
-            # transpose aggregation: d(self) -> dst rows, d(agg) -> sources
-            cu.aggregate_bwd(sm.indptr[h], sm.indices[h], self._n_dst(h), 0, sm.cap_dst[h], s["dX"],
-                             s["ip"], 0, 0.0, s["ip"], AGG_MEAN, None, None, None, prev["dH"], self.err)
-            cu.act_bwd(prev["dH"], prev["H"], prev["dY"], self._n_dst(prev["h"]), 0, prev["op"], scale, prev["gb"],
-                       prev["rows"])
+        s = self.lay[l]
+        h = s["h"]
+        # dW += dY^T X (split-K over the block's rows, fp32 reductions into the gradient)
+        self._dw(s["dY"], s["X"], s["op"], s["K"], s["rows"], self._n_dst(h), s["gW"])
+        if l == 0:
+            return
+        # dX = dY W (W read MN-major)
+        self._gemm(s["dY"], False, s["W"], True, s["rows"], self._n_dst(h), s["K"], s["op"], None, 1, s["dX"],
+                   GEMM_STORE_BF16)
+        prev = self.lay[l - 1]
+        # transpose aggregation: d(self) -> dst rows, d(agg) -> sources
+        cu.aggregate_bwd(sm.indptr[h], sm.indices[h], self._n_dst(h), 0, sm.cap_dst[h], s["dX"],
+                         s["ip"], 0, 0.0, s["ip"], AGG_MEAN, None, None, None, prev["dH"], self.err)
+        cu.act_bwd(prev["dH"], prev["H"], prev["dY"], self._n_dst(prev["h"]), 0, prev["op"], scale, prev["gb"],
+                   prev["rows"])
 
 
 class GcnEngine(BlockEngine):
@@ -733,31 +783,30 @@ class GcnEngine(BlockEngine):
             if s["last"]:
                 self._ce(s["H"], self.n_classes, s["dY"], s["gb"] if training else None, h)
 
-    def _backward(self):
+    def _backward_layer(self, l):
         cu, sm = self.cu, self.sm
         scale = 1.0 / (1.0 - self.p) if self.p > 0 else 1.0
-        for l in range(self.L - 1, -1, -1):
-            s = self.lay[l]
-            h = s["h"]
-            if not s["last"]:
-                cu.act_bwd(s["dH"], s["H"], s["dY"], self._n_dst(h), 0, s["op"], scale, s["gb"], s["rows"])
-            prev = self.lay[l - 1] if l > 0 else None
-            if s["first_proj"]:
-                cu.aggregate_bwd(sm.indptr[h], sm.indices[h], self._n_dst(h), 0, sm.cap_dst[h], s["dY"], 0, -1, 0.0,
-                                 s["op"], AGG_GCN, None, s["snorm"], None, s["dZ32"], self.err)
-                cu.f32_to_bf16_rows(s["dZ32"], s["dZ"], s["op"], sm.n_src(h), s["srows"], True, 64)
-                A = s["Xg"] if "Xg" in s else (self._working.feat if l == 0 else prev["H"])
-                self._dw(A, s["dZ"], s["ip"], s["op"], s["srows"], sm.n_src(h), s["gW"])
-                if prev is not None:
-                    self._gemm(s["dZ"], False, s["W"], False, s["srows"], sm.n_src(h), s["ip"], s["op"], None, 1,
-                               prev["dH"], GEMM_STORE_F32)
-            else:
-                self._dw(s["X"], s["dY"], s["ip"], s["op"], s["rows"], self._n_dst(h), s["gW"])
-                if prev is not None:
-                    self._gemm(s["dY"], False, s["W"], False, s["rows"], self._n_dst(h), s["ip"], s["op"], None, 1,
-                               s["dX"], GEMM_STORE_BF16)
-                    cu.aggregate_bwd(sm.indptr[h], sm.indices[h], self._n_dst(h), 0, sm.cap_dst[h], s["dX"], 0, -1,
-                                     0.0, s["ip"], AGG_GCN, None, s["snorm"], None, prev["dH"], self.err)
+        s = self.lay[l]
+        h = s["h"]
+        if not s["last"]:
+            cu.act_bwd(s["dH"], s["H"], s["dY"], self._n_dst(h), 0, s["op"], scale, s["gb"], s["rows"])
+        prev = self.lay[l - 1] if l > 0 else None
+        if s["first_proj"]:
+            cu.aggregate_bwd(sm.indptr[h], sm.indices[h], self._n_dst(h), 0, sm.cap_dst[h], s["dY"], 0, -1, 0.0,
+                             s["op"], AGG_GCN, None, s["snorm"], None, s["dZ32"], self.err)
+            cu.f32_to_bf16_rows(s["dZ32"], s["dZ"], s["op"], sm.n_src(h), s["srows"], True, 64)
+            A = s["Xg"] if "Xg" in s else (self._working.feat if l == 0 else prev["H"])
+            self._dw(A, s["dZ"], s["ip"], s["op"], s["srows"], sm.n_src(h), s["gW"])
+            if prev is not None:
+                self._gemm(s["dZ"], False, s["W"], False, s["srows"], sm.n_src(h), s["ip"], s["op"], None, 1,
+                           prev["dH"], GEMM_STORE_F32)
+        else:
+            self._dw(s["X"], s["dY"], s["ip"], s["op"], s["rows"], self._n_dst(h), s["gW"])
+            if prev is not None:
+                self._gemm(s["dY"], False, s["W"], False, s["rows"], self._n_dst(h), s["ip"], s["op"], None, 1,
+                           s["dX"], GEMM_STORE_BF16)
+                cu.aggregate_bwd(sm.indptr[h], sm.indices[h], self._n_dst(h), 0, sm.cap_dst[h], s["dX"], 0, -1,
+                                 0.0, s["ip"], AGG_GCN, None, s["snorm"], None, prev["dH"], self.err)
 
 
 class GinEngine(BlockEngine):
@@ -825,30 +874,29 @@ class GinEngine(BlockEngine):
             if s["last"]:
                 self._ce(s["H"], self.n_classes, s["dl"], None, h)
 
-    def _backward(self):
+    def _backward_layer(self, l):
         cu, sm = self.cu, self.sm
-        for l in range(self.L - 1, -1, -1):
-            s = self.lay[l]
-            h = s["h"]
-            n = self._n_dst(h)
-            dy = s["dl"] if s["last"] else s["dH"]
-            cu.zero_(s["bs_out"])
-            cu.batchnorm_bwd(s["T1"], s["H"], dy, True, s["op"], n, s["rows"], s["s_out"], s["bs_out"], s["g_out"],
-                             s["dg_out"], s["db_out"], s["bn_out"].eps, s["dT1"])
-            self._dw(s["dT1"], s["U"], s["op"], s["hp"], s["rows"], n, s["gW1"])
-            self._gemm(s["dT1"], False, s["W1"], True, s["rows"], n, s["hp"], s["op"], None, 1, s["dU"],
-                       GEMM_STORE_F32)
-            cu.zero_(s["bs_mlp"])
-            cu.batchnorm_bwd(s["T0"], s["U"], s["dU"], True, s["hp"], n, s["rows"], s["s_mlp"], s["bs_mlp"],
-                             s["g_mlp"], s["dg_mlp"], s["db_mlp"], s["bn_mlp"].eps, s["dT0"])
-            self._dw(s["dT0"], s["X"], s["hp"], s["ip"], s["rows"], n, s["gW0"])
-            if l == 0:
-                break
-            prev = self.lay[l - 1]
-            self._gemm(s["dT0"], False, s["W0"], True, s["rows"], n, s["ip"], s["hp"], None, 1, s["dX"],
-                       GEMM_STORE_BF16)
-            cu.aggregate_bwd(sm.indptr[h], sm.indices[h], n, 0, sm.cap_dst[h], s["dX"], 0, -1, 1.0 + s["eps"],
-                             s["ip"], AGG_SUM, None, None, None, prev["dH"], self.err)
+        s = self.lay[l]
+        h = s["h"]
+        n = self._n_dst(h)
+        dy = s["dl"] if s["last"] else s["dH"]
+        cu.zero_(s["bs_out"])
+        cu.batchnorm_bwd(s["T1"], s["H"], dy, True, s["op"], n, s["rows"], s["s_out"], s["bs_out"], s["g_out"],
+                         s["dg_out"], s["db_out"], s["bn_out"].eps, s["dT1"])
+        self._dw(s["dT1"], s["U"], s["op"], s["hp"], s["rows"], n, s["gW1"])
+        self._gemm(s["dT1"], False, s["W1"], True, s["rows"], n, s["hp"], s["op"], None, 1, s["dU"],
+                   GEMM_STORE_F32)
+        cu.zero_(s["bs_mlp"])
+        cu.batchnorm_bwd(s["T0"], s["U"], s["dU"], True, s["hp"], n, s["rows"], s["s_mlp"], s["bs_mlp"],
+                         s["g_mlp"], s["dg_mlp"], s["db_mlp"], s["bn_mlp"].eps, s["dT0"])
+        self._dw(s["dT0"], s["X"], s["hp"], s["ip"], s["rows"], n, s["gW0"])
+        if l == 0:
+            return
+        prev = self.lay[l - 1]
+        self._gemm(s["dT0"], False, s["W0"], True, s["rows"], n, s["ip"], s["hp"], None, 1, s["dX"],
+                   GEMM_STORE_BF16)
+        cu.aggregate_bwd(sm.indptr[h], sm.indices[h], n, 0, sm.cap_dst[h], s["dX"], 0, -1, 1.0 + s["eps"],
+                         s["ip"], AGG_SUM, None, None, None, prev["dH"], self.err)
 
 
 class GatEngine(BlockEngine):
@@ -923,29 +971,28 @@ class GatEngine(BlockEngine):
             if s["last"]:
                 self._ce(s["H_out"], self.n_classes, s["dl"], None, h)
 
-    def _backward(self):
+    def _backward_layer(self, l):
         cu, sm = self.cu, self.sm
         scale = 1.0 / (1.0 - self.p) if self.p > 0 else 1.0
-        for l in range(self.L - 1, -1, -1):
-            s = self.lay[l]
-            h = s["h"]
-            if s["last"]:
-                dout = s["dl"]
-            else:
-                cu.act_bwd(s["dH"], s["H_out"], s["dY"], self._n_dst(h), 0, s["hfp"], scale, None, s["rows"])
-                dout = s["dY"]
-            A = self._A(l, s)
-            if s["in_fast"]:
-                self._input_layer_bwd(s, h, dout, A)
-                continue
-            cu.gat_bwd(sm.indptr[h], sm.indices[h], self._n_dst(h), s["rows"], sm.n_src(h), s["srows"], s["H"],
-                       s["F"], s["Z"], s["al"], s["ar"], s["el"], s["er"], s["smax"], s["ssum"], 0.2, s["last"], dout,
-                       s["escr"], s["del_"], s["der"], s["dz"], s["gb"], s["gal"], s["gar"], s["dzb"], self.err)
-            self._dw(s["dzb"], A, s["HF"], s["ip"], s["srows"], sm.n_src(h), s["gW"])
-            if l > 0:
-                prev = self.lay[l - 1]
-                self._gemm(s["dzb"], False, s["W"], True, s["srows"], sm.n_src(h), s["ip"], s["HF"], None, 1,
-                           prev["dH"], GEMM_STORE_F32)
+        s = self.lay[l]
+        h = s["h"]
+        if s["last"]:
+            dout = s["dl"]
+        else:
+            cu.act_bwd(s["dH"], s["H_out"], s["dY"], self._n_dst(h), 0, s["hfp"], scale, None, s["rows"])
+            dout = s["dY"]
+        A = self._A(l, s)
+        if s["in_fast"]:
+            self._input_layer_bwd(s, h, dout, A)
+            return
+        cu.gat_bwd(sm.indptr[h], sm.indices[h], self._n_dst(h), s["rows"], sm.n_src(h), s["srows"], s["H"],
+                   s["F"], s["Z"], s["al"], s["ar"], s["el"], s["er"], s["smax"], s["ssum"], 0.2, s["last"], dout,
+                   s["escr"], s["del_"], s["der"], s["dz"], s["gb"], s["gal"], s["gar"], s["dzb"], self.err)
+        self._dw(s["dzb"], A, s["HF"], s["ip"], s["srows"], sm.n_src(h), s["gW"])
+        if l > 0:
+            prev = self.lay[l - 1]
+            self._gemm(s["dzb"], False, s["W"], True, s["srows"], sm.n_src(h), s["ip"], s["HF"], None, 1,
+                       prev["dH"], GEMM_STORE_F32)
 
 
     def _input_layer_bwd(self, s, h, dout, A):
@@ -1046,33 +1093,32 @@ class PinSageEngine(BlockEngine):
             if s["last"]:
                 self._ce(s["H"], self.n_classes, s["dl"], None, h)
 
-    def _backward(self):
+    def _backward_layer(self, l):
         cu, sm = self.cu, self.sm
         p = self.p
-        for l in range(self.L - 1, -1, -1):
-            s = self.lay[l]
-            h = s["h"]
-            n = self._n_dst(h)
-            cu.l2norm_bwd(s["H"], s["dl"] if s["last"] else s["dH"], s["norms"], s["op"], n, s["rows"], s["dZ32"])
-            cu.act_bwd(s["dZ32"], s["Z"], s["dZ"], n, 0, s["op"], 1.0, s["gwb"], s["rows"])
-            self._dw(s["dZ"], s["X"], s["op"], s["kw"], s["rows"], n, s["gW"])
-            self._gemm(s["dZ"], False, s["W"], True, s["rows"], n, s["kw"], s["op"], None, 1, s["dX"],
-                       GEMM_STORE_BF16)
-            hid, ip = s["hid"], s["ip"]
-            dnv, dhd = s["dX"][:, :hid], s["dX"][:, hid:hid + ip]
-            cu.dropout_rows(dnv, dnv, hid, s["kw"], n, s["rows"], p, self.counters, 8 * l + 2)
-            cu.aggregate_bwd(sm.indptr[h], sm.indices[h], n, 0, sm.cap_dst[h], s["dX"], 0, -1, 0.0, hid,
-                             AGG_WEIGHTED, sm.w[h], None, None, s["dN32"], self.err)
-            cu.act_bwd(s["dN32"], s["N"], s["dN"], sm.n_src(h), 0, hid, 1.0, s["gqb"], s["srows"])
-            self._dw(s["dN"], s["Hd"], hid, ip, s["srows"], sm.n_src(h), s["gQ"])
-            if l == 0:
-                continue
-            prev = self.lay[l - 1]
-            cu.dropout_rows(dhd, dhd, ip, s["kw"], n, s["rows"], p, self.counters, 8 * l + 3)
-            self._gemm(s["dN"], False, s["Q"], True, s["srows"], sm.n_src(h), ip, hid, None, 1, prev["dH"],
-                       GEMM_STORE_F32)
-            cu.dropout_grad(prev["dH"], ip, ip, sm.n_src(h), s["srows"], p, self.counters, 8 * l + 1)
-            cu.add_bf16_rows(prev["dH"], dhd, ip, n, s["rows"])
+        s = self.lay[l]
+        h = s["h"]
+        n = self._n_dst(h)
+        cu.l2norm_bwd(s["H"], s["dl"] if s["last"] else s["dH"], s["norms"], s["op"], n, s["rows"], s["dZ32"])
+        cu.act_bwd(s["dZ32"], s["Z"], s["dZ"], n, 0, s["op"], 1.0, s["gwb"], s["rows"])
+        self._dw(s["dZ"], s["X"], s["op"], s["kw"], s["rows"], n, s["gW"])
+        self._gemm(s["dZ"], False, s["W"], True, s["rows"], n, s["kw"], s["op"], None, 1, s["dX"],
+                   GEMM_STORE_BF16)
+        hid, ip = s["hid"], s["ip"]
+        dnv, dhd = s["dX"][:, :hid], s["dX"][:, hid:hid + ip]
+        cu.dropout_rows(dnv, dnv, hid, s["kw"], n, s["rows"], p, self.counters, 8 * l + 2)
+        cu.aggregate_bwd(sm.indptr[h], sm.indices[h], n, 0, sm.cap_dst[h], s["dX"], 0, -1, 0.0, hid,
+                         AGG_WEIGHTED, sm.w[h], None, None, s["dN32"], self.err)
+        cu.act_bwd(s["dN32"], s["N"], s["dN"], sm.n_src(h), 0, hid, 1.0, s["gqb"], s["srows"])
+        self._dw(s["dN"], s["Hd"], hid, ip, s["srows"], sm.n_src(h), s["gQ"])
+        if l == 0:
+            return
+        prev = self.lay[l - 1]
+        cu.dropout_rows(dhd, dhd, ip, s["kw"], n, s["rows"], p, self.counters, 8 * l + 3)
+        self._gemm(s["dN"], False, s["Q"], True, s["srows"], sm.n_src(h), ip, hid, None, 1, prev["dH"],
+                   GEMM_STORE_F32)
+        cu.dropout_grad(prev["dH"], ip, ip, sm.n_src(h), s["srows"], p, self.counters, 8 * l + 1)
+        cu.add_bf16_rows(prev["dH"], dhd, ip, n, s["rows"])
 
 
 ENGINES = {"sage": SageEngine, "gcn": GcnEngine, "gin": GinEngine, "gat": GatEngine, "pinsage": PinSageEngine}
@@ -1085,68 +1131,3 @@ def make_engine(model, *args, **kwargs):
     except KeyError:
         raise ValueError(f"no GPU engine for model {getattr(model, 'name', None)}") from None
     return cls(model, *args, **kwargs)
-
-
-class FusedAllReduceAdam:
-    """Coverage-weighted gradient all-reduce fused with Adam (peer memory, one kernel).
-
-    One-shot for small buffers (every rank reads all W copies: lowest latency) and
-    two-shot for large ones at W > 2 (owner-reduce then owner-broadcast: 2 (W-1)/W of
-    the bytes per rank).  ``two_shot`` forces the choice; None picks by size: on four
-    B200s one-shot is faster up to 4 MB (37 vs 48 us at 1 MB) and even at 16 MB, two-shot
-    from 64 MB (405 vs 471 us); with eight ranks one-shot reads twice the peer bytes,
-    so the crossover is taken four times lower."""
-
-    @staticmethod
-    def two_shot_bytes(world):
-        return (16 << 20) if world <= 4 else (4 << 20)
-
-    def __init__(self, comm, n, chunk=None, timeout_s=30.0, two_shot=None):
-        from grappa_b200.parallel.comm import PeerBuffer
-
-        self.comm = comm
-        self.n = int(n)
-        W = comm.world
-        if two_shot is None:
-            two_shot = W > 2 and self.n * 4 >= self.two_shot_bytes(W)
-        self.two_shot = bool(two_shot) and W > 1
-        if chunk is None:
-            # enough chunks to keep every SM busy, 16 KB at least, 1 MB at most
-            chunk = max(4096, min(262144, (self.n // (148 * 4)) // 4 * 4))
-        self.chunk = int(chunk)
-        self.n_chunks = (self.n + self.chunk - 1) // self.chunk
-        half = (self.n * 4 + 255) // 256 * 256
-        flag_bytes = (W * self.n_chunks * 4 + 255) // 256 * 256
-        flag2_bytes = (self.n_chunks * 4 + 255) // 256 * 256
-        self.buf = PeerBuffer(comm, 2 * half + flag_bytes + flag2_bytes)
-        me = comm.rank
-        self.send_local = [self.buf.ptrs[me], self.buf.ptrs[me] + half]
-        self.send_peer = []
-        for p in range(W):
-            self.send_peer += [self.buf.ptrs[p], self.buf.ptrs[p] + half]
-        self.flags_local = self.buf.ptrs[me] + 2 * half
-        self.flags_peer = [self.buf.ptrs[p] + 2 * half for p in range(W)]
-        if self.two_shot:
-            self.flags2_local = self.buf.ptrs[me] + 2 * half + flag_bytes
-            self.flags2_peer = [self.buf.ptrs[p] + 2 * half + flag_bytes for p in range(W)]
-        else:
-            self.flags2_local, self.flags2_peer = 0, []
-        self.timeout_ns = int(timeout_s * 1e9)
-        torch.cuda.synchronize()
-        comm.barrier()
-
-    def step(self, grad, cov, counters, param, m, v, wbf, lr, b1, b2, eps, err, grid=0, cu=None):
-        cu = cu or _native.cuda()
-        cu.allreduce_adam(self.comm.rank, self.comm.world, grad, self.chunk, self.send_local, self.send_peer,
-                          self.flags_local, self.flags_peer, cov, counters, param, m, v, wbf, lr, b1, b2, eps, 0.0,
-                          True, None, err, grid, self.timeout_ns, self.flags2_local, self.flags2_peer)
-
-    def reduce(self, grad, cov, counters, out, err, grid=0):
-        """All-reduce only (no Adam): out = sum_r c_r grad_r / W."""
-        _native.cuda().allreduce_adam(self.comm.rank, self.comm.world, grad, self.chunk, self.send_local,
-                                      self.send_peer, self.flags_local, self.flags_peer, cov, counters, None, None,
-                                      None, None, 0.0, 0.9, 0.999, 1e-8, 0.0, False, out, err, grid, self.timeout_ns,
-                                      self.flags2_local, self.flags2_peer)
-
-    def close(self):
-        self.buf.close()

@@ -6,9 +6,9 @@ weight c_r (the mean coverage ratio of the batch's seeds) and by 1/W, then the
 buckets are summed with an all-reduce: g = sum_r c_r g_r / W.  It is kept as the
 NCCL/gloo path (CPU training, and the baseline the fused kernel is compared with).
 
-On GPUs the product path is the fused kernel of grappa_b200/csrc/cuda/peer.cu
-(``grappa_b200.engine.FusedAllReduceAdam``), which does the scaling, the
-all-reduce over NVLink peer memory and Adam in one launch.
+On GPUs the product path is the fused kernel of grappa_b200/csrc/cuda/allreduce.cu
+(``grappa_b200.parallel.allreduce.FusedAllReduceAdam``), which does the scaling, the
+all-reduce over NVLink peer memory and Adam in one launch per gradient bucket.
 """
 from typing import Tuple, cast
 

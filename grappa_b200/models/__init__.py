@@ -148,17 +148,18 @@ class GIN(_Base):
         self.dropout_p = 0.0
         self.layers = nn.ModuleList()
         self.batch_norms = nn.ModuleList()
-        for layer in range(num_layers - 1):
-            mlp = GINMLP(self, f"layers.{layer}.mlp", input_dim if layer == 0 else hidden_dim, hidden_dim, hidden_dim)
+        # layer i's segments (its MLP, then its output BatchNorm) are contiguous in the
+        # flat buffer, so that a layer's gradient is one bucket of the all-reduce
+        for layer in range(num_layers):
+            last = layer == num_layers - 1
+            mlp = GINMLP(self, f"layers.{layer}.mlp", input_dim if layer == 0 else hidden_dim, hidden_dim,
+                         output_dim if last else hidden_dim)
             self.layers.append(GINConv(mlp, 0.0))
-            self.batch_norms.append(nn.BatchNorm1d(hidden_dim))
-        mlp = GINMLP(self, f"layers.{num_layers - 1}.mlp", hidden_dim, hidden_dim, output_dim)
-        self.layers.append(GINConv(mlp, 0.0))
-        self.batch_norms.append(nn.BatchNorm1d(output_dim))
-        for i, bn in enumerate(self.batch_norms):
-            self.add_segment(f"batch_norms.{i}", 2, bn.num_features)
-            self.bind(bn, "weight", f"batch_norms.{i}", 0, slice(0, bn.num_features))
-            self.bind(bn, "bias", f"batch_norms.{i}", 1, slice(0, bn.num_features))
+            bn = nn.BatchNorm1d(output_dim if last else hidden_dim)
+            self.batch_norms.append(bn)
+            self.add_segment(f"batch_norms.{layer}", 2, bn.num_features)
+            self.bind(bn, "weight", f"batch_norms.{layer}", 0, slice(0, bn.num_features))
+            self.bind(bn, "bias", f"batch_norms.{layer}", 1, slice(0, bn.num_features))
         self.finalize(self.reset_parameters)
 
     def reset_parameters(self):

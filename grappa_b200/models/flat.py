@@ -65,6 +65,31 @@ class FlatModule(nn.Module):
     def segment(self, name):
         return self._segments[name]
 
+    def layer_buckets(self, n_layers):
+        """[(lo, hi)] element range of every layer's parameters (segments named
+        ``layers.{i}.*`` or ``batch_norms.{i}``) in the flat buffer, or None when a layer's
+        segments are not contiguous.  Ranges start on 64-element boundaries."""
+        import re
+
+        spans = {}
+        for name, seg in self._segments.items():
+            m = re.match(r"^(?:layers|batch_norms)\.(\d+)(?:\.|$)", name)
+            if m is None:
+                return None
+            i = int(m.group(1))
+            end = (seg.offset + seg.numel + 63) // 64 * 64
+            lo, hi, total = spans.get(i, (seg.offset, end, 0))
+            spans[i] = (min(lo, seg.offset), max(hi, end), total + (end - seg.offset))
+        if sorted(spans) != list(range(n_layers)):
+            return None
+        out = []
+        for i in range(n_layers):
+            lo, hi, total = spans[i]
+            if hi - lo != total:
+                return None  # another layer's segment lies inside this layer's range
+            out.append((lo, hi))
+        return out
+
     def finalize(self, init_fn, device="cpu"):
         flat = torch.zeros(self._size, dtype=torch.float32, device=device)
         self._rebind(flat)

@@ -26,7 +26,7 @@ from grappa_b200.graph_store import PartitionStore, next_neighbor
 
 class MiniBatchTrainer:
     def __init__(self, model, own, fanouts, batch_size, lr=3e-3, repart_every=10, comm=None, seed=0,
-                 fused_allreduce=True, use_cuda_graph=True):
+                 fused_allreduce=True, use_cuda_graph=True, ar_mode=None):
         self.model = model
         self.own = own
         self.comm = comm
@@ -49,7 +49,7 @@ class MiniBatchTrainer:
         self.batch_size = max(1, math.ceil(n_local / nb))  # reference: adjust_bs
         self.engine = make_engine(model, self.store.cap_nodes, fanouts, self.batch_size, self.device, lr=lr,
                                  comm=comm, seed=seed, fused_allreduce=fused_allreduce,
-                                 use_cuda_graph=use_cuda_graph)
+                                 use_cuda_graph=use_cuda_graph, ar_mode=ar_mode)
         self._maybe_repartition(0)
         self._warm = False
 
@@ -253,7 +253,7 @@ class FullGraphTrainer:
     (training, validation and test); here only the training nodes contribute."""
 
     def __init__(self, model, own, lr=3e-3, repart_every=10, comm=None, seed=0, fused_allreduce=True,
-                 use_cuda_graph=True):
+                 use_cuda_graph=True, ar_mode=None):
         from grappa_b200.engine import make_engine
 
         self.model, self.own, self.comm = model, own, comm
@@ -269,7 +269,8 @@ class FullGraphTrainer:
         w = self.store.repartition(self.nbr_idx)
         blocks = full_graph_blocks(w, len(model.layers), own)
         self.engine = make_engine(model, self.store.cap_nodes, [], 0, self.device, lr=lr, comm=comm, seed=seed,
-                                  fused_allreduce=fused_allreduce, use_cuda_graph=use_cuda_graph, blocks=blocks)
+                                  fused_allreduce=fused_allreduce, use_cuda_graph=use_cuda_graph, blocks=blocks,
+                                  ar_mode=ar_mode)
         self.engine.bind_working(w, own.label, own.gideg)
         self._last_repart = 0
         self._warm = False

@@ -28,8 +28,8 @@ def test_every_workload_has_a_metric():
     assert bench.METRICS["sage"].startswith("s/epoch")
 
 
-def test_two_shot_crossover():
-    from grappa_b200.engine import FusedAllReduceAdam
+def test_one_shot_crossover():
+    from grappa_b200.parallel.allreduce import FusedAllReduceAdam
 
-    assert FusedAllReduceAdam.two_shot_bytes(4) == 16 << 20
-    assert FusedAllReduceAdam.two_shot_bytes(8) == 4 << 20
+    lim = FusedAllReduceAdam.one_shot_max_bytes
+    assert lim(2) >= lim(4) >= lim(8) > 0

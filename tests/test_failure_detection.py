@@ -103,23 +103,34 @@ def test_peer_waits_give_up_with_error_status():
 
     cu = _native.cuda()
     dev = torch.device("cuda", 0)
-    n, chunk = 4096, 4096
+    n = 4096
     # a two-rank all-reduce whose "peer" never publishes: this rank's own buffers stand
-    # in for the peer's, and nothing ever raises the peer's flag
-    send = [torch.zeros(n, device=dev) for _ in range(4)]
-    flags = [torch.zeros(2, dtype=torch.int32, device=dev) for _ in range(2)]
-    grad = torch.randn(n, device=dev)
-    out = torch.zeros(n, device=dev)
+    # in for the peer's, and nothing ever raises the peer's flags
+    pages = [torch.zeros(2 * 8 * 160, dtype=torch.int32, device=dev) for _ in range(2)]
+    scales = [torch.zeros(2, device=dev) for _ in range(2)]
+    grads = [torch.randn(n, device=dev) for _ in range(2)]
+    params = [torch.zeros(n, device=dev) for _ in range(2)]
+    slots = [torch.zeros(n, device=dev) for _ in range(4)]
+    m, v = torch.zeros(n, device=dev), torch.zeros(n, device=dev)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     counters = new_counters(0, dev)
-    t0 = time.time()
-    cu.allreduce_adam(0, 2, grad, chunk, [send[0].data_ptr(), send[1].data_ptr()],
-                      [t.data_ptr() for t in send], flags[0].data_ptr(), [flags[0].data_ptr(), flags[1].data_ptr()],
-                      None, counters, None, None, None, None, 0.0, 0.9, 0.999, 1e-8, 0.0, False, out, err, 1,
-                      int(0.2e9))
-    torch.cuda.synchronize()
-    assert time.time() - t0 < 30
-    assert int(err.item()) & 8  # kErrPeerTimeout
+    for mode in (0, 1):  # one-shot, shard
+        err.zero_()
+        plan = cu.ArPlan()
+        plan.add(rank=0, world=2, mode=mode, grad_bf16=False, lo=0, hi=n, grad=grads[0].data_ptr(),
+                 grad_peer=[g.data_ptr() for g in grads] if mode else [],
+                 slot_local=[] if mode else [slots[0].data_ptr(), slots[1].data_ptr()],
+                 slot_peer=[] if mode else [t.data_ptr() for t in slots], param=params[0].data_ptr(),
+                 param_peer=[t.data_ptr() for t in params] if mode else [], m=m, v=v, wbf=None,
+                 scale_local=scales[0].data_ptr(), scale_peer=[t.data_ptr() for t in scales] if mode else [],
+                 flags_local=pages[0].data_ptr(), flags_peer=[t.data_ptr() for t in pages], cov=None,
+                 counters=counters, lr=1e-3, b1=0.9, b2=0.999, eps=1e-8, wd=0.0, do_adam=True, grad_out=None,
+                 err=err, grid=2, timeout_ns=int(0.2e9))
+        t0 = time.time()
+        plan.launch(0)
+        torch.cuda.synchronize()
+        assert time.time() - t0 < 30
+        assert int(err.item()) & 8  # kErrPeerTimeout
     # the device barrier gives up the same way
     err.zero_()
     epoch = torch.zeros(1, dtype=torch.int64, device=dev)

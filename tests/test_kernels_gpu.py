@@ -342,28 +342,40 @@ def test_adam_matches_torch():
     assert torch.equal(wbf, bf(param))
 
 
-def test_fused_allreduce_adam_single_rank():
-    from grappa_b200.engine import FusedAllReduceAdam
+@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_fused_allreduce_adam_single_rank(mode, dtype):
+    """One rank, two buckets (launched last first), a ragged end: the fused kernel's Adam
+    on the coverage-scaled gradient against torch's Adam; the gradient is cleared and
+    the bf16 copy is the rounding of the fp32 master."""
+    from grappa_b200.parallel.allreduce import FusedAllReduceAdam
     from grappa_b200.parallel.comm import Comm
 
     torch.manual_seed(10)
-    n = 50000
+    n = 50003
     p0 = torch.randn(n)
     p_ref = torch.nn.Parameter(p0.clone())
     opt = torch.optim.Adam([p_ref], lr=1e-2)
-    ar = FusedAllReduceAdam(Comm(), n, chunk=4096)
-    param, m, v = p0.clone().to(DEV), torch.zeros(n, device=DEV), torch.zeros(n, device=DEV)
+    ar = FusedAllReduceAdam(Comm(), n, buckets=[(0, 20000), (20000, n)], grad_dtype=dtype, modes=[mode, mode])
+    ar.param.copy_(p0)
+    m, v = torch.zeros(n, device=DEV), torch.zeros(n, device=DEV)
+    wbf = torch.zeros(n, dtype=torch.bfloat16, device=DEV)
     counters = new_counters(0, DEV)
     err = err_tensor()
     cov = torch.tensor([16.0, 20.0], device=DEV)  # c_r = 0.8
+    ar.bind(counters, m, v, wbf, 1e-2, err=err, cov=cov)
     for _ in range(4):
-        g = torch.randn(n)
-        p_ref.grad = g * 0.8
+        g = torch.randn(n).to(dtype)
+        p_ref.grad = g.float() * 0.8
         opt.step()
-        grad = g.to(DEV)
-        ar.step(grad, cov, counters, param, m, v, None, 1e-2, 0.9, 0.999, 1e-8, err)
+        ar.grad.copy_(g.to(DEV))
+        ar.launch(1)
+        ar.launch(0)
         cu().step_end(counters)
         torch.cuda.synchronize()
         assert err.item() == 0
-    torch.testing.assert_close(param.cpu(), p_ref.detach(), rtol=1e-5, atol=1e-6)
+        assert bool((ar.grad == 0).all())
+    torch.testing.assert_close(ar.param.cpu(), p_ref.detach(), rtol=1e-5, atol=1e-6)
+    assert torch.equal(wbf, ar.param.to(torch.bfloat16))
     ar.close()
+

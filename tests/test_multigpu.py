@@ -57,42 +57,67 @@ def _entry(rank, port, fn, q, *args):
         q.put((rank, False, traceback.format_exc()))
 
 
-def _ar_body(rank, two_shot=False):
-    from grappa_b200.engine import FusedAllReduceAdam
+def _ar_body(rank, mode, dtype_name):
+    """Two ranks, two buckets, three steps of the fused all-reduce + Adam against torch's
+    Adam on the coverage-weighted mean of both ranks' gradients (rebuilt on the CPU)."""
+    from grappa_b200.parallel.allreduce import FusedAllReduceAdam
     from grappa_b200.parallel.comm import Comm
     from grappa_b200.sampler_gpu import new_counters
 
+    dtype = getattr(torch, dtype_name)
     dev = torch.device("cuda", rank)
     n = 300001
     comm = Comm()
-    ar = FusedAllReduceAdam(comm, n, chunk=4096, two_shot=two_shot)
+    buckets = [(0, 120000), (120000, n)]
+    ar = FusedAllReduceAdam(comm, n, buckets, grad_dtype=dtype, modes=[mode, mode])
+    p0 = torch.randn(n, generator=torch.Generator(device="cpu").manual_seed(5))
+    ar.param.copy_(p0)
+    m, v = torch.zeros(n, device=dev), torch.zeros(n, device=dev)
+    wbf = torch.zeros(n, dtype=torch.bfloat16, device=dev)
     counters = new_counters(0, dev)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
-    out = torch.zeros(n, device=dev)
-    results = []
+    cov = torch.zeros(2, device=dev)
+    ar.bind(counters, m, v, wbf, 1e-2, err=err, cov=cov)
+    p_ref = torch.nn.Parameter(p0.clone())
+    opt = torch.optim.Adam([p_ref], lr=1e-2)
+    cleared = True
     for step in range(3):
-        g = torch.Generator(device="cpu").manual_seed(100 * step + rank)
-        grad = torch.randn(n, generator=g).to(dev)
-        c = 0.5 + 0.25 * rank  # coverage weight of this rank
-        cov = torch.tensor([c * 8.0, 8.0], device=dev)
-        ar.reduce(grad, cov, counters, out, err)
-        counters[3] += 1  # next step (flags and send-slot parity)
+        grads = [torch.randn(n, generator=torch.Generator(device="cpu").manual_seed(100 * step + r)).to(dtype)
+                 for r in range(WORLD)]
+        c = [0.5 + 0.25 * r for r in range(WORLD)]  # coverage weight of each rank
+        cov.copy_(torch.tensor([c[rank] * 8.0, 8.0]))
+        ar.grad.copy_(grads[rank])
+        ar.launch(1)  # buckets in backward order
+        ar.launch(0)
         torch.cuda.synchronize()
-        assert err.item() == 0
-        want = torch.zeros(n)
+        assert err.item() == 0, err.item()
+        cleared = cleared and bool((ar.grad == 0).all())
+        counters[3] += 1  # next step (flag tags and slot parity)
+        counters[5] += 1  # Adam step
+        want = torch.zeros(n, dtype=torch.float64)
         for r in range(WORLD):
-            gr = torch.randn(n, generator=torch.Generator(device="cpu").manual_seed(100 * step + r))
-            want += (0.5 + 0.25 * r) * gr / WORLD
-        results.append(float((out.cpu() - want).abs().max()))
+            want += c[r] / WORLD * grads[r].double()
+        p_ref.grad = want.float()
+        opt.step()
+    ar.sync_moments(m, v)
+    out = {"param": ar.param.cpu().clone(), "ref": p_ref.detach().clone(), "cleared": cleared,
+           "wbf_ok": bool(torch.equal(wbf, ar.param.to(torch.bfloat16))),
+           "m_err": float((m.cpu() - opt.state[p_ref]["exp_avg"]).abs().max())}
     ar.close()
-    return results
+    return out
 
 
-@pytest.mark.parametrize("two_shot", [False, True])
-def test_fused_allreduce_two_ranks(two_shot):
-    res = _run(_ar_body, _free_port(), two_shot)
+@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("dtype_name", ["float32", "bfloat16"])
+def test_fused_allreduce_two_ranks(mode, dtype_name):
+    res = _run(_ar_body, _free_port(), mode, dtype_name)
     for r in range(WORLD):
-        assert max(res[r]) < 1e-5, res
+        o = res[r]
+        assert o["cleared"] and o["wbf_ok"]
+        torch.testing.assert_close(o["param"], o["ref"], rtol=1e-5, atol=1e-5)
+        assert o["m_err"] < 1e-5
+    # every rank holds bit-identical parameters
+    assert torch.equal(res[0]["param"], res[1]["param"])
 
 
 def _repart_body(rank):
@@ -151,7 +176,7 @@ def test_repartition_two_ranks():
     assert all(v > 10 for v in res.values())
 
 
-def _train_body(rank):
+def _train_body(rank, ar_mode=None):
     import torch.nn.functional as F
 
     from grappa_b200.dataset import synthetic as S
@@ -165,7 +190,7 @@ def _train_body(rank):
     own = partition_from_global(g, WORLD, rank, dev, part_seed=3)
     torch.manual_seed(0)
     model = SAGE(g.spec.feat_dim, 64, g.spec.n_classes, 3, F.relu, 0.5)
-    tr = MiniBatchTrainer(model, own, [10, 10, 5], 128, comm=Comm(), seed=2, repart_every=2)
+    tr = MiniBatchTrainer(model, own, [10, 10, 5], 128, comm=Comm(), seed=2, repart_every=2, ar_mode=ar_mode)
     tr.warmup()
     losses = []
     for e in range(5):  # crosses two repartitions
@@ -178,8 +203,9 @@ def _train_body(rank):
     return {"losses": losses, "flat_sum": float(flat.double().sum()), "flat_head": flat[:64].tolist(), "acc": acc}
 
 
-def test_partition_parallel_training_two_ranks():
-    res = _run(_train_body, _free_port())
+@pytest.mark.parametrize("ar_mode", [None, "shard"])
+def test_partition_parallel_training_two_ranks(ar_mode):
+    res = _run(_train_body, _free_port(), ar_mode)
     a, b = res[0], res[1]
     # the fused all-reduce + Adam keeps the replicas bit-identical
     assert a["flat_head"] == b["flat_head"] and a["flat_sum"] == b["flat_sum"]
