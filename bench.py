@@ -169,7 +169,8 @@ def main():
     ap.add_argument("--no-graph", action="store_true", help="disable CUDA graph capture")
     ap.add_argument("--no-fused-ar", action="store_true", help="use the NCCL gradient path")
     ap.add_argument("--skip-e2e", action="store_true")
-    ap.add_argument("--eval", action="store_true", help="report validation/test accuracy after training")
+    ap.add_argument("--no-eval", action="store_true",
+                    help="skip the validation/test accuracy after the timed epochs (default for the 111M-node GAT)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -185,6 +186,8 @@ def main():
     from grappa_b200.trainer import FullGraphTrainer, MiniBatchTrainer
 
     wl = WORKLOADS[args.workload]
+    if args.workload == "gat" and args.config is None:
+        args.no_eval = True  # 111M nodes: the layer-wise pass is not part of this benchmark
     if args.config is None:
         args.config = wl["graph"]
 
@@ -279,11 +282,16 @@ def main():
                "last_mean_loss": None if loss is None else round(loss, 5)}
         trainer.engine.check_errors()
 
+    # accuracy after the timed epochs (outside the timed region): exact full-neighbour
+    # layer-wise inference across partitions, summed over ranks
     acc = None
-    if args.eval:
-        acc = {"val_acc": round(trainer.evaluate(own.val_mask), 4),
-               "test_acc": round(trainer.evaluate(own.test_mask), 4),
-               "epochs_trained": e1 + (0 if args.skip_e2e else args.steps)}
+    if not args.no_eval:
+        t0 = time.perf_counter()
+        va, te = trainer.evaluate_exact([own.val_mask, own.test_mask])
+        acc = {"val_acc": round(va, 4), "test_acc": round(te, 4),
+               "epochs_trained": e1 + (0 if args.skip_e2e else args.steps),
+               "method": "exact layer-wise inference, full neighbourhoods across partitions",
+               "seconds": round(time.perf_counter() - t0, 3)}
 
     out = {
         "metric": METRICS[args.workload],

@@ -1,9 +1,9 @@
 // K-AR kernels: coverage-weighted gradient all-reduce fused with Adam (see allreduce.h).
 //
-// Memory ordering.  A rank signals "my data is ready" with __threadfence_system()
-// followed by st.release.sys of the tag into the reader's flag word; the reader polls
-// with ld.acquire.sys (one thread per flag), then __syncthreads() orders the CTA's
-// loads after the acquire.  Gradients written by earlier kernels of the stream are
+// Memory ordering.  A rank signals "my data is ready" with a release pattern: after
+// __syncthreads(), thread 0 runs fence.acq_rel.sys and stores the tag into every
+// reader's flag word with st.relaxed.sys; the reader polls with ld.acquire.sys (one
+// thread per flag), then __syncthreads() orders the CTA's loads after the acquire.  Gradients written by earlier kernels of the stream are
 // complete when the kernel starts.
 //
 // Buffer reuse.  kShard: rank r clears piece j of shard s of its gradient only after
@@ -28,8 +28,12 @@ using dev::ceil_div;
 constexpr int kThreads = 512;
 constexpr int kU = 4;  // 16-byte vectors per thread in flight per peer
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// A release pattern: one fence.acq_rel.sys, then a relaxed system-scope store per
+// reader.  (A st.release per reader would fence once per store; each fence waits for
+// the previous remote store to be acknowledged over NVLink.)
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
@@ -219,8 +223,8 @@ __global__ void __launch_bounds__(kThreads, 1) ar_shard_kernel(Args a) {
   if (threadIdx.x == 0) {
     s_fail = 0;
     a.scale_local[par] = my_scale(a);
-    __threadfence_system();
-    for (int p = 0; p < W; ++p) st_release_sys(ready_flag(a.flags_peer[p], r, j), tag);
+    fence_acq_rel_sys();
+    for (int p = 0; p < W; ++p) st_relaxed_sys(ready_flag(a.flags_peer[p], r, j), tag);
   }
   __syncthreads();
   // 2. wait until every rank's piece j of shard r is ready; read the ranks' scales
@@ -282,9 +286,9 @@ __global__ void __launch_bounds__(kThreads, 1) ar_shard_kernel(Args a) {
   // 4. piece j of shard r is updated: flag every other rank
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence_system();
+    fence_acq_rel_sys();
     for (int p = 0; p < W; ++p)
-      if (p != r) st_release_sys(done_flag(a.flags_peer[p], r, j), tag);
+      if (p != r) st_relaxed_sys(done_flag(a.flags_peer[p], r, j), tag);
   }
   // 5. all-gather: piece j of every other shard from its owner (rotated start, so that
   //    the ranks read different owners at any one time)
@@ -376,8 +380,8 @@ __global__ void __launch_bounds__(kThreads, 1) ar_oneshot_kernel(Args a) {
   __syncthreads();
   if (threadIdx.x == 0) {
     s_fail = 0;
-    __threadfence_system();
-    for (int p = 0; p < W; ++p) st_release_sys(done_flag(a.flags_peer[p], r, j), tag);
+    fence_acq_rel_sys();
+    for (int p = 0; p < W; ++p) st_relaxed_sys(done_flag(a.flags_peer[p], r, j), tag);
   }
   __syncthreads();
   // 2. wait for every rank's piece j

@@ -27,6 +27,64 @@ from grappa_b200.graph_store import PartitionStore, next_neighbor, partition_fro
 from grappa_b200.sampler_gpu import C_EPOCH, C_STEP, GpuNeighborSampler, new_counters
 
 
+def to_block_device(dst, indptr, src):
+    """Block of one hop on the device: ``dst`` (unique global ids, the block's first source
+    nodes), the in-edges of dst[i] being ``src[indptr[i]:indptr[i+1]]`` (global ids).  The
+    sources follow the destinations in order of first appearance in the edge list (the
+    reference's to_block order, t10n/dgl_dsg/compliant.py:40-47)."""
+    n_dst = int(dst.numel())
+    allids = torch.cat([dst.long(), src.long()])
+    uniq, inv = torch.unique(allids, return_inverse=True)
+    first = torch.full((uniq.numel(),), allids.numel(), dtype=torch.int64, device=dst.device)
+    first.scatter_reduce_(0, inv, torch.arange(allids.numel(), device=dst.device), reduce="amin")
+    order = torch.argsort(first)
+    pos = torch.empty_like(order)
+    pos[order] = torch.arange(order.numel(), device=dst.device)
+    local = pos[inv]
+    return Block(indptr.to(torch.int64), local[n_dst:].to(torch.int32), uniq[order], n_dst, int(order.numel()))
+
+
+def _segments(indptr, n):
+    """(edge -> segment index, edge -> offset inside its segment) of a CSR indptr."""
+    deg = (indptr[1:] - indptr[:-1]).long()
+    seg = torch.repeat_interleave(torch.arange(n, device=indptr.device), deg)
+    off = torch.arange(int(indptr[-1]), device=indptr.device) - indptr[:-1].long()[seg]
+    return seg, off
+
+
+class _XbLoader:
+    """Cross-partition mini-batches over target nodes (reference: HostXBBatchSampler,
+    t10n/xbsampler.py:61-128): per hop the frontier is grouped by owner, the ids go to
+    their owners, every owner samples its requests on the GPU from its complete in-edge
+    CSR, and the sampled neighbour lists come back (peer-memory all-to-all); the hop's
+    block is built on the device.  Every rank runs the same number of batches."""
+
+    def __init__(self, loader, targets, fanouts, batch_size, n_batches):
+        self.ld, self.targets, self.fanouts = loader, targets, fanouts
+        self.bs, self.n_batches = max(1, int(batch_size)), int(n_batches)
+        self.i = 0
+
+    def __iter__(self):
+        self.i = 0
+        return self
+
+    def __len__(self):
+        return self.n_batches
+
+    def __next__(self):
+        if self.i >= self.n_batches:
+            raise StopIteration
+        out = self.targets[self.i * self.bs:(self.i + 1) * self.bs]
+        seeds, blocks = out, []
+        for hop, fanout in enumerate(reversed(self.fanouts)):
+            indptr, src = self.ld._xb_hop(seeds, int(fanout), hop, self.i)
+            blk = to_block_device(seeds, indptr, src)
+            seeds = blk.srcdata["_ID"]
+            blocks.insert(0, blk)
+        self.i += 1
+        return seeds, out, blocks
+
+
 class _GpuEpoch:
     """Iterator over one epoch of device-sampled mini-batches."""
 
@@ -204,6 +262,129 @@ class IsolatedDataloaderGPU:
         src_ids[local] = uniq
         return Block(indptr, local[rest], self.w2g[src_ids], rows.numel(), src_ids.numel())
 
+    # ------------------------------------------------------------------ cross-border inference
+    def _peer_a2a(self):
+        if getattr(self, "_a2a", None) is None:
+            from grappa_b200.cl import PeerAllToAll
+
+            self._a2a = PeerAllToAll(self.comm, self.device)
+        return self._a2a
+
+    def _sample_own(self, gids, fanout, hop, batch):
+        """In-neighbours (global ids) of own global ids ``gids``: all of them for fanout < 0,
+        else ``fanout`` distinct ones drawn by the GPU sampling kernel (Philox keys from
+        (seed, batch, hop)).  Returns (indptr int64 [n + 1], sources int64)."""
+        cu = _native.cuda()
+        n = int(gids.numel())
+        lo = self.prefix_sum[self.rank]
+        rows = (gids.long() - lo).to(torch.int32)
+        deg = (self.own.indptr[1:] - self.own.indptr[:-1])[rows.long()] if n else rows.long()
+        cap = int(deg.sum()) if fanout < 0 else int(torch.clamp(deg, max=fanout).sum())
+        out_ip = torch.zeros(n + 1, dtype=torch.int32, device=self.device)
+        out_nbr = torch.zeros(max(1, cap), dtype=torch.int32, device=self.device)
+        n_e = torch.zeros(1, dtype=torch.int32, device=self.device)
+        scratch = torch.zeros(cu.sample_scratch_words(max(1, n)), dtype=torch.int64, device=self.device)
+        err = torch.zeros(1, dtype=torch.int32, device=self.device)
+        ctr = new_counters(self.seed, self.device)
+        ctr[C_EPOCH], ctr[C_STEP] = 1 << 20, batch  # draws apart from the training epochs
+        cu.sample_hop(self.own.indptr, self.own.indices, rows, None, n, None, int(fanout), False, ctr, hop, None,
+                      None, out_ip, out_nbr, n_e, scratch, err, max(1, n))
+        if int(err.item()):
+            raise RuntimeError(f"device error word {int(err.item()):#x} in cross-border sampling")
+        return out_ip.to(torch.int64), out_nbr[: int(n_e.item())].to(torch.int64)
+
+    def _xb_hop(self, seeds, fanout, hop, batch):
+        """In-neighbours of arbitrary global ids, sampled by their owners."""
+        from grappa_b200.xborder import _group_by_owner
+
+        seeds = seeds.to(self.device).long()
+        if self.world == 1:
+            return self._sample_own(seeds, fanout, hop, batch)
+        a2a = self._peer_a2a()
+        sorted_ids, order, counts = _group_by_owner(seeds, self.prefix_sum, self.world)
+        requests = a2a.exchange(list(torch.split(sorted_ids, counts)))
+        sizes = [int(q.numel()) for q in requests]
+        ip, nbr = self._sample_own(torch.cat(requests), fanout, hop, batch)
+        deg = ip[1:] - ip[:-1]
+        bounds = [0]
+        for z in sizes:
+            bounds.append(bounds[-1] + z)
+        deg_parts = [deg[bounds[p]:bounds[p + 1]].contiguous() for p in range(self.world)]
+        nbr_parts = [nbr[int(ip[bounds[p]]):int(ip[bounds[p + 1]])].contiguous() for p in range(self.world)]
+        deg_back = torch.cat(a2a.exchange(deg_parts))      # degrees of sorted_ids
+        nbr_back = torch.cat(a2a.exchange(nbr_parts))      # their neighbours, in sorted order
+        n = int(seeds.numel())
+        ip_sorted = torch.zeros(n + 1, dtype=torch.int64, device=self.device)
+        ip_sorted[1:] = torch.cumsum(deg_back, 0)
+        deg_orig = torch.empty_like(deg_back)
+        deg_orig[order] = deg_back
+        ip_orig = torch.zeros(n + 1, dtype=torch.int64, device=self.device)
+        ip_orig[1:] = torch.cumsum(deg_orig, 0)
+        inv_order = torch.empty_like(order)
+        inv_order[order] = torch.arange(n, device=self.device)
+        seg, off = _segments(ip_orig, n)
+        src = nbr_back[ip_sorted[:-1][inv_order[seg]] + off]
+        return ip_orig, src
+
+    def _equal_batches(self, n_targets, batch_size):
+        n_batch = (n_targets + batch_size - 1) // batch_size
+        if self.world > 1:
+            n_batch = int(self.comm.all_reduce_max([n_batch])[0])
+        bs = max(1, (n_targets + n_batch - 1) // n_batch) if n_batch else 1
+        return n_batch, bs
+
+    def xb_dataloader(self, args, force_even=True, full_neighbor=False, subset_tag="all"):
+        """Cross-partition sampled mini-batches over the own nodes of ``subset_tag`` (the
+        training fanouts, or full neighbourhoods); yields (input_nodes, output_nodes,
+        blocks) with global ids."""
+        fanouts = [-1 if full_neighbor else int(f) for f in self.fanouts]
+        target = self.get_node_subset(subset_tag).to(self.device)
+        n_batch, bs = self._equal_batches(int(target.numel()), int(args.batch_size_eval))
+        return _XbLoader(self, target, fanouts, bs, n_batch)
+
+    def xb_dataloader_per_layer(self, args, subset_tag="all"):
+        """One full-neighbour hop per batch of own target nodes, for layer-wise inference
+        (the own in-edge lists are complete, so no exchange is needed)."""
+        target = self.get_node_subset(subset_tag).to(self.device)
+        n_batch, bs = self._equal_batches(int(target.numel()), int(args.batch_size_eval))
+        return _XbLoader(self, target, [-1], bs, n_batch)
+
+    def xb_get_batch_input(self, batch_input, target_nodes):
+        """Features of arbitrary global ids, fetched from their owners."""
+        return self.xb_get_batch_emb(batch_input, target_nodes, self.own.feat)
+
+    def xb_get_batch_emb(self, batch_input, target_nodes, emb_self):
+        """Rows of a per-rank table (``emb_self``: this rank's own nodes) for arbitrary
+        global ids, fetched from their owners through peer memory."""
+        from grappa_b200.xborder import xb_gather_peer
+
+        if self.world == 1:
+            rows = emb_self[(target_nodes.to(emb_self.device).long() - self.prefix_sum[self.rank])]
+            cols = batch_input.shape[1]
+            batch_input.copy_(rows[:, :cols].to(batch_input.device, batch_input.dtype))
+            return batch_input
+        return xb_gather_peer(self._peer_a2a(), batch_input, target_nodes, emb_self, self.rank, self.world,
+                              self.prefix_sum)
+
+    def xb_scatter_emb(self, emb, target_nodes, emb_self):
+        """emb_self[id] = row of ``emb`` for own ids; other rows go to their owners."""
+        from grappa_b200.xborder import _group_by_owner
+
+        ids = target_nodes.to(self.device).long()
+        lo = self.prefix_sum[self.rank]
+        if self.world == 1:
+            emb_self[ids - lo] = emb.to(emb_self.device, emb_self.dtype)
+            return emb_self
+        sorted_ids, order, counts = _group_by_owner(ids, self.prefix_sum, self.world)
+        a2a = self._peer_a2a()
+        got_ids = a2a.exchange(list(torch.split(sorted_ids, counts)))
+        rows = emb.to(self.device, emb_self.dtype)[order]
+        got_rows = a2a.exchange(list(torch.split(rows, counts)))
+        for q, r_ in zip(got_ids, got_rows):
+            if q.numel():
+                emb_self[q.long() - lo] = r_
+        return emb_self
+
     def infer_train_mask_of(self, seeds):
         return self.train_mask[seeds.to(self.device).long() - self.prefix_sum[self.rank]]
 
@@ -214,4 +395,7 @@ class IsolatedDataloaderGPU:
         return self.test_mask[seeds.to(self.device).long() - self.prefix_sum[self.rank]]
 
     def close(self):
+        if getattr(self, "_a2a", None) is not None:
+            self._a2a.close()
+            self._a2a = None
         self.store.close()

@@ -188,3 +188,100 @@ def infer_layer(model, layer_i, block, h):
         raise ValueError(f"{name} is not supported")
     ctx.check()
     return out.float()
+
+
+def _layer_in_width(model, layer_i):
+    layer = model.layers[layer_i]
+    if model.name == "gin":
+        return pad8(layer.apply_func.linears[0].in_features)
+    if model.name == "pinsage":
+        return pad8(layer.input_dims)
+    return pad8(layer.in_feats)
+
+
+class ExactInference:
+    """Exact full-neighbour layer-wise inference of every own node on the GPU, across
+    partitions (reference: run_infer_xborder_by_layer, t10n/infer.py:89-198).
+
+    Each rank holds the complete in-edge CSR of its own nodes, so the block of a layer
+    is local: destinations = own nodes, sources = own nodes plus ``own.ext_src`` (the
+    sorted external in-neighbours).  Per layer every rank (1) writes its own nodes'
+    layer input into a peer-mapped table, (2) after a barrier pulls the rows of its
+    external sources straight from their owners' tables over NVLink (pull_rows, one
+    kernel: the global id says which rank and row to read, so no id exchange is
+    needed), (3) runs the layer on the sm_100a kernels (``infer_layer``).  The last
+    layer's logits give the accuracy on the own nodes of each mask, summed over ranks.
+    Collective: every rank calls ``accuracy`` with the same masks."""
+
+    def __init__(self, model, own, comm=None):
+        from grappa_b200.block import Block
+        from grappa_b200.parallel.comm import Comm, PeerBuffer
+
+        self.model, self.own = model, own
+        self.comm = comm if comm is not None else Comm()
+        dev = own.indices.device
+        self.device = dev
+        r = own.rank
+        lo, hi = own.prefix[r], own.prefix[r + 1]
+        n_own = hi - lo
+        ext = own.ext_src.to(dev, torch.int64)
+        self.n_own, self.n_ext = n_own, int(ext.numel())
+        g = own.indices.to(torch.int64)
+        inside = (g >= lo) & (g < hi)
+        loc = torch.where(inside, g - lo, n_own + torch.searchsorted(ext, g))
+        src_ids = torch.cat([torch.arange(lo, hi, device=dev, dtype=torch.int64), ext])
+        self.block = Block(own.indptr, loc.to(torch.int32), src_ids, n_own, n_own + self.n_ext)
+        self.ext_ids = ext
+        self.n_ext_dev = torch.tensor([self.n_ext], dtype=torch.int32, device=dev)
+        self.width = max(_layer_in_width(model, i) for i in range(len(model.layers)))
+        self.prefix_dev = torch.tensor(own.prefix, dtype=torch.int64, device=dev)
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        # this rank's layer-input rows, readable by every rank
+        self.table = PeerBuffer(self.comm, max(256, n_own * self.width * 2))
+        self.T = self.table.tensor(torch.bfloat16, [max(1, n_own), self.width])
+
+    def _sync(self):
+        torch.cuda.synchronize(self.device)
+        self.comm.barrier()
+
+    def logits(self):
+        """fp32 [n_own, n_classes] logits of the own nodes with full neighbourhoods."""
+        model, own = self.model, self.own
+        d0 = own.feat.shape[1]
+        self.T.zero_()
+        self.T[:, :d0].copy_(own.feat)
+        h = None
+        with torch.no_grad():
+            for l in range(len(model.layers)):
+                w = _layer_in_width(model, l)
+                X = torch.zeros((self.n_own + self.n_ext, w), dtype=torch.bfloat16, device=self.device)
+                X[: self.n_own].copy_(self.T[:, :w])
+                self._sync()  # every rank's table holds layer l's input
+                if self.n_ext:
+                    tables = [self.table.ptrs[p] for p in range(own.world)]
+                    _native.cuda().pull_rows(tables, self.width, 2, w * 2, self.ext_ids, self.n_ext_dev, 0,
+                                             self.prefix_dev, X.data_ptr(), w, self.n_own, self.n_ext, self.err)
+                self._sync()  # every rank has read the tables: they may be overwritten
+                h = infer_layer(model, l, self.block, X)
+                if l + 1 < len(model.layers):
+                    self.T.zero_()
+                    self.T[:, :h.shape[1]].copy_(h.to(torch.bfloat16))
+        if int(self.err.item()):
+            raise RuntimeError(f"device error word {int(self.err.item()):#x} in exact inference")
+        return h
+
+    def accuracy(self, masks):
+        """Accuracy on the own nodes selected by each mask, over all ranks."""
+        logits = self.logits()
+        pred = torch.argmax(logits, dim=1)
+        ok = pred == self.own.label.to(pred.device).long()
+        vals = []
+        for m in masks:
+            m = m.to(pred.device).bool()
+            vals += [float(ok[m].sum()), float(m.sum())]
+        if self.comm.world > 1:
+            vals = self.comm.all_reduce_sum(vals)
+        return [vals[2 * i] / max(vals[2 * i + 1], 1.0) for i in range(len(masks))]
+
+    def close(self):
+        self.table.close()

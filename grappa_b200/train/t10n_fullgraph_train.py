@@ -127,7 +127,9 @@ def run_gpu(args):
         losses.append(loss)
         rank_print("epoch_|epoch|{:04d}|part|{:04d}|epoch_seconds|{:.4f}|loss|{:.4f}".format(
             epoch, rank, time.time() - tic, loss))
-    acc = {k: tr.evaluate(m) for k, m in (("val", own.val_mask), ("test", own.test_mask), ("train", own.train_mask))}
+    # exact layer-wise inference across partitions (full neighbourhoods, not the isolated partition)
+    va, te, trn = tr.evaluate_exact([own.val_mask, own.test_mask, own.train_mask])
+    acc = {"val": va, "test": te, "train": trn}
     rank_print("infer_|epoch|{:04d}|part|{:04d}|val_acc|{:.4f}|test_acc|{:.4f}|train_acc|{:.4f}".format(
         args.num_epochs - 1, rank, acc["val"], acc["test"], acc["train"]))
     save_to_ckpt(args, args.num_epochs - 1, rank, model, tr.engine.optimizer_state_dict(), losses[-1] if losses else 0)

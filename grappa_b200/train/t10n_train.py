@@ -200,7 +200,7 @@ def run_gpu(args):
         rank_print("epoch_|epoch|{:04d}|part|{:04d}|epoch_seconds|{:.4f}|loss|{:.4f}|n_seed|{:012d}".format(
             epoch, rank, toc - tic, float(loss), int(trainer.train_ids.numel())))
         if epoch != 0 and (epoch + 1) % args.eval_every == 0:
-            val_acc = trainer.evaluate(own.val_mask)
+            val_acc = trainer.evaluate_exact([own.val_mask])[0]
             rank_print(f"epoch={epoch}, val_acc={val_acc}")
             if val_acc >= best["val_acc"]:
                 best["val_acc"] = val_acc
@@ -209,8 +209,9 @@ def run_gpu(args):
     if best["state_dict"] is not None:
         t0 = time.time()
         trainer.load_state_dict(best["state_dict"])
-        acc = {k: trainer.evaluate(m) for k, m in (("val", own.val_mask), ("test", own.test_mask),
-                                                   ("train", own.train_mask))}
+        # exact layer-wise inference across partitions (reference: run_infer_xborder_by_layer)
+        va, te, trn = trainer.evaluate_exact([own.val_mask, own.test_mask, own.train_mask])
+        acc = {"val": va, "test": te, "train": trn}
         rank_print("infer_|epoch|{:04d}|part|{:04d}|val_acc|{:.4f}|test_acc|{:.4f}|train_acc|{:.4f}|time_sec|{:.4f}"
                    .format(epoch, rank, acc["val"], acc["test"], acc["train"], time.time() - t0))
         summary.update(val_acc=acc["val"], test_acc=acc["test"], train_acc=acc["train"])

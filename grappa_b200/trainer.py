@@ -184,6 +184,12 @@ class MiniBatchTrainer:
             correct, total = self.comm.all_reduce_sum([correct, total])
         return correct / max(total, 1.0)
 
+    def evaluate_exact(self, masks):
+        """Exact accuracy (full neighbourhoods across partitions, layer by layer, the
+        reference's run_infer_xborder_by_layer) on the own nodes selected by each mask,
+        over all ranks; a collective.  ``evaluate`` samples instead."""
+        return _exact_accuracy(self, masks)
+
     def load_state_dict(self, state_dict):
         """Load model weights into the flat master buffer and refresh the bf16 working copy."""
         self.model.load_state_dict(state_dict)
@@ -194,10 +200,22 @@ class MiniBatchTrainer:
         if getattr(self, "_pool", None) is not None:
             self._pool.shutdown(wait=True)
             self._pool = None
+        if getattr(self, "_exact", None) is not None:
+            self._exact.close()
+            self._exact = None
         self.engine._graph = None
         if self.engine.allreduce is not None:
             self.engine.allreduce.close()
         self.store.close()
+
+
+def _exact_accuracy(trainer, masks):
+    from grappa_b200.infer_gpu import ExactInference
+
+    torch.cuda.synchronize(trainer.device)
+    if getattr(trainer, "_exact", None) is None:
+        trainer._exact = ExactInference(trainer.model, trainer.own, trainer.comm)
+    return trainer._exact.accuracy(masks)
 
 
 def full_graph_blocks(working, n_layers, own):
@@ -322,6 +340,10 @@ class FullGraphTrainer:
             correct, total = self.comm.all_reduce_sum([correct, total])
         return correct / max(total, 1.0)
 
+    def evaluate_exact(self, masks):
+        """Exact full-neighbour layer-wise accuracy over all ranks (see MiniBatchTrainer)."""
+        return _exact_accuracy(self, masks)
+
     def load_state_dict(self, state_dict):
         """Load model weights into the flat master buffer and refresh the bf16 working copy."""
         self.model.load_state_dict(state_dict)
@@ -329,6 +351,9 @@ class FullGraphTrainer:
             self.engine.wbf.copy_(self.engine.flat)
 
     def close(self):
+        if getattr(self, "_exact", None) is not None:
+            self._exact.close()
+            self._exact = None
         self.engine._graph = None
         if self.engine.allreduce is not None:
             self.engine.allreduce.close()

@@ -3,9 +3,12 @@
 ``XBorder`` is the C++ helper (grappa_b200/csrc/host/xborder.cc).  ``xb_gather``
 fetches rows (features or embeddings) of arbitrary global ids owner-computes
 style: ids are grouped by owner and exchanged, every owner gathers the requested
-rows from its shard and sends them back (two ragged all-to-alls).  This is the
-CPU/gloo path; on GPUs the same fetch is a direct peer-memory pull
-(grappa_b200/csrc/cuda/peer.cu, pull_rows).
+rows from its shard and sends them back (two ragged all-to-alls).  With NCCL/gloo
+that is the CPU path; when ``comm_dev`` is a ``grappa_b200.cl.PeerAllToAll`` both
+exchanges run through NVLink peer memory (``xb_gather_peer``).  Exact layer-wise
+inference on GPUs skips the id exchange altogether: the global id names the owner
+and the row, so it pulls the rows straight from the owners' tables
+(grappa_b200/csrc/cuda/peer.cu, pull_rows; grappa_b200.infer_gpu.ExactInference).
 """
 import torch
 
@@ -44,8 +47,39 @@ def xb_ad_hoc_fill_batch_feat(xb, device, input_nodes, local_feat_n, rank, nbr_i
     return out.to(device)
 
 
+def _group_by_owner(ids, prefix_sum, world_size):
+    """(ids sorted by owner, the sort order, per-owner counts) on the ids' device."""
+    bounds = torch.tensor(prefix_sum[1:], dtype=torch.int64, device=ids.device)
+    owner = torch.bucketize(ids, bounds, right=True)
+    order = torch.argsort(owner, stable=True)
+    counts = torch.bincount(owner, minlength=world_size).cpu().tolist()
+    return ids[order], order, counts
+
+
+def xb_gather_peer(a2a, batch_input, target_nodes, emb_self, rank, world_size, prefix_sum):
+    """GPU form of ``xb_gather``: the ids grouped by owner go to the owners and the owners'
+    rows come back, both through the peer-memory all-to-all ``a2a``."""
+    dev = emb_self.device
+    ids = target_nodes.to(dev).long()
+    sorted_ids, order, counts = _group_by_owner(ids, prefix_sum, world_size)
+    requests = a2a.exchange(list(torch.split(sorted_ids, counts)))
+    lo = prefix_sum[rank]
+    replies = [emb_self[(q.long() - lo)].contiguous() for q in requests]
+    rows = a2a.exchange(replies)
+    got = torch.cat(rows) if rows else emb_self[:0]
+    out = torch.empty((ids.numel(),) + tuple(emb_self.shape[1:]), dtype=emb_self.dtype, device=dev)
+    out[order] = got
+    cols = batch_input.shape[1] if batch_input.dim() > 1 else None
+    batch_input.copy_((out[:, :cols] if cols is not None else out).to(batch_input.device, batch_input.dtype))
+    return batch_input
+
+
 def xb_gather(xb, comm_dev, batch_input, target_nodes, emb_self, rank, world_size, prefix_sum):
     """batch_input[i] = row of global id target_nodes[i], fetched from its owner."""
+    from grappa_b200.cl import PeerAllToAll
+
+    if isinstance(comm_dev, PeerAllToAll):
+        return xb_gather_peer(comm_dev, batch_input, target_nodes, emb_self, rank, world_size, prefix_sum)
     groups, mask = xb_group_by_partition(xb, target_nodes, world_size)
     own_idx = torch.nonzero(mask[rank]).flatten()
     if own_idx.numel():
