@@ -168,6 +168,8 @@ def main():
     ap.add_argument("--batch", type=int, default=1024, help="seeds per GPU per mini-batch")
     ap.add_argument("--no-graph", action="store_true", help="disable CUDA graph capture")
     ap.add_argument("--no-fused-ar", action="store_true", help="use the NCCL gradient path")
+    ap.add_argument("--no-ar-overlap", action="store_true",
+                    help="one fused all-reduce after the backward pass instead of one per layer during it")
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--no-eval", action="store_true",
                     help="skip the validation/test accuracy after the timed epochs (default for the 111M-node GAT)")
@@ -222,7 +224,7 @@ def main():
     else:
         trainer = MiniBatchTrainer(model, own, wl["fanouts"], args.batch, lr=3e-3, repart_every=wl["repart"],
                                    comm=comm, seed=7, fused_allreduce=not args.no_fused_ar,
-                                   use_cuda_graph=not args.no_graph)
+                                   use_cuda_graph=not args.no_graph, overlap_allreduce=not args.no_ar_overlap)
     trainer.warmup()
     launches_per_step = trainer.engine.launches_per_step
     def run_epoch(e):
@@ -293,6 +295,16 @@ def main():
                "method": "exact layer-wise inference, full neighbourhoods across partitions",
                "seconds": round(time.perf_counter() - t0, 3)}
 
+    # device time of each step phase over a few eager steps (after the timed epochs)
+    phases = None
+    if not full:
+        ps, pc = trainer.epoch_seeds(0, on_host=False)
+        trainer.engine.set_epoch(e1 + args.steps + 1)
+        phases = {k: round(v, 4) for k, v in trainer.engine.time_phases(ps, pc, min(8, trainer.n_batches)).items()}
+        phases["note"] = ("eager steps, CUDA events on the launching stream; with the per-layer all-reduce "
+                          "the update phase is the wait for the last buckets")
+        trainer.engine.check_errors()
+
     out = {
         "metric": METRICS[args.workload],
         "value": round(ms_dev / 1000.0, 6),
@@ -327,6 +339,8 @@ def main():
     }
     if acc:
         out["accuracy"] = acc
+    if phases:
+        out["phase_ms"] = phases
     if args.workload != "sage":
         out["workload"] = args.workload
     if rank == 0:

@@ -375,10 +375,35 @@ void sampler_counters(Tensor main, Tensor dst, int64_t step_offset) {
                              stream());
 }
 
-void step_end(Tensor counters) {
+void step_end(Tensor counters, OptT ring_slot, OptT fstats, OptT istats) {
   c10::cuda::CUDAGuard g(counters.device());
   TORCH_CHECK(counters.numel() >= 6, "counters needs 6 entries");
-  d::launch_step_end(ptr<int64_t>(counters, at::kLong, "counters"), stream());
+  d::launch_step_end(ptr<int64_t>(counters, at::kLong, "counters"), optr<int64_t>(ring_slot, at::kLong, "ring_slot"),
+                     optr<float>(fstats, at::kFloat, "fstats"), fstats ? static_cast<int>(fstats->numel()) : 0,
+                     optr<int32_t>(istats, at::kInt, "istats"), istats ? static_cast<int>(istats->numel()) : 0,
+                     stream());
+}
+
+void sample_prologue(Tensor main, Tensor dst, int64_t step_offset, OptT cov, OptT table_slot, OptT count_table,
+                     Tensor seeds, Tensor n_seeds, OptT labels, OptT seed_labels, OptT gideg, OptT seed_gideg) {
+  c10::cuda::CUDAGuard g(main.device());
+  TORCH_CHECK(main.numel() >= 6 && dst.numel() >= 6, "counters need 6 entries");
+  d::SamplePrologueArgs a;
+  a.main = ptr<int64_t>(main, at::kLong, "main");
+  a.dst = ptr<int64_t>(dst, at::kLong, "dst");
+  a.step_offset = step_offset;
+  a.cov = optr<float>(cov, at::kFloat, "cov");
+  a.table_slot = optr<int64_t>(table_slot, at::kLong, "table_slot");
+  a.count_table = optr<int32_t>(count_table, at::kInt, "count_table");
+  a.n_rows = count_table ? static_cast<int32_t>(count_table->numel()) : 0;
+  a.B = static_cast<int32_t>(seeds.numel());
+  a.seeds = ptr<int32_t>(seeds, at::kInt, "seeds");
+  a.n_seeds = ptr<int32_t>(n_seeds, at::kInt, "n_seeds");
+  a.labels = optr<int32_t>(labels, at::kInt, "labels");
+  a.seed_labels = optr<int32_t>(seed_labels, at::kInt, "seed_labels");
+  a.gideg = optr<int64_t>(gideg, at::kLong, "gideg");
+  a.seed_gideg = optr<int64_t>(seed_gideg, at::kLong, "seed_gideg");
+  d::launch_sample_prologue(a, stream());
 }
 
 // --------------------------------------------------------------------------- peer memory
@@ -943,7 +968,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dropout_mask", &dropout_mask);
   m.def("adam", &adam);
   m.def("zero_", &zero_);
-  m.def("step_end", &step_end);
+  m.def("step_end", &step_end, py::arg("counters"), py::arg("ring_slot") = py::none(), py::arg("fstats") = py::none(),
+        py::arg("istats") = py::none());
+  m.def("sample_prologue", &sample_prologue);
   m.def("sampler_counters", &sampler_counters);
   m.def("peer_alloc", [](int64_t bytes) { return reinterpret_cast<int64_t>(grappa::peer::alloc(bytes)); });
   m.def("peer_free", [](int64_t p) { grappa::peer::release(reinterpret_cast<void*>(p)); });

@@ -180,6 +180,22 @@ __global__ void __launch_bounds__(kThreads) gat_scores_kernel(GatArgs a) {
 }
 
 // ------------------------------------------------------------------ forward
+// One pass over the in-edges of a destination with an online softmax: the edges are
+// taken 32 at a time (one coalesced load of their source ids, then lane t loads the
+// el row of edge t), every head's running max m and denominator s are updated from the
+// batch's scores by warp reductions, the accumulated rows are rescaled by exp(m_old -
+// m_new), and the z rows of the batch are added with the weights exp(x - m), four
+// edges' rows in flight per lane.  The output is acc / s (+ bias); m and s are kept
+// for the backward, which recomputes the attention from them.
+template <int CPL>
+__device__ __forceinline__ float pick_head(const float (&v)[kMaxHeads], int h) {
+  float r = 0.f;
+#pragma unroll
+  for (int hh = 0; hh < kMaxHeads; ++hh)
+    if (hh == h) r = v[hh];
+  return r;
+}
+
 template <int CPL>
 __global__ void __launch_bounds__(kThreads) gat_fwd_kernel(GatArgs a) {
   extern __shared__ float s_row[];  // mean_heads: [warps][HF]
@@ -199,6 +215,19 @@ __global__ void __launch_bounds__(kThreads) gat_fwd_kernel(GatArgs a) {
     thr = static_cast<uint32_t>(static_cast<double>(a.dropout_p) * 4294967296.0);
     ks = 1.f / (1.f - a.dropout_p);
   }
+  constexpr int EU = CPL <= 1 ? 4 : 2;  // edges whose z rows are in flight together
+  int h0[CPL], h1[CPL];
+  uint32_t in0[CPL];  // bit j: column c0 + j belongs to head h0 (else to h1)
+#pragma unroll
+  for (int q = 0; q < CPL; ++q) {
+    const int c0 = (lane + 32 * q) * 8;
+    h0[q] = min(c0 / F, H - 1);
+    h1[q] = min(h0[q] + 1, H - 1);
+    in0[q] = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if ((c0 + j) / F == h0[q]) in0[q] |= 1u << j;
+  }
   for (int v = (blockIdx.x * kThreads + threadIdx.x) >> 5; v < rows_end; v += warps_total) {
     if (v >= n_dst) {
       for (int c = lane * 8; c < a.ldo; c += 256)
@@ -206,54 +235,102 @@ __global__ void __launch_bounds__(kThreads) gat_fwd_kernel(GatArgs a) {
       continue;
     }
     const int beg = a.indptr[v], end = a.indptr[v + 1];
-    // pass 1: lane h owns head h
-    float m = -INFINITY, s = 0.f, er_h = 0.f;
-    if (lane < H) {
-      er_h = a.er[static_cast<int64_t>(v) * H + lane];
-      for (int e = beg; e < end; ++e) {
-        const int u = a.indices[e];
-        const float x = leaky(a.el[static_cast<int64_t>(u) * H + lane] + er_h, a.slope);
-        if (x > m) {
-          s = s * __expf(m - x) + 1.f;
-          m = x;
-        } else {
-          s += __expf(x - m);
-        }
-      }
-      a.smax[static_cast<int64_t>(v) * H + lane] = m;
-      a.ssum[static_cast<int64_t>(v) * H + lane] = s;
-    }
-    // pass 2: weighted sum of z rows
-    float acc[CPL][8];
-    int h0[CPL];
+    float er[kMaxHeads], m[kMaxHeads], sden[kMaxHeads];
 #pragma unroll
-    for (int q = 0; q < CPL; ++q) {
-      h0[q] = min(((lane + 32 * q) * 8) / F, H - 1);
+    for (int h = 0; h < kMaxHeads; ++h) {
+      er[h] = h < H ? a.er[static_cast<int64_t>(v) * H + h] : 0.f;
+      m[h] = -INFINITY;
+      sden[h] = 0.f;
+    }
+    float acc[CPL][8];
+#pragma unroll
+    for (int q = 0; q < CPL; ++q)
 #pragma unroll
       for (int j = 0; j < 8; ++j) acc[q][j] = 0.f;
-    }
-    for (int e = beg; e < end; ++e) {
-      const int u = a.indices[e];
-      // attention of every head for this edge, computed by lane h and broadcast
-      float al = 0.f;
-      if (lane < H) {
-        const float x = leaky(a.el[static_cast<int64_t>(u) * H + lane] + er_h, a.slope);
-        al = __expf(x - m) / s;
+    for (int cb = beg; cb < end; cb += 32) {
+      const int cnt = min(32, end - cb);
+      const bool mine = lane < cnt;
+      const int my_u = mine ? a.indices[cb + lane] : 0;
+      float w[kMaxHeads], sc[kMaxHeads];
+      float x[kMaxHeads];
+      if (H == 4) {
+        float4 e4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (mine) e4 = *reinterpret_cast<const float4*>(a.el + static_cast<int64_t>(my_u) * 4);
+        x[0] = e4.x; x[1] = e4.y; x[2] = e4.z; x[3] = e4.w;
+#pragma unroll
+        for (int h = 4; h < kMaxHeads; ++h) x[h] = 0.f;
+      } else {
+#pragma unroll
+        for (int h = 0; h < kMaxHeads; ++h) x[h] = (mine && h < H) ? a.el[static_cast<int64_t>(my_u) * H + h] : 0.f;
+      }
+#pragma unroll
+      for (int h = 0; h < kMaxHeads; ++h) {
+        if (h >= H) {
+          w[h] = 0.f;
+          sc[h] = 1.f;
+          continue;
+        }
+        const float xs = mine ? leaky(x[h] + er[h], a.slope) : -INFINITY;
+        float bm = xs;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o));
+        const float nm = fmaxf(m[h], bm);
+        sc[h] = __expf(m[h] - nm);  // 0 on the first batch (m = -inf)
+        w[h] = mine ? __expf(xs - nm) : 0.f;
+        sden[h] = sden[h] * sc[h] + warp_sum(w[h]);
+        m[h] = nm;
       }
 #pragma unroll
       for (int q = 0; q < CPL; ++q) {
         const int c0 = (lane + 32 * q) * 8;
-        const float a0 = __shfl_sync(0xffffffffu, al, h0[q]);
-        const float a1 = __shfl_sync(0xffffffffu, al, min(h0[q] + 1, H - 1));
-        if (c0 >= HF) continue;
-        float f[8];
-        bf16x8_to_f32(*reinterpret_cast<const uint4*>(a.z + static_cast<int64_t>(u) * a.ldz + c0), f);
+        const float s0 = pick_head<CPL>(sc, h0[q]), s1 = pick_head<CPL>(sc, h1[q]);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int h = (c0 + j) / F;
-          acc[q][j] += (h == h0[q] ? a0 : a1) * f[j];
-        }
+        for (int j = 0; j < 8; ++j) acc[q][j] *= ((in0[q] >> j) & 1u) ? s0 : s1;
       }
+      for (int k = 0; k < cnt; k += EU) {
+        uint4 zv[EU][CPL];
+        float wt0[EU][CPL], wt1[EU][CPL];
+#pragma unroll
+        for (int t = 0; t < EU; ++t) {
+          const int src_lane = min(k + t, 31);
+          const int u = __shfl_sync(0xffffffffu, my_u, src_lane);
+          const bool ok = k + t < cnt;
+          float wl[kMaxHeads];
+#pragma unroll
+          for (int h = 0; h < kMaxHeads; ++h) wl[h] = h < H ? __shfl_sync(0xffffffffu, w[h], src_lane) : 0.f;
+#pragma unroll
+          for (int q = 0; q < CPL; ++q) {
+            const int c0 = (lane + 32 * q) * 8;
+            wt0[t][q] = ok ? pick_head<CPL>(wl, h0[q]) : 0.f;
+            wt1[t][q] = ok ? pick_head<CPL>(wl, h1[q]) : 0.f;
+            zv[t][q] = make_uint4(0, 0, 0, 0);
+            if (ok && c0 < HF) zv[t][q] = *reinterpret_cast<const uint4*>(a.z + static_cast<int64_t>(u) * a.ldz + c0);
+          }
+        }
+#pragma unroll
+        for (int t = 0; t < EU; ++t)
+#pragma unroll
+          for (int q = 0; q < CPL; ++q) {
+            const int c0 = (lane + 32 * q) * 8;
+            float f[8];
+            bf16x8_to_f32(zv[t][q], f);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[q][j] = fmaf(((in0[q] >> j) & 1u) ? wt0[t][q] : wt1[t][q], f[j], acc[q][j]);
+          }
+      }
+    }
+    // normalise by the softmax denominators; keep the statistics for the backward
+    if (lane < H) {
+      a.smax[static_cast<int64_t>(v) * H + lane] = pick_head<CPL>(m, lane);
+      a.ssum[static_cast<int64_t>(v) * H + lane] = pick_head<CPL>(sden, lane);
+    }
+#pragma unroll
+    for (int q = 0; q < CPL; ++q) {
+      const int c0 = (lane + 32 * q) * 8;
+      const float d0 = pick_head<CPL>(sden, h0[q]), d1 = pick_head<CPL>(sden, h1[q]);
+      const float i0 = d0 > 0.f ? 1.f / d0 : 0.f, i1 = d1 > 0.f ? 1.f / d1 : 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[q][j] *= ((in0[q] >> j) & 1u) ? i0 : i1;
     }
     if (!a.mean_heads) {
 #pragma unroll

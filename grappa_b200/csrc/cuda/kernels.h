@@ -407,8 +407,38 @@ void launch_gat_dw_combine(const float* T, int64_t ldt, const float* xl, const f
                            const float* attn_r, int heads, int feat, int in_dim, float* dw, int64_t ldw,
                            cudaStream_t stream);
 
-// counters = [seed, epoch, step_in_epoch, global_step, gen, adam_t]: advance the step
-void launch_step_end(int64_t* counters, cudaStream_t stream);
+// counters = [seed, epoch, step_in_epoch, global_step, gen, adam_t]: advance the step.
+// With ring_slot (a device int64 holding the address of a float ring, 0 for none) the
+// step's loss fstats[2] is stored at ring[step_in_epoch] first (the ring may be pinned
+// host memory: a device -> host write); fstats[0..nf) and istats[0..ni) are then
+// cleared for the next step (nf = ni = 0 keeps them).
+void launch_step_end(int64_t* counters, const int64_t* ring_slot, float* fstats, int nf, int32_t* istats, int ni,
+                     cudaStream_t stream);
+
+// Step prologue of a sampler: its counters for the step step_offset ahead of the
+// main ones (as launch_sampler_counters), its coverage sums cleared, and the step's
+// seeds.  With table_slot (a device int64 holding the address of an int32 [n_rows, B]
+// seed table, which may be pinned host memory read over PCIe; 0 = seeds already in
+// place) row main[step] + step_offset is copied into seeds and its count
+// count_table[row] (0 past the last row) into *n_seeds.  Then the labels (int32) and
+// global in-degrees (int64, optional) of the seeds are gathered.
+struct SamplePrologueArgs {
+  const int64_t* main = nullptr;
+  int64_t* dst = nullptr;
+  int64_t step_offset = 0;
+  float* cov = nullptr;
+  const int64_t* table_slot = nullptr;
+  const int32_t* count_table = nullptr;
+  int32_t n_rows = 0;
+  int32_t B = 0;
+  int32_t* seeds = nullptr;
+  int32_t* n_seeds = nullptr;
+  const int32_t* labels = nullptr;
+  int32_t* seed_labels = nullptr;
+  const int64_t* gideg = nullptr;
+  int64_t* seed_gideg = nullptr;
+};
+void launch_sample_prologue(const SamplePrologueArgs& a, cudaStream_t stream);
 // The counters a sampler draws with for the step step_offset ahead of the main
 // counters (seed, epoch, step + offset), with its own compaction generation (+1).
 void launch_sampler_counters(const int64_t* main, int64_t* dst, int64_t step_offset, cudaStream_t stream);

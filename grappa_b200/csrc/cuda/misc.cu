@@ -289,11 +289,52 @@ __global__ void sampler_counters_kernel(const int64_t* main, int64_t* dst, int64
   dst[5] = main[5];
 }
 
-__global__ void step_end_kernel(int64_t* counters) {
+__global__ void step_end_kernel(int64_t* counters, const int64_t* ring_slot, float* fstats, int nf, int32_t* istats,
+                                int ni) {
+  if (ring_slot) {
+    float* ring = reinterpret_cast<float*>(static_cast<uintptr_t>(*ring_slot));
+    if (ring && fstats) ring[counters[2]] = fstats[2];
+  }
+  for (int i = 0; i < nf; ++i) fstats[i] = 0.f;
+  for (int i = 0; i < ni; ++i) istats[i] = 0;
   counters[2] += 1;
   counters[3] += 1;
   counters[4] += 1;
   counters[5] += 1;
+}
+
+__global__ void sample_prologue_kernel(SamplePrologueArgs a) {
+  const int64_t row = a.main[2] + a.step_offset;
+  const int32_t* table =
+      a.table_slot ? reinterpret_cast<const int32_t*>(static_cast<uintptr_t>(*a.table_slot)) : nullptr;
+  const int n = table ? (row >= 0 && row < a.n_rows ? a.count_table[row] : 0) : *a.n_seeds;
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    a.dst[0] = a.main[0];
+    a.dst[1] = a.main[1];
+    a.dst[2] = a.main[2] + a.step_offset;
+    a.dst[3] = a.main[3] + a.step_offset;
+    a.dst[4] += 1;  // the sampler's own compaction generation
+    a.dst[5] = a.main[5];
+    if (a.cov) {
+      a.cov[0] = 0.f;
+      a.cov[1] = 0.f;
+    }
+  }
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.B; i += gridDim.x * blockDim.x) {
+    int32_t s;
+    if (table) {
+      s = i < n ? table[row * a.B + i] : 0;
+      a.seeds[i] = s;
+    } else {
+      s = a.seeds[i];
+    }
+    if (i < n) {
+      if (a.seed_labels) a.seed_labels[i] = a.labels[s];
+      if (a.seed_gideg) a.seed_gideg[i] = a.gideg[s];
+    }
+  }
+  // every block derived n itself; one writes it (the table-less path only reads it)
+  if (table && blockIdx.x == 0 && threadIdx.x == 0) *a.n_seeds = n;
 }
 
 }  // namespace
@@ -389,8 +430,20 @@ void launch_sampler_counters(const int64_t* main, int64_t* dst, int64_t step_off
   GB_LAUNCH_CHECK();
 }
 
-void launch_step_end(int64_t* counters, cudaStream_t stream) {
-  step_end_kernel<<<1, 1, 0, stream>>>(counters);
+void launch_step_end(int64_t* counters, const int64_t* ring_slot, float* fstats, int nf, int32_t* istats, int ni,
+                     cudaStream_t stream) {
+  step_end_kernel<<<1, 1, 0, stream>>>(counters, ring_slot, fstats, fstats ? nf : 0, istats, istats ? ni : 0);
+  GB_LAUNCH_CHECK();
+}
+
+void launch_sample_prologue(const SamplePrologueArgs& a, cudaStream_t stream) {
+  if (a.B <= 0) throw std::invalid_argument("sample_prologue: empty batch capacity");
+  if (a.table_slot && !a.count_table) throw std::invalid_argument("sample_prologue: a seed table needs its counts");
+  if ((a.seed_labels && !a.labels) || (a.seed_gideg && !a.gideg))
+    throw std::invalid_argument("sample_prologue: gathered outputs need their tables");
+  const int threads = 1024;
+  const int blocks = static_cast<int>(std::min<int64_t>(8, (a.B + threads - 1) / threads));
+  sample_prologue_kernel<<<blocks, threads, 0, stream>>>(a);
   GB_LAUNCH_CHECK();
 }
 

@@ -47,7 +47,7 @@ KERNELS_PER_CALL = {
     "sample_hop": 1, "walk_hop": 1, "compact": 3, "gemm": 1, "aggregate": 1, "aggregate_bwd": 1, "act_bwd": 1,
     "gather_scalar": 1, "gather_rows": 1, "adam": 1, "step_end": 1, "src_norm": 2,
     "pull_rows": 1, "csr_merge": 1, "mark_ids": 1, "iota_map": 1, "mark_compact": 1, "peer_copy": 1, "a2a_pull": 1, "peer_barrier": 1,
-    "shuffle_keys": 1, "cross_entropy": 1, "batchnorm_fwd": 2, "batchnorm_bwd": 2, "l2norm_fwd": 1,
+    "shuffle_keys": 1, "sample_prologue": 1, "cross_entropy": 1, "batchnorm_fwd": 2, "batchnorm_bwd": 2, "l2norm_fwd": 1,
     "l2norm_bwd": 1, "dropout_rows": 1, "dropout_grad": 1, "f32_to_bf16_rows": 1, "add_bf16_rows": 1,
     "gat_scores": 1, "gat_fwd": 1, "gat_bwd": 2, "gat_bwd_input": 2, "gat_dw_combine": 1, "sampler_counters": 1,
 }
@@ -251,6 +251,11 @@ class BlockEngine:
         self.fstats = torch.zeros(4, dtype=torch.float32, device=dev)  # cov_sum, cov_n, loss_sum, spare
         self.istats = torch.zeros(2, dtype=torch.int32, device=dev)   # correct, spare
         self._ce_dummy = torch.zeros((1, 1), dtype=torch.float32, device=dev)
+        # device slots read by the step graphs: [address of the epoch's seed table (0 =
+        # seeds loaded by the host), address of the per-step loss ring (0 = none)]
+        self._slots = torch.zeros(2, dtype=torch.int64, device=dev)
+        self._count_table = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._seed_table = None
         if self.allreduce is not None:
             self.allreduce.bind(self.counters, self.m, self.v, self.wbf, self.lr, self.betas, self.eps, self.err)
 
@@ -425,11 +430,13 @@ class BlockEngine:
             return
         w = self._working
         sm = self.samplers[q]
-        cu = self.cu
-        cu.sampler_counters(self.counters, self.scnt[q], step_offset)
-        cu.zero_(self.covs[q])
-        cu.gather_scalar(self.labels, sm.seeds, sm.n_seeds(), 0, self.B, self.seed_labels[q])
-        sm.sample(w.indptr, w.indices, self.scnt[q], gideg=self.gideg, cov=self.covs[q], err=self.err)
+        # one prologue kernel: the sampler's counters, its coverage sums cleared, the
+        # step's seeds from the epoch table (when one is bound), their labels and degrees
+        self.cu.sample_prologue(self.counters, self.scnt[q], step_offset, self.covs[q], self._slots[0:1],
+                                self._count_table, sm.seeds, sm.cnt[0:1], self.labels, self.seed_labels[q],
+                                self.gideg, sm.seed_gideg if self.gideg is not None else None)
+        sm.sample(w.indptr, w.indices, self.scnt[q], gideg=self.gideg, cov=self.covs[q], err=self.err,
+                  seed_gideg_ready=True)
 
     def _sample(self):
         self._sample_into(self.p_cur, 0)
@@ -490,11 +497,11 @@ class BlockEngine:
 
     def _overlapped_step_body(self, p, prefetch):
         """Layers of the step on sampler p; with ``prefetch`` the next step is sampled
-        into the other sampler on a side stream that joins before the counters advance."""
+        into the other sampler on a side stream that joins before the counters advance.
+        The step's loss goes to the bound ring and the statistics are cleared for the
+        next step by step_end (the graphs start with them cleared)."""
         self._select(p)
         main = torch.cuda.current_stream(self.device)
-        self.cu.zero_(self.fstats)
-        self.cu.zero_(self.istats)
         if prefetch:
             side = torch.cuda.Stream(device=self.device)
             side.wait_stream(main)
@@ -505,13 +512,30 @@ class BlockEngine:
         self._update()
         if prefetch:
             main.wait_stream(side)
-        self.cu.step_end(self.counters)
+        self.cu.step_end(self.counters, self._slots[1:2], self.fstats, self.istats)
 
     def _graph_for(self, key):
         g = self._graphs.get(key)
         if g is None:
             torch.cuda.synchronize(self.device)
-            if key[0] == "sample":
+            if key[0] == "epoch":
+                nb = key[1]
+
+                def body():
+                    # one epoch: the first step's sampling, then every step with the next
+                    # step's sampling on the side stream; seeds come from the bound table
+                    self.cu.zero_(self.fstats)
+                    self.cu.zero_(self.istats)
+                    self._select(0)
+                    self._sample_into(0, 0)
+                    p = 0
+                    for s_ in range(nb):
+                        self._overlapped_step_body(p, s_ + 1 < nb)
+                        p ^= 1
+                    self._select(0)
+
+                g = self._capture(body)
+            elif key[0] == "sample":
                 p = key[1]
 
                 def body():
@@ -540,18 +564,39 @@ class BlockEngine:
                 if ring is not None:
                     ring[s:s + 1].copy_(self.fstats[2:3], non_blocking=True)
             return
-        p = 0
-        self._load_into(p, seeds[0], counts[0])
-        self._graph_for(("sample", p)).replay()
-        for s in range(nb):
-            nxt = s + 1 < nb
-            if nxt:
-                self._load_into(1 - p, seeds[s + 1], counts[s + 1])
-            self._graph_for(("step", p, nxt)).replay()
-            if ring is not None:
-                ring[s:s + 1].copy_(self.fstats[2:3], non_blocking=True)
-            p ^= 1
+        self._bind_epoch(seeds, counts, ring)
+        self._graph_for(("epoch", nb)).replay()
+        self._slots.zero_()  # eager steps after the epoch load their own seeds
         self._select(0)
+
+    def _bind_epoch(self, seeds, counts, ring):
+        """Point the epoch graph at this epoch's seed table and loss ring.  Seeds in pinned
+        host memory are read by the step prologue straight over PCIe (the host -> device
+        copy of each step's seeds), device seeds are copied into a fixed table first; the
+        loss ring (pinned host memory) is written by step_end (device -> host)."""
+        nb, B = int(seeds.shape[0]), int(seeds.shape[1])
+        if B != self.B:
+            raise ValueError("seed table width differs from the batch capacity")
+        if self._count_table.numel() != nb:
+            # the captured graphs hold the table's address: capture again
+            torch.cuda.synchronize(self.device)
+            self._count_table = torch.zeros(nb, dtype=torch.int32, device=self.device)
+            self._graphs = {}
+            self._graph = None
+        self._count_table.copy_(counts.view(-1), non_blocking=True)
+        if seeds.is_cuda:
+            if self._seed_table is None or tuple(self._seed_table.shape) != (nb, B):
+                self._seed_table = torch.zeros((nb, B), dtype=torch.int32, device=self.device)
+            self._seed_table.copy_(seeds, non_blocking=True)
+            table = self._seed_table.data_ptr()
+        else:
+            if not seeds.is_pinned():
+                raise ValueError("host seed tables must be pinned (read by the device over PCIe)")
+            table = seeds.data_ptr()
+        if ring is not None and not ring.is_pinned():
+            raise ValueError("the loss ring must be pinned host memory")
+        self._slots[0].fill_(table)
+        self._slots[1].fill_(0 if ring is None else ring.data_ptr())
 
     def load_seeds(self, seeds, count):
         """Copy this step's seeds ([B] int32) and seed count ([1] int32) into the static

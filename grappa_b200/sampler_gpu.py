@@ -88,16 +88,18 @@ class GpuNeighborSampler:
         return self.seeds if h == 0 else self.src[h - 1]
 
     # sampling --------------------------------------------------------------------------
-    def sample(self, indptr, indices, counters, gideg=None, cov=None, err=None):
+    def sample(self, indptr, indices, counters, gideg=None, cov=None, err=None, seed_gideg_ready=False):
         """Sample every hop from ``self.seeds[:cnt[0]]`` on the graph (indptr int64 [n+1],
         indices int32).  ``counters`` (device int64 [6]) supplies seed/epoch/step for the
         Philox keys and the compaction tag generation; gideg (per node, int64) and cov
-        (float [2]) enable the coverage counter of the seed hop."""
+        (float [2]) enable the coverage counter of the seed hop; ``seed_gideg_ready`` says
+        that the seeds' in-degrees are already in ``seed_gideg`` (the engine's step
+        prologue gathers them)."""
         cu = self.cu
         err = self.err if err is None else err
         if indptr.numel() - 1 > self.n_nodes_cap:
             raise ValueError("graph larger than the sampler's node capacity")
-        if gideg is not None:
+        if gideg is not None and not seed_gideg_ready:
             cu.gather_scalar(gideg, self.seeds, self.n_seeds(), 0, self.B, self.seed_gideg)
         for h in range(self.L):
             dst = self.dst(h)

@@ -26,7 +26,7 @@ from grappa_b200.graph_store import PartitionStore, next_neighbor
 
 class MiniBatchTrainer:
     def __init__(self, model, own, fanouts, batch_size, lr=3e-3, repart_every=10, comm=None, seed=0,
-                 fused_allreduce=True, use_cuda_graph=True, ar_mode=None):
+                 fused_allreduce=True, use_cuda_graph=True, ar_mode=None, overlap_allreduce=True):
         self.model = model
         self.own = own
         self.comm = comm
@@ -49,7 +49,8 @@ class MiniBatchTrainer:
         self.batch_size = max(1, math.ceil(n_local / nb))  # reference: adjust_bs
         self.engine = make_engine(model, self.store.cap_nodes, fanouts, self.batch_size, self.device, lr=lr,
                                  comm=comm, seed=seed, fused_allreduce=fused_allreduce,
-                                 use_cuda_graph=use_cuda_graph, ar_mode=ar_mode)
+                                 use_cuda_graph=use_cuda_graph, ar_mode=ar_mode,
+                                 overlap_allreduce=overlap_allreduce)
         self._maybe_repartition(0)
         self._warm = False
 
