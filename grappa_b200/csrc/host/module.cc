@@ -16,12 +16,14 @@
 #include <deque>
 #include <memory>
 #include <mutex>
+#include <optional>
 #include <thread>
 #include <unordered_map>
 
 #include "chunking.h"
 #include "graph_host.h"
 #include "grappa/rng.h"
+#include "mlpart.h"
 #include "xborder.h"
 
 namespace py = pybind11;
@@ -493,6 +495,32 @@ PYBIND11_MODULE(_C, m) {
 
   auto ms = m.def_submodule("c_seq");
   ms.def("print_string", [](const std::string& s) { py::print(s); });
+  // multilevel k-way edge-cut partition balanced by node count and training nodes
+  // (the reference's METIS assignment with the train mask as a balance type)
+  ms.def(
+      "multilevel_partition",
+      [](int64_t n, arr<int64_t> u, arr<int64_t> v, int64_t n_part, std::optional<arr<int8_t>> train, uint64_t seed,
+         double imbalance) {
+        if (u.size() != v.size()) throw std::invalid_argument("u and v differ in length");
+        if (train && train->size() != n) throw std::invalid_argument("train mask needs one entry per node");
+        grappa::host::MlPartOptions opt;
+        opt.n_parts = n_part;
+        opt.seed = seed;
+        opt.imbalance = imbalance;
+        const int8_t* tr = train ? train->data() : nullptr;
+        std::vector<int64_t> part;
+        {
+          py::gil_scoped_release rel;
+          part = grappa::host::multilevel_partition(n, u.data(), v.data(), static_cast<int64_t>(u.size()), tr, opt);
+        }
+        return to_py(std::move(part));
+      },
+      py::arg("n"), py::arg("u"), py::arg("v"), py::arg("n_part"), py::arg("train") = py::none(), py::arg("seed") = 0,
+      py::arg("imbalance") = 0.03);
+  ms.def("edge_cut", [](int64_t n, arr<int64_t> u, arr<int64_t> v, arr<int64_t> part) {
+    if (part.size() != n) throw std::invalid_argument("one part per node");
+    return grappa::host::edge_cut(n, u.data(), v.data(), static_cast<int64_t>(u.size()), part.data());
+  });
   ms.def("build", [](const std::string& path, int64_t n_n, int64_t n_e, int64_t feat_dim, int64_t n_part,
                      arr<int64_t> src, arr<int64_t> dst, arr<int64_t> nid2pid) {
     (void)feat_dim;

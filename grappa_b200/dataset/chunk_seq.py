@@ -4,10 +4,12 @@ Reads a dataset in the pre-partition layout (``t10n.json`` + ``*.bin.npy``, see
 grappa_b200.dataset.synthetic.to_t10n_layout), assigns nodes to partitions and
 writes the partition chunks with the C++ writer (grappa_b200._C.c_seq).
 
-Partition methods: ``hash`` / ``random`` (seeded hash of the node id) and
-``lp`` (label-propagation refinement of the hash assignment that keeps the
-partitions balanced; the reference's ``metis`` needs DGL's METIS binding, which
-is not part of this framework — ``metis`` is accepted as an alias of ``lp``).
+Partition methods: ``hash`` / ``random`` (seeded hash of the node id), ``metis``
+(multilevel k-way edge-cut partition balanced by node count and by training nodes,
+grappa_b200/csrc/host/mlpart.cc: the role of the reference's
+dgl.metis_partition_assignment with the train mask as a balance type,
+t10n/dataset/chunk_seq.py:47-50) and ``lp`` (label-propagation refinement of the
+hash assignment under a size cap).
 """
 import json
 import os
@@ -20,13 +22,18 @@ from grappa_b200 import _native
 from grappa_b200.dataset.meta import t10n_chunk_path
 
 
-def assign_partitions(u, v, n, n_part, method="hash", seed=0, rounds=4):
+def assign_partitions(u, v, n, n_part, method="hash", seed=0, rounds=4, train_mask=None):
     if n_part == 1:
         return np.zeros(n, dtype=np.int64)
+    if method == "metis":
+        tr = None if train_mask is None else np.ascontiguousarray(train_mask, dtype=np.int8)
+        return _native.host().c_seq.multilevel_partition(n, np.ascontiguousarray(u, dtype=np.int64),
+                                                        np.ascontiguousarray(v, dtype=np.int64), n_part, tr,
+                                                        seed, 0.03)
     pid = _native.host().c_dist.random_assign_pid(n, n_part, seed)
     if method in ("hash", "random"):
         return pid
-    if method not in ("lp", "metis"):
+    if method != "lp":
         raise ValueError(f"unknown partition method {method}")
     return label_propagation(u, v, n, n_part, pid, rounds)
 
@@ -66,7 +73,8 @@ def build_chunks_seq(dest_path, dataset_name, src_path, part_method, n_part, see
     edges = np.load(cfg["edge_file_bin"])
     n, m, dim = int(cfg["num_nodes"]), int(cfg["num_edges"]), int(cfg["feat_dim"])
     u, v = edges[:m].astype(np.int64), edges[m:].astype(np.int64)
-    pid = assign_partitions(u, v, n, n_part, part_method, seed)
+    train = np.load(cfg["train_mask_file_bin"]).astype(np.int8) if part_method == "metis" else None
+    pid = assign_partitions(u, v, n, n_part, part_method, seed, train_mask=train)
     c = _native.host().c_seq
     stats = c.build(out, n, m, dim, n_part, u, v, pid)
     c.split_node_feat(out, n, dim, n_part, np.load(cfg["node_feats_file_bin"]).astype(np.float32))
@@ -85,7 +93,7 @@ def build_chunks_from_graph(graph, dest_path, n_part, part_method="hash", seed=0
     n = graph.n_nodes
     u = graph.u.cpu().numpy().astype(np.int64)
     v = graph.v.cpu().numpy().astype(np.int64)
-    pid = assign_partitions(u, v, n, n_part, part_method, seed)
+    pid = assign_partitions(u, v, n, n_part, part_method, seed, train_mask=graph.train_mask.cpu().numpy())
     c = _native.host().c_seq
     stats = c.build(out, n, len(u), graph.spec.feat_dim, n_part, u, v, pid)
     c.split_node_feat(out, n, graph.spec.feat_dim, n_part, graph.feat.cpu().numpy().astype(np.float32))

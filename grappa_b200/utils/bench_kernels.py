@@ -1,9 +1,10 @@
 """Kernel microbenchmarks on one GPU: the tcgen05 GEMM against torch.matmul (cuBLAS)
-on the training shapes, and the aggregation / sampling kernels against the HBM
-roofline.  CUDA-event device times after warm-up, inputs sized as in a training
-step of the ogbn-products-shaped workload (``--scale`` multiplies the row counts).
+on the training shapes, the aggregation kernel against the HBM roofline, and the
+fused all-reduce + Adam kernel on one rank (its local HBM side).  CUDA-event device
+times after warm-up, inputs sized as in a training step of the ogbn-products-shaped
+workload (``--scale`` multiplies the row counts).
 
-    python -m grappa_b200.utils.bench_kernels [--scale 1]
+    python -m grappa_b200.utils.bench_kernels [--scale 1] [--part gemm,aggregate,ar]
 Prints one JSON line per measurement.
 """
 import argparse
@@ -14,8 +15,11 @@ import torch
 
 from grappa_b200 import _native
 
-HBM_GBS = 6555.8
-BF16_TFLOPS = 1655.8
+# measured on this GPU type: STREAM-style copy, cuBLAS bf16 GEMM as a burst and
+# sustained for seconds under the power cap (the figure for kernels inside a long step)
+HBM_GBS = 6536.4
+BF16_TFLOPS = 1615.2
+BF16_TFLOPS_SUSTAINED = 1375.2
 
 
 def _time(fn, iters=50, warmup=5):
@@ -108,17 +112,58 @@ def aggregate_case(n_dst, n_src, deg, dim):
             "frac_of_hbm": bytes_ / (t * 1e-3) / 1e9 / HBM_GBS}
 
 
+def ar_case(nbytes, mode, dtype=torch.float32):
+    """The fused all-reduce + Adam kernel on one rank (W = 1): the local HBM traffic of
+    a bucket (gradient read and clear, Adam on fp32 master weights, moments and the bf16
+    copy), without peers.  ``mode`` 0 = one-shot, 1 = shard."""
+    from grappa_b200.parallel.allreduce import FusedAllReduceAdam
+    from grappa_b200.parallel.comm import Comm
+    from grappa_b200.sampler_gpu import new_counters
+
+    dev = torch.device("cuda", 0)
+    esz = 4 if dtype == torch.float32 else 2
+    n = max(8, nbytes // esz // 8 * 8)
+    ar = FusedAllReduceAdam(Comm(), n, grad_dtype=dtype, modes=[mode])
+    m, v = torch.zeros(n, device=dev), torch.zeros(n, device=dev)
+    wbf = torch.zeros(n, dtype=torch.bfloat16, device=dev)
+    counters = new_counters(0, dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    ar.bind(counters, m, v, wbf, 1e-3, err=err)
+    cu = _native.cuda()
+
+    def run():
+        ar.launch(0)
+        cu.step_end(counters)
+
+    t = _time(run, iters=20, warmup=3)
+    assert int(err.item()) == 0
+    # gradient read + clear, param/m/v read + write, bf16 write (+ the slot copy of one-shot)
+    bytes_ = n * (2 * esz + 24 + 2 + (8 if mode == 0 else 0))
+    ar.close()
+    return {"bench": "allreduce_adam_1rank", "mode": mode, "grad_dtype": str(dtype).split(".")[-1], "bytes": n * esz,
+            "ms": t, "frac_of_hbm": bytes_ / (t * 1e-3) / 1e9 / HBM_GBS}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--scale", type=float, default=1.0)
+    ap.add_argument("--part", default="gemm,aggregate", help="comma list of gemm, aggregate, ar")
+    ap.add_argument("--ar-bytes", type=int, default=256 << 20)
     a = ap.parse_args()
     s = a.scale
-    rows = [gemm_case(int(20853 * s), 208, 256), gemm_case(int(20853 * s), 208, 256, p=0.5),
-            gemm_case(int(3250 * s), 512, 256), gemm_case(int(139058 * s), 104, 256),
-            gemm_case(65536, 256, 256), gemm_case(131072, 1024, 1024)]
-    rows += [dw_case(int(20853 * s), int(180224 * s), 256, 208), dw_case(int(3250 * s), int(16384 * s), 256, 512),
-             dw_case(int(1021 * s), int(1024 * s), 48, 512)]
-    rows += [aggregate_case(int(20853 * s), int(133975 * s), 14, 104), aggregate_case(int(3250 * s), int(20853 * s), 8, 256)]
+    parts = a.part.split(",")
+    rows = []
+    if "gemm" in parts:
+        rows += [gemm_case(int(20853 * s), 208, 256), gemm_case(int(20853 * s), 208, 256, p=0.5),
+                 gemm_case(int(3250 * s), 512, 256), gemm_case(int(139058 * s), 104, 256),
+                 gemm_case(65536, 256, 256), gemm_case(131072, 1024, 1024)]
+        rows += [dw_case(int(20853 * s), int(180224 * s), 256, 208), dw_case(int(3250 * s), int(16384 * s), 256, 512),
+                 dw_case(int(1021 * s), int(1024 * s), 48, 512)]
+    if "aggregate" in parts:
+        rows += [aggregate_case(int(20853 * s), int(133975 * s), 14, 104),
+                 aggregate_case(int(3250 * s), int(20853 * s), 8, 256)]
+    if "ar" in parts:
+        rows += [ar_case(a.ar_bytes, 1), ar_case(a.ar_bytes, 0), ar_case(a.ar_bytes, 1, torch.bfloat16)]
     for r in rows:
         print(json.dumps(r), flush=True)
 

@@ -105,3 +105,61 @@ def test_training_reduces_loss(tiny):
     trainer.close()
     assert last < first
     assert acc > 1.5 / g.spec.n_classes
+
+
+def test_accuracy_parity_with_fp32_cpu_training():
+    """Accuracy parity at equal epochs (the CPU/gloo configuration's shapes on one rank):
+    2-layer GraphSAGE-mean, hidden 64, dropout 0.5, fanout [10, 5], 512 seeds, Adam 3e-3,
+    10 epochs on the 16,384-node RMAT graph.  The GPU engine (bf16 operands, CUDA
+    graphs) and the fp32 PyTorch model trained on the same seeds, the same sampled blocks
+    (host sampler replaying the GPU's Philox draws) and the same dropout masks reach test
+    accuracies within 0.5 points (exact full-neighbour inference for both)."""
+    from grappa_b200.block import Block
+    from grappa_b200.infer import apply_layer
+
+    spec = S.SPECS["rmat16k"]
+    g = S.build(spec, DEV)
+    own = partition_from_global(g, 1, 0, DEV)
+    torch.manual_seed(0)
+    model = SAGE(spec.feat_dim, 64, spec.n_classes, 2, F.relu, 0.5)
+    cpu_model = SAGE(spec.feat_dim, 64, spec.n_classes, 2, F.relu, 0.5)
+    cpu_model.load_state_dict(model.state_dict())
+    fan, seed, epochs = [10, 5], 11, 10
+    tr = MiniBatchTrainer(model, own, fan, 512, lr=3e-3, comm=None, seed=seed)
+    tr.warmup()  # one training step at (epoch 0, step 0), then the graphs
+    for e in range(epochs):
+        tr.train_epoch(e)
+    tr.engine.check_errors()
+    gpu_acc = tr.evaluate_exact([own.test_mask])[0]
+    # fp32 CPU replay of the same steps
+    hg = _cpu_graph(own)
+    feat = own.feat[:, : spec.feat_dim].float().cpu()
+    labels = own.label.long().cpu()
+    opt = torch.optim.Adam(cpu_model.parameters(), lr=3e-3)
+    steps = []
+    for e in range(epochs):
+        sd, cnt = tr.epoch_seeds(e, on_host=True)
+        if e == 0:
+            steps.append((0, 0, sd[0, : int(cnt[0, 0])].long().numpy()))
+        steps += [(e, s, sd[s, : int(cnt[s, 0])].long().numpy()) for s in range(sd.shape[0])]
+    cpu_model.train()
+    for e, s, seeds in steps:
+        rb, _, _ = _native.host().graph.sample_batch(hg, fan, seeds, None, seed, e, s, False)
+        blocks = blocks_from_host(rb)
+        cpu_model.dropout_key = (seed, e, s)
+        out = cpu_model(blocks, feat[blocks[0].srcdata["_ID"]])
+        loss = F.cross_entropy(out, labels[torch.from_numpy(seeds)])
+        opt.zero_grad()
+        loss.backward()
+        opt.step()
+    cpu_model.eval()
+    blk = Block(own.indptr.cpu(), own.indices.cpu().long(), torch.arange(own.n_nodes), own.n_nodes)
+    h = feat
+    with torch.no_grad():
+        for i in range(2):
+            h = apply_layer(cpu_model, i, blk, h)
+    test = own.test_mask.cpu().bool()
+    cpu_acc = float((h.argmax(1)[test] == labels[test]).float().mean())
+    tr.close()
+    assert gpu_acc > 1.5 / spec.n_classes
+    assert abs(gpu_acc - cpu_acc) <= 0.005, (gpu_acc, cpu_acc)
