@@ -131,7 +131,7 @@ void compact(Tensor dst_nid, Tensor n_dst_dev, Tensor nbr, Tensor n_edges_dev, T
 void gemm(Tensor A, bool a_mn, Tensor B, bool b_mn, int64_t M_cap, OptT M_dev, int64_t N, int64_t K_cap, OptT K_dev,
           int64_t splits, Tensor C, int64_t mode, OptT bias, int64_t act, double dropout_p, OptT counters, int64_t salt,
           OptT labels, int64_t n_classes, OptT dlogits, OptT loss_sum, OptT correct, OptT pred_out, OptT n_rows_dev,
-          OptT dbias, Tensor err, int64_t bn) {
+          OptT dbias, Tensor err, int64_t bn, OptT act_mask, double mask_scale, int64_t zero_tail_rows) {
   c10::cuda::CUDAGuard g(A.device());
   d::GemmProblem p;
   p.A = ptr2d<at::BFloat16>(A, at::kBFloat16, "A");
@@ -179,6 +179,13 @@ void gemm(Tensor A, bool a_mn, Tensor B, bool b_mn, int64_t M_cap, OptT M_dev, i
   a.n_rows_dev = optr<int32_t>(n_rows_dev, at::kInt, "n_rows_dev");
   a.dbias = optr<float>(dbias, at::kFloat, "dbias");
   a.err = ptr<int32_t>(err, at::kInt, "err");
+  if (act_mask.has_value()) {
+    a.act_mask = reinterpret_cast<const __nv_bfloat16*>(ptr2d<at::BFloat16>(*act_mask, at::kBFloat16, "act_mask"));
+    a.ld_mask = act_mask->stride(0);
+    TORCH_CHECK(act_mask->size(0) >= a.M_cap, "act_mask needs M_cap rows");
+  }
+  a.mask_scale = static_cast<float>(mask_scale);
+  a.zero_tail_rows = static_cast<int32_t>(zero_tail_rows);
   if (mode == d::kCrossEntropy)
     TORCH_CHECK(a.labels && a.dlogits && a.loss_sum && a.correct, "cross-entropy epilogue needs labels/dlogits/loss/correct");
   d::launch_gemm(p, a, static_cast<int>(bn), stream());
@@ -934,7 +941,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("scan_scratch"), py::arg("err"), py::arg("cap_dst"), py::arg("cap_edges"), py::arg("counters"),
         py::arg("slot"), py::arg("k1_done") = false);
   m.def("compact_scratch_words", &compact_scratch_words);
-  m.def("gemm", &gemm);
+  m.def("gemm", &gemm, py::arg("A"), py::arg("a_mn"), py::arg("B"), py::arg("b_mn"), py::arg("M_cap"), py::arg("M_dev"),
+        py::arg("N"), py::arg("K_cap"), py::arg("K_dev"), py::arg("splits"), py::arg("C"), py::arg("mode"),
+        py::arg("bias"), py::arg("act"), py::arg("dropout_p"), py::arg("counters"), py::arg("salt"), py::arg("labels"),
+        py::arg("n_classes"), py::arg("dlogits"), py::arg("loss_sum"), py::arg("correct"), py::arg("pred_out"),
+        py::arg("n_rows_dev"), py::arg("dbias"), py::arg("err"), py::arg("bn"), py::arg("act_mask") = py::none(),
+        py::arg("mask_scale") = 1.0, py::arg("zero_tail_rows") = 0);
   m.def("aggregate", &aggregate, py::arg("indptr"), py::arg("indices"), py::arg("n_dst_dev"), py::arg("n_dst"),
         py::arg("cap_dst"), py::arg("src"), py::arg("src_map"), py::arg("dim"), py::arg("mode"), py::arg("edge_w"),
         py::arg("src_norm"), py::arg("dst_norm"), py::arg("out"), py::arg("agg_col"), py::arg("self_col"),

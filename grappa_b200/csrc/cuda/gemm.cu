@@ -164,6 +164,24 @@ __device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, 
                : "memory");
 }
 
+// Activation backward on 32 accumulator columns of row m: keep acc * mask_scale where
+// the forward output (the mask tensor) is non-zero.
+__device__ __forceinline__ void apply_act_mask(const GemmArgs& a, int m, int nc, float (&v)[32]) {
+  const __nv_bfloat16* hm = a.act_mask + static_cast<int64_t>(m) * a.ld_mask + nc;
+  if (nc + 32 <= a.N) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      float h[8];
+      bf16x8_to_f32(*reinterpret_cast<const uint4*>(hm + j), h);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) v[j + q] = h[q] != 0.f ? v[j + q] * a.mask_scale : 0.f;
+    }
+  } else {
+    for (int j = 0; j < 32; ++j)
+      v[j] = (nc + j < a.N && __bfloat162float(hm[j]) != 0.f) ? v[j] * a.mask_scale : 0.f;
+  }
+}
+
 // Epilogue of one 128 x BN accumulator tile for the store and atomic modes: warp
 // `quarter` drains TMEM lanes 32 * quarter + (0..31), i.e. rows m0 + 32 * quarter +
 // lane, columns [c_begin, c_end) (multiples of 64 on the TMA-store path); `trow` is
@@ -186,8 +204,12 @@ __device__ __forceinline__ void store_tile(const GemmArgs& a, const CUtensorMap*
     const uint32_t thr = static_cast<uint32_t>(static_cast<double>(a.dropout_p) * 4294967296.0);
     const bool live = m < M;
     // a 32-row slab that crosses the live row count stores its live rows directly,
-    // so that rows >= M are never written
+    // so that rows >= M are never written (except the zeroed tail rows)
     const bool slab_full = m0 + quarter * 32 + 32 <= M;
+    const int64_t tail_end = a.zero_tail_rows > 0
+                                 ? min(static_cast<int64_t>(ceil_div(M, a.zero_tail_rows)) * a.zero_tail_rows, a.c_rows)
+                                 : 0;
+    const bool zero_row = !live && m < tail_end;
 #pragma unroll 1
     for (int c = c_begin; c < c_end; c += 32) {
       float v[32];
@@ -200,6 +222,7 @@ __device__ __forceinline__ void store_tile(const GemmArgs& a, const CUtensorMap*
         if (a.act == 1) x = fmaxf(x, 0.f);
         v[j] = live ? x : 0.f;
       }
+      if (a.act_mask && live) apply_act_mask(a, m, nc, v);
       if (a.dropout_p > 0.f && live) {
         const uint64_t base = static_cast<uint64_t>(m) * static_cast<uint64_t>(a.ldc) + static_cast<uint64_t>(nc);
 #pragma unroll
@@ -218,7 +241,7 @@ __device__ __forceinline__ void store_tile(const GemmArgs& a, const CUtensorMap*
           const int k = ((c & 63) >> 3) + q;
           *reinterpret_cast<uint4*>(panel + ((k ^ (lane & 7)) << 4)) = f32_to_bf16x8(v + 8 * q);
         }
-      } else if (live && ok && nc < a.N) {
+      } else if ((live || zero_row) && ok && nc < a.N) {
         __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.C) + static_cast<int64_t>(m) * a.ldc + nc;
         if (nc + 32 <= a.ldc) {
 #pragma unroll
@@ -246,12 +269,20 @@ __device__ __forceinline__ void store_tile(const GemmArgs& a, const CUtensorMap*
                                     : 0ull;
     const float keep_scale = a.dropout_p > 0.f ? 1.0f / (1.0f - a.dropout_p) : 1.0f;
     const uint32_t thr = static_cast<uint32_t>(static_cast<double>(a.dropout_p) * 4294967296.0);
+    const int64_t tail_end = a.zero_tail_rows > 0
+                                 ? min(static_cast<int64_t>(ceil_div(M, a.zero_tail_rows)) * a.zero_tail_rows, a.c_rows)
+                                 : 0;
 #pragma unroll 1
     for (int c = c_begin; c < c_end; c += 32) {
       float v[32];
       tmem_ld32(trow + c, v);
-      if (!ok || m >= M) continue;
       const int nc = n0 + c;
+      if (ok && m >= M && m < tail_end && nc < a.N && a.c_mode == kStoreBf16) {
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.C) + static_cast<int64_t>(m) * a.ldc + nc;
+        for (int j = 0; j < 32 && nc + j < a.ldc; ++j) dst[j] = __float2bfloat16_rn(0.f);
+        continue;
+      }
+      if (!ok || m >= M) continue;
       if (nc >= a.N) continue;
       if (a.c_mode == kAtomicF32) {
         float* dst = reinterpret_cast<float*>(a.C) + static_cast<int64_t>(m) * a.ldc + nc;
@@ -270,6 +301,7 @@ __device__ __forceinline__ void store_tile(const GemmArgs& a, const CUtensorMap*
         if (a.act == 1) x = fmaxf(x, 0.f);
         v[j] = x;
       }
+      if (a.act_mask) apply_act_mask(a, m, nc, v);
       if (a.dropout_p > 0.f) {
         const uint64_t base = static_cast<uint64_t>(m) * static_cast<uint64_t>(a.ldc) + static_cast<uint64_t>(nc);
 #pragma unroll
@@ -844,6 +876,10 @@ void launch_gemm(const GemmProblem& p, GemmArgs a, int bn, cudaStream_t stream) 
                   static_cast<unsigned>(a.splits));
   if (a.c_mode == kCrossEntropy && (a.N > bn || a.n_classes > bn)) throw std::invalid_argument("cross-entropy epilogue needs N <= BN");
   if (a.c_mode == kCrossEntropy && a.ld_dl % 8 != 0) throw std::invalid_argument("dlogits stride must be a multiple of 8");
+  if (a.act_mask && (a.c_mode != kStoreBf16 || a.bias || a.act || a.dropout_p > 0.f || a.ld_mask % 8 != 0))
+    throw std::invalid_argument("activation-backward epilogue: bf16 store only, no bias/activation/dropout, mask stride % 8");
+  if (a.zero_tail_rows > 0 && a.c_mode != kStoreBf16)
+    throw std::invalid_argument("zeroed tail rows need the bf16 store mode");
 #define GB_GEMM_CASE(BNV)                                                           \
   if (bn == BNV) {                                                                  \
     if (!p.a_mn && !p.b_mn) return launch_t<BNV, false, false>(p, a, grid, stream); \

@@ -129,6 +129,15 @@ struct GemmArgs {
   float* dbias = nullptr;              // cross-entropy epilogue: += column sums of the gradient
   int32_t* err = nullptr;
   int64_t c_rows = 0;                  // rows of C (bf16 stores go through a TMA store of that extent)
+  // activation backward fused into a bf16 store (no bias, ReLU or dropout then):
+  // out = mask[m, n] != 0 ? acc * mask_scale : 0, with mask the layer's forward output
+  // (ReLU + dropout leave exact zeros where the gradient is cut)
+  const __nv_bfloat16* act_mask = nullptr;
+  int64_t ld_mask = 0;
+  float mask_scale = 1.f;
+  // > 0: rows [M, roundup(M, zero_tail_rows)) of C (below c_rows) are written as zeros,
+  // so that a later split-K GEMM over whole 64-row blocks reads zeros past the live rows
+  int32_t zero_tail_rows = 0;
 };
 void launch_gemm(const GemmProblem& p, GemmArgs a, int bn, cudaStream_t stream);
 

@@ -337,10 +337,11 @@ class BlockEngine:
                               self.fstats[2:3], self.istats[0:1])
 
     def _gemm(self, A, a_mn, B, b_mn, M_cap, M_dev, N, K_cap, K_dev, splits, C, mode, bias=None, act=0, p=0.0,
-              salt=0, bn=None):
+              salt=0, bn=None, act_mask=None, mask_scale=1.0, zero_tail_rows=0):
         bn = bn or gemm_bn(M_cap, N, b_mn)
         self.cu.gemm(A, a_mn, B, b_mn, M_cap, M_dev, N, K_cap, K_dev, splits, C, mode, bias, act, p,
-                     self.counters if p > 0 else None, salt, None, 0, None, None, None, None, None, None, self.err, bn)
+                     self.counters if p > 0 else None, salt, None, 0, None, None, None, None, None, None, self.err, bn,
+                     act_mask, mask_scale, zero_tail_rows)
 
     def _dw(self, A, B, M, N, K_cap, K_dev, gW):
         """gW[M, N] += A^T B with A [K, M], B [K, N] (both MN-major), split-K over rows.
@@ -988,8 +989,9 @@ class GatEngine(BlockEngine):
                 s["dl"] = torch.zeros((rows, s["fo"]), **z)
             else:
                 s["H_out"] = torch.zeros((rows, hfp), **z)
+                # written by the next layer's dX GEMM with the ReLU/dropout backward fused
+                # into its epilogue (no fp32 gradient rows, no separate activation pass)
                 s["dY"] = torch.zeros((rows, hfp), **z)
-                s["dH"] = torch.zeros((rows, hfp), **f32)
             self.lay.append(s)
 
     def _A(self, l, s):
@@ -1021,11 +1023,9 @@ class GatEngine(BlockEngine):
         scale = 1.0 / (1.0 - self.p) if self.p > 0 else 1.0
         s = self.lay[l]
         h = s["h"]
-        if s["last"]:
-            dout = s["dl"]
-        else:
-            cu.act_bwd(s["dH"], s["H_out"], s["dY"], self._n_dst(h), 0, s["hfp"], scale, None, s["rows"])
-            dout = s["dY"]
+        # a hidden layer's dY was written by the layer above's dX GEMM (activation backward
+        # fused into its epilogue)
+        dout = s["dl"] if s["last"] else s["dY"]
         A = self._A(l, s)
         if s["in_fast"]:
             self._input_layer_bwd(s, h, dout, A)
@@ -1035,9 +1035,10 @@ class GatEngine(BlockEngine):
                    s["escr"], s["del_"], s["der"], s["dz"], s["gb"], s["gal"], s["gar"], s["dzb"], self.err)
         self._dw(s["dzb"], A, s["HF"], s["ip"], s["srows"], sm.n_src(h), s["gW"])
         if l > 0:
+            # dX = dz W, then the previous layer's ReLU + dropout backward, in one GEMM
             prev = self.lay[l - 1]
             self._gemm(s["dzb"], False, s["W"], True, s["srows"], sm.n_src(h), s["ip"], s["HF"], None, 1,
-                       prev["dH"], GEMM_STORE_F32)
+                       prev["dY"], GEMM_STORE_BF16, act_mask=prev["H_out"], mask_scale=scale, zero_tail_rows=64)
 
 
     def _input_layer_bwd(self, s, h, dout, A):

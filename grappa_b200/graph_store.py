@@ -125,6 +125,7 @@ class PartitionStore:
         self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.working = None
         self._peer = None
+        self.repart_log = []
         self.cap_nodes = own.n_nodes
         if self.world > 1:
             self._export()
@@ -178,6 +179,8 @@ class PartitionStore:
         sz = self._sizes
         n_r, n_q = own.n_nodes, sz[q]["n"]
         peer = self._peer
+        ev = [torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
+        ev[0].record()
         # 1. halo = (ext_r U ext_q) \ (V_r U V_q), found by marking a dense global-id array
         cu.mark_ids(peer["ext"].ptrs[r], None, sz[r]["ext"], self._mark)
         cu.mark_ids(peer["ext"].ptrs[q], None, sz[q]["ext"], self._mark)
@@ -195,9 +198,28 @@ class PartitionStore:
         tables = [peer["feat"].ptrs[p] for p in range(self.world)]
         cu.pull_rows(tables, fs, esz, fs * esz, self._halo_ids, self._n_halo, 0, self._prefix_dev,
                      self._feat_w.data_ptr(), fs, n_r + n_q, self._halo_ids.numel(), self.err)
+        ev[1].record()
+        # bytes this rank pulls over NVLink: q's external-source list and CSR, q's feature
+        # rows and the halo rows (their count is on the device until the log is read)
+        pulled = sz[q]["ext"] * 4 + (n_q + 1) * 8 + sz[q]["e"] * 4 + n_q * fs * esz
+        self.repart_log.append({"events": ev, "bytes_fixed": pulled, "row_bytes": fs * esz,
+                                "n_halo": self._n_halo.clone()})
         self.working = WorkingGraph(self._indptr_w, self._indices_w, self._feat_w, n_r, n_q, self._n_halo,
                                     self.cap_nodes, q)
         return self.working
+
+    def repartition_stats(self, link_gbs=770.0):
+        """Device time and NVLink bytes of every peer-memory repartition so far (synchronises):
+        [{'ms', 'bytes', 'frac_of_link_roofline'}], the roofline being the pulled bytes at
+        ``link_gbs`` GB/s (the measured peer bandwidth per direction; nominal 900)."""
+        torch.cuda.synchronize(self.device)
+        out = []
+        for rec in self.repart_log:
+            ms = rec["events"][0].elapsed_time(rec["events"][1])
+            b = rec["bytes_fixed"] + int(rec["n_halo"].item()) * rec["row_bytes"]
+            out.append({"ms": round(ms, 4), "bytes": int(b),
+                        "frac_of_link_roofline": round(b / (link_gbs * 1e9) * 1e3 / ms, 4) if ms > 0 else None})
+        return out
 
     def check_errors(self):
         e = int(self.err.item())

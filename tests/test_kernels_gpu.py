@@ -131,6 +131,29 @@ def test_gemm_dropout_matches_host_mask():
     torch.testing.assert_close(C.float(), want, rtol=2e-2, atol=3e-2)
 
 
+@pytest.mark.parametrize("cap,live,N,K,bn", [(1024, 700, 256, 256, 256), (512, 130, 64, 512, 64),
+                                             (2048, 2000, 128, 96, 128)])
+def test_gemm_activation_backward_epilogue(cap, live, N, K, bn):
+    """bf16 store with the ReLU/dropout backward fused: out = (H != 0) * (A B^T) * scale on
+    the live rows, zeros on the tail rows up to the next multiple of 64."""
+    torch.manual_seed(4)
+    A = bf(torch.randn(cap, K, device=DEV))
+    B = bf(torch.randn(N, K, device=DEV) / math.sqrt(K))
+    H = bf(torch.relu(torch.randn(cap, N, device=DEV)))  # about half exact zeros
+    C = torch.full((cap, N), 7.0, dtype=torch.bfloat16, device=DEV)
+    m_dev = torch.tensor([live], dtype=torch.int32, device=DEV)
+    err = err_tensor()
+    cu().gemm(A, False, B, False, cap, m_dev, N, K, None, 1, C, 0, None, 0, 0.0, None, 0, None, 0, None, None, None,
+              None, None, None, err, bn, H, 2.0, 64)
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    want = torch.where(H[:live] != 0, (A[:live].float() @ B.float().t()) * 2.0, torch.zeros((), device=DEV))
+    torch.testing.assert_close(C[:live].float(), want, rtol=2e-2, atol=3e-2)
+    tail = min(cap, (live + 63) // 64 * 64)
+    assert bool((C[live:tail] == 0).all())
+    assert bool((C[tail:] == 7.0).all())
+
+
 @pytest.mark.parametrize("Mo,Kx,R,live,splits", [(48, 208, 700, 650, 3), (256, 512, 4096, 4000, 8),
                                                  (256, 208, 130, 100, 1), (1024, 1024, 8192, 8000, 4)])
 def test_gemm_dw_mn_major_split_k(Mo, Kx, R, live, splits):
