@@ -101,7 +101,7 @@ int64_t compact_scratch_words(int64_t cap_e) { return d::compact_scan_scratch_wo
 
 void compact(Tensor dst_nid, Tensor n_dst_dev, Tensor nbr, Tensor n_edges_dev, Tensor map, Tensor src_nid,
              Tensor src_sampled, Tensor indices, Tensor n_src_out, Tensor scan_scratch, Tensor err, int64_t cap_dst,
-             int64_t cap_edges, Tensor counters, int64_t slot, bool k1_done) {
+             int64_t cap_edges, Tensor counters, int64_t slot, bool k1_done, OptT t_cnt, OptT t_rank) {
   c10::cuda::CUDAGuard g(dst_nid.device());
   TORCH_CHECK(slot >= 0 && slot < 16, "slot must be in [0, 16)");
   TORCH_CHECK(counters.numel() >= 6, "counters needs 6 entries");
@@ -119,12 +119,56 @@ void compact(Tensor dst_nid, Tensor n_dst_dev, Tensor nbr, Tensor n_edges_dev, T
   a.cap_src = static_cast<int32_t>(std::min(src_nid.numel(), src_sampled.numel()));
   a.scan_scratch = reinterpret_cast<unsigned long long*>(ptr<int64_t>(scan_scratch, at::kLong, "scan_scratch"));
   a.err = ptr<int32_t>(err, at::kInt, "err");
+  a.t_cnt = optr<int32_t>(t_cnt, at::kInt, "t_cnt");
+  a.t_rank = optr<int32_t>(t_rank, at::kInt, "t_rank");
+  TORCH_CHECK(!a.t_cnt || (a.t_rank && t_cnt->numel() >= a.cap_src && t_rank->numel() >= cap_edges),
+              "the transpose counters need t_cnt[cap_src] and t_rank[cap_edges]");
   TORCH_CHECK(nbr.numel() >= cap_edges && indices.numel() >= cap_edges, "edge buffers smaller than cap_edges");
   TORCH_CHECK(dst_nid.numel() >= cap_dst && a.cap_src >= cap_dst, "dst/src buffers smaller than cap_dst");
   TORCH_CHECK(scan_scratch.numel() >= d::compact_scan_scratch_words(static_cast<int>(cap_edges)), "scan_scratch too small");
   const int64_t* gen = ptr<int64_t>(counters, at::kLong, "counters") + 4;
   d::launch_compact(a, static_cast<int>(cap_dst), static_cast<int>(cap_edges), gen, static_cast<int>(slot), num_sms(),
                     stream(), k1_done);
+}
+
+void block_transpose(Tensor indptr, Tensor indices, Tensor n_dst_dev, Tensor n_src_dev, Tensor t_cnt, Tensor t_rank,
+                     Tensor tptr, Tensor tdst, Tensor err) {
+  c10::cuda::CUDAGuard g(indptr.device());
+  const int cap_src = static_cast<int>(std::min(t_cnt.numel(), tptr.numel() - 1));
+  const int cap_e = static_cast<int>(std::min(t_rank.numel(), tdst.numel()));
+  d::launch_block_transpose(ptr<int32_t>(indptr, at::kInt, "indptr"), ptr<int32_t>(indices, at::kInt, "indices"),
+                            ptr<int32_t>(n_dst_dev, at::kInt, "n_dst"), ptr<int32_t>(n_src_dev, at::kInt, "n_src"),
+                            ptr<int32_t>(t_cnt, at::kInt, "t_cnt"), ptr<int32_t>(t_rank, at::kInt, "t_rank"),
+                            ptr<int32_t>(tptr, at::kInt, "tptr"), ptr<int32_t>(tdst, at::kInt, "tdst"), cap_src, cap_e,
+                            ptr<int32_t>(err, at::kInt, "err"), stream());
+}
+
+void aggregate_bwd_gather(Tensor indptr, Tensor tptr, Tensor tdst, Tensor n_dst_dev, Tensor n_src_dev, Tensor dout,
+                          int64_t self_col, int64_t agg_col, int64_t dim, Tensor mask, double scale, Tensor dy,
+                          OptT dbias, Tensor err) {
+  c10::cuda::CUDAGuard g(dout.device());
+  d::AggBwdGatherArgs a;
+  a.indptr = ptr<int32_t>(indptr, at::kInt, "indptr");
+  a.tptr = ptr<int32_t>(tptr, at::kInt, "tptr");
+  a.tdst = ptr<int32_t>(tdst, at::kInt, "tdst");
+  a.n_dst_ptr = ptr<int32_t>(n_dst_dev, at::kInt, "n_dst");
+  a.n_src_ptr = ptr<int32_t>(n_src_dev, at::kInt, "n_src");
+  a.dout = reinterpret_cast<const __nv_bfloat16*>(ptr2d<at::BFloat16>(dout, at::kBFloat16, "dout"));
+  a.dout_stride = dout.stride(0);
+  a.self_col = static_cast<int32_t>(self_col);
+  a.agg_col = static_cast<int32_t>(agg_col);
+  a.dim = static_cast<int32_t>(dim);
+  a.mask = reinterpret_cast<const __nv_bfloat16*>(ptr2d<at::BFloat16>(mask, at::kBFloat16, "mask"));
+  a.mask_stride = mask.stride(0);
+  a.scale = static_cast<float>(scale);
+  a.dy = reinterpret_cast<__nv_bfloat16*>(ptr2d<at::BFloat16>(dy, at::kBFloat16, "dy"));
+  a.dy_stride = dy.stride(0);
+  a.dbias = optr<float>(dbias, at::kFloat, "dbias");
+  a.cap_rows = static_cast<int32_t>(std::min(dy.size(0), mask.size(0)));
+  TORCH_CHECK(tptr.numel() >= a.cap_rows + 1, "tptr needs cap_rows + 1 entries");
+  TORCH_CHECK(dy.size(1) >= dim && mask.size(1) >= dim, "dy and mask need dim columns");
+  a.err = ptr<int32_t>(err, at::kInt, "err");
+  d::launch_aggregate_bwd_gather(a, stream());
 }
 
 // --------------------------------------------------------------------------- GEMM
@@ -939,8 +983,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("compact", &compact, py::arg("dst_nid"), py::arg("n_dst_dev"), py::arg("nbr"), py::arg("n_edges_dev"),
         py::arg("map"), py::arg("src_nid"), py::arg("src_sampled"), py::arg("indices"), py::arg("n_src_out"),
         py::arg("scan_scratch"), py::arg("err"), py::arg("cap_dst"), py::arg("cap_edges"), py::arg("counters"),
-        py::arg("slot"), py::arg("k1_done") = false);
+        py::arg("slot"), py::arg("k1_done") = false, py::arg("t_cnt") = py::none(), py::arg("t_rank") = py::none());
   m.def("compact_scratch_words", &compact_scratch_words);
+  m.def("block_transpose", &block_transpose);
+  m.def("aggregate_bwd_gather", &aggregate_bwd_gather);
   m.def("gemm", &gemm, py::arg("A"), py::arg("a_mn"), py::arg("B"), py::arg("b_mn"), py::arg("M_cap"), py::arg("M_dev"),
         py::arg("N"), py::arg("K_cap"), py::arg("K_dev"), py::arg("splits"), py::arg("C"), py::arg("mode"),
         py::arg("bias"), py::arg("act"), py::arg("dropout_p"), py::arg("counters"), py::arg("salt"), py::arg("labels"),

@@ -126,10 +126,60 @@ __global__ void __launch_bounds__(kThreads) compact_k3(CompactArgs a) {
     if (lid >= a.cap_src || lid < 0) lid = 0;
     a.indices[e] = lid;
     a.src_sampled[lid] = 1;
+    if (a.t_cnt) a.t_rank[e] = atomicAdd(a.t_cnt + lid, 1);
+  }
+}
+
+constexpr int kTpThreads = 1024;
+
+__global__ void __launch_bounds__(kTpThreads) block_transpose_kernel(const int32_t* indptr, const int32_t* indices,
+                                                                      const int32_t* n_dst_ptr, const int32_t* n_src_ptr,
+                                                                      int32_t* t_cnt, const int32_t* t_rank,
+                                                                      int32_t* tptr, int32_t* tdst, int cap_src,
+                                                                      int cap_edges, int32_t* err) {
+  __shared__ long long s_scan[kTpThreads / 32];
+  __shared__ long long s_carry;
+  const int n_src = min(*n_src_ptr, cap_src);
+  const int n_dst = *n_dst_ptr;
+  if (threadIdx.x == 0) s_carry = 0;
+  __syncthreads();
+  // exclusive scan of the per-source counts, 1024 at a time; the counts are cleared
+  for (int base = 0; base < n_src; base += kTpThreads) {
+    const int i = base + static_cast<int>(threadIdx.x);
+    const int c = i < n_src ? t_cnt[i] : 0;
+    if (i < n_src) t_cnt[i] = 0;
+    long long total;
+    const long long excl = block_exclusive_scan<kTpThreads, long long>(c, s_scan, &total);
+    const long long carry = s_carry;
+    if (i < n_src) tptr[i] = static_cast<int32_t>(carry + excl);
+    __syncthreads();
+    if (threadIdx.x == 0) s_carry = carry + total;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) tptr[n_src] = static_cast<int32_t>(s_carry);
+  __syncthreads();
+  // fill: one warp per destination, its edges by lane
+  const int warps = kTpThreads / 32;
+  for (int v = threadIdx.x >> 5; v < n_dst; v += warps) {
+    const int beg = indptr[v], end = indptr[v + 1];
+    for (int e = beg + static_cast<int>(lane_id()); e < end; e += 32) {
+      const int s = indices[e];
+      const int k = (s >= 0 && s < n_src) ? tptr[s] + t_rank[e] : -1;
+      if (k >= 0 && k < cap_edges) tdst[k] = v;
+      else set_error(err, kErrBadIndex);
+    }
   }
 }
 
 }  // namespace
+
+void launch_block_transpose(const int32_t* indptr, const int32_t* indices, const int32_t* n_dst_ptr,
+                            const int32_t* n_src_ptr, int32_t* t_cnt, const int32_t* t_rank, int32_t* tptr,
+                            int32_t* tdst, int cap_src, int cap_edges, int32_t* err, cudaStream_t stream) {
+  block_transpose_kernel<<<1, kTpThreads, 0, stream>>>(indptr, indices, n_dst_ptr, n_src_ptr, t_cnt, t_rank, tptr, tdst,
+                                                       cap_src, cap_edges, err);
+  GB_LAUNCH_CHECK();
+}
 
 int compact_scan_scratch_words(int cap_edges) {
   return static_cast<int>(ceil_div(cap_edges > 0 ? cap_edges : 1, kTile)) + 1;

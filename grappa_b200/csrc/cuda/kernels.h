@@ -82,12 +82,25 @@ struct CompactArgs {
   int32_t cap_src = 0;
   unsigned long long* scan_scratch = nullptr;
   int32_t* err = nullptr;
+  // optional transpose of the block (launch_block_transpose): K3 counts the edges of
+  // every local src (t_cnt, zero before; the transpose clears it again) and stores
+  // each edge's rank among its source's edges (t_rank)
+  int32_t* t_cnt = nullptr;
+  int32_t* t_rank = nullptr;
 };
 // gen: device generation counter; tags are derived on the device from (*gen, slot)
 // so that a captured graph keeps drawing fresh tags (slot < 16 per generation).
 void launch_compact(const CompactArgs& a, int cap_dst, int cap_edges, const int64_t* gen, int slot, int num_sms,
                     cudaStream_t stream, bool k1_done = false);
 int compact_scan_scratch_words(int cap_edges);
+
+// The block's edges grouped by source (CSR by local src): tptr[n_src + 1] from an
+// exclusive scan of t_cnt (cleared as it is read), tdst[k] = the destination of the
+// k-th edge of its source (edge order within a source: t_rank).  One CTA (the blocks
+// that need it are the inner hops: tens of thousands of nodes at most).
+void launch_block_transpose(const int32_t* indptr, const int32_t* indices, const int32_t* n_dst_ptr,
+                            const int32_t* n_src_ptr, int32_t* t_cnt, const int32_t* t_rank, int32_t* tptr,
+                            int32_t* tdst, int cap_src, int cap_edges, int32_t* err, cudaStream_t stream);
 
 // ---------------------------------------------------------------- GEMM
 enum GemmMode : int { kStoreBf16 = 0, kStoreF32 = 1, kAtomicF32 = 2, kCrossEntropy = 3 };
@@ -196,6 +209,33 @@ struct AggBwdArgs {
   int32_t* err = nullptr;
 };
 void launch_aggregate_bwd(const AggBwdArgs& a, int cap_dst, cudaStream_t stream);
+
+// Mean-aggregation backward gathered by source, with the previous layer's ReLU/dropout
+// backward fused: for every local src u of the block
+//   g_u = [u < n_dst] dout[u, self_col:] + sum_{v: u in N(v)} dout[v, agg_col:] / deg_v
+//   dy_u = mask[u] != 0 ? g_u * scale : 0       (bf16), dbias += sum_u dy_u
+// over the transposed block (tptr/tdst); rows [n_src, roundup(n_src, 64)) of dy are
+// zeroed.  Replaces aggregate_bwd (fp32 scatter) + act_bwd for GraphSAGE.
+struct AggBwdGatherArgs {
+  const int32_t* indptr = nullptr;      // block CSR by dst (degrees)
+  const int32_t* tptr = nullptr;        // transposed block [n_src + 1]
+  const int32_t* tdst = nullptr;
+  const int32_t* n_dst_ptr = nullptr;
+  const int32_t* n_src_ptr = nullptr;
+  const __nv_bfloat16* dout = nullptr;  // [n_dst, >= max(self_col, agg_col) + dim]
+  int64_t dout_stride = 0;
+  int32_t self_col = 0, agg_col = 0;
+  int32_t dim = 0;
+  const __nv_bfloat16* mask = nullptr;  // the previous layer's forward output [cap_rows, mask_stride]
+  int64_t mask_stride = 0;
+  float scale = 1.f;
+  __nv_bfloat16* dy = nullptr;          // [cap_rows, dy_stride]
+  int64_t dy_stride = 0;
+  float* dbias = nullptr;
+  int32_t cap_rows = 0;
+  int32_t* err = nullptr;
+};
+void launch_aggregate_bwd_gather(const AggBwdGatherArgs& a, cudaStream_t stream);
 
 // GCN normalisation: out-degree of every local src of a block (clamped >= 1) ^ -1/2
 void launch_src_norm(const int32_t* indices, const int32_t* n_edges_ptr, int cap_edges, const int32_t* n_src_ptr,

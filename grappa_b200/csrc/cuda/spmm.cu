@@ -299,6 +299,117 @@ __global__ void __launch_bounds__(kThreads) aggregate_bwd_kernel(AggBwdArgs a) {
   }
 }
 
+// Mean-aggregation backward gathered by source with the activation backward fused
+// (see AggBwdGatherArgs).  One warp per source row, lane l owning 8-column chunks
+// l, l + 32, ...; the row's transposed edges are read 32 at a time (one coalesced
+// load of their destinations, with the destinations' degrees), then four rows of the
+// output gradient are in flight per lane.  Column sums of dy go to dbias with one
+// atomic per column and block.
+template <int CPL>
+__global__ void __launch_bounds__(kThreads) aggregate_bwd_gather_kernel(AggBwdGatherArgs a) {
+  __shared__ float s_col[kThreads / 32][CPL * 256];
+  const int n_src = min(*a.n_src_ptr, a.cap_rows);
+  const int n_dst = *a.n_dst_ptr;
+  const int chunks = a.dim >> 3;
+  const int lane = threadIdx.x & 31;
+  const int wib = threadIdx.x >> 5;
+  const int warps_total = (gridDim.x * kThreads) >> 5;
+  const int rows_end = min(a.cap_rows, static_cast<int>(ceil_div(n_src, 64) * 64));
+  float bsum[CPL][8];
+#pragma unroll
+  for (int q = 0; q < CPL; ++q)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) bsum[q][j] = 0.f;
+  for (int u = (blockIdx.x * kThreads + threadIdx.x) >> 5; u < rows_end; u += warps_total) {
+    __nv_bfloat16* dyrow = a.dy + static_cast<int64_t>(u) * a.dy_stride;
+    if (u >= n_src) {
+      for (int c = lane; c < chunks; c += 32) *reinterpret_cast<uint4*>(dyrow + c * 8) = make_uint4(0, 0, 0, 0);
+      continue;
+    }
+    float acc[CPL][8];
+#pragma unroll
+    for (int q = 0; q < CPL; ++q) {
+      const int c = lane + 32 * q;
+      if (u < n_dst && c < chunks) {
+        bf16x8_to_f32(*reinterpret_cast<const uint4*>(a.dout + static_cast<int64_t>(u) * a.dout_stride + a.self_col +
+                                                        c * 8), acc[q]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[q][j] = 0.f;
+      }
+    }
+    const int beg = a.tptr[u], end = a.tptr[u + 1];
+    for (int cb = beg; cb < end; cb += 32) {
+      const int cnt = min(32, end - cb);
+      int my_v = 0;
+      float my_w = 0.f;
+      if (lane < cnt) {
+        my_v = a.tdst[cb + lane];
+        if (my_v >= 0 && my_v < n_dst) {
+          const int d = a.indptr[my_v + 1] - a.indptr[my_v];
+          my_w = d > 0 ? 1.f / static_cast<float>(d) : 0.f;
+        } else {
+          my_v = 0;
+          set_error(a.err, kErrBadIndex);
+        }
+      }
+      for (int k = 0; k < cnt; k += 4) {
+        uint4 x[4][CPL];
+        float w[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const int v = __shfl_sync(0xffffffffu, my_v, min(k + t, 31));
+          w[t] = __shfl_sync(0xffffffffu, my_w, min(k + t, 31));
+          if (k + t >= cnt) w[t] = 0.f;
+#pragma unroll
+          for (int q = 0; q < CPL; ++q) {
+            const int c = lane + 32 * q;
+            x[t][q] = make_uint4(0, 0, 0, 0);
+            if (k + t < cnt && c < chunks)
+              x[t][q] = *reinterpret_cast<const uint4*>(a.dout + static_cast<int64_t>(v) * a.dout_stride + a.agg_col +
+                                                        c * 8);
+          }
+        }
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+#pragma unroll
+          for (int q = 0; q < CPL; ++q) {
+            float f[8];
+            bf16x8_to_f32(x[t][q], f);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[q][j] = fmaf(w[t], f[j], acc[q][j]);
+          }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < CPL; ++q) {
+      const int c = lane + 32 * q;
+      if (c >= chunks) continue;
+      float h[8];
+      bf16x8_to_f32(*reinterpret_cast<const uint4*>(a.mask + static_cast<int64_t>(u) * a.mask_stride + c * 8), h);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        acc[q][j] = h[j] != 0.f ? acc[q][j] * a.scale : 0.f;
+        bsum[q][j] += acc[q][j];
+      }
+      *reinterpret_cast<uint4*>(dyrow + c * 8) = f32_to_bf16x8(acc[q]);
+    }
+  }
+  if (a.dbias) {
+#pragma unroll
+    for (int q = 0; q < CPL; ++q)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s_col[wib][(lane + 32 * q) * 8 + j] = bsum[q][j];
+    __syncthreads();
+    for (int c = threadIdx.x; c < a.dim; c += blockDim.x) {
+      float t = 0.f;
+#pragma unroll
+      for (int w = 0; w < kThreads / 32; ++w) t += s_col[w][c];
+      if (t != 0.f) atomicAdd(a.dbias + c, t);
+    }
+  }
+}
+
 __global__ void out_degree_kernel(const int32_t* indices, const int32_t* n_edges_ptr, float* deg) {
   const int n_e = *n_edges_ptr;
   for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < n_e; e += gridDim.x * blockDim.x)
@@ -356,6 +467,18 @@ void launch_aggregate_bwd(const AggBwdArgs& a, int cap_dst, cudaStream_t stream)
   else if (chunks <= 64) aggregate_bwd_kernel<2><<<grid, kThreads, 0, stream>>>(a);
   else if (chunks <= 128) aggregate_bwd_kernel<4><<<grid, kThreads, 0, stream>>>(a);
   else throw std::invalid_argument("aggregate_bwd: dim > 1024 not supported");
+  GB_LAUNCH_CHECK();
+}
+
+void launch_aggregate_bwd_gather(const AggBwdGatherArgs& a, cudaStream_t stream) {
+  if (a.dim % 8 != 0 || a.dout_stride % 8 != 0 || a.dy_stride % 8 != 0 || a.mask_stride % 8 != 0 ||
+      a.self_col % 8 != 0 || a.agg_col % 8 != 0)
+    throw std::invalid_argument("aggregate_bwd_gather: dims, strides and columns must be multiples of 8");
+  const int grid = grid_for_rows(a.cap_rows);
+  const int chunks = a.dim / 8;
+  if (chunks <= 32) aggregate_bwd_gather_kernel<1><<<grid, kThreads, 0, stream>>>(a);
+  else if (chunks <= 64) aggregate_bwd_gather_kernel<2><<<grid, kThreads, 0, stream>>>(a);
+  else throw std::invalid_argument("aggregate_bwd_gather: dim > 512 not supported");
   GB_LAUNCH_CHECK();
 }
 

@@ -50,6 +50,7 @@ KERNELS_PER_CALL = {
     "shuffle_keys": 1, "sample_prologue": 1, "cross_entropy": 1, "batchnorm_fwd": 2, "batchnorm_bwd": 2, "l2norm_fwd": 1,
     "l2norm_bwd": 1, "dropout_rows": 1, "dropout_grad": 1, "f32_to_bf16_rows": 1, "add_bf16_rows": 1,
     "gat_scores": 1, "gat_fwd": 1, "gat_bwd": 2, "gat_bwd_input": 2, "gat_dw_combine": 1, "sampler_counters": 1,
+    "block_transpose": 1, "aggregate_bwd_gather": 1,
 }
 
 
@@ -258,6 +259,14 @@ class BlockEngine:
         self._seed_table = None
         if self.allreduce is not None:
             self.allreduce.bind(self.counters, self.m, self.v, self.wbf, self.lr, self.betas, self.eps, self.err)
+        # one rank: Adam per layer on the comm stream as soon as the layer's gradient is
+        # complete (the same overlap as the per-layer all-reduce)
+        self._adam_slices = None
+        if self.world == 1 and overlap_allreduce:
+            buckets = model.layer_buckets(self.L)
+            if buckets is not None:
+                self._adam_slices = [tuple(t[lo:hi] for t in (self.flat, self.m, self.v, self.grad, self.wbf))
+                                     for lo, hi in buckets]
 
         # block sources: with CUDA graphs two samplers alternate, so that the next
         # step's sampling (a side stream inside the step graph) overlaps this step's
@@ -376,15 +385,20 @@ class BlockEngine:
         its parameters: reduce its bucket (all-reduce + Adam) on the comm stream while
         the backward pass goes on with the layers before it (the reference's DDP buckets
         reduced by the comm hook as autograd produces them)."""
-        if not self._ar_by_layer:
+        if not (self._ar_by_layer or self._adam_slices):
             return
         comm = self._comm_stream()
         comm.wait_stream(torch.cuda.current_stream(self.device))
         if getattr(self, "_aux", None) is not None:
             comm.wait_stream(self._aux)
         with torch.cuda.stream(comm):
-            self.allreduce.launch(l, self._cov())
-        self.cu.count += 1
+            if self._ar_by_layer:
+                self.allreduce.launch(l, self._cov())
+                self.cu.count += 1
+            else:
+                p, m, v, g, w = self._adam_slices[l]
+                b1, b2 = self.betas
+                self.cu.adam(p, m, v, g, w, self.lr, b1, b2, self.eps, 0.0, self.counters, 1.0, None, True)
         self._comm_used = True
 
     def _backward(self):
@@ -468,6 +482,11 @@ class BlockEngine:
             dist.all_reduce(self.grad)
             cu.adam(self.flat, self.m, self.v, self.grad, self.wbf, self.lr, b1, b2, self.eps, 0.0, self.counters,
                     1.0, None, True)
+        elif self._adam_slices:
+            # every layer's Adam was launched on the comm stream during the backward pass
+            if getattr(self, "_comm_used", False):
+                torch.cuda.current_stream(self.device).wait_stream(self._comm)
+                self._comm_used = False
         else:
             cu.adam(self.flat, self.m, self.v, self.grad, self.wbf, self.lr, b1, b2, self.eps, 0.0, self.counters,
                     1.0, None, True)
@@ -702,9 +721,17 @@ class BlockEngine:
 
 
 class SageEngine(BlockEngine):
-    """GraphSAGE (mean): [h_dst | mean h_src] . [W_self | W_neigh]^T + b in one GEMM."""
+    """GraphSAGE (mean): [h_dst | mean h_src] . [W_self | W_neigh]^T + b in one GEMM.
+    The backward of every inner hop runs gathered by source over the block's transpose
+    (built by the sampler on its side stream), with the previous layer's ReLU/dropout
+    backward fused: no fp32 gradient rows and no separate activation pass."""
 
     model_name = "sage"
+
+    def _make_sampler(self, batch_size, n_nodes_cap, dev):
+        # hops 0 .. L-2 feed a backward aggregation (the input layer's hop does not)
+        return GpuNeighborSampler(self.fanouts, batch_size, n_nodes_cap, dev, cu=self.cu,
+                                  transpose_hops=tuple(range(self.L - 1)))
 
     def _alloc_layers(self):
         dev = self.device
@@ -720,7 +747,8 @@ class SageEngine(BlockEngine):
                         dY=torch.zeros((rows, op), dtype=torch.bfloat16, device=dev))
             if l < self.L - 1:
                 spec["H"] = torch.zeros((rows, op), dtype=torch.bfloat16, device=dev)
-                spec["dH"] = torch.zeros((rows, op), dtype=torch.float32, device=dev)
+                if self.full_graph or not getattr(self.sm, "tptr", None):
+                    spec["dH"] = torch.zeros((rows, op), dtype=torch.float32, device=dev)
             else:
                 spec["ce_fused"] = op <= 64
                 if not spec["ce_fused"]:
@@ -764,6 +792,11 @@ class SageEngine(BlockEngine):
         self._gemm(s["dY"], False, s["W"], True, s["rows"], self._n_dst(h), s["K"], s["op"], None, 1, s["dX"],
                    GEMM_STORE_BF16)
         prev = self.lay[l - 1]
+        if "dH" not in prev:
+            # gathered by source over the block's transpose, activation backward fused
+            cu.aggregate_bwd_gather(sm.indptr[h], sm.tptr[h], sm.tdst[h], self._n_dst(h), sm.n_src(h), s["dX"], 0,
+                                    s["ip"], s["ip"], prev["H"], scale, prev["dY"], prev["gb"], self.err)
+            return
         # transpose aggregation: d(self) -> dst rows, d(agg) -> sources
         cu.aggregate_bwd(sm.indptr[h], sm.indices[h], self._n_dst(h), 0, sm.cap_dst[h], s["dX"],
                          s["ip"], 0, 0.0, s["ip"], AGG_MEAN, None, None, None, prev["dH"], self.err)

@@ -43,7 +43,7 @@ def hop_capacities(batch_size, fanouts, n_nodes_cap):
 
 
 class GpuNeighborSampler:
-    def __init__(self, fanouts, batch_size, n_nodes_cap, device, cu=None, replace=False):
+    def __init__(self, fanouts, batch_size, n_nodes_cap, device, cu=None, replace=False, transpose_hops=()):
         self.cu = cu if cu is not None else _native.cuda()
         self.fanouts = [int(f) for f in fanouts]
         self.L = len(self.fanouts)
@@ -70,6 +70,14 @@ class GpuNeighborSampler:
         # dense tagged id map of the compaction (never cleared: tags decrease call to call)
         self.map = torch.full((self.n_nodes_cap,), -1, dtype=torch.int64, device=dev)
         self.err = torch.zeros(1, **i32)
+        # blocks also kept grouped by source (CSR by local src) for the gathered backward
+        self.transpose_hops = tuple(int(h) for h in transpose_hops)
+        self.t_cnt, self.t_rank, self.tptr, self.tdst = {}, {}, {}, {}
+        for h in self.transpose_hops:
+            self.t_cnt[h] = torch.zeros(self.cap_src[h], **i32)
+            self.t_rank[h] = torch.zeros(self.cap_e[h], **i32)
+            self.tptr[h] = torch.zeros(self.cap_src[h] + 1, **i32)
+            self.tdst[h] = torch.zeros(self.cap_e[h], **i32)
 
     # device counters ------------------------------------------------------------------
     def n_seeds(self):
@@ -110,9 +118,13 @@ class GpuNeighborSampler:
                           counters, h, self.seed_gideg if (h == 0 and gideg is not None) else None,
                           cov if h == 0 else None, self.indptr[h], self.nbr[h], self.n_edges(h), self.sscr[h], err,
                           self.cap_dst[h], self.map, self.src[h], self.sampled[h])
+            tr = h in self.t_cnt
             cu.compact(dst, self.n_dst(h), self.nbr[h], self.n_edges(h), self.map, self.src[h], self.sampled[h],
                        self.indices[h], self.n_src(h), self.cscr[h], err, self.cap_dst[h], self.cap_e[h], counters, h,
-                       True)
+                       True, self.t_cnt.get(h), self.t_rank.get(h))
+            if tr:
+                cu.block_transpose(self.indptr[h], self.indices[h], self.n_dst(h), self.n_src(h), self.t_cnt[h],
+                                   self.t_rank[h], self.tptr[h], self.tdst[h], err)
 
     def blocks(self):
         """Materialise the sampled blocks (input layer first) with exact sizes (host sync)."""

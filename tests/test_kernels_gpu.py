@@ -274,6 +274,55 @@ def test_aggregate_backward(mode, dim):
     torch.testing.assert_close(dsrc.cpu(), h.grad, rtol=1e-3, atol=1e-3)
 
 
+def test_block_transpose_and_gathered_mean_backward():
+    """The block transpose (CSR by source) and the gathered mean backward with the fused
+    activation backward against a scatter reference in fp32."""
+    torch.manual_seed(8)
+    n_dst, n_src, cap, dim = 300, 1000, 1088, 64
+    deg = torch.randint(0, 12, (n_dst,))
+    indptr = torch.zeros(n_dst + 1, dtype=torch.int32)
+    indptr[1:] = torch.cumsum(deg, 0)
+    E = int(indptr[-1])
+    indices = torch.randint(0, n_src, (E,), dtype=torch.int32)
+    # edge ranks among each source's edges (what compaction K3 records with atomics)
+    t_cnt = torch.zeros(cap, dtype=torch.int32)
+    t_rank = torch.zeros(E, dtype=torch.int32)
+    for e in torch.randperm(E).tolist():
+        u = int(indices[e])
+        t_rank[e] = t_cnt[u]
+        t_cnt[u] += 1
+    d = dict(device=DEV)
+    tptr = torch.zeros(cap + 1, dtype=torch.int32, **d)
+    tdst = torch.full((E,), -1, dtype=torch.int32, **d)
+    nd, ns = torch.tensor([n_dst], dtype=torch.int32, **d), torch.tensor([n_src], dtype=torch.int32, **d)
+    err = err_tensor()
+    t_cnt_d = t_cnt.to(DEV)
+    cu().block_transpose(indptr.to(DEV), indices.to(DEV), nd, ns, t_cnt_d, t_rank.to(DEV), tptr, tdst, err)
+    torch.cuda.synchronize()
+    assert err.item() == 0 and bool((t_cnt_d == 0).all())
+    # every (src, dst) edge appears once in the transposed lists
+    v_of_e = torch.repeat_interleave(torch.arange(n_dst), deg)
+    tp, td = tptr.cpu(), tdst.cpu()
+    got = sorted((u, int(td[k])) for u in range(n_src) for k in range(int(tp[u]), int(tp[u + 1])))
+    assert got == sorted(zip(indices.tolist(), v_of_e.tolist()))
+    dX = bf(torch.randn(n_dst, 2 * dim, device=DEV))
+    H = bf(torch.relu(torch.randn(cap, dim, device=DEV)))
+    dy = torch.full((cap, dim), 5.0, dtype=torch.bfloat16, **d)
+    db = torch.zeros(dim, **d)
+    cu().aggregate_bwd_gather(indptr.to(DEV), tptr, tdst, nd, ns, dX, 0, dim, dim, H, 2.0, dy, db, err)
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    g = torch.zeros(n_src, dim, **d)
+    g[:n_dst] += dX[:, :dim].float()
+    w = (1.0 / deg.clamp(min=1).float())[v_of_e].to(DEV)
+    g.index_add_(0, indices.long().to(DEV), dX[v_of_e.to(DEV), dim:].float() * w[:, None])
+    want = torch.where(H[:n_src] != 0, g * 2.0, torch.zeros((), **d))
+    torch.testing.assert_close(dy[:n_src].float(), want, rtol=2e-2, atol=2e-2)
+    tail = (n_src + 63) // 64 * 64
+    assert bool((dy[n_src:tail] == 0).all()) and bool((dy[tail:] == 5.0).all())
+    torch.testing.assert_close(db, dy[:n_src].float().sum(0), rtol=1e-3, atol=1e-2)
+
+
 def test_act_bwd_mask_bias_and_clear():
     torch.manual_seed(8)
     R, n, dim = 700, 613, 256
