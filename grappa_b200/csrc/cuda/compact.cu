@@ -132,35 +132,37 @@ __global__ void __launch_bounds__(kThreads) compact_k3(CompactArgs a) {
 
 constexpr int kTpThreads = 1024;
 
-__global__ void __launch_bounds__(kTpThreads) block_transpose_kernel(const int32_t* indptr, const int32_t* indices,
-                                                                      const int32_t* n_dst_ptr, const int32_t* n_src_ptr,
-                                                                      int32_t* t_cnt, const int32_t* t_rank,
-                                                                      int32_t* tptr, int32_t* tdst, int cap_src,
-                                                                      int cap_edges, int32_t* err) {
+// Exclusive scan of the per-source edge counts into tptr (one CTA: each thread sums a
+// contiguous run of counts, one block scan of the 1024 partial sums, then each thread
+// writes its run's prefixes); the counts are cleared for the next block.
+__global__ void __launch_bounds__(kTpThreads) block_transpose_scan_kernel(const int32_t* n_src_ptr, int32_t* t_cnt,
+                                                                           int32_t* tptr, int cap_src) {
   __shared__ long long s_scan[kTpThreads / 32];
-  __shared__ long long s_carry;
   const int n_src = min(*n_src_ptr, cap_src);
-  const int n_dst = *n_dst_ptr;
-  if (threadIdx.x == 0) s_carry = 0;
-  __syncthreads();
-  // exclusive scan of the per-source counts, 1024 at a time; the counts are cleared
-  for (int base = 0; base < n_src; base += kTpThreads) {
-    const int i = base + static_cast<int>(threadIdx.x);
-    const int c = i < n_src ? t_cnt[i] : 0;
-    if (i < n_src) t_cnt[i] = 0;
-    long long total;
-    const long long excl = block_exclusive_scan<kTpThreads, long long>(c, s_scan, &total);
-    const long long carry = s_carry;
-    if (i < n_src) tptr[i] = static_cast<int32_t>(carry + excl);
-    __syncthreads();
-    if (threadIdx.x == 0) s_carry = carry + total;
-    __syncthreads();
+  const int per = (n_src + kTpThreads - 1) / kTpThreads;
+  const int b = min(n_src, static_cast<int>(threadIdx.x) * per), e = min(n_src, b + per);
+  long long sum = 0;
+  for (int i = b; i < e; ++i) sum += t_cnt[i];
+  long long total;
+  long long run = block_exclusive_scan<kTpThreads, long long>(sum, s_scan, &total);
+  for (int i = b; i < e; ++i) {
+    tptr[i] = static_cast<int32_t>(run);
+    run += t_cnt[i];
+    t_cnt[i] = 0;
   }
-  if (threadIdx.x == 0) tptr[n_src] = static_cast<int32_t>(s_carry);
-  __syncthreads();
-  // fill: one warp per destination, its edges by lane
-  const int warps = kTpThreads / 32;
-  for (int v = threadIdx.x >> 5; v < n_dst; v += warps) {
+  if (threadIdx.x == 0) tptr[n_src] = static_cast<int32_t>(total);
+}
+
+// tdst[tptr[s] + rank_e] = v for every edge e = (s -> v): one warp per destination.
+__global__ void __launch_bounds__(kThreads) block_transpose_fill_kernel(const int32_t* indptr, const int32_t* indices,
+                                                                         const int32_t* n_dst_ptr,
+                                                                         const int32_t* n_src_ptr, const int32_t* t_rank,
+                                                                         const int32_t* tptr, int32_t* tdst,
+                                                                         int cap_edges, int32_t* err) {
+  const int n_dst = *n_dst_ptr;
+  const int n_src = *n_src_ptr;
+  const int warps = (gridDim.x * kThreads) >> 5;
+  for (int v = (blockIdx.x * kThreads + threadIdx.x) >> 5; v < n_dst; v += warps) {
     const int beg = indptr[v], end = indptr[v + 1];
     for (int e = beg + static_cast<int>(lane_id()); e < end; e += 32) {
       const int s = indices[e];
@@ -176,8 +178,16 @@ __global__ void __launch_bounds__(kTpThreads) block_transpose_kernel(const int32
 void launch_block_transpose(const int32_t* indptr, const int32_t* indices, const int32_t* n_dst_ptr,
                             const int32_t* n_src_ptr, int32_t* t_cnt, const int32_t* t_rank, int32_t* tptr,
                             int32_t* tdst, int cap_src, int cap_edges, int32_t* err, cudaStream_t stream) {
-  block_transpose_kernel<<<1, kTpThreads, 0, stream>>>(indptr, indices, n_dst_ptr, n_src_ptr, t_cnt, t_rank, tptr, tdst,
-                                                       cap_src, cap_edges, err);
+  block_transpose_scan_kernel<<<1, kTpThreads, 0, stream>>>(n_src_ptr, t_cnt, tptr, cap_src);
+  GB_LAUNCH_CHECK();
+  const int cap_dst = cap_src;  // destinations are the first sources
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int grid = static_cast<int>(std::min<long long>(ceil_div(cap_dst > 0 ? cap_dst : 1, kThreads / 32),
+                                                        static_cast<long long>(sms) * 8));
+  block_transpose_fill_kernel<<<grid, kThreads, 0, stream>>>(indptr, indices, n_dst_ptr, n_src_ptr, t_rank, tptr, tdst,
+                                                            cap_edges, err);
   GB_LAUNCH_CHECK();
 }
 

@@ -187,18 +187,21 @@ __global__ void __launch_bounds__(kThreads) gat_scores_kernel(GatArgs a) {
 // m_new), and the z rows of the batch are added with the weights exp(x - m), four
 // edges' rows in flight per lane.  The output is acc / s (+ bias); m and s are kept
 // for the backward, which recomputes the attention from them.
-template <int CPL>
-__device__ __forceinline__ float pick_head(const float (&v)[kMaxHeads], int h) {
+template <int HM>
+__device__ __forceinline__ float pick_head(const float (&v)[HM], int h) {
   float r = 0.f;
 #pragma unroll
-  for (int hh = 0; hh < kMaxHeads; ++hh)
+  for (int hh = 0; hh < HM; ++hh)
     if (hh == h) r = v[hh];
   return r;
 }
 
-template <int CPL>
+// HM: the head count rounded up to 4 or kMaxHeads (sizes the per-head register arrays)
+template <int CPL, int HM>
 __global__ void __launch_bounds__(kThreads) gat_fwd_kernel(GatArgs a) {
   extern __shared__ float s_row[];  // mean_heads: [warps][HF]
+  __shared__ float s_w[kThreads / 32][32][HM];  // the batch's edge weights, per head
+  __shared__ int s_u[kThreads / 32][32];        // the batch's source rows
   const int n_dst = a.n_dst_ptr ? min(*a.n_dst_ptr, a.cap_dst) : a.cap_dst;
   const int H = a.heads, F = a.feat, HF = H * F;
   const int lane = threadIdx.x & 31;
@@ -235,9 +238,9 @@ __global__ void __launch_bounds__(kThreads) gat_fwd_kernel(GatArgs a) {
       continue;
     }
     const int beg = a.indptr[v], end = a.indptr[v + 1];
-    float er[kMaxHeads], m[kMaxHeads], sden[kMaxHeads];
+    float er[HM], m[HM], sden[HM];
 #pragma unroll
-    for (int h = 0; h < kMaxHeads; ++h) {
+    for (int h = 0; h < HM; ++h) {
       er[h] = h < H ? a.er[static_cast<int64_t>(v) * H + h] : 0.f;
       m[h] = -INFINITY;
       sden[h] = 0.f;
@@ -251,22 +254,22 @@ __global__ void __launch_bounds__(kThreads) gat_fwd_kernel(GatArgs a) {
       const int cnt = min(32, end - cb);
       const bool mine = lane < cnt;
       const int my_u = mine ? a.indices[cb + lane] : 0;
-      float w[kMaxHeads], sc[kMaxHeads];
-      float x[kMaxHeads];
-      if (H == 4) {
+      float x[HM];
+      if (HM == 4 && H == 4) {
         float4 e4 = make_float4(0.f, 0.f, 0.f, 0.f);
         if (mine) e4 = *reinterpret_cast<const float4*>(a.el + static_cast<int64_t>(my_u) * 4);
-        x[0] = e4.x; x[1] = e4.y; x[2] = e4.z; x[3] = e4.w;
-#pragma unroll
-        for (int h = 4; h < kMaxHeads; ++h) x[h] = 0.f;
+        x[0] = e4.x;
+        x[1] = e4.y;
+        x[2] = e4.z;
+        x[3] = e4.w;
       } else {
 #pragma unroll
-        for (int h = 0; h < kMaxHeads; ++h) x[h] = (mine && h < H) ? a.el[static_cast<int64_t>(my_u) * H + h] : 0.f;
+        for (int h = 0; h < HM; ++h) x[h] = (mine && h < H) ? a.el[static_cast<int64_t>(my_u) * H + h] : 0.f;
       }
+      float sc[HM];
 #pragma unroll
-      for (int h = 0; h < kMaxHeads; ++h) {
+      for (int h = 0; h < HM; ++h) {
         if (h >= H) {
-          w[h] = 0.f;
           sc[h] = 1.f;
           continue;
         }
@@ -276,14 +279,16 @@ __global__ void __launch_bounds__(kThreads) gat_fwd_kernel(GatArgs a) {
         for (int o = 16; o > 0; o >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o));
         const float nm = fmaxf(m[h], bm);
         sc[h] = __expf(m[h] - nm);  // 0 on the first batch (m = -inf)
-        w[h] = mine ? __expf(xs - nm) : 0.f;
-        sden[h] = sden[h] * sc[h] + warp_sum(w[h]);
+        const float w = mine ? __expf(xs - nm) : 0.f;
+        s_w[wib][lane][h] = w;
+        sden[h] = sden[h] * sc[h] + warp_sum(w);
         m[h] = nm;
       }
+      s_u[wib][lane] = my_u;
+      __syncwarp();
 #pragma unroll
       for (int q = 0; q < CPL; ++q) {
-        const int c0 = (lane + 32 * q) * 8;
-        const float s0 = pick_head<CPL>(sc, h0[q]), s1 = pick_head<CPL>(sc, h1[q]);
+        const float s0 = pick_head<HM>(sc, h0[q]), s1 = pick_head<HM>(sc, h1[q]);
 #pragma unroll
         for (int j = 0; j < 8; ++j) acc[q][j] *= ((in0[q] >> j) & 1u) ? s0 : s1;
       }
@@ -292,17 +297,13 @@ __global__ void __launch_bounds__(kThreads) gat_fwd_kernel(GatArgs a) {
         float wt0[EU][CPL], wt1[EU][CPL];
 #pragma unroll
         for (int t = 0; t < EU; ++t) {
-          const int src_lane = min(k + t, 31);
-          const int u = __shfl_sync(0xffffffffu, my_u, src_lane);
           const bool ok = k + t < cnt;
-          float wl[kMaxHeads];
-#pragma unroll
-          for (int h = 0; h < kMaxHeads; ++h) wl[h] = h < H ? __shfl_sync(0xffffffffu, w[h], src_lane) : 0.f;
+          const int u = s_u[wib][ok ? k + t : 0];
 #pragma unroll
           for (int q = 0; q < CPL; ++q) {
             const int c0 = (lane + 32 * q) * 8;
-            wt0[t][q] = ok ? pick_head<CPL>(wl, h0[q]) : 0.f;
-            wt1[t][q] = ok ? pick_head<CPL>(wl, h1[q]) : 0.f;
+            wt0[t][q] = ok ? s_w[wib][k + t][h0[q]] : 0.f;
+            wt1[t][q] = ok ? s_w[wib][k + t][h1[q]] : 0.f;
             zv[t][q] = make_uint4(0, 0, 0, 0);
             if (ok && c0 < HF) zv[t][q] = *reinterpret_cast<const uint4*>(a.z + static_cast<int64_t>(u) * a.ldz + c0);
           }
@@ -311,23 +312,22 @@ __global__ void __launch_bounds__(kThreads) gat_fwd_kernel(GatArgs a) {
         for (int t = 0; t < EU; ++t)
 #pragma unroll
           for (int q = 0; q < CPL; ++q) {
-            const int c0 = (lane + 32 * q) * 8;
             float f[8];
             bf16x8_to_f32(zv[t][q], f);
 #pragma unroll
             for (int j = 0; j < 8; ++j) acc[q][j] = fmaf(((in0[q] >> j) & 1u) ? wt0[t][q] : wt1[t][q], f[j], acc[q][j]);
           }
       }
+      __syncwarp();  // the batch's weights are read before the next batch writes them
     }
     // normalise by the softmax denominators; keep the statistics for the backward
     if (lane < H) {
-      a.smax[static_cast<int64_t>(v) * H + lane] = pick_head<CPL>(m, lane);
-      a.ssum[static_cast<int64_t>(v) * H + lane] = pick_head<CPL>(sden, lane);
+      a.smax[static_cast<int64_t>(v) * H + lane] = pick_head<HM>(m, lane);
+      a.ssum[static_cast<int64_t>(v) * H + lane] = pick_head<HM>(sden, lane);
     }
 #pragma unroll
     for (int q = 0; q < CPL; ++q) {
-      const int c0 = (lane + 32 * q) * 8;
-      const float d0 = pick_head<CPL>(sden, h0[q]), d1 = pick_head<CPL>(sden, h1[q]);
+      const float d0 = pick_head<HM>(sden, h0[q]), d1 = pick_head<HM>(sden, h1[q]);
       const float i0 = d0 > 0.f ? 1.f / d0 : 0.f, i1 = d1 > 0.f ? 1.f / d1 : 0.f;
 #pragma unroll
       for (int j = 0; j < 8; ++j) acc[q][j] *= ((in0[q] >> j) & 1u) ? i0 : i1;
@@ -892,7 +892,18 @@ void launch_gat_fwd(const GatArgs& a, cudaStream_t stream) {
   if (a.ldo % 8 != 0) throw std::invalid_argument("gat: out stride % 8");
   if (a.dropout_p > 0.f && !a.counters) throw std::invalid_argument("gat: dropout needs the step counters");
   const size_t smem = a.mean_heads ? (kThreads / 32) * a.heads * a.feat * sizeof(float) : 0;
-  GAT_DISPATCH(gat_fwd_kernel, grid_warps(a.cap_dst), smem);
+  const int grid = grid_warps(a.cap_dst);
+  const int cpl = cpl_for(a.heads * a.feat);
+#define GAT_FWD(C)                                                                      \
+  do {                                                                                  \
+    if (a.heads <= 4) gat_fwd_kernel<C, 4><<<grid, kThreads, smem, stream>>>(a);        \
+    else gat_fwd_kernel<C, kMaxHeads><<<grid, kThreads, smem, stream>>>(a);            \
+  } while (0)
+  if (cpl <= 1) GAT_FWD(1);
+  else if (cpl <= 2) GAT_FWD(2);
+  else GAT_FWD(4);
+#undef GAT_FWD
+  GB_LAUNCH_CHECK();
 }
 
 bool seg_heads(int F) { return F >= 8 && F <= 256 && (F & (F - 1)) == 0; }

@@ -96,8 +96,9 @@ int compact_scan_scratch_words(int cap_edges);
 
 // The block's edges grouped by source (CSR by local src): tptr[n_src + 1] from an
 // exclusive scan of t_cnt (cleared as it is read), tdst[k] = the destination of the
-// k-th edge of its source (edge order within a source: t_rank).  One CTA (the blocks
-// that need it are the inner hops: tens of thousands of nodes at most).
+// k-th edge of its source (edge order within a source: t_rank).  A one-CTA scan (the
+// blocks that need it are the inner hops: tens of thousands of nodes at most) and a
+// fill with one warp per destination.
 void launch_block_transpose(const int32_t* indptr, const int32_t* indices, const int32_t* n_dst_ptr,
                             const int32_t* n_src_ptr, int32_t* t_cnt, const int32_t* t_rank, int32_t* tptr,
                             int32_t* tdst, int cap_src, int cap_edges, int32_t* err, cudaStream_t stream);

@@ -50,7 +50,7 @@ KERNELS_PER_CALL = {
     "shuffle_keys": 1, "sample_prologue": 1, "cross_entropy": 1, "batchnorm_fwd": 2, "batchnorm_bwd": 2, "l2norm_fwd": 1,
     "l2norm_bwd": 1, "dropout_rows": 1, "dropout_grad": 1, "f32_to_bf16_rows": 1, "add_bf16_rows": 1,
     "gat_scores": 1, "gat_fwd": 1, "gat_bwd": 2, "gat_bwd_input": 2, "gat_dw_combine": 1, "sampler_counters": 1,
-    "block_transpose": 1, "aggregate_bwd_gather": 1,
+    "block_transpose": 2, "aggregate_bwd_gather": 1,
 }
 
 
@@ -262,6 +262,7 @@ class BlockEngine:
         # one rank: Adam per layer on the comm stream as soon as the layer's gradient is
         # complete (the same overlap as the per-layer all-reduce)
         self._adam_slices = None
+        self._launched = set()
         if self.world == 1 and overlap_allreduce:
             buckets = model.layer_buckets(self.L)
             if buckets is not None:
@@ -392,19 +393,27 @@ class BlockEngine:
         if getattr(self, "_aux", None) is not None:
             comm.wait_stream(self._aux)
         with torch.cuda.stream(comm):
-            if self._ar_by_layer:
-                self.allreduce.launch(l, self._cov())
-                self.cu.count += 1
-            else:
-                p, m, v, g, w = self._adam_slices[l]
-                b1, b2 = self.betas
-                self.cu.adam(p, m, v, g, w, self.lr, b1, b2, self.eps, 0.0, self.counters, 1.0, None, True)
+            self._launch_update(l)
+        self._launched.add(l)
         self._comm_used = True
 
-    def _backward(self):
+    def _launch_update(self, l):
+        """All-reduce + Adam (or Adam alone) of layer l's parameters on the current stream."""
+        if self._ar_by_layer:
+            self.allreduce.launch(l, self._cov())
+            self.cu.count += 1
+        else:
+            p, m, v, g, w = self._adam_slices[l]
+            b1, b2 = self.betas
+            self.cu.adam(p, m, v, g, w, self.lr, b1, b2, self.eps, 0.0, self.counters, 1.0, None, True)
+
+    def _backward(self, update=False):
+        """The backward pass; with ``update`` every layer's update is launched on the comm
+        stream as soon as its gradient is complete (else ``_update`` runs them all)."""
         for l in range(self.L - 1, -1, -1):
             self._backward_layer(l)
-            self._grad_ready(l)
+            if update:
+                self._grad_ready(l)
 
     def _backward_layer(self, l):
         raise NotImplementedError
@@ -463,15 +472,19 @@ class BlockEngine:
         self._join_aux()
         cu = self.cu
         b1, b2 = self.betas
-        if self.fused_allreduce:
-            if self._ar_by_layer:
-                # every bucket was launched on the comm stream during the backward pass
-                if getattr(self, "_comm_used", False):
-                    torch.cuda.current_stream(self.device).wait_stream(self._comm)
-                    self._comm_used = False
-            else:
-                self.allreduce.launch_all(self._cov())
-                self.cu.count += len(self.allreduce.buckets)
+        if self._ar_by_layer or self._adam_slices:
+            # per-layer updates: those not launched during the backward pass run here,
+            # then the comm stream joins
+            for l in range(self.L - 1, -1, -1):
+                if l not in self._launched:
+                    self._launch_update(l)
+            self._launched = set()
+            if getattr(self, "_comm_used", False):
+                torch.cuda.current_stream(self.device).wait_stream(self._comm)
+                self._comm_used = False
+        elif self.fused_allreduce:
+            self.allreduce.launch_all(self._cov())
+            self.cu.count += len(self.allreduce.buckets)
         elif self.world > 1:
             # the reference's path (t10n/grad.py:6-24): scale by c_r / W, NCCL SUM all-reduce, Adam
             import torch.distributed as dist
@@ -482,11 +495,6 @@ class BlockEngine:
             dist.all_reduce(self.grad)
             cu.adam(self.flat, self.m, self.v, self.grad, self.wbf, self.lr, b1, b2, self.eps, 0.0, self.counters,
                     1.0, None, True)
-        elif self._adam_slices:
-            # every layer's Adam was launched on the comm stream during the backward pass
-            if getattr(self, "_comm_used", False):
-                torch.cuda.current_stream(self.device).wait_stream(self._comm)
-                self._comm_used = False
         else:
             cu.adam(self.flat, self.m, self.v, self.grad, self.wbf, self.lr, b1, b2, self.eps, 0.0, self.counters,
                     1.0, None, True)
@@ -496,7 +504,7 @@ class BlockEngine:
         self.cu.zero_(self.istats)
         self._sample()
         self._forward(True)
-        self._backward()
+        self._backward(update=True)
         self._update()
         self.cu.step_end(self.counters)
 
@@ -528,7 +536,7 @@ class BlockEngine:
             with torch.cuda.stream(side):
                 self._sample_into(1 - p, 1)
         self._forward(True)
-        self._backward()
+        self._backward(update=True)
         self._update()
         if prefetch:
             main.wait_stream(side)
@@ -671,7 +679,8 @@ class BlockEngine:
             self.cu.zero_(self.istats)
             e = ev[s]
             e[0].record()
-            for k, fn in enumerate((self._sample, lambda: self._forward(True), self._backward, self._update)):
+            for k, fn in enumerate((self._sample, lambda: self._forward(True), lambda: self._backward(update=True),
+                                    self._update)):
                 nvtx.range_push(names[k])
                 fn()
                 nvtx.range_pop()
