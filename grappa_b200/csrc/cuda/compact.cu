@@ -132,25 +132,26 @@ __global__ void __launch_bounds__(kThreads) compact_k3(CompactArgs a) {
 
 constexpr int kTpThreads = 1024;
 
-// Exclusive scan of the per-source edge counts into tptr (one CTA: each thread sums a
-// contiguous run of counts, one block scan of the 1024 partial sums, then each thread
-// writes its run's prefixes); the counts are cleared for the next block.
+// Exclusive scan of the per-source edge counts into tptr (one CTA, coalesced: 1024
+// counts per iteration, each iteration's block scan plus a running carry); the counts
+// are cleared for the next block.
 __global__ void __launch_bounds__(kTpThreads) block_transpose_scan_kernel(const int32_t* n_src_ptr, int32_t* t_cnt,
                                                                            int32_t* tptr, int cap_src) {
-  __shared__ long long s_scan[kTpThreads / 32];
+  __shared__ int s_scan[kTpThreads / 32];
   const int n_src = min(*n_src_ptr, cap_src);
-  const int per = (n_src + kTpThreads - 1) / kTpThreads;
-  const int b = min(n_src, static_cast<int>(threadIdx.x) * per), e = min(n_src, b + per);
-  long long sum = 0;
-  for (int i = b; i < e; ++i) sum += t_cnt[i];
-  long long total;
-  long long run = block_exclusive_scan<kTpThreads, long long>(sum, s_scan, &total);
-  for (int i = b; i < e; ++i) {
-    tptr[i] = static_cast<int32_t>(run);
-    run += t_cnt[i];
-    t_cnt[i] = 0;
+  int carry = 0;
+  for (int base = 0; base < n_src; base += kTpThreads) {
+    const int i = base + static_cast<int>(threadIdx.x);
+    const int c = i < n_src ? t_cnt[i] : 0;
+    int total;
+    const int excl = block_exclusive_scan<kTpThreads, int>(c, s_scan, &total);
+    if (i < n_src) {
+      tptr[i] = carry + excl;
+      t_cnt[i] = 0;
+    }
+    carry += total;
   }
-  if (threadIdx.x == 0) tptr[n_src] = static_cast<int32_t>(total);
+  if (threadIdx.x == 0) tptr[n_src] = carry;
 }
 
 // tdst[tptr[s] + rank_e] = v for every edge e = (s -> v): one warp per destination.

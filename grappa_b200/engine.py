@@ -41,6 +41,23 @@ AGG_MEAN, AGG_SUM, AGG_GCN, AGG_WEIGHTED = 0, 1, 2, 3
 # GAT input layer: dW from attention-weighted input rows instead of a per-source dz
 # (GRAPPA_GAT_INPUT_BWD=0 selects the dz path, for comparisons)
 GAT_INPUT_LAYER_BWD = os.environ.get("GRAPPA_GAT_INPUT_BWD", "1") != "0"
+# GraphSAGE backward gathered by source over the block transpose (1) or scattered with
+# fp32 reductions plus a separate activation pass (0, the default: the transposes add
+# two kernels per hop to the sampling stream, which measured slower overall)
+SAGE_GATHER_BWD = os.environ.get("GRAPPA_SAGE_GATHER_BWD", "0") != "0"
+# stream priorities inside the step graphs: the layer chain, the weight gradients and
+# the updates at the highest priority, the next step's sampling at the lowest
+STREAM_PRIORITY = os.environ.get("GRAPPA_STREAM_PRIORITY", "1") != "0"
+# one rank: Adam per layer on the comm stream during the backward pass (1) or one Adam
+# pass after it (0, the default: measured faster on one GPU)
+ADAM_PER_LAYER = os.environ.get("GRAPPA_ADAM_PER_LAYER", "0") != "0"
+
+
+def _stream(device, high):
+    if not STREAM_PRIORITY:
+        return torch.cuda.Stream(device=device)
+    lo, hi = torch.cuda.Stream.priority_range()
+    return torch.cuda.Stream(device=device, priority=hi if high else lo)
 
 # kernels launched by each binding (memsets excluded)
 KERNELS_PER_CALL = {
@@ -263,7 +280,7 @@ class BlockEngine:
         # complete (the same overlap as the per-layer all-reduce)
         self._adam_slices = None
         self._launched = set()
-        if self.world == 1 and overlap_allreduce:
+        if self.world == 1 and overlap_allreduce and ADAM_PER_LAYER:
             buckets = model.layer_buckets(self.L)
             if buckets is not None:
                 self._adam_slices = [tuple(t[lo:hi] for t in (self.flat, self.m, self.v, self.grad, self.wbf))
@@ -368,7 +385,7 @@ class BlockEngine:
 
     def _aux_stream(self):
         if getattr(self, "_aux", None) is None:
-            self._aux = torch.cuda.Stream(device=self.device)
+            self._aux = _stream(self.device, True)
         return self._aux
 
     def _join_aux(self):
@@ -378,7 +395,7 @@ class BlockEngine:
 
     def _comm_stream(self):
         if getattr(self, "_comm", None) is None:
-            self._comm = torch.cuda.Stream(device=self.device)
+            self._comm = _stream(self.device, True)
         return self._comm
 
     def _grad_ready(self, l):
@@ -509,7 +526,7 @@ class BlockEngine:
         self.cu.step_end(self.counters)
 
     def _capture(self, body):
-        s = torch.cuda.Stream(device=self.device)
+        s = _stream(self.device, True)
         s.wait_stream(torch.cuda.current_stream(self.device))
         g = torch.cuda.CUDAGraph()
         with torch.cuda.stream(s):
@@ -531,7 +548,7 @@ class BlockEngine:
         self._select(p)
         main = torch.cuda.current_stream(self.device)
         if prefetch:
-            side = torch.cuda.Stream(device=self.device)
+            side = _stream(self.device, False)
             side.wait_stream(main)
             with torch.cuda.stream(side):
                 self._sample_into(1 - p, 1)
@@ -740,7 +757,7 @@ class SageEngine(BlockEngine):
     def _make_sampler(self, batch_size, n_nodes_cap, dev):
         # hops 0 .. L-2 feed a backward aggregation (the input layer's hop does not)
         return GpuNeighborSampler(self.fanouts, batch_size, n_nodes_cap, dev, cu=self.cu,
-                                  transpose_hops=tuple(range(self.L - 1)))
+                                  transpose_hops=tuple(range(self.L - 1)) if SAGE_GATHER_BWD else ())
 
     def _alloc_layers(self):
         dev = self.device
