@@ -48,9 +48,9 @@ SAGE_GATHER_BWD = os.environ.get("GRAPPA_SAGE_GATHER_BWD", "0") != "0"
 # stream priorities inside the step graphs: the layer chain, the weight gradients and
 # the updates at the highest priority, the next step's sampling at the lowest
 STREAM_PRIORITY = os.environ.get("GRAPPA_STREAM_PRIORITY", "1") != "0"
-# one rank: Adam per layer on the comm stream during the backward pass (1) or one Adam
-# pass after it (0, the default: measured faster on one GPU)
-ADAM_PER_LAYER = os.environ.get("GRAPPA_ADAM_PER_LAYER", "0") != "0"
+# one rank: Adam per layer on the comm stream during the backward pass (1, the default)
+# or one Adam pass after it (0)
+ADAM_PER_LAYER = os.environ.get("GRAPPA_ADAM_PER_LAYER", "1") != "0"
 
 
 def _stream(device, high):
@@ -191,7 +191,7 @@ class GpuWalkSampler(GpuNeighborSampler):
         self.wscr = [torch.zeros(self.cu.walk_scratch_words(self.cap_dst[h]), dtype=torch.int64, device=self.device)
                      for h in range(self.L)]
 
-    def sample(self, indptr, indices, counters, gideg=None, cov=None, err=None):
+    def sample(self, indptr, indices, counters, gideg=None, cov=None, err=None, seed_gideg_ready=False):
         cu = self.cu
         err = self.err if err is None else err
         for h in range(self.L):
