@@ -807,8 +807,9 @@ void f32_to_bf16_rows(Tensor src, Tensor dst, int64_t dim, OptT n_dev, int64_t c
 // --------------------------------------------------------------------------- gat.cu
 d::GatArgs gat_args(Tensor indptr, Tensor indices, OptT n_dst_dev, int64_t cap_dst, OptT n_src_dev, int64_t cap_src,
                     int64_t heads, int64_t feat, Tensor z, Tensor attn_l, Tensor attn_r, Tensor el, Tensor er,
-                    Tensor smax, Tensor ssum, double slope) {
+                    Tensor smax, Tensor ssum, double slope, int64_t zmod = 0) {
   d::GatArgs a;
+  a.zmod = static_cast<int32_t>(zmod);
   a.indptr = ptr<int32_t>(indptr, at::kInt, "indptr");
   a.indices = ptr<int32_t>(indices, at::kInt, "indices");
   a.n_dst_ptr = optr<int32_t>(n_dst_dev, at::kInt, "n_dst_dev");
@@ -826,7 +827,7 @@ d::GatArgs gat_args(Tensor indptr, Tensor indices, OptT n_dst_dev, int64_t cap_d
   a.smax = ptr<float>(smax, at::kFloat, "smax");
   a.ssum = ptr<float>(ssum, at::kFloat, "ssum");
   a.slope = static_cast<float>(slope);
-  TORCH_CHECK(z.size(0) >= cap_src && z.size(1) >= heads * feat, "gat: z too small");
+  TORCH_CHECK(z.size(0) >= cap_src && z.size(1) >= (zmod > 0 ? zmod : heads * feat), "gat: z too small");
   TORCH_CHECK(el.numel() >= cap_src * heads && er.numel() >= cap_dst * heads, "gat: score buffers too small");
   TORCH_CHECK(smax.numel() >= cap_dst * heads && ssum.numel() >= cap_dst * heads, "gat: softmax buffers too small");
   TORCH_CHECK(attn_l.is_cuda() && attn_r.is_cuda() && attn_l.scalar_type() == at::kFloat, "gat: attention vectors");
@@ -916,6 +917,90 @@ void gat_bwd_input(Tensor indptr, Tensor indices, OptT n_dst_dev, int64_t cap_ds
   TORCH_CHECK(y.size(0) >= cap_dst && y.size(1) >= heads * in_dim, "gat: y too small");
   TORCH_CHECK(xl.numel() >= heads * in_dim && xr.numel() >= heads * in_dim, "gat: xl / xr too small");
   d::launch_gat_bwd_input(a, stream());
+}
+
+// GAT input layer with the projection after the aggregation (gat.cu): the rows are the
+// layer's input x (in_dim columns, shared by every head), the attention vectors wl/wr
+// (fp32 [heads * in_dim]) come from gat_in_prep
+void gat_in_scores(Tensor indptr, Tensor indices, OptT n_dst_dev, int64_t cap_dst, OptT n_src_dev, int64_t cap_src,
+                   int64_t heads, int64_t in_dim, Tensor x, Tensor wl, Tensor wr, Tensor el, Tensor er, Tensor smax,
+                   Tensor ssum, double slope) {
+  c10::cuda::CUDAGuard g(x.device());
+  auto a = gat_args(indptr, indices, n_dst_dev, cap_dst, n_src_dev, cap_src, heads, in_dim, x, wl, wr, el, er, smax, ssum,
+                    slope, in_dim);
+  d::launch_gat_scores(a, stream());
+}
+
+void gat_in_fwd(Tensor indptr, Tensor indices, OptT n_dst_dev, int64_t cap_dst, OptT n_src_dev, int64_t cap_src,
+                int64_t heads, int64_t in_dim, Tensor x, Tensor wl, Tensor wr, Tensor el, Tensor er, Tensor smax,
+                Tensor ssum, double slope, Tensor y) {
+  c10::cuda::CUDAGuard g(x.device());
+  auto a = gat_args(indptr, indices, n_dst_dev, cap_dst, n_src_dev, cap_src, heads, in_dim, x, wl, wr, el, er, smax, ssum,
+                    slope, in_dim);
+  a.bias = nullptr;
+  a.mean_heads = false;
+  a.act = 0;
+  a.out = reinterpret_cast<__nv_bfloat16*>(ptr2d<at::BFloat16>(y, at::kBFloat16, "y"));
+  a.ldo = y.stride(0);
+  TORCH_CHECK(y.size(0) >= cap_dst && y.size(1) >= heads * in_dim, "gat_in_fwd: y too small");
+  d::launch_gat_fwd(a, stream());
+}
+
+void gat_in_bwd(Tensor indptr, Tensor indices, OptT n_dst_dev, int64_t cap_dst, OptT n_src_dev, int64_t cap_src,
+                int64_t heads, int64_t in_dim, Tensor x, Tensor wl, Tensor wr, Tensor el, Tensor er, Tensor smax,
+                Tensor ssum, double slope, Tensor gx, Tensor edge_scratch, Tensor del, Tensor der, Tensor xl, Tensor xr,
+                Tensor err) {
+  c10::cuda::CUDAGuard g(x.device());
+  auto a = gat_args(indptr, indices, n_dst_dev, cap_dst, n_src_dev, cap_src, heads, in_dim, x, wl, wr, el, er, smax, ssum,
+                    slope, in_dim);
+  a.mean_heads = false;
+  a.dout = reinterpret_cast<const __nv_bfloat16*>(ptr2d<at::BFloat16>(gx, at::kBFloat16, "gx"));
+  a.lddo = gx.stride(0);
+  a.edge_scratch = ptr<float>(edge_scratch, at::kFloat, "edge_scratch");
+  a.del = ptr<float>(del, at::kFloat, "del");
+  a.der = ptr<float>(der, at::kFloat, "der");
+  a.dattn_l = ptr<float>(xl, at::kFloat, "xl");  // sum_u del x_u: the virtual rows' "attention" gradient
+  a.dattn_r = ptr<float>(xr, at::kFloat, "xr");
+  a.err = ptr<int32_t>(err, at::kInt, "err");
+  TORCH_CHECK(edge_scratch.numel() >= static_cast<int64_t>(indices.numel()) * heads, "gat: edge scratch too small");
+  TORCH_CHECK(gx.size(0) >= cap_dst && gx.size(1) >= heads * in_dim, "gat_in_bwd: gx too small");
+  TORCH_CHECK(xl.numel() >= heads * in_dim && xr.numel() >= heads * in_dim, "gat_in_bwd: xl / xr too small");
+  d::launch_gat_bwd(a, stream());
+}
+
+void gat_in_prep(Tensor w, Tensor attn_l, Tensor attn_r, int64_t heads, int64_t feat, int64_t in_dim, Tensor wl,
+                 Tensor wr, Tensor wbd) {
+  c10::cuda::CUDAGuard g(w.device());
+  TORCH_CHECK(w.size(0) >= heads * feat && w.size(1) >= in_dim, "gat_in_prep: w too small");
+  TORCH_CHECK(wbd.size(0) >= heads * feat && wbd.size(1) >= heads * in_dim, "gat_in_prep: wbd too small");
+  TORCH_CHECK(wl.numel() >= heads * in_dim && wr.numel() >= heads * in_dim, "gat_in_prep: wl / wr too small");
+  d::launch_gat_in_prep(reinterpret_cast<const __nv_bfloat16*>(ptr2d<at::BFloat16>(w, at::kBFloat16, "w")), w.stride(0),
+                        attn_l.data_ptr<float>(), attn_r.data_ptr<float>(), static_cast<int>(heads),
+                        static_cast<int>(feat), static_cast<int>(in_dim), static_cast<int>(wbd.size(0)),
+                        ptr<float>(wl, at::kFloat, "wl"), ptr<float>(wr, at::kFloat, "wr"),
+                        reinterpret_cast<__nv_bfloat16*>(ptr2d<at::BFloat16>(wbd, at::kBFloat16, "wbd")), wbd.stride(0),
+                        stream());
+}
+
+void gat_in_dw(Tensor T, Tensor xl, Tensor xr, Tensor attn_l, Tensor attn_r, Tensor w32, int64_t heads, int64_t feat,
+               int64_t in_dim, Tensor dw, OptT dattn_l, OptT dattn_r) {
+  c10::cuda::CUDAGuard g(T.device());
+  TORCH_CHECK(T.size(0) >= heads * feat && T.size(1) >= heads * in_dim, "gat_in_dw: T too small");
+  TORCH_CHECK(dw.size(0) >= heads * feat && dw.size(1) >= in_dim && w32.size(1) >= in_dim, "gat_in_dw: dw / w too small");
+  d::launch_gat_in_dw(ptr2d<float>(T, at::kFloat, "T"), T.stride(0), ptr<float>(xl, at::kFloat, "xl"),
+                      ptr<float>(xr, at::kFloat, "xr"), attn_l.data_ptr<float>(), attn_r.data_ptr<float>(),
+                      ptr2d<float>(w32, at::kFloat, "w32"), w32.stride(0), static_cast<int>(heads), static_cast<int>(feat),
+                      static_cast<int>(in_dim), ptr2d<float>(dw, at::kFloat, "dw"), dw.stride(0),
+                      dattn_l.has_value() ? dattn_l->data_ptr<float>() : nullptr,
+                      dattn_r.has_value() ? dattn_r->data_ptr<float>() : nullptr, stream());
+}
+
+void col_sum_bf16(Tensor x, OptT n_dev, int64_t cols, Tensor out) {
+  c10::cuda::CUDAGuard g(x.device());
+  TORCH_CHECK(x.size(1) >= cols && out.numel() >= cols, "col_sum_bf16: sizes");
+  d::launch_col_sum_bf16(reinterpret_cast<const __nv_bfloat16*>(ptr2d<at::BFloat16>(x, at::kBFloat16, "x")), x.stride(0),
+                         optr<int32_t>(n_dev, at::kInt, "n_dev"), static_cast<int>(x.size(0)), static_cast<int>(cols),
+                         ptr<float>(out, at::kFloat, "out"), stream());
 }
 
 void gat_dw_combine(Tensor T, Tensor xl, Tensor xr, Tensor attn_l, Tensor attn_r, int64_t heads, int64_t feat,
@@ -1014,6 +1099,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gat_bwd", &gat_bwd);
   m.def("gat_bwd_input", &gat_bwd_input);
   m.def("gat_dw_combine", &gat_dw_combine);
+  m.def("gat_in_scores", &gat_in_scores);
+  m.def("gat_in_fwd", &gat_in_fwd);
+  m.def("gat_in_bwd", &gat_in_bwd);
+  m.def("gat_in_prep", &gat_in_prep);
+  m.def("gat_in_dw", &gat_in_dw);
+  m.def("col_sum_bf16", &col_sum_bf16);
   m.def("aggregate_bwd", &aggregate_bwd);
   m.def("src_norm", &src_norm);
   m.def("act_bwd", &act_bwd);

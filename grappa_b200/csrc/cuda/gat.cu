@@ -67,6 +67,8 @@ __device__ __forceinline__ void red_add_v4f(float* p, float a, float b, float c,
   asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d));
 }
 __device__ __forceinline__ float leaky(float x, float s) { return x > 0.f ? x : x * s; }
+// column of z that virtual column c reads (a.zmod > 0: one row shared by every head)
+__device__ __forceinline__ int zcol(const GatArgs& a, int c) { return a.zmod > 0 ? c % a.zmod : c; }
 
 // Column sums of per-lane partials (lane owns columns (lane + 32 q) * 8 + j, the
 // same in every warp) over the block's warps in shared memory, then one atomic per
@@ -118,7 +120,7 @@ __global__ void __launch_bounds__(kThreads) gat_scores_kernel(GatArgs a) {
         float sl = 0.f, sr = 0.f;
         if (c0 < HF) {
           float f[8], al[8], ar[8];
-          bf16x8_to_f32(*reinterpret_cast<const uint4*>(a.z + static_cast<int64_t>(r) * a.ldz + c0), f);
+          bf16x8_to_f32(*reinterpret_cast<const uint4*>(a.z + static_cast<int64_t>(r) * a.ldz + zcol(a, c0)), f);
           *reinterpret_cast<float4*>(al) = __ldg(reinterpret_cast<const float4*>(a.attn_l + c0));
           *reinterpret_cast<float4*>(al + 4) = __ldg(reinterpret_cast<const float4*>(a.attn_l + c0 + 4));
           *reinterpret_cast<float4*>(ar) = __ldg(reinterpret_cast<const float4*>(a.attn_r + c0));
@@ -152,7 +154,7 @@ __global__ void __launch_bounds__(kThreads) gat_scores_kernel(GatArgs a) {
       const int c0 = (lane + 32 * q) * 8;
       if (c0 >= HF) continue;
       float f[8];
-      bf16x8_to_f32(*reinterpret_cast<const uint4*>(a.z + static_cast<int64_t>(r) * a.ldz + c0), f);
+      bf16x8_to_f32(*reinterpret_cast<const uint4*>(a.z + static_cast<int64_t>(r) * a.ldz + zcol(a, c0)), f);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int c = c0 + j;
@@ -305,7 +307,7 @@ __global__ void __launch_bounds__(kThreads) gat_fwd_kernel(GatArgs a) {
             wt0[t][q] = ok ? s_w[wib][k + t][h0[q]] : 0.f;
             wt1[t][q] = ok ? s_w[wib][k + t][h1[q]] : 0.f;
             zv[t][q] = make_uint4(0, 0, 0, 0);
-            if (ok && c0 < HF) zv[t][q] = *reinterpret_cast<const uint4*>(a.z + static_cast<int64_t>(u) * a.ldz + c0);
+            if (ok && c0 < HF) zv[t][q] = *reinterpret_cast<const uint4*>(a.z + static_cast<int64_t>(u) * a.ldz + zcol(a, c0));
           }
         }
 #pragma unroll
@@ -341,7 +343,7 @@ __global__ void __launch_bounds__(kThreads) gat_fwd_kernel(GatArgs a) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const int c = c0 + j;
-          float x = c < HF ? acc[q][j] + a.bias[c] : 0.f;
+          float x = c < HF ? acc[q][j] + (a.bias ? a.bias[c] : 0.f) : 0.f;
           if (a.act == 1) x = fmaxf(x, 0.f);
           o[j] = x;
         }
@@ -362,7 +364,7 @@ __global__ void __launch_bounds__(kThreads) gat_fwd_kernel(GatArgs a) {
         const int c0 = (lane + 32 * q) * 8;
 #pragma unroll
         for (int j = 0; j < 8; ++j)
-          if (c0 + j < HF) row[c0 + j] = acc[q][j] + a.bias[c0 + j];
+          if (c0 + j < HF) row[c0 + j] = acc[q][j] + (a.bias ? a.bias[c0 + j] : 0.f);
       }
       __syncwarp();
       const float inv_h = 1.f / static_cast<float>(H);
@@ -545,7 +547,8 @@ __global__ void __launch_bounds__(kThreads, bwd_min_blocks<CPL, CPLY>()) gat_bwd
           for (int q = 0; q < CPL; ++q) {
             const int c0 = (lane + 32 * q) * 8;
             zv[t][q] = make_uint4(0, 0, 0, 0);
-            if (ok && c0 < HF) zv[t][q] = *reinterpret_cast<const uint4*>(a.z + static_cast<int64_t>(uu[t]) * a.ldz + c0);
+            if (ok && c0 < HF)
+              zv[t][q] = *reinterpret_cast<const uint4*>(a.z + static_cast<int64_t>(uu[t]) * a.ldz + zcol(a, c0));
           }
         }
         uint4 xv[CPLY > 0 ? EU : 1][NY];
@@ -638,7 +641,7 @@ __global__ void __launch_bounds__(kThreads, bwd_min_blocks<CPL, CPLY>()) gat_bwd
           atomicAdd(a.del + static_cast<int64_t>(u) * H + lane, dx);
           der_acc += dx;
         }
-        if constexpr (CPLY == 0) {
+        if (CPLY == 0 && a.dz) {
 #pragma unroll
           for (int q = 0; q < CPL; ++q) {
             const int c0 = (lane + 32 * q) * 8;
@@ -734,7 +737,7 @@ __global__ void __launch_bounds__(kThreads, 1) gat_bwd_node_kernel(GatArgs a) {
         const int c0 = (lane + 32 * q) * 8;
         zv[i][q] = make_uint4(0, 0, 0, 0);
         if (u < n_src && c0 < HF)
-          zv[i][q] = *reinterpret_cast<const uint4*>(a.z + static_cast<int64_t>(u) * a.ldz + c0);
+          zv[i][q] = *reinterpret_cast<const uint4*>(a.z + static_cast<int64_t>(u) * a.ldz + zcol(a, c0));
       }
     }
     float4 dv[DZ ? R : 1][CPL][2];
@@ -747,7 +750,7 @@ __global__ void __launch_bounds__(kThreads, 1) gat_bwd_node_kernel(GatArgs a) {
           const int c0 = (lane + 32 * q) * 8;
           const float* d = a.dz + static_cast<int64_t>(u0 + i) * a.lddz + c0;
           dv[i][q][0] = dv[i][q][1] = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (u0 + i < n_src && c0 < HF) {
+          if (a.dz && u0 + i < n_src && c0 < HF) {
             if (c0 + 8 <= HF) {
               dv[i][q][0] = *reinterpret_cast<const float4*>(d);
               dv[i][q][1] = *reinterpret_cast<const float4*>(d + 4);
@@ -786,7 +789,7 @@ __global__ void __launch_bounds__(kThreads, 1) gat_bwd_node_kernel(GatArgs a) {
           drb = __shfl_sync(0xffffffffu, dr[i], hb);
         }
         if (u >= rows_end) continue;
-        if (DZ && c0 >= a.lddzb) continue;
+        if (DZ && a.dz_bf16 && c0 >= a.lddzb) continue;
         float o[8];
         if (u < n_src && c0 < HF) {
           float zf[8];
@@ -809,7 +812,7 @@ __global__ void __launch_bounds__(kThreads, 1) gat_bwd_node_kernel(GatArgs a) {
                         : 0.f;
             }
           }
-          if constexpr (DZ) {
+          if (DZ && a.dz) {
             float* d = a.dz + static_cast<int64_t>(u) * a.lddz + c0;
             if (c0 + 8 <= HF) {
               *reinterpret_cast<float4*>(d) = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -822,7 +825,7 @@ __global__ void __launch_bounds__(kThreads, 1) gat_bwd_node_kernel(GatArgs a) {
 #pragma unroll
           for (int j = 0; j < 8; ++j) o[j] = 0.f;
         }
-        if constexpr (DZ) *reinterpret_cast<uint4*>(a.dz_bf16 + static_cast<int64_t>(u) * a.lddzb + c0) = f32_to_bf16x8(o);
+        if (DZ && a.dz_bf16) *reinterpret_cast<uint4*>(a.dz_bf16 + static_cast<int64_t>(u) * a.lddzb + c0) = f32_to_bf16x8(o);
       }
       if constexpr (!DZ) {
 #pragma unroll
@@ -862,10 +865,79 @@ __global__ void gat_dw_combine_kernel(const float* T, int64_t ldt, const float* 
   }
 }
 
+// wl/wr (fp32 [H * IN]) and the block-diagonal Wbd (bf16 [rows, H * IN]) of the input
+// layer's projection-after-aggregation form (see launch_gat_in_prep)
+__global__ void gat_in_prep_kernel(const __nv_bfloat16* w, int64_t ldw, const float* attn_l, const float* attn_r,
+                                   int H, int F, int IN, int rows, float* wl, float* wr, __nv_bfloat16* wbd,
+                                   int64_t ldwbd) {
+  const int HIN = H * IN;
+  const int64_t total = static_cast<int64_t>(rows) * HIN;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total + 2 * HIN;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    if (i < total) {
+      const int r = static_cast<int>(i / HIN), c = static_cast<int>(i % HIN);
+      const int h = c / IN, k = c % IN;
+      const bool on = r < H * F && r / F == h;
+      wbd[static_cast<int64_t>(r) * ldwbd + c] = on ? w[static_cast<int64_t>(r) * ldw + k] : __float2bfloat16_rn(0.f);
+    } else {
+      const int j = static_cast<int>(i - total);  // [0, 2 HIN)
+      const bool left = j < HIN;
+      const int c = left ? j : j - HIN;
+      const int h = c / IN, k = c % IN;
+      const float* av = left ? attn_l : attn_r;
+      float t = 0.f;
+      for (int f = 0; f < F; ++f)
+        t += __bfloat162float(w[static_cast<int64_t>(h * F + f) * ldw + k]) * av[h * F + f];
+      (left ? wl : wr)[c] = t;
+    }
+  }
+}
+
+// dW[r, k] += T[r, h*IN + k] + a_l[r] xl[h, k] + a_r[r] xr[h, k] for r < H*F (h = r / F);
+// dattn_l[r] += W[r, :] . xl[h, :], dattn_r[r] += W[r, :] . xr[h, :]
+__global__ void gat_in_dw_kernel(const float* T, int64_t ldt, const float* xl, const float* xr, const float* attn_l,
+                                 const float* attn_r, const float* w, int64_t ldw_in, int H, int F, int IN, float* dw,
+                                 int64_t ldw, float* dattn_l, float* dattn_r) {
+  const int HF = H * F;
+  const int total = HF * IN;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total + HF; i += gridDim.x * blockDim.x) {
+    if (i < total) {
+      const int r = i / IN, k = i % IN, h = r / F;
+      dw[static_cast<int64_t>(r) * ldw + k] +=
+          T[static_cast<int64_t>(r) * ldt + h * IN + k] + attn_l[r] * xl[h * IN + k] + attn_r[r] * xr[h * IN + k];
+    } else {
+      const int r = i - total, h = r / F;
+      float tl = 0.f, tr = 0.f;
+      for (int k = 0; k < IN; ++k) {
+        const float wv = w[static_cast<int64_t>(r) * ldw_in + k];
+        tl = fmaf(wv, xl[h * IN + k], tl);
+        tr = fmaf(wv, xr[h * IN + k], tr);
+      }
+      if (dattn_l) dattn_l[r] += tl;
+      if (dattn_r) dattn_r[r] += tr;
+    }
+  }
+}
+
+// out[c] += sum over live rows of x[r, c]: one thread per column, rows split over blocks
+__global__ void col_sum_bf16_kernel(const __nv_bfloat16* x, int64_t ldx, const int32_t* n_ptr, int cap_rows, int cols,
+                                    float* out) {
+  const int n = n_ptr ? min(*n_ptr, cap_rows) : cap_rows;
+  const int rows_per = (n + gridDim.y - 1) / gridDim.y;
+  const int r0 = blockIdx.y * rows_per, r1 = min(n, r0 + rows_per);
+  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < cols; c += gridDim.x * blockDim.x) {
+    float t = 0.f;
+    for (int r = r0; r < r1; ++r) t += __bfloat162float(x[static_cast<int64_t>(r) * ldx + c]);
+    if (t != 0.f) atomicAdd(out + c, t);
+  }
+}
+
 int cpl_for(int hf) { return (hf + 255) / 256; }
 
 void check(const GatArgs& a) {
   if (a.heads <= 0 || a.heads > kMaxHeads) throw std::invalid_argument("gat: 1..8 heads");
+  if (a.zmod > 0 && (a.zmod != a.feat || a.zmod % 8 != 0))
+    throw std::invalid_argument("gat: shared-row mode needs feat == zmod, a multiple of 8");
   const int hf = a.heads * a.feat;
   if (hf > 1024) throw std::invalid_argument("gat: heads * feat <= 1024");
   if (a.ldz % 8 != 0) throw std::invalid_argument("gat: z stride % 8");
@@ -946,6 +1018,33 @@ void launch_gat_bwd_input(const GatArgs& a, cudaStream_t stream) {
   if (cply <= 1) gat_bwd_cpl<1>(a, stream);
   else if (cply <= 2) gat_bwd_cpl<2>(a, stream);
   else gat_bwd_cpl<4>(a, stream);
+}
+
+void launch_gat_in_prep(const __nv_bfloat16* w, int64_t ldw, const float* attn_l, const float* attn_r, int heads,
+                        int feat, int in_dim, int rows, float* wl, float* wr, __nv_bfloat16* wbd, int64_t ldwbd,
+                        cudaStream_t stream) {
+  const int64_t total = static_cast<int64_t>(rows) * heads * in_dim + 2 * heads * in_dim;
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ceil_div(total, 256), sms() * 4)));
+  gat_in_prep_kernel<<<grid, 256, 0, stream>>>(w, ldw, attn_l, attn_r, heads, feat, in_dim, rows, wl, wr, wbd, ldwbd);
+  GB_LAUNCH_CHECK();
+}
+
+void launch_gat_in_dw(const float* T, int64_t ldt, const float* xl, const float* xr, const float* attn_l,
+                      const float* attn_r, const float* w, int64_t ldw_in, int heads, int feat, int in_dim, float* dw,
+                      int64_t ldw, float* dattn_l, float* dattn_r, cudaStream_t stream) {
+  const int total = heads * feat * in_dim + heads * feat;
+  const int grid = std::max(1, std::min((total + 255) / 256, sms() * 4));
+  gat_in_dw_kernel<<<grid, 256, 0, stream>>>(T, ldt, xl, xr, attn_l, attn_r, w, ldw_in, heads, feat, in_dim, dw, ldw,
+                                             dattn_l, dattn_r);
+  GB_LAUNCH_CHECK();
+}
+
+void launch_col_sum_bf16(const __nv_bfloat16* x, int64_t ldx, const int32_t* n_ptr, int cap_rows, int cols, float* out,
+                         cudaStream_t stream) {
+  const dim3 grid(static_cast<unsigned>(std::max(1, (cols + 255) / 256)),
+                  static_cast<unsigned>(std::max(1, std::min(sms() * 2, (cap_rows + 255) / 256))));
+  col_sum_bf16_kernel<<<grid, 256, 0, stream>>>(x, ldx, n_ptr, cap_rows, cols, out);
+  GB_LAUNCH_CHECK();
 }
 
 void launch_gat_dw_combine(const float* T, int64_t ldt, const float* xl, const float* xr, const float* attn_l,

@@ -448,6 +448,10 @@ struct GatArgs {
   int64_t ldy = 0;
   float* xl = nullptr;                  // [H * in_dim] (zero before)
   float* xr = nullptr;                  // [H * in_dim] (zero before)
+  // > 0: z is a row of zmod columns shared by every head (column c of the H * F
+  // "virtual" row reads z[c % zmod], F = zmod): the GAT input layer then runs on its
+  // input rows x, with the projection applied after the aggregation (gat.cu)
+  int32_t zmod = 0;
 };
 void launch_gat_scores(const GatArgs& a, cudaStream_t stream);
 void launch_gat_fwd(const GatArgs& a, cudaStream_t stream);
@@ -456,6 +460,21 @@ void launch_gat_bwd_input(const GatArgs& a, cudaStream_t stream);
 void launch_gat_dw_combine(const float* T, int64_t ldt, const float* xl, const float* xr, const float* attn_l,
                            const float* attn_r, int heads, int feat, int in_dim, float* dw, int64_t ldw,
                            cudaStream_t stream);
+// Input layer with the projection after the aggregation:
+//   wl[h, k] = sum_f W[hF+f, k] a_l[hF+f],  wr likewise (fp32 [H * in_dim] each), and the
+//   block-diagonal weight Wbd[hF+f, h*in_dim + k] = W[hF+f, k] (bf16 [rows, H * in_dim]),
+// so that el = x . wl, er = x . wr and out = y Wbd^T with y_v[h] = sum_u a_uvh x_u.
+void launch_gat_in_prep(const __nv_bfloat16* w, int64_t ldw, const float* attn_l, const float* attn_r, int heads,
+                        int feat, int in_dim, int rows, float* wl, float* wr, __nv_bfloat16* wbd, int64_t ldwbd,
+                        cudaStream_t stream);
+// Its weight and attention gradients from T = dout^T y, xl, xr (as launch_gat_dw_combine)
+// plus dattn_l[r] += W[r, :] . xl[h(r), :], dattn_r[r] += W[r, :] . xr[h(r), :].
+void launch_gat_in_dw(const float* T, int64_t ldt, const float* xl, const float* xr, const float* attn_l,
+                      const float* attn_r, const float* w, int64_t ldw_in, int heads, int feat, int in_dim, float* dw,
+                      int64_t ldw, float* dattn_l, float* dattn_r, cudaStream_t stream);
+// dbias[c] += sum over the live rows of x[r, c] (bf16 rows)
+void launch_col_sum_bf16(const __nv_bfloat16* x, int64_t ldx, const int32_t* n_ptr, int cap_rows, int cols,
+                         float* out, cudaStream_t stream);
 
 // counters = [seed, epoch, step_in_epoch, global_step, gen, adam_t]: advance the step.
 // With ring_slot (a device int64 holding the address of a float ring, 0 for none) the

@@ -38,9 +38,12 @@ from grappa_b200.sampler_gpu import C_EPOCH, C_STEP, GpuNeighborSampler, new_cou
 
 GEMM_STORE_BF16, GEMM_STORE_F32, GEMM_ATOMIC_F32, GEMM_CROSS_ENTROPY = 0, 1, 2, 3
 AGG_MEAN, AGG_SUM, AGG_GCN, AGG_WEIGHTED = 0, 1, 2, 3
-# GAT input layer: dW from attention-weighted input rows instead of a per-source dz
-# (GRAPPA_GAT_INPUT_BWD=0 selects the dz path, for comparisons)
-GAT_INPUT_LAYER_BWD = os.environ.get("GRAPPA_GAT_INPUT_BWD", "1") != "0"
+# GAT input layer.  "x" (default): attention on the input rows, projection after the
+# aggregation (el = x.wl, y_v[h] = sum a_uv x_u, out = y Wbd^T: no per-source z = x W^T
+# and no per-source dz); "bwd": z = x W^T forward, dW from attention-weighted input rows
+# in the backward; "0": the plain z / dz path (for comparisons)
+GAT_INPUT_MODE = os.environ.get("GRAPPA_GAT_INPUT", os.environ.get("GRAPPA_GAT_INPUT_BWD", "x"))
+GAT_INPUT_LAYER_BWD = GAT_INPUT_MODE != "0"
 # GraphSAGE backward gathered by source over the block transpose (1) or scattered with
 # fp32 reductions plus a separate activation pass (0, the default: the transposes add
 # two kernels per hop to the sampling stream, which measured slower overall)
@@ -67,6 +70,7 @@ KERNELS_PER_CALL = {
     "shuffle_keys": 1, "sample_prologue": 1, "cross_entropy": 1, "batchnorm_fwd": 2, "batchnorm_bwd": 2, "l2norm_fwd": 1,
     "l2norm_bwd": 1, "dropout_rows": 1, "dropout_grad": 1, "f32_to_bf16_rows": 1, "add_bf16_rows": 1,
     "gat_scores": 1, "gat_fwd": 1, "gat_bwd": 2, "gat_bwd_input": 2, "gat_dw_combine": 1, "sampler_counters": 1,
+    "gat_in_scores": 1, "gat_in_fwd": 1, "gat_in_bwd": 2, "gat_in_prep": 1, "gat_in_dw": 1, "col_sum_bf16": 1,
     "block_transpose": 2, "aggregate_bwd_gather": 1,
 }
 
@@ -1023,17 +1027,29 @@ class GatEngine(BlockEngine):
             last = l == self.L - 1
             A = self._seg(layer.seg_a)
             gA = self._seg(layer.seg_a, self.grad)
-            # input layer: dW from attention-weighted input rows, no dz (gat.cu)
-            in_fast = GAT_INPUT_LAYER_BWD and l == 0 and not last and H * ip <= 1024
+            # input layer without a per-source dz (gat.cu): attention on x with the
+            # projection after the aggregation ("x"), or dW from attention-weighted
+            # input rows ("bwd")
+            in_ok = GAT_INPUT_LAYER_BWD and l == 0 and not last and H * ip <= 1024
+            in_x = in_ok and GAT_INPUT_MODE == "x"
+            in_fast = in_ok and not in_x
             s = dict(h=h, H=H, F=F, HF=HF, ip=ip, hfp=hfp, rows=rows, srows=srows, last=last, in_fast=in_fast,
-                     W=self._seg(layer.seg_w, self.wbf), gW=self._seg(layer.seg_w, self.grad),
-                     al=A[0], ar=A[1], gal=gA[0], gar=gA[1],
+                     in_x=in_x, W=self._seg(layer.seg_w, self.wbf), W32=self._seg(layer.seg_w),
+                     gW=self._seg(layer.seg_w, self.grad), al=A[0], ar=A[1], gal=gA[0], gar=gA[1],
                      bias=self._seg(layer.seg_b)[0], gb=self._seg(layer.seg_b, self.grad)[0],
-                     Z=torch.zeros((srows, hfp), **z), el=torch.zeros(srows * H, **f32),
+                     Z=None if in_x else torch.zeros((srows, hfp), **z), el=torch.zeros(srows * H, **f32),
                      er=torch.zeros(rows * H, **f32), smax=torch.zeros(rows * H, **f32),
                      ssum=torch.zeros(rows * H, **f32), escr=torch.zeros(ecap * H, **f32),
                      del_=torch.zeros(srows * H, **f32), der=torch.zeros(rows * H, **f32))
-            if in_fast:
+            if in_x:
+                hin = H * ip
+                s["Yin"] = torch.zeros((rows, hin), **z)   # y_v[h] = sum_u a_uvh x_u
+                s["G"] = torch.zeros((rows, hin), **z)     # dL/dy = dout Wbd
+                s["Wbd"] = torch.zeros((hfp, hin), **z)    # block-diagonal W (row hF+f: W[hF+f] at columns h*ip)
+                s["wlr"] = torch.zeros(2 * hin, **f32)     # wl[h] = sum_f a_l[h,f] W[hF+f], wr
+                s["T"] = torch.zeros((hfp, hin), **f32)
+                s["xlr"] = torch.zeros(2 * hin, **f32)
+            elif in_fast:
                 s["Yin"] = torch.zeros((rows, H * ip), **z)
                 s["T"] = torch.zeros((hfp, H * ip), **f32)
                 s["xlr"] = torch.zeros(2 * H * ip, **f32)
@@ -1066,12 +1082,15 @@ class GatEngine(BlockEngine):
                 A = self._gathered_input(0, s) if "Xg" in s else self._working.feat
             else:
                 A = self.lay[l - 1]["H_out"]
+            p = self.p if (training and not s["last"]) else 0.0
+            if s["in_x"]:
+                self._input_layer_fwd(s, h, A, p, l)
+                continue
             self._gemm(A, False, s["W"], False, s["srows"], sm.n_src(h), s["HF"], s["ip"], None, 1, s["Z"],
                        GEMM_STORE_BF16)
             args = (sm.indptr[h], sm.indices[h], self._n_dst(h), s["rows"], sm.n_src(h), s["srows"], s["H"], s["F"],
                     s["Z"], s["al"], s["ar"], s["el"], s["er"], s["smax"], s["ssum"], 0.2)
             cu.gat_scores(*args)
-            p = self.p if (training and not s["last"]) else 0.0
             cu.gat_fwd(*args, s["bias"], s["last"], 0 if s["last"] else 1, p, self.counters if p > 0 else None,
                        l, s["H_out"])
             if s["last"]:
@@ -1086,6 +1105,9 @@ class GatEngine(BlockEngine):
         # fused into its epilogue)
         dout = s["dl"] if s["last"] else s["dY"]
         A = self._A(l, s)
+        if s["in_x"]:
+            self._input_layer_bwd_x(s, h, dout, A)
+            return
         if s["in_fast"]:
             self._input_layer_bwd(s, h, dout, A)
             return
@@ -1099,6 +1121,56 @@ class GatEngine(BlockEngine):
             self._gemm(s["dzb"], False, s["W"], True, s["srows"], sm.n_src(h), s["ip"], s["HF"], None, 1,
                        prev["dY"], GEMM_STORE_BF16, act_mask=prev["H_out"], mask_scale=scale, zero_tail_rows=64)
 
+
+    def _input_layer_fwd(self, s, h, X, p, l):
+        """Input layer with the projection after the aggregation: the logits are
+        el_u = x_u . wl[h] (wl[h] = sum_f a_l[h,f] W[hF+f]), the softmax-weighted sum runs
+        over the input rows (y_v[h] = sum_u a_uvh x_u, [rows, H*in]) and one GEMM against
+        the block-diagonal W (bias, ReLU and dropout in its epilogue) gives the layer's
+        output.  Equal to W x then attention (the weights are linear in x); it reads in
+        columns per edge instead of H*F and needs no projection of every source row."""
+        cu, sm = self.cu, self.sm
+        H, ip = s["H"], s["ip"]
+        hin = H * ip
+        wl, wr = s["wlr"][:hin], s["wlr"][hin:]
+        cu.gat_in_prep(s["W"], s["al"], s["ar"], H, s["F"], ip, wl, wr, s["Wbd"])
+        args = (sm.indptr[h], sm.indices[h], self._n_dst(h), s["rows"], sm.n_src(h), s["srows"], H, ip, X, wl, wr,
+                s["el"], s["er"], s["smax"], s["ssum"], 0.2)
+        cu.gat_in_scores(*args)
+        cu.gat_in_fwd(*args, s["Yin"])
+        self._gemm(s["Yin"], False, s["Wbd"], False, s["rows"], self._n_dst(h), s["HF"], hin, None, 1, s["H_out"],
+                   GEMM_STORE_BF16, bias=s["bias"], act=1, p=p, salt=l, zero_tail_rows=64)
+
+    def _input_layer_bwd_x(self, s, h, dout, X):
+        """Backward of ``_input_layer_fwd``: G = dout Wbd (dL/dy), the attention backward
+        over the input rows gives xl[h] = sum_u del[u,h] x_u and xr[h]; then
+        dW[hF+f] = (dout^T y)[hF+f, h-block] + a_l[h,f] xl[h] + a_r[h,f] xr[h],
+        da_l[h,f] = W[hF+f] . xl[h] (same for a_r) and db = column sums of dout.  The
+        dout^T y GEMM and the bias sums run on the auxiliary stream."""
+        cu, sm = self.cu, self.sm
+        H, ip = s["H"], s["ip"]
+        hin = H * ip
+        wl, wr = s["wlr"][:hin], s["wlr"][hin:]
+        xl, xr = s["xlr"][:hin], s["xlr"][hin:]
+        main = torch.cuda.current_stream(self.device)
+        aux = self._aux_stream()
+        aux.wait_stream(main)
+        n_tiles = math.ceil(s["hfp"] / 128) * math.ceil(hin / 256)
+        with torch.cuda.stream(aux):
+            cu.zero_(s["T"])
+            self._gemm(dout, True, s["Yin"], True, s["hfp"], None, hin, s["rows"], self._n_dst(h),
+                       split_k(s["rows"], n_tiles), s["T"], GEMM_ATOMIC_F32, bn=256)
+            cu.col_sum_bf16(dout, self._n_dst(h), s["HF"], s["gb"])
+        self._gemm(dout, False, s["Wbd"], True, s["rows"], self._n_dst(h), hin, s["HF"], None, 1, s["G"],
+                   GEMM_STORE_BF16)
+        cu.zero_(s["xlr"])
+        cu.gat_in_bwd(sm.indptr[h], sm.indices[h], self._n_dst(h), s["rows"], sm.n_src(h), s["srows"], H, ip, X, wl,
+                      wr, s["el"], s["er"], s["smax"], s["ssum"], 0.2, s["G"], s["escr"], s["del_"], s["der"], xl, xr,
+                      self.err)
+        aux.wait_stream(main)
+        with torch.cuda.stream(aux):
+            cu.gat_in_dw(s["T"], xl, xr, s["al"], s["ar"], s["W32"], H, s["F"], ip, s["gW"], s["gal"], s["gar"])
+        self._aux_used = True
 
     def _input_layer_bwd(self, s, h, dout, A):
         """dW of the input layer as dout^T y plus two rank-1 terms (y = attention-weighted

@@ -208,3 +208,71 @@ def test_gat_kernels(H, F_, mean_heads, max_deg):
     torch.testing.assert_close(dar, arr.grad, atol=5e-2, rtol=3e-2)
     assert torch.all(dz == 0) and torch.all(dl_ == 0)
     assert int(err) == 0
+
+
+@pytest.mark.parametrize("H,F_,ip,max_deg", [(4, 64, 104, 40), (2, 24, 40, 8), (3, 16, 16, 70)])
+def test_gat_input_layer_projection_after_aggregation(H, F_, ip, max_deg):
+    """Input layer with the attention on x and the projection after the aggregation
+    (gat_in_prep, gat_in_scores, gat_in_fwd, then y Wbd^T) against the loop oracle on
+    z = x W^T; its backward (gat_in_bwd on dL/dy = dout Wbd, gat_in_dw on dout^T y,
+    col_sum_bf16) against autograd through the oracle.  torch stands in for the GEMMs."""
+    torch.manual_seed(4)
+    n_dst, n_src = 70, 300
+    deg = torch.randint(0, max_deg + 1, (n_dst,))
+    indptr = torch.zeros(n_dst + 1, dtype=torch.int32)
+    indptr[1:] = torch.cumsum(deg, 0)
+    E = int(indptr[-1])
+    indices = torch.randint(0, n_src, (E,), dtype=torch.int32)
+    indptr, indices = indptr.to(DEV), indices.to(DEV)
+    HF, hin = H * F_, H * ip
+    f32 = dict(dtype=torch.float32, device=DEV)
+    x = bf(torch.randn(n_src, ip, device=DEV))
+    W = bf(torch.randn(HF, ip, device=DEV) * 0.1)
+    al = torch.randn(HF, device=DEV) * 0.3
+    ar = torch.randn(HF, device=DEV) * 0.3
+    wl, wr = torch.zeros(hin, **f32), torch.zeros(hin, **f32)
+    Wbd = torch.full((HF, hin), 7.0, dtype=torch.bfloat16, device=DEV)
+    cu().gat_in_prep(W, al, ar, H, F_, ip, wl, wr, Wbd)
+    Wh = W.float().view(H, F_, ip)
+    torch.testing.assert_close(wl, (al.view(H, F_, 1) * Wh).sum(1).flatten(), atol=1e-4, rtol=1e-4)
+    torch.testing.assert_close(wr, (ar.view(H, F_, 1) * Wh).sum(1).flatten(), atol=1e-4, rtol=1e-4)
+    assert torch.equal(Wbd.float(), torch.block_diag(*Wh))
+    el, er = torch.zeros(n_src * H, **f32), torch.zeros(n_dst * H, **f32)
+    smax, ssum = torch.zeros(n_dst * H, **f32), torch.zeros(n_dst * H, **f32)
+    nd = torch.tensor([n_dst], dtype=torch.int32, device=DEV)
+    ns = torch.tensor([n_src], dtype=torch.int32, device=DEV)
+    args = (indptr, indices, nd, n_dst, ns, n_src, H, ip, x, wl, wr, el, er, smax, ssum, 0.2)
+    cu().gat_in_scores(*args)
+    Y = torch.zeros(n_dst, hin, dtype=torch.bfloat16, device=DEV)
+    cu().gat_in_fwd(*args, Y)
+    xf = x.float()
+    Wr = W.float().clone().requires_grad_(True)
+    alr, arr = al.clone().requires_grad_(True), ar.clone().requires_grad_(True)
+    ref = _gat_ref(indptr, indices, n_dst, xf @ Wr.t(), alr, arr, torch.zeros(HF, **f32), H, F_, 0.2, False)
+    torch.testing.assert_close(Y.float() @ Wbd.float().t(), ref, atol=3e-2, rtol=3e-2)
+    # backward
+    g = bf(torch.randn(n_dst, HF, device=DEV))
+    G = (g.float() @ Wbd.float()).bfloat16()
+    escr = torch.zeros(max(E, 1) * H, **f32)
+    dl_, dr_ = torch.zeros(n_src * H, **f32), torch.zeros(n_dst * H, **f32)
+    xl, xr = torch.zeros(hin, **f32), torch.zeros(hin, **f32)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    cu().gat_in_bwd(*args, G, escr, dl_, dr_, xl, xr, err)
+    T = g.float().t() @ Y.float()
+    dW = torch.zeros(HF, ip, **f32)
+    dal, dar = torch.zeros(HF, **f32), torch.zeros(HF, **f32)
+    cu().gat_in_dw(T, xl, xr, al, ar, W.float(), H, F_, ip, dW, dal, dar)
+    db = torch.zeros(HF, **f32)
+    cu().col_sum_bf16(g, nd, HF, db)
+    torch.cuda.synchronize()
+    ref.backward(g.float())
+
+    def rel(a, b):
+        return float((a - b).norm() / b.norm().clamp(min=1e-12))
+
+    assert rel(dW, Wr.grad) < 2e-2, rel(dW, Wr.grad)
+    assert rel(dal, alr.grad) < 3e-2, rel(dal, alr.grad)
+    assert rel(dar, arr.grad) < 3e-2, rel(dar, arr.grad)
+    torch.testing.assert_close(db, g.float().sum(0), atol=1e-2, rtol=1e-3)
+    assert torch.all(dl_ == 0)
+    assert int(err) == 0
