@@ -137,31 +137,57 @@ class FullGraphBlocks:
     t10n_fullgraph_train.py:163-205): dst = src = rows [0, n), edges = in-edges among
     them.  Same interface as GpuNeighborSampler; ``sample`` does nothing."""
 
-    def __init__(self, indptr, indices, n_layers, device, labels, train_rows, cov=None):
+    def __init__(self, indptr, indices, n_layers, device, labels, train_rows, cov=None, cap_nodes=0, cap_edges=0):
         dev = torch.device(device)
+        self.device = dev
         self.L = int(n_layers)
-        n = int(indptr.numel() - 1)
-        self.n = n
-        self.B = n
+        n, E = int(indptr.numel() - 1), int(indices.numel())
+        # buffers sized for the largest working graph a repartition can produce, so that
+        # ``refill`` keeps every pointer (and the engine's captured step graph) valid
+        cap_n, cap_e = max(n, int(cap_nodes)), max(1, E, int(cap_edges))
+        self.B = cap_n
         i32 = dict(dtype=torch.int32, device=dev)
-        self.cnt = torch.tensor([n] + [int(indices.numel()), n, 0] * self.L, **i32)
-        self.seeds = torch.arange(n, **i32)
-        ip = indptr.to(dev, torch.int32).contiguous()
-        ix = indices.to(dev, torch.int32).contiguous()
+        self.cnt = torch.zeros(1 + 3 * self.L, **i32)
+        self.seeds = torch.arange(cap_n, **i32)
+        ip = torch.zeros(cap_n + 1, **i32)
+        ix = torch.zeros(cap_e, **i32)
         self.indptr = [ip] * self.L
         self.indices = [ix] * self.L
         self.src = [self.seeds] * self.L
-        self.cap_dst = [n] * self.L
-        self.cap_src = [n] * self.L
-        self.cap_e = [max(1, int(ix.numel()))] * self.L
+        self.cap_dst = [cap_n] * self.L
+        self.cap_src = [cap_n] * self.L
+        self.cap_e = [cap_e] * self.L
         self.w = [None] * self.L
-        self.labels = labels.to(dev, torch.int32).contiguous()
-        self.row_mask = train_rows.to(dev, torch.uint8).contiguous()
-        self.n_sel = torch.tensor([int(self.row_mask.sum())], **i32)
+        self.labels = torch.zeros(cap_n, **i32)
+        self.row_mask = torch.zeros(cap_n, dtype=torch.uint8, device=dev)
+        self.n_sel = torch.zeros(1, **i32)
         # [coverage sum, count] of the partition's training rows (weight 1 when not given)
-        self.cov = (torch.ones(2, dtype=torch.float32, device=dev) if cov is None
-                    else cov.to(dev, torch.float32).contiguous())
+        self.cov = torch.ones(2, dtype=torch.float32, device=dev)
         self.full_graph = True
+        self.refill(indptr, indices, labels, train_rows, cov)
+
+    def refill(self, indptr, indices, labels, train_rows, cov=None):
+        """Load another working graph into the same buffers (False when it does not fit):
+        rows [0, n) and the n + 1 row pointers, the edges, labels, training rows and
+        coverage; the live sizes go to the device counters the kernels read."""
+        n, E = int(indptr.numel() - 1), int(indices.numel())
+        if n > self.cap_dst[0] or E > self.cap_e[0]:
+            return False
+        self.n = n
+        ip, ix = self.indptr[0], self.indices[0]
+        ip[: n + 1].copy_(indptr)
+        ip[n + 1:].fill_(E)
+        ix[:E].copy_(indices)
+        self.labels[:n].copy_(labels)
+        self.row_mask.zero_()
+        self.row_mask[:n].copy_(train_rows)
+        self.n_sel.copy_(self.row_mask.sum().to(torch.int32).view(1))
+        if cov is None:
+            self.cov.fill_(1.0)
+        else:
+            self.cov.copy_(cov)
+        self.cnt.copy_(torch.tensor([n] + [E, n, 0] * self.L, dtype=torch.int32))
+        return True
 
     def n_seeds(self):
         return self.cnt[0:1]

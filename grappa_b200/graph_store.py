@@ -153,6 +153,7 @@ class PartitionStore:
         max_ext = max(s["ext"] for s in self._sizes)
         cap_halo = min(own.n_global, int(own.ext_src.numel()) + max_ext)
         self.cap_nodes = own.n_nodes + max_n + cap_halo
+        self.cap_own_nbr = own.n_nodes + max_n
         self.cap_edges = own.n_edges + max_e
         dev = self.device
         self._indptr_w = torch.zeros(self.cap_nodes + 1, dtype=torch.int64, device=dev)

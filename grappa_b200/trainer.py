@@ -219,11 +219,13 @@ def _exact_accuracy(trainer, masks):
     return trainer._exact.accuracy(masks)
 
 
-def full_graph_blocks(working, n_layers, own):
+def full_graph_blocks(working, n_layers, own, cap_nodes=0, cap_edges=0, into=None):
     """FullGraphBlocks of the working graph's own + neighbour rows: the in-edges whose
     source is one of those rows (halo sources dropped, as the reference's isolated
     full-graph partition holds only the two chunks, t10n/dataloader.py:492-502).
-    Labels and the training mask exist for the own rows only.
+    Labels and the training mask exist for the own rows only.  ``into``: a FullGraphBlocks
+    to refill in place when the graph fits (its pointers, and a step graph captured on
+    them, stay valid); ``cap_nodes`` / ``cap_edges`` size a new one.
 
     The coverage weight c_r of the partition is the mini-batch path's per-seed ratio
     (csrc/graph/sampling_h.h:97-116, t10n/dataloader.py:647-663) averaged over every
@@ -250,7 +252,11 @@ def full_graph_blocks(working, n_layers, own):
     train = torch.zeros(n, dtype=torch.uint8, device=dev)
     train[: working.n_own] = own.train_mask.to(torch.uint8)
     cov = coverage_of_rows(cnt[: working.n_own], own.gideg.to(dev), own.train_mask.to(dev))
-    return FullGraphBlocks(new_ip, ind[keep], n_layers, dev, labels, train, cov=cov)
+    ind = ind[keep]
+    if into is not None and into.refill(new_ip, ind, labels, train, cov):
+        return into
+    return FullGraphBlocks(new_ip, ind, n_layers, dev, labels, train, cov=cov, cap_nodes=cap_nodes,
+                           cap_edges=cap_edges)
 
 
 def coverage_of_rows(kept_deg, gideg, mask):
@@ -286,7 +292,9 @@ class FullGraphTrainer:
         if self.world > 1:
             self.nbr_idx = next_neighbor(self.nbr_idx, self.rank, self.world)
         w = self.store.repartition(self.nbr_idx)
-        blocks = full_graph_blocks(w, len(model.layers), own)
+        # capacity of the own + neighbour rows and their edges over every repartition
+        self._caps = (getattr(self.store, "cap_own_nbr", 0), getattr(self.store, "cap_edges", 0))
+        blocks = full_graph_blocks(w, len(model.layers), own, *self._caps)
         self.engine = make_engine(model, self.store.cap_nodes, [], 0, self.device, lr=lr, comm=comm, seed=seed,
                                   fused_allreduce=fused_allreduce, use_cuda_graph=use_cuda_graph, blocks=blocks,
                                   ar_mode=ar_mode)
@@ -300,10 +308,15 @@ class FullGraphTrainer:
         t0 = time.perf_counter()
         self.nbr_idx = next_neighbor(self.nbr_idx, self.rank, self.world)
         w = self.store.repartition(self.nbr_idx)
-        self.engine.set_blocks(full_graph_blocks(w, len(self.model.layers), self.own))
+        cur = self.engine.sm
+        blocks = full_graph_blocks(w, len(self.model.layers), self.own, *self._caps, into=cur)
+        if blocks is not cur:
+            self.engine.set_blocks(blocks)
+            self._warm = False
         self.engine.bind_working(w, self.own.label, self.own.gideg)
+        if self.engine._graph is None:
+            self._warm = False
         self._last_repart = epoch
-        self._warm = False
         self.repart_seconds.append(time.perf_counter() - t0)
 
     def warmup(self):

@@ -41,3 +41,34 @@ def test_full_graph_coverage_three_partitions():
     fb2 = full_graph_blocks(working_graph_host(parts2, 0, 1), 3, parts2[0])
     s2, n2 = fb2.cov.tolist()
     assert abs(s2 - n2) < 1e-3
+
+
+def test_full_graph_blocks_refill_in_place():
+    """A repartition refills the block source in place when the new working graph fits
+    its capacities: every buffer keeps its address (a captured step graph stays valid)
+    and the live part equals a freshly built block source; the device counters carry
+    the new sizes and the rows past them read as empty."""
+    W, seed = 3, 7
+    g = S.build(S.SPECS["tiny"], "cpu")
+    parts = [partition_from_global(g, W, r, "cpu", part_seed=seed) for r in range(W)]
+    cap_n = parts[0].n_nodes + max(p.n_nodes for p in parts)
+    cap_e = parts[0].n_edges + max(p.n_edges for p in parts)
+    fb = full_graph_blocks(working_graph_host(parts, 0, 1), 2, parts[0], cap_n, cap_e)
+    ptrs = [t.data_ptr() for t in (fb.indptr[0], fb.indices[0], fb.labels, fb.row_mask, fb.cov, fb.cnt)]
+    w2 = working_graph_host(parts, 0, 2)
+    out = full_graph_blocks(w2, 2, parts[0], cap_n, cap_e, into=fb)
+    assert out is fb
+    assert ptrs == [t.data_ptr() for t in (fb.indptr[0], fb.indices[0], fb.labels, fb.row_mask, fb.cov, fb.cnt)]
+    ref = full_graph_blocks(w2, 2, parts[0])
+    n, E = ref.n, int(ref.cnt[1])
+    assert fb.n == n and fb.cnt.tolist() == ref.cnt.tolist()
+    assert torch.equal(fb.indptr[0][: n + 1], ref.indptr[0][: n + 1])
+    assert torch.all(fb.indptr[0][n + 1:] == E)
+    assert torch.equal(fb.indices[0][:E], ref.indices[0][:E])
+    assert torch.equal(fb.labels[:n], ref.labels[:n]) and int(fb.row_mask[n:].sum()) == 0
+    assert torch.equal(fb.row_mask[:n], ref.row_mask[:n]) and int(fb.n_sel) == int(ref.n_sel)
+    assert torch.allclose(fb.cov, ref.cov)
+    # a graph larger than the capacities gets a new block source
+    small = full_graph_blocks(working_graph_host(parts, 0, 1), 2, parts[0])
+    assert full_graph_blocks(working_graph_host(parts, 0, 2), 2, parts[0], into=small) is not small or \
+        ref.n <= small.cap_dst[0]
