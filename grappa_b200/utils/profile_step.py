@@ -19,7 +19,8 @@ With ``--phases N`` the CUDA-event device time of each step phase (sample,
 forward, backward, update) averaged over N eager steps is printed; with
 ``--graphs N`` the device time of N replays of each captured graph: sampling
 alone, the step without and with the next step's sampling on its side stream (the
-overlap that the training loop uses).  Workloads: 3-layer models on the
+overlap that the training loop uses); with ``--kernel-times N`` the CUDA-event time of
+every kernel binding call, averaged over N eager steps.  Workloads: 3-layer models on the
 ogbn-products-shaped synthetic graph (``--config`` picks another spec), 1024 seeds
 per batch, one GPU.
 """
@@ -44,6 +45,8 @@ def main():
     ap.add_argument("--batch", type=int, default=1024)
     ap.add_argument("--phases", type=int, default=0, help="time the phases of this many eager steps")
     ap.add_argument("--graphs", type=int, default=0, help="time this many replays of each step graph")
+    ap.add_argument("--kernel-times", type=int, default=0,
+                    help="CUDA-event time of every kernel binding call over this many eager steps")
     a = ap.parse_args()
     name, hidden, fanouts = WORKLOADS[a.workload]
     dev = torch.device("cuda", 0)
@@ -68,10 +71,30 @@ def main():
     out = {"workload": a.workload, "launches_per_step": eng.launches_per_step, "block_counts": eng.sm.cnt.tolist()}
     if a.phases:
         out["phase_ms"] = eng.time_phases(seeds, counts, a.phases)
+    if a.kernel_times:
+        out["kernel_us"] = kernel_times(eng, seeds, counts, a.kernel_times)
     tr.close()
     if a.graphs:
         out["graph_ms"] = time_graphs(model, own, fanouts, a.batch, a.graphs)
     print(json.dumps(out))
+
+
+def kernel_times(eng, seeds, counts, n):
+    """Mean device time (us per step) of each kernel binding call of an eager step, keyed
+    by its order in the step ("12:gat_bwd"), from CUDA events on the stream that issued
+    it.  Calls on the side streams overlap others, so the times do not add up to the
+    step; the ranking shows where a step's device time goes."""
+    eng.cu.timer = []
+    per = {}
+    for s in range(n):
+        eng.cu.timer.clear()
+        eng.step(seeds[(s + 2) % seeds.shape[0]], counts[(s + 2) % counts.shape[0]])
+        torch.cuda.synchronize()
+        for i, (name, e0, e1) in enumerate(eng.cu.timer):
+            key = f"{i:02d}:{name}"
+            per[key] = per.get(key, 0.0) + e0.elapsed_time(e1) * 1000.0 / n
+    eng.cu.timer = None
+    return {k: round(v, 1) for k, v in sorted(per.items(), key=lambda kv: -kv[1])}
 
 
 def time_graphs(model, own, fanouts, batch, n):
