@@ -76,10 +76,20 @@ __global__ void pull_rows_kernel(PullRowsArgs a) {
   }
 }
 
+// four independent 16-byte loads in flight per thread (peer sources: the NVLink round
+// trip is hidden by the loads in flight, not by the grid size)
 __global__ void copy_kernel(uint4* dst, const uint4* src, int64_t n16) {
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n16;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
-    dst[i] = src[i];
+  constexpr int kU = 4;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n16; i += kU * stride) {
+    uint4 v[kU];
+#pragma unroll
+    for (int k = 0; k < kU; ++k)
+      if (i + k * stride < n16) v[k] = src[i + k * stride];
+#pragma unroll
+    for (int k = 0; k < kU; ++k)
+      if (i + k * stride < n16) dst[i + k * stride] = v[k];
+  }
 }
 
 // Each thread moves 8 independent 16-byte words per iteration (8 P2P loads in flight)
@@ -217,6 +227,34 @@ __global__ void __launch_bounds__(kMcThreads) mark_compact_kernel(uint8_t* mark,
   }
 }
 
+// out[e] = map[src[e]] for e < n: the source (peer memory) read as 16-byte words, two
+// in flight per thread, after a scalar head up to the first 16-byte boundary; the
+// translated values are stored as single words (local memory, any alignment)
+__device__ __forceinline__ void merge_segment(const int32_t* src, int64_t n, int32_t* out, const int32_t* map,
+                                              int64_t tid, int64_t stride) {
+  if (n <= 0) return;
+  const int64_t mis = static_cast<int64_t>((reinterpret_cast<uintptr_t>(src) >> 2) & 3);
+  const int64_t head = mis ? (4 - mis < n ? 4 - mis : n) : 0;
+  if (tid < head) out[tid] = map[src[tid]];
+  const int4* s4 = reinterpret_cast<const int4*>(src + head);
+  int32_t* o = out + head;
+  const int64_t n4 = (n - head) >> 2;
+  for (int64_t i = tid; i < n4; i += 2 * stride) {
+    const bool two = i + stride < n4;
+    const int4 x = s4[i];
+    int4 y = make_int4(0, 0, 0, 0);
+    if (two) y = s4[i + stride];
+    int32_t* p = o + 4 * i;
+    p[0] = map[x.x]; p[1] = map[x.y]; p[2] = map[x.z]; p[3] = map[x.w];
+    if (two) {
+      int32_t* q = o + 4 * (i + stride);
+      q[0] = map[y.x]; q[1] = map[y.y]; q[2] = map[y.z]; q[3] = map[y.w];
+    }
+  }
+  const int64_t t0 = head + 4 * n4;
+  if (tid < n - t0) out[t0 + tid] = map[src[t0 + tid]];
+}
+
 __global__ void csr_merge_kernel(CsrMergeArgs a) {
   const int64_t ea0 = a.indptr_a[0], ea = a.indptr_a[a.n_a] - ea0;
   const int64_t eb0 = a.n_b > 0 ? a.indptr_b[0] : 0;
@@ -231,10 +269,10 @@ __global__ void csr_merge_kernel(CsrMergeArgs a) {
     else o = ea + eb;
     a.indptr_out[v] = o < a.cap_edges ? o : a.cap_edges;
   }
-  for (int64_t e = tid; e < ea + eb && e < a.cap_edges; e += stride) {
-    const int32_t g = e < ea ? a.indices_a[ea0 + e] : a.indices_b[eb0 + (e - ea)];
-    a.indices_out[e] = a.map[g];
-  }
+  const int64_t na = ea < a.cap_edges ? ea : a.cap_edges;
+  const int64_t nb = ea + eb < a.cap_edges ? eb : a.cap_edges - na;
+  merge_segment(a.indices_a + ea0, na, a.indices_out, a.map, tid, stride);
+  merge_segment(a.indices_b + eb0, nb, a.indices_out + na, a.map, tid, stride);
 }
 
 int sm_count() {

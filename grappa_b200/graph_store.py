@@ -182,6 +182,20 @@ class PartitionStore:
         peer = self._peer
         ev = [torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
         ev[0].record()
+        # q's feature rows (the largest transfer, independent of the CSR and halo work)
+        # stream over NVLink on a side stream while the marks, the CSR merge and the halo
+        # pulls run here; the own rows are copied once (they never change)
+        fs = self.feat_stride
+        esz = own.feat.element_size()
+        main = torch.cuda.current_stream(self.device)
+        if getattr(self, "_side", None) is None:
+            self._side = torch.cuda.Stream(device=self.device)
+        self._side.wait_stream(main)
+        with torch.cuda.stream(self._side):
+            if not getattr(self, "_own_rows_in", False):
+                self._feat_w[:n_r].copy_(own.feat)
+                self._own_rows_in = True
+            cu.peer_copy(self._feat_w.data_ptr() + n_r * fs * esz, peer["feat"].ptrs[q], n_q * fs * esz)
         # 1. halo = (ext_r U ext_q) \ (V_r U V_q), found by marking a dense global-id array
         cu.mark_ids(peer["ext"].ptrs[r], None, sz[r]["ext"], self._mark)
         cu.mark_ids(peer["ext"].ptrs[q], None, sz[q]["ext"], self._mark)
@@ -191,14 +205,11 @@ class PartitionStore:
         # 2. working CSR: own in-edges, then q's in-edges pulled from q, sources translated
         cu.csr_merge(peer["indptr"].ptrs[r], peer["indices"].ptrs[r], n_r, peer["indptr"].ptrs[q],
                      peer["indices"].ptrs[q], n_q, self._map, self._indptr_w, self._indices_w, self.err)
-        # 3. features: own rows, q's rows (bulk copy over NVLink), halo rows from their owners
-        fs = self.feat_stride
-        esz = own.feat.element_size()
-        self._feat_w[:n_r].copy_(own.feat)
-        cu.peer_copy(self._feat_w.data_ptr() + n_r * fs * esz, peer["feat"].ptrs[q], n_q * fs * esz)
+        # 3. halo feature rows from their owners (q's rows are on the side stream)
         tables = [peer["feat"].ptrs[p] for p in range(self.world)]
         cu.pull_rows(tables, fs, esz, fs * esz, self._halo_ids, self._n_halo, 0, self._prefix_dev,
                      self._feat_w.data_ptr(), fs, n_r + n_q, self._halo_ids.numel(), self.err)
+        main.wait_stream(self._side)
         ev[1].record()
         # bytes this rank pulls over NVLink: q's external-source list and CSR, q's feature
         # rows and the halo rows (their count is on the device until the log is read)

@@ -452,3 +452,37 @@ def test_fused_allreduce_adam_single_rank(mode, dtype):
     assert torch.equal(wbf, ar.param.to(torch.bfloat16))
     ar.close()
 
+
+
+@pytest.mark.parametrize("a0,b0", [(0, 0), (3, 5), (1, 2)])
+def test_csr_merge_and_copy(a0, b0):
+    """csr_merge (two CSRs concatenated, sources translated through the map; 16-byte
+    source words after a scalar head, so edge offsets that are not multiples of four
+    are covered) and the unrolled copy against torch, on local memory."""
+    torch.manual_seed(5)
+    n_glob = 5000
+    da, db = torch.randint(0, 40, (300,)), torch.randint(0, 40, (211,))
+    ipa = torch.cat([torch.zeros(1, dtype=torch.int64), torch.cumsum(da, 0)]) + a0
+    ipb = torch.cat([torch.zeros(1, dtype=torch.int64), torch.cumsum(db, 0)]) + b0
+    ia = torch.randint(0, n_glob, (int(ipa[-1]) + 7,), dtype=torch.int32)
+    ib = torch.randint(0, n_glob, (int(ipb[-1]) + 7,), dtype=torch.int32)
+    mp = torch.randperm(n_glob).to(torch.int32)
+    ipa_d, ipb_d, ia_d, ib_d, mp_d = (t.to(DEV) for t in (ipa, ipb, ia, ib, mp))
+    ea, eb = int(ipa[-1] - a0), int(ipb[-1] - b0)
+    out_ip = torch.full((300 + 211 + 4,), -1, dtype=torch.int64, device=DEV)
+    out_ix = torch.full((ea + eb + 9,), -1, dtype=torch.int32, device=DEV)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    cu().csr_merge(ipa_d.data_ptr(), ia_d.data_ptr(), 300, ipb_d.data_ptr(), ib_d.data_ptr(), 211, mp_d, out_ip,
+                   out_ix, err)
+    torch.cuda.synchronize()
+    want_ip = torch.cat([ipa - a0, (ipb[1:] - b0) + ea, torch.full((3,), ea + eb, dtype=torch.int64)])
+    assert torch.equal(out_ip.cpu(), want_ip)
+    want_ix = mp[torch.cat([ia[a0:a0 + ea], ib[b0:b0 + eb]]).long()]
+    assert torch.equal(out_ix[:ea + eb].cpu(), want_ix)
+    assert torch.all(out_ix[ea + eb:] == -1) and int(err) == 0
+    # copy: 16-byte words, a count that is not a multiple of the unroll
+    src = torch.randint(0, 1 << 30, (4 * 100003,), dtype=torch.int32, device=DEV)
+    dst = torch.zeros_like(src)
+    cu().peer_copy(dst.data_ptr(), src.data_ptr(), src.numel() * 4)
+    torch.cuda.synchronize()
+    assert torch.equal(dst, src)
