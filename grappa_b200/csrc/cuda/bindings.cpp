@@ -175,7 +175,8 @@ void aggregate_bwd_gather(Tensor indptr, Tensor tptr, Tensor tdst, Tensor n_dst_
 void gemm(Tensor A, bool a_mn, Tensor B, bool b_mn, int64_t M_cap, OptT M_dev, int64_t N, int64_t K_cap, OptT K_dev,
           int64_t splits, Tensor C, int64_t mode, OptT bias, int64_t act, double dropout_p, OptT counters, int64_t salt,
           OptT labels, int64_t n_classes, OptT dlogits, OptT loss_sum, OptT correct, OptT pred_out, OptT n_rows_dev,
-          OptT dbias, Tensor err, int64_t bn, OptT act_mask, double mask_scale, int64_t zero_tail_rows) {
+          OptT dbias, Tensor err, int64_t bn, OptT act_mask, double mask_scale, int64_t zero_tail_rows, OptT att_l,
+          OptT att_r, OptT att_el, OptT att_er, int64_t att_heads, int64_t att_feat, OptT att_n_dst) {
   c10::cuda::CUDAGuard g(A.device());
   d::GemmProblem p;
   p.A = ptr2d<at::BFloat16>(A, at::kBFloat16, "A");
@@ -230,6 +231,18 @@ void gemm(Tensor A, bool a_mn, Tensor B, bool b_mn, int64_t M_cap, OptT M_dev, i
   }
   a.mask_scale = static_cast<float>(mask_scale);
   a.zero_tail_rows = static_cast<int32_t>(zero_tail_rows);
+  if (att_el.has_value()) {
+    a.att_l = optr<float>(att_l, at::kFloat, "att_l");
+    a.att_r = optr<float>(att_r, at::kFloat, "att_r");
+    a.att_el = optr<float>(att_el, at::kFloat, "att_el");
+    a.att_er = optr<float>(att_er, at::kFloat, "att_er");
+    a.att_heads = static_cast<int32_t>(att_heads);
+    a.att_feat = static_cast<int32_t>(att_feat);
+    a.att_n_dst = optr<int32_t>(att_n_dst, at::kInt, "att_n_dst");
+    TORCH_CHECK(att_el->numel() >= M_cap * att_heads, "att_el too small");
+    TORCH_CHECK(att_l.has_value() && att_l->numel() >= N && att_r.has_value() && att_r->numel() >= N,
+                "attention vectors too small");
+  }
   if (mode == d::kCrossEntropy)
     TORCH_CHECK(a.labels && a.dlogits && a.loss_sum && a.correct, "cross-entropy epilogue needs labels/dlogits/loss/correct");
   d::launch_gemm(p, a, static_cast<int>(bn), stream());
@@ -1077,7 +1090,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("bias"), py::arg("act"), py::arg("dropout_p"), py::arg("counters"), py::arg("salt"), py::arg("labels"),
         py::arg("n_classes"), py::arg("dlogits"), py::arg("loss_sum"), py::arg("correct"), py::arg("pred_out"),
         py::arg("n_rows_dev"), py::arg("dbias"), py::arg("err"), py::arg("bn"), py::arg("act_mask") = py::none(),
-        py::arg("mask_scale") = 1.0, py::arg("zero_tail_rows") = 0);
+        py::arg("mask_scale") = 1.0, py::arg("zero_tail_rows") = 0, py::arg("att_l") = py::none(),
+        py::arg("att_r") = py::none(), py::arg("att_el") = py::none(), py::arg("att_er") = py::none(),
+        py::arg("att_heads") = 0, py::arg("att_feat") = 0, py::arg("att_n_dst") = py::none());
   m.def("aggregate", &aggregate, py::arg("indptr"), py::arg("indices"), py::arg("n_dst_dev"), py::arg("n_dst"),
         py::arg("cap_dst"), py::arg("src"), py::arg("src_map"), py::arg("dim"), py::arg("mode"), py::arg("edge_w"),
         py::arg("src_norm"), py::arg("dst_norm"), py::arg("out"), py::arg("agg_col"), py::arg("self_col"),

@@ -5,6 +5,8 @@
 
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
+#include <utility>
 #include <stdexcept>
 #include <string>
 
@@ -21,6 +23,47 @@ enum : int32_t {
   kErrPeerTimeout = 1 << 3,    // a wait on a peer GPU's flag ran out of time
   kErrMmaTimeout = 1 << 4,     // a wait on a tensor-core/TMA barrier ran out of time
 };
+
+// Programmatic dependent launch (PDL).  A kernel launched by launch_k may be scheduled
+// while the previous kernel of its stream is still running; GB_PDL_ENTRY(), the first
+// statement of every kernel here, waits (griddepcontrol.wait) until the grids it
+// depends on have completed and their writes are visible, then lets the next kernel
+// of the stream be scheduled (griddepcontrol.launch_dependents: it only starts once
+// every block of this grid has executed this or exited, and it waits the same way).
+// Only block scheduling and launch latency overlap, never the kernels' memory
+// accesses.  Without the launch attribute both instructions are no-ops.
+#define GB_PDL_ENTRY()                                         \
+  do {                                                         \
+    asm volatile("griddepcontrol.wait;" ::: "memory");         \
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); \
+  } while (0)
+
+// PDL launches unless GRAPPA_PDL=0 (read once per process)
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("GRAPPA_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+// kernel<<<grid, block, smem, stream>>>(args...) with the programmatic-serialisation
+// attribute (the kernel must start with GB_PDL_ENTRY()).
+template <typename... KArgs, typename... Args>
+inline void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                     Args&&... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  GB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+}
 
 __device__ __forceinline__ void set_error(int32_t* err, int32_t bit) {
   if (err) atomicOr(err, bit);

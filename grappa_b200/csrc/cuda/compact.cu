@@ -38,6 +38,7 @@ __device__ __forceinline__ unsigned long long tag_word(const int64_t* gen, int s
 }
 
 __global__ void __launch_bounds__(kThreads) compact_k1(CompactArgs a, const int64_t* gen, int slot) {
+  GB_PDL_ENTRY();
   const int n_dst = *a.n_dst_ptr;
   const int n_e = *a.n_edges_ptr;
   const unsigned long long tw = tag_word(gen, slot);
@@ -61,6 +62,7 @@ __global__ void __launch_bounds__(kThreads) compact_k1(CompactArgs a, const int6
 }
 
 __global__ void __launch_bounds__(kThreads) compact_k2(CompactArgs a, const int64_t* gen, int slot) {
+  GB_PDL_ENTRY();
   __shared__ long long s_scan[kThreads / 32];
   __shared__ int s_tile;
   __shared__ long long s_prefix;
@@ -117,6 +119,7 @@ __global__ void __launch_bounds__(kThreads) compact_k2(CompactArgs a, const int6
 }
 
 __global__ void __launch_bounds__(kThreads) compact_k3(CompactArgs a) {
+  GB_PDL_ENTRY();
   const int n_e = *a.n_edges_ptr;
   for (long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < n_e;
        e += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -137,6 +140,7 @@ constexpr int kTpThreads = 1024;
 // are cleared for the next block.
 __global__ void __launch_bounds__(kTpThreads) block_transpose_scan_kernel(const int32_t* n_src_ptr, int32_t* t_cnt,
                                                                            int32_t* tptr, int cap_src) {
+  GB_PDL_ENTRY();
   __shared__ int s_scan[kTpThreads / 32];
   const int n_src = min(*n_src_ptr, cap_src);
   int carry = 0;
@@ -160,6 +164,7 @@ __global__ void __launch_bounds__(kThreads) block_transpose_fill_kernel(const in
                                                                          const int32_t* n_src_ptr, const int32_t* t_rank,
                                                                          const int32_t* tptr, int32_t* tdst,
                                                                          int cap_edges, int32_t* err) {
+  GB_PDL_ENTRY();
   const int n_dst = *n_dst_ptr;
   const int n_src = *n_src_ptr;
   const int warps = (gridDim.x * kThreads) >> 5;
@@ -179,7 +184,7 @@ __global__ void __launch_bounds__(kThreads) block_transpose_fill_kernel(const in
 void launch_block_transpose(const int32_t* indptr, const int32_t* indices, const int32_t* n_dst_ptr,
                             const int32_t* n_src_ptr, int32_t* t_cnt, const int32_t* t_rank, int32_t* tptr,
                             int32_t* tdst, int cap_src, int cap_edges, int32_t* err, cudaStream_t stream) {
-  block_transpose_scan_kernel<<<1, kTpThreads, 0, stream>>>(n_src_ptr, t_cnt, tptr, cap_src);
+  launch_k(block_transpose_scan_kernel, 1, kTpThreads, 0, stream, n_src_ptr, t_cnt, tptr, cap_src);
   GB_LAUNCH_CHECK();
   const int cap_dst = cap_src;  // destinations are the first sources
   int dev = 0, sms = 148;
@@ -187,7 +192,7 @@ void launch_block_transpose(const int32_t* indptr, const int32_t* indices, const
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int grid = static_cast<int>(std::min<long long>(ceil_div(cap_dst > 0 ? cap_dst : 1, kThreads / 32),
                                                         static_cast<long long>(sms) * 8));
-  block_transpose_fill_kernel<<<grid, kThreads, 0, stream>>>(indptr, indices, n_dst_ptr, n_src_ptr, t_rank, tptr, tdst,
+  launch_k(block_transpose_fill_kernel, grid, kThreads, 0, stream, indptr, indices, n_dst_ptr, n_src_ptr, t_rank, tptr, tdst,
                                                             cap_edges, err);
   GB_LAUNCH_CHECK();
 }
@@ -202,15 +207,15 @@ void launch_compact(const CompactArgs& a, int cap_dst, int cap_edges, const int6
   if (!k1_done) {
     const long long work1 = static_cast<long long>(cap_dst) + cap_edges;
     const int g1 = static_cast<int>(std::min<long long>(grid_stride, ceil_div(work1 > 0 ? work1 : 1, kThreads)));
-    compact_k1<<<g1, kThreads, 0, stream>>>(a, gen, slot);
+    launch_k(compact_k1, g1, kThreads, 0, stream, a, gen, slot);
     GB_LAUNCH_CHECK();
   }
   const int tiles = static_cast<int>(ceil_div(cap_edges > 0 ? cap_edges : 1, kTile));
   GB_CUDA_CHECK(cudaMemsetAsync(a.scan_scratch, 0, sizeof(unsigned long long) * (tiles + 1), stream));
-  compact_k2<<<tiles, kThreads, 0, stream>>>(a, gen, slot);
+  launch_k(compact_k2, tiles, kThreads, 0, stream, a, gen, slot);
   GB_LAUNCH_CHECK();
   const int g3 = static_cast<int>(std::min<long long>(grid_stride, ceil_div(cap_edges > 0 ? cap_edges : 1, kThreads)));
-  compact_k3<<<g3, kThreads, 0, stream>>>(a);
+  launch_k(compact_k3, g3, kThreads, 0, stream, a);
   GB_LAUNCH_CHECK();
 }
 

@@ -102,6 +102,7 @@ __device__ void block_col_atomic(const float (&v)[CPL][8], float* dst, int HF) {
 // ------------------------------------------------------------------ scores
 template <int CPL>
 __global__ void __launch_bounds__(kThreads) gat_scores_kernel(GatArgs a) {
+  GB_PDL_ENTRY();
   const int n_src = a.n_src_ptr ? min(*a.n_src_ptr, a.cap_src) : a.cap_src;
   const int n_dst = a.n_dst_ptr ? min(*a.n_dst_ptr, a.cap_dst) : a.cap_dst;
   const int HF = a.heads * a.feat;
@@ -201,6 +202,7 @@ __device__ __forceinline__ float pick_head(const float (&v)[HM], int h) {
 // HM: the head count rounded up to 4 or kMaxHeads (sizes the per-head register arrays)
 template <int CPL, int HM>
 __global__ void __launch_bounds__(kThreads) gat_fwd_kernel(GatArgs a) {
+  GB_PDL_ENTRY();
   extern __shared__ float s_row[];  // mean_heads: [warps][HF]
   __shared__ float s_w[kThreads / 32][32][HM];  // the batch's edge weights, per head
   __shared__ int s_u[kThreads / 32][32];        // the batch's source rows
@@ -466,6 +468,7 @@ constexpr int bwd_min_blocks() { return CPL + CPLY <= 3 ? 2 : 1; }
 
 template <int CPL, int CPLY, bool SEG>
 __global__ void __launch_bounds__(kThreads, bwd_min_blocks<CPL, CPLY>()) gat_bwd_edge_kernel(GatArgs a) {
+  GB_PDL_ENTRY();
   const int n_dst = a.n_dst_ptr ? min(*a.n_dst_ptr, a.cap_dst) : a.cap_dst;
   const int H = a.heads, F = a.feat, HF = H * F;
   const int IN = a.in_dim, HIN = H * a.in_dim;  // input-layer mode (CPLY > 0)
@@ -689,6 +692,7 @@ constexpr int kNodeRows = 4;
 
 template <int CPL, int CPLY, bool SEG>
 __global__ void __launch_bounds__(kThreads, 1) gat_bwd_node_kernel(GatArgs a) {
+  GB_PDL_ENTRY();
   const int n_src = a.n_src_ptr ? min(*a.n_src_ptr, a.cap_src) : a.cap_src;
   const int n_dst = a.n_dst_ptr ? min(*a.n_dst_ptr, a.cap_dst) : a.cap_dst;
   const int H = a.heads, F = a.feat, HF = H * F;
@@ -710,6 +714,9 @@ __global__ void __launch_bounds__(kThreads, 1) gat_bwd_node_kernel(GatArgs a) {
     hy[q] = CPLY > 0 ? min(c0 / max(IN, 1), H - 1) : 0;
     ky[q] = c0 - hy[q] * IN;
   }
+  // z is read only for the attention-vector gradients (da_l = sum del z); the input
+  // layer gets them as W xl instead (gat_in_dw) and passes none
+  const bool want_g = a.dattn_l || a.dattn_r;
   float gl[CPL][8], gr[CPL][8], xl[NY][8], xr[NY][8];
 #pragma unroll
   for (int q = 0; q < CPL; ++q)
@@ -736,7 +743,7 @@ __global__ void __launch_bounds__(kThreads, 1) gat_bwd_node_kernel(GatArgs a) {
       for (int q = 0; q < CPL; ++q) {
         const int c0 = (lane + 32 * q) * 8;
         zv[i][q] = make_uint4(0, 0, 0, 0);
-        if (u < n_src && c0 < HF)
+        if (want_g && u < n_src && c0 < HF)
           zv[i][q] = *reinterpret_cast<const uint4*>(a.z + static_cast<int64_t>(u) * a.ldz + zcol(a, c0));
       }
     }
@@ -857,6 +864,7 @@ __global__ void __launch_bounds__(kThreads, 1) gat_bwd_node_kernel(GatArgs a) {
 __global__ void gat_dw_combine_kernel(const float* T, int64_t ldt, const float* xl, const float* xr,
                                       const float* attn_l, const float* attn_r, int H, int F, int IN, float* dw,
                                       int64_t ldw) {
+  GB_PDL_ENTRY();
   const int total = H * F * IN;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
     const int r = i / IN, k = i % IN, h = r / F;
@@ -870,6 +878,7 @@ __global__ void gat_dw_combine_kernel(const float* T, int64_t ldt, const float* 
 __global__ void gat_in_prep_kernel(const __nv_bfloat16* w, int64_t ldw, const float* attn_l, const float* attn_r,
                                    int H, int F, int IN, int rows, float* wl, float* wr, __nv_bfloat16* wbd,
                                    int64_t ldwbd) {
+  GB_PDL_ENTRY();
   const int HIN = H * IN;
   const int64_t total = static_cast<int64_t>(rows) * HIN;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total + 2 * HIN;
@@ -898,6 +907,7 @@ __global__ void gat_in_prep_kernel(const __nv_bfloat16* w, int64_t ldw, const fl
 __global__ void gat_in_dw_kernel(const float* T, int64_t ldt, const float* xl, const float* xr, const float* attn_l,
                                  const float* attn_r, const float* w, int64_t ldw_in, int H, int F, int IN, float* dw,
                                  int64_t ldw, float* dattn_l, float* dattn_r) {
+  GB_PDL_ENTRY();
   const int HF = H * F;
   const int total = HF * IN;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total + HF; i += gridDim.x * blockDim.x) {
@@ -922,6 +932,7 @@ __global__ void gat_in_dw_kernel(const float* T, int64_t ldt, const float* xl, c
 // out[c] += sum over live rows of x[r, c]: one thread per column, rows split over blocks
 __global__ void col_sum_bf16_kernel(const __nv_bfloat16* x, int64_t ldx, const int32_t* n_ptr, int cap_rows, int cols,
                                     float* out) {
+  GB_PDL_ENTRY();
   const int n = n_ptr ? min(*n_ptr, cap_rows) : cap_rows;
   const int rows_per = (n + gridDim.y - 1) / gridDim.y;
   const int r0 = blockIdx.y * rows_per, r1 = min(n, r0 + rows_per);
@@ -948,9 +959,9 @@ void check(const GatArgs& a) {
 #define GAT_DISPATCH(KERNEL, GRID, SMEM)                                               \
   do {                                                                                 \
     const int cpl = cpl_for(a.heads * a.feat);                                         \
-    if (cpl <= 1) KERNEL<1><<<GRID, kThreads, SMEM, stream>>>(a);                      \
-    else if (cpl <= 2) KERNEL<2><<<GRID, kThreads, SMEM, stream>>>(a);                 \
-    else KERNEL<4><<<GRID, kThreads, SMEM, stream>>>(a);                               \
+    if (cpl <= 1) launch_k(KERNEL<1>, GRID, kThreads, SMEM, stream, a);                      \
+    else if (cpl <= 2) launch_k(KERNEL<2>, GRID, kThreads, SMEM, stream, a);                 \
+    else launch_k(KERNEL<4>, GRID, kThreads, SMEM, stream, a);                               \
     GB_LAUNCH_CHECK();                                                                 \
   } while (0)
 
@@ -968,8 +979,8 @@ void launch_gat_fwd(const GatArgs& a, cudaStream_t stream) {
   const int cpl = cpl_for(a.heads * a.feat);
 #define GAT_FWD(C)                                                                      \
   do {                                                                                  \
-    if (a.heads <= 4) gat_fwd_kernel<C, 4><<<grid, kThreads, smem, stream>>>(a);        \
-    else gat_fwd_kernel<C, kMaxHeads><<<grid, kThreads, smem, stream>>>(a);            \
+    if (a.heads <= 4) launch_k(gat_fwd_kernel<C, 4>, grid, kThreads, smem, stream, a);        \
+    else launch_k(gat_fwd_kernel<C, kMaxHeads>, grid, kThreads, smem, stream, a);            \
   } while (0)
   if (cpl <= 1) GAT_FWD(1);
   else if (cpl <= 2) GAT_FWD(2);
@@ -983,9 +994,9 @@ bool seg_heads(int F) { return F >= 8 && F <= 256 && (F & (F - 1)) == 0; }
 template <int CPL, int CPLY, bool SEG>
 void gat_bwd_pair(const GatArgs& a, cudaStream_t stream) {
   constexpr int mb = bwd_min_blocks<CPL, CPLY>();
-  gat_bwd_edge_kernel<CPL, CPLY, SEG><<<grid_warps(a.cap_dst, mb), kThreads, 0, stream>>>(a);
+  launch_k(gat_bwd_edge_kernel<CPL, CPLY, SEG>, grid_warps(a.cap_dst, mb), kThreads, 0, stream, a);
   GB_LAUNCH_CHECK();
-  gat_bwd_node_kernel<CPL, CPLY, SEG><<<grid_warps(static_cast<int>(ceil_div(a.cap_src, kNodeRows)), 1), kThreads, 0, stream>>>(a);
+  launch_k(gat_bwd_node_kernel<CPL, CPLY, SEG>, grid_warps(static_cast<int>(ceil_div(a.cap_src, kNodeRows)), 1), kThreads, 0, stream, a);
   GB_LAUNCH_CHECK();
 }
 
@@ -1025,7 +1036,7 @@ void launch_gat_in_prep(const __nv_bfloat16* w, int64_t ldw, const float* attn_l
                         cudaStream_t stream) {
   const int64_t total = static_cast<int64_t>(rows) * heads * in_dim + 2 * heads * in_dim;
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ceil_div(total, 256), sms() * 4)));
-  gat_in_prep_kernel<<<grid, 256, 0, stream>>>(w, ldw, attn_l, attn_r, heads, feat, in_dim, rows, wl, wr, wbd, ldwbd);
+  launch_k(gat_in_prep_kernel, grid, 256, 0, stream, w, ldw, attn_l, attn_r, heads, feat, in_dim, rows, wl, wr, wbd, ldwbd);
   GB_LAUNCH_CHECK();
 }
 
@@ -1034,7 +1045,7 @@ void launch_gat_in_dw(const float* T, int64_t ldt, const float* xl, const float*
                       int64_t ldw, float* dattn_l, float* dattn_r, cudaStream_t stream) {
   const int total = heads * feat * in_dim + heads * feat;
   const int grid = std::max(1, std::min((total + 255) / 256, sms() * 4));
-  gat_in_dw_kernel<<<grid, 256, 0, stream>>>(T, ldt, xl, xr, attn_l, attn_r, w, ldw_in, heads, feat, in_dim, dw, ldw,
+  launch_k(gat_in_dw_kernel, grid, 256, 0, stream, T, ldt, xl, xr, attn_l, attn_r, w, ldw_in, heads, feat, in_dim, dw, ldw,
                                              dattn_l, dattn_r);
   GB_LAUNCH_CHECK();
 }
@@ -1043,7 +1054,7 @@ void launch_col_sum_bf16(const __nv_bfloat16* x, int64_t ldx, const int32_t* n_p
                          cudaStream_t stream) {
   const dim3 grid(static_cast<unsigned>(std::max(1, (cols + 255) / 256)),
                   static_cast<unsigned>(std::max(1, std::min(sms() * 2, (cap_rows + 255) / 256))));
-  col_sum_bf16_kernel<<<grid, 256, 0, stream>>>(x, ldx, n_ptr, cap_rows, cols, out);
+  launch_k(col_sum_bf16_kernel, grid, 256, 0, stream, x, ldx, n_ptr, cap_rows, cols, out);
   GB_LAUNCH_CHECK();
 }
 
@@ -1052,7 +1063,7 @@ void launch_gat_dw_combine(const float* T, int64_t ldt, const float* xl, const f
                            cudaStream_t stream) {
   const int total = heads * feat * in_dim;
   const int grid = std::max(1, std::min((total + 255) / 256, sms() * 4));
-  gat_dw_combine_kernel<<<grid, 256, 0, stream>>>(T, ldt, xl, xr, attn_l, attn_r, heads, feat, in_dim, dw, ldw);
+  launch_k(gat_dw_combine_kernel, grid, 256, 0, stream, T, ldt, xl, xr, attn_l, attn_r, heads, feat, in_dim, dw, ldw);
   GB_LAUNCH_CHECK();
 }
 

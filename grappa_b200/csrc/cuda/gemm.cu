@@ -187,6 +187,37 @@ __device__ __forceinline__ void apply_act_mask(const GemmArgs& a, int m, int nc,
 // lane, columns [c_begin, c_end) (multiples of 64 on the TMA-store path); `trow` is
 // that warp's TMEM address of the tile, `stage` its 32 x (c_end - c_begin) bf16
 // staging panels for the TMA store (kTmaStore), `ok` false after an aborted wait.
+// attention-logit epilogue: the 32 stored values v of row m, columns nc.. (heads of
+// att_feat columns), rounded to bf16 as stored, dotted with att_l / att_r per head and
+// reduced into el / er (one reduction per head the chunk touches)
+__device__ __forceinline__ void att_logits(const GemmArgs& a, int m, int nc, const float* v) {
+  const int F = a.att_feat, H = a.att_heads;
+  const bool dst = a.att_n_dst && m < *a.att_n_dst;
+  int h = nc / F, bound = (h + 1) * F;
+  float sl = 0.f, sr = 0.f;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const int c = nc + j;
+    if (c >= a.N) break;
+    if (c == bound) {
+      if (h < H) {
+        atomicAdd(a.att_el + static_cast<int64_t>(m) * H + h, sl);
+        if (dst) atomicAdd(a.att_er + static_cast<int64_t>(m) * H + h, sr);
+      }
+      ++h;
+      bound += F;
+      sl = sr = 0.f;
+    }
+    const float z = __bfloat162float(__float2bfloat16_rn(v[j]));
+    sl = fmaf(z, __ldg(a.att_l + c), sl);
+    sr = fmaf(z, __ldg(a.att_r + c), sr);
+  }
+  if (h < H) {
+    atomicAdd(a.att_el + static_cast<int64_t>(m) * H + h, sl);
+    if (dst) atomicAdd(a.att_er + static_cast<int64_t>(m) * H + h, sr);
+  }
+}
+
 template <int BN, bool kTmaStore>
 __device__ __forceinline__ void store_tile(const GemmArgs& a, const CUtensorMap* tmC, uint32_t trow, int m0, int n0,
                                            int M, int quarter, int lane, uint8_t* stage, bool ok, int c_begin = 0,
@@ -223,6 +254,7 @@ __device__ __forceinline__ void store_tile(const GemmArgs& a, const CUtensorMap*
         v[j] = live ? x : 0.f;
       }
       if (a.act_mask && live) apply_act_mask(a, m, nc, v);
+      if (a.att_el && live && nc < a.N) att_logits(a, m, nc, v);
       if (a.dropout_p > 0.f && live) {
         const uint64_t base = static_cast<uint64_t>(m) * static_cast<uint64_t>(a.ldc) + static_cast<uint64_t>(nc);
 #pragma unroll
@@ -302,6 +334,7 @@ __device__ __forceinline__ void store_tile(const GemmArgs& a, const CUtensorMap*
         v[j] = x;
       }
       if (a.act_mask) apply_act_mask(a, m, nc, v);
+      if (a.att_el) att_logits(a, m, nc, v);
       if (a.dropout_p > 0.f) {
         const uint64_t base = static_cast<uint64_t>(m) * static_cast<uint64_t>(a.ldc) + static_cast<uint64_t>(nc);
 #pragma unroll
@@ -352,6 +385,7 @@ template <int BN, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 2)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmC, GemmArgs a) {
+  GB_PDL_ENTRY();
   using S = Smem<BN>;
   constexpr int kStages = S::kStages;
   constexpr bool kTmaStore = BN % 64 == 0 && 4 * 32 * BN * 2 <= kStages * S::kStageBytes;
@@ -611,6 +645,7 @@ template <int BN, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(p_threads<BN>(), 1)
     gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                            const __grid_constant__ CUtensorMap tmC, GemmArgs a) {
+  GB_PDL_ENTRY();
   using S = PSmem<BN>;
   constexpr int kStages = S::kStages;
   constexpr bool kTmaStore = BN % 64 == 0;
@@ -854,7 +889,7 @@ void launch_t(const GemmProblem& p, const GemmArgs& a, dim3 grid, cudaStream_t s
     }
     const int64_t tiles = static_cast<int64_t>(grid.x) * grid.y * grid.z;
     const unsigned g = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(tiles, sm_count())));
-    kern<<<g, p_threads<BN>(), P::kBytes, stream>>>(ma, mb, mc, a);
+    launch_k(kern, g, p_threads<BN>(), P::kBytes, stream, ma, mb, mc, a);
     GB_LAUNCH_CHECK();
     return;
   }
@@ -864,7 +899,7 @@ void launch_t(const GemmProblem& p, const GemmArgs& a, dim3 grid, cudaStream_t s
     GB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes));
     attr_device = dev;
   }
-  kern<<<grid, kThreads, S::kBytes, stream>>>(ma, mb, mc, a);
+  launch_k(kern, grid, kThreads, S::kBytes, stream, ma, mb, mc, a);
   GB_LAUNCH_CHECK();
 }
 
@@ -878,6 +913,9 @@ void launch_gemm(const GemmProblem& p, GemmArgs a, int bn, cudaStream_t stream) 
   if (a.c_mode == kCrossEntropy && a.ld_dl % 8 != 0) throw std::invalid_argument("dlogits stride must be a multiple of 8");
   if (a.act_mask && (a.c_mode != kStoreBf16 || a.bias || a.act || a.dropout_p > 0.f || a.ld_mask % 8 != 0))
     throw std::invalid_argument("activation-backward epilogue: bf16 store only, no bias/activation/dropout, mask stride % 8");
+  if (a.att_el && (a.c_mode != kStoreBf16 || a.bias || a.act || a.dropout_p > 0.f || a.act_mask || !a.att_l ||
+                   !a.att_r || !a.att_er || a.att_heads <= 0 || a.att_feat <= 0 || a.att_heads * a.att_feat != a.N))
+    throw std::invalid_argument("attention-logit epilogue: plain bf16 store of N = heads * feat, vectors and outputs given");
   if (a.zero_tail_rows > 0 && a.c_mode != kStoreBf16)
     throw std::invalid_argument("zeroed tail rows need the bf16 store mode");
 #define GB_GEMM_CASE(BNV)                                                           \

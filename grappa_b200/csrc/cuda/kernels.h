@@ -152,6 +152,15 @@ struct GemmArgs {
   // > 0: rows [M, roundup(M, zero_tail_rows)) of C (below c_rows) are written as zeros,
   // so that a later split-K GEMM over whole 64-row blocks reads zeros past the live rows
   int32_t zero_tail_rows = 0;
+  // GAT attention logits of a bf16 z = x W^T store (no bias, activation or dropout):
+  // el[m, h] += sum_f bf16(z[m, hF+f]) att_l[hF+f], and er the same with att_r for
+  // rows m < *att_n_dst; el / er are zeroed by the caller
+  const float* att_l = nullptr;
+  const float* att_r = nullptr;
+  float* att_el = nullptr;
+  float* att_er = nullptr;
+  int32_t att_heads = 0, att_feat = 0;
+  const int32_t* att_n_dst = nullptr;
 };
 void launch_gemm(const GemmProblem& p, GemmArgs a, int bn, cudaStream_t stream);
 

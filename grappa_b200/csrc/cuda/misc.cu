@@ -52,6 +52,7 @@ __device__ __forceinline__ uint4 act_bwd_chunk(const ActBwdArgs& a, const float4
 // (fp32, cleared for the next step), H and dY once and is bound by the latency of
 // those loads at one row in flight per thread.
 __global__ void act_bwd_kernel(ActBwdArgs a, int chunks) {
+  GB_PDL_ENTRY();
   extern __shared__ float s_col[];  // [blockDim.x * 8]
   const int n = a.n_ptr ? *a.n_ptr : a.n;
   const int rpb = blockDim.x / chunks;
@@ -105,6 +106,7 @@ __global__ void act_bwd_kernel(ActBwdArgs a, int chunks) {
 template <bool F32>
 __global__ void gather_rows_kernel(const void* table, int64_t ts, int dim, const int32_t* ids, const int32_t* n_ptr,
                                    int n_static, __nv_bfloat16* out, int64_t os) {
+  GB_PDL_ENTRY();
   const int n = n_ptr ? *n_ptr : n_static;
   const int chunks = dim >> 3;
   const int lane = threadIdx.x & 31;
@@ -129,6 +131,7 @@ __global__ void gather_rows_kernel(const void* table, int64_t ts, int dim, const
 
 template <typename T>
 __global__ void gather_scalar_kernel(const T* table, const int32_t* ids, const int32_t* n_ptr, int n_static, T* out) {
+  GB_PDL_ENTRY();
   const int n = n_ptr ? *n_ptr : n_static;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) out[i] = table[ids[i]];
 }
@@ -136,6 +139,7 @@ __global__ void gather_scalar_kernel(const T* table, const int32_t* ids, const i
 // ---------------------------------------------------------------- generators
 __global__ void rmat_kernel(int64_t n, int scale, uint64_t ta, uint64_t tb, uint64_t tc, uint64_t key, int64_t e0,
                             int64_t count, int64_t* keys) {
+  GB_PDL_ENTRY();
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < count;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const uint64_t e = static_cast<uint64_t>(e0 + i);
@@ -159,6 +163,7 @@ __global__ void rmat_kernel(int64_t n, int scale, uint64_t ta, uint64_t tb, uint
 }
 
 __global__ void shuffle_keys_kernel(const int64_t* ids, int64_t n, uint64_t k, int64_t* keys) {
+  GB_PDL_ENTRY();
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x)
     keys[i] = static_cast<int64_t>(mix64(static_cast<uint64_t>(ids[i]) ^ k) >> 1);
@@ -166,6 +171,7 @@ __global__ void shuffle_keys_kernel(const int64_t* ids, int64_t n, uint64_t k, i
 
 // Box-Muller transform of Philox uniforms (standard normal samples).
 __global__ void normal_kernel(float* out, int64_t n, uint64_t key) {
+  GB_PDL_ENTRY();
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; 2 * i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const U4 r = index_draw4(key, static_cast<uint64_t>(i), 7u);
@@ -184,6 +190,7 @@ __global__ void normal_kernel(float* out, int64_t n, uint64_t key) {
 // past d zeroed).  d is even, so a Box-Muller pair never straddles two rows.
 __global__ void normal_rows_kernel(__nv_bfloat16* out, int64_t ld, int64_t row0, int64_t rows, int d,
                                    uint64_t key) {
+  GB_PDL_ENTRY();
   const int64_t pairs_per_row = d / 2;
   const int64_t total = rows * pairs_per_row;
   for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
@@ -206,6 +213,7 @@ __global__ void normal_rows_kernel(__nv_bfloat16* out, int64_t ld, int64_t row0,
 
 __global__ void dropout_mask_kernel(uint8_t* mask, int64_t rows, int64_t cols, int64_t ld, uint32_t thr,
                                     const int64_t* counters, uint32_t salt) {
+  GB_PDL_ENTRY();
   const uint64_t key = hop_key(static_cast<uint64_t>(counters[0]) ^ 0xD80Full, static_cast<uint64_t>(counters[1]),
                                static_cast<uint64_t>(counters[2]), salt);
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < rows * cols;
@@ -235,6 +243,7 @@ __device__ __forceinline__ float adam_elem(const AdamArgs& a, float g, float& p,
 // scalar path.
 template <bool VEC>
 __global__ void adam_kernel(AdamArgs a) {
+  GB_PDL_ENTRY();
   const float t = static_cast<float>(*a.step + 1);
   const float bc1 = 1.f - powf(a.beta1, t);
   const float bc2 = 1.f - powf(a.beta2, t);
@@ -281,6 +290,7 @@ __global__ void adam_kernel(AdamArgs a) {
 
 // counters = [seed, epoch, step_in_epoch, global_step, gen, adam_t]
 __global__ void sampler_counters_kernel(const int64_t* main, int64_t* dst, int64_t step_offset) {
+  GB_PDL_ENTRY();
   dst[0] = main[0];
   dst[1] = main[1];
   dst[2] = main[2] + step_offset;
@@ -291,6 +301,7 @@ __global__ void sampler_counters_kernel(const int64_t* main, int64_t* dst, int64
 
 __global__ void step_end_kernel(int64_t* counters, const int64_t* ring_slot, float* fstats, int nf, int32_t* istats,
                                 int ni) {
+  GB_PDL_ENTRY();
   if (ring_slot) {
     float* ring = reinterpret_cast<float*>(static_cast<uintptr_t>(*ring_slot));
     if (ring && fstats) ring[counters[2]] = fstats[2];
@@ -304,6 +315,7 @@ __global__ void step_end_kernel(int64_t* counters, const int64_t* ring_slot, flo
 }
 
 __global__ void sample_prologue_kernel(SamplePrologueArgs a) {
+  GB_PDL_ENTRY();
   const int64_t row = a.main[2] + a.step_offset;
   const int32_t* table =
       a.table_slot ? reinterpret_cast<const int32_t*>(static_cast<uintptr_t>(*a.table_slot)) : nullptr;
@@ -350,7 +362,7 @@ void launch_act_bwd(const ActBwdArgs& a, cudaStream_t stream) {
   // at a few blocks per SM so that those atomics do not queue up on the same words
   const int per_sm = a.dbias ? 3 : 8;
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ceil_div(rows, rpb), int64_t(sm_count()) * per_sm)));
-  act_bwd_kernel<<<grid, threads, threads * 8 * sizeof(float), stream>>>(a, chunks);
+  launch_k(act_bwd_kernel, grid, threads, threads * 8 * sizeof(float), stream, a, chunks);
   GB_LAUNCH_CHECK();
 }
 
@@ -360,20 +372,20 @@ void launch_gather_rows_bf16(const void* table, bool table_f32, int64_t table_st
   if (dim % 8 != 0) throw std::invalid_argument("gather: dim must be a multiple of 8");
   const int grid = grid_1d(static_cast<int64_t>(cap) * 32, 256, 16);
   if (table_f32)
-    gather_rows_kernel<true><<<grid, 256, 0, stream>>>(table, table_stride, dim, ids, n_ptr, n, out, out_stride);
+    launch_k(gather_rows_kernel<true>, grid, 256, 0, stream, table, table_stride, dim, ids, n_ptr, n, out, out_stride);
   else
-    gather_rows_kernel<false><<<grid, 256, 0, stream>>>(table, table_stride, dim, ids, n_ptr, n, out, out_stride);
+    launch_k(gather_rows_kernel<false>, grid, 256, 0, stream, table, table_stride, dim, ids, n_ptr, n, out, out_stride);
   GB_LAUNCH_CHECK();
 }
 
 void launch_gather_i32(const int32_t* table, const int32_t* ids, const int32_t* n_ptr, int n, int cap, int32_t* out,
                        cudaStream_t stream) {
-  gather_scalar_kernel<int32_t><<<grid_1d(cap, 256), 256, 0, stream>>>(table, ids, n_ptr, n, out);
+  launch_k(gather_scalar_kernel<int32_t>, grid_1d(cap, 256), 256, 0, stream, table, ids, n_ptr, n, out);
   GB_LAUNCH_CHECK();
 }
 void launch_gather_i64(const int64_t* table, const int32_t* ids, const int32_t* n_ptr, int n, int cap, int64_t* out,
                        cudaStream_t stream) {
-  gather_scalar_kernel<int64_t><<<grid_1d(cap, 256), 256, 0, stream>>>(table, ids, n_ptr, n, out);
+  launch_k(gather_scalar_kernel<int64_t>, grid_1d(cap, 256), 256, 0, stream, table, ids, n_ptr, n, out);
   GB_LAUNCH_CHECK();
 }
 
@@ -382,7 +394,7 @@ void launch_rmat_candidates(int64_t n, int scale, double a, double b, double c, 
   const uint64_t ta = static_cast<uint64_t>(a * 4294967296.0);
   const uint64_t tb = static_cast<uint64_t>((a + b) * 4294967296.0);
   const uint64_t tc = static_cast<uint64_t>((a + b + c) * 4294967296.0);
-  rmat_kernel<<<grid_1d(count, 256, 32), 256, 0, stream>>>(n, scale, ta, tb, tc, mix64(seed ^ 0x524D4154ull), e_begin,
+  launch_k(rmat_kernel, grid_1d(count, 256, 32), 256, 0, stream, n, scale, ta, tb, tc, mix64(seed ^ 0x524D4154ull), e_begin,
                                                           count, keys);
   GB_LAUNCH_CHECK();
 }
@@ -390,19 +402,19 @@ void launch_rmat_candidates(int64_t n, int scale, double a, double b, double c, 
 void launch_shuffle_keys(const int64_t* ids, int64_t n, uint64_t seed, uint64_t epoch, int64_t* keys,
                          cudaStream_t stream) {
   const uint64_t k = mix64(mix64(seed ^ 0x5348554646ull) ^ epoch);
-  shuffle_keys_kernel<<<grid_1d(n, 256, 16), 256, 0, stream>>>(ids, n, k, keys);
+  launch_k(shuffle_keys_kernel, grid_1d(n, 256, 16), 256, 0, stream, ids, n, k, keys);
   GB_LAUNCH_CHECK();
 }
 
 void launch_normal_fill(float* out, int64_t n, uint64_t seed, cudaStream_t stream) {
-  normal_kernel<<<grid_1d((n + 1) / 2, 256, 32), 256, 0, stream>>>(out, n, mix64(seed ^ 0x4E4F524Dull));
+  launch_k(normal_kernel, grid_1d((n + 1) / 2, 256, 32), 256, 0, stream, out, n, mix64(seed ^ 0x4E4F524Dull));
   GB_LAUNCH_CHECK();
 }
 
 void launch_normal_rows_bf16(__nv_bfloat16* out, int64_t ld, int64_t row0, int64_t rows, int d, uint64_t seed,
                              cudaStream_t stream) {
   if (d % 2 != 0) throw std::invalid_argument("normal_rows: d must be even");
-  normal_rows_kernel<<<grid_1d(rows * (d / 2), 256, 32), 256, 0, stream>>>(out, ld, row0, rows, d,
+  launch_k(normal_rows_kernel, grid_1d(rows * (d / 2), 256, 32), 256, 0, stream, out, ld, row0, rows, d,
                                                                           mix64(seed ^ 0x4E4F524Dull));
   GB_LAUNCH_CHECK();
 }
@@ -410,7 +422,7 @@ void launch_normal_rows_bf16(__nv_bfloat16* out, int64_t ld, int64_t row0, int64
 void launch_dropout_mask(uint8_t* mask, int64_t rows, int64_t cols, int64_t ld, float p, const int64_t* counters,
                          uint32_t salt, cudaStream_t stream) {
   const uint32_t thr = static_cast<uint32_t>(static_cast<double>(p) * 4294967296.0);
-  dropout_mask_kernel<<<grid_1d(rows * cols, 256, 16), 256, 0, stream>>>(mask, rows, cols, ld, thr, counters, salt);
+  launch_k(dropout_mask_kernel, grid_1d(rows * cols, 256, 16), 256, 0, stream, mask, rows, cols, ld, thr, counters, salt);
   GB_LAUNCH_CHECK();
 }
 
@@ -419,20 +431,20 @@ void launch_adam(const AdamArgs& a, cudaStream_t stream) {
                      reinterpret_cast<uintptr_t>(a.m) | reinterpret_cast<uintptr_t>(a.v)) & 15u) == 0 &&
                    (reinterpret_cast<uintptr_t>(a.param_bf16) & 7u) == 0;
   if (vec)
-    adam_kernel<true><<<grid_1d((a.n + 3) / 4, 256, 4), 256, 0, stream>>>(a);
+    launch_k(adam_kernel<true>, grid_1d((a.n + 3) / 4, 256, 4), 256, 0, stream, a);
   else
-    adam_kernel<false><<<grid_1d(a.n, 256, 4), 256, 0, stream>>>(a);
+    launch_k(adam_kernel<false>, grid_1d(a.n, 256, 4), 256, 0, stream, a);
   GB_LAUNCH_CHECK();
 }
 
 void launch_sampler_counters(const int64_t* main, int64_t* dst, int64_t step_offset, cudaStream_t stream) {
-  sampler_counters_kernel<<<1, 1, 0, stream>>>(main, dst, step_offset);
+  launch_k(sampler_counters_kernel, 1, 1, 0, stream, main, dst, step_offset);
   GB_LAUNCH_CHECK();
 }
 
 void launch_step_end(int64_t* counters, const int64_t* ring_slot, float* fstats, int nf, int32_t* istats, int ni,
                      cudaStream_t stream) {
-  step_end_kernel<<<1, 1, 0, stream>>>(counters, ring_slot, fstats, fstats ? nf : 0, istats, istats ? ni : 0);
+  launch_k(step_end_kernel, 1, 1, 0, stream, counters, ring_slot, fstats, fstats ? nf : 0, istats, istats ? ni : 0);
   GB_LAUNCH_CHECK();
 }
 
@@ -443,7 +455,7 @@ void launch_sample_prologue(const SamplePrologueArgs& a, cudaStream_t stream) {
     throw std::invalid_argument("sample_prologue: gathered outputs need their tables");
   const int threads = 1024;
   const int blocks = static_cast<int>(std::min<int64_t>(8, (a.B + threads - 1) / threads));
-  sample_prologue_kernel<<<blocks, threads, 0, stream>>>(a);
+  launch_k(sample_prologue_kernel, blocks, threads, 0, stream, a);
   GB_LAUNCH_CHECK();
 }
 

@@ -38,6 +38,7 @@ __device__ __forceinline__ int tail_rows(int n, int cap, int zt) {
 // ------------------------------------------------------------------ cross-entropy
 template <int CPL>
 __global__ void __launch_bounds__(256) cross_entropy_kernel(CeArgs a) {
+  GB_PDL_ENTRY();
   const int n = live_rows(a.n_rows_ptr, a.cap_rows);
   const int rows_end = tail_rows(n, a.cap_rows, a.zero_tail_rows);
   const int n_sel = a.n_sel_ptr ? *a.n_sel_ptr : n;
@@ -120,6 +121,7 @@ __global__ void __launch_bounds__(256) cross_entropy_kernel(CeArgs a) {
 // column sums of x and x^2 over the live rows: one thread per column pair, the
 // block's rows strided over the grid
 __global__ void bn_stats_kernel(BnArgs a) {
+  GB_PDL_ENTRY();
   const int n = live_rows(a.n_ptr, a.cap);
   const int pairs = a.dim >> 1;
   for (int cp = threadIdx.x; cp < pairs; cp += blockDim.x) {
@@ -150,6 +152,7 @@ __device__ __forceinline__ void bn_moments(const float* sums, int dim, int c, in
 }
 
 __global__ void bn_apply_kernel(BnArgs a) {
+  GB_PDL_ENTRY();
   extern __shared__ float sh[];  // [2 * dim]: scale, shift
   const int n = live_rows(a.n_ptr, a.cap);
   for (int c = threadIdx.x; c < a.dim; c += blockDim.x) {
@@ -196,6 +199,7 @@ __global__ void bn_apply_kernel(BnArgs a) {
 
 // g = dy * relu'(y); column sums of g and g * xhat
 __global__ void bn_bwd_reduce_kernel(BnBwdArgs a) {
+  GB_PDL_ENTRY();
   const int n = live_rows(a.n_ptr, a.cap);
   for (int c = threadIdx.x; c < a.dim; c += blockDim.x) {
     float mean, rstd, var;
@@ -215,6 +219,7 @@ __global__ void bn_bwd_reduce_kernel(BnBwdArgs a) {
 }
 
 __global__ void bn_bwd_apply_kernel(BnBwdArgs a) {
+  GB_PDL_ENTRY();
   const int n = live_rows(a.n_ptr, a.cap);
   const float inv_n = 1.f / static_cast<float>(n > 0 ? n : 1);
   if (blockIdx.x == 0) {
@@ -254,6 +259,7 @@ __global__ void bn_bwd_apply_kernel(BnBwdArgs a) {
 // ------------------------------------------------------------------ L2 normalisation
 __global__ void l2norm_fwd_kernel(const __nv_bfloat16* z, int64_t ldz, int dim, const int32_t* n_ptr, int cap,
                                   __nv_bfloat16* y, int64_t ldy, float* norms) {
+  GB_PDL_ENTRY();
   const int n = live_rows(n_ptr, cap);
   const int lane = threadIdx.x & 31;
   const int warps_total = (gridDim.x * blockDim.x) >> 5;
@@ -289,6 +295,7 @@ __global__ void l2norm_fwd_kernel(const __nv_bfloat16* z, int64_t ldz, int dim, 
 __global__ void l2norm_bwd_kernel(const __nv_bfloat16* y, int64_t ldy, float* dy, const __nv_bfloat16* dyb,
                                   int64_t lddy, const float* norms, int dim, const int32_t* n_ptr, int cap, float* dz,
                                   int64_t lddz) {
+  GB_PDL_ENTRY();
   const int n = live_rows(n_ptr, cap);
   const int lane = threadIdx.x & 31;
   const int warps_total = (gridDim.x * blockDim.x) >> 5;
@@ -330,6 +337,7 @@ __global__ void l2norm_bwd_kernel(const __nv_bfloat16* y, int64_t ldy, float* dy
 
 __global__ void add_bf16_rows_kernel(float* dst, int64_t ldd, const __nv_bfloat16* src, int64_t lds, int dim,
                                      const int32_t* n_ptr, int cap) {
+  GB_PDL_ENTRY();
   const int n = live_rows(n_ptr, cap);
   const int chunks = dim >> 3;
   const int64_t total = static_cast<int64_t>(n) * chunks;
@@ -354,6 +362,7 @@ __device__ __forceinline__ uint64_t dropout_key(const int64_t* counters, uint32_
 __global__ void dropout_rows_kernel(const __nv_bfloat16* in, int64_t ldi, __nv_bfloat16* out, int64_t ldo, int dim,
                                     int64_t ld_mask, const int32_t* n_ptr, int cap, float p, const int64_t* counters,
                                     uint32_t salt) {
+  GB_PDL_ENTRY();
   const int n = live_rows(n_ptr, cap);
   const int rows_end = tail_rows(n, cap, 64);
   const int chunks = dim >> 3;
@@ -384,6 +393,7 @@ __global__ void dropout_rows_kernel(const __nv_bfloat16* in, int64_t ldi, __nv_b
 
 __global__ void dropout_grad_kernel(float* g, int64_t ldg, int dim, int64_t ld_mask, const int32_t* n_ptr, int cap,
                                     float p, const int64_t* counters, uint32_t salt) {
+  GB_PDL_ENTRY();
   const int n = live_rows(n_ptr, cap);
   const int chunks = dim >> 3;
   const uint64_t key = dropout_key(counters, salt);
@@ -406,6 +416,7 @@ __global__ void dropout_grad_kernel(float* g, int64_t ldg, int dim, int64_t ld_m
 
 __global__ void f32_to_bf16_rows_kernel(float* src, int64_t lds, __nv_bfloat16* dst, int64_t ldd, int dim,
                                         const int32_t* n_ptr, int cap, bool clear, int zt) {
+  GB_PDL_ENTRY();
   const int n = live_rows(n_ptr, cap);
   const int rows_end = tail_rows(n, cap, zt);
   const int chunks = dim >> 3;
@@ -437,12 +448,12 @@ void launch_cross_entropy(const CeArgs& a, cudaStream_t stream) {
   if (a.n_classes <= 0 || a.n_classes > 1024) throw std::invalid_argument("cross_entropy: 1..1024 classes");
   const int grid = grid_1d(static_cast<int64_t>(a.cap_rows) * 32, 256, 8);
   const int cpl = (std::max(a.n_classes, static_cast<int32_t>(a.ld_dl)) + 31) / 32;
-  if (cpl <= 1) cross_entropy_kernel<1><<<grid, 256, 0, stream>>>(a);
-  else if (cpl <= 2) cross_entropy_kernel<2><<<grid, 256, 0, stream>>>(a);
-  else if (cpl <= 4) cross_entropy_kernel<4><<<grid, 256, 0, stream>>>(a);
-  else if (cpl <= 8) cross_entropy_kernel<8><<<grid, 256, 0, stream>>>(a);
-  else if (cpl <= 16) cross_entropy_kernel<16><<<grid, 256, 0, stream>>>(a);
-  else cross_entropy_kernel<32><<<grid, 256, 0, stream>>>(a);
+  if (cpl <= 1) launch_k(cross_entropy_kernel<1>, grid, 256, 0, stream, a);
+  else if (cpl <= 2) launch_k(cross_entropy_kernel<2>, grid, 256, 0, stream, a);
+  else if (cpl <= 4) launch_k(cross_entropy_kernel<4>, grid, 256, 0, stream, a);
+  else if (cpl <= 8) launch_k(cross_entropy_kernel<8>, grid, 256, 0, stream, a);
+  else if (cpl <= 16) launch_k(cross_entropy_kernel<16>, grid, 256, 0, stream, a);
+  else launch_k(cross_entropy_kernel<32>, grid, 256, 0, stream, a);
   GB_LAUNCH_CHECK();
 }
 
@@ -450,27 +461,27 @@ void launch_batchnorm_fwd(const BnArgs& a, cudaStream_t stream) {
   if (a.dim % 8 != 0 || a.ldx % 2 != 0 || a.ldy % 8 != 0) throw std::invalid_argument("batchnorm: dim % 8");
   if (a.training) {
     const int g = grid_1d(static_cast<int64_t>(a.cap) * 256 / 64, 256, 4);
-    bn_stats_kernel<<<g, 256, 0, stream>>>(a);
+    launch_k(bn_stats_kernel, g, 256, 0, stream, a);
     GB_LAUNCH_CHECK();
   }
   const int g2 = grid_1d(static_cast<int64_t>(a.cap) * (a.dim / 2), 256, 8);
-  bn_apply_kernel<<<g2, 256, 2 * a.dim * sizeof(float), stream>>>(a);
+  launch_k(bn_apply_kernel, g2, 256, 2 * a.dim * sizeof(float), stream, a);
   GB_LAUNCH_CHECK();
 }
 
 void launch_batchnorm_bwd(const BnBwdArgs& a, cudaStream_t stream) {
   const int g = grid_1d(static_cast<int64_t>(a.cap) * 256 / 64, 256, 4);
-  bn_bwd_reduce_kernel<<<g, 256, 0, stream>>>(a);
+  launch_k(bn_bwd_reduce_kernel, g, 256, 0, stream, a);
   GB_LAUNCH_CHECK();
   const int g2 = grid_1d(static_cast<int64_t>(a.cap) * a.dim, 256, 8);
-  bn_bwd_apply_kernel<<<g2, 256, 0, stream>>>(a);
+  launch_k(bn_bwd_apply_kernel, g2, 256, 0, stream, a);
   GB_LAUNCH_CHECK();
 }
 
 void launch_l2norm_fwd(const __nv_bfloat16* z, int64_t ldz, int32_t dim, const int32_t* n_ptr, int cap,
                        __nv_bfloat16* y, int64_t ldy, float* norms, cudaStream_t stream) {
   if (dim % 8 != 0) throw std::invalid_argument("l2norm: dim % 8");
-  l2norm_fwd_kernel<<<grid_1d(static_cast<int64_t>(cap) * 32, 256, 8), 256, 0, stream>>>(z, ldz, dim, n_ptr, cap, y,
+  launch_k(l2norm_fwd_kernel, grid_1d(static_cast<int64_t>(cap) * 32, 256, 8), 256, 0, stream, z, ldz, dim, n_ptr, cap, y,
                                                                                          ldy, norms);
   GB_LAUNCH_CHECK();
 }
@@ -479,7 +490,7 @@ void launch_l2norm_bwd(const __nv_bfloat16* y, int64_t ldy, float* dy, const __n
                        const float* norms, int32_t dim, const int32_t* n_ptr, int cap, float* dz, int64_t lddz,
                        cudaStream_t stream) {
   if (dim % 8 != 0) throw std::invalid_argument("l2norm: dim % 8");
-  l2norm_bwd_kernel<<<grid_1d(static_cast<int64_t>(cap) * 32, 256, 8), 256, 0, stream>>>(y, ldy, dy, dy_bf16, lddy,
+  launch_k(l2norm_bwd_kernel, grid_1d(static_cast<int64_t>(cap) * 32, 256, 8), 256, 0, stream, y, ldy, dy, dy_bf16, lddy,
                                                                                          norms, dim, n_ptr, cap, dz,
                                                                                          lddz);
   GB_LAUNCH_CHECK();
@@ -488,7 +499,7 @@ void launch_l2norm_bwd(const __nv_bfloat16* y, int64_t ldy, float* dy, const __n
 void launch_add_bf16_rows(float* dst, int64_t ldd, const __nv_bfloat16* src, int64_t lds, int32_t dim,
                           const int32_t* n_ptr, int cap, cudaStream_t stream) {
   if (dim % 8 != 0 || lds % 8 != 0) throw std::invalid_argument("add_bf16_rows: alignment");
-  add_bf16_rows_kernel<<<grid_1d(static_cast<int64_t>(cap) * (dim / 8), 256, 8), 256, 0, stream>>>(dst, ldd, src, lds,
+  launch_k(add_bf16_rows_kernel, grid_1d(static_cast<int64_t>(cap) * (dim / 8), 256, 8), 256, 0, stream, dst, ldd, src, lds,
                                                                                                    dim, n_ptr, cap);
   GB_LAUNCH_CHECK();
 }
@@ -497,7 +508,7 @@ void launch_dropout_rows(const __nv_bfloat16* in, int64_t ldi, __nv_bfloat16* ou
                          int64_t ld_mask, const int32_t* n_ptr, int cap, float p, const int64_t* counters,
                          uint32_t salt, cudaStream_t stream) {
   if (dim % 8 != 0 || ld_mask % 8 != 0) throw std::invalid_argument("dropout_rows: dim and ld_mask % 8");
-  dropout_rows_kernel<<<grid_1d(static_cast<int64_t>(cap) * (dim / 8), 256, 8), 256, 0, stream>>>(
+  launch_k(dropout_rows_kernel, grid_1d(static_cast<int64_t>(cap) * (dim / 8), 256, 8), 256, 0, stream, 
       in, ldi, out, ldo, dim, ld_mask, n_ptr, cap, p, counters, salt);
   GB_LAUNCH_CHECK();
 }
@@ -505,7 +516,7 @@ void launch_dropout_rows(const __nv_bfloat16* in, int64_t ldi, __nv_bfloat16* ou
 void launch_dropout_grad(float* g, int64_t ldg, int32_t dim, int64_t ld_mask, const int32_t* n_ptr, int cap, float p,
                          const int64_t* counters, uint32_t salt, cudaStream_t stream) {
   if (dim % 8 != 0 || ld_mask % 8 != 0) throw std::invalid_argument("dropout_grad: dim and ld_mask % 8");
-  dropout_grad_kernel<<<grid_1d(static_cast<int64_t>(cap) * (dim / 8), 256, 8), 256, 0, stream>>>(
+  launch_k(dropout_grad_kernel, grid_1d(static_cast<int64_t>(cap) * (dim / 8), 256, 8), 256, 0, stream, 
       g, ldg, dim, ld_mask, n_ptr, cap, p, counters, salt);
   GB_LAUNCH_CHECK();
 }
@@ -513,7 +524,7 @@ void launch_dropout_grad(float* g, int64_t ldg, int32_t dim, int64_t ld_mask, co
 void launch_f32_to_bf16_rows(float* src, int64_t lds, __nv_bfloat16* dst, int64_t ldd, int32_t dim,
                              const int32_t* n_ptr, int cap, bool clear, int32_t zero_tail_rows, cudaStream_t stream) {
   if (dim % 8 != 0 || lds % 4 != 0 || ldd % 8 != 0) throw std::invalid_argument("f32_to_bf16_rows: alignment");
-  f32_to_bf16_rows_kernel<<<grid_1d(static_cast<int64_t>(cap) * (dim / 8), 256, 8), 256, 0, stream>>>(
+  launch_k(f32_to_bf16_rows_kernel, grid_1d(static_cast<int64_t>(cap) * (dim / 8), 256, 8), 256, 0, stream, 
       src, lds, dst, ldd, dim, n_ptr, cap, clear, zero_tail_rows);
   GB_LAUNCH_CHECK();
 }

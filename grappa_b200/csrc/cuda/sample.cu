@@ -68,6 +68,7 @@ __device__ void warp_pick_distinct(uint64_t key, uint64_t nid, uint32_t d, uint3
 }
 
 __global__ void __launch_bounds__(kThreads) sample_hop_kernel(SampleHopArgs a) {
+  GB_PDL_ENTRY();
   __shared__ long long s_scan[kWarps];
   __shared__ long long s_off[kTileNodes];
   __shared__ int32_t s_pick[kTileNodes];
@@ -205,7 +206,7 @@ __global__ void __launch_bounds__(kThreads) sample_hop_kernel(SampleHopArgs a) {
 void launch_sample_hop(const SampleHopArgs& a, int cap_dst, cudaStream_t stream) {
   const int tiles = static_cast<int>(ceil_div(cap_dst > 0 ? cap_dst : 1, kTileNodes));
   GB_CUDA_CHECK(cudaMemsetAsync(a.scan_scratch, 0, sizeof(unsigned long long) * (tiles + 1), stream));
-  sample_hop_kernel<<<tiles, kThreads, 0, stream>>>(a);
+  launch_k(sample_hop_kernel, tiles, kThreads, 0, stream, a);
   GB_LAUNCH_CHECK();
 }
 

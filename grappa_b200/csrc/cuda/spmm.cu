@@ -47,6 +47,7 @@ __host__ __device__ __forceinline__ int next_pow2(int x) {
 
 template <int CPL>
 __global__ void __launch_bounds__(kThreads) aggregate_kernel(AggArgs a) {
+  GB_PDL_ENTRY();
   const int n_dst = a.n_dst_ptr ? *a.n_dst_ptr : a.n_dst;
   const int chunks = a.dim >> 3;
   const int lpe = CPL == 1 ? next_pow2(chunks) : 32;  // lanes per edge
@@ -227,6 +228,7 @@ __global__ void __launch_bounds__(kThreads) aggregate_kernel(AggArgs a) {
 
 template <int CPL>
 __global__ void __launch_bounds__(kThreads) aggregate_bwd_kernel(AggBwdArgs a) {
+  GB_PDL_ENTRY();
   const int n_dst = a.n_dst_ptr ? *a.n_dst_ptr : a.n_dst;
   const int chunks = a.dim >> 3;
   const int lpe = CPL == 1 ? next_pow2(chunks) : 32;
@@ -307,6 +309,7 @@ __global__ void __launch_bounds__(kThreads) aggregate_bwd_kernel(AggBwdArgs a) {
 // atomic per column and block.
 template <int CPL>
 __global__ void __launch_bounds__(kThreads) aggregate_bwd_gather_kernel(AggBwdGatherArgs a) {
+  GB_PDL_ENTRY();
   __shared__ float s_col[kThreads / 32][CPL * 256];
   const int n_src = min(*a.n_src_ptr, a.cap_rows);
   const int n_dst = *a.n_dst_ptr;
@@ -411,11 +414,13 @@ __global__ void __launch_bounds__(kThreads) aggregate_bwd_gather_kernel(AggBwdGa
 }
 
 __global__ void out_degree_kernel(const int32_t* indices, const int32_t* n_edges_ptr, float* deg) {
+  GB_PDL_ENTRY();
   const int n_e = *n_edges_ptr;
   for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < n_e; e += gridDim.x * blockDim.x)
     atomicAdd(deg + indices[e], 1.f);
 }
 __global__ void rsqrt_clear_kernel(float* deg, const int32_t* n_ptr, int cap, float* out) {
+  GB_PDL_ENTRY();
   const int n = n_ptr ? *n_ptr : cap;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     const float d = deg[i];
@@ -452,9 +457,9 @@ void launch_aggregate(const AggArgs& args, int cap_dst, cudaStream_t stream) {
   const int rows = a.zero_tail_rows > 0 ? static_cast<int>(ceil_div(cap_dst, a.zero_tail_rows) * a.zero_tail_rows) : cap_dst;
   const int grid = grid_for_rows(rows);
   const int chunks = a.dim / 8;
-  if (chunks <= 32) aggregate_kernel<1><<<grid, kThreads, 0, stream>>>(a);
-  else if (chunks <= 64) aggregate_kernel<2><<<grid, kThreads, 0, stream>>>(a);
-  else if (chunks <= 128) aggregate_kernel<4><<<grid, kThreads, 0, stream>>>(a);
+  if (chunks <= 32) launch_k(aggregate_kernel<1>, grid, kThreads, 0, stream, a);
+  else if (chunks <= 64) launch_k(aggregate_kernel<2>, grid, kThreads, 0, stream, a);
+  else if (chunks <= 128) launch_k(aggregate_kernel<4>, grid, kThreads, 0, stream, a);
   else throw std::invalid_argument("aggregate: dim > 1024 not supported");
   GB_LAUNCH_CHECK();
 }
@@ -463,9 +468,9 @@ void launch_aggregate_bwd(const AggBwdArgs& a, int cap_dst, cudaStream_t stream)
   if (a.dim % 8 != 0 || a.dsrc_stride % 4 != 0) throw std::invalid_argument("aggregate_bwd: bad dim/stride");
   const int grid = grid_for_rows(cap_dst);
   const int chunks = a.dim / 8;
-  if (chunks <= 32) aggregate_bwd_kernel<1><<<grid, kThreads, 0, stream>>>(a);
-  else if (chunks <= 64) aggregate_bwd_kernel<2><<<grid, kThreads, 0, stream>>>(a);
-  else if (chunks <= 128) aggregate_bwd_kernel<4><<<grid, kThreads, 0, stream>>>(a);
+  if (chunks <= 32) launch_k(aggregate_bwd_kernel<1>, grid, kThreads, 0, stream, a);
+  else if (chunks <= 64) launch_k(aggregate_bwd_kernel<2>, grid, kThreads, 0, stream, a);
+  else if (chunks <= 128) launch_k(aggregate_bwd_kernel<4>, grid, kThreads, 0, stream, a);
   else throw std::invalid_argument("aggregate_bwd: dim > 1024 not supported");
   GB_LAUNCH_CHECK();
 }
@@ -476,8 +481,8 @@ void launch_aggregate_bwd_gather(const AggBwdGatherArgs& a, cudaStream_t stream)
     throw std::invalid_argument("aggregate_bwd_gather: dims, strides and columns must be multiples of 8");
   const int grid = grid_for_rows(a.cap_rows);
   const int chunks = a.dim / 8;
-  if (chunks <= 32) aggregate_bwd_gather_kernel<1><<<grid, kThreads, 0, stream>>>(a);
-  else if (chunks <= 64) aggregate_bwd_gather_kernel<2><<<grid, kThreads, 0, stream>>>(a);
+  if (chunks <= 32) launch_k(aggregate_bwd_gather_kernel<1>, grid, kThreads, 0, stream, a);
+  else if (chunks <= 64) launch_k(aggregate_bwd_gather_kernel<2>, grid, kThreads, 0, stream, a);
   else throw std::invalid_argument("aggregate_bwd_gather: dim > 512 not supported");
   GB_LAUNCH_CHECK();
 }
@@ -485,10 +490,10 @@ void launch_aggregate_bwd_gather(const AggBwdGatherArgs& a, cudaStream_t stream)
 void launch_src_norm(const int32_t* indices, const int32_t* n_edges_ptr, int cap_edges, const int32_t* n_src_ptr,
                      int cap_src, float* deg_scratch, float* src_norm, cudaStream_t stream) {
   const int g1 = static_cast<int>(std::min<int64_t>(ceil_div(cap_edges > 0 ? cap_edges : 1, 256), sm_count() * 8));
-  out_degree_kernel<<<g1, 256, 0, stream>>>(indices, n_edges_ptr, deg_scratch);
+  launch_k(out_degree_kernel, g1, 256, 0, stream, indices, n_edges_ptr, deg_scratch);
   GB_LAUNCH_CHECK();
   const int g2 = static_cast<int>(std::min<int64_t>(ceil_div(cap_src > 0 ? cap_src : 1, 256), sm_count() * 8));
-  rsqrt_clear_kernel<<<g2, 256, 0, stream>>>(deg_scratch, n_src_ptr, cap_src, src_norm);
+  launch_k(rsqrt_clear_kernel, g2, 256, 0, stream, deg_scratch, n_src_ptr, cap_src, src_norm);
   GB_LAUNCH_CHECK();
 }
 

@@ -30,6 +30,7 @@ constexpr int kTileNodes = 64;
 constexpr int kMaxK = 32;
 
 __global__ void __launch_bounds__(kThreads) walk_hop_kernel(WalkHopArgs a) {
+  GB_PDL_ENTRY();
   __shared__ long long s_scan[kWarps];
   __shared__ int32_t s_cnt[kTileNodes];
   __shared__ int32_t s_nbr[kTileNodes][kMaxK];
@@ -131,7 +132,7 @@ void launch_walk_hop(const WalkHopArgs& a, int cap_dst, cudaStream_t stream) {
   if (a.num_neighbors <= 0 || a.num_neighbors > kMaxK) throw std::invalid_argument("walk_hop: 1..32 neighbours");
   const int tiles = static_cast<int>(ceil_div(cap_dst > 0 ? cap_dst : 1, kTileNodes));
   GB_CUDA_CHECK(cudaMemsetAsync(a.scan_scratch, 0, sizeof(unsigned long long) * (tiles + 1), stream));
-  walk_hop_kernel<<<tiles, kThreads, 0, stream>>>(a);
+  launch_k(walk_hop_kernel, tiles, kThreads, 0, stream, a);
   GB_LAUNCH_CHECK();
 }
 

@@ -46,6 +46,9 @@ AGG_MEAN, AGG_SUM, AGG_GCN, AGG_WEIGHTED = 0, 1, 2, 3
 # with "x" against 0.93 with "bwd"); "0": the plain z / dz path (for comparisons)
 GAT_INPUT_MODE = os.environ.get("GRAPPA_GAT_INPUT", os.environ.get("GRAPPA_GAT_INPUT_BWD", "auto"))
 GAT_INPUT_LAYER_BWD = GAT_INPUT_MODE != "0"
+# GAT attention logits el / er reduced in the epilogue of the z = x W^T GEMM (1, the
+# default) or by a separate pass over z (0)
+GAT_FUSED_LOGITS = os.environ.get("GRAPPA_GAT_FUSED_LOGITS", "1") != "0"
 # GraphSAGE backward gathered by source over the block transpose (1) or scattered with
 # fp32 reductions plus a separate activation pass (0, the default: the transposes add
 # two kernels per hop to the sampling stream, which measured slower overall)
@@ -407,11 +410,17 @@ class BlockEngine:
                               self.fstats[2:3], self.istats[0:1])
 
     def _gemm(self, A, a_mn, B, b_mn, M_cap, M_dev, N, K_cap, K_dev, splits, C, mode, bias=None, act=0, p=0.0,
-              salt=0, bn=None, act_mask=None, mask_scale=1.0, zero_tail_rows=0):
+              salt=0, bn=None, act_mask=None, mask_scale=1.0, zero_tail_rows=0, att=None):
+        """``att`` = (att_l, att_r, el, er, heads, feat, n_dst): GAT attention logits of
+        the stored bf16 rows reduced into el / er (zeroed by the caller) in the epilogue."""
         bn = bn or gemm_bn(M_cap, N, b_mn)
+        kw = {}
+        if att is not None:
+            kw = dict(att_l=att[0], att_r=att[1], att_el=att[2], att_er=att[3], att_heads=att[4], att_feat=att[5],
+                      att_n_dst=att[6])
         self.cu.gemm(A, a_mn, B, b_mn, M_cap, M_dev, N, K_cap, K_dev, splits, C, mode, bias, act, p,
                      self.counters if p > 0 else None, salt, None, 0, None, None, None, None, None, None, self.err, bn,
-                     act_mask, mask_scale, zero_tail_rows)
+                     act_mask, mask_scale, zero_tail_rows, **kw)
 
     def _dw(self, A, B, M, N, K_cap, K_dev, gW):
         """gW[M, N] += A^T B with A [K, M], B [K, N] (both MN-major), split-K over rows.
@@ -1125,11 +1134,18 @@ class GatEngine(BlockEngine):
             if s["in_x"]:
                 self._input_layer_fwd(s, h, A, p, l)
                 continue
-            self._gemm(A, False, s["W"], False, s["srows"], sm.n_src(h), s["HF"], s["ip"], None, 1, s["Z"],
-                       GEMM_STORE_BF16)
             args = (sm.indptr[h], sm.indices[h], self._n_dst(h), s["rows"], sm.n_src(h), s["srows"], s["H"], s["F"],
                     s["Z"], s["al"], s["ar"], s["el"], s["er"], s["smax"], s["ssum"], 0.2)
-            cu.gat_scores(*args)
+            if GAT_FUSED_LOGITS:
+                # z = x W^T with the attention logits el / er reduced in the GEMM epilogue
+                cu.zero_(s["el"])
+                cu.zero_(s["er"])
+                self._gemm(A, False, s["W"], False, s["srows"], sm.n_src(h), s["HF"], s["ip"], None, 1, s["Z"],
+                           GEMM_STORE_BF16, att=(s["al"], s["ar"], s["el"], s["er"], s["H"], s["F"], self._n_dst(h)))
+            else:
+                self._gemm(A, False, s["W"], False, s["srows"], sm.n_src(h), s["HF"], s["ip"], None, 1, s["Z"],
+                           GEMM_STORE_BF16)
+                cu.gat_scores(*args)
             cu.gat_fwd(*args, s["bias"], s["last"], 0 if s["last"] else 1, p, self.counters if p > 0 else None,
                        l, s["H_out"])
             if s["last"]:
@@ -1219,10 +1235,11 @@ class GatEngine(BlockEngine):
         Hh, ip = s["H"], s["ip"]
         xl, xr = s["xlr"][:Hh * ip], s["xlr"][Hh * ip:]
         cu.zero_(s["xlr"])
+        # no attention-vector gradients here: da_l[hF+f] = sum_u del[u,h] z_u[hF+f] =
+        # W[hF+f] . xl[h], formed by gat_in_dw (the node pass then reads no z rows)
         cu.gat_bwd_input(sm.indptr[h], sm.indices[h], self._n_dst(h), s["rows"], sm.n_src(h), s["srows"], Hh,
                          s["F"], s["Z"], s["al"], s["ar"], s["el"], s["er"], s["smax"], s["ssum"], 0.2, dout,
-                         s["escr"], s["del_"], s["der"], s["gb"], s["gal"], s["gar"], A, ip, s["Yin"], xl, xr,
-                         self.err)
+                         s["escr"], s["del_"], s["der"], s["gb"], None, None, A, ip, s["Yin"], xl, xr, self.err)
         main = torch.cuda.current_stream(self.device)
         aux = self._aux_stream()
         aux.wait_stream(main)
@@ -1231,7 +1248,7 @@ class GatEngine(BlockEngine):
             cu.zero_(s["T"])
             self._gemm(dout, True, s["Yin"], True, s["hfp"], None, Hh * ip, s["rows"], self._n_dst(h),
                        split_k(s["rows"], n_tiles), s["T"], GEMM_ATOMIC_F32, bn=256)
-            cu.gat_dw_combine(s["T"], xl, xr, s["al"], s["ar"], Hh, s["F"], ip, s["gW"])
+            cu.gat_in_dw(s["T"], xl, xr, s["al"], s["ar"], s["W32"], Hh, s["F"], ip, s["gW"], s["gal"], s["gar"])
         self._aux_used = True
 
 

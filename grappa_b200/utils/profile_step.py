@@ -51,9 +51,12 @@ def main():
     name, hidden, fanouts = WORKLOADS[a.workload]
     dev = torch.device("cuda", 0)
     spec = S.SPECS[a.config]
-    g = S.build(spec, dev)
-    own = partition_from_global(g, 1, 0, dev, part_seed=spec.seed)
-    del g
+    if spec.n_nodes >= S.LEAN_MIN_NODES:
+        own = S.build_partition(spec, 1, 0, dev)  # graphs of 100M+ nodes: built without the global copy
+    else:
+        g = S.build(spec, dev)
+        own = partition_from_global(g, 1, 0, dev, part_seed=spec.seed)
+        del g
     torch.cuda.empty_cache()
     torch.manual_seed(0)
     model = get_model(name, spec.feat_dim, spec.n_classes, num_hidden=hidden, num_layers=3, dropout=0.5, n_heads=4)

@@ -154,6 +154,34 @@ def test_gemm_activation_backward_epilogue(cap, live, N, K, bn):
     assert bool((C[tail:] == 7.0).all())
 
 
+@pytest.mark.parametrize("M,live,n_dst,H,F_,K,bn", [(4096, 3000, 700, 4, 64, 128, 256), (1024, 1000, 1000, 4, 172, 256, 256),
+                                                   (700, 650, 90, 3, 24, 104, 64)])
+def test_gemm_attention_logit_epilogue(M, live, n_dst, H, F_, K, bn):
+    """z = x W^T stored bf16 with the GAT logits in the epilogue: el[m, h] = z[m, h] . a_l[h]
+    for live rows, er the same with a_r for the first n_dst rows, from the stored values
+    (heads of 172 columns straddle the 32-column chunks and the 256-column tiles)."""
+    torch.manual_seed(6)
+    N = H * F_
+    A = bf(torch.randn(M, K, device=DEV))
+    B = bf(torch.randn(N, K, device=DEV) / math.sqrt(K))
+    al, ar = torch.randn(N, device=DEV), torch.randn(N, device=DEV)
+    C = torch.zeros((M, N), dtype=torch.bfloat16, device=DEV)
+    el, er = torch.zeros(M * H, device=DEV), torch.zeros(M * H, device=DEV)
+    m_dev = torch.tensor([live], dtype=torch.int32, device=DEV)
+    nd = torch.tensor([n_dst], dtype=torch.int32, device=DEV)
+    err = err_tensor()
+    cu().gemm(A, False, B, False, M, m_dev, N, K, None, 1, C, 0, None, 0, 0.0, None, 0, None, 0, None, None, None,
+              None, None, None, err, bn, att_l=al, att_r=ar, att_el=el, att_er=er, att_heads=H, att_feat=F_,
+              att_n_dst=nd)
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    z = C[:live].float().view(live, H, F_)
+    torch.testing.assert_close(C[:live].float(), A[:live].float() @ B.float().t(), rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(el.view(M, H)[:live], (z * al.view(H, F_)).sum(-1), rtol=1e-3, atol=1e-3)
+    torch.testing.assert_close(er.view(M, H)[:n_dst], (z[:n_dst] * ar.view(H, F_)).sum(-1), rtol=1e-3, atol=1e-3)
+    assert bool((el.view(M, H)[live:] == 0).all()) and bool((er.view(M, H)[n_dst:] == 0).all())
+
+
 @pytest.mark.parametrize("Mo,Kx,R,live,splits", [(48, 208, 700, 650, 3), (256, 512, 4096, 4000, 8),
                                                  (256, 208, 130, 100, 1), (1024, 1024, 8192, 8000, 4)])
 def test_gemm_dw_mn_major_split_k(Mo, Kx, R, live, splits):
