@@ -83,7 +83,9 @@ void sample_hop(Tensor indptr, Tensor indices, Tensor dst_nid, OptT n_dst_dev, i
   TORCH_CHECK(dst_nid.numel() >= cap_dst, "dst_nid smaller than cap_dst");
   TORCH_CHECK(!a.frontier || frontier->numel() >= cap_dst, "frontier smaller than cap_dst");
   TORCH_CHECK(!a.gideg || gideg->numel() >= cap_dst, "gideg smaller than cap_dst");
-  TORCH_CHECK(scan_scratch.numel() >= d::sample_scan_scratch_words(static_cast<int>(cap_dst)), "scan_scratch too small");
+  // exactly sized: the scan numbers its launches by the grid size (common.cuh LookBack)
+  TORCH_CHECK(scan_scratch.numel() == d::sample_scan_scratch_words(static_cast<int>(cap_dst)),
+              "scan_scratch must hold exactly sample_scratch_words(capacity) words and be used with that capacity only");
   if (map.has_value()) {
     TORCH_CHECK(src_nid.has_value() && src_sampled.has_value(), "fused compaction needs map, src_nid and src_sampled");
     TORCH_CHECK(counters.numel() >= 6 && hop >= 0 && hop < 16, "fused compaction: counters[4] and hop slot");
@@ -125,7 +127,9 @@ void compact(Tensor dst_nid, Tensor n_dst_dev, Tensor nbr, Tensor n_edges_dev, T
               "the transpose counters need t_cnt[cap_src] and t_rank[cap_edges]");
   TORCH_CHECK(nbr.numel() >= cap_edges && indices.numel() >= cap_edges, "edge buffers smaller than cap_edges");
   TORCH_CHECK(dst_nid.numel() >= cap_dst && a.cap_src >= cap_dst, "dst/src buffers smaller than cap_dst");
-  TORCH_CHECK(scan_scratch.numel() >= d::compact_scan_scratch_words(static_cast<int>(cap_edges)), "scan_scratch too small");
+  // exactly sized: the scan numbers its launches by the grid size (common.cuh LookBack)
+  TORCH_CHECK(scan_scratch.numel() == d::compact_scan_scratch_words(static_cast<int>(cap_edges)),
+              "scan_scratch must hold exactly compact_scratch_words(capacity) words and be used with that capacity only");
   const int64_t* gen = ptr<int64_t>(counters, at::kLong, "counters") + 4;
   d::launch_compact(a, static_cast<int>(cap_dst), static_cast<int>(cap_edges), gen, static_cast<int>(slot), num_sms(),
                     stream(), k1_done);
@@ -1053,7 +1057,9 @@ void walk_hop(Tensor indptr, Tensor indices, Tensor dst_nid, OptT n_dst_dev, int
   a.scan_scratch = reinterpret_cast<unsigned long long*>(ptr<int64_t>(scan_scratch, at::kLong, "scan_scratch"));
   a.err = ptr<int32_t>(err, at::kInt, "err");
   TORCH_CHECK(out_indptr.numel() >= cap_dst + 1 && dst_nid.numel() >= cap_dst, "walk_hop: buffers smaller than cap_dst");
-  TORCH_CHECK(scan_scratch.numel() >= d::walk_scan_scratch_words(static_cast<int>(cap_dst)), "scan_scratch too small");
+  // exactly sized: the scan numbers its launches by the grid size (common.cuh LookBack)
+  TORCH_CHECK(scan_scratch.numel() == d::walk_scan_scratch_words(static_cast<int>(cap_dst)),
+              "scan_scratch must hold exactly walk_scratch_words(capacity) words and be used with that capacity only");
   d::launch_walk_hop(a, static_cast<int>(cap_dst), stream());
 }
 

@@ -134,39 +134,64 @@ __device__ __forceinline__ T block_exclusive_scan(T v, T* smem, T* total) {
 // (1 aggregate, 2 inclusive prefix), bits 61..0 = value.  The caller zeroes the
 // scratch before the launch.  Waits are bounded: after kSpinLimit polls the tile
 // records kErrScanTimeout and proceeds with what it has.
+// Decoupled look-back scan over the tiles of one launch.  scratch[0] is a ticket
+// counter that is never reset: the CTAs of a launch take consecutive tickets (every CTA
+// takes exactly one, and a launch starts after the previous one on its stream has
+// finished), so ticket / gridDim.x numbers the launch and ticket % gridDim.x is the
+// tile.  Tile t's status word scratch[1 + t] = flag (2 bits) | launch tag (30 bits) |
+// value (32 bits); a word whose tag is not this launch's is not ready.  So the scratch
+// needs no clearing between launches (no memset node in a captured step); clearing it
+// (tag 0, flag 0) is also valid.  The same grid size must be used with one scratch.
 struct LookBack {
   static constexpr unsigned long long kAgg = 1ull << 62;
   static constexpr unsigned long long kPre = 2ull << 62;
-  static constexpr unsigned long long kMask = (1ull << 62) - 1;
+  static constexpr unsigned long long kTagMask = (1ull << 30) - 1;
+  static constexpr unsigned long long kValMask = 0xFFFFFFFFull;
   static constexpr int kSpinLimit = 1 << 20;
 
-  __device__ static int ticket(unsigned long long* scratch, int* smem_slot) {
-    if (threadIdx.x == 0) *smem_slot = static_cast<int>(atomicAdd(scratch, 1ull));
+  struct Ticket {
+    int tile;
+    unsigned long long tag;
+  };
+
+  // smem_slot: two ints of shared memory
+  __device__ static Ticket ticket(unsigned long long* scratch, int* smem_slot) {
+    if (threadIdx.x == 0) {
+      const unsigned long long t = atomicAdd(scratch, 1ull);
+      smem_slot[0] = static_cast<int>(t % gridDim.x);
+      smem_slot[1] = static_cast<int>((t / gridDim.x) & kTagMask);
+    }
     __syncthreads();
-    return *smem_slot;
+    return {smem_slot[0], static_cast<unsigned long long>(smem_slot[1])};
   }
 
-  // Called by all lanes of warp 0.  Returns the exclusive prefix of tile t.
-  __device__ static long long exclusive_prefix(unsigned long long* scratch, int t, long long agg,
+  __device__ static unsigned long long word(unsigned long long flag, unsigned long long tag, long long v) {
+    return flag | (tag << 32) | (static_cast<unsigned long long>(v) & kValMask);
+  }
+
+  // Called by all lanes of warp 0.  Returns the exclusive prefix of tile tk.tile (values
+  // below 2^32).
+  __device__ static long long exclusive_prefix(unsigned long long* scratch, Ticket tk, long long agg,
                                                int32_t* err) {
     unsigned long long* status = scratch + 1;
+    const int t = tk.tile;
     if (t == 0) {
-      if (lane_id() == 0) st_release_u64(status, kPre | (static_cast<unsigned long long>(agg) & kMask));
+      if (lane_id() == 0) st_release_u64(status, word(kPre, tk.tag, agg));
       return 0;
     }
-    if (lane_id() == 0) st_release_u64(status + t, kAgg | (static_cast<unsigned long long>(agg) & kMask));
+    if (lane_id() == 0) st_release_u64(status + t, word(kAgg, tk.tag, agg));
     long long prefix = 0;
     int j = t - 1;
     while (j >= 0) {
       const int idx = j - static_cast<int>(lane_id());
-      unsigned long long s = kPre;  // lanes past tile 0 act as a zero prefix
+      unsigned long long s = kPre | (tk.tag << 32);  // lanes past tile 0 act as a zero prefix
       if (idx >= 0) {
         int spins = 0;
         s = ld_acquire_u64(status + idx);
-        while ((s >> 62) == 0) {
+        while ((s >> 62) == 0 || ((s >> 32) & kTagMask) != tk.tag) {
           if (++spins > kSpinLimit) {
             set_error(err, kErrScanTimeout);
-            s = kPre;
+            s = kPre | (tk.tag << 32);
             break;
           }
           if (spins > 64) __nanosleep(32);
@@ -175,13 +200,12 @@ struct LookBack {
       }
       const uint32_t pre_mask = __ballot_sync(0xffffffffu, (s >> 62) == 2);
       const int first_pre = pre_mask ? __ffs(pre_mask) - 1 : 32;  // nearest prefix lane
-      long long v = (static_cast<int>(lane_id()) <= first_pre && idx >= 0) ? static_cast<long long>(s & kMask) : 0;
+      long long v = (static_cast<int>(lane_id()) <= first_pre && idx >= 0) ? static_cast<long long>(s & kValMask) : 0;
       prefix += warp_sum(v);
       if (pre_mask) break;
       j -= 32;
     }
-    if (lane_id() == 0)
-      st_release_u64(status + t, kPre | (static_cast<unsigned long long>(prefix + agg) & kMask));
+    if (lane_id() == 0) st_release_u64(status + t, word(kPre, tk.tag, prefix + agg));
     return prefix;
   }
 };

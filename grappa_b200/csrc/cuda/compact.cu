@@ -64,9 +64,10 @@ __global__ void __launch_bounds__(kThreads) compact_k1(CompactArgs a, const int6
 __global__ void __launch_bounds__(kThreads) compact_k2(CompactArgs a, const int64_t* gen, int slot) {
   GB_PDL_ENTRY();
   __shared__ long long s_scan[kThreads / 32];
-  __shared__ int s_tile;
+  __shared__ int s_tile[2];
   __shared__ long long s_prefix;
-  const int tile = LookBack::ticket(a.scan_scratch, &s_tile);
+  const LookBack::Ticket tk = LookBack::ticket(a.scan_scratch, s_tile);
+  const int tile = tk.tile;
   const int n_dst = *a.n_dst_ptr;
   const int n_e = *a.n_edges_ptr;
   // capacity-sized grid: tiles past the last live one leave before the scan
@@ -94,7 +95,7 @@ __global__ void __launch_bounds__(kThreads) compact_k2(CompactArgs a, const int6
   long long total;
   const long long excl = block_exclusive_scan<kThreads, long long>(cnt, s_scan, &total);
   if ((threadIdx.x >> 5) == 0) {
-    const long long p = LookBack::exclusive_prefix(a.scan_scratch, tile, total, a.err);
+    const long long p = LookBack::exclusive_prefix(a.scan_scratch, tk, total, a.err);
     if (lane_id() == 0) s_prefix = p;
   }
   __syncthreads();
@@ -211,7 +212,7 @@ void launch_compact(const CompactArgs& a, int cap_dst, int cap_edges, const int6
     GB_LAUNCH_CHECK();
   }
   const int tiles = static_cast<int>(ceil_div(cap_edges > 0 ? cap_edges : 1, kTile));
-  GB_CUDA_CHECK(cudaMemsetAsync(a.scan_scratch, 0, sizeof(unsigned long long) * (tiles + 1), stream));
+  // no clearing of the scan scratch: its look-back words carry the launch number
   launch_k(compact_k2, tiles, kThreads, 0, stream, a, gen, slot);
   GB_LAUNCH_CHECK();
   const int g3 = static_cast<int>(std::min<long long>(grid_stride, ceil_div(cap_edges > 0 ? cap_edges : 1, kThreads)));

@@ -185,9 +185,10 @@ __global__ void __launch_bounds__(kMcThreads) mark_compact_kernel(uint8_t* mark,
                                                                    unsigned long long* scratch, int64_t cap_out,
                                                                    int32_t* err) {
   __shared__ long long s_scan[kMcThreads / 32];
-  __shared__ int s_tile;
+  __shared__ int s_tile[2];
   __shared__ long long s_prefix;
-  const int tile = dev::LookBack::ticket(scratch, &s_tile);
+  const dev::LookBack::Ticket tk = dev::LookBack::ticket(scratch, s_tile);
+  const int tile = tk.tile;
   const int64_t g0 = static_cast<int64_t>(tile) * kMcTile + threadIdx.x * kMcItems;
   uint32_t bits = 0;
   int cnt = 0;
@@ -202,7 +203,7 @@ __global__ void __launch_bounds__(kMcThreads) mark_compact_kernel(uint8_t* mark,
   long long total;
   const long long excl = dev::block_exclusive_scan<kMcThreads, long long>(cnt, s_scan, &total);
   if ((threadIdx.x >> 5) == 0) {
-    const long long p = dev::LookBack::exclusive_prefix(scratch, tile, total, err);
+    const long long p = dev::LookBack::exclusive_prefix(scratch, tk, total, err);
     if (dev::lane_id() == 0) s_prefix = p;
   }
   __syncthreads();

@@ -76,11 +76,12 @@ __global__ void __launch_bounds__(kThreads) sample_hop_kernel(SampleHopArgs a) {
   __shared__ long long s_beg[kTileNodes];
   __shared__ long long s_deg[kTileNodes];
   __shared__ int32_t s_acc[kWarps][kSmemAcc];
-  __shared__ int s_tile;
+  __shared__ int s_tile[2];
   __shared__ long long s_prefix;
   __shared__ float s_cov[2][kWarps];
 
-  const int tile = LookBack::ticket(a.scan_scratch, &s_tile);
+  const LookBack::Ticket tk = LookBack::ticket(a.scan_scratch, s_tile);
+  const int tile = tk.tile;
   const int n_dst = a.n_dst_ptr ? *a.n_dst_ptr : a.n_dst;
   // the grid is sized by the capacity; tiles past the last live one take no part in
   // the scan (no live tile waits on them), so they leave at once
@@ -133,7 +134,7 @@ __global__ void __launch_bounds__(kThreads) sample_hop_kernel(SampleHopArgs a) {
   long long total;
   const long long excl = block_exclusive_scan<kThreads, long long>(pick, s_scan, &total);
   if ((threadIdx.x >> 5) == 0) {
-    const long long p = LookBack::exclusive_prefix(a.scan_scratch, tile, total, a.err);
+    const long long p = LookBack::exclusive_prefix(a.scan_scratch, tk, total, a.err);
     if (lane_id() == 0) s_prefix = p;
     if (a.gideg && a.cov_accum && lane_id() < 2) {
       float s = 0.f;
@@ -205,7 +206,7 @@ __global__ void __launch_bounds__(kThreads) sample_hop_kernel(SampleHopArgs a) {
 
 void launch_sample_hop(const SampleHopArgs& a, int cap_dst, cudaStream_t stream) {
   const int tiles = static_cast<int>(ceil_div(cap_dst > 0 ? cap_dst : 1, kTileNodes));
-  GB_CUDA_CHECK(cudaMemsetAsync(a.scan_scratch, 0, sizeof(unsigned long long) * (tiles + 1), stream));
+  // no clearing of the scan scratch: its look-back words carry the launch number
   launch_k(sample_hop_kernel, tiles, kThreads, 0, stream, a);
   GB_LAUNCH_CHECK();
 }

@@ -36,10 +36,11 @@ __global__ void __launch_bounds__(kThreads) walk_hop_kernel(WalkHopArgs a) {
   __shared__ int32_t s_nbr[kTileNodes][kMaxK];
   __shared__ float s_w[kTileNodes][kMaxK];
   __shared__ int32_t s_visit[kWarps][32];
-  __shared__ int s_tile;
+  __shared__ int s_tile[2];
   __shared__ long long s_prefix;
 
-  const int tile = LookBack::ticket(a.scan_scratch, &s_tile);
+  const LookBack::Ticket tk = LookBack::ticket(a.scan_scratch, s_tile);
+  const int tile = tk.tile;
   const int n_dst = a.n_dst_ptr ? *a.n_dst_ptr : a.n_dst;
   // capacity-sized grid: tiles past the last live one leave before the scan
   const int last_tile = n_dst > 0 ? (n_dst - 1) / kTileNodes : 0;
@@ -98,7 +99,7 @@ __global__ void __launch_bounds__(kThreads) walk_hop_kernel(WalkHopArgs a) {
   long long total;
   const long long excl = block_exclusive_scan<kThreads, long long>(my_cnt, s_scan, &total);
   if (w == 0) {
-    const long long p = LookBack::exclusive_prefix(a.scan_scratch, tile, total, a.err);
+    const long long p = LookBack::exclusive_prefix(a.scan_scratch, tk, total, a.err);
     if (lane == 0) s_prefix = p;
   }
   __syncthreads();
@@ -131,7 +132,7 @@ void launch_walk_hop(const WalkHopArgs& a, int cap_dst, cudaStream_t stream) {
     throw std::invalid_argument("walk_hop: num_walks * length must be in [1, 32]");
   if (a.num_neighbors <= 0 || a.num_neighbors > kMaxK) throw std::invalid_argument("walk_hop: 1..32 neighbours");
   const int tiles = static_cast<int>(ceil_div(cap_dst > 0 ? cap_dst : 1, kTileNodes));
-  GB_CUDA_CHECK(cudaMemsetAsync(a.scan_scratch, 0, sizeof(unsigned long long) * (tiles + 1), stream));
+  // no clearing of the scan scratch: its look-back words carry the launch number
   launch_k(walk_hop_kernel, tiles, kThreads, 0, stream, a);
   GB_LAUNCH_CHECK();
 }
