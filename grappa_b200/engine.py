@@ -46,9 +46,10 @@ AGG_MEAN, AGG_SUM, AGG_GCN, AGG_WEIGHTED = 0, 1, 2, 3
 # with "x" against 0.93 with "bwd"); "0": the plain z / dz path (for comparisons)
 GAT_INPUT_MODE = os.environ.get("GRAPPA_GAT_INPUT", os.environ.get("GRAPPA_GAT_INPUT_BWD", "auto"))
 GAT_INPUT_LAYER_BWD = GAT_INPUT_MODE != "0"
-# GAT attention logits el / er reduced in the epilogue of the z = x W^T GEMM (1, the
-# default) or by a separate pass over z (0)
-GAT_FUSED_LOGITS = os.environ.get("GRAPPA_GAT_FUSED_LOGITS", "1") != "0"
+# GAT attention logits el / er reduced in the epilogue of the z = x W^T GEMM (1) or by
+# a separate pass over z (0, the default: the longer GEMM epilogue measured 0.977
+# s/epoch on the 111M-node workload against 0.923 with the separate pass)
+GAT_FUSED_LOGITS = os.environ.get("GRAPPA_GAT_FUSED_LOGITS", "0") != "0"
 # GraphSAGE backward gathered by source over the block transpose (1) or scattered with
 # fp32 reductions plus a separate activation pass (0, the default: the transposes add
 # two kernels per hop to the sampling stream, which measured slower overall)
