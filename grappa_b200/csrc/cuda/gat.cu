@@ -910,19 +910,26 @@ __global__ void gat_in_dw_kernel(const float* T, int64_t ldt, const float* xl, c
   GB_PDL_ENTRY();
   const int HF = H * F;
   const int total = HF * IN;
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total + HF; i += gridDim.x * blockDim.x) {
-    if (i < total) {
-      const int r = i / IN, k = i % IN, h = r / F;
-      dw[static_cast<int64_t>(r) * ldw + k] +=
-          T[static_cast<int64_t>(r) * ldt + h * IN + k] + attn_l[r] * xl[h * IN + k] + attn_r[r] * xr[h * IN + k];
-    } else {
-      const int r = i - total, h = r / F;
-      float tl = 0.f, tr = 0.f;
-      for (int k = 0; k < IN; ++k) {
-        const float wv = w[static_cast<int64_t>(r) * ldw_in + k];
-        tl = fmaf(wv, xl[h * IN + k], tl);
-        tr = fmaf(wv, xr[h * IN + k], tr);
-      }
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int r = i / IN, k = i % IN, h = r / F;
+    dw[static_cast<int64_t>(r) * ldw + k] +=
+        T[static_cast<int64_t>(r) * ldt + h * IN + k] + attn_l[r] * xl[h * IN + k] + attn_r[r] * xr[h * IN + k];
+  }
+  if (!dattn_l && !dattn_r) return;
+  // da_l[r] += W[r, :] . xl[h], one warp per row (lanes split the row, then a warp sum)
+  const int lane = threadIdx.x & 31;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  for (int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < HF; r += warps) {
+    const int h = r / F;
+    float tl = 0.f, tr = 0.f;
+    for (int k = lane; k < IN; k += 32) {
+      const float wv = w[static_cast<int64_t>(r) * ldw_in + k];
+      tl = fmaf(wv, xl[h * IN + k], tl);
+      tr = fmaf(wv, xr[h * IN + k], tr);
+    }
+    tl = warp_sum(tl);
+    tr = warp_sum(tr);
+    if (lane == 0) {
       if (dattn_l) dattn_l[r] += tl;
       if (dattn_r) dattn_r[r] += tr;
     }
@@ -1043,7 +1050,7 @@ void launch_gat_in_prep(const __nv_bfloat16* w, int64_t ldw, const float* attn_l
 void launch_gat_in_dw(const float* T, int64_t ldt, const float* xl, const float* xr, const float* attn_l,
                       const float* attn_r, const float* w, int64_t ldw_in, int heads, int feat, int in_dim, float* dw,
                       int64_t ldw, float* dattn_l, float* dattn_r, cudaStream_t stream) {
-  const int total = heads * feat * in_dim + heads * feat;
+  const int total = std::max(heads * feat * in_dim, heads * feat * 32);
   const int grid = std::max(1, std::min((total + 255) / 256, sms() * 4));
   launch_k(gat_in_dw_kernel, grid, 256, 0, stream, T, ldt, xl, xr, attn_l, attn_r, w, ldw_in, heads, feat, in_dim, dw, ldw,
                                              dattn_l, dattn_r);
