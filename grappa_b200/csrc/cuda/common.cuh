@@ -34,12 +34,13 @@ enum : int32_t {
 // attribute the wait is a no-op.
 #define GB_PDL_ENTRY() asm volatile("griddepcontrol.wait;" ::: "memory")
 
-// PDL launches only with GRAPPA_PDL=1 (read once per process; measured no faster in
-// the captured training steps)
+// PDL launches unless GRAPPA_PDL=0 (read once per process).  Wait-only PDL measured
+// 0.0399 against 0.0410 s/epoch on the GraphSAGE workload and 0.904 against 0.928 on
+// GAT; triggering at kernel entry was slower than no PDL.
 inline bool pdl_enabled() {
   static const bool on = [] {
     const char* e = std::getenv("GRAPPA_PDL");
-    return e && e[0] == '1';
+    return !(e && e[0] == '0');
   }();
   return on;
 }
