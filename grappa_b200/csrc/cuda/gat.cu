@@ -33,6 +33,8 @@
 // a GEMM forms dout^T y and gat_dw_combine adds its diagonal head blocks and the two
 // rank-1 terms into dW.
 #include <algorithm>
+#include <cstdlib>
+#include <string>
 
 #include "common.cuh"
 #include "grappa/rng.h"
@@ -199,9 +201,11 @@ __device__ __forceinline__ float pick_head(const float (&v)[HM], int h) {
   return r;
 }
 
-// HM: the head count rounded up to 4 or kMaxHeads (sizes the per-head register arrays)
-template <int CPL, int HM>
-__global__ void __launch_bounds__(kThreads) gat_fwd_kernel(GatArgs a) {
+// HM: the head count rounded up to 4 or kMaxHeads (sizes the per-head register arrays);
+// EU_: edges whose z rows are in flight together (0: 4 for CPL 1, else 2); MINB: CTAs
+// per SM the registers are capped for (occupancy against registers per lane)
+template <int CPL, int HM, int EU_ = 0, int MINB = 1>
+__global__ void __launch_bounds__(kThreads, MINB) gat_fwd_kernel(GatArgs a) {
   GB_PDL_ENTRY();
   extern __shared__ float s_row[];  // mean_heads: [warps][HF]
   __shared__ float s_w[kThreads / 32][32][HM];  // the batch's edge weights, per head
@@ -222,7 +226,7 @@ __global__ void __launch_bounds__(kThreads) gat_fwd_kernel(GatArgs a) {
     thr = static_cast<uint32_t>(static_cast<double>(a.dropout_p) * 4294967296.0);
     ks = 1.f / (1.f - a.dropout_p);
   }
-  constexpr int EU = CPL <= 1 ? 4 : 2;  // edges whose z rows are in flight together
+  constexpr int EU = EU_ > 0 ? EU_ : (CPL <= 1 ? 4 : 2);  // edges whose z rows are in flight together
   int h0[CPL], h1[CPL];
   uint32_t in0[CPL];  // bit j: column c0 + j belongs to head h0 (else to h1)
 #pragma unroll
@@ -466,8 +470,9 @@ __device__ __forceinline__ float edge_head_dot(const float (&go)[CPL][8], const 
 template <int CPL, int CPLY>
 constexpr int bwd_min_blocks() { return CPL + CPLY <= 3 ? 2 : 1; }
 
-template <int CPL, int CPLY, bool SEG>
-__global__ void __launch_bounds__(kThreads, bwd_min_blocks<CPL, CPLY>()) gat_bwd_edge_kernel(GatArgs a) {
+// MINB > 0: registers capped for MINB CTAs per SM (the occupancy variants)
+template <int CPL, int CPLY, bool SEG, int MINB = 0>
+__global__ void __launch_bounds__(kThreads, MINB > 0 ? MINB : bwd_min_blocks<CPL, CPLY>()) gat_bwd_edge_kernel(GatArgs a) {
   GB_PDL_ENTRY();
   const int n_dst = a.n_dst_ptr ? min(*a.n_dst_ptr, a.cap_dst) : a.cap_dst;
   const int H = a.heads, F = a.feat, HF = H * F;
@@ -690,8 +695,8 @@ __global__ void __launch_bounds__(kThreads, bwd_min_blocks<CPL, CPLY>()) gat_bwd
 // da_r += der z.  del is cleared for the next step after its rows are consumed.
 constexpr int kNodeRows = 4;
 
-template <int CPL, int CPLY, bool SEG>
-__global__ void __launch_bounds__(kThreads, 1) gat_bwd_node_kernel(GatArgs a) {
+template <int CPL, int CPLY, bool SEG, int MINB = 0>
+__global__ void __launch_bounds__(kThreads, MINB > 0 ? MINB : 1) gat_bwd_node_kernel(GatArgs a) {
   GB_PDL_ENTRY();
   const int n_src = a.n_src_ptr ? min(*a.n_src_ptr, a.cap_src) : a.cap_src;
   const int n_dst = a.n_dst_ptr ? min(*a.n_dst_ptr, a.cap_dst) : a.cap_dst;
@@ -972,6 +977,17 @@ void check(const GatArgs& a) {
     GB_LAUNCH_CHECK();                                                                 \
   } while (0)
 
+// GRAPPA_GAT_OCC = 2 or 3: the forward (3 CTAs per SM) and the backward node pass (2;
+// with 3 also the edge pass) of the common shapes (one 8-column chunk per lane) capped
+// in registers for occupancy; 0 (default): the registers the compiler picks
+static int gat_occ() {
+  static const int v = [] {
+    const char* e = std::getenv("GRAPPA_GAT_OCC");
+    return e ? std::atoi(e) : 0;
+  }();
+  return v;
+}
+
 void launch_gat_scores(const GatArgs& a, cudaStream_t stream) {
   check(a);
   GAT_DISPATCH(gat_scores_kernel, grid_warps(a.cap_src), 0);
@@ -989,7 +1005,22 @@ void launch_gat_fwd(const GatArgs& a, cudaStream_t stream) {
     if (a.heads <= 4) launch_k(gat_fwd_kernel<C, 4>, grid, kThreads, smem, stream, a);        \
     else launch_k(gat_fwd_kernel<C, kMaxHeads>, grid, kThreads, smem, stream, a);            \
   } while (0)
-  if (cpl <= 1) GAT_FWD(1);
+  // variants of the common case (<= 4 heads, H * F <= 256) picked by GRAPPA_GAT_FWD
+  // ("eu,minb": 4,1 default; 8,1; 4,3; 8,2)
+  static const int variant = [] {
+    const char* e = std::getenv("GRAPPA_GAT_FWD");
+    if (!e) return 0;
+    const std::string v(e);
+    return v == "8,1" ? 1 : v == "4,3" ? 2 : v == "8,2" ? 3 : 0;
+  }();
+  const int occ = gat_occ();
+  if (cpl <= 1 && a.heads <= 4 && variant > 0) {
+    if (variant == 1) launch_k(gat_fwd_kernel<1, 4, 8, 1>, grid, kThreads, smem, stream, a);
+    else if (variant == 2) launch_k(gat_fwd_kernel<1, 4, 4, 3>, grid, kThreads, smem, stream, a);
+    else launch_k(gat_fwd_kernel<1, 4, 8, 2>, grid, kThreads, smem, stream, a);
+  } else if (cpl <= 1 && a.heads <= 4 && occ >= 2) {
+    launch_k(gat_fwd_kernel<1, 4, 4, 3>, grid, kThreads, smem, stream, a);  // 80 registers, 3 CTAs per SM
+  } else if (cpl <= 1) GAT_FWD(1);
   else if (cpl <= 2) GAT_FWD(2);
   else GAT_FWD(4);
 #undef GAT_FWD
@@ -998,13 +1029,27 @@ void launch_gat_fwd(const GatArgs& a, cudaStream_t stream) {
 
 bool seg_heads(int F) { return F >= 8 && F <= 256 && (F & (F - 1)) == 0; }
 
+// EMB / NMB: CTAs per SM the edge / node pass registers are capped for (0: default)
+template <int CPL, int CPLY, bool SEG, int EMB, int NMB>
+void gat_bwd_launch(const GatArgs& a, cudaStream_t stream) {
+  constexpr int mb = EMB > 0 ? EMB : bwd_min_blocks<CPL, CPLY>();
+  launch_k(gat_bwd_edge_kernel<CPL, CPLY, SEG, EMB>, grid_warps(a.cap_dst, mb), kThreads, 0, stream, a);
+  GB_LAUNCH_CHECK();
+  launch_k(gat_bwd_node_kernel<CPL, CPLY, SEG, NMB>,
+           grid_warps(static_cast<int>(ceil_div(a.cap_src, kNodeRows)), NMB > 0 ? NMB : 1), kThreads, 0, stream, a);
+  GB_LAUNCH_CHECK();
+}
+
 template <int CPL, int CPLY, bool SEG>
 void gat_bwd_pair(const GatArgs& a, cudaStream_t stream) {
-  constexpr int mb = bwd_min_blocks<CPL, CPLY>();
-  launch_k(gat_bwd_edge_kernel<CPL, CPLY, SEG>, grid_warps(a.cap_dst, mb), kThreads, 0, stream, a);
-  GB_LAUNCH_CHECK();
-  launch_k(gat_bwd_node_kernel<CPL, CPLY, SEG>, grid_warps(static_cast<int>(ceil_div(a.cap_src, kNodeRows)), 1), kThreads, 0, stream, a);
-  GB_LAUNCH_CHECK();
+  // one 8-column chunk per lane: the node pass capped for 2 CTAs per SM (128 registers
+  // instead of 178-184); with GRAPPA_GAT_OCC=3 both passes for 3
+  if constexpr (CPL == 1 && SEG && (CPLY == 0 || CPLY == 2)) {
+    const int occ = gat_occ();
+    if (occ == 2) return gat_bwd_launch<CPL, CPLY, SEG, 0, 2>(a, stream);
+    if (occ >= 3) return gat_bwd_launch<CPL, CPLY, SEG, 3, 3>(a, stream);
+  }
+  gat_bwd_launch<CPL, CPLY, SEG, 0, 0>(a, stream);
 }
 
 template <int CPLY>

@@ -180,7 +180,9 @@ class PartitionStore:
         sz = self._sizes
         n_r, n_q = own.n_nodes, sz[q]["n"]
         peer = self._peer
-        ev = [torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
+        # events: start, marks + halo compaction, CSR merge, halo rows, end (main stream);
+        # feature-copy start and end (side stream)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
         ev[0].record()
         # q's feature rows (the largest transfer, independent of the CSR and halo work)
         # stream over NVLink on a side stream while the marks, the CSR merge and the halo
@@ -192,30 +194,36 @@ class PartitionStore:
             self._side = torch.cuda.Stream(device=self.device)
         self._side.wait_stream(main)
         with torch.cuda.stream(self._side):
+            ev[5].record()
             if not getattr(self, "_own_rows_in", False):
                 self._feat_w[:n_r].copy_(own.feat)
                 self._own_rows_in = True
             cu.peer_copy(self._feat_w.data_ptr() + n_r * fs * esz, peer["feat"].ptrs[q], n_q * fs * esz)
+            ev[6].record()
         # 1. halo = (ext_r U ext_q) \ (V_r U V_q), found by marking a dense global-id array
         cu.mark_ids(peer["ext"].ptrs[r], None, sz[r]["ext"], self._mark)
         cu.mark_ids(peer["ext"].ptrs[q], None, sz[q]["ext"], self._mark)
         cu.iota_map(self._map, own.prefix[r], n_r, 0, self._mark)
         cu.iota_map(self._map, own.prefix[q], n_q, n_r, self._mark)
         cu.mark_compact(self._mark, self._halo_ids, self._map, n_r + n_q, self._n_halo, self._mc_scratch, self.err)
+        ev[1].record()
         # 2. working CSR: own in-edges, then q's in-edges pulled from q, sources translated
         cu.csr_merge(peer["indptr"].ptrs[r], peer["indices"].ptrs[r], n_r, peer["indptr"].ptrs[q],
                      peer["indices"].ptrs[q], n_q, self._map, self._indptr_w, self._indices_w, self.err)
+        ev[2].record()
         # 3. halo feature rows from their owners (q's rows are on the side stream)
         tables = [peer["feat"].ptrs[p] for p in range(self.world)]
         cu.pull_rows(tables, fs, esz, fs * esz, self._halo_ids, self._n_halo, 0, self._prefix_dev,
                      self._feat_w.data_ptr(), fs, n_r + n_q, self._halo_ids.numel(), self.err)
+        ev[3].record()
         main.wait_stream(self._side)
-        ev[1].record()
+        ev[4].record()
         # bytes this rank pulls over NVLink: q's external-source list and CSR, q's feature
         # rows and the halo rows (their count is on the device until the log is read)
         pulled = sz[q]["ext"] * 4 + (n_q + 1) * 8 + sz[q]["e"] * 4 + n_q * fs * esz
         self.repart_log.append({"events": ev, "bytes_fixed": pulled, "row_bytes": fs * esz,
-                                "n_halo": self._n_halo.clone()})
+                                "n_halo": self._n_halo.clone(), "csr_bytes": (n_q + 1) * 8 + sz[q]["e"] * 4,
+                                "feat_bytes": n_q * fs * esz})
         self.working = WorkingGraph(self._indptr_w, self._indices_w, self._feat_w, n_r, n_q, self._n_halo,
                                     self.cap_nodes, q)
         return self.working
@@ -227,10 +235,16 @@ class PartitionStore:
         torch.cuda.synchronize(self.device)
         out = []
         for rec in self.repart_log:
-            ms = rec["events"][0].elapsed_time(rec["events"][1])
+            ev = rec["events"]
+            ms = ev[0].elapsed_time(ev[4])
             b = rec["bytes_fixed"] + int(rec["n_halo"].item()) * rec["row_bytes"]
+            t = lambda i, j: round(ev[i].elapsed_time(ev[j]), 4)  # noqa: E731
             out.append({"ms": round(ms, 4), "bytes": int(b),
-                        "frac_of_link_roofline": round(b / (link_gbs * 1e9) * 1e3 / ms, 4) if ms > 0 else None})
+                        "frac_of_link_roofline": round(b / (link_gbs * 1e9) * 1e3 / ms, 4) if ms > 0 else None,
+                        "phases_ms": {"marks": t(0, 1), "csr_merge": t(1, 2), "halo_rows": t(2, 3),
+                                      "feature_copy": t(5, 6), "join": t(3, 4)},
+                        "csr_gbs": round(rec["csr_bytes"] / max(t(1, 2), 1e-6) / 1e6, 1),
+                        "feature_gbs": round(rec["feat_bytes"] / max(t(5, 6), 1e-6) / 1e6, 1)})
         return out
 
     def check_errors(self):
