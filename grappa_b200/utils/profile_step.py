@@ -20,7 +20,9 @@ forward, backward, update) averaged over N eager steps is printed; with
 ``--graphs N`` the device time of N replays of each captured graph: sampling
 alone, the step without and with the next step's sampling on its side stream (the
 overlap that the training loop uses); with ``--kernel-times N`` the CUDA-event time of
-every kernel binding call, averaged over N eager steps.  Workloads: 3-layer models on the
+every kernel binding call, averaged over N eager steps; with ``--trace N`` each
+kernel's device time inside N replays of the step graph (CUPTI activity records,
+for the ranking only: a profiled number is not a benchmark value).  Workloads: 3-layer models on the
 ogbn-products-shaped synthetic graph (``--config`` picks another spec), 1024 seeds
 per batch, one GPU.
 """
@@ -47,6 +49,9 @@ def main():
     ap.add_argument("--graphs", type=int, default=0, help="time this many replays of each step graph")
     ap.add_argument("--kernel-times", type=int, default=0,
                     help="CUDA-event time of every kernel binding call over this many eager steps")
+    ap.add_argument("--trace", type=int, default=0,
+                    help="per-kernel device time inside this many replays of the step graph (CUPTI activity "
+                         "records through torch.profiler; warm caches, kernels as they overlap in the step)")
     a = ap.parse_args()
     name, hidden, fanouts = WORKLOADS[a.workload]
     dev = torch.device("cuda", 0)
@@ -79,6 +84,8 @@ def main():
     tr.close()
     if a.graphs:
         out["graph_ms"] = time_graphs(model, own, fanouts, a.batch, a.graphs)
+    if a.trace:
+        out["trace"] = trace_graph(model, own, fanouts, a.batch, a.trace)
     print(json.dumps(out))
 
 
@@ -98,6 +105,48 @@ def kernel_times(eng, seeds, counts, n):
             per[key] = per.get(key, 0.0) + e0.elapsed_time(e1) * 1000.0 / n
     eng.cu.timer = None
     return {k: round(v, 1) for k, v in sorted(per.items(), key=lambda kv: -kv[1])}
+
+
+def trace_graph(model, own, fanouts, batch, n):
+    """Replays of the step graph with the next step's sampling beside it (the training
+    loop's unit) under torch.profiler: every kernel's mean device time per replay, the
+    busy span of each replay and the sum of kernel times."""
+    from torch.profiler import ProfilerActivity, profile
+
+    tr = MiniBatchTrainer(model, own, fanouts, batch, comm=None, seed=3, use_cuda_graph=True)
+    tr.warmup()
+    eng = tr.engine
+    seeds, counts = tr.epoch_seeds(0, on_host=False)
+    eng.set_epoch(0)
+    eng._load_into(0, seeds[0], counts[0])
+    eng._load_into(1, seeds[1], counts[1])
+    g = eng._graph_for(("step", 0, True))
+    for _ in range(5):
+        g.replay()
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(n):
+            g.replay()
+        torch.cuda.synchronize()
+    eng.check_errors()
+    tr.close()
+    per, spans = {}, []
+    evs = [e for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+    for e in evs:
+        name = e.name[:80]
+        t = per.setdefault(name, [0.0, 0])
+        t[0] += e.time_range.end - e.time_range.start
+        t[1] += 1
+    total = sum(v[0] for v in per.values()) / n
+    if evs:
+        t0 = min(e.time_range.start for e in evs)
+        t1 = max(e.time_range.end for e in evs)
+        spans = (t1 - t0) / n
+    rows = sorted(((v[0] / n, v[1] / n, k) for k, v in per.items()), reverse=True)
+    return {"replays": n, "span_us_per_replay": round(spans, 1) if spans else None,
+            "kernel_us_sum_per_replay": round(total, 1),
+            "kernels": [{"name": k, "us_per_replay": round(v, 2), "launches_per_replay": round(c, 2)}
+                        for v, c, k in rows]}
 
 
 def time_graphs(model, own, fanouts, batch, n):
