@@ -683,6 +683,44 @@ void csr_merge(int64_t indptr_a, int64_t indices_a, int64_t n_a, int64_t indptr_
 }
 
 
+// --------------------------------------------------------------------------- head.cu
+void sage_head(Tensor indptr, Tensor indices, Tensor n_dst_dev, int64_t cap_dst, Tensor h, int64_t ip, Tensor w,
+               OptT bias, int64_t n_classes, Tensor labels, Tensor x, Tensor dl, OptT dx, Tensor loss_sum,
+               Tensor correct, OptT dbias, OptT pred_out) {
+  c10::cuda::CUDAGuard g(h.device());
+  d::SageHeadArgs a;
+  a.indptr = ptr<int32_t>(indptr, at::kInt, "indptr");
+  a.indices = ptr<int32_t>(indices, at::kInt, "indices");
+  a.n_dst_ptr = ptr<int32_t>(n_dst_dev, at::kInt, "n_dst_dev");
+  a.cap_dst = static_cast<int32_t>(cap_dst);
+  a.h = reinterpret_cast<const __nv_bfloat16*>(ptr2d<at::BFloat16>(h, at::kBFloat16, "h"));
+  a.ldh = h.stride(0);
+  a.ip = static_cast<int32_t>(ip);
+  a.w = reinterpret_cast<const __nv_bfloat16*>(ptr2d<at::BFloat16>(w, at::kBFloat16, "w"));
+  a.ldw = w.stride(0);
+  a.bias = optr<float>(bias, at::kFloat, "bias");
+  a.n_classes = static_cast<int32_t>(n_classes);
+  a.labels = ptr<int32_t>(labels, at::kInt, "labels");
+  a.x = reinterpret_cast<__nv_bfloat16*>(ptr2d<at::BFloat16>(x, at::kBFloat16, "x"));
+  a.ldx = x.stride(0);
+  a.dl = reinterpret_cast<__nv_bfloat16*>(ptr2d<at::BFloat16>(dl, at::kBFloat16, "dl"));
+  a.ld_dl = dl.stride(0);
+  if (dx.has_value()) {
+    a.dx = reinterpret_cast<__nv_bfloat16*>(ptr2d<at::BFloat16>(*dx, at::kBFloat16, "dx"));
+    a.lddx = dx->stride(0);
+    TORCH_CHECK(dx->size(0) >= cap_dst && dx->size(1) >= 2 * ip, "sage_head: dx too small");
+  }
+  a.loss_sum = ptr<float>(loss_sum, at::kFloat, "loss_sum");
+  a.correct = ptr<int32_t>(correct, at::kInt, "correct");
+  a.dbias = optr<float>(dbias, at::kFloat, "dbias");
+  a.pred_out = optr<int32_t>(pred_out, at::kInt, "pred_out");
+  TORCH_CHECK(w.size(0) >= n_classes && w.size(1) >= 2 * ip, "sage_head: w too small");
+  TORCH_CHECK(x.size(0) >= cap_dst && x.size(1) >= 2 * ip, "sage_head: x too small");
+  TORCH_CHECK(dl.size(0) >= cap_dst && dl.size(1) >= n_classes, "sage_head: dl too small");
+  TORCH_CHECK(labels.numel() >= cap_dst, "sage_head: labels too short");
+  d::launch_sage_head(a, stream());
+}
+
 // --------------------------------------------------------------------------- nn.cu
 void cross_entropy(Tensor logits, int64_t n_classes, Tensor labels, OptT n_rows_dev, int64_t cap_rows, OptT row_mask,
                    OptT n_sel_dev, Tensor dlogits, OptT dbias, Tensor loss_sum, Tensor correct) {
@@ -1091,6 +1129,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("compact_scratch_words", &compact_scratch_words);
   m.def("block_transpose", &block_transpose);
   m.def("aggregate_bwd_gather", &aggregate_bwd_gather);
+  m.def("sage_head", &sage_head, py::arg("indptr"), py::arg("indices"), py::arg("n_dst_dev"), py::arg("cap_dst"),
+        py::arg("h"), py::arg("ip"), py::arg("w"), py::arg("bias"), py::arg("n_classes"), py::arg("labels"), py::arg("x"),
+        py::arg("dl"), py::arg("dx"), py::arg("loss_sum"), py::arg("correct"), py::arg("dbias"),
+        py::arg("pred_out") = py::none());
+  m.def("sage_head_supported", [](int64_t ip, int64_t c) { return d::sage_head_supported(static_cast<int>(ip), static_cast<int>(c)); });
   m.def("gemm", &gemm, py::arg("A"), py::arg("a_mn"), py::arg("B"), py::arg("b_mn"), py::arg("M_cap"), py::arg("M_dev"),
         py::arg("N"), py::arg("K_cap"), py::arg("K_dev"), py::arg("splits"), py::arg("C"), py::arg("mode"),
         py::arg("bias"), py::arg("act"), py::arg("dropout_p"), py::arg("counters"), py::arg("salt"), py::arg("labels"),

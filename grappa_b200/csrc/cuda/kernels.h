@@ -164,6 +164,34 @@ struct GemmArgs {
 };
 void launch_gemm(const GemmProblem& p, GemmArgs a, int bn, cudaStream_t stream);
 
+// ---------------------------------------------------------------- fused SAGE head (head.cu)
+struct SageHeadArgs {
+  const int32_t* indptr = nullptr;      // last block, CSR by destination
+  const int32_t* indices = nullptr;
+  const int32_t* n_dst_ptr = nullptr;
+  int32_t cap_dst = 0;
+  const __nv_bfloat16* h = nullptr;     // source rows (the previous layer's output), ip columns used
+  int64_t ldh = 0;
+  int32_t ip = 0;                       // multiple of 8, <= 256
+  const __nv_bfloat16* w = nullptr;     // [n_classes][2 ip]: self half, then neighbour half
+  int64_t ldw = 0;
+  const float* bias = nullptr;
+  int32_t n_classes = 0;                // <= 64
+  const int32_t* labels = nullptr;      // per destination row
+  __nv_bfloat16* x = nullptr;           // [cap, 2 ip] out: [h_v | mean h_u]
+  int64_t ldx = 0;
+  __nv_bfloat16* dl = nullptr;          // [cap, ld_dl] out: dlogits, rows to the next multiple of 64 zeroed
+  int64_t ld_dl = 0;
+  __nv_bfloat16* dx = nullptr;          // [cap, 2 ip] out: dlogits W (null: forward only)
+  int64_t lddx = 0;
+  float* loss_sum = nullptr;
+  int32_t* correct = nullptr;
+  float* dbias = nullptr;
+  int32_t* pred_out = nullptr;
+};
+bool sage_head_supported(int ip, int n_classes);
+void launch_sage_head(const SageHeadArgs& a, cudaStream_t stream);
+
 // ---------------------------------------------------------------- aggregation (K-SpMM)
 enum AggMode : int { kAggMean = 0, kAggSum = 1, kAggGcn = 2, kAggWeighted = 3 };
 

@@ -54,6 +54,10 @@ GAT_FUSED_LOGITS = os.environ.get("GRAPPA_GAT_FUSED_LOGITS", "0") != "0"
 # fp32 reductions plus a separate activation pass (0, the default: the transposes add
 # two kernels per hop to the sampling stream, which measured slower overall)
 SAGE_GATHER_BWD = os.environ.get("GRAPPA_SAGE_GATHER_BWD", "0") != "0"
+# GraphSAGE output layer (aggregation, logits, cross-entropy, dlogits and dX) as one
+# CUDA-core kernel (csrc/cuda/head.cu) instead of an aggregation, a tensor-core GEMM
+# with a cross-entropy epilogue on a handful of SMs and a dX GEMM
+SAGE_FUSED_HEAD = os.environ.get("GRAPPA_SAGE_HEAD", "1") != "0"
 # stream priorities inside the step graphs: the layer chain, the weight gradients and
 # the updates at the highest priority, the next step's sampling at the lowest
 STREAM_PRIORITY = os.environ.get("GRAPPA_STREAM_PRIORITY", "1") != "0"
@@ -77,7 +81,7 @@ KERNELS_PER_CALL = {
     "l2norm_bwd": 1, "dropout_rows": 1, "dropout_grad": 1, "f32_to_bf16_rows": 1, "add_bf16_rows": 1,
     "gat_scores": 1, "gat_fwd": 1, "gat_bwd": 2, "gat_bwd_input": 2, "gat_dw_combine": 1, "sampler_counters": 1,
     "gat_in_scores": 1, "gat_in_fwd": 1, "gat_in_bwd": 2, "gat_in_prep": 1, "gat_in_dw": 1, "col_sum_bf16": 1,
-    "block_transpose": 2, "aggregate_bwd_gather": 1,
+    "block_transpose": 2, "aggregate_bwd_gather": 1, "sage_head": 1,
 }
 
 
@@ -830,6 +834,8 @@ class SageEngine(BlockEngine):
                     spec["dH"] = torch.zeros((rows, op), dtype=torch.float32, device=dev)
             else:
                 spec["ce_fused"] = op <= 64
+                spec["head"] = (SAGE_FUSED_HEAD and l > 0 and not self.full_graph
+                                and self.cu.sage_head_supported(ip, self.n_classes))
                 if not spec["ce_fused"]:
                     spec["logits"] = torch.zeros((rows, op), dtype=torch.bfloat16, device=dev)
             if l > 0:
@@ -842,6 +848,13 @@ class SageEngine(BlockEngine):
         for l, s in enumerate(self.lay):
             h = s["h"]
             src, src_map = self._input(l)
+            if s.get("head"):
+                # aggregation, logits, loss, dlogits (dY) and dX of the output layer
+                labels, _, _ = self._labels_rows()
+                cu.sage_head(sm.indptr[h], sm.indices[h], self._n_dst(h), sm.cap_dst[h], src, s["ip"], s["W"],
+                             s["bias"], self.n_classes, labels, s["X"], s["dY"], s["dX"] if training else None,
+                             self.fstats[2:3], self.istats[0:1], s["gb"] if training else None)
+                continue
             cu.aggregate(sm.indptr[h], sm.indices[h], self._n_dst(h), 0, sm.cap_dst[h], src, src_map,
                          s["ip"], AGG_MEAN, None, None, None, s["X"], s["ip"], 0, 0.0, 0, self.err)
             if l < L - 1:
@@ -867,9 +880,10 @@ class SageEngine(BlockEngine):
         self._dw(s["dY"], s["X"], s["op"], s["K"], s["rows"], self._n_dst(h), s["gW"])
         if l == 0:
             return
-        # dX = dY W (W read MN-major)
-        self._gemm(s["dY"], False, s["W"], True, s["rows"], self._n_dst(h), s["K"], s["op"], None, 1, s["dX"],
-                   GEMM_STORE_BF16)
+        # dX = dY W (W read MN-major; the fused output layer wrote it in the forward pass)
+        if not s.get("head"):
+            self._gemm(s["dY"], False, s["W"], True, s["rows"], self._n_dst(h), s["K"], s["op"], None, 1, s["dX"],
+                       GEMM_STORE_BF16)
         prev = self.lay[l - 1]
         if "dH" not in prev:
             # gathered by source over the block's transpose, activation backward fused

@@ -1,5 +1,6 @@
 """Numerics of the row-wise network kernels (nn.cu, gat.cu) against plain PyTorch
 fp32 references of the same ops, on bf16-exact inputs."""
+import math
 import pytest
 import torch
 import torch.nn.functional as F
@@ -276,3 +277,53 @@ def test_gat_input_layer_projection_after_aggregation(H, F_, ip, max_deg):
     torch.testing.assert_close(db, g.float().sum(0), atol=1e-2, rtol=1e-3)
     assert torch.all(dl_ == 0)
     assert int(err) == 0
+
+
+@pytest.mark.parametrize("ip,C,n_dst,max_deg", [(256, 47, 1021, 5), (104, 20, 300, 9), (64, 64, 130, 0)])
+def test_sage_head_matches_torch(ip, C, n_dst, max_deg):
+    """Fused GraphSAGE output layer: [h_v | mean h_u], logits, mean cross-entropy, the
+    bf16 dlogits (tail rows to the next multiple of 64 zeroed), the bias gradient, the
+    correct count and dX = dlogits W, against fp32 torch on the same bf16 operands."""
+    torch.manual_seed(7)
+    n_src = n_dst + 500
+    cap = (n_dst + 63) // 64 * 64 + 64
+    deg = torch.randint(0, max_deg + 1, (n_dst,))
+    indptr = torch.zeros(n_dst + 1, dtype=torch.int32)
+    indptr[1:] = torch.cumsum(deg, 0)
+    indices = torch.randint(0, n_src, (int(indptr[-1]) + 1,), dtype=torch.int32)
+    h = bf(torch.randn(n_src, ip, device=DEV))
+    cp = (C + 7) // 8 * 8
+    w = torch.zeros(cp, 2 * ip, dtype=torch.bfloat16, device=DEV)
+    w[:C] = bf(torch.randn(C, 2 * ip, device=DEV) / math.sqrt(2 * ip))
+    bias = torch.randn(cp, device=DEV) * 0.1
+    labels = torch.randint(0, C, (cap,), dtype=torch.int32, device=DEV)
+    x = torch.zeros(cap, 2 * ip, dtype=torch.bfloat16, device=DEV)
+    dl = torch.full((cap, cp), 5.0, dtype=torch.bfloat16, device=DEV)
+    dx = torch.zeros(cap, 2 * ip, dtype=torch.bfloat16, device=DEV)
+    loss, correct = torch.zeros(1, device=DEV), torch.zeros(1, dtype=torch.int32, device=DEV)
+    db = torch.zeros(cp, device=DEV)
+    nd = torch.tensor([n_dst], dtype=torch.int32, device=DEV)
+    cu().sage_head(indptr.to(DEV), indices.to(DEV), nd, cap, h, ip, w, bias, C, labels, x, dl, dx, loss, correct, db)
+    torch.cuda.synchronize()
+    # oracle
+    hf = h.float().cpu()
+    rows = []
+    for v in range(n_dst):
+        u = indices[indptr[v]:indptr[v + 1]].long()
+        agg = hf[u].mean(0) if u.numel() else torch.zeros(ip)
+        rows.append(torch.cat([hf[v], agg]))
+    xr = bf(torch.stack(rows)).float()
+    torch.testing.assert_close(x[:n_dst].float().cpu(), xr, atol=1e-2, rtol=1e-2)
+    z = xr @ w[:C].float().cpu().t() + bias[:C].cpu()
+    y = labels[:n_dst].long().cpu()
+    want_loss = F.cross_entropy(z, y)
+    assert abs(float(loss) - float(want_loss)) < 2e-3 * max(1.0, float(want_loss))
+    assert int(correct) == int((z.argmax(1) == y).sum())
+    g = (torch.softmax(z, 1) - F.one_hot(y, C).float()) / n_dst
+    torch.testing.assert_close(dl[:n_dst, :C].float().cpu(), g, atol=2e-4, rtol=2e-2)
+    assert bool((dl[:n_dst, C:] == 0).all())
+    tail = min(cap, (n_dst + 63) // 64 * 64)
+    assert bool((dl[n_dst:tail] == 0).all()) and bool((dl[tail:] == 5.0).all())
+    torch.testing.assert_close(db[:C].cpu(), bf(g).float().sum(0), atol=1e-4, rtol=1e-3)
+    want_dx = bf(g).float() @ w[:C].float().cpu()
+    torch.testing.assert_close(dx[:n_dst].float().cpu(), want_dx, atol=1e-4, rtol=2e-2)
