@@ -101,11 +101,19 @@ class FusedAllReduceAdam:
         comm.barrier()
 
     def _grid(self, lo, hi, mode, esz):
-        """CTAs of a bucket's launch: about 64 KB of peer reads per CTA, 8 at least (the
-        flag round trips dominate small buckets) and one per SM at most."""
+        """CTAs of a bucket's launch: about 64 KB of peer reads or 256 KB of local Adam
+        traffic per CTA, whichever asks for more, 8 at least (the flag round trips
+        dominate small buckets) and one per SM at most.  The local traffic is 30 bytes
+        per updated element (fp32 master, both moments, bf16 copy) plus the one-shot
+        mode's published copy and its W reads."""
         n = hi - lo
-        reads = n * (4 * (self.W - 1) if mode == ONE_SHOT else esz)
-        return int(max(8, min(_MAX_CTAS, math.ceil(reads / 65536))))
+        W = self.W
+        if mode == ONE_SHOT:
+            peer, local = n * 4 * (W - 1), n * (30 + 4 * (W + 1))
+        else:
+            peer, local = n * esz * (W - 1) / W, n * (30.0 / W + 2 * esz)
+        want = max(math.ceil(peer / 65536), math.ceil(local / 262144))
+        return int(max(8, min(_MAX_CTAS, want)))
 
     # ---------------------------------------------------------------------- binding
     def adopt_params(self, model):
