@@ -144,10 +144,76 @@ def ar_case(nbytes, mode, dtype=torch.float32):
             "ms": t, "frac_of_hbm": bytes_ / (t * 1e-3) / 1e9 / HBM_GBS}
 
 
+def _time_graph(fn, reps=20, iters=20):
+    """Device time of one fn() from a CUDA graph holding reps calls (launch overhead
+    excluded, as inside the training step graph)."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(reps):
+            fn()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / (iters * reps)
+
+
+def head_case(n_dst=1021, n_src=3250, deg=5, ip=256, C=47):
+    """GraphSAGE output layer of a 1024-seed step: the fused head kernel against the
+    aggregation + cross-entropy GEMM + dX GEMM it replaces (both inside CUDA graphs)."""
+    from grappa_b200.engine import bn_for
+
+    cu = _native.cuda()
+    dev = torch.device("cuda", 0)
+    cap = 1024
+    op = (C + 7) // 8 * 8
+    indptr = torch.arange(0, (n_dst + 1) * deg, deg, dtype=torch.int32, device=dev)
+    indices = torch.randint(0, n_src, (n_dst * deg,), dtype=torch.int32, device=dev)
+    h = torch.randn(n_src, ip, device=dev).to(torch.bfloat16)
+    w = torch.zeros(op, 2 * ip, device=dev, dtype=torch.bfloat16)
+    w[:C] = (torch.randn(C, 2 * ip, device=dev) / math.sqrt(2 * ip)).to(torch.bfloat16)
+    bias = torch.zeros(op, device=dev)
+    labels = torch.randint(0, C, (cap,), dtype=torch.int32, device=dev)
+    x = torch.zeros(cap, 2 * ip, device=dev, dtype=torch.bfloat16)
+    dl = torch.zeros(cap, op, device=dev, dtype=torch.bfloat16)
+    dx = torch.zeros(cap, 2 * ip, device=dev, dtype=torch.bfloat16)
+    loss, correct = torch.zeros(1, device=dev), torch.zeros(1, dtype=torch.int32, device=dev)
+    db = torch.zeros(op, device=dev)
+    nd = torch.tensor([n_dst], dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    dummy = torch.zeros((1, 1), device=dev)
+
+    def fused():
+        cu.sage_head(indptr, indices, nd, cap, h, ip, w, bias, C, labels, x, dl, dx, loss, correct, db)
+
+    def unfused():
+        cu.aggregate(indptr, indices, nd, 0, cap, h, None, ip, 0, None, None, None, x, ip, 0, 0.0, 0, err)
+        cu.gemm(x, False, w, False, cap, nd, op, 2 * ip, None, 1, dummy, 3, bias, 0, 0.0, None, 0, labels, C, dl, loss,
+                correct, None, nd, db, err, bn_for(op))
+        cu.gemm(dl, False, w, True, cap, nd, 2 * ip, op, None, 1, dx, 0, None, 0, 0.0, None, 0, None, 0, None, None,
+                None, None, None, None, err, 256)
+
+    t_f, t_u = _time_graph(fused), _time_graph(unfused)
+    assert int(err.item()) == 0
+    return {"bench": "sage_head", "n_dst": n_dst, "ip": ip, "classes": C, "fused_us": t_f * 1e3,
+            "aggregate_ce_gemm_dx_gemm_us": t_u * 1e3}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--scale", type=float, default=1.0)
-    ap.add_argument("--part", default="gemm,aggregate", help="comma list of gemm, aggregate, ar")
+    ap.add_argument("--part", default="gemm,aggregate", help="comma list of gemm, aggregate, head, ar")
     ap.add_argument("--ar-bytes", type=int, default=256 << 20)
     a = ap.parse_args()
     s = a.scale
@@ -162,6 +228,8 @@ def main():
     if "aggregate" in parts:
         rows += [aggregate_case(int(20853 * s), int(133975 * s), 14, 104),
                  aggregate_case(int(3250 * s), int(20853 * s), 8, 256)]
+    if "head" in parts:
+        rows += [head_case()]
     if "ar" in parts:
         rows += [ar_case(a.ar_bytes, 1), ar_case(a.ar_bytes, 0), ar_case(a.ar_bytes, 1, torch.bfloat16)]
     for r in rows:
