@@ -204,7 +204,8 @@ __device__ __forceinline__ float pick_head(const float (&v)[HM], int h) {
 // HM: the head count rounded up to 4 or kMaxHeads (sizes the per-head register arrays);
 // EU_: edges whose z rows are in flight together (0: 4 for CPL 1, else 2); MINB: CTAs
 // per SM the registers are capped for (occupancy against registers per lane)
-template <int CPL, int HM, int EU_ = 0, int MINB = 1>
+// SEGF: F % 8 == 0, so every 8-column chunk lies in one head (no per-element head pick)
+template <int CPL, int HM, int EU_ = 0, int MINB = 1, bool SEGF = false>
 __global__ void __launch_bounds__(kThreads, MINB) gat_fwd_kernel(GatArgs a) {
   GB_PDL_ENTRY();
   extern __shared__ float s_row[];  // mean_heads: [warps][HF]
@@ -298,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, MINB) gat_fwd_kernel(GatArgs a) {
       for (int q = 0; q < CPL; ++q) {
         const float s0 = pick_head<HM>(sc, h0[q]), s1 = pick_head<HM>(sc, h1[q]);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[q][j] *= ((in0[q] >> j) & 1u) ? s0 : s1;
+        for (int j = 0; j < 8; ++j) acc[q][j] *= (SEGF || ((in0[q] >> j) & 1u)) ? s0 : s1;
       }
       for (int k = 0; k < cnt; k += EU) {
         uint4 zv[EU][CPL];
@@ -311,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, MINB) gat_fwd_kernel(GatArgs a) {
           for (int q = 0; q < CPL; ++q) {
             const int c0 = (lane + 32 * q) * 8;
             wt0[t][q] = ok ? s_w[wib][k + t][h0[q]] : 0.f;
-            wt1[t][q] = ok ? s_w[wib][k + t][h1[q]] : 0.f;
+            wt1[t][q] = (!SEGF && ok) ? s_w[wib][k + t][h1[q]] : 0.f;
             zv[t][q] = make_uint4(0, 0, 0, 0);
             if (ok && c0 < HF) zv[t][q] = *reinterpret_cast<const uint4*>(a.z + static_cast<int64_t>(u) * a.ldz + zcol(a, c0));
           }
@@ -323,7 +324,7 @@ __global__ void __launch_bounds__(kThreads, MINB) gat_fwd_kernel(GatArgs a) {
             float f[8];
             bf16x8_to_f32(zv[t][q], f);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) acc[q][j] = fmaf(((in0[q] >> j) & 1u) ? wt0[t][q] : wt1[t][q], f[j], acc[q][j]);
+            for (int j = 0; j < 8; ++j) acc[q][j] = fmaf((SEGF || ((in0[q] >> j) & 1u)) ? wt0[t][q] : wt1[t][q], f[j], acc[q][j]);
           }
       }
       __syncwarp();  // the batch's weights are read before the next batch writes them
@@ -338,7 +339,7 @@ __global__ void __launch_bounds__(kThreads, MINB) gat_fwd_kernel(GatArgs a) {
       const float d0 = pick_head<HM>(sden, h0[q]), d1 = pick_head<HM>(sden, h1[q]);
       const float i0 = d0 > 0.f ? 1.f / d0 : 0.f, i1 = d1 > 0.f ? 1.f / d1 : 0.f;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) acc[q][j] *= ((in0[q] >> j) & 1u) ? i0 : i1;
+      for (int j = 0; j < 8; ++j) acc[q][j] *= (SEGF || ((in0[q] >> j) & 1u)) ? i0 : i1;
     }
     if (!a.mean_heads) {
 #pragma unroll
@@ -1020,7 +1021,9 @@ void launch_gat_fwd(const GatArgs& a, cudaStream_t stream) {
     else if (variant == 2) launch_k(gat_fwd_kernel<1, 4, 4, 3>, grid, kThreads, smem, stream, a);
     else launch_k(gat_fwd_kernel<1, 4, 8, 2>, grid, kThreads, smem, stream, a);
   } else if (cpl <= 1 && a.heads <= 4 && occ >= 2) {
-    launch_k(gat_fwd_kernel<1, 4, 4, 3>, grid, kThreads, smem, stream, a);  // 80 registers, 3 CTAs per SM
+    // register cap for 3 CTAs per SM; heads of a multiple of 8 columns skip the head picks
+    if (a.feat % 8 == 0) launch_k(gat_fwd_kernel<1, 4, 4, 3, true>, grid, kThreads, smem, stream, a);
+    else launch_k(gat_fwd_kernel<1, 4, 4, 3>, grid, kThreads, smem, stream, a);
   } else if (cpl <= 1) GAT_FWD(1);
   else if (cpl <= 2) GAT_FWD(2);
   else GAT_FWD(4);
