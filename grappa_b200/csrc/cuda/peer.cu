@@ -190,16 +190,19 @@ __global__ void __launch_bounds__(kMcThreads) mark_compact_kernel(uint8_t* mark,
   const dev::LookBack::Ticket tk = dev::LookBack::ticket(scratch, s_tile);
   const int tile = tk.tile;
   const int64_t g0 = static_cast<int64_t>(tile) * kMcTile + threadIdx.x * kMcItems;
+  // the thread's 16 mark bytes as one 16-byte load (byte loads for the ragged tail)
   uint32_t bits = 0;
-  int cnt = 0;
+  if (g0 + kMcItems <= n_global) {
+    const uint4 w = *reinterpret_cast<const uint4*>(mark + g0);
+    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-  for (int q = 0; q < kMcItems; ++q) {
-    const int64_t g = g0 + q;
-    if (g < n_global && mark[g]) {
-      bits |= 1u << q;
-      ++cnt;
-    }
+    for (int q = 0; q < kMcItems; ++q)
+      if ((words[q >> 2] >> (8 * (q & 3))) & 0xFFu) bits |= 1u << q;
+  } else {
+    for (int q = 0; q < kMcItems; ++q)
+      if (g0 + q < n_global && mark[g0 + q]) bits |= 1u << q;
   }
+  const int cnt = __popc(bits);
   long long total;
   const long long excl = dev::block_exclusive_scan<kMcThreads, long long>(cnt, s_scan, &total);
   if ((threadIdx.x >> 5) == 0) {
@@ -208,11 +211,16 @@ __global__ void __launch_bounds__(kMcThreads) mark_compact_kernel(uint8_t* mark,
   }
   __syncthreads();
   long long k = s_prefix + excl;
+  if (bits) {  // clear the marks for the next repartition
+    if (g0 + kMcItems <= n_global) *reinterpret_cast<uint4*>(mark + g0) = make_uint4(0, 0, 0, 0);
+    else
+      for (int q = 0; q < kMcItems; ++q)
+        if (g0 + q < n_global) mark[g0 + q] = 0;
+  }
 #pragma unroll
   for (int q = 0; q < kMcItems; ++q) {
     if (!(bits & (1u << q))) continue;
     const int64_t g = g0 + q;
-    mark[g] = 0;
     if (k < cap_out) {
       out_ids[k] = g;
       map[g] = base + static_cast<int32_t>(k);

@@ -514,3 +514,33 @@ def test_csr_merge_and_copy(a0, b0):
     cu().peer_copy(dst.data_ptr(), src.data_ptr(), src.numel() * 4)
     torch.cuda.synchronize()
     assert torch.equal(dst, src)
+
+
+@pytest.mark.parametrize("n_global", [100003, 4096 * 3, 17])
+def test_mark_compact_halo_ids(n_global):
+    """Halo discovery of the repartition: marked ids (minus the iota-mapped own and
+    neighbour ranges) are compacted in id order into out_ids, the map gets base + rank,
+    the count goes to n_out and the marks are cleared; run twice on the same buffers
+    (16-byte mark words, a ragged tail, the tagged look-back scan)."""
+    torch.manual_seed(8)
+    mark = torch.zeros(n_global, dtype=torch.uint8, device=DEV)
+    mp = torch.full((n_global,), -1, dtype=torch.int32, device=DEV)
+    scratch = torch.zeros(cu().mark_compact_scratch_words(n_global), dtype=torch.int64, device=DEV)
+    out = torch.full((n_global,), -1, dtype=torch.int64, device=DEV)
+    n_out = torch.zeros(1, dtype=torch.int32, device=DEV)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    for it in range(2):
+        ids = torch.randint(0, n_global, (max(1, n_global // 7),), dtype=torch.int32, device=DEV)
+        cu().mark_ids(ids.data_ptr(), None, ids.numel(), mark)
+        lo, cnt = n_global // 3, n_global // 5
+        cu().iota_map(mp, lo, cnt, 0, mark)
+        base = cnt
+        cu().mark_compact(mark, out, mp, base, n_out, scratch, err)
+        torch.cuda.synchronize()
+        want = torch.unique(ids.long())
+        want = want[(want < lo) | (want >= lo + cnt)]
+        k = int(n_out)
+        assert k == want.numel() and int(err) == 0
+        assert torch.equal(out[:k].cpu(), want.cpu())
+        assert torch.equal(mp[want].cpu(), torch.arange(base, base + k, dtype=torch.int32))
+        assert int(mark.sum()) == 0
