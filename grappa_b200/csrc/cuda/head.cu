@@ -16,6 +16,7 @@
 // are reduced across the warp by a transposing butterfly (31 shuffles per 32
 // classes), after which lane c holds class c (and class 32 + c).
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -233,6 +234,287 @@ __global__ void __launch_bounds__(kThreads) sage_head_kernel(SageHeadArgs a) {
   }
 }
 
+// ---------------------------------------------------------------- tile version
+// 16 destination rows per CTA (8 warps).  The two contractions of the layer run as
+// warp-level bf16 MMAs (m16n8k16, fp32 accumulation) on operands staged in shared
+// memory: logits Z[16 x C] = X[16 x 2ip] W^T (the k-steps split over the warps, the
+// partial tiles summed through shared memory) and dX[16 x 2ip] = dZ[16 x C] W (the
+// n-tiles split over the warps).  Aggregation and the softmax cross-entropy run as in
+// the row version, two rows per warp; W is copied into shared memory with cp.async
+// while the rows are aggregated.
+constexpr int kTileRows = 16;
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t a, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(a));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t a, uint32_t& r0, uint32_t& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(a));
+}
+__device__ __forceinline__ void ldsm_x2_t(uint32_t a, uint32_t& r0, uint32_t& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(a));
+}
+__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+// shared-memory layout of the tile kernel (row strides padded by 8 elements: ldmatrix
+// rows of one 8x8 matrix fall into distinct 16-byte bank groups)
+struct HeadTileLayout {
+  int K, ldk, KC, ldc, NT;
+  size_t w_off, x_off, z_off, d_off, bytes;
+  __host__ __device__ HeadTileLayout(int ip, int C) {
+    K = 2 * ip;
+    ldk = K + 8;
+    NT = (C + 7) / 8;           // n-tiles of the logits
+    KC = ((NT * 8 + 15) / 16) * 16;  // classes padded to whole k-steps of the dX product
+    ldc = KC + 8;
+    w_off = 0;                                                    // W   [KC][ldk] bf16
+    x_off = w_off + static_cast<size_t>(KC) * ldk * 2;           // X   [16][ldk] bf16 (then dX)
+    z_off = x_off + static_cast<size_t>(kTileRows) * ldk * 2;    // Z   [kWarps][16][NT*8] f32
+    d_off = z_off + static_cast<size_t>(kWarps) * kTileRows * NT * 8 * 4;  // dZ [16][ldc] bf16
+    bytes = d_off + static_cast<size_t>(kTileRows) * ldc * 2;
+  }
+};
+
+__global__ void __launch_bounds__(kThreads) sage_head_tile_kernel(SageHeadArgs a) {
+  GB_PDL_ENTRY();
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ float s_db[64];
+  __shared__ float s_loss;
+  __shared__ int s_correct;
+  const int ip = a.ip, C = a.n_classes;
+  const HeadTileLayout L(ip, C);
+  const int K = L.K, ldk = L.ldk, NT = L.NT, KC = L.KC, ldc = L.ldc;
+  __nv_bfloat16* s_w = reinterpret_cast<__nv_bfloat16*>(smem_raw + L.w_off);
+  __nv_bfloat16* s_x = reinterpret_cast<__nv_bfloat16*>(smem_raw + L.x_off);
+  float* s_z = reinterpret_cast<float*>(smem_raw + L.z_off);
+  __nv_bfloat16* s_d = reinterpret_cast<__nv_bfloat16*>(smem_raw + L.d_off);
+  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+  const int n = min(*a.n_dst_ptr, a.cap_dst);
+  const int tail = min(a.cap_dst, static_cast<int>(ceil_div(n, 64) * 64));
+  const int r0 = blockIdx.x * kTileRows;
+  if (r0 >= tail) return;
+  // ---- W into shared memory (cp.async, overlapping the aggregation); rows >= C zero
+  const int kc8 = K / 8;
+  for (int i = threadIdx.x; i < KC * kc8; i += kThreads) {
+    const int c = i / kc8, k8 = i % kc8;
+    __nv_bfloat16* dst = s_w + c * ldk + k8 * 8;
+    if (c < C) {
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)),
+                   "l"(a.w + static_cast<int64_t>(c) * a.ldw + k8 * 8));
+    } else {
+      *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+    }
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  if (threadIdx.x < 64) s_db[threadIdx.x] = 0.f;
+  if (threadIdx.x == 0) {
+    s_loss = 0.f;
+    s_correct = 0;
+  }
+  for (int i = threadIdx.x; i < kTileRows * (ldc / 8); i += kThreads)
+    *reinterpret_cast<uint4*>(s_d + (i / (ldc / 8)) * ldc + (i % (ldc / 8)) * 8) = make_uint4(0, 0, 0, 0);
+  // ---- aggregation: rows 2 wib, 2 wib + 1 of the tile
+  const bool has_cols = lane * 8 < ip;
+  const int c0 = lane * 8;
+  for (int rr = 0; rr < 2; ++rr) {
+    const int t = 2 * wib + rr, v = r0 + t;
+    uint4 ps = make_uint4(0, 0, 0, 0), pa = make_uint4(0, 0, 0, 0);
+    if (v < n && has_cols) {
+      const int beg = a.indptr[v], end = a.indptr[v + 1];
+      float xs[8], xa[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) xa[j] = 0.f;
+      const uint4 self = *reinterpret_cast<const uint4*>(a.h + static_cast<int64_t>(v) * a.ldh + c0);
+      int e = beg;
+      for (; e + 3 < end; e += 4) {
+        uint4 r[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          r[q] = *reinterpret_cast<const uint4*>(a.h + static_cast<int64_t>(a.indices[e + q]) * a.ldh + c0);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float f[8];
+          bf16x8_to_f32(r[q], f);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) xa[j] += f[j];
+        }
+      }
+      for (; e < end; ++e) {
+        float f[8];
+        bf16x8_to_f32(*reinterpret_cast<const uint4*>(a.h + static_cast<int64_t>(a.indices[e]) * a.ldh + c0), f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) xa[j] += f[j];
+      }
+      const float sc = end > beg ? 1.f / static_cast<float>(end - beg) : 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) xa[j] *= sc;
+      bf16x8_to_f32(self, xs);
+      ps = f32_to_bf16x8(xs);
+      pa = f32_to_bf16x8(xa);
+      __nv_bfloat16* xr = a.x + static_cast<int64_t>(v) * a.ldx;
+      *reinterpret_cast<uint4*>(xr + c0) = ps;
+      *reinterpret_cast<uint4*>(xr + ip + c0) = pa;
+    }
+    if (has_cols) {  // rows past the count enter the products as zeros
+      *reinterpret_cast<uint4*>(s_x + t * ldk + c0) = ps;
+      *reinterpret_cast<uint4*>(s_x + t * ldk + ip + c0) = pa;
+    }
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
+  // ---- logits: warp wib takes k-steps wib, wib + 8, ...; partial tiles to s_z
+  {
+    const int g = lane >> 2, tq = lane & 3;
+    float acc[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[j][q] = 0.f;
+    const int ksteps = K / 16;
+    for (int ks = wib; ks < ksteps; ks += kWarps) {
+      const int k0 = ks * 16;
+      uint32_t x0, x1, x2, x3;
+      ldsm_x4(smem_addr(s_x + (lane & 15) * ldk + k0 + (lane >> 4) * 8), x0, x1, x2, x3);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (j >= NT) break;
+        uint32_t b0, b1;
+        const int l16 = lane & 15;
+        ldsm_x2(smem_addr(s_w + (j * 8 + (l16 & 7)) * ldk + k0 + (l16 >> 3) * 8), b0, b1);
+        mma_bf16(acc[j], x0, x1, x2, x3, b0, b1);
+      }
+    }
+    float* zw = s_z + wib * kTileRows * NT * 8;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (j >= NT) break;
+      const int col = j * 8 + tq * 2;
+      zw[g * NT * 8 + col] = acc[j][0];
+      zw[g * NT * 8 + col + 1] = acc[j][1];
+      zw[(g + 8) * NT * 8 + col] = acc[j][2];
+      zw[(g + 8) * NT * 8 + col + 1] = acc[j][3];
+    }
+  }
+  __syncthreads();
+  // ---- softmax cross-entropy, two rows per warp (lane c: class c and 32 + c)
+  const float inv_n = 1.0f / static_cast<float>(n > 0 ? n : 1);
+  float db_a = 0.f, db_b = 0.f, loss_acc = 0.f;
+  int correct_acc = 0;
+  const int ZW = NT * 8;
+  for (int rr = 0; rr < 2; ++rr) {
+    const int t = 2 * wib + rr, v = r0 + t;
+    if (v >= tail) continue;
+    __nv_bfloat16* dlr = a.dl + static_cast<int64_t>(v) * a.ld_dl;
+    if (v >= n) {
+      for (int j = lane; j < a.ld_dl; j += 32) dlr[j] = __float2bfloat16_rn(0.f);
+      continue;
+    }
+    float za = -INFINITY, zb = -INFINITY;
+    if (lane < C) {
+      float s = a.bias ? a.bias[lane] : 0.f;
+      for (int w = 0; w < kWarps; ++w) s += s_z[(w * kTileRows + t) * ZW + lane];
+      za = s;
+    }
+    if (32 + lane < C) {
+      float s = a.bias ? a.bias[32 + lane] : 0.f;
+      for (int w = 0; w < kWarps; ++w) s += s_z[(w * kTileRows + t) * ZW + 32 + lane];
+      zb = s;
+    }
+    float mx = fmaxf(za, zb);
+    int arg = za >= zb ? lane : 32 + lane;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float om = __shfl_xor_sync(0xffffffffu, mx, o);
+      const int oa = __shfl_xor_sync(0xffffffffu, arg, o);
+      if (om > mx || (om == mx && oa < arg)) {
+        mx = om;
+        arg = oa;
+      }
+    }
+    const float ea = lane < C ? __expf(za - mx) : 0.f;
+    const float eb = 32 + lane < C ? __expf(zb - mx) : 0.f;
+    const float lse = mx + __logf(warp_sum(ea + eb));
+    const int y = a.labels[v];
+    const float zy = __shfl_sync(0xffffffffu, y < 32 ? za : zb, y & 31);
+    if (lane == 0) {
+      loss_acc += (lse - zy) * inv_n;
+      correct_acc += arg == y;
+      if (a.pred_out) a.pred_out[v] = arg;
+    }
+    float ga = lane < C ? (__expf(za - lse) - (lane == y ? 1.f : 0.f)) * inv_n : 0.f;
+    float gb = 32 + lane < C ? (__expf(zb - lse) - (32 + lane == y ? 1.f : 0.f)) * inv_n : 0.f;
+    const __nv_bfloat16 ha = __float2bfloat16_rn(ga), hb = __float2bfloat16_rn(gb);
+    db_a += __bfloat162float(ha);
+    db_b += __bfloat162float(hb);
+    if (lane < a.ld_dl) dlr[lane] = ha;
+    if (32 + lane < a.ld_dl) dlr[32 + lane] = hb;
+    if (lane < KC) s_d[t * ldc + lane] = ha;
+    if (32 + lane < KC) s_d[t * ldc + 32 + lane] = hb;
+  }
+  if (a.dbias) {
+    if (lane < C && db_a != 0.f) atomicAdd(&s_db[lane], db_a);
+    if (32 + lane < C && db_b != 0.f) atomicAdd(&s_db[32 + lane], db_b);
+  }
+  if (lane == 0) {
+    if (loss_acc != 0.f) atomicAdd(&s_loss, loss_acc);
+    if (correct_acc) atomicAdd(&s_correct, correct_acc);
+  }
+  __syncthreads();
+  // ---- dX = dZ W: warp wib takes n-tiles wib, wib + 8, ... of the 2 ip columns; the
+  // bf16 result is staged in the X tile, then stored as 16-byte rows
+  if (a.dx) {
+    const int g = lane >> 2, tq = lane & 3;
+    const int l16 = lane & 15;
+    const int kst = KC / 16;
+    uint32_t da[4][4];
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+      if (s >= kst) break;
+      ldsm_x4(smem_addr(s_d + (lane & 15) * ldc + s * 16 + (lane >> 4) * 8), da[s][0], da[s][1], da[s][2], da[s][3]);
+    }
+    for (int nt = wib; nt < K / 8; nt += kWarps) {
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int s = 0; s < 4; ++s) {
+        if (s >= kst) break;
+        uint32_t b0, b1;
+        ldsm_x2_t(smem_addr(s_w + (s * 16 + l16) * ldk + nt * 8), b0, b1);
+        mma_bf16(acc, da[s][0], da[s][1], da[s][2], da[s][3], b0, b1);
+      }
+      const int col = nt * 8 + tq * 2;
+      *reinterpret_cast<uint32_t*>(s_x + g * ldk + col) = pack_bf16x2(acc[0], acc[1]);
+      *reinterpret_cast<uint32_t*>(s_x + (g + 8) * ldk + col) = pack_bf16x2(acc[2], acc[3]);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < kTileRows * kc8; i += kThreads) {
+      const int t = i / kc8, k8 = i % kc8, v = r0 + t;
+      if (v < n)
+        *reinterpret_cast<uint4*>(a.dx + static_cast<int64_t>(v) * a.lddx + k8 * 8) =
+            *reinterpret_cast<const uint4*>(s_x + t * ldk + k8 * 8);
+    }
+  }
+  if (a.dbias && threadIdx.x < C && s_db[threadIdx.x] != 0.f) atomicAdd(a.dbias + threadIdx.x, s_db[threadIdx.x]);
+  if (threadIdx.x == 0) {
+    if (a.loss_sum && s_loss != 0.f) atomicAdd(a.loss_sum, s_loss);
+    if (a.correct && s_correct) atomicAdd(a.correct, s_correct);
+  }
+}
+
 }  // namespace
 
 bool sage_head_supported(int ip, int n_classes) {
@@ -244,6 +526,19 @@ void launch_sage_head(const SageHeadArgs& a, cudaStream_t stream) {
   if (a.ldh % 8 || a.ldx % 8 || a.ldw % 8 || (a.dx && a.lddx % 8))
     throw std::invalid_argument("sage head: row strides must be multiples of 8 elements");
   if (a.ld_dl < a.n_classes) throw std::invalid_argument("sage head: dlogits row shorter than the classes");
+  static const bool tile = [] {
+    const char* e = std::getenv("GRAPPA_SAGE_HEAD_TILE");
+    return !(e && e[0] == '0');
+  }();
+  if (tile) {
+    const HeadTileLayout L(a.ip, a.n_classes);
+    GB_CUDA_CHECK(cudaFuncSetAttribute(sage_head_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(L.bytes)));
+    const int tiles = static_cast<int>(ceil_div(a.cap_dst > 0 ? a.cap_dst : 1, kTileRows));
+    launch_k(sage_head_tile_kernel, tiles, kThreads, L.bytes, stream, a);
+    GB_LAUNCH_CHECK();
+    return;
+  }
   const int nc = a.n_classes <= 32 ? 32 : 64;
   const size_t smem = static_cast<size_t>(nc) * 2 * a.ip * sizeof(__nv_bfloat16);
   int dev = 0, sms = 148;
