@@ -204,8 +204,6 @@ def head_case(n_dst=1021, n_src=3250, deg=5, ip=256, C=47):
         cu.gemm(dl, False, w, True, cap, nd, 2 * ip, op, None, 1, dx, 0, None, 0, 0.0, None, 0, None, 0, None, None,
                 None, None, None, None, err, 256)
 
-    import os
-
     t_f, t_u = _time_graph(fused), _time_graph(unfused)
     assert int(err.item()) == 0
     return {"bench": "sage_head", "n_dst": n_dst, "ip": ip, "classes": C, "fused_us": t_f * 1e3,
