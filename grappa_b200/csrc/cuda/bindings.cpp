@@ -686,7 +686,7 @@ void csr_merge(int64_t indptr_a, int64_t indices_a, int64_t n_a, int64_t indptr_
 // --------------------------------------------------------------------------- head.cu
 void sage_head(Tensor indptr, Tensor indices, Tensor n_dst_dev, int64_t cap_dst, Tensor h, int64_t ip, Tensor w,
                OptT bias, int64_t n_classes, Tensor labels, Tensor x, Tensor dl, OptT dx, Tensor loss_sum,
-               Tensor correct, OptT dbias, OptT pred_out) {
+               Tensor correct, OptT dbias, OptT pred_out, OptT dsrc) {
   c10::cuda::CUDAGuard g(h.device());
   d::SageHeadArgs a;
   a.indptr = ptr<int32_t>(indptr, at::kInt, "indptr");
@@ -714,6 +714,11 @@ void sage_head(Tensor indptr, Tensor indices, Tensor n_dst_dev, int64_t cap_dst,
   a.correct = ptr<int32_t>(correct, at::kInt, "correct");
   a.dbias = optr<float>(dbias, at::kFloat, "dbias");
   a.pred_out = optr<int32_t>(pred_out, at::kInt, "pred_out");
+  if (dsrc.has_value()) {
+    a.dsrc = ptr2d<float>(*dsrc, at::kFloat, "dsrc");
+    a.ld_dsrc = dsrc->stride(0);
+    TORCH_CHECK(dsrc->size(1) >= ip && dsrc->size(0) >= h.size(0), "sage_head: dsrc too small");
+  }
   TORCH_CHECK(w.size(0) >= n_classes && w.size(1) >= 2 * ip, "sage_head: w too small");
   TORCH_CHECK(x.size(0) >= cap_dst && x.size(1) >= 2 * ip, "sage_head: x too small");
   TORCH_CHECK(dl.size(0) >= cap_dst && dl.size(1) >= n_classes, "sage_head: dl too small");
@@ -1132,7 +1137,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sage_head", &sage_head, py::arg("indptr"), py::arg("indices"), py::arg("n_dst_dev"), py::arg("cap_dst"),
         py::arg("h"), py::arg("ip"), py::arg("w"), py::arg("bias"), py::arg("n_classes"), py::arg("labels"), py::arg("x"),
         py::arg("dl"), py::arg("dx"), py::arg("loss_sum"), py::arg("correct"), py::arg("dbias"),
-        py::arg("pred_out") = py::none());
+        py::arg("pred_out") = py::none(), py::arg("dsrc") = py::none());
+  m.def("sage_head_fused_bwd", [] {
+    const char* e = std::getenv("GRAPPA_SAGE_HEAD_TILE");
+    return !(e && e[0] == '0');
+  });
   m.def("sage_head_supported", [](int64_t ip, int64_t c) { return d::sage_head_supported(static_cast<int>(ip), static_cast<int>(c)); });
   m.def("gemm", &gemm, py::arg("A"), py::arg("a_mn"), py::arg("B"), py::arg("b_mn"), py::arg("M_cap"), py::arg("M_dev"),
         py::arg("N"), py::arg("K_cap"), py::arg("K_dev"), py::arg("splits"), py::arg("C"), py::arg("mode"),

@@ -266,6 +266,9 @@ __device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
+__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+}
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&v);
@@ -477,7 +480,7 @@ __global__ void __launch_bounds__(kThreads) sage_head_tile_kernel(SageHeadArgs a
   __syncthreads();
   // ---- dX = dZ W: warp wib takes n-tiles wib, wib + 8, ... of the 2 ip columns; the
   // bf16 result is staged in the X tile, then stored as 16-byte rows
-  if (a.dx) {
+  if (a.dx || a.dsrc) {
     const int g = lane >> 2, tq = lane & 3;
     const int l16 = lane & 15;
     const int kst = KC / 16;
@@ -501,11 +504,36 @@ __global__ void __launch_bounds__(kThreads) sage_head_tile_kernel(SageHeadArgs a
       *reinterpret_cast<uint32_t*>(s_x + (g + 8) * ldk + col) = pack_bf16x2(acc[2], acc[3]);
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < kTileRows * kc8; i += kThreads) {
-      const int t = i / kc8, k8 = i % kc8, v = r0 + t;
-      if (v < n)
-        *reinterpret_cast<uint4*>(a.dx + static_cast<int64_t>(v) * a.lddx + k8 * 8) =
-            *reinterpret_cast<const uint4*>(s_x + t * ldk + k8 * 8);
+    if (a.dx) {
+      for (int i = threadIdx.x; i < kTileRows * kc8; i += kThreads) {
+        const int t = i / kc8, k8 = i % kc8, v = r0 + t;
+        if (v < n)
+          *reinterpret_cast<uint4*>(a.dx + static_cast<int64_t>(v) * a.lddx + k8 * 8) =
+              *reinterpret_cast<const uint4*>(s_x + t * ldk + k8 * 8);
+      }
+    }
+    if (a.dsrc && has_cols) {
+      // the aggregation's backward from the bf16 dx rows: self half to the row itself,
+      // neighbour half / deg to every in-neighbour (two rows per warp, 8 columns a lane)
+      for (int rr = 0; rr < 2; ++rr) {
+        const int t = 2 * wib + rr, v = r0 + t;
+        if (v >= n) continue;
+        const int beg = a.indptr[v], end = a.indptr[v + 1];
+        const float sc = end > beg ? 1.f / static_cast<float>(end - beg) : 0.f;
+        float fs[8], fa[8];
+        bf16x8_to_f32(*reinterpret_cast<const uint4*>(s_x + t * ldk + c0), fs);
+        bf16x8_to_f32(*reinterpret_cast<const uint4*>(s_x + t * ldk + ip + c0), fa);
+        float* d = a.dsrc + static_cast<int64_t>(v) * a.ld_dsrc + c0;
+        red_add_v4(d, fs[0], fs[1], fs[2], fs[3]);
+        red_add_v4(d + 4, fs[4], fs[5], fs[6], fs[7]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) fa[j] *= sc;
+        for (int e = beg; e < end; ++e) {
+          float* du = a.dsrc + static_cast<int64_t>(a.indices[e]) * a.ld_dsrc + c0;
+          red_add_v4(du, fa[0], fa[1], fa[2], fa[3]);
+          red_add_v4(du + 4, fa[4], fa[5], fa[6], fa[7]);
+        }
+      }
     }
   }
   if (a.dbias && threadIdx.x < C && s_db[threadIdx.x] != 0.f) atomicAdd(a.dbias + threadIdx.x, s_db[threadIdx.x]);
@@ -522,14 +550,17 @@ bool sage_head_supported(int ip, int n_classes) {
 }
 
 void launch_sage_head(const SageHeadArgs& a, cudaStream_t stream) {
-  if (!sage_head_supported(a.ip, a.n_classes)) throw std::invalid_argument("sage head: ip % 8, ip <= 256, <= 64 classes");
-  if (a.ldh % 8 || a.ldx % 8 || a.ldw % 8 || (a.dx && a.lddx % 8))
-    throw std::invalid_argument("sage head: row strides must be multiples of 8 elements");
-  if (a.ld_dl < a.n_classes) throw std::invalid_argument("sage head: dlogits row shorter than the classes");
+  // GRAPPA_SAGE_HEAD_TILE=0: the row version (no fused aggregation backward)
   static const bool tile = [] {
     const char* e = std::getenv("GRAPPA_SAGE_HEAD_TILE");
     return !(e && e[0] == '0');
   }();
+  if (!sage_head_supported(a.ip, a.n_classes)) throw std::invalid_argument("sage head: ip % 8, ip <= 256, <= 64 classes");
+  if (a.dsrc && (a.ld_dsrc % 4 || !tile))
+    throw std::invalid_argument("sage head: the fused aggregation backward needs the tile kernel and ld_dsrc % 4");
+  if (a.ldh % 8 || a.ldx % 8 || a.ldw % 8 || (a.dx && a.lddx % 8))
+    throw std::invalid_argument("sage head: row strides must be multiples of 8 elements");
+  if (a.ld_dl < a.n_classes) throw std::invalid_argument("sage head: dlogits row shorter than the classes");
   if (tile) {
     const HeadTileLayout L(a.ip, a.n_classes);
     GB_CUDA_CHECK(cudaFuncSetAttribute(sage_head_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

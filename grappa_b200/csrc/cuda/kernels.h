@@ -184,6 +184,11 @@ struct SageHeadArgs {
   int64_t ld_dl = 0;
   __nv_bfloat16* dx = nullptr;          // [cap, 2 ip] out: dlogits W (null: forward only)
   int64_t lddx = 0;
+  // tile version: the mean aggregation's backward of dx, fused: dsrc[v] += dx[v, :ip],
+  // dsrc[u] += dx[v, ip:] / deg(v) for the in-neighbours u (fp32 reductions; the rows
+  // of the previous layer's output, zero before)
+  float* dsrc = nullptr;
+  int64_t ld_dsrc = 0;
   float* loss_sum = nullptr;
   int32_t* correct = nullptr;
   float* dbias = nullptr;

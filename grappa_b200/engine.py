@@ -836,6 +836,10 @@ class SageEngine(BlockEngine):
                 spec["ce_fused"] = op <= 64
                 spec["head"] = (SAGE_FUSED_HEAD and l > 0 and not self.full_graph
                                 and self.cu.sage_head_supported(ip, self.n_classes))
+                # the previous layer keeps fp32 gradient rows (scatter backward): the head
+                # kernel reduces into them itself
+                spec["head_bwd"] = bool(spec["head"] and self.cu.sage_head_fused_bwd()
+                                        and "dH" in self.lay[l - 1])
                 if not spec["ce_fused"]:
                     spec["logits"] = torch.zeros((rows, op), dtype=torch.bfloat16, device=dev)
             if l > 0:
@@ -849,11 +853,15 @@ class SageEngine(BlockEngine):
             h = s["h"]
             src, src_map = self._input(l)
             if s.get("head"):
-                # aggregation, logits, loss, dlogits (dY) and dX of the output layer
+                # aggregation, logits, loss, dlogits (dY) and dX of the output layer; with
+                # the tile kernel also the aggregation's backward into the previous layer's
+                # fp32 gradient rows (no dX written)
                 labels, _, _ = self._labels_rows()
+                fused_bwd = training and s["head_bwd"]
                 cu.sage_head(sm.indptr[h], sm.indices[h], self._n_dst(h), sm.cap_dst[h], src, s["ip"], s["W"],
-                             s["bias"], self.n_classes, labels, s["X"], s["dY"], s["dX"] if training else None,
-                             self.fstats[2:3], self.istats[0:1], s["gb"] if training else None)
+                             s["bias"], self.n_classes, labels, s["X"], s["dY"],
+                             s["dX"] if training and not fused_bwd else None, self.fstats[2:3], self.istats[0:1],
+                             s["gb"] if training else None, dsrc=self.lay[l - 1]["dH"] if fused_bwd else None)
                 continue
             cu.aggregate(sm.indptr[h], sm.indices[h], self._n_dst(h), 0, sm.cap_dst[h], src, src_map,
                          s["ip"], AGG_MEAN, None, None, None, s["X"], s["ip"], 0, 0.0, 0, self.err)
@@ -890,9 +898,11 @@ class SageEngine(BlockEngine):
             cu.aggregate_bwd_gather(sm.indptr[h], sm.tptr[h], sm.tdst[h], self._n_dst(h), sm.n_src(h), s["dX"], 0,
                                     s["ip"], s["ip"], prev["H"], scale, prev["dY"], prev["gb"], self.err)
             return
-        # transpose aggregation: d(self) -> dst rows, d(agg) -> sources
-        cu.aggregate_bwd(sm.indptr[h], sm.indices[h], self._n_dst(h), 0, sm.cap_dst[h], s["dX"],
-                         s["ip"], 0, 0.0, s["ip"], AGG_MEAN, None, None, None, prev["dH"], self.err)
+        # transpose aggregation: d(self) -> dst rows, d(agg) -> sources (done by the
+        # fused output layer in the forward pass)
+        if not s.get("head_bwd"):
+            cu.aggregate_bwd(sm.indptr[h], sm.indices[h], self._n_dst(h), 0, sm.cap_dst[h], s["dX"],
+                             s["ip"], 0, 0.0, s["ip"], AGG_MEAN, None, None, None, prev["dH"], self.err)
         cu.act_bwd(prev["dH"], prev["H"], prev["dY"], self._n_dst(prev["h"]), 0, prev["op"], scale, prev["gb"],
                    prev["rows"])
 
