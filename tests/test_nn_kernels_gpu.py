@@ -327,3 +327,18 @@ def test_sage_head_matches_torch(ip, C, n_dst, max_deg):
     torch.testing.assert_close(db[:C].cpu(), bf(g).float().sum(0), atol=1e-4, rtol=1e-3)
     want_dx = bf(g).float() @ w[:C].float().cpu()
     torch.testing.assert_close(dx[:n_dst].float().cpu(), want_dx, atol=1e-4, rtol=2e-2)
+    if not cu().sage_head_fused_bwd():
+        return
+    # the aggregation's backward fused into the tile kernel (dx not written)
+    dsrc = torch.zeros(n_src, ip, device=DEV)
+    cu().sage_head(indptr.to(DEV), indices.to(DEV), nd, cap, h, ip, w, bias, C, labels, x, dl, None, loss, correct, db,
+                   dsrc=dsrc)
+    torch.cuda.synchronize()
+    gx = dx[:n_dst].float().cpu()
+    want = torch.zeros(n_src, ip)
+    want[:n_dst] += gx[:, :ip]
+    for v in range(n_dst):
+        u = indices[indptr[v]:indptr[v + 1]].long()
+        if u.numel():
+            want.index_add_(0, u, (gx[v, ip:] / u.numel()).expand(u.numel(), ip))
+    torch.testing.assert_close(dsrc.cpu(), want, atol=1e-5, rtol=1e-3)
