@@ -210,10 +210,74 @@ def head_case(n_dst=1021, n_src=3250, deg=5, ip=256, C=47):
             "aggregate_ce_gemm_dx_gemm_us": t_u * 1e3}
 
 
+def repart_case(n_part=600_000, deg=50, n_global=2_449_029, halo=400_000, dim=104):
+    """The repartition kernels on local memory (the peer pointers replaced by this GPU's
+    own buffers, so the numbers are HBM-side; over NVLink the same kernels read the
+    neighbour's memory): CSR merge of two partitions of n_part nodes and deg in-edges each
+    through the global-id map, halo compaction over n_global marks, a pull of `halo`
+    feature rows by global id and the bulk copy of a partition's rows.  CUDA-event
+    device times; achieved bytes against the measured HBM copy bandwidth."""
+    cu = _native.cuda()
+    dev = torch.device("cuda", 0)
+    i32, i64 = dict(dtype=torch.int32, device=dev), dict(dtype=torch.int64, device=dev)
+    E = n_part * deg
+    ip = torch.arange(0, (n_part + 1) * deg, deg, **i64)
+    ia = torch.randint(0, n_global, (E,), **i32)
+    ib = torch.randint(0, n_global, (E,), **i32)
+    mp = torch.randint(0, 2 * n_part + halo, (n_global,), **i32)
+    out_ip = torch.zeros(2 * n_part + 1, **i64)
+    out_ix = torch.zeros(2 * E, **i32)
+    err = torch.zeros(1, **i32)
+
+    def merge():
+        cu.csr_merge(ip.data_ptr(), ia.data_ptr(), n_part, ip.data_ptr(), ib.data_ptr(), n_part, mp, out_ip, out_ix,
+                     err)
+
+    t_merge = _time(merge, iters=20)
+    merge_bytes = 2 * E * 4 * 2 + 2 * E * 4 + 2 * (n_part + 1) * 8 * 2  # indices r/w, map gathers, indptr
+    mark = torch.zeros(n_global, dtype=torch.uint8, device=dev)
+    ids = torch.randint(0, n_global, (halo * 2,), **i32)
+    out_ids = torch.zeros(n_global, **i64)
+    n_out = torch.zeros(1, **i32)
+    scr = torch.zeros(cu.mark_compact_scratch_words(n_global), **i64)
+
+    def marks():
+        cu.mark_ids(ids.data_ptr(), None, ids.numel(), mark)
+        cu.mark_compact(mark, out_ids, mp, 0, n_out, scr, err)
+
+    t_marks = _time(marks, iters=20)
+    marks_bytes = ids.numel() * (4 + 32) + n_global + int(n_out.item()) * 12
+    table = torch.randn(n_global, dim, device=dev).to(torch.bfloat16)
+    gids = torch.randint(0, n_global, (halo,), **i64)
+    prefix = torch.tensor([0, n_global], **i64)
+    out = torch.zeros(halo, dim, device=dev, dtype=torch.bfloat16)
+
+    def pull():
+        cu.pull_rows([table.data_ptr()], dim, 2, dim * 2, gids, None, halo, prefix, out.data_ptr(), dim, 0, halo, err)
+
+    t_pull = _time(pull, iters=20)
+    pull_bytes = halo * (dim * 2 * 2 + 8)
+    rows = table[:n_part]
+    dst = torch.empty_like(rows)
+
+    def copy():
+        cu.peer_copy(dst.data_ptr(), rows.data_ptr(), rows.numel() * 2)
+
+    t_copy = _time(copy, iters=20)
+    copy_bytes = rows.numel() * 2 * 2
+    assert int(err.item()) == 0
+    res = []
+    for name, t, b in (("csr_merge", t_merge, merge_bytes), ("mark_ids+mark_compact", t_marks, marks_bytes),
+                       ("pull_rows", t_pull, pull_bytes), ("bulk_copy", t_copy, copy_bytes)):
+        res.append({"bench": "repartition_kernel", "kernel": name, "ms": t, "bytes": int(b),
+                    "frac_of_hbm": b / (t * 1e-3) / 1e9 / HBM_GBS})
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--scale", type=float, default=1.0)
-    ap.add_argument("--part", default="gemm,aggregate", help="comma list of gemm, aggregate, head, ar")
+    ap.add_argument("--part", default="gemm,aggregate", help="comma list of gemm, aggregate, head, repart, ar")
     ap.add_argument("--ar-bytes", type=int, default=256 << 20)
     a = ap.parse_args()
     s = a.scale
@@ -230,6 +294,8 @@ def main():
                  aggregate_case(int(3250 * s), int(20853 * s), 8, 256)]
     if "head" in parts:
         rows += [head_case()]
+    if "repart" in parts:
+        rows += repart_case()
     if "ar" in parts:
         rows += [ar_case(a.ar_bytes, 1), ar_case(a.ar_bytes, 0), ar_case(a.ar_bytes, 1, torch.bfloat16)]
     for r in rows:
