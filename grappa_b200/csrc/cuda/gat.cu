@@ -1053,6 +1053,15 @@ void gat_bwd_pair(const GatArgs& a, cudaStream_t stream) {
     if (occ == 2) return gat_bwd_launch<CPL, CPLY, SEG, 0, 2>(a, stream);
     if (occ >= 3) return gat_bwd_launch<CPL, CPLY, SEG, 3, 3>(a, stream);
   }
+  if constexpr (CPL == 4 && !SEG && CPLY == 0) {
+    // wide last layer (H * F up to 1024): GRAPPA_GAT_OCC_LAST=2 caps its edge pass for
+    // 2 CTAs per SM (219 -> 128 registers)
+    static const int last = [] {
+      const char* e = std::getenv("GRAPPA_GAT_OCC_LAST");
+      return e ? std::atoi(e) : 0;
+    }();
+    if (last == 2) return gat_bwd_launch<CPL, CPLY, SEG, 2, 0>(a, stream);
+  }
   gat_bwd_launch<CPL, CPLY, SEG, 0, 0>(a, stream);
 }
 
