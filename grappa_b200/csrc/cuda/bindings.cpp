@@ -103,7 +103,7 @@ int64_t compact_scratch_words(int64_t cap_e) { return d::compact_scan_scratch_wo
 
 void compact(Tensor dst_nid, Tensor n_dst_dev, Tensor nbr, Tensor n_edges_dev, Tensor map, Tensor src_nid,
              Tensor src_sampled, Tensor indices, Tensor n_src_out, Tensor scan_scratch, Tensor err, int64_t cap_dst,
-             int64_t cap_edges, Tensor counters, int64_t slot, bool k1_done, OptT t_cnt, OptT t_rank) {
+             int64_t cap_edges, Tensor counters, int64_t slot, bool k1_done, OptT t_cnt, OptT t_rank, bool run_k3) {
   c10::cuda::CUDAGuard g(dst_nid.device());
   TORCH_CHECK(slot >= 0 && slot < 16, "slot must be in [0, 16)");
   TORCH_CHECK(counters.numel() >= 6, "counters needs 6 entries");
@@ -131,8 +131,33 @@ void compact(Tensor dst_nid, Tensor n_dst_dev, Tensor nbr, Tensor n_edges_dev, T
   TORCH_CHECK(scan_scratch.numel() == d::compact_scan_scratch_words(static_cast<int>(cap_edges)),
               "scan_scratch must hold exactly compact_scratch_words(capacity) words and be used with that capacity only");
   const int64_t* gen = ptr<int64_t>(counters, at::kLong, "counters") + 4;
+  TORCH_CHECK(run_k3 || !a.t_cnt, "the transpose counters are made by K3: run it with the hop");
   d::launch_compact(a, static_cast<int>(cap_dst), static_cast<int>(cap_edges), gen, static_cast<int>(slot), num_sms(),
-                    stream(), k1_done);
+                    stream(), k1_done, run_k3);
+}
+
+// K3 of several hops after the last hop's K2 (see compact.cu)
+void compact_edges(std::vector<Tensor> nbr, std::vector<Tensor> n_edges_dev, std::vector<Tensor> indices,
+                   std::vector<int64_t> cap_src, Tensor map) {
+  c10::cuda::CUDAGuard g(map.device());
+  const size_t n = nbr.size();
+  TORCH_CHECK(n >= 1 && n <= static_cast<size_t>(d::CompactEdgesArgs::kMaxHops) && n_edges_dev.size() == n &&
+                  indices.size() == n && cap_src.size() == n,
+              "compact_edges: one nbr, count, indices and capacity per hop (1..8 hops)");
+  d::CompactEdgesArgs a;
+  int64_t total = 0;
+  for (size_t h = 0; h < n; ++h) {
+    TORCH_CHECK(indices[h].numel() >= nbr[h].numel(), "compact_edges: indices shorter than nbr");
+    a.hops[h].nbr = ptr<int32_t>(nbr[h], at::kInt, "nbr");
+    a.hops[h].n_edges_ptr = ptr<int32_t>(n_edges_dev[h], at::kInt, "n_edges_dev");
+    a.hops[h].indices = ptr<int32_t>(indices[h], at::kInt, "indices");
+    a.hops[h].cap_src = static_cast<int32_t>(cap_src[h]);
+    total = std::max<int64_t>(total, nbr[h].numel());
+  }
+  a.n_hops = static_cast<int32_t>(n);
+  a.map = reinterpret_cast<const unsigned long long*>(ptr<int64_t>(map, at::kLong, "map"));
+  a.n_graph_nodes = map.numel();
+  d::launch_compact_edges(a, total, num_sms(), stream());
 }
 
 void block_transpose(Tensor indptr, Tensor indices, Tensor n_dst_dev, Tensor n_src_dev, Tensor t_cnt, Tensor t_rank,
@@ -1130,7 +1155,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("compact", &compact, py::arg("dst_nid"), py::arg("n_dst_dev"), py::arg("nbr"), py::arg("n_edges_dev"),
         py::arg("map"), py::arg("src_nid"), py::arg("src_sampled"), py::arg("indices"), py::arg("n_src_out"),
         py::arg("scan_scratch"), py::arg("err"), py::arg("cap_dst"), py::arg("cap_edges"), py::arg("counters"),
-        py::arg("slot"), py::arg("k1_done") = false, py::arg("t_cnt") = py::none(), py::arg("t_rank") = py::none());
+        py::arg("slot"), py::arg("k1_done") = false, py::arg("t_cnt") = py::none(), py::arg("t_rank") = py::none(),
+        py::arg("run_k3") = true);
+  m.def("compact_edges", &compact_edges, py::arg("nbr"), py::arg("n_edges_dev"), py::arg("indices"),
+        py::arg("cap_src"), py::arg("map"));
   m.def("compact_scratch_words", &compact_scratch_words);
   m.def("block_transpose", &block_transpose);
   m.def("aggregate_bwd_gather", &aggregate_bwd_gather);

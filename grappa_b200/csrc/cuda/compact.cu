@@ -88,6 +88,11 @@ __global__ void __launch_bounds__(kThreads) compact_k2(CompactArgs a, const int6
       if (ids[q] >= 0 && ids[q] < a.n_graph_nodes) {
         const unsigned long long m = a.map[ids[q]];
         fresh[q] = m == (tw | static_cast<unsigned long long>(n_dst + e));
+        // a destination node sampled as a neighbour: part of the next hop's frontier
+        // (marked here so that the edge rewrite K3 can run after the later hops)
+        const unsigned long long pos = m & 0xffffffffull;
+        if (!fresh[q] && (m >> 32) == (tw >> 32) && pos < static_cast<unsigned long long>(n_dst))
+          a.src_sampled[pos] = 1;
       }
       cnt += fresh[q];
     }
@@ -106,7 +111,7 @@ __global__ void __launch_bounds__(kThreads) compact_k2(CompactArgs a, const int6
     if (lid < a.cap_src) {
       a.map[ids[q]] = tw | static_cast<unsigned long long>(lid);
       a.src_nid[lid] = ids[q];
-      a.src_sampled[lid] = 0;
+      a.src_sampled[lid] = 1;  // first appearance as a neighbour
     } else {
       set_error(a.err, kErrCapacity);
     }
@@ -131,6 +136,27 @@ __global__ void __launch_bounds__(kThreads) compact_k3(CompactArgs a) {
     a.indices[e] = lid;
     a.src_sampled[lid] = 1;
     if (a.t_cnt) a.t_rank[e] = atomicAdd(a.t_cnt + lid, 1);
+  }
+}
+
+// K3 of several hops in one launch, after the last hop's K2.  A node's local position
+// survives the later hops' passes: the next hop's destinations are this hop's sources
+// in order, so its K1 writes the same position under a new tag, and its K2 rewrites only
+// nodes that are not among them; so low32(map[id]) still is the local source index of
+// every neighbour id of every earlier hop.
+__global__ void __launch_bounds__(kThreads) compact_k3_multi(CompactEdgesArgs a) {
+  GB_PDL_ENTRY();
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (int h = 0; h < a.n_hops; ++h) {
+    const CompactEdgesArgs::Hop hp = a.hops[h];
+    const int n_e = *hp.n_edges_ptr;
+    for (long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < n_e; e += stride) {
+      const int32_t id = hp.nbr[e];
+      int32_t lid = 0;
+      if (id >= 0 && id < a.n_graph_nodes) lid = static_cast<int32_t>(a.map[id] & 0xffffffffull);
+      if (lid >= hp.cap_src || lid < 0) lid = 0;
+      hp.indices[e] = lid;
+    }
   }
 }
 
@@ -202,8 +228,16 @@ int compact_scan_scratch_words(int cap_edges) {
   return static_cast<int>(ceil_div(cap_edges > 0 ? cap_edges : 1, kTile)) + 1;
 }
 
+void launch_compact_edges(const CompactEdgesArgs& a, int64_t cap_edges_total, int num_sms, cudaStream_t stream) {
+  if (a.n_hops < 1 || a.n_hops > CompactEdgesArgs::kMaxHops) throw std::invalid_argument("compact_edges: 1..8 hops");
+  const int g = static_cast<int>(std::min<long long>(static_cast<long long>(num_sms) * 8,
+                                                     ceil_div(cap_edges_total > 0 ? cap_edges_total : 1, kThreads)));
+  launch_k(compact_k3_multi, g, kThreads, 0, stream, a);
+  GB_LAUNCH_CHECK();
+}
+
 void launch_compact(const CompactArgs& a, int cap_dst, int cap_edges, const int64_t* gen, int slot, int num_sms,
-                    cudaStream_t stream, bool k1_done) {
+                    cudaStream_t stream, bool k1_done, bool run_k3) {
   const int grid_stride = num_sms * 8;
   if (!k1_done) {
     const long long work1 = static_cast<long long>(cap_dst) + cap_edges;
@@ -215,6 +249,7 @@ void launch_compact(const CompactArgs& a, int cap_dst, int cap_edges, const int6
   // no clearing of the scan scratch: its look-back words carry the launch number
   launch_k(compact_k2, tiles, kThreads, 0, stream, a, gen, slot);
   GB_LAUNCH_CHECK();
+  if (!run_k3) return;
   const int g3 = static_cast<int>(std::min<long long>(grid_stride, ceil_div(cap_edges > 0 ? cap_edges : 1, kThreads)));
   launch_k(compact_k3, g3, kThreads, 0, stream, a);
   GB_LAUNCH_CHECK();

@@ -90,8 +90,24 @@ struct CompactArgs {
 };
 // gen: device generation counter; tags are derived on the device from (*gen, slot)
 // so that a captured graph keeps drawing fresh tags (slot < 16 per generation).
+// run_k3 = false: the edge rewrite is left to launch_compact_edges after the last hop
 void launch_compact(const CompactArgs& a, int cap_dst, int cap_edges, const int64_t* gen, int slot, int num_sms,
-                    cudaStream_t stream, bool k1_done = false);
+                    cudaStream_t stream, bool k1_done = false, bool run_k3 = true);
+// the edge rewrite (K3: indices[e] = local index of nbr[e]) of several hops in one launch
+struct CompactEdgesArgs {
+  static constexpr int kMaxHops = 8;
+  struct Hop {
+    const int32_t* nbr = nullptr;
+    const int32_t* n_edges_ptr = nullptr;
+    int32_t* indices = nullptr;
+    int32_t cap_src = 0;
+  };
+  Hop hops[kMaxHops];
+  int32_t n_hops = 0;
+  const unsigned long long* map = nullptr;
+  int64_t n_graph_nodes = 0;
+};
+void launch_compact_edges(const CompactEdgesArgs& a, int64_t cap_edges_total, int num_sms, cudaStream_t stream);
 int compact_scan_scratch_words(int cap_edges);
 
 // The block's edges grouped by source (CSR by local src): tptr[n_src + 1] from an

@@ -81,7 +81,7 @@ KERNELS_PER_CALL = {
     "l2norm_bwd": 1, "dropout_rows": 1, "dropout_grad": 1, "f32_to_bf16_rows": 1, "add_bf16_rows": 1,
     "gat_scores": 1, "gat_fwd": 1, "gat_bwd": 2, "gat_bwd_input": 2, "gat_dw_combine": 1, "sampler_counters": 1,
     "gat_in_scores": 1, "gat_in_fwd": 1, "gat_in_bwd": 2, "gat_in_prep": 1, "gat_in_dw": 1, "col_sum_bf16": 1,
-    "block_transpose": 2, "aggregate_bwd_gather": 1, "sage_head": 1,
+    "block_transpose": 2, "aggregate_bwd_gather": 1, "sage_head": 1, "compact_edges": 1,
 }
 
 
@@ -106,6 +106,8 @@ class LaunchCounter:
             n = k
             if name == "compact" and ((len(a) > 15 and a[15]) or kw.get("k1_done")):
                 n -= 1  # the first pass ran inside the sampling kernel
+            if name == "compact" and kw.get("run_k3") is False:
+                n -= 1  # the edge rewrite runs in compact_edges
             self.count += n
             if self.timer is None:
                 return f(*a, **kw)

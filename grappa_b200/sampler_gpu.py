@@ -119,12 +119,17 @@ class GpuNeighborSampler:
                           cov if h == 0 else None, self.indptr[h], self.nbr[h], self.n_edges(h), self.sscr[h], err,
                           self.cap_dst[h], self.map, self.src[h], self.sampled[h])
             tr = h in self.t_cnt
+            # without block transposes every hop's edge rewrite (K3) waits for one launch
+            # after the last hop (compact_edges): the next hop needs only K2's outputs
             cu.compact(dst, self.n_dst(h), self.nbr[h], self.n_edges(h), self.map, self.src[h], self.sampled[h],
                        self.indices[h], self.n_src(h), self.cscr[h], err, self.cap_dst[h], self.cap_e[h], counters, h,
-                       True, self.t_cnt.get(h), self.t_rank.get(h))
+                       True, self.t_cnt.get(h), self.t_rank.get(h), run_k3=bool(self.t_cnt))
             if tr:
                 cu.block_transpose(self.indptr[h], self.indices[h], self.n_dst(h), self.n_src(h), self.t_cnt[h],
                                    self.t_rank[h], self.tptr[h], self.tdst[h], err)
+        if not self.t_cnt:
+            cu.compact_edges(self.nbr, [self.n_edges(h) for h in range(self.L)], self.indices,
+                             [self.cap_src[h] for h in range(self.L)], self.map)
 
     def blocks(self):
         """Materialise the sampled blocks (input layer first) with exact sizes (host sync)."""
