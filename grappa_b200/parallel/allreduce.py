@@ -56,12 +56,14 @@ class FusedAllReduceAdam:
     @staticmethod
     def one_shot_max_bytes(world):
         # one-shot reads W-1 peer copies against 2 (W-1)/W for the shard mode, but pays
-        # one flag round trip instead of two
+        # one flag round trip instead of two.  Measured crossovers (fp32): W = 2 between
+        # 4 and 16 MB, W = 4 at 4 MB (41.0 vs 41.8 us), W = 8 between 1 MB (36.2 vs
+        # 54.8 us) and 4 MB (82.7 vs 60.3 us)
         if world <= 2:
             return 8 << 20
         if world <= 4:
-            return 1 << 20
-        return 256 << 10
+            return 4 << 20
+        return 2 << 20
 
     def __init__(self, comm, n, buckets=None, grad_dtype=torch.float32, modes=None, timeout_s=30.0, grids=None):
         from grappa_b200.parallel.comm import PeerBuffer
