@@ -180,8 +180,8 @@ class PartitionStore:
         sz = self._sizes
         n_r, n_q = own.n_nodes, sz[q]["n"]
         peer = self._peer
-        # events: start, marks + halo compaction, CSR merge, halo rows, end (main stream);
-        # feature-copy start and end (side stream)
+        # events: start, marks + halo compaction, CSR merge, end (main stream); halo rows
+        # done (second side stream); feature-copy start and end (side stream)
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
         ev[0].record()
         # q's feature rows (the largest transfer, independent of the CSR and halo work)
@@ -207,16 +207,22 @@ class PartitionStore:
         cu.iota_map(self._map, own.prefix[q], n_q, n_r, self._mark)
         cu.mark_compact(self._mark, self._halo_ids, self._map, n_r + n_q, self._n_halo, self._mc_scratch, self.err)
         ev[1].record()
-        # 2. working CSR: own in-edges, then q's in-edges pulled from q, sources translated
+        # 2. halo feature rows from their owners, on a second side stream beside the CSR
+        # merge (both need only the halo ids and the map)
+        if getattr(self, "_side2", None) is None:
+            self._side2 = torch.cuda.Stream(device=self.device)
+        self._side2.wait_stream(main)
+        tables = [peer["feat"].ptrs[p] for p in range(self.world)]
+        with torch.cuda.stream(self._side2):
+            cu.pull_rows(tables, fs, esz, fs * esz, self._halo_ids, self._n_halo, 0, self._prefix_dev,
+                         self._feat_w.data_ptr(), fs, n_r + n_q, self._halo_ids.numel(), self.err)
+            ev[3].record()
+        # 3. working CSR: own in-edges, then q's in-edges pulled from q, sources translated
         cu.csr_merge(peer["indptr"].ptrs[r], peer["indices"].ptrs[r], n_r, peer["indptr"].ptrs[q],
                      peer["indices"].ptrs[q], n_q, self._map, self._indptr_w, self._indices_w, self.err)
         ev[2].record()
-        # 3. halo feature rows from their owners (q's rows are on the side stream)
-        tables = [peer["feat"].ptrs[p] for p in range(self.world)]
-        cu.pull_rows(tables, fs, esz, fs * esz, self._halo_ids, self._n_halo, 0, self._prefix_dev,
-                     self._feat_w.data_ptr(), fs, n_r + n_q, self._halo_ids.numel(), self.err)
-        ev[3].record()
         main.wait_stream(self._side)
+        main.wait_stream(self._side2)
         ev[4].record()
         # bytes this rank pulls over NVLink: q's external-source list and CSR, q's feature
         # rows and the halo rows (their count is on the device until the log is read)
@@ -241,8 +247,8 @@ class PartitionStore:
             t = lambda i, j: round(ev[i].elapsed_time(ev[j]), 4)  # noqa: E731
             out.append({"ms": round(ms, 4), "bytes": int(b),
                         "frac_of_link_roofline": round(b / (link_gbs * 1e9) * 1e3 / ms, 4) if ms > 0 else None,
-                        "phases_ms": {"marks": t(0, 1), "csr_merge": t(1, 2), "halo_rows": t(2, 3),
-                                      "feature_copy": t(5, 6), "join": t(3, 4)},
+                        "phases_ms": {"marks": t(0, 1), "csr_merge": t(1, 2), "halo_rows": t(1, 3),
+                                      "feature_copy": t(5, 6), "join": round(max(t(2, 4), 0.0), 4)},
                         "csr_gbs": round(rec["csr_bytes"] / max(t(1, 2), 1e-6) / 1e6, 1),
                         "feature_gbs": round(rec["feat_bytes"] / max(t(5, 6), 1e-6) / 1e6, 1)})
         return out
