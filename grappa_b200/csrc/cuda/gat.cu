@@ -224,8 +224,8 @@ __global__ void __launch_bounds__(kThreads, MINB) gat_fwd_kernel(GatArgs a) {
   if (a.dropout_p > 0.f) {
     key = hop_key(static_cast<uint64_t>(a.counters[0]) ^ 0xD80Full, static_cast<uint64_t>(a.counters[1]),
                   static_cast<uint64_t>(a.counters[2]), a.dropout_salt);
-    thr = static_cast<uint32_t>(static_cast<double>(a.dropout_p) * 4294967296.0);
-    ks = 1.f / (1.f - a.dropout_p);
+    thr = dropout_thr8(a.dropout_p);
+    ks = dropout_scale8(thr);
   }
   constexpr int EU = EU_ > 0 ? EU_ : (CPL <= 1 ? 4 : 2);  // edges whose z rows are in flight together
   int h0[CPL], h1[CPL];
@@ -356,11 +356,9 @@ __global__ void __launch_bounds__(kThreads, MINB) gat_fwd_kernel(GatArgs a) {
         }
         if (a.dropout_p > 0.f) {
           const uint64_t base = static_cast<uint64_t>(v) * static_cast<uint64_t>(a.ldo) + static_cast<uint64_t>(c0);
-          const U4 r0 = index_draw4(key, base >> 2, 0);
-          const U4 r1 = index_draw4(key, (base >> 2) + 1, 0);
-          const uint32_t w[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+          const uint32_t keep = dropout_keep_bits(key, base, 8, thr);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) o[j] = w[j] >= thr ? o[j] * ks : 0.f;
+          for (int j = 0; j < 8; ++j) o[j] = (keep >> j) & 1u ? o[j] * ks : 0.f;
         }
         *reinterpret_cast<uint4*>(a.out + static_cast<int64_t>(v) * a.ldo + c0) = f32_to_bf16x8(o);
       }

@@ -231,8 +231,8 @@ __device__ __forceinline__ void store_tile(const GemmArgs& a, const CUtensorMap*
                                               static_cast<uint64_t>(a.counters[1]),
                                               static_cast<uint64_t>(a.counters[2]), a.dropout_salt)
                                     : 0ull;
-    const float keep_scale = a.dropout_p > 0.f ? 1.0f / (1.0f - a.dropout_p) : 1.0f;
-    const uint32_t thr = static_cast<uint32_t>(static_cast<double>(a.dropout_p) * 4294967296.0);
+    const uint32_t thr8 = dropout_thr8(a.dropout_p);
+    const float keep_scale = dropout_scale8(thr8);
     const bool live = m < M;
     // a 32-row slab that crosses the live row count stores its live rows directly,
     // so that rows >= M are never written (except the zeroed tail rows)
@@ -257,14 +257,9 @@ __device__ __forceinline__ void store_tile(const GemmArgs& a, const CUtensorMap*
       if (a.att_el && live && nc < a.N) att_logits(a, m, nc, v);
       if (a.dropout_p > 0.f && live) {
         const uint64_t base = static_cast<uint64_t>(m) * static_cast<uint64_t>(a.ldc) + static_cast<uint64_t>(nc);
+        const uint32_t keep = dropout_keep_bits(key, base, 32, thr8);
 #pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-          const U4 r = index_draw4(key, (base + j) >> 2, 0);
-          v[j] = r.x >= thr ? v[j] * keep_scale : 0.f;
-          v[j + 1] = r.y >= thr ? v[j + 1] * keep_scale : 0.f;
-          v[j + 2] = r.z >= thr ? v[j + 2] * keep_scale : 0.f;
-          v[j + 3] = r.w >= thr ? v[j + 3] * keep_scale : 0.f;
-        }
+        for (int j = 0; j < 32; ++j) v[j] = (keep >> j) & 1u ? v[j] * keep_scale : 0.f;
       }
       if (slab_full) {
         uint8_t* panel = stage + ((c - c_begin) >> 6) * 4096 + lane * 128;
@@ -299,8 +294,8 @@ __device__ __forceinline__ void store_tile(const GemmArgs& a, const CUtensorMap*
                                               static_cast<uint64_t>(a.counters[1]),
                                               static_cast<uint64_t>(a.counters[2]), a.dropout_salt)
                                     : 0ull;
-    const float keep_scale = a.dropout_p > 0.f ? 1.0f / (1.0f - a.dropout_p) : 1.0f;
-    const uint32_t thr = static_cast<uint32_t>(static_cast<double>(a.dropout_p) * 4294967296.0);
+    const uint32_t thr8 = dropout_thr8(a.dropout_p);
+    const float keep_scale = dropout_scale8(thr8);
     const int64_t tail_end = a.zero_tail_rows > 0
                                  ? min(static_cast<int64_t>(ceil_div(M, a.zero_tail_rows)) * a.zero_tail_rows, a.c_rows)
                                  : 0;
@@ -336,16 +331,11 @@ __device__ __forceinline__ void store_tile(const GemmArgs& a, const CUtensorMap*
       if (a.act_mask) apply_act_mask(a, m, nc, v);
       if (a.att_el) att_logits(a, m, nc, v);
       if (a.dropout_p > 0.f) {
+        // one Philox call covers 16 consecutive elements (byte-resolution masks)
         const uint64_t base = static_cast<uint64_t>(m) * static_cast<uint64_t>(a.ldc) + static_cast<uint64_t>(nc);
+        const uint32_t keep = dropout_keep_bits(key, base, 32, thr8);
 #pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-          // one Philox call covers 4 consecutive elements (base + j is a multiple of 4)
-          const U4 r = index_draw4(key, (base + j) >> 2, 0);
-          v[j] = r.x >= thr ? v[j] * keep_scale : 0.f;
-          v[j + 1] = r.y >= thr ? v[j + 1] * keep_scale : 0.f;
-          v[j + 2] = r.z >= thr ? v[j + 2] * keep_scale : 0.f;
-          v[j + 3] = r.w >= thr ? v[j + 3] * keep_scale : 0.f;
-        }
+        for (int j = 0; j < 32; ++j) v[j] = (keep >> j) & 1u ? v[j] * keep_scale : 0.f;
       }
       if (a.c_mode == kStoreBf16) {
         __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.C) + static_cast<int64_t>(m) * a.ldc + nc;

@@ -220,8 +220,7 @@ __global__ void dropout_mask_kernel(uint8_t* mask, int64_t rows, int64_t cols, i
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t r = i / cols, c = i % cols;
     const uint64_t idx = static_cast<uint64_t>(r) * static_cast<uint64_t>(ld) + static_cast<uint64_t>(c);
-    const U4 w = index_draw4(key, idx >> 2, 0);
-    mask[i] = u4_word(w, static_cast<int>(idx & 3)) >= thr ? 1 : 0;
+    mask[i] = static_cast<uint8_t>(dropout_keep_bits(key, idx, 1, thr) & 1u);
   }
 }
 
@@ -421,7 +420,7 @@ void launch_normal_rows_bf16(__nv_bfloat16* out, int64_t ld, int64_t row0, int64
 
 void launch_dropout_mask(uint8_t* mask, int64_t rows, int64_t cols, int64_t ld, float p, const int64_t* counters,
                          uint32_t salt, cudaStream_t stream) {
-  const uint32_t thr = static_cast<uint32_t>(static_cast<double>(p) * 4294967296.0);
+  const uint32_t thr = dropout_thr8(p);
   launch_k(dropout_mask_kernel, grid_1d(rows * cols, 256, 16), 256, 0, stream, mask, rows, cols, ld, thr, counters, salt);
   GB_LAUNCH_CHECK();
 }

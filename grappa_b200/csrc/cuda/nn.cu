@@ -367,8 +367,8 @@ __global__ void dropout_rows_kernel(const __nv_bfloat16* in, int64_t ldi, __nv_b
   const int rows_end = tail_rows(n, cap, 64);
   const int chunks = dim >> 3;
   const uint64_t key = dropout_key(counters, salt);
-  const uint32_t thr = static_cast<uint32_t>(static_cast<double>(p) * 4294967296.0);
-  const float ks = p > 0.f ? 1.f / (1.f - p) : 1.f;
+  const uint32_t thr = dropout_thr8(p);
+  const float ks = dropout_scale8(thr);
   const int64_t total = static_cast<int64_t>(rows_end) * chunks;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -382,11 +382,9 @@ __global__ void dropout_rows_kernel(const __nv_bfloat16* in, int64_t ldi, __nv_b
     float f[8];
     bf16x8_to_f32(*reinterpret_cast<const uint4*>(in + static_cast<int64_t>(r) * ldi + c), f);
     const uint64_t base = static_cast<uint64_t>(r) * static_cast<uint64_t>(ld_mask) + static_cast<uint64_t>(c);
-    const U4 r0 = index_draw4(key, base >> 2, 0);
-    const U4 r1 = index_draw4(key, (base >> 2) + 1, 0);
-    const uint32_t w[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+    const uint32_t keep = dropout_keep_bits(key, base, 8, thr);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) f[j] = w[j] >= thr ? f[j] * ks : 0.f;
+    for (int j = 0; j < 8; ++j) f[j] = (keep >> j) & 1u ? f[j] * ks : 0.f;
     *op = f32_to_bf16x8(f);
   }
 }
@@ -397,8 +395,8 @@ __global__ void dropout_grad_kernel(float* g, int64_t ldg, int dim, int64_t ld_m
   const int n = live_rows(n_ptr, cap);
   const int chunks = dim >> 3;
   const uint64_t key = dropout_key(counters, salt);
-  const uint32_t thr = static_cast<uint32_t>(static_cast<double>(p) * 4294967296.0);
-  const float ks = p > 0.f ? 1.f / (1.f - p) : 1.f;
+  const uint32_t thr = dropout_thr8(p);
+  const float ks = dropout_scale8(thr);
   const int64_t total = static_cast<int64_t>(n) * chunks;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -406,11 +404,9 @@ __global__ void dropout_grad_kernel(float* g, int64_t ldg, int dim, int64_t ld_m
     const int c = static_cast<int>(i % chunks) * 8;
     float* gp = g + static_cast<int64_t>(r) * ldg + c;
     const uint64_t base = static_cast<uint64_t>(r) * static_cast<uint64_t>(ld_mask) + static_cast<uint64_t>(c);
-    const U4 r0 = index_draw4(key, base >> 2, 0);
-    const U4 r1 = index_draw4(key, (base >> 2) + 1, 0);
-    const uint32_t w[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+    const uint32_t keep = dropout_keep_bits(key, base, 8, thr);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) gp[j] = w[j] >= thr ? gp[j] * ks : 0.f;
+    for (int j = 0; j < 8; ++j) gp[j] = (keep >> j) & 1u ? gp[j] * ks : 0.f;
   }
 }
 

@@ -178,8 +178,8 @@ __global__ void __launch_bounds__(kThreads) aggregate_kernel(AggArgs a) {
       if (a.dropout_p > 0.f) {
         key = hop_key(static_cast<uint64_t>(a.counters[0]) ^ 0xD80Full, static_cast<uint64_t>(a.counters[1]),
                       static_cast<uint64_t>(a.counters[2]), a.dropout_salt);
-        thr = static_cast<uint32_t>(static_cast<double>(a.dropout_p) * 4294967296.0);
-        keep_scale = 1.f / (1.f - a.dropout_p);
+        thr = dropout_thr8(a.dropout_p);
+        keep_scale = dropout_scale8(thr);
       }
 #pragma unroll
       for (int q = 0; q < CPL; ++q) {
@@ -209,16 +209,9 @@ __global__ void __launch_bounds__(kThreads) aggregate_kernel(AggArgs a) {
         if (a.dropout_p > 0.f) {
           const uint64_t base = static_cast<uint64_t>(row) * static_cast<uint64_t>(a.out_stride) +
                                 static_cast<uint64_t>(a.agg_col + c * 8);
-          const U4 r0 = index_draw4(key, base >> 2, 0);
-          const U4 r1 = index_draw4(key, (base >> 2) + 1, 0);
-          o[0] = r0.x >= thr ? o[0] * keep_scale : 0.f;
-          o[1] = r0.y >= thr ? o[1] * keep_scale : 0.f;
-          o[2] = r0.z >= thr ? o[2] * keep_scale : 0.f;
-          o[3] = r0.w >= thr ? o[3] * keep_scale : 0.f;
-          o[4] = r1.x >= thr ? o[4] * keep_scale : 0.f;
-          o[5] = r1.y >= thr ? o[5] * keep_scale : 0.f;
-          o[6] = r1.z >= thr ? o[6] * keep_scale : 0.f;
-          o[7] = r1.w >= thr ? o[7] * keep_scale : 0.f;
+          const uint32_t keep = dropout_keep_bits(key, base, 8, thr);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] = (keep >> j) & 1u ? o[j] * keep_scale : 0.f;
         }
         *reinterpret_cast<uint4*>(a.out + row * a.out_stride + a.agg_col + c * 8) = f32_to_bf16x8(o);
       }

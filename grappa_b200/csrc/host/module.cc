@@ -408,19 +408,18 @@ PYBIND11_MODULE(_C, m) {
     return to_py(std::move(out));
   });
 
-  // Dropout keep-mask with the same Philox stream as the GEMM epilogue on the GPU:
-  // element (r, c) of a row-major buffer with row stride ld is kept iff the draw of
-  // linear index r*ld + c is >= p * 2^32 (key from seed, epoch, step, salt).
+  // Dropout keep-mask with the same Philox stream as the GPU kernels: element (r, c)
+  // of a row-major buffer with row stride ld is kept iff byte (idx % 16) of the draw of
+  // group idx / 16 (idx = r*ld + c) is >= round(p * 256) (key from seed, epoch, step, salt).
   m.def("dropout_mask", [](uint64_t seed, uint64_t epoch, uint64_t step, uint32_t salt, int64_t rows,
                            int64_t cols, int64_t ld, double p) {
     std::vector<uint8_t> mask(static_cast<size_t>(rows * cols));
     const uint64_t key = grappa::hop_key(seed ^ 0xD80Full, epoch, step, salt);
-    const uint32_t thr = static_cast<uint32_t>(p * 4294967296.0);
+    const uint32_t thr = grappa::dropout_thr8(static_cast<float>(p));
 #pragma omp parallel for schedule(static)
     for (int64_t i = 0; i < rows * cols; ++i) {
       const uint64_t idx = static_cast<uint64_t>(i / cols) * static_cast<uint64_t>(ld) + static_cast<uint64_t>(i % cols);
-      const grappa::U4 w = grappa::index_draw4(key, idx >> 2, 0);
-      mask[i] = grappa::u4_word(w, static_cast<int>(idx & 3)) >= thr ? 1 : 0;
+      mask[i] = static_cast<uint8_t>(grappa::dropout_keep_bits(key, idx, 1, thr) & 1u);
     }
     return to_py(std::move(mask));
   });

@@ -89,6 +89,39 @@ GB_HD U4 index_draw4(uint64_t key, uint64_t idx, uint32_t salt) {
   return philox4x32_10(c, static_cast<uint32_t>(key), static_cast<uint32_t>(key >> 32));
 }
 
+// Dropout masks at byte resolution: the probability is quantised to t / 256
+// (t = round(p * 256)) and element idx is kept iff byte idx % 16 of the 16-byte draw of
+// group idx / 16 is >= t, so one Philox call serves 16 elements; kept values are scaled
+// by 256 / (256 - t), which keeps the expectation exact for the quantised probability.
+constexpr uint32_t kDropoutSalt = 0x44u;
+GB_HD uint32_t dropout_thr8(float p) {
+  int t = static_cast<int>(p * 256.0f + 0.5f);
+  return static_cast<uint32_t>(t < 0 ? 0 : (t > 255 ? 255 : t));
+}
+GB_HD float dropout_scale8(uint32_t thr8) { return 256.0f / static_cast<float>(256u - thr8); }
+// bit b: byte b of the draw is >= thr8
+GB_HD uint32_t keep16(const U4& r, uint32_t thr8) {
+  uint32_t k = 0;
+  const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+  for (int i = 0; i < 4; ++i)
+    for (int b = 0; b < 4; ++b)
+      if (((w[i] >> (8 * b)) & 0xFFu) >= thr8) k |= 1u << (4 * i + b);
+  return k;
+}
+// keep bits of the n <= 32 consecutive elements base .. base + n - 1 (bit j: base + j)
+GB_HD uint32_t dropout_keep_bits(uint64_t key, uint64_t base, int n, uint32_t thr8) {
+  uint64_t g = base >> 4;
+  const int off = static_cast<int>(base & 15u);
+  uint64_t acc = static_cast<uint64_t>(keep16(index_draw4(key, g, kDropoutSalt), thr8)) >> off;
+  int have = 16 - off;
+  while (have < n) {
+    ++g;
+    acc |= static_cast<uint64_t>(keep16(index_draw4(key, g, kDropoutSalt), thr8)) << have;
+    have += 16;
+  }
+  return n >= 32 ? static_cast<uint32_t>(acc) : static_cast<uint32_t>(acc & ((1ull << n) - 1));
+}
+
 // Uniform float in [0, 1) from the top 24 bits of a draw.
 GB_HD float u01(uint32_t r) { return static_cast<float>(r >> 8) * (1.0f / 16777216.0f); }
 

@@ -145,6 +145,15 @@ def gemm_bn(M_cap, N, mn_major=False, sms=148):
     return bn
 
 
+def dropout_scale(p):
+    """Scale of the kept values of the kernels' dropout masks: the probability is
+    quantised to t / 256 (byte-resolution masks, grappa/rng.h), t = round(256 p)."""
+    if p <= 0:
+        return 1.0
+    t = min(255, max(0, int(p * 256.0 + 0.5)))
+    return 256.0 / (256 - t)
+
+
 def split_k(rows, n_tiles, sms=148, min_kblocks=8):
     """Number of split-K slices for a dW GEMM over ``rows`` reduction rows."""
     kblocks = max(1, math.ceil(rows / 64))
@@ -883,7 +892,7 @@ class SageEngine(BlockEngine):
 
     def _backward_layer(self, l):
         cu, sm = self.cu, self.sm
-        scale = 1.0 / (1.0 - self.p) if self.p > 0 else 1.0
+        scale = dropout_scale(self.p)
         s = self.lay[l]
         h = s["h"]
         # dW += dY^T X (split-K over the block's rows, fp32 reductions into the gradient)
@@ -969,7 +978,7 @@ class GcnEngine(BlockEngine):
 
     def _backward_layer(self, l):
         cu, sm = self.cu, self.sm
-        scale = 1.0 / (1.0 - self.p) if self.p > 0 else 1.0
+        scale = dropout_scale(self.p)
         s = self.lay[l]
         h = s["h"]
         if not s["last"]:
@@ -1180,7 +1189,7 @@ class GatEngine(BlockEngine):
 
     def _backward_layer(self, l):
         cu, sm = self.cu, self.sm
-        scale = 1.0 / (1.0 - self.p) if self.p > 0 else 1.0
+        scale = dropout_scale(self.p)
         s = self.lay[l]
         h = s["h"]
         # a hidden layer's dY was written by the layer above's dX GEMM (activation backward
