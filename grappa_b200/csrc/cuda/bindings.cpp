@@ -688,7 +688,7 @@ void mark_compact(Tensor mark, Tensor out_ids, Tensor map, int64_t base, Tensor 
 }
 
 void csr_merge(int64_t indptr_a, int64_t indices_a, int64_t n_a, int64_t indptr_b, int64_t indices_b, int64_t n_b,
-               Tensor map, Tensor indptr_out, Tensor indices_out, Tensor err) {
+               Tensor map, Tensor indptr_out, Tensor indices_out, Tensor err, int64_t g0_a, int64_t g0_b) {
   c10::cuda::CUDAGuard g(map.device());
   grappa::peer::CsrMergeArgs a;
   a.indptr_a = as_ptr<const int64_t>(indptr_a);
@@ -703,7 +703,11 @@ void csr_merge(int64_t indptr_a, int64_t indices_a, int64_t n_a, int64_t indptr_
   a.cap_edges = indices_out.numel();
   a.n_rows_total = indptr_out.numel() - 1;
   a.err = ptr<int32_t>(err, at::kInt, "err");
+  a.g0_a = g0_a;
+  a.g0_b = g0_b;
   TORCH_CHECK(a.n_rows_total >= n_a + n_b, "indptr_out too short");
+  TORCH_CHECK((g0_a < 0 || g0_a + n_a <= map.numel()) && (g0_b < 0 || g0_b + n_b <= map.numel()),
+              "csr_merge: partition ranges outside the map");
   grappa::peer::launch_csr_merge(a, stream());
 }
 
@@ -1239,5 +1243,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("iota_map", &iota_map);
   m.def("mark_compact", &mark_compact);
   m.def("mark_compact_scratch_words", [](int64_t n) { return grappa::peer::mark_compact_scratch_words(n); });
-  m.def("csr_merge", &csr_merge);
+  m.def("csr_merge", &csr_merge, py::arg("indptr_a"), py::arg("indices_a"), py::arg("n_a"), py::arg("indptr_b"),
+        py::arg("indices_b"), py::arg("n_b"), py::arg("map"), py::arg("indptr_out"), py::arg("indices_out"),
+        py::arg("err"), py::arg("g0_a") = -1, py::arg("g0_b") = -1);
 }

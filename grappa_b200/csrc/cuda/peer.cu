@@ -239,7 +239,20 @@ __global__ void __launch_bounds__(kMcThreads) mark_compact_kernel(uint8_t* mark,
 // out[e] = map[src[e]] for e < n: the source (peer memory) read as 16-byte words, two
 // in flight per thread, after a scalar head up to the first 16-byte boundary; the
 // translated values are stored as single words (local memory, any alignment)
-__device__ __forceinline__ void merge_segment(const int32_t* src, int64_t n, int32_t* out, const int32_t* map,
+// working id of global id g: the two partitions' ranges arithmetically, the rest
+// (halo sources) through the map
+struct Translate {
+  const int32_t* map;
+  int64_t g0_a, n_a, g0_b, n_b;
+  __device__ __forceinline__ int32_t operator()(int32_t g) const {
+    const int64_t da = static_cast<int64_t>(g) - g0_a, db = static_cast<int64_t>(g) - g0_b;
+    if (g0_a >= 0 && da >= 0 && da < n_a) return static_cast<int32_t>(da);
+    if (g0_b >= 0 && db >= 0 && db < n_b) return static_cast<int32_t>(n_a + db);
+    return map[g];
+  }
+};
+
+__device__ __forceinline__ void merge_segment(const int32_t* src, int64_t n, int32_t* out, const Translate map,
                                               int64_t tid, int64_t stride) {
   if (n <= 0) return;
   const int64_t mis = static_cast<int64_t>((reinterpret_cast<uintptr_t>(src) >> 2) & 3);
@@ -280,8 +293,9 @@ __global__ void csr_merge_kernel(CsrMergeArgs a) {
   }
   const int64_t na = ea < a.cap_edges ? ea : a.cap_edges;
   const int64_t nb = ea + eb < a.cap_edges ? eb : a.cap_edges - na;
-  merge_segment(a.indices_a + ea0, na, a.indices_out, a.map, tid, stride);
-  merge_segment(a.indices_b + eb0, nb, a.indices_out + na, a.map, tid, stride);
+  const Translate tr{a.map, a.g0_a, a.n_a, a.g0_b, a.n_b};
+  merge_segment(a.indices_a + ea0, na, a.indices_out, tr, tid, stride);
+  merge_segment(a.indices_b + eb0, nb, a.indices_out + na, tr, tid, stride);
 }
 
 int sm_count() {

@@ -89,6 +89,9 @@ struct CsrMergeArgs {
   const int32_t* indices_b = nullptr;
   int64_t n_b = 0;
   const int32_t* map = nullptr;
+  // sources in [g0_a, g0_a + n_a) map to g - g0_a and those in [g0_b, g0_b + n_b) to
+  // n_a + g - g0_b without reading the map (g0 < 0: always read the map)
+  int64_t g0_a = -1, g0_b = -1;
   int64_t* indptr_out = nullptr;
   int32_t* indices_out = nullptr;
   int64_t cap_edges = 0;

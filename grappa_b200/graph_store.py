@@ -218,8 +218,11 @@ class PartitionStore:
                          self._feat_w.data_ptr(), fs, n_r + n_q, self._halo_ids.numel(), self.err)
             ev[3].record()
         # 3. working CSR: own in-edges, then q's in-edges pulled from q, sources translated
+        # own and neighbour sources translate arithmetically (their ids are the ranges the
+        # id map holds as iotas); only halo sources read the map
         cu.csr_merge(peer["indptr"].ptrs[r], peer["indices"].ptrs[r], n_r, peer["indptr"].ptrs[q],
-                     peer["indices"].ptrs[q], n_q, self._map, self._indptr_w, self._indices_w, self.err)
+                     peer["indices"].ptrs[q], n_q, self._map, self._indptr_w, self._indices_w, self.err,
+                     g0_a=own.prefix[r], g0_b=own.prefix[q])
         ev[2].record()
         main.wait_stream(self._side)
         main.wait_stream(self._side2)

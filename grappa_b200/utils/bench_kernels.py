@@ -225,13 +225,14 @@ def repart_case(n_part=600_000, deg=50, n_global=2_449_029, halo=400_000, dim=10
     ia = torch.randint(0, n_global, (E,), **i32)
     ib = torch.randint(0, n_global, (E,), **i32)
     mp = torch.randint(0, 2 * n_part + halo, (n_global,), **i32)
+    mp[: 2 * n_part] = torch.arange(2 * n_part, **i32)  # own and neighbour ranges (translated arithmetically)
     out_ip = torch.zeros(2 * n_part + 1, **i64)
     out_ix = torch.zeros(2 * E, **i32)
     err = torch.zeros(1, **i32)
 
     def merge():
         cu.csr_merge(ip.data_ptr(), ia.data_ptr(), n_part, ip.data_ptr(), ib.data_ptr(), n_part, mp, out_ip, out_ix,
-                     err)
+                     err, g0_a=0, g0_b=n_part)
 
     t_merge = _time(merge, iters=20)
     merge_bytes = 2 * E * 4 * 2 + 2 * E * 4 + 2 * (n_part + 1) * 8 * 2  # indices r/w, map gathers, indptr

@@ -508,6 +508,21 @@ def test_csr_merge_and_copy(a0, b0):
     want_ix = mp[torch.cat([ia[a0:a0 + ea], ib[b0:b0 + eb]]).long()]
     assert torch.equal(out_ix[:ea + eb].cpu(), want_ix)
     assert torch.all(out_ix[ea + eb:] == -1) and int(err) == 0
+    # partition ranges translated arithmetically: the same result as a map holding
+    # iotas there
+    g0a, g0b = 1000, 3000
+    mp2 = mp.clone()
+    mp2[g0a:g0a + 300] = torch.arange(300, dtype=torch.int32)
+    mp2[g0b:g0b + 211] = 300 + torch.arange(211, dtype=torch.int32)
+    want2 = mp2[torch.cat([ia[a0:a0 + ea], ib[b0:b0 + eb]]).long()]
+    mp2_d = mp2.to(DEV)
+    mp2_d[g0a:g0a + 300] = -5  # not read for sources in the ranges
+    mp2_d[g0b:g0b + 211] = -5
+    out_ix.fill_(-1)
+    cu().csr_merge(ipa_d.data_ptr(), ia_d.data_ptr(), 300, ipb_d.data_ptr(), ib_d.data_ptr(), 211, mp2_d, out_ip,
+                   out_ix, err, g0_a=g0a, g0_b=g0b)
+    torch.cuda.synchronize()
+    assert torch.equal(out_ix[:ea + eb].cpu(), want2)
     # copy: 16-byte words, a count that is not a multiple of the unroll
     src = torch.randint(0, 1 << 30, (4 * 100003,), dtype=torch.int32, device=DEV)
     dst = torch.zeros_like(src)
