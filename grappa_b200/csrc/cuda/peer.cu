@@ -244,7 +244,7 @@ __global__ void __launch_bounds__(kMcThreads) mark_compact_kernel(uint8_t* mark,
 struct Translate {
   const int32_t* map;
   int64_t g0_a, n_a, g0_b, n_b;
-  __device__ __forceinline__ int32_t operator()(int32_t g) const {
+  __device__ __forceinline__ int32_t operator[](int32_t g) const {
     const int64_t da = static_cast<int64_t>(g) - g0_a, db = static_cast<int64_t>(g) - g0_b;
     if (g0_a >= 0 && da >= 0 && da < n_a) return static_cast<int32_t>(da);
     if (g0_b >= 0 && db >= 0 && db < n_b) return static_cast<int32_t>(n_a + db);
