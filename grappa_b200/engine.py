@@ -53,7 +53,7 @@ GAT_FUSED_LOGITS = os.environ.get("GRAPPA_GAT_FUSED_LOGITS", "0") != "0"
 # GraphSAGE backward gathered by source over the block transpose (1) or scattered with
 # fp32 reductions plus a separate activation pass (0, the default: the transposes add
 # two kernels per hop to the sampling stream, which measured slower overall)
-SAGE_GATHER_BWD = os.environ.get("GRAPPA_SAGE_GATHER_BWD", "0") != "0"
+SAGE_GATHER_BWD = os.environ.get("GRAPPA_SAGE_GATHER_BWD", "0")  # "0", "1" (every hop) or "inner"
 # GraphSAGE output layer (aggregation, logits, cross-entropy, dlogits and dX) as one
 # CUDA-core kernel (csrc/cuda/head.cu) instead of an aggregation, a tensor-core GEMM
 # with a cross-entropy epilogue on a handful of SMs and a dX GEMM
@@ -823,9 +823,15 @@ class SageEngine(BlockEngine):
     model_name = "sage"
 
     def _make_sampler(self, batch_size, n_nodes_cap, dev):
-        # hops 0 .. L-2 feed a backward aggregation (the input layer's hop does not)
-        return GpuNeighborSampler(self.fanouts, batch_size, n_nodes_cap, dev, cu=self.cu,
-                                  transpose_hops=tuple(range(self.L - 1)) if SAGE_GATHER_BWD else ())
+        # hops 0 .. L-2 feed a backward aggregation (the input layer's hop does not);
+        # "inner" leaves hop 0 to the fused output layer's scatter
+        if SAGE_GATHER_BWD == "1":
+            hops = tuple(range(self.L - 1))
+        elif SAGE_GATHER_BWD == "inner" and SAGE_FUSED_HEAD and not self.full_graph:
+            hops = tuple(range(1, self.L - 1))
+        else:
+            hops = ()
+        return GpuNeighborSampler(self.fanouts, batch_size, n_nodes_cap, dev, cu=self.cu, transpose_hops=hops)
 
     def _alloc_layers(self):
         dev = self.device
@@ -841,7 +847,9 @@ class SageEngine(BlockEngine):
                         dY=torch.zeros((rows, op), dtype=torch.bfloat16, device=dev))
             if l < self.L - 1:
                 spec["H"] = torch.zeros((rows, op), dtype=torch.bfloat16, device=dev)
-                if self.full_graph or not getattr(self.sm, "tptr", None):
+                # fp32 gradient rows unless the next layer's hop (L-2-l) has a block
+                # transpose (gathered backward with the activation backward fused)
+                if self.full_graph or (self.L - 2 - l) not in (getattr(self.sm, "tptr", None) or {}):
                     spec["dH"] = torch.zeros((rows, op), dtype=torch.float32, device=dev)
             else:
                 spec["ce_fused"] = op <= 64

@@ -123,13 +123,15 @@ class GpuNeighborSampler:
             # after the last hop (compact_edges): the next hop needs only K2's outputs
             cu.compact(dst, self.n_dst(h), self.nbr[h], self.n_edges(h), self.map, self.src[h], self.sampled[h],
                        self.indices[h], self.n_src(h), self.cscr[h], err, self.cap_dst[h], self.cap_e[h], counters, h,
-                       True, self.t_cnt.get(h), self.t_rank.get(h), run_k3=bool(self.t_cnt))
+                       True, self.t_cnt.get(h), self.t_rank.get(h), run_k3=tr)
             if tr:
                 cu.block_transpose(self.indptr[h], self.indices[h], self.n_dst(h), self.n_src(h), self.t_cnt[h],
                                    self.t_rank[h], self.tptr[h], self.tdst[h], err)
-        if not self.t_cnt:
-            cu.compact_edges(self.nbr, [self.n_edges(h) for h in range(self.L)], self.indices,
-                             [self.cap_src[h] for h in range(self.L)], self.map)
+        # the hops without a transpose get their edge rewrite here, in one launch
+        late = [h for h in range(self.L) if h not in self.t_cnt]
+        if late:
+            cu.compact_edges([self.nbr[h] for h in late], [self.n_edges(h) for h in late],
+                             [self.indices[h] for h in late], [self.cap_src[h] for h in late], self.map)
 
     def blocks(self):
         """Materialise the sampled blocks (input layer first) with exact sizes (host sync)."""
