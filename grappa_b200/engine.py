@@ -827,7 +827,7 @@ class SageEngine(BlockEngine):
         # "inner" leaves hop 0 to the fused output layer's scatter
         if SAGE_GATHER_BWD == "1":
             hops = tuple(range(self.L - 1))
-        elif SAGE_GATHER_BWD == "inner" and SAGE_FUSED_HEAD and not self.full_graph:
+        elif SAGE_GATHER_BWD == "inner" and SAGE_FUSED_HEAD:  # mini-batch samplers only
             hops = tuple(range(1, self.L - 1))
         else:
             hops = ()
