@@ -56,6 +56,8 @@ GAT_FUSED_LOGITS = os.environ.get("GRAPPA_GAT_FUSED_LOGITS", "0") != "0"
 # "0" (default), "1" (every hop) or "inner" (the hops the fused output layer does not
 # cover; measured 0.0366 against 0.0358 s/epoch with the default)
 SAGE_GATHER_BWD = os.environ.get("GRAPPA_SAGE_GATHER_BWD", "0")
+# output tiles per SM the GEMM tile width aims for (gemm_bn)
+GEMM_CTAS_PER_SM = float(os.environ.get("GRAPPA_GEMM_TILES_PER_SM", "2"))
 # GraphSAGE output layer (aggregation, logits, cross-entropy, dlogits and dX) as one
 # CUDA-core kernel (csrc/cuda/head.cu) instead of an aggregation, a tensor-core GEMM
 # with a cross-entropy epilogue on a handful of SMs and a dX GEMM
@@ -142,7 +144,7 @@ def gemm_bn(M_cap, N, mn_major=False, sms=148):
     if bn == 48:
         return bn
     mt = math.ceil(max(1, M_cap // 3) / 128)
-    while bn > 64 and mt * math.ceil(N / bn) < 2 * sms:
+    while bn > 64 and mt * math.ceil(N / bn) < GEMM_CTAS_PER_SM * sms:
         bn //= 2
     return bn
 
