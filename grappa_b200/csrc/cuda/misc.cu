@@ -1,5 +1,7 @@
 // Element-wise and gather kernels of the training step, the synthetic-data
 // generators, and the fused Adam update.
+#include <cstdlib>
+
 #include "common.cuh"
 #include "grappa/rng.h"
 #include "kernels.h"
@@ -357,9 +359,15 @@ void launch_act_bwd(const ActBwdArgs& a, cudaStream_t stream) {
   const int rpb = std::max(1, 256 / chunks);
   const int threads = chunks * rpb;
   const int rows = a.cap_rows > 0 ? a.cap_rows : a.n;
-  // with a bias gradient every block ends with one atomic per column: keep the grid
-  // at a few blocks per SM so that those atomics do not queue up on the same words
-  const int per_sm = a.dbias ? 3 : 8;
+  // with a bias gradient every block ends with one atomic per column: fewer blocks per
+  // SM than without, so that those atomics do not queue up on the same words
+  // (GRAPPA_ACT_BWD_BLOCKS_PER_SM overrides the count with a bias gradient)
+  static const int per_sm_bias = [] {
+    const char* e = std::getenv("GRAPPA_ACT_BWD_BLOCKS_PER_SM");
+    const int v = e ? std::atoi(e) : 6;
+    return v > 0 ? v : 6;
+  }();
+  const int per_sm = a.dbias ? per_sm_bias : 8;
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ceil_div(rows, rpb), int64_t(sm_count()) * per_sm)));
   launch_k(act_bwd_kernel, grid, threads, threads * 8 * sizeof(float), stream, a, chunks);
   GB_LAUNCH_CHECK();
