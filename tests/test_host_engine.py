@@ -199,3 +199,20 @@ def test_rmat_candidates_deterministic():
     assert np.array_equal(a[100:], b[:4900])
     valid = a[a >= 0]
     assert len(valid) > 2000 and np.all(valid // 1000 < valid % 1000)
+
+
+def test_dropout_mask_byte_resolution():
+    """Byte-resolution masks: the probability is quantised to 1/256 (p and p + 1/1024 give
+    the same mask), the keep rate follows the quantised p, and element (r, c) of a
+    buffer with row stride ld is the element r * ld + c of the flat mask (so the mask of
+    a row does not depend on where the 16-element draw groups start)."""
+    import numpy as np
+
+    a = np.asarray(host().dropout_mask(5, 1, 2, 3, 40, 100, 104, 0.2))
+    b = np.asarray(host().dropout_mask(5, 1, 2, 3, 40, 100, 104, 0.2 + 1.0 / 1024))
+    assert np.array_equal(a, b)
+    q = round(0.2 * 256) / 256
+    assert abs(a.mean() - (1 - q)) < 0.02
+    flat = np.asarray(host().dropout_mask(5, 1, 2, 3, 1, 40 * 104, 40 * 104, 0.2)).reshape(40, 104)[:, :100]
+    assert np.array_equal(a.reshape(40, 100), flat)
+    assert abs(np.asarray(host().dropout_mask(5, 1, 2, 3, 64, 256, 256, 0.5)).mean() - 0.5) < 0.01
