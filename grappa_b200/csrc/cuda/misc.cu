@@ -361,11 +361,12 @@ void launch_act_bwd(const ActBwdArgs& a, cudaStream_t stream) {
   const int rows = a.cap_rows > 0 ? a.cap_rows : a.n;
   // with a bias gradient every block ends with one atomic per column: fewer blocks per
   // SM than without, so that those atomics do not queue up on the same words
-  // (GRAPPA_ACT_BWD_BLOCKS_PER_SM overrides the count with a bias gradient)
+  // (GRAPPA_ACT_BWD_BLOCKS_PER_SM overrides the count with a bias gradient; the
+  // GraphSAGE epoch measured 0.0360 s with 3, 0.0364 with 6, 0.0378 with 12)
   static const int per_sm_bias = [] {
     const char* e = std::getenv("GRAPPA_ACT_BWD_BLOCKS_PER_SM");
-    const int v = e ? std::atoi(e) : 6;
-    return v > 0 ? v : 6;
+    const int v = e ? std::atoi(e) : 3;
+    return v > 0 ? v : 3;
   }();
   const int per_sm = a.dbias ? per_sm_bias : 8;
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ceil_div(rows, rpb), int64_t(sm_count()) * per_sm)));
