@@ -755,6 +755,58 @@ void sage_head(Tensor indptr, Tensor indices, Tensor n_dst_dev, int64_t cap_dst,
   d::launch_sage_head(a, stream());
 }
 
+void sage_layer_fwd(Tensor indptr, Tensor indices, Tensor n_dst_dev, int64_t cap_dst, Tensor h, int64_t ip, Tensor w,
+                    int64_t op, OptT bias, int64_t act, double dropout_p, OptT counters, int64_t salt, Tensor x,
+                    Tensor out) {
+  c10::cuda::CUDAGuard g(h.device());
+  d::SageLayerArgs a;
+  a.indptr = ptr<int32_t>(indptr, at::kInt, "indptr");
+  a.indices = ptr<int32_t>(indices, at::kInt, "indices");
+  a.n_dst_ptr = ptr<int32_t>(n_dst_dev, at::kInt, "n_dst_dev");
+  a.cap_dst = static_cast<int32_t>(cap_dst);
+  a.ip = static_cast<int32_t>(ip);
+  a.op = static_cast<int32_t>(op);
+  a.w = reinterpret_cast<const __nv_bfloat16*>(ptr2d<at::BFloat16>(w, at::kBFloat16, "w"));
+  a.ldw = w.stride(0);
+  a.h = reinterpret_cast<const __nv_bfloat16*>(ptr2d<at::BFloat16>(h, at::kBFloat16, "h"));
+  a.ldh = h.stride(0);
+  a.bias = optr<float>(bias, at::kFloat, "bias");
+  a.act = static_cast<int32_t>(act);
+  a.dropout_p = static_cast<float>(dropout_p);
+  a.counters = optr<int64_t>(counters, at::kLong, "counters");
+  a.dropout_salt = static_cast<uint32_t>(salt);
+  a.x = reinterpret_cast<__nv_bfloat16*>(ptr2d<at::BFloat16>(x, at::kBFloat16, "x"));
+  a.ldx = x.stride(0);
+  a.out = reinterpret_cast<__nv_bfloat16*>(ptr2d<at::BFloat16>(out, at::kBFloat16, "out"));
+  a.ldo = out.stride(0);
+  TORCH_CHECK(w.size(0) >= op && w.size(1) >= 2 * ip, "sage_layer_fwd: w too small");
+  TORCH_CHECK(x.size(0) >= cap_dst && x.size(1) >= 2 * ip, "sage_layer_fwd: x too small");
+  TORCH_CHECK(out.size(0) >= cap_dst && out.size(1) >= op, "sage_layer_fwd: out too small");
+  d::launch_sage_layer_fwd(a, stream());
+}
+
+void sage_layer_bwd(Tensor indptr, Tensor indices, Tensor n_dst_dev, int64_t cap_dst, Tensor dy, int64_t ip, Tensor w,
+                    int64_t op, Tensor dsrc) {
+  c10::cuda::CUDAGuard g(dy.device());
+  d::SageLayerArgs a;
+  a.indptr = ptr<int32_t>(indptr, at::kInt, "indptr");
+  a.indices = ptr<int32_t>(indices, at::kInt, "indices");
+  a.n_dst_ptr = ptr<int32_t>(n_dst_dev, at::kInt, "n_dst_dev");
+  a.cap_dst = static_cast<int32_t>(cap_dst);
+  a.ip = static_cast<int32_t>(ip);
+  a.op = static_cast<int32_t>(op);
+  a.w = reinterpret_cast<const __nv_bfloat16*>(ptr2d<at::BFloat16>(w, at::kBFloat16, "w"));
+  a.ldw = w.stride(0);
+  a.dy = reinterpret_cast<const __nv_bfloat16*>(ptr2d<at::BFloat16>(dy, at::kBFloat16, "dy"));
+  a.lddy = dy.stride(0);
+  a.dsrc = ptr2d<float>(dsrc, at::kFloat, "dsrc");
+  a.ld_dsrc = dsrc.stride(0);
+  TORCH_CHECK(w.size(0) >= op && w.size(1) >= 2 * ip, "sage_layer_bwd: w too small");
+  TORCH_CHECK(dy.size(0) >= cap_dst && dy.size(1) >= op, "sage_layer_bwd: dy too small");
+  TORCH_CHECK(dsrc.size(1) >= ip, "sage_layer_bwd: dsrc too narrow");
+  d::launch_sage_layer_bwd(a, stream());
+}
+
 // --------------------------------------------------------------------------- nn.cu
 void cross_entropy(Tensor logits, int64_t n_classes, Tensor labels, OptT n_rows_dev, int64_t cap_rows, OptT row_mask,
                    OptT n_sel_dev, Tensor dlogits, OptT dbias, Tensor loss_sum, Tensor correct) {
@@ -1174,6 +1226,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     const char* e = std::getenv("GRAPPA_SAGE_HEAD_TILE");
     return !(e && e[0] == '0');
   });
+  m.def("sage_layer_fwd", &sage_layer_fwd);
+  m.def("sage_layer_bwd", &sage_layer_bwd);
+  m.def("sage_layer_tile_supported",
+        [](int64_t ip, int64_t op) { return d::sage_layer_tile_supported(static_cast<int>(ip), static_cast<int>(op)); });
   m.def("sage_head_supported", [](int64_t ip, int64_t c) { return d::sage_head_supported(static_cast<int>(ip), static_cast<int>(c)); });
   m.def("gemm", &gemm, py::arg("A"), py::arg("a_mn"), py::arg("B"), py::arg("b_mn"), py::arg("M_cap"), py::arg("M_dev"),
         py::arg("N"), py::arg("K_cap"), py::arg("K_dev"), py::arg("splits"), py::arg("C"), py::arg("mode"),

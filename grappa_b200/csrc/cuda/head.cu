@@ -19,6 +19,7 @@
 #include <cstdlib>
 
 #include "common.cuh"
+#include "grappa/rng.h"
 #include "kernels.h"
 
 namespace grappa {
@@ -543,7 +544,285 @@ __global__ void __launch_bounds__(kThreads) sage_head_tile_kernel(SageHeadArgs a
   }
 }
 
+// ---------------------------------------------------------------- middle layers
+// A hidden GraphSAGE layer as 16-row tiles, each tile split over two CTAs by output
+// columns (blockIdx.y), so that the CTA's slice of W fits in shared memory:
+//   forward   H[v, n] = dropout(relu([h_v | mean h_u] . W[n] + b[n])) for its 128
+//             columns n (the aggregation is done by both CTAs of a tile; half 0 also
+//             stores the aggregated rows X for the weight gradient)
+//   backward  dX = dY W for its half of the 2 ip input columns, reduced straight into
+//             the previous layer's fp32 gradient rows: the self half to dsrc[v], the
+//             neighbour half / deg(v) to dsrc[u] of every in-neighbour u
+// (an aggregation and a tcgen05 GEMM, and a dX GEMM and an aggregation backward, are
+// replaced; the block has a few thousand rows, so a 128-row tensor-core tile would
+// leave most SMs idle).
+constexpr int kFwdCols = 128;  // output columns per forward CTA
+
+struct LayerTileLayout {
+  int ip, K, ldk, op, ldo;
+  size_t w_off, x_off, bytes;
+};
+__host__ __device__ inline LayerTileLayout fwd_layout(int ip) {
+  LayerTileLayout L;
+  L.ip = ip;
+  L.K = 2 * ip;
+  L.ldk = L.K + 8;
+  L.op = 0;
+  L.ldo = 0;
+  L.w_off = 0;                                                    // W slice [128][ldk]
+  L.x_off = static_cast<size_t>(kFwdCols) * L.ldk * 2;            // X tile  [16][ldk]
+  L.bytes = L.x_off + static_cast<size_t>(kTileRows) * L.ldk * 2;
+  return L;
+}
+__host__ __device__ inline LayerTileLayout bwd_layout(int ip, int op) {
+  LayerTileLayout L;
+  L.ip = ip;
+  L.K = op;                 // reduction over the layer's outputs
+  L.ldk = ip + 8;           // W half [op][ldk]
+  L.op = op;
+  L.ldo = op + 8;           // dY tile [16][ldo], then the dX half [16][ldk]
+  L.w_off = 0;
+  L.x_off = static_cast<size_t>(op) * L.ldk * 2;
+  const size_t dy = static_cast<size_t>(kTileRows) * L.ldo * 2, dx = static_cast<size_t>(kTileRows) * L.ldk * 2;
+  L.bytes = L.x_off + (dy > dx ? dy : dx);
+  return L;
+}
+
+__global__ void __launch_bounds__(kThreads) sage_fwd_tile_kernel(SageLayerArgs a) {
+  GB_PDL_ENTRY();
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int ip = a.ip;
+  const LayerTileLayout L = fwd_layout(ip);
+  const int K = L.K, ldk = L.ldk;
+  __nv_bfloat16* s_w = reinterpret_cast<__nv_bfloat16*>(smem_raw + L.w_off);
+  __nv_bfloat16* s_x = reinterpret_cast<__nv_bfloat16*>(smem_raw + L.x_off);
+  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+  const int n = min(*a.n_dst_ptr, a.cap_dst);
+  const int r0 = blockIdx.x * kTileRows;
+  const int n0 = blockIdx.y * kFwdCols;
+  if (r0 >= n) return;
+  // W rows n0 .. n0 + 127 into shared memory
+  const int kc8 = K / 8;
+  for (int i = threadIdx.x; i < kFwdCols * kc8; i += kThreads) {
+    const int c = i / kc8, k8 = i % kc8;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(s_w + c * ldk + k8 * 8)),
+                 "l"(a.w + static_cast<int64_t>(n0 + c) * a.ldw + k8 * 8));
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  // aggregation: rows 2 wib, 2 wib + 1 of the tile
+  const bool has_cols = lane * 8 < ip;
+  const int c0 = lane * 8;
+  for (int rr = 0; rr < 2; ++rr) {
+    const int t = 2 * wib + rr, v = r0 + t;
+    uint4 ps = make_uint4(0, 0, 0, 0), pa = make_uint4(0, 0, 0, 0);
+    if (v < n && has_cols) {
+      const int beg = a.indptr[v], end = a.indptr[v + 1];
+      float xa[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) xa[j] = 0.f;
+      ps = *reinterpret_cast<const uint4*>(a.h + static_cast<int64_t>(v) * a.ldh + c0);
+      int e = beg;
+      for (; e + 3 < end; e += 4) {
+        uint4 r[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          r[q] = *reinterpret_cast<const uint4*>(a.h + static_cast<int64_t>(a.indices[e + q]) * a.ldh + c0);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float f[8];
+          bf16x8_to_f32(r[q], f);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) xa[j] += f[j];
+        }
+      }
+      for (; e < end; ++e) {
+        float f[8];
+        bf16x8_to_f32(*reinterpret_cast<const uint4*>(a.h + static_cast<int64_t>(a.indices[e]) * a.ldh + c0), f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) xa[j] += f[j];
+      }
+      const float sc = end > beg ? 1.f / static_cast<float>(end - beg) : 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) xa[j] *= sc;
+      pa = f32_to_bf16x8(xa);
+      if (blockIdx.y == 0) {
+        __nv_bfloat16* xr = a.x + static_cast<int64_t>(v) * a.ldx;
+        *reinterpret_cast<uint4*>(xr + c0) = ps;
+        *reinterpret_cast<uint4*>(xr + ip + c0) = pa;
+      }
+    }
+    if (has_cols) {
+      *reinterpret_cast<uint4*>(s_x + t * ldk + c0) = ps;
+      *reinterpret_cast<uint4*>(s_x + t * ldk + ip + c0) = pa;
+    }
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
+  // Z[16 x 128] = X W_slice^T: warp wib takes n-tiles 2 wib, 2 wib + 1
+  const int g = lane >> 2, tq = lane & 3, l16 = lane & 15;
+  float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+  for (int ks = 0; ks < K / 16; ++ks) {
+    const int k0 = ks * 16;
+    uint32_t x0, x1, x2, x3;
+    ldsm_x4(smem_addr(s_x + (lane & 15) * ldk + k0 + (lane >> 4) * 8), x0, x1, x2, x3);
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      uint32_t b0, b1;
+      ldsm_x2(smem_addr(s_w + ((2 * wib + j) * 8 + (l16 & 7)) * ldk + k0 + (l16 >> 3) * 8), b0, b1);
+      mma_bf16(acc[j], x0, x1, x2, x3, b0, b1);
+    }
+  }
+  // bias, ReLU, dropout (byte-resolution mask of the output element index), bf16 store
+  uint64_t key = 0;
+  uint32_t thr8 = 0;
+  float ks = 1.f;
+  if (a.dropout_p > 0.f) {
+    key = hop_key(static_cast<uint64_t>(a.counters[0]) ^ 0xD80Full, static_cast<uint64_t>(a.counters[1]),
+                  static_cast<uint64_t>(a.counters[2]), a.dropout_salt);
+    thr8 = dropout_thr8(a.dropout_p);
+    ks = dropout_scale8(thr8);
+  }
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int col = n0 + (2 * wib + j) * 8 + tq * 2;
+#pragma unroll
+    for (int hrow = 0; hrow < 2; ++hrow) {
+      const int v = r0 + g + 8 * hrow;
+      if (v >= n) continue;
+      float o0 = acc[j][2 * hrow] + (a.bias ? a.bias[col] : 0.f);
+      float o1 = acc[j][2 * hrow + 1] + (a.bias ? a.bias[col + 1] : 0.f);
+      if (a.act == 1) {
+        o0 = fmaxf(o0, 0.f);
+        o1 = fmaxf(o1, 0.f);
+      }
+      if (a.dropout_p > 0.f) {
+        const uint64_t idx = static_cast<uint64_t>(v) * static_cast<uint64_t>(a.ldo) + static_cast<uint64_t>(col);
+        const uint32_t keep = dropout_keep_bits(key, idx, 2, thr8);
+        o0 = (keep & 1u) ? o0 * ks : 0.f;
+        o1 = (keep & 2u) ? o1 * ks : 0.f;
+      }
+      *reinterpret_cast<uint32_t*>(a.out + static_cast<int64_t>(v) * a.ldo + col) = pack_bf16x2(o0, o1);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) sage_bwd_tile_kernel(SageLayerArgs a) {
+  GB_PDL_ENTRY();
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int ip = a.ip, op = a.op;
+  const LayerTileLayout L = bwd_layout(ip, op);
+  const int ldk = L.ldk, ldo = L.ldo;
+  __nv_bfloat16* s_w = reinterpret_cast<__nv_bfloat16*>(smem_raw + L.w_off);  // [op][ldk]: W[:, half]
+  __nv_bfloat16* s_t = reinterpret_cast<__nv_bfloat16*>(smem_raw + L.x_off);  // dY tile, then dX half
+  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+  const int n = min(*a.n_dst_ptr, a.cap_dst);
+  const int r0 = blockIdx.x * kTileRows;
+  const int half = blockIdx.y;  // 0: self columns [0, ip), 1: neighbour columns [ip, 2 ip)
+  if (r0 >= n) return;
+  const int ic8 = ip / 8;
+  for (int i = threadIdx.x; i < op * ic8; i += kThreads) {
+    const int k = i / ic8, c8 = i % ic8;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(s_w + k * ldk + c8 * 8)),
+                 "l"(a.w + static_cast<int64_t>(k) * a.ldw + half * ip + c8 * 8));
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  const int oc8 = op / 8;
+  for (int i = threadIdx.x; i < kTileRows * oc8; i += kThreads) {
+    const int t = i / oc8, c8 = i % oc8, v = r0 + t;
+    uint4 d = make_uint4(0, 0, 0, 0);
+    if (v < n) d = *reinterpret_cast<const uint4*>(a.dy + static_cast<int64_t>(v) * a.lddy + c8 * 8);
+    *reinterpret_cast<uint4*>(s_t + t * ldo + c8 * 8) = d;
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
+  // dX half [16 x ip] = dY [16 x op] W[:, half]: warp wib takes n-tiles wib, wib + 8, ...
+  const int g = lane >> 2, tq = lane & 3, l16 = lane & 15;
+  const int ntiles = ip / 8, ksteps = op / 16;
+  float acc[4][4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) acc[j][q] = 0.f;
+  for (int ks = 0; ks < ksteps; ++ks) {
+    const int k0 = ks * 16;
+    uint32_t d0, d1, d2, d3;
+    ldsm_x4(smem_addr(s_t + (lane & 15) * ldo + k0 + (lane >> 4) * 8), d0, d1, d2, d3);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int nt = wib + 8 * j;
+      if (nt >= ntiles) break;
+      uint32_t b0, b1;
+      ldsm_x2_t(smem_addr(s_w + (k0 + l16) * ldk + nt * 8), b0, b1);
+      mma_bf16(acc[j], d0, d1, d2, d3, b0, b1);
+    }
+  }
+  __syncthreads();  // every warp has read the dY tile: its buffer takes the dX half
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int nt = wib + 8 * j;
+    if (nt >= ntiles) break;
+    const int col = nt * 8 + tq * 2;
+    *reinterpret_cast<uint32_t*>(s_t + g * ldk + col) = pack_bf16x2(acc[j][0], acc[j][1]);
+    *reinterpret_cast<uint32_t*>(s_t + (g + 8) * ldk + col) = pack_bf16x2(acc[j][2], acc[j][3]);
+  }
+  __syncthreads();
+  // the aggregation's backward from the bf16 dX rows, two rows per warp, 8 columns a lane
+  const bool has_cols = lane * 8 < ip;
+  const int c0 = lane * 8;
+  if (!has_cols) return;
+  for (int rr = 0; rr < 2; ++rr) {
+    const int t = 2 * wib + rr, v = r0 + t;
+    if (v >= n) continue;
+    float f[8];
+    bf16x8_to_f32(*reinterpret_cast<const uint4*>(s_t + t * ldk + c0), f);
+    if (half == 0) {
+      float* d = a.dsrc + static_cast<int64_t>(v) * a.ld_dsrc + c0;
+      red_add_v4(d, f[0], f[1], f[2], f[3]);
+      red_add_v4(d + 4, f[4], f[5], f[6], f[7]);
+    } else {
+      const int beg = a.indptr[v], end = a.indptr[v + 1];
+      const float sc = end > beg ? 1.f / static_cast<float>(end - beg) : 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) f[j] *= sc;
+      for (int e = beg; e < end; ++e) {
+        float* du = a.dsrc + static_cast<int64_t>(a.indices[e]) * a.ld_dsrc + c0;
+        red_add_v4(du, f[0], f[1], f[2], f[3]);
+        red_add_v4(du + 4, f[4], f[5], f[6], f[7]);
+      }
+    }
+  }
+}
+
 }  // namespace
+
+bool sage_layer_tile_supported(int ip, int op) {
+  return ip > 0 && ip % 16 == 0 && ip <= 256 && op > 0 && op % kFwdCols == 0 && op <= 256 &&
+         fwd_layout(ip).bytes <= 200 * 1024 && bwd_layout(ip, op).bytes <= 200 * 1024;
+}
+
+void launch_sage_layer_fwd(const SageLayerArgs& a, cudaStream_t stream) {
+  if (!sage_layer_tile_supported(a.ip, a.op)) throw std::invalid_argument("sage layer tile: unsupported shape");
+  if (a.ldh % 8 || a.ldx % 8 || a.ldw % 8 || a.ldo % 2) throw std::invalid_argument("sage layer tile: strides");
+  if (a.dropout_p > 0.f && !a.counters) throw std::invalid_argument("sage layer tile: dropout needs the counters");
+  const LayerTileLayout L = fwd_layout(a.ip);
+  GB_CUDA_CHECK(cudaFuncSetAttribute(sage_fwd_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(L.bytes)));
+  const dim3 grid(static_cast<unsigned>(ceil_div(a.cap_dst > 0 ? a.cap_dst : 1, kTileRows)),
+                  static_cast<unsigned>(a.op / kFwdCols));
+  launch_k(sage_fwd_tile_kernel, grid, kThreads, L.bytes, stream, a);
+  GB_LAUNCH_CHECK();
+}
+
+void launch_sage_layer_bwd(const SageLayerArgs& a, cudaStream_t stream) {
+  if (!sage_layer_tile_supported(a.ip, a.op)) throw std::invalid_argument("sage layer tile: unsupported shape");
+  if (a.lddy % 8 || a.ldw % 8 || a.ld_dsrc % 4 || !a.dsrc) throw std::invalid_argument("sage layer tile: strides");
+  const LayerTileLayout L = bwd_layout(a.ip, a.op);
+  GB_CUDA_CHECK(cudaFuncSetAttribute(sage_bwd_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(L.bytes)));
+  const dim3 grid(static_cast<unsigned>(ceil_div(a.cap_dst > 0 ? a.cap_dst : 1, kTileRows)), 2u);
+  launch_k(sage_bwd_tile_kernel, grid, kThreads, L.bytes, stream, a);
+  GB_LAUNCH_CHECK();
+}
 
 bool sage_head_supported(int ip, int n_classes) {
   return ip > 0 && ip % 8 == 0 && ip <= 256 && n_classes > 0 && n_classes <= 64;

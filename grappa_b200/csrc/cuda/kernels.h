@@ -211,6 +211,39 @@ struct SageHeadArgs {
   int32_t* pred_out = nullptr;
 };
 bool sage_head_supported(int ip, int n_classes);
+
+// hidden GraphSAGE layer as 16-row MMA tiles (head.cu): forward = aggregation + X W^T +
+// bias / ReLU / dropout; backward = dY W reduced into the previous layer's fp32
+// gradient rows through the aggregation's transpose
+struct SageLayerArgs {
+  const int32_t* indptr = nullptr;
+  const int32_t* indices = nullptr;
+  const int32_t* n_dst_ptr = nullptr;
+  int32_t cap_dst = 0;
+  int32_t ip = 0, op = 0;               // input width (of each half of X), output width
+  const __nv_bfloat16* w = nullptr;     // [op][2 ip]
+  int64_t ldw = 0;
+  // forward
+  const __nv_bfloat16* h = nullptr;     // source rows, ip columns used
+  int64_t ldh = 0;
+  const float* bias = nullptr;
+  int32_t act = 1;
+  float dropout_p = 0.f;
+  const int64_t* counters = nullptr;
+  uint32_t dropout_salt = 0;
+  __nv_bfloat16* x = nullptr;           // [cap, 2 ip] aggregated rows (for dW)
+  int64_t ldx = 0;
+  __nv_bfloat16* out = nullptr;         // [cap, op]
+  int64_t ldo = 0;
+  // backward
+  const __nv_bfloat16* dy = nullptr;    // [cap, op]
+  int64_t lddy = 0;
+  float* dsrc = nullptr;                // previous layer's fp32 gradient rows
+  int64_t ld_dsrc = 0;
+};
+bool sage_layer_tile_supported(int ip, int op);
+void launch_sage_layer_fwd(const SageLayerArgs& a, cudaStream_t stream);
+void launch_sage_layer_bwd(const SageLayerArgs& a, cudaStream_t stream);
 void launch_sage_head(const SageHeadArgs& a, cudaStream_t stream);
 
 // ---------------------------------------------------------------- aggregation (K-SpMM)

@@ -62,6 +62,10 @@ GEMM_CTAS_PER_SM = float(os.environ.get("GRAPPA_GEMM_TILES_PER_SM", "2"))
 # CUDA-core kernel (csrc/cuda/head.cu) instead of an aggregation, a tensor-core GEMM
 # with a cross-entropy epilogue on a handful of SMs and a dX GEMM
 SAGE_FUSED_HEAD = os.environ.get("GRAPPA_SAGE_HEAD", "1") != "0"
+# hidden GraphSAGE layers after the first as 16-row MMA tile kernels (aggregation +
+# projection forward; projection transpose + aggregation backward) instead of an
+# aggregation and a tcgen05 GEMM each way
+SAGE_TILE_LAYERS = os.environ.get("GRAPPA_SAGE_TILE_LAYERS", "0") != "0"
 # stream priorities inside the step graphs: the layer chain, the weight gradients and
 # the updates at the highest priority, the next step's sampling at the lowest
 STREAM_PRIORITY = os.environ.get("GRAPPA_STREAM_PRIORITY", "1") != "0"
@@ -85,7 +89,8 @@ KERNELS_PER_CALL = {
     "l2norm_bwd": 1, "dropout_rows": 1, "dropout_grad": 1, "f32_to_bf16_rows": 1, "add_bf16_rows": 1,
     "gat_scores": 1, "gat_fwd": 1, "gat_bwd": 2, "gat_bwd_input": 2, "gat_dw_combine": 1, "sampler_counters": 1,
     "gat_in_scores": 1, "gat_in_fwd": 1, "gat_in_bwd": 2, "gat_in_prep": 1, "gat_in_dw": 1, "col_sum_bf16": 1,
-    "block_transpose": 2, "aggregate_bwd_gather": 1, "sage_head": 1, "compact_edges": 1,
+    "block_transpose": 2, "aggregate_bwd_gather": 1, "sage_head": 1, "compact_edges": 1, "sage_layer_fwd": 1,
+    "sage_layer_bwd": 1,
 }
 
 
@@ -867,6 +872,8 @@ class SageEngine(BlockEngine):
                     spec["logits"] = torch.zeros((rows, op), dtype=torch.bfloat16, device=dev)
             if l > 0:
                 spec["dX"] = torch.zeros((rows, K), dtype=torch.bfloat16, device=dev)
+            spec["tile"] = bool(SAGE_TILE_LAYERS and 0 < l < self.L - 1 and not self.full_graph
+                                and "dH" in self.lay[l - 1] and self.cu.sage_layer_tile_supported(ip, op))
             self.lay.append(spec)
 
     def _forward(self, training=True):
@@ -885,6 +892,11 @@ class SageEngine(BlockEngine):
                              s["bias"], self.n_classes, labels, s["X"], s["dY"],
                              s["dX"] if training and not fused_bwd else None, self.fstats[2:3], self.istats[0:1],
                              s["gb"] if training else None, dsrc=self.lay[l - 1]["dH"] if fused_bwd else None)
+                continue
+            if s.get("tile"):
+                p = self.p if training else 0.0
+                cu.sage_layer_fwd(sm.indptr[h], sm.indices[h], self._n_dst(h), sm.cap_dst[h], src, s["ip"], s["W"],
+                                  s["op"], s["bias"], 1, p, self.counters if p > 0 else None, l, s["X"], s["H"])
                 continue
             cu.aggregate(sm.indptr[h], sm.indices[h], self._n_dst(h), 0, sm.cap_dst[h], src, src_map,
                          s["ip"], AGG_MEAN, None, None, None, s["X"], s["ip"], 0, 0.0, 0, self.err)
@@ -910,6 +922,15 @@ class SageEngine(BlockEngine):
         # dW += dY^T X (split-K over the block's rows, fp32 reductions into the gradient)
         self._dw(s["dY"], s["X"], s["op"], s["K"], s["rows"], self._n_dst(h), s["gW"])
         if l == 0:
+            return
+        if s.get("tile"):
+            # dY W reduced into the previous layer's fp32 rows through the aggregation's
+            # transpose, then the previous layer's activation backward
+            prev = self.lay[l - 1]
+            cu.sage_layer_bwd(sm.indptr[h], sm.indices[h], self._n_dst(h), sm.cap_dst[h], s["dY"], s["ip"], s["W"],
+                              s["op"], prev["dH"])
+            cu.act_bwd(prev["dH"], prev["H"], prev["dY"], self._n_dst(prev["h"]), 0, prev["op"], scale, prev["gb"],
+                       prev["rows"])
             return
         # dX = dY W (W read MN-major; the fused output layer wrote it in the forward pass)
         if not s.get("head"):

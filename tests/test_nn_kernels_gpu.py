@@ -342,3 +342,56 @@ def test_sage_head_matches_torch(ip, C, n_dst, max_deg):
         if u.numel():
             want.index_add_(0, u, (gx[v, ip:] / u.numel()).expand(u.numel(), ip))
     torch.testing.assert_close(dsrc.cpu(), want, atol=1e-5, rtol=1e-3)
+
+
+@pytest.mark.parametrize("ip,op,n_dst,max_deg,p", [(256, 256, 3250, 9, 0.0), (256, 256, 700, 12, 0.5),
+                                                   (128, 128, 100, 0, 0.0)])
+def test_sage_layer_tiles_match_torch(ip, op, n_dst, max_deg, p):
+    """Hidden GraphSAGE layer as MMA tiles: forward H = dropout(relu([h_v | mean h_u] W^T + b))
+    (and the aggregated rows X), backward dsrc += the aggregation's transpose of dY W,
+    against fp32 torch on the same bf16 operands (dropout mask from the host mirror)."""
+    from grappa_b200.sampler_gpu import new_counters
+
+    torch.manual_seed(9)
+    n_src = n_dst + 900
+    cap = (n_dst + 15) // 16 * 16 + 16
+    deg = torch.randint(0, max_deg + 1, (n_dst,))
+    indptr = torch.zeros(n_dst + 1, dtype=torch.int32)
+    indptr[1:] = torch.cumsum(deg, 0)
+    indices = torch.randint(0, n_src, (int(indptr[-1]) + 1,), dtype=torch.int32)
+    h = bf(torch.randn(n_src, ip, device=DEV))
+    w = bf(torch.randn(op, 2 * ip, device=DEV) / math.sqrt(2 * ip))
+    bias = torch.randn(op, device=DEV) * 0.1
+    x = torch.zeros(cap, 2 * ip, dtype=torch.bfloat16, device=DEV)
+    out = torch.full((cap, op), 3.0, dtype=torch.bfloat16, device=DEV)
+    nd = torch.tensor([n_dst], dtype=torch.int32, device=DEV)
+    counters = new_counters(13, DEV)
+    counters[1], counters[2] = 2, 7
+    cu().sage_layer_fwd(indptr.to(DEV), indices.to(DEV), nd, cap, h, ip, w, op, bias, 1, p,
+                        counters if p > 0 else None, 1, x, out)
+    torch.cuda.synchronize()
+    hf = h.float().cpu()
+    rows = []
+    for v in range(n_dst):
+        u = indices[indptr[v]:indptr[v + 1]].long()
+        rows.append(torch.cat([hf[v], hf[u].mean(0) if u.numel() else torch.zeros(ip)]))
+    xr = bf(torch.stack(rows)).float()
+    torch.testing.assert_close(x[:n_dst].float().cpu(), xr, atol=1e-2, rtol=1e-2)
+    want = torch.relu(xr @ w.float().cpu().t() + bias.cpu())
+    if p > 0:
+        mask = torch.from_numpy(_native.host().dropout_mask(13, 2, 7, 1, n_dst, op, op, p)).view(n_dst, op).float()
+        want = want * mask / (1 - p)
+    torch.testing.assert_close(out[:n_dst].float().cpu(), want, atol=3e-2, rtol=2e-2)
+    # backward
+    dy = bf(torch.randn(cap, op, device=DEV) * 0.1)
+    dsrc = torch.zeros(n_src, ip, device=DEV)
+    cu().sage_layer_bwd(indptr.to(DEV), indices.to(DEV), nd, cap, dy, ip, w, op, dsrc)
+    torch.cuda.synchronize()
+    dx = bf(dy[:n_dst].float() @ w.float()).float().cpu()
+    wantd = torch.zeros(n_src, ip)
+    wantd[:n_dst] += dx[:, :ip]
+    for v in range(n_dst):
+        u = indices[indptr[v]:indptr[v + 1]].long()
+        if u.numel():
+            wantd.index_add_(0, u, (dx[v, ip:] / u.numel()).expand(u.numel(), ip))
+    torch.testing.assert_close(dsrc.cpu(), wantd, atol=2e-3, rtol=2e-2)
