@@ -50,7 +50,66 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 }
 
 // ---------------------------------------------------------------- repartition
+// Rows of up to 2 KB: a row takes 8, 16 or 32 lanes (each up to four 16-byte chunks),
+// a warp moves 32 / lanes rows per step and four steps' rows are loaded before the
+// first store, so that many peer reads are in flight per warp (a halo pull is a few
+// hundred thousand random rows, bound by the round trip of each).
+constexpr int kPullUnroll = 4;
 __global__ void pull_rows_kernel(PullRowsArgs a) {
+  int64_t n = a.n_ptr ? *a.n_ptr : a.n;
+  if (n > a.cap) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) dev::set_error(a.err, dev::kErrCapacity);
+    n = a.cap;
+  }
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  const int64_t wid = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int chunks = a.row_bytes >> 4;
+  const int lpr = chunks <= 8 ? 8 : (chunks <= 16 ? 16 : 32);
+  const int rpw = 32 / lpr;
+  const int sub = lane % lpr, slot = lane / lpr;
+  const int64_t g_lo = a.prefix[0], g_hi = a.prefix[a.world];
+  const int64_t per_step = static_cast<int64_t>(rpw) * kPullUnroll;
+  for (int64_t r0 = wid * per_step; r0 < n; r0 += warps * per_step) {
+    const uint4* src[kPullUnroll];
+    uint4* dst[kPullUnroll];
+#pragma unroll
+    for (int u = 0; u < kPullUnroll; ++u) {
+      const int64_t r = r0 + u * rpw + slot;
+      src[u] = nullptr;
+      dst[u] = nullptr;
+      if (r >= n) continue;
+      const int64_t g = a.gids[r];
+      if (g < g_lo || g >= g_hi) {
+        if (sub == 0) dev::set_error(a.err, dev::kErrBadIndex);
+        continue;
+      }
+      int p = 0;
+      while (p + 1 < a.world && g >= a.prefix[p + 1]) ++p;
+      src[u] = reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(a.tables[p]) +
+                                              (g - a.prefix[p]) * a.table_stride * a.elem_bytes);
+      dst[u] = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(a.out) + (a.out_row0 + r) * a.out_stride * a.elem_bytes);
+    }
+    uint4 v[kPullUnroll][4];
+#pragma unroll
+    for (int u = 0; u < kPullUnroll; ++u)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int c = sub + k * lpr;
+        if (src[u] && c < chunks) v[u][k] = src[u][c];
+      }
+#pragma unroll
+    for (int u = 0; u < kPullUnroll; ++u)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int c = sub + k * lpr;
+        if (dst[u] && c < chunks) dst[u][c] = v[u][k];
+      }
+  }
+}
+
+// rows wider than 2 KB: one warp per row
+__global__ void pull_rows_wide_kernel(PullRowsArgs a) {
   int64_t n = a.n_ptr ? *a.n_ptr : a.n;
   if (n > a.cap) {
     if (blockIdx.x == 0 && threadIdx.x == 0) dev::set_error(a.err, dev::kErrCapacity);
@@ -323,7 +382,14 @@ void launch_pull_rows(const PullRowsArgs& a_in, int64_t cap, cudaStream_t stream
   PullRowsArgs a = a_in;
   a.cap = cap;
   if (cap == 0) return;
-  pull_rows_kernel<<<grid_for(cap * 32, 256, 16), 256, 0, stream>>>(a);
+  if (a.row_bytes <= 2048) {
+    const int chunks = a.row_bytes / 16;
+    const int rows_per_warp = 32 / (chunks <= 8 ? 8 : (chunks <= 16 ? 16 : 32));
+    pull_rows_kernel<<<grid_for(ceil_div(cap, static_cast<int64_t>(rows_per_warp) * kPullUnroll) * 32, 256, 16), 256, 0,
+                       stream>>>(a);
+  } else {
+    pull_rows_wide_kernel<<<grid_for(cap * 32, 256, 16), 256, 0, stream>>>(a);
+  }
   GB_LAUNCH_CHECK();
 }
 

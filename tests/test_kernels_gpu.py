@@ -559,3 +559,25 @@ def test_mark_compact_halo_ids(n_global):
         assert torch.equal(out[:k].cpu(), want.cpu())
         assert torch.equal(mp[want].cpu(), torch.arange(base, base + k, dtype=torch.int32))
         assert int(mark.sum()) == 0
+
+
+@pytest.mark.parametrize("dim,n_ids", [(32, 1000), (104, 5001), (128, 777), (608, 3001), (1100, 400)])
+def test_pull_rows_widths(dim, n_ids):
+    """pull_rows at every row width class (8, 16 or 32 lanes per row with several rows
+    per warp in flight, and one warp per row above 2 KB) from three local "rank" tables,
+    into rows at an offset of a wider output."""
+    torch.manual_seed(10)
+    sizes = [300, 1, 500]
+    tabs = [torch.randn(s, dim, device=DEV).to(torch.bfloat16) for s in sizes]
+    full = torch.cat(tabs)
+    prefix = torch.tensor([0, 300, 301, 801], dtype=torch.int64, device=DEV)
+    gids = torch.randint(0, 801, (n_ids,), dtype=torch.int64, device=DEV)
+    ld = dim + 8
+    out = torch.zeros((n_ids + 10, ld), dtype=torch.bfloat16, device=DEV)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    cu().pull_rows([t.data_ptr() for t in tabs], dim, 2, dim * 2, gids, None, n_ids, prefix, out.data_ptr(), ld, 5,
+                   n_ids, err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert torch.equal(out[5:5 + n_ids, :dim], full[gids.long()])
+    assert bool((out[:5] == 0).all()) and bool((out[5 + n_ids:] == 0).all()) and bool((out[:, dim:] == 0).all())
