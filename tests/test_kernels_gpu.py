@@ -561,7 +561,7 @@ def test_mark_compact_halo_ids(n_global):
         assert int(mark.sum()) == 0
 
 
-@pytest.mark.parametrize("dim,n_ids", [(32, 1000), (104, 5001), (128, 777), (608, 3001), (1100, 400)])
+@pytest.mark.parametrize("dim,n_ids", [(32, 1000), (104, 5001), (128, 777), (608, 3001), (1104, 400)])
 def test_pull_rows_widths(dim, n_ids):
     """pull_rows at every row width class (8, 16 or 32 lanes per row with several rows
     per warp in flight, and one warp per row above 2 KB) from three local "rank" tables,
