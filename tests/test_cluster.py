@@ -1,0 +1,45 @@
+"""Cluster deployment helpers (CPU): hosts files, the SLURM job-array script of a sweep
+and the container commands; nothing is submitted or run."""
+import os
+
+import pytest
+
+from grappa_b200 import cluster, launch
+
+
+def test_parse_hosts_file(tmp_path):
+    p = tmp_path / "hosts"
+    p.write_text("# machines\nnode01 n_gpu=8\n\nnode02 n_gpu=4\nnode03\n")
+    assert cluster.parse_hosts_file(str(p)) == [("node01", 8), ("node02", 4), ("node03", -1)]
+
+
+def test_slurm_job_array_runs_the_sweep(tmp_path):
+    out, logs = tmp_path / "jobs", tmp_path / "log"
+    cluster.main(["slurm", "--out", str(out), "--log_dir", str(logs), "--graphs", "rmat16k,reddit",
+                  "--models", "sage,gat", "--nproc", "8", "--partition", "gpu", "--job_name", "sw"])
+    script = (out / "sw.sbatch").read_text()
+    sweep = (out / "sweep.txt").read_text().splitlines()
+    assert len(sweep) == 4  # 2 graphs x 2 models
+    for line in ("#SBATCH --nodes=1", "#SBATCH --exclusive", "#SBATCH --gres=gpu:8", "#SBATCH --array=0-3",
+                 "#SBATCH --partition=gpu", "MASTER_ADDR=127.0.0.1"):
+        assert line in script
+    assert str(out / "sweep.txt") in script and "SLURM_ARRAY_TASK_ID + 1" in script
+    # each line is a launch.py sweep command with its log redirection, one rank per GPU
+    assert all("--nproc-per-node 8" in c and "--num_gpus 8" in c and str(logs) in c for c in sweep)
+    assert os.access(out / "sw.sbatch", os.X_OK)
+
+
+def test_slurm_rejects_multi_node():
+    with pytest.raises(ValueError, match="one node"):
+        cluster.slurm_script(3, "sweep.txt", job_name="x", gpus=8, cpus=8, mem="0", time_limit="1:00:00",
+                             log_dir="log", nodes=2)
+
+
+def test_docker_command_shares_ipc_and_all_gpus(capsys):
+    argv = cluster.docker_command("img:1", "python -m x", data_path="/data", workspace="/ws", name="n1")
+    assert argv[:3] == ["docker", "run", "--rm"]
+    assert "--gpus=all" in argv and "--ipc=host" in argv
+    assert argv[-4:] == ["img:1", "bash", "-lc", "python -m x"]
+    assert cluster.main(["docker", "--image", "img:1", "--data_path", "/data", "--models", "sage,gcn"]) == 0
+    lines = capsys.readouterr().out.strip().splitlines()
+    assert len(lines) == 2 and all(line.startswith("docker run") for line in lines)
