@@ -1,6 +1,8 @@
 #include "graph_host.h"
 
+#ifdef _OPENMP
 #include <omp.h>
+#endif
 
 #include <algorithm>
 #include <cmath>

@@ -10,20 +10,16 @@
 #include <pybind11/pybind11.h>
 #include <pybind11/stl.h>
 
-#include <atomic>
 #include <cmath>
-#include <condition_variable>
-#include <deque>
 #include <memory>
-#include <mutex>
 #include <optional>
-#include <thread>
 #include <unordered_map>
 
 #include "chunking.h"
 #include "graph_host.h"
 #include "grappa/rng.h"
 #include "mlpart.h"
+#include "pipeline.h"
 #include "xborder.h"
 
 namespace py = pybind11;
@@ -143,51 +139,49 @@ HostBatch sample_batch(const CSC& g, const std::vector<int64_t>& fanouts, const 
   return hb;
 }
 
-// Pipelined batch producer: a worker thread keeps up to kMaxQueue sampled
-// batches ready (reference: csrc/python/py_graph.cc:50-371, which busy-waits;
-// here the consumer sleeps on a condition variable).
+// Pipelined batch producer: a worker thread keeps up to two sampled batches ready
+// (BatchPipeline; the reference's py_graph.cc:50-371 busy-waits, here the consumer
+// sleeps on a condition variable).
 class HostSampler {
  public:
-  static constexpr size_t kMaxQueue = 2;
   HostSampler(HostGraph* g, std::vector<int64_t> fanouts, bool repeated, bool count_resampling,
               uint64_t seed)
       : g_(g), fanouts_(std::move(fanouts)), repeated_(repeated), count_(count_resampling),
-        seed_(seed) {}
-  ~HostSampler() { stop(); }
+        seed_(seed), pipe_(2) {}
+  ~HostSampler() { pipe_.stop(); }
 
   void reinit(arr<int64_t> targets, py::object gideg, int64_t batch_size, int64_t n_batch,
               int64_t epoch) {
-    stop();
-    targets_.assign(targets.data(), targets.data() + targets.size());
-    gideg_.clear();
+    pipe_.stop();  // the worker reads targets_/gideg_: end it before they change
+    if (batch_size <= 0) throw std::invalid_argument("batch_size must be positive");
+    std::vector<int64_t> gd_new;
     if (!gideg.is_none()) {
       auto gd = gideg.cast<arr<int64_t>>();
       if (gd.size() != targets.size()) throw std::invalid_argument("gideg and targets differ in length");
-      gideg_.assign(gd.data(), gd.data() + gd.size());
+      gd_new.assign(gd.data(), gd.data() + gd.size());
     }
-    if (batch_size <= 0) throw std::invalid_argument("batch_size must be positive");
+    targets_.assign(targets.data(), targets.data() + targets.size());
+    gideg_ = std::move(gd_new);
     bs_ = batch_size;
-    n_batch_ = n_batch < 0 ? (static_cast<int64_t>(targets_.size()) + bs_ - 1) / bs_ : n_batch;
+    const int64_t nb = n_batch < 0 ? (static_cast<int64_t>(targets_.size()) + bs_ - 1) / bs_ : n_batch;
     epoch_ = epoch < 0 ? epoch_ + 1 : epoch;
-    produced_ = 0;
-    consumed_ = 0;
-    stop_ = false;
-    worker_ = std::thread([this] { run(); });
+    const int64_t ep = epoch_, bs = bs_;
+    pipe_.start(nb, [this, ep, bs](int64_t s) {
+      const int64_t n = static_cast<int64_t>(targets_.size());
+      const int64_t b = std::min(n, s * bs), e = std::min(n, b + bs);
+      return std::make_unique<HostBatch>(sample_batch(
+          g_->csc, fanouts_, targets_.data() + b, e - b,
+          (count_ && !gideg_.empty()) ? gideg_.data() + b : nullptr, seed_, ep, s, repeated_));
+    });
   }
 
   py::tuple next_batch() {
     std::unique_ptr<HostBatch> b;
     {
       py::gil_scoped_release rel;
-      std::unique_lock<std::mutex> lk(mu_);
-      if (consumed_ >= n_batch_) throw py::stop_iteration();
-      cv_.wait(lk, [this] { return !q_.empty() || err_; });
-      if (err_ && q_.empty()) throw std::runtime_error("HostSampler worker failed: " + err_msg_);
-      b = std::move(q_.front());
-      q_.pop_front();
-      consumed_++;
+      b = pipe_.next();
     }
-    cv_.notify_all();
+    if (!b) throw py::stop_iteration();
     py::list blocks;
     for (auto& blk : b->blocks) blocks.append(block_to_py(blk));
     return py::make_tuple(to_py(std::move(b->seeds)), blocks, b->cov_sum, b->cov_n);
@@ -222,57 +216,13 @@ class HostSampler {
   int64_t epoch() const { return epoch_; }
 
  private:
-  void run() {
-    try {
-      for (int64_t s = 0; s < n_batch_; ++s) {
-        {
-          std::unique_lock<std::mutex> lk(mu_);
-          cv_.wait(lk, [this] { return q_.size() < kMaxQueue || stop_; });
-          if (stop_) return;
-        }
-        const int64_t n = static_cast<int64_t>(targets_.size());
-        const int64_t b = std::min(n, s * bs_), e = std::min(n, b + bs_);
-        auto hb = std::make_unique<HostBatch>(sample_batch(
-            g_->csc, fanouts_, targets_.data() + b, e - b,
-            (count_ && !gideg_.empty()) ? gideg_.data() + b : nullptr, seed_, epoch_, s, repeated_));
-        {
-          std::lock_guard<std::mutex> lk(mu_);
-          q_.push_back(std::move(hb));
-          produced_++;
-        }
-        cv_.notify_all();
-      }
-    } catch (const std::exception& ex) {
-      std::lock_guard<std::mutex> lk(mu_);
-      err_ = true;
-      err_msg_ = ex.what();
-      cv_.notify_all();
-    }
-  }
-  void stop() {
-    {
-      std::lock_guard<std::mutex> lk(mu_);
-      stop_ = true;
-    }
-    cv_.notify_all();
-    if (worker_.joinable()) worker_.join();
-    std::lock_guard<std::mutex> lk(mu_);
-    q_.clear();
-    err_ = false;
-  }
-
   HostGraph* g_;
   std::vector<int64_t> fanouts_;
   bool repeated_, count_;
   uint64_t seed_;
   std::vector<int64_t> targets_, gideg_;
-  int64_t bs_ = 1, n_batch_ = 0, epoch_ = -1, produced_ = 0, consumed_ = 0;
-  std::mutex mu_;
-  std::condition_variable cv_;
-  std::deque<std::unique_ptr<HostBatch>> q_;
-  std::thread worker_;
-  bool stop_ = false, err_ = false;
-  std::string err_msg_;
+  int64_t bs_ = 1, epoch_ = -1;
+  grappa::host::BatchPipeline<HostBatch> pipe_;
 };
 
 template <typename T>

@@ -1,20 +1,30 @@
 // Native tests of the C++ host engine (CSC build, sampling rule, coverage ratio,
-// compaction order, random walks, cross-partition ids, chunk writer), built and run
-// without Python:
+// compaction order, random walks, cross-partition ids, chunk writer, multilevel
+// partitioner, batch prefetch pipeline), built and run without Python:
 //   g++ -O2 -std=c++17 -fopenmp -Igrappa_b200/csrc/include -Igrappa_b200/csrc/host \
-//       grappa_b200/csrc/host/tests/test_host.cc grappa_b200/csrc/host/{graph_host,xborder,chunking}.cc
+//       grappa_b200/csrc/host/tests/test_host.cc \
+//       grappa_b200/csrc/host/{graph_host,xborder,chunking,mlpart}.cc -lpthread
+// The test suite also builds it with -fsanitize=address,undefined and, without
+// OpenMP (whose runtime the thread sanitizer cannot see into), -fsanitize=thread.
 // The reference ships smoke executables on a toy graph u = {1,2,3,4,5,100,101,101},
 // v = {10,12,200,24,200,120,200,300} (csrc/test/test_build_graph.cc:11-20,
 // test_sampling_h.cc:12-61); the same graph is used here, with assertions.
+#include <atomic>
+#include <chrono>
 #include <cstdio>
 #include <cstdlib>
+#include <memory>
 #include <set>
+#include <stdexcept>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "chunking.h"
 #include "graph_host.h"
 #include "grappa/rng.h"
+#include "mlpart.h"
+#include "pipeline.h"
 #include "xborder.h"
 
 using namespace grappa::host;
@@ -119,6 +129,172 @@ static void test_chunks() {
   CHECK(st.bridge_edges[0 * 2 + 1] == 1 && st.bridge_edges[1 * 2 + 0] == 1);
 }
 
+// Grid graph rows x cols (4-neighbour), both directions listed.
+static void grid(int64_t rows, int64_t cols, std::vector<int64_t>* u, std::vector<int64_t>* v) {
+  for (int64_t r = 0; r < rows; ++r)
+    for (int64_t c = 0; c < cols; ++c) {
+      const int64_t a = r * cols + c;
+      if (c + 1 < cols) {
+        u->push_back(a); v->push_back(a + 1);
+        u->push_back(a + 1); v->push_back(a);
+      }
+      if (r + 1 < rows) {
+        u->push_back(a); v->push_back(a + cols);
+        u->push_back(a + cols); v->push_back(a);
+      }
+    }
+}
+
+static void test_multilevel_partition() {
+  const int64_t rows = 40, cols = 50, n = rows * cols;
+  std::vector<int64_t> u, v;
+  grid(rows, cols, &u, &v);
+  std::vector<int8_t> train(n, 0);
+  for (int64_t i = 0; i < n; i += 3) train[i] = 1;  // a third of the nodes train
+  const int64_t m = static_cast<int64_t>(u.size());
+  for (int64_t k : {2, 4, 7}) {
+    MlPartOptions opt;
+    opt.n_parts = k;
+    opt.imbalance = 0.05;
+    opt.seed = 11;
+    const std::vector<int64_t> p = multilevel_partition(n, u.data(), v.data(), m, train.data(), opt);
+    CHECK(static_cast<int64_t>(p.size()) == n);
+    std::vector<int64_t> nodes(k, 0), seeds(k, 0);
+    bool in_range = true;
+    for (int64_t i = 0; i < n; ++i) {
+      if (p[i] < 0 || p[i] >= k) { in_range = false; continue; }
+      ++nodes[p[i]];
+      seeds[p[i]] += train[i];
+    }
+    CHECK(in_range);
+    const int64_t n_train = (n + 2) / 3;
+    for (int64_t q = 0; q < k; ++q) {
+      // both weights within the allowed excess over the even share (plus one vertex of slack)
+      CHECK(nodes[q] <= static_cast<int64_t>(1.05 * n / k) + 1);
+      CHECK(seeds[q] <= static_cast<int64_t>(1.05 * n_train / k) + 1);
+      CHECK(nodes[q] > 0);
+    }
+    // a grid cut into k blocks cuts O(sqrt(n)) edges per part; hashing cuts ~(k-1)/k of them
+    const int64_t cut = edge_cut(n, u.data(), v.data(), m, p.data());
+    std::vector<int64_t> hashed(n);
+    for (int64_t i = 0; i < n; ++i) hashed[i] = static_cast<int64_t>(grappa::mix64(static_cast<uint64_t>(i)) % k);
+    const int64_t cut_hash = edge_cut(n, u.data(), v.data(), m, hashed.data());
+    CHECK(cut * 5 < cut_hash);
+    CHECK(multilevel_partition(n, u.data(), v.data(), m, train.data(), opt) == p);  // deterministic
+  }
+  // one part: everything in part 0, no cut
+  MlPartOptions one;
+  one.n_parts = 1;
+  const std::vector<int64_t> p1 = multilevel_partition(n, u.data(), v.data(), m, nullptr, one);
+  CHECK(edge_cut(n, u.data(), v.data(), m, p1.data()) == 0);
+  bool threw = false;
+  try {
+    const std::vector<int64_t> bu = {0}, bv = {n};  // endpoint out of range
+    MlPartOptions two;
+    multilevel_partition(n, bu.data(), bv.data(), 1, nullptr, two);
+  } catch (const std::invalid_argument&) {
+    threw = true;
+  }
+  CHECK(threw);
+}
+
+struct Item {
+  int64_t step;
+  std::vector<int64_t> payload;
+};
+
+static void test_pipeline_order_and_depth() {
+  BatchPipeline<Item> pipe(2);
+  std::atomic<int64_t> calls{0};
+  pipe.start(50, [&](int64_t s) {
+    calls++;
+    auto it = std::make_unique<Item>();
+    it->step = s;
+    it->payload.assign(static_cast<size_t>(s % 7 + 1), s);
+    return it;
+  });
+  for (int64_t s = 0; s < 50; ++s) {
+    if (s == 10) {
+      // give the producer time to run ahead: it must stop at the depth
+      std::this_thread::sleep_for(std::chrono::milliseconds(20));
+      CHECK(pipe.ready() <= pipe.depth());
+      CHECK(pipe.produced() - pipe.consumed() <= static_cast<int64_t>(pipe.depth()));
+    }
+    auto it = pipe.next();
+    CHECK(it && it->step == s && it->payload.size() == static_cast<size_t>(s % 7 + 1));
+  }
+  CHECK(pipe.next() == nullptr);  // exhausted
+  CHECK(calls.load() == 50 && pipe.consumed() == 50);
+}
+
+static void test_pipeline_restart_and_stop() {
+  BatchPipeline<Item> pipe(2);
+  auto make = [](int64_t base) {
+    return [base](int64_t s) {
+      auto it = std::make_unique<Item>();
+      it->step = base + s;
+      return it;
+    };
+  };
+  pipe.start(1000, make(0));
+  auto a = pipe.next();
+  CHECK(a && a->step == 0);
+  std::this_thread::sleep_for(std::chrono::milliseconds(5));  // producer now blocks on a full queue
+  pipe.start(3, make(100));                                    // restart drops the old epoch
+  for (int64_t s = 0; s < 3; ++s) {
+    auto it = pipe.next();
+    CHECK(it && it->step == 100 + s);
+  }
+  CHECK(pipe.next() == nullptr);
+  pipe.start(1000, make(0));
+  pipe.stop();
+  CHECK(pipe.next() == nullptr);  // stopped: no item, no wait
+  for (int r = 0; r < 20; ++r) pipe.start(5, make(r));  // rapid restarts join cleanly
+  CHECK(pipe.next()->step == 19);
+  // a consumer blocked in next() is woken by stop() from another thread
+  pipe.start(1000, [](int64_t s) -> std::unique_ptr<Item> {
+    if (s > 0) std::this_thread::sleep_for(std::chrono::milliseconds(200));
+    auto it = std::make_unique<Item>();
+    it->step = s;
+    return it;
+  });
+  CHECK(pipe.next()->step == 0);
+  std::thread stopper([&] {
+    std::this_thread::sleep_for(std::chrono::milliseconds(10));
+    pipe.stop();
+  });
+  auto none = pipe.next();  // waits for item 1 until stop() wakes it (or item 1 arrives)
+  stopper.join();
+  CHECK(none == nullptr || none->step == 1);
+}
+
+static void test_pipeline_failure() {
+  BatchPipeline<Item> pipe(2);
+  pipe.start(10, [](int64_t s) -> std::unique_ptr<Item> {
+    if (s == 3) throw std::runtime_error("bad seed block");
+    auto it = std::make_unique<Item>();
+    it->step = s;
+    return it;
+  });
+  for (int64_t s = 0; s < 3; ++s) {
+    auto it = pipe.next();
+    CHECK(it && it->step == s);  // items made before the failure still arrive
+  }
+  bool threw = false;
+  try {
+    pipe.next();
+  } catch (const std::runtime_error& e) {
+    threw = std::string(e.what()).find("bad seed block") != std::string::npos;
+  }
+  CHECK(threw);
+  pipe.start(2, [](int64_t s) {  // a new start clears the failure
+    auto it = std::make_unique<Item>();
+    it->step = s;
+    return it;
+  });
+  CHECK(pipe.next()->step == 0 && pipe.next()->step == 1);
+}
+
 int main() {
   test_build();
   test_pick_offsets();
@@ -126,6 +302,10 @@ int main() {
   test_random_walk();
   test_xborder();
   test_chunks();
+  test_multilevel_partition();
+  test_pipeline_order_and_depth();
+  test_pipeline_restart_and_stop();
+  test_pipeline_failure();
   if (g_failed) {
     std::fprintf(stderr, "%d check(s) failed\n", g_failed);
     return 1;

@@ -1,6 +1,8 @@
 #include "xborder.h"
 
+#ifdef _OPENMP
 #include <omp.h>
+#endif
 
 #include <algorithm>
 #include <cstring>
@@ -36,12 +38,20 @@ std::vector<std::vector<int64_t>> XBorder::group_by_partition(const int64_t* ids
                                                               int8_t* mask) const {
   if (mask) mask_by_partition(ids, n, mask);
   std::vector<std::vector<int64_t>> out(n_part_);
+#ifdef _OPENMP
   const int nt = omp_get_max_threads();
+#else
+  const int nt = 1;
+#endif
   std::vector<std::vector<std::vector<int64_t>>> local(nt, std::vector<std::vector<int64_t>>(n_part_));
 #pragma omp parallel
   {
+#ifdef _OPENMP
     const int t = omp_get_thread_num();
     const int T = omp_get_num_threads();
+#else
+    const int t = 0, T = 1;
+#endif
     const int64_t len = (n + T - 1) / T;
     const int64_t b = std::min(n, t * len), e = std::min(n, b + len);
     for (int64_t i = b; i < e; ++i) {

@@ -106,6 +106,35 @@ def test_host_sampler_pipeline_matches_direct():
         s.next_batch()
 
 
+def test_host_sampler_restart_mid_epoch():
+    """A reinit while the worker still has batches queued ends that epoch; the new one
+    starts from its own first batch (the epoch number keys the draws)."""
+    u, v, n = small_graph(seed=5)
+    g = G.HostGraph(u, v, n)
+    targets = np.arange(200, dtype=np.int64)
+    s = G.HostSampler(g, [6, 3], False, False, 9)
+    s.reinit(targets, None, 20, -1, 0)
+    s.next_batch()
+    s.reinit(targets[::-1].copy(), None, 20, -1, 7)
+    assert s.epoch == 7
+    seeds, blocks, _, _ = s.next_batch()
+    assert np.array_equal(seeds, targets[::-1][:20])
+    ref_blocks, _, _ = G.sample_batch(g, [6, 3], targets[::-1][:20].copy(), None, 9, 7, 0, False)
+    for a, b in zip(blocks, ref_blocks):
+        assert np.array_equal(a["indices"], b["indices"])
+    for _ in range(9):
+        s.next_batch()
+    with pytest.raises(StopIteration):
+        s.next_batch()
+    s.reinit(targets, None, 50, 2, -1)  # epoch -1: the next epoch number
+    assert s.epoch == 8
+    assert len(s.next_batch()[0]) == 50 and len(s.next_batch()[0]) == 50
+    with pytest.raises(StopIteration):
+        s.next_batch()
+    with pytest.raises(ValueError):
+        s.reinit(targets, None, 0, -1, 0)
+
+
 def test_reference_style_coo_output():
     u, v, n = small_graph(seed=4)
     g = G.HostGraph(u, v, n)
