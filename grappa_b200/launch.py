@@ -10,6 +10,12 @@ product here is one 8-GPU box.
     python -m grappa_b200.launch --data_path D --graphs rmat16k --models sage,gcn \\
         --layers_fanouts "2:10,5" --nproc 2 --num_gpus -1 --runs 1 [--dry_run]
     python -m grappa_b200.launch --table log      # markdown table of the infer_ lines
+
+With ``--partition`` the sweep first builds the chunk sets it needs that are not on
+disk (``grappa_b200.dataset.partition seq`` from ``{data_path}/t10n/{graph}``, after
+generating that directory for a synthetic graph name when it is missing), the role of
+the reference's ``t10nrun.py --task partition`` (experiments/grappa/t10nrun.py,
+partition.sh.template).
 """
 import argparse
 import itertools
@@ -47,10 +53,32 @@ def sweep(args):
         yield tag, cmd
 
 
+def partition_commands(args):
+    """Yield (tag, command) for every chunk set of the sweep missing under data_path
+    (n_part = nproc), preceded once per graph by its generation when the graph's
+    pre-partition directory has no t10n.json."""
+    from grappa_b200.dataset.meta import t10n_chunk_path
+
+    generated = set()
+    for part, graph in dict.fromkeys(itertools.product(args.parts.split(","), args.graphs.split(","))):
+        if os.path.isdir(os.path.join(args.data_path, t10n_chunk_path(graph, part, args.nproc))):
+            continue
+        src = os.path.join(args.data_path, "t10n", graph)
+        if graph not in generated and not os.path.exists(os.path.join(src, "t10n.json")):
+            generated.add(graph)
+            yield f"generate_{graph}", (f"{sys.executable} -m grappa_b200.dataset.partition generate "
+                                        f"--graph_name {graph} --out {shlex.quote(src)}")
+        yield f"partition_{part}_{graph}_{args.nproc}", (
+            f"{sys.executable} -m grappa_b200.dataset.partition seq --src_path {shlex.quote(src)} "
+            f"--dest_path {shlex.quote(args.data_path)} --graph_name {graph} --part_method {part} "
+            f"--n_part {args.nproc}")
+
+
 def run_sweep(args):
     os.makedirs(args.log_dir, exist_ok=True)
     failed = 0
-    for tag, cmd in sweep(args):
+    steps = list(partition_commands(args)) if getattr(args, "partition", False) else []
+    for tag, cmd in steps + list(sweep(args)):
         print(cmd, flush=True)
         if args.dry_run:
             continue
@@ -115,6 +143,8 @@ def main(argv=None):
     ap.add_argument("--log_dir", default="log")
     ap.add_argument("--port", type=int, default=29611)
     ap.add_argument("--timeout", type=int, default=3600)
+    ap.add_argument("--partition", action="store_true",
+                    help="first build the missing chunk sets (and synthetic source graphs) of the sweep")
     ap.add_argument("--dry_run", action="store_true")
     args = ap.parse_args(argv)
     if args.table:
