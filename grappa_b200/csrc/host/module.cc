@@ -19,6 +19,7 @@
 #include "graph_host.h"
 #include "grappa/rng.h"
 #include "mlpart.h"
+#include "numa.h"
 #include "pipeline.h"
 #include "xborder.h"
 
@@ -44,14 +45,20 @@ py::array_t<T> to_py_copy(const std::vector<T>& v) {
   return to_py(std::move(c));
 }
 
+// Host CSC of a partition.  With numa_node >= 0 its arrays are placed on that node
+// (reference: csrc/python/py_graph.cc:23-34, numa_set_membind before the build; here
+// a preferred-node policy for the build only).
 class HostGraph {
  public:
-  HostGraph(arr<int64_t> u, arr<int64_t> v, int64_t n_nodes) {
+  HostGraph(arr<int64_t> u, arr<int64_t> v, int64_t n_nodes, int numa_node) {
     if (u.size() != v.size()) throw std::invalid_argument("u and v differ in length");
     py::gil_scoped_release rel;
+    grappa::host::MemPolicyScope place(numa_node);  // inactive for numa_node < 0
+    numa_placed = place.active();
     csc = grappa::host::build_csc(u.data(), v.data(), static_cast<int64_t>(u.size()), n_nodes);
   }
   CSC csc;
+  bool numa_placed = false;
 };
 
 struct HostBatch {
@@ -246,8 +253,12 @@ PYBIND11_MODULE(_C, m) {
   m.doc() = "grappa_b200 host engine (CSC build, sampling, cross-partition ids, chunking)";
   auto mg = m.def_submodule("graph");
   py::class_<HostGraph>(mg, "HostGraph")
-      .def(py::init<arr<int64_t>, arr<int64_t>, int64_t>(), py::arg("u"), py::arg("v"),
-           py::arg("n_nodes") = -1)
+      .def(py::init<arr<int64_t>, arr<int64_t>, int64_t, int>(), py::arg("u"), py::arg("v"),
+           py::arg("n_nodes") = -1, py::arg("numa_node") = -1)
+      .def_readonly("numa_placed", &HostGraph::numa_placed)
+      .def("numa_node_of_indices", [](HostGraph& g) {
+        return g.csc.indices.empty() ? -1 : grappa::host::numa_node_of(g.csc.indices.data());
+      })
       .def_property_readonly("n_nodes", [](HostGraph& g) { return g.csc.n_nodes; })
       .def_property_readonly("n_edges", [](HostGraph& g) { return g.csc.n_edges; })
       .def("indptr", [](HostGraph& g) { return to_py_copy(g.csc.indptr); })
@@ -388,6 +399,54 @@ PYBIND11_MODULE(_C, m) {
     }
     return to_py(std::move(out));
   });
+
+  // NUMA placement and bandwidth (libnuma-free; reference: test/numa_bench.c and the
+  // numa_set_membind of csrc/python/py_graph.cc:23-34)
+  auto mn = m.def_submodule("numa");
+  mn.def("nodes", &grappa::host::numa_nodes, "online NUMA node ids");
+  mn.def("node_cpus", &grappa::host::numa_node_cpus, py::arg("node"),
+         "CPUs of a node that this process may run on");
+  mn.def("parse_cpulist", [](const std::string& s) { return grappa::host::parse_cpulist(s.c_str()); });
+  mn.def(
+      "node_of", [](py::buffer b) {
+        py::buffer_info info = b.request();
+        return info.size == 0 ? -1 : grappa::host::numa_node_of(info.ptr);
+      },
+      py::arg("buffer"), "NUMA node of the buffer's first page (-1 if unknown)");
+  mn.def("pin_thread", &grappa::host::pin_thread_to_node, py::arg("node"),
+         "pin the calling thread to the node's CPUs");
+  mn.def(
+      "bandwidth",
+      [](int cpu_node, int mem_node, int64_t mbytes, int threads, int reps) {
+        grappa::host::Bandwidth r;
+        {
+          py::gil_scoped_release rel;
+          r = grappa::host::memory_bandwidth(cpu_node, mem_node, static_cast<size_t>(mbytes) << 20, threads, reps);
+        }
+        py::dict d;
+        d["cpu_node"] = cpu_node;
+        d["mem_node"] = mem_node;
+        d["mem_node_seen"] = r.mem_node_seen;
+        d["write_gbs"] = r.write_gbs;
+        d["read_gbs"] = r.read_gbs;
+        return d;
+      },
+      py::arg("cpu_node"), py::arg("mem_node"), py::arg("mbytes") = 256, py::arg("threads") = 0, py::arg("reps") = 3);
+  // with numa.MemPolicy(node): pages this thread faults in come from `node` first
+  struct PyMemPolicy {
+    int node;
+    std::unique_ptr<grappa::host::MemPolicyScope> scope;
+  };
+  py::class_<PyMemPolicy>(mn, "MemPolicy")
+      .def(py::init([](int node) { return PyMemPolicy{node, nullptr}; }), py::arg("node"))
+      .def("__enter__", [](PyMemPolicy& p) {
+        p.scope = std::make_unique<grappa::host::MemPolicyScope>(p.node);
+        return p.scope->active();
+      })
+      .def("__exit__", [](PyMemPolicy& p, py::object, py::object, py::object) {
+        p.scope.reset();
+        return false;
+      });
 
   auto mx = m.def_submodule("xborder");
   py::class_<grappa::host::XBorder>(mx, "XBorder")

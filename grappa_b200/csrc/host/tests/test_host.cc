@@ -1,14 +1,18 @@
 // Native tests of the C++ host engine (CSC build, sampling rule, coverage ratio,
 // compaction order, random walks, cross-partition ids, chunk writer, multilevel
-// partitioner, batch prefetch pipeline), built and run without Python:
+// partitioner, batch prefetch pipeline, NUMA placement), built and run without Python:
 //   g++ -O2 -std=c++17 -fopenmp -Igrappa_b200/csrc/include -Igrappa_b200/csrc/host \
 //       grappa_b200/csrc/host/tests/test_host.cc \
-//       grappa_b200/csrc/host/{graph_host,xborder,chunking,mlpart}.cc -lpthread
+//       grappa_b200/csrc/host/{graph_host,xborder,chunking,mlpart,numa}.cc -lpthread
 // The test suite also builds it with -fsanitize=address,undefined and, without
 // OpenMP (whose runtime the thread sanitizer cannot see into), -fsanitize=thread.
 // The reference ships smoke executables on a toy graph u = {1,2,3,4,5,100,101,101},
 // v = {10,12,200,24,200,120,200,300} (csrc/test/test_build_graph.cc:11-20,
 // test_sampling_h.cc:12-61); the same graph is used here, with assertions.
+#include <linux/mempolicy.h>
+#include <sys/syscall.h>
+#include <unistd.h>
+
 #include <atomic>
 #include <chrono>
 #include <cstdio>
@@ -24,6 +28,7 @@
 #include "graph_host.h"
 #include "grappa/rng.h"
 #include "mlpart.h"
+#include "numa.h"
 #include "pipeline.h"
 #include "xborder.h"
 
@@ -295,6 +300,58 @@ static void test_pipeline_failure() {
   CHECK(pipe.next()->step == 0 && pipe.next()->step == 1);
 }
 
+static int thread_policy_mode() {
+  int mode = -1;
+  unsigned long mask[16] = {0};
+  if (syscall(SYS_get_mempolicy, &mode, mask, 1024UL, nullptr, 0UL) != 0) return -1;
+  return mode & ~MPOL_MODE_FLAGS;
+}
+
+static void test_numa() {
+  CHECK(parse_cpulist("0-3,8,10-11\n") == (std::vector<int>{0, 1, 2, 3, 8, 10, 11}));
+  CHECK(parse_cpulist("5") == (std::vector<int>{5}));
+  CHECK(parse_cpulist("").empty());
+  CHECK(parse_cpulist("x-y").empty());
+  const std::vector<int> nodes = numa_nodes();
+  CHECK(!nodes.empty());
+  const int node = nodes.front();
+  CHECK(!numa_node_cpus(node).empty());
+  CHECK(numa_node_cpus(-1).empty());
+  {
+    MemPolicyScope bad(100000);  // not a node: nothing changes
+    CHECK(!bad.active());
+  }
+  const int mode0 = thread_policy_mode();
+  {
+    MemPolicyScope scope(node);
+    if (scope.active()) {
+      CHECK(thread_policy_mode() == MPOL_PREFERRED);
+      std::vector<int64_t> v(1 << 20, 1);  // faulted in by this thread under the policy
+      const int seen = numa_node_of(v.data());
+      CHECK(seen == -1 || seen == node);
+    }
+  }
+  CHECK(thread_policy_mode() == mode0);  // the thread's policy is back
+  // a CSC built under the policy is the same graph
+  CSC a = toy();
+  CSC b;
+  {
+    MemPolicyScope scope(node);
+    b = toy();
+  }
+  CHECK(a.indptr == b.indptr && a.indices == b.indices);
+  Bandwidth bw = memory_bandwidth(node, node, 16u << 20, 2, 1);
+  CHECK(bw.write_gbs > 0.1 && bw.read_gbs > 0.1);
+  CHECK(bw.mem_node_seen == -1 || bw.mem_node_seen == node);
+  bool threw = false;
+  try {
+    memory_bandwidth(node, 100000, 16u << 20, 2, 1);
+  } catch (const std::invalid_argument&) {
+    threw = true;
+  }
+  CHECK(threw);
+}
+
 int main() {
   test_build();
   test_pick_offsets();
@@ -306,6 +363,7 @@ int main() {
   test_pipeline_order_and_depth();
   test_pipeline_restart_and_stop();
   test_pipeline_failure();
+  test_numa();
   if (g_failed) {
     std::fprintf(stderr, "%d check(s) failed\n", g_failed);
     return 1;

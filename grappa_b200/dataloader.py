@@ -29,9 +29,9 @@ import torch
 from grappa_b200._native import host
 from grappa_b200.dataset.io_dist import ChunkIO
 from grappa_b200.dataset.meta import name_to_meta, t10n_chunk_path
-from grappa_b200.device_allocator import DeviceAllocCPUServing
+from grappa_b200.device_allocator import DeviceAllocCPUServing, T10nDeviceAllocator
 from grappa_b200.sampler import HostBatchSamplerWithCounter
-from grappa_b200.util import pprint, timing
+from grappa_b200.util import pprint, set_py_affinity, timing
 from grappa_b200.xborder import XBorder, xb_gather, xb_group_by_partition, xb_scatter
 from grappa_b200.xbsampler import HostXBBatchSampler
 
@@ -67,6 +67,11 @@ class IsolatedDataloader:
         self.num_part = int(args.n_part)
         self.rank, self.world = _dist()
         assert self.world == self.num_part, "one partition per rank"
+        # the host graph goes on the GPU's NUMA node, the process's CPUs there when
+        # enabled (reference: t10n/dataloader.py:60-63)
+        ta = T10nDeviceAllocator(getattr(args, "num_gpus", -1))
+        self.node_id = ta.get_numa_affinity(ta.get_local_gpu_id(self.world, self.rank))
+        set_py_affinity(self.node_id)
         self.nbr_idx = self.rank
         self.seed = int(getattr(args, "seed", 0))
         self.fanouts = [int(f) for f in str(args.fan_out).split(",")]
@@ -164,7 +169,8 @@ class IsolatedDataloader:
 
     def build_partition_v2_t10n(self):
         tic = time.time()
-        self.cur_g = host().graph.HostGraph(self.part_src.numpy(), self.part_dst.numpy(), self.prefix_sum[-1])
+        self.cur_g = host().graph.HostGraph(self.part_src.numpy(), self.part_dst.numpy(), self.prefix_sum[-1],
+                                            self.node_id)
         self._pp(f"rank:{self.rank:02d} NUM_EDGES: {self.part_src.shape[0]}")
         self._pp(f"rank:{self.rank:02d} BLD_GRAPH: {time.time() - tic:.2f} s")
 

@@ -11,7 +11,7 @@ import pytest
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 HOST = os.path.join(ROOT, "grappa_b200", "csrc", "host")
 SOURCES = [os.path.join(HOST, "tests", "test_host.cc")] + [
-    os.path.join(HOST, f) for f in ("graph_host.cc", "xborder.cc", "chunking.cc", "mlpart.cc")]
+    os.path.join(HOST, f) for f in ("graph_host.cc", "xborder.cc", "chunking.cc", "mlpart.cc", "numa.cc")]
 
 BUILDS = {
     "openmp": (["-O2", "-fopenmp"], ["-L/usr/lib/gcc/x86_64-linux-gnu/13", "-lgomp"], {}),
