@@ -30,26 +30,15 @@ import shlex
 import subprocess
 import sys
 
-from grappa_b200 import launch
+from grappa_b200 import launch, util
 
 
 def parse_hosts_file(path):
     """[(host, n_gpu)] from a hosts file with one ``host [n_gpu=K]`` line per machine (the
     reference's format; n_gpu is -1 when the line gives none).  Blank lines and lines
     starting with '#' are skipped."""
-    out = []
-    with open(path) as f:
-        for line in f:
-            line = line.strip()
-            if not line or line.startswith("#"):
-                continue
-            fields = line.split()
-            n_gpu = -1
-            for tok in fields[1:]:
-                if tok.startswith("n_gpu="):
-                    n_gpu = int(tok.split("=", 1)[1])
-            out.append((fields[0], n_gpu))
-    return out
+    hosts, n_gpu = util.parse_hosts_file(path)
+    return list(zip(hosts, n_gpu))
 
 
 def sweep_commands(args):
