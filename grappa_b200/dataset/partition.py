@@ -12,10 +12,10 @@ t10n/dataset/chunk_dist.py:278-318 (the two chunkers).
     # chunks in one process (methods: hash, random, metis, lp)
     python -m grappa_b200.dataset.partition seq --src_path DATA/t10n/rmat16k --dest_path DATA \\
         --graph_name rmat16k --part_method metis --n_part 8
-    # chunks with one gloo rank per partition (hash partitioning)
+    # chunks with gloo ranks, each writing n_part / ranks partitions (hash partitioning)
     python -m torch.distributed.run --nproc-per-node 8 --master-addr 127.0.0.1 \\
         -m grappa_b200.dataset.partition dist --src_path DATA/t10n/rmat16k --dest_path DATA \\
-        --graph_name rmat16k
+        --graph_name rmat16k --n_part 16
     # what a chunk directory holds: nodes, edges, bridges, training nodes per partition
     python -m grappa_b200.dataset.partition info --path DATA/chunking_rmat16k_metis_008
 """
@@ -88,7 +88,7 @@ def main(argv=None):
     g = sub.add_parser("generate", help="seeded synthetic graph in the pre-partition layout")
     g.add_argument("--graph_name", required=True)
     g.add_argument("--out", required=True)
-    for name, help_ in (("seq", "chunks in one process"), ("dist", "chunks with one gloo rank per partition")):
+    for name, help_ in (("seq", "chunks in one process"), ("dist", "chunks with gloo ranks (n_part a multiple of them)")):
         p = sub.add_parser(name, help=help_)
         p.add_argument("--src_path", required=True, help="directory with t10n.json")
         p.add_argument("--dest_path", required=True)
@@ -98,6 +98,8 @@ def main(argv=None):
             p.add_argument("--part_method", default="hash", choices=["hash", "random", "metis", "lp"])
             p.add_argument("--n_part", type=int, required=True)
         else:
+            p.add_argument("--part_method", default="hash", choices=["hash", "random"])
+            p.add_argument("--n_part", type=int, default=None, help="a multiple of the ranks (default: the ranks)")
             p.add_argument("--pg_timeout", type=int, default=600, help="seconds")
     i = sub.add_parser("info", help="per-partition counts of a chunk directory")
     i.add_argument("--path", required=True)
@@ -124,7 +126,8 @@ def main(argv=None):
 
         dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=a.pg_timeout))
         try:
-            out = build_chunks_dist(a.dest_path, a.graph_name, a.src_path, a.seed)
+            out = build_chunks_dist(dist.get_world_size(), dist.get_rank(), a.dest_path, a.graph_name, a.src_path,
+                                    a.part_method, a.n_part, a.seed)
             if dist.get_rank() == 0:
                 print(_table(*chunk_info(out)))
         finally:

@@ -8,7 +8,7 @@ names resolve to the grappa_b200 modules of the same role, imported on first use
         device_allocator, util}                      -> grappa_b200.<same name>
   t10n.dataset.{meta, io_dist, chunk_seq, chunk_dist, dgl_to_t10n}
                                                      -> grappa_b200.dataset.<same name>
-  t10n.dgl_dsg.sampler                               -> grappa_b200.dgl_dsg
+  t10n.dgl_dsg.{sampler, compliant}                  -> grappa_b200.dgl_dsg
   t10n._C.{graph, xborder, c_seq, c_dist}            -> grappa_b200._C (C++ host engine)
 """
 import importlib
@@ -35,6 +35,7 @@ _ALIASES = {
     "t10n.dataset.dgl_to_t10n": "grappa_b200.dataset.dgl_to_t10n",
     "t10n.dgl_dsg": "grappa_b200.dgl_dsg",
     "t10n.dgl_dsg.sampler": "grappa_b200.dgl_dsg",
+    "t10n.dgl_dsg.compliant": "grappa_b200.dgl_dsg",
     "t10n._C": "grappa_b200._C",
 }
 

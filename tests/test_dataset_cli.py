@@ -86,29 +86,39 @@ def _free_port():
     return p
 
 
-def test_dist_chunks_match_seq_hash(src):
-    """Two gloo ranks write the same hash partition as the one-process chunker: the same
-    nodes, in-degrees, features, labels and masks per partition and the same edges."""
+@pytest.mark.parametrize("n_part", [2, 4])
+def test_dist_chunks_match_seq_hash(src, n_part):
+    """Two gloo ranks (one or two partitions each) write the same hash partition as the
+    one-process chunker: the same nodes, in-degrees, features, labels and masks per
+    partition and the same edges."""
     d, s = src
-    dest = str(d / "dist")
+    dest = str(d / f"dist{n_part}")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
            "--master-addr", "127.0.0.1", "--master-port", str(_free_port()), "-m", "grappa_b200.dataset.partition",
-           "dist", "--src_path", s, "--dest_path", dest, "--graph_name", "tiny", "--pg_timeout", "120"]
+           "dist", "--src_path", s, "--dest_path", dest, "--graph_name", "tiny", "--n_part", str(n_part),
+           "--pg_timeout", "120"]
     r = subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
-    assert partition.main(["seq", "--src_path", s, "--dest_path", str(d / "seq2"), "--graph_name", "tiny",
-                           "--part_method", "hash", "--n_part", "2"]) == 0
-    pd, ps = os.path.join(dest, "chunking_tiny_hash_002"), str(d / "seq2" / "chunking_tiny_hash_002")
-    for i in range(2):
+    seq_dest = str(d / f"seq{n_part}")
+    assert partition.main(["seq", "--src_path", s, "--dest_path", seq_dest, "--graph_name", "tiny",
+                           "--part_method", "hash", "--n_part", str(n_part)]) == 0
+    name = f"chunking_tiny_hash_{n_part:03}"
+    pd, ps = os.path.join(dest, name), os.path.join(seq_dest, name)
+    for i in range(n_part):
         oid_d = np.fromfile(pfile(pd, i, "oid"), dtype=np.int64)
         oid_s = np.fromfile(pfile(ps, i, "oid"), dtype=np.int64)
         assert np.array_equal(oid_d, oid_s)
         for ext, dt in (("ideg", np.int64), ("label", np.float32), ("train", np.int8), ("valid", np.int8),
-                        ("test", np.int8), ("nfeat", np.float32)):
-            assert np.array_equal(np.fromfile(pfile(pd, i, ext), dtype=dt), np.fromfile(pfile(ps, i, ext), dtype=dt))
-    assert np.array_equal(_edges(pd, 2), _edges(ps, 2))
+                        ("test", np.int8), ("nfeat", np.float32), ("u", np.int64), ("v", np.int64)):
+            a = np.fromfile(pfile(pd, i, ext), dtype=dt)
+            b = np.fromfile(pfile(ps, i, ext), dtype=dt)
+            if ext in ("u", "v"):
+                assert a.shape == b.shape
+            else:
+                assert np.array_equal(a, b), ext
+    assert np.array_equal(_edges(pd, n_part), _edges(ps, n_part))
     _, pairs = _source_edges(s)
-    assert np.array_equal(_edges(pd, 2), pairs)
+    assert np.array_equal(_edges(pd, n_part), pairs)
 
 
 def test_info_rejects_a_directory_without_chunks(tmp_path):
@@ -140,3 +150,43 @@ def test_sweep_builds_missing_chunk_sets_first(tmp_path, capsys):
     assert sum("dataset.partition generate" in l for l in lines) == 1  # rmat16k only
     chunks = [l for l in lines if "dataset.partition seq" in l]
     assert len(chunks) == 3 and not any("--part_method hash" in l and "--graph_name tiny" in l for l in chunks)
+
+
+def test_dataset_io_layouts_and_strides(tmp_path):
+    """DatasetIO reads flat and row-pair edge files and raw mmap.npy node arrays; the
+    per-rank split covers every row exactly once."""
+    from grappa_b200.dataset import io_dist
+
+    n, m = 10, 7
+    u = np.arange(m, dtype=np.int64)
+    v = (np.arange(m, dtype=np.int64) * 3) % n
+    np.save(tmp_path / "flat.bin.npy", np.concatenate([u, v]))
+    np.save(tmp_path / "pairs.bin.npy", np.stack([u, v], 1))
+    feat = np.arange(n * 4, dtype=np.float32).reshape(n, 4)
+    feat.tofile(tmp_path / "feat_mmap.npy")
+    cfg = {"num_nodes": n, "num_edges": m, "feat_dim": 4, "edge_file_bin": str(tmp_path / "flat.bin.npy"),
+           "node_feats_file_bin": str(tmp_path / "feat_mmap.npy")}
+    (tmp_path / "t10n.json").write_text(json.dumps(cfg))
+    for cls, edge_file in ((io_dist.OgbprIO, "flat"), (io_dist.DatasetIO, "flat"), (io_dist.Igb260mIO, "pairs"),
+                           (io_dist.DatasetIO, "pairs")):
+        cfg["edge_file_bin"] = str(tmp_path / f"{edge_file}.bin.npy")
+        (tmp_path / "t10n.json").write_text(json.dumps(cfg))
+        io = cls(str(tmp_path), str(tmp_path))
+        eu, ev = io.read_edge(2, 5)
+        assert eu.tolist() == u[2:5].tolist() and ev.tolist() == v[2:5].tolist()
+    rows = io.read("node_feats_file_bin", 3, 6)
+    assert np.array_equal(rows.numpy(), feat[3:6])
+    assert np.array_equal(io.read_rows("node_feats_file_bin", [1, 7]).numpy(), feat[[1, 7]])
+    assert io.zero("node_feats_file_bin", 5).shape == (5, 4)
+    io.write("node_feats_file_bin", 2, rows)
+    assert np.array_equal(np.fromfile(tmp_path / "p2.nfeat.bin", dtype=np.float32).reshape(-1, 4), feat[3:6])
+    with pytest.raises(TypeError):
+        io.write("train_mask_file_bin", 0, rows)  # float rows for an int8 key
+    assert isinstance(io_dist.get_dataset_io(str(tmp_path), str(tmp_path), "igb260m"), io_dist.Igb260mIO)
+    for total in (0, 1, 9, 10, 11, 1000003):
+        for world in (1, 3, 4, 8):
+            counts = [io_dist.per_rank_local_num(world, r, total) for r in range(world)]
+            stride = io_dist.per_rank_stride(world, 0, total)
+            assert sum(counts) == total and all(c <= stride for c in counts)
+            assert io_dist.per_rank_padding(world, 0, total) % world == 0
+            assert io_dist.per_rank_padding(world, 0, total) >= total
