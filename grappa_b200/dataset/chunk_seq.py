@@ -11,7 +11,6 @@ dgl.metis_partition_assignment with the train mask as a balance type,
 t10n/dataset/chunk_seq.py:47-50) and ``lp`` (label-propagation refinement of the
 hash assignment under a size cap).
 """
-import json
 import os
 import pathlib
 
@@ -64,24 +63,33 @@ def label_propagation(u, v, n, n_part, pid, rounds=4, slack=1.05):
 
 
 def build_chunks_seq(dest_path, dataset_name, src_path, part_method, n_part, seed=0):
-    with open(os.path.join(src_path, "t10n.json")) as f:
-        cfg = json.load(f)
+    """Chunk ``src_path`` (a t10n.json directory) into
+    ``dest_path/chunking_{dataset}_{part_method}_{n_part:03}`` in this process (reference:
+    t10n/dataset/chunk_seq.py:110-150).  Inputs are read through the dataset IO (flat or
+    row-pair edge files, .npy or raw memory-mapped node arrays).  Returns the output
+    directory and the writer's statistics."""
+    from grappa_b200.dataset.io_dist import get_dataset_io
+
     out = os.path.join(dest_path, t10n_chunk_path(dataset_name, part_method, n_part))
     if os.path.exists(out):
         raise FileExistsError(f"please delete {out} first")
+    io = get_dataset_io(src_path, out, dataset_name)
+    cfg = io.ds_cfg
+    n, dim = int(cfg["num_nodes"]), int(cfg["feat_dim"])
     pathlib.Path(out).mkdir(parents=True)
-    edges = np.load(cfg["edge_file_bin"])
-    n, m, dim = int(cfg["num_nodes"]), int(cfg["num_edges"]), int(cfg["feat_dim"])
-    u, v = edges[:m].astype(np.int64), edges[m:].astype(np.int64)
-    train = np.load(cfg["train_mask_file_bin"]).astype(np.int8) if part_method == "metis" else None
-    pid = assign_partitions(u, v, n, n_part, part_method, seed, train_mask=train)
+    u, v = (t.numpy() for t in io.read_edge(0, io.num_edges()))
+    m = int(u.shape[0])
+
+    def node(key):
+        return io.read(key, 0, n).numpy()
+
+    train = node("train_mask_file_bin")
+    pid = assign_partitions(u, v, n, n_part, part_method, seed, train_mask=train if part_method == "metis" else None)
     c = _native.host().c_seq
     stats = c.build(out, n, m, dim, n_part, u, v, pid)
-    c.split_node_feat(out, n, dim, n_part, np.load(cfg["node_feats_file_bin"]).astype(np.float32))
-    c.split_node_data(out, n, n_part, np.load(cfg["node_label_file"]).astype(np.float32),
-                      np.load(cfg["train_mask_file_bin"]).astype(np.int8),
-                      np.load(cfg["val_mask_file_bin"]).astype(np.int8),
-                      np.load(cfg["test_mask_file_bin"]).astype(np.int8))
+    c.split_node_feat(out, n, dim, n_part, node("node_feats_file_bin"))
+    c.split_node_data(out, n, n_part, node("node_label_file"), train, node("val_mask_file_bin"),
+                      node("test_mask_file_bin"))
     return out, stats
 
 

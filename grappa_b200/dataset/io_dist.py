@@ -138,8 +138,8 @@ class DatasetIO:
     """Reader of a pre-partition dataset (``src_path/t10n.json``) and writer of the
     per-partition files under ``dest_path``.
 
-    Node arrays are ``.bin.npy`` files (np.load, memory-mapped) or raw ``mmap.npy``
-    arrays of the key's dtype and the shape t10n.json implies.  The edge file is either
+    Node arrays are ``.npy`` files (np.load, memory-mapped) or raw ``mmap.npy`` arrays
+    (no header) of the key's dtype and the shape t10n.json implies.  The edge file is either
     flat, all sources then all destinations (``edge_layout = "flat"``, the t10n layout),
     or one (u, v) row per edge (``"pairs"``, the IGB release's layout); ``"auto"`` tells
     them apart by the array's shape."""
@@ -185,8 +185,11 @@ class DatasetIO:
         path = self.ds_cfg[key]
         if not os.path.isabs(path) and not os.path.exists(path):
             path = os.path.join(self.src_path, path)
-        if path.endswith("mmap.npy"):
-            a = np.memmap(path, dtype=self.get_npy_dtype(key), mode="r", shape=self.get_npy_shape(key))
+        with open(path, "rb") as f:
+            has_header = f.read(6) == b"\x93NUMPY"
+        if path.endswith("mmap.npy") and not has_header:
+            shape = None if key == "edge_file_bin" else self.get_npy_shape(key)
+            a = np.memmap(path, dtype=self.get_npy_dtype(key), mode="r", shape=shape)
         else:
             a = np.load(path, mmap_mode="r")
         return a
