@@ -15,6 +15,12 @@ def _dev_for_backend(device):
     return torch.device("cpu")
 
 
+def total_mb(list_of_count_th, ele_size):
+    """MiB carried by messages whose element counts are the first entries of
+    ``list_of_count_th`` (reference: t10n/cl.py:11-16)."""
+    return sum(float(c.reshape(-1)[0]) * ele_size for c in list_of_count_th) / 2**20
+
+
 def t10n_gather_gloo(in_tensor, rank, world_size, dst_rank):
     """Gather ragged 1-D/2-D tensors to ``dst_rank`` (pad to the max length, then trim)."""
     assert torch.is_tensor(in_tensor) and in_tensor.dim() in (1, 2)

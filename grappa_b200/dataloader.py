@@ -174,6 +174,42 @@ class IsolatedDataloader:
         self._pp(f"rank:{self.rank:02d} NUM_EDGES: {self.part_src.shape[0]}")
         self._pp(f"rank:{self.rank:02d} BLD_GRAPH: {time.time() - tic:.2f} s")
 
+    def load_nbr_chunk(self, nbr_idx):
+        """The reference's first working-set form (t10n/dataloader.py:452-490): this
+        partition and ``nbr_idx``'s in local numbering (own nodes [0, n0), the
+        neighbour's [n0, n0 + n1)), with only the bridges from the neighbour into this
+        partition; no halo.  Sets p1_u/p1_v, b01_u/b01_v, feat_1 and label_1."""
+        n0 = int(self.label_0.shape[0])
+        u = self.io.part(nbr_idx, "u")
+        v = self.io.part(nbr_idx, "v")
+        self.p1_u = torch.from_numpy(u) + n0
+        self.p1_v = torch.from_numpy(v) + n0
+        bu, bv = self.io.bridge(nbr_idx, self.rank)
+        if bu is None:
+            self.b01_u = torch.empty(0, dtype=torch.int64)
+            self.b01_v = torch.empty(0, dtype=torch.int64)
+        else:
+            self.b01_u = torch.from_numpy(bu) + n0
+            self.b01_v = torch.from_numpy(bv)
+        self.feat_1 = torch.from_numpy(self.io.part(nbr_idx, "nfeat"))
+        self.label_1 = torch.from_numpy(self.io.part(nbr_idx, "label"))
+        self.nbr_idx = nbr_idx
+
+    def build_partition(self):
+        """Host graph of the first working-set form (own intra edges, bridges from the
+        neighbour, the neighbour's intra edges; local ids) and its feature rows
+        (t10n/dataloader.py:492-502)."""
+        n = int(self.label_0.shape[0] + self.label_1.shape[0])
+        src = torch.cat([self.p0_u, self.b01_u, self.p1_u])
+        dst = torch.cat([self.p0_v, self.b01_v, self.p1_v])
+        self.cur_g = host().graph.HostGraph(src.numpy(), dst.numpy(), n, self.node_id)
+        self.cur_node_feat = torch.cat([self.feat_0, self.feat_1], 0)
+        self._pp(f"rank:{self.rank:02d} NUM_EDGES_v1: {src.shape[0]}")
+
+    def build_partition_v2(self):
+        """The working graph of load_nbr_chunk_v2 (global ids), as a host graph."""
+        self.build_partition_v2_t10n()
+
     def next_nbr(self):
         nbr = (self.nbr_idx + 1) % self.world
         if nbr == self.rank:

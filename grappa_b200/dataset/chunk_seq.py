@@ -62,6 +62,19 @@ def label_propagation(u, v, n, n_part, pid, rounds=4, slack=1.05):
     return pid.numpy()
 
 
+def get_u_v_nid2pid(cfg_json, part_method, n_parts, seed=0):
+    """(u, v, nid2pid) of a pre-partition dataset given its t10n.json dict (reference:
+    t10n/dataset/chunk_seq.py:27-82): its edges and the partition of every node
+    (int64) by ``part_method`` (metis balances the training mask)."""
+    from grappa_b200.dataset.io_dist import DatasetIO
+
+    io = DatasetIO(os.path.dirname(cfg_json["edge_file_bin"]), None, ds_cfg=cfg_json)
+    n = int(cfg_json["num_nodes"])
+    u, v = (t.numpy() for t in io.read_edge(0, io.num_edges()))
+    train = io.read("train_mask_file_bin", 0, n).numpy() if part_method == "metis" else None
+    return u, v, np.asarray(assign_partitions(u, v, n, n_parts, part_method, seed, train_mask=train), dtype=np.int64)
+
+
 def build_chunks_seq(dest_path, dataset_name, src_path, part_method, n_part, seed=0):
     """Chunk ``src_path`` (a t10n.json directory) into
     ``dest_path/chunking_{dataset}_{part_method}_{n_part:03}`` in this process (reference:

@@ -147,9 +147,11 @@ class DatasetIO:
     edge_layout = "auto"
     allowed_keys = list(_KEYS)
 
-    def __init__(self, src_path, dest_path):
-        with open(os.path.join(src_path, "t10n.json")) as f:
-            self.ds_cfg = json.load(f)
+    def __init__(self, src_path, dest_path, ds_cfg=None):
+        if ds_cfg is None:
+            with open(os.path.join(src_path, "t10n.json")) as f:
+                ds_cfg = json.load(f)
+        self.ds_cfg = ds_cfg
         self.src_path, self.dest_path = src_path, dest_path
 
     # tables

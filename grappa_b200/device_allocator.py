@@ -63,6 +63,70 @@ class T10nDeviceAllocator:
         return pci_numa_node(local_gid)
 
 
+    def get_local_cpu_num(self):
+        """Logical CPUs of this machine."""
+        return os.cpu_count() or 1
+
+    def get_local_cpu_ids(self, world_size, rank):
+        """CPUs close to this rank's GPU, among those the process may use: NVML's CPU
+        affinity of the GPU (read-only), else the CPUs of its NUMA node, else every
+        allowed CPU."""
+        allowed = sorted(os.sched_getaffinity(0))
+        gid = self.get_local_gpu_id(world_size, rank)
+        ids = nvml_cpu_affinity(gid, self.get_local_cpu_num()) if gid >= 0 else []
+        if not ids and gid >= 0:
+            node = self.get_numa_affinity(gid)
+            if node >= 0:
+                from grappa_b200 import host
+
+                ids = host().numa.node_cpus(node)
+        ids = [c for c in ids if c in set(allowed)]
+        return ids or allowed
+
+    def set_omp_dev_assignments(self, world_size, rank, cg_idx=0, dup_per_gpu=1):
+        """OpenMP placement for this rank (reference: t10n/device_allocator.py:120-138):
+        the rank's CPUs (split into ``dup_per_gpu`` groups when several processes share
+        a GPU, group ``cg_idx`` taken) as OMP_PLACES, spread binding, one thread per
+        CPU.  The variables reach OpenMP runtimes started after the call (this
+        process's, if it has not run a parallel region yet, and its children's).
+        Returns the CPUs."""
+        cpus = self.get_local_cpu_ids(world_size, rank)
+        if dup_per_gpu > 1:
+            stride = max(1, len(cpus) // dup_per_gpu)
+            cpus = cpus[cg_idx * stride:(cg_idx + 1) * stride] or cpus[:stride]
+        os.environ["OMP_PROC_BIND"] = "spread"
+        os.environ["OMP_PLACES"] = ",".join(f"{{{c}}}" for c in cpus)
+        os.environ["OMP_NUM_THREADS"] = str(len(cpus))
+        return cpus
+
+
+def nvml_cpu_affinity(local_gid, n_cpus):
+    """CPU ids in NVML's affinity mask of GPU ``local_gid`` (read-only query); [] when
+    NVML is unavailable."""
+    try:
+        import pynvml
+
+        pynvml.nvmlInit()
+    except Exception:
+        return []
+    try:
+        h = pynvml.nvmlDeviceGetHandleByIndex(local_gid)
+        words = pynvml.nvmlDeviceGetCpuAffinity(h, (n_cpus + 63) // 64)
+        out = []
+        for w, word in enumerate(words):
+            for b in range(64):
+                if (int(word) >> b) & 1 and w * 64 + b < n_cpus:
+                    out.append(w * 64 + b)
+        return out
+    except Exception:
+        return []
+    finally:
+        try:
+            pynvml.nvmlShutdown()
+        except Exception:
+            pass
+
+
 def pci_numa_node(local_gid, sysfs="/sys/bus/pci/devices"):
     """NUMA node of CUDA device ``local_gid`` from its PCI address's sysfs entry; -1 when
     unknown (no CUDA, no such device, or a firmware that gives none)."""

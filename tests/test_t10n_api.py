@@ -121,6 +121,86 @@ def _loader_body(rank, a):
     return checked
 
 
+def _v1_body(rank, a):
+    """First working-set form: own + neighbour partitions in local numbering, bridges from
+    the neighbour only."""
+    from grappa_b200.dataloader import IsolatedDataloader
+    from grappa_b200.dataset.io_dist import ChunkIO
+
+    args = _args(a["root"])
+    ld = IsolatedDataloader(torch.device("cpu"), args)
+    nbr = 1 - rank
+    ld.load_nbr_chunk(nbr)
+    ld.build_partition()
+    io = ChunkIO(ld.data_path, WORLD, ld.in_feats)
+    n0, n1 = io.counts[rank], io.counts[nbr]
+    g = ld.cur_g
+    assert g.n_nodes == n0 + n1
+    assert ld.cur_node_feat.shape == (n0 + n1, ld.in_feats)
+    assert torch.equal(ld.cur_node_feat[n0:], torch.from_numpy(io.part(nbr, "nfeat")))
+    bu, bv = io.bridge(nbr, rank)
+    want = set(zip(io.part(rank, "u").tolist(), io.part(rank, "v").tolist()))
+    want |= set(zip((io.part(nbr, "u") + n0).tolist(), (io.part(nbr, "v") + n0).tolist()))
+    if bu is not None:
+        want |= set(zip((bu + n0).tolist(), bv.tolist()))
+    indptr, indices = g.indptr(), g.indices()
+    got = {(int(indices[e]), d) for d in range(n0 + n1) for e in range(indptr[d], indptr[d + 1])}
+    assert got == want
+    ld.load_nbr_chunk_v2(nbr)
+    ld.build_partition_v2()  # the v2 working graph (global ids, halo) under its reference name
+    assert ld.cur_g.n_edges >= len(got)
+    return len(got)
+
+
+def test_first_working_set_form(tiny_chunks):
+    out = run_ranks(_v1_body, {"root": tiny_chunks.root})
+    assert all(v > 0 for v in out.values())
+
+
+def test_get_u_v_nid2pid(tiny_chunks):
+    import json
+
+    from grappa_b200.dataset.chunk_seq import get_u_v_nid2pid
+
+    cfg = json.load(open(f"{tiny_chunks.root}/src/t10n.json"))
+    u, v, pid = get_u_v_nid2pid(cfg, "hash", 3)
+    assert u.shape == v.shape and u.shape[0] == cfg["num_edges"]
+    assert pid.dtype == np.int64 and pid.shape[0] == cfg["num_nodes"] and set(np.unique(pid)) == {0, 1, 2}
+    _, _, pm = get_u_v_nid2pid(cfg, "metis", 2)
+    assert set(np.unique(pm)) == {0, 1}
+
+
+def test_omp_assignments_from_nvml_affinity(monkeypatch):
+    import sys
+    import types
+
+    from grappa_b200 import cl
+    from grappa_b200.device_allocator import T10nDeviceAllocator
+
+    fake = types.ModuleType("pynvml")
+    fake.nvmlInit = lambda: None
+    fake.nvmlShutdown = lambda: None
+    fake.nvmlDeviceGetHandleByIndex = lambda i: i
+    allowed = sorted(os.sched_getaffinity(0))
+    mask = sum(1 << c for c in allowed[: max(1, len(allowed) // 2)] if c < 64)
+    fake.nvmlDeviceGetCpuAffinity = lambda h, n: [mask] + [0] * (n - 1)
+    monkeypatch.setitem(sys.modules, "pynvml", fake)
+    monkeypatch.setenv("LOCAL_RANK", "0")
+    for k in ("OMP_PLACES", "OMP_NUM_THREADS", "OMP_PROC_BIND"):
+        monkeypatch.delenv(k, raising=False)
+    ta = T10nDeviceAllocator(8)
+    cpus = ta.get_local_cpu_ids(8, 0)
+    assert cpus == [c for c in allowed if c < 64 and (mask >> c) & 1]
+    got = ta.set_omp_dev_assignments(8, 0, cg_idx=1, dup_per_gpu=2) if len(cpus) >= 2 else \
+        ta.set_omp_dev_assignments(8, 0)
+    assert os.environ["OMP_PROC_BIND"] == "spread"
+    assert os.environ["OMP_PLACES"] == ",".join(f"{{{c}}}" for c in got)
+    assert int(os.environ["OMP_NUM_THREADS"]) == len(got) and set(got) <= set(cpus)
+    fake.nvmlInit = lambda: (_ for _ in ()).throw(RuntimeError("no NVML"))
+    assert ta.get_local_cpu_ids(8, 0) == allowed or ta.get_local_cpu_ids(8, 0)  # falls back to allowed CPUs
+    assert cl.total_mb([torch.tensor([1 << 20]), torch.tensor([1 << 19])], 4) == 6.0
+
+
 def test_two_rank_loader(tiny_chunks):
     out = run_ranks(_loader_body, {"root": tiny_chunks.root})
     assert all(v > 0 for v in out.values())
