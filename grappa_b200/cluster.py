@@ -23,6 +23,13 @@ unless given ``--execute``.
     python -m grappa_b200.cluster docker --image grappa_b200:latest --data_path /data \\
         --graphs rmat16k --nproc 8 [--execute]
     python -m grappa_b200.cluster hosts hosts.txt     # parse a hosts file ("host n_gpu=K")
+    python -m grappa_b200.cluster inline --host_file hosts.txt --tag_id probe -- nvidia-smi -L
+
+``inline`` runs one shell command on every host of a hosts file over ssh (the
+reference's ``t10nrun.py --task inline`` / ``--task test``), each host's output in
+``{log_dir}/{tag_id}_{idx}.txt``; ``--time_limit`` ends the ssh sessions it started
+when they run over (the reference's ``--task kill`` matches processes by name on every
+host instead).
 """
 import argparse
 import os
@@ -169,6 +176,14 @@ def main(argv=None):
     dk.add_argument("--execute", action="store_true")
     hs = sub.add_parser("hosts", help="print the (host, n_gpu) pairs of a hosts file")
     hs.add_argument("path")
+    il = sub.add_parser("inline", help="run one shell command on every host of a hosts file over ssh")
+    il.add_argument("--host_file", required=True)
+    il.add_argument("--tag_id", default="inline")
+    il.add_argument("--work_dir", default=".")
+    il.add_argument("--log_dir", default="log")
+    il.add_argument("--time_limit", type=float, default=None, help="seconds")
+    il.add_argument("--dry_run", action="store_true")
+    il.add_argument("command", nargs=argparse.REMAINDER, help="-- then the command")
     args = ap.parse_args(argv)
     if getattr(args, "num_gpus", 0) is None:
         args.num_gpus = args.nproc  # one rank per GPU of the node
@@ -177,6 +192,18 @@ def main(argv=None):
         return 0
     if args.cmd == "docker":
         return 1 if run_docker(args) else 0
+    if args.cmd == "inline":
+        cmd = args.command[1:] if args.command[:1] == ["--"] else args.command
+        if not cmd:
+            ap.error("inline needs a command after --")
+        line = " ".join(shlex.quote(c) for c in cmd) if len(cmd) > 1 else cmd[0]
+        out = util.cluster_run(args.host_file, args.tag_id, lambda hosts, i: line, work_dir=args.work_dir,
+                               log_dir=args.log_dir, time_limit=args.time_limit, dry_run=args.dry_run)
+        if args.dry_run:
+            for argv_ in out:
+                print(" ".join(shlex.quote(a) for a in argv_))
+            return 0
+        return 1 if any(c != 0 for c in out) else 0
     for host, n in parse_hosts_file(args.path):
         print(host, n)
     return 0

@@ -1,5 +1,6 @@
-"""Cluster deployment helpers (CPU): hosts files, the SLURM job-array script of a sweep
-and the container commands; nothing is submitted or run."""
+"""Cluster deployment helpers (CPU): hosts files, the SLURM job-array script of a sweep,
+the container commands and the per-host inline command (through a stand-in ssh that
+runs it locally); nothing is submitted."""
 import os
 
 import pytest
@@ -43,3 +44,24 @@ def test_docker_command_shares_ipc_and_all_gpus(capsys):
     assert cluster.main(["docker", "--image", "img:1", "--data_path", "/data", "--models", "sage,gcn"]) == 0
     lines = capsys.readouterr().out.strip().splitlines()
     assert len(lines) == 2 and all(line.startswith("docker run") for line in lines)
+
+
+def test_inline_command_on_every_host(tmp_path, monkeypatch, capsys):
+    import stat
+
+    hosts = tmp_path / "hosts"
+    hosts.write_text("h1 n_gpu=8\nh2 n_gpu=8\n")
+    assert cluster.main(["inline", "--host_file", str(hosts), "--dry_run", "--", "nvidia-smi", "-L"]) == 0
+    lines = capsys.readouterr().out.strip().splitlines()
+    assert len(lines) == 2 and lines[0].startswith("ssh ") and " h1 " in lines[0] and "nvidia-smi -L" in lines[0]
+    bindir = tmp_path / "bin"
+    bindir.mkdir()
+    fake = bindir / "ssh"  # runs the command here, as if on the host
+    fake.write_text("#!/bin/bash\nwhile [ \"$1\" = -o ]; do shift 2; done\nshift\nexec bash -c \"$1\"\n")
+    fake.chmod(fake.stat().st_mode | stat.S_IEXEC)
+    monkeypatch.setenv("PATH", f"{bindir}:{os.environ['PATH']}")
+    log = tmp_path / "log"
+    assert cluster.main(["inline", "--host_file", str(hosts), "--tag_id", "t", "--log_dir", str(log), "--",
+                         "echo hello"]) == 0
+    assert (log / "t_0.txt").read_text().strip() == "hello" and (log / "t_1.txt").read_text().strip() == "hello"
+    assert cluster.main(["inline", "--host_file", str(hosts), "--log_dir", str(log), "--", "exit 3"]) == 1
