@@ -120,6 +120,35 @@ static void test_xborder() {
   CHECK(xb.resolve(5, &pid, &row) && pid == 0 && row == 5);
 }
 
+static void test_group_by_partition_large() {
+  // many slices (one per thread), ids outside every partition, input order kept per owner
+  const std::vector<int64_t> prefix = {0, 1000, 1001, 50000, 50000, 70000};  // an empty partition too
+  XBorder xb(0, 5, prefix);
+  const int64_t n = 200003;
+  std::vector<int64_t> ids(n);
+  uint64_t x = 12345;
+  for (int64_t i = 0; i < n; ++i) {
+    x = x * 6364136223846793005ull + 1442695040888963407ull;
+    ids[i] = static_cast<int64_t>((x >> 33) % 71000) - 500;  // some below 0, some past the last node
+  }
+  std::vector<int8_t> mask(static_cast<size_t>(5 * n), 7);
+  auto g = xb.group_by_partition(ids.data(), n, mask.data());
+  std::vector<std::vector<int64_t>> want(5);
+  bool mask_ok = true;
+  for (int64_t i = 0; i < n; ++i) {
+    const int64_t p = xb.owner(ids[i]);
+    if (p >= 0) want[p].push_back(ids[i]);
+    for (int64_t q = 0; q < 5; ++q) mask_ok &= mask[static_cast<size_t>(q * n + i)] == (q == p ? 1 : 0);
+  }
+  CHECK(g == want);
+  CHECK(mask_ok);
+  CHECK(g[3].empty());
+  std::vector<int8_t> mask2(static_cast<size_t>(5 * n), 7);
+  xb.mask_by_partition(ids.data(), n, mask2.data());
+  CHECK(mask2 == mask);
+  CHECK(xb.group_by_partition(ids.data(), n, nullptr) == want);
+}
+
 static void test_chunks() {
   char tmpl[] = "/tmp/grappa_chunk_XXXXXX";
   const char* dir = mkdtemp(tmpl);
@@ -358,6 +387,7 @@ int main() {
   test_sample_hop();
   test_random_walk();
   test_xborder();
+  test_group_by_partition_large();
   test_chunks();
   test_multilevel_partition();
   test_pipeline_order_and_depth();

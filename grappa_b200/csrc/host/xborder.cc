@@ -25,42 +25,75 @@ int64_t XBorder::owner(int64_t gid) const {
   return (p < 0 || p >= n_part_) ? -1 : p;
 }
 
+namespace {
+
+int team_size() {
+#ifdef _OPENMP
+  return omp_get_max_threads();
+#else
+  return 1;
+#endif
+}
+
+}  // namespace
+
 void XBorder::mask_by_partition(const int64_t* ids, int64_t n, int8_t* mask) const {
-  std::memset(mask, 0, static_cast<size_t>(n_part_ * n));
 #pragma omp parallel for schedule(static)
   for (int64_t i = 0; i < n; ++i) {
     const int64_t p = owner(ids[i]);
-    if (p >= 0) mask[p * n + i] = 1;
+    for (int64_t q = 0; q < n_part_; ++q) mask[q * n + i] = static_cast<int8_t>(q == p);
   }
 }
 
+// Two passes over contiguous slices, one slice per thread: count each slice's ids per
+// owner (zeroing the slice's mask columns on the way), then write every id straight to
+// its place in its owner's list (slice order = input order) and set its mask entry.
 std::vector<std::vector<int64_t>> XBorder::group_by_partition(const int64_t* ids, int64_t n,
                                                               int8_t* mask) const {
-  if (mask) mask_by_partition(ids, n, mask);
-  std::vector<std::vector<int64_t>> out(n_part_);
-#ifdef _OPENMP
-  const int nt = omp_get_max_threads();
-#else
-  const int nt = 1;
-#endif
-  std::vector<std::vector<std::vector<int64_t>>> local(nt, std::vector<std::vector<int64_t>>(n_part_));
-#pragma omp parallel
-  {
-#ifdef _OPENMP
-    const int t = omp_get_thread_num();
-    const int T = omp_get_num_threads();
-#else
-    const int t = 0, T = 1;
-#endif
-    const int64_t len = (n + T - 1) / T;
-    const int64_t b = std::min(n, t * len), e = std::min(n, b + len);
+  const int nt = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(team_size(), (n + 4095) / 4096)));
+  const int64_t P = n_part_;
+  std::vector<int64_t> cnt(static_cast<size_t>(nt) * P, 0);
+  auto slice = [&](int t, int64_t* b, int64_t* e) {
+    const int64_t len = (n + nt - 1) / nt;
+    *b = std::min(n, t * len);
+    *e = std::min(n, *b + len);
+  };
+#pragma omp parallel for num_threads(nt) schedule(static, 1)
+  for (int t = 0; t < nt; ++t) {
+    int64_t b, e;
+    slice(t, &b, &e);
+    int64_t* c = cnt.data() + static_cast<size_t>(t) * P;
+    if (mask)
+      for (int64_t q = 0; q < P; ++q) std::memset(mask + q * n + b, 0, static_cast<size_t>(e - b));
     for (int64_t i = b; i < e; ++i) {
       const int64_t p = owner(ids[i]);
-      if (p >= 0) local[t][p].push_back(ids[i]);
+      if (p >= 0) ++c[p];
     }
   }
-  for (int64_t p = 0; p < n_part_; ++p)
-    for (int t = 0; t < nt; ++t) out[p].insert(out[p].end(), local[t][p].begin(), local[t][p].end());
+  std::vector<std::vector<int64_t>> out(static_cast<size_t>(P));
+  std::vector<int64_t> pos(static_cast<size_t>(nt) * P, 0);
+  // the lists are sized (and their pages zeroed) by the team, one list per iteration
+#pragma omp parallel for num_threads(nt) schedule(dynamic, 1)
+  for (int64_t q = 0; q < P; ++q) {
+    int64_t total = 0;
+    for (int t = 0; t < nt; ++t) {
+      pos[static_cast<size_t>(t) * P + q] = total;
+      total += cnt[static_cast<size_t>(t) * P + q];
+    }
+    out[static_cast<size_t>(q)].resize(static_cast<size_t>(total));
+  }
+#pragma omp parallel for num_threads(nt) schedule(static, 1)
+  for (int t = 0; t < nt; ++t) {
+    int64_t b, e;
+    slice(t, &b, &e);
+    int64_t* w = pos.data() + static_cast<size_t>(t) * P;
+    for (int64_t i = b; i < e; ++i) {
+      const int64_t p = owner(ids[i]);
+      if (p < 0) continue;
+      out[static_cast<size_t>(p)][static_cast<size_t>(w[p]++)] = ids[i];
+      if (mask) mask[p * n + i] = 1;
+    }
+  }
   return out;
 }
 

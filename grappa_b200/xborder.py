@@ -20,7 +20,7 @@ XBorder = _native.host().xborder.XBorder
 
 
 def xb_mask_by_partition(xb, ids_th, n_part):
-    mask = torch.zeros([n_part, ids_th.shape[0]], dtype=torch.int8)
+    mask = torch.empty([n_part, ids_th.shape[0]], dtype=torch.int8)  # every entry written
     xb.mask_by_partition(ids_th.cpu().numpy(), mask.numpy())
     return mask
 
@@ -31,7 +31,7 @@ def xb_group_by_partition_v1(xb, ids_th, n_part):
 
 
 def xb_group_by_partition(xb, ids_th, n_part):
-    mask = torch.zeros([n_part, ids_th.shape[0]], dtype=torch.int8)
+    mask = torch.empty([n_part, ids_th.shape[0]], dtype=torch.int8)  # every entry written
     groups = xb.group_by_partition(ids_th.cpu().numpy(), mask.numpy())
     return [torch.from_numpy(g) for g in groups], mask
 
