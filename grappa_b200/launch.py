@@ -98,25 +98,39 @@ _INFER = re.compile(r"infer_.*\|test_acc\|([\d.]+)")
 
 
 def result_table(log_dir):
-    """Markdown table (rows model_layers, columns graph) of the last infer_ line's test accuracy."""
-    data = defaultdict(dict)
+    """Markdown table (rows model_layers, columns graph) of the last infer_ line's test
+    accuracy, as the reference's help.py prints it.  When the logs hold several partition
+    methods the rows are split by method (``sage_3 [metis]``), and several runs of one
+    configuration are averaged (``0.6146 (3 runs)``)."""
+    data = defaultdict(lambda: defaultdict(list))
+    parts = set()
     for root, _, files in os.walk(log_dir):
         for fname in files:
             m = _FILE.search(fname)
             if not m:
                 continue
-            _, graph, model, layers = m.groups()
+            part, graph, model, layers = m.groups()
             with open(os.path.join(root, fname)) as f:
                 lines = [l for l in f if "infer_" in l and "test_acc" in l]
             if not lines:
                 continue
             a = _INFER.search(lines[-1])
             if a:
-                data[f"{model}_{layers}"][graph] = float(a.group(1))
+                parts.add(part)
+                data[(model, int(layers), part)][graph].append(float(a.group(1)))
+    split = len(parts) > 1
     graphs = sorted({g for d in data.values() for g in d})
     out = ["| " + " | ".join(["Model_Layer"] + graphs) + " |", "|" + "|".join(["---"] * (len(graphs) + 1)) + "|"]
-    for key in sorted(data, key=lambda k: (k.split("_")[0], int(k.split("_")[1]))):
-        out.append("| " + " | ".join([key] + [str(data[key].get(g, "")) for g in graphs]) + " |")
+
+    def cell(v):
+        if not v:
+            return ""
+        mean = round(sum(v) / len(v), 4)
+        return str(mean) if len(v) == 1 else f"{mean} ({len(v)} runs)"
+
+    for model, layers, part in sorted(data):
+        name = f"{model}_{layers}" + (f" [{part}]" if split else "")
+        out.append("| " + " | ".join([name] + [cell(data[(model, layers, part)].get(g, [])) for g in graphs]) + " |")
     return "\n".join(out)
 
 

@@ -350,3 +350,11 @@ def test_launcher_sweep_and_table(tmp_path):
         "rank0 infer_|epoch|0009|part|0000|val_acc|0.7|test_acc|0.6100|train_acc|0.8\n")
     table = launch.result_table(str(tmp_path))
     assert "| sage_2 | 0.75 |" in table and "| gcn_3 | 0.61 |" in table
+    # a second run is averaged; a second partition method splits the rows
+    (tmp_path / "t10n_hash_rmat16k_sage_2_1_R2_0.txt").write_text(
+        "rank0 infer_|epoch|0009|part|0000|val_acc|0.8|test_acc|0.7700|train_acc|0.9\n")
+    assert "| sage_2 | 0.76 (2 runs) |" in launch.result_table(str(tmp_path))
+    (tmp_path / "t10n_metis_rmat16k_sage_2_1_R1_0.txt").write_text(
+        "rank0 infer_|epoch|0009|part|0000|val_acc|0.8|test_acc|0.8000|train_acc|0.9\n")
+    table = launch.result_table(str(tmp_path))
+    assert "| sage_2 [hash] | 0.76 (2 runs) |" in table and "| sage_2 [metis] | 0.8 |" in table
