@@ -19,6 +19,7 @@ epoch / state_dict / optimizer_state_dict / loss.
 """
 import argparse
 import datetime
+import json
 import os
 import socket
 import time
@@ -34,8 +35,67 @@ from grappa_b200.grad import coverage_all_reduce
 from grappa_b200.models import get_model
 
 
+_METRICS = None  # JSONL sink of the metric lines (--metrics_jsonl)
+
+
+def parse_metrics_line(line):
+    """A ``kind_|key|value|key|value|...`` log line (step_, epoch_, infer_, or the
+    full-graph trainer's per-step ``epoch|...`` line) as a dict with ``event`` and typed
+    values; trailing ``name:value`` fields are kept too.  None for other text."""
+    fields = line.strip().split("|")
+    head = fields[0]
+    if head in ("step_", "epoch_", "infer_"):
+        rec, rest = {"event": head[:-1]}, fields[1:]
+    elif head == "epoch" and len(fields) > 2:
+        rec, rest = {"event": "step"}, fields
+    else:
+        return None
+
+    def value(x):
+        for cast in (int, float):
+            try:
+                return cast(x)
+            except ValueError:
+                pass
+        return x
+
+    i = 0
+    while i < len(rest):
+        tok = rest[i]
+        if ":" in tok:  # a trailing name:value field
+            k, _, v = tok.partition(":")
+            rec[k] = value(v)
+            i += 1
+        elif i + 1 < len(rest):
+            rec[tok] = value(rest[i + 1])
+            i += 2
+        else:
+            i += 1
+    return rec
+
+
+def set_metrics_sink(path):
+    """Append every metric line as one JSON object to ``path`` ({rank} in the path: one
+    file per rank; otherwise rank 0 only).  Each record also holds the rank and the
+    wall-clock time."""
+    global _METRICS
+    rank = dist.get_rank() if dist.is_initialized() else 0
+    if not path or ("{rank}" not in path and rank != 0):
+        _METRICS = None
+        return
+    path = path.format(rank=rank)
+    os.makedirs(os.path.dirname(os.path.abspath(path)), exist_ok=True)
+    _METRICS = open(path, "a")
+
+
 def rank_print(*args, **kwargs):
     rank = dist.get_rank() if dist.is_initialized() else 0
+    if _METRICS is not None and args and isinstance(args[0], str):
+        rec = parse_metrics_line(args[0])
+        if rec is not None:
+            rec.update(rank=rank, time=time.time())
+            _METRICS.write(json.dumps(rec) + "\n")
+            _METRICS.flush()
     if rank % 2 == 0:
         print(f"rank{rank}", *args, **kwargs, flush=True)
 
@@ -226,6 +286,7 @@ def main(args, init_pg=True):
     if init_pg and not args.standalone:
         backend = args.backend if args.num_gpus != -1 else "gloo"
         dist.init_process_group(backend=backend, timeout=datetime.timedelta(seconds=args.pg_timeout))
+    set_metrics_sink(getattr(args, "metrics_jsonl", None))
     if args.num_gpus == -1:
         return run_cpu(args)
     return run_gpu(args)
@@ -262,6 +323,8 @@ def build_parser():
     p.add_argument("--close_dd", action="store_true", help="native sampler (the only sampler of this framework)")
     p.add_argument("--seed", type=int, default=0, help="seed of sampling, shuffling and initialisation")
     p.add_argument("--pg_timeout", type=int, default=600, help="process group timeout in seconds")
+    p.add_argument("--metrics_jsonl", type=str, default=None,
+                   help="also append the step_/epoch_/infer_ lines as JSON objects to this file ({rank}: one per rank)")
     return p
 
 

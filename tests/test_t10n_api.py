@@ -250,7 +250,8 @@ def _cli_body(rank, a):
                 str(WORLD), "--model", a["model"], "--num_hidden", "16", "--num_layers", "2", "--fan_out", "5,5",
                 "--num_epochs", "4", "--batch_size", "256", "--batch_size_eval", "1000", "--lr", "0.01",
                 "--repart_every", "2", "--eval_every", "2", "--log_every", "5", "--tag_id", "test",
-                "--checkpoint_path", a["ckpt"], "--checkpoint_every", "4", "--close_dd"]
+                "--checkpoint_path", a["ckpt"], "--checkpoint_every", "4", "--close_dd",
+                "--metrics_jsonl", os.path.join(a["ckpt"], "metrics_{rank}.jsonl")]
     from grappa_b200.train import t10n_train
 
     return t10n_train.main(t10n_train.parse_args(), init_pg=False)
@@ -270,6 +271,15 @@ def test_cli_trains_on_cpu_ranks(tiny_chunks, tmp_path, model):
     ck = torch.load(os.path.join(str(tmp_path), "epoch_003.pt"), weights_only=False)
     assert set(ck) == {"epoch", "state_dict", "optimizer_state_dict", "loss"}
     assert ck["epoch"] == 3
+    import json
+
+    for rank in range(WORLD):  # the metric lines as JSON, one file per rank
+        recs = [json.loads(l) for l in open(os.path.join(str(tmp_path), f"metrics_{rank}.jsonl"))]
+        epochs = [r for r in recs if r["event"] == "epoch"]
+        assert [r["epoch"] for r in epochs] == [0, 1, 2, 3] and all(r["rank"] == rank for r in recs)
+        assert all(r["epoch_seconds"] > 0 for r in epochs)
+        infer = [r for r in recs if r["event"] == "infer"]
+        assert infer and all(0.0 <= r["test_acc"] <= 1.0 for r in infer)
 
 
 def test_partition_from_chunks_matches_global(tiny_chunks):
@@ -292,16 +302,24 @@ def test_partition_from_chunks_matches_global(tiny_chunks):
 def _full_cli_body(rank, a):
     sys.argv = ["t10n_fullgraph_train", "--data_path", a["root"], "--graph_name", "tiny", "--part_method", "hash",
                 "--n_part", str(WORLD), "--model", "gcn", "--num_hidden", "16", "--num_layers", "2", "--num_epochs",
-                "6", "--lr", "0.02", "--repart_every", "3", "--log_every", "2", "--tag_id", "t", "--dropout", "0.0"]
+                "6", "--lr", "0.02", "--repart_every", "3", "--log_every", "2", "--tag_id", "t", "--dropout", "0.0",
+                "--metrics_jsonl", a["metrics"]]
     from grappa_b200.train import t10n_fullgraph_train as fg
 
     return fg.main(fg.build_parser().parse_args(), init_pg=False)
 
 
-def test_fullgraph_cli_cpu_ranks(tiny_chunks):
-    out = run_ranks(_full_cli_body, {"root": tiny_chunks.root})
+def test_fullgraph_cli_cpu_ranks(tiny_chunks, tmp_path):
+    import json
+
+    path = str(tmp_path / "fg.jsonl")
+    out = run_ranks(_full_cli_body, {"root": tiny_chunks.root, "metrics": path})
     for r in range(WORLD):
         assert out[r]["loss"][-1] < out[r]["loss"][0]
+    recs = [json.loads(l) for l in open(path)]  # no {rank} in the path: rank 0 only
+    assert {r["rank"] for r in recs} == {0}
+    assert [r["epoch"] for r in recs if r["event"] == "epoch"] == list(range(6))
+    assert any(r["event"] == "step" and "loss" in r for r in recs)
 
 
 def test_t10n_alias_and_converters(tmp_path, tiny_chunks):
