@@ -26,6 +26,7 @@ import torch.nn.functional as F
 from grappa_b200.dataset.meta import name_to_meta
 from grappa_b200.grad import coverage_all_reduce
 from grappa_b200.models import get_model
+from grappa_b200.train import resilience
 from grappa_b200.train.t10n_train import build_parser, rank_print, save_to_ckpt, set_metrics_sink
 
 
@@ -142,7 +143,7 @@ def main(args, init_pg=True):
         import datetime
 
         backend = args.backend if args.num_gpus != -1 else "gloo"
-        dist.init_process_group(backend=backend, timeout=datetime.timedelta(seconds=args.pg_timeout))
+        resilience.init_process_group(backend, datetime.timedelta(seconds=args.pg_timeout))
     set_metrics_sink(getattr(args, "metrics_jsonl", None))
     return run_cpu(args) if args.num_gpus == -1 else run_gpu(args)
 

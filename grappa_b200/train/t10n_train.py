@@ -33,6 +33,8 @@ import torch.nn.functional as F
 from grappa_b200.dataset.meta import name_to_meta
 from grappa_b200.grad import coverage_all_reduce
 from grappa_b200.models import get_model
+from grappa_b200.parallel.watchdog import PeerFailure
+from grappa_b200.train import resilience
 
 
 _METRICS = None  # JSONL sink of the metric lines (--metrics_jsonl)
@@ -142,64 +144,82 @@ def run_cpu(args):
     model = get_model(args.model, meta.n_dim, meta.n_label, num_hidden=args.num_hidden, num_layers=args.num_layers,
                       dropout=args.dropout)
     optimizer = torch.optim.Adam(model.parameters(), lr=args.lr)
-    ckpt_epoch = resume_from_ckpt(model, optimizer, args.resume_path)
+    ckpt_epoch = resume_from_ckpt(model, optimizer, resilience.resolve_resume(args))
     loader = IsolatedDataloader(device, args)
     rank = loader.get_rank()
     world = loader.world
+    watchdog = resilience.start_watchdog(args)
     best = {"val_acc": 0.0, "state_dict": None}
     iter_tput, epoch_loss = [], []
     loss = torch.zeros(())
     epoch = ckpt_epoch
+    if ckpt_epoch >= 0:
+        rank_print(f"resumed from epoch {ckpt_epoch}")
     for epoch in range(ckpt_epoch + 1, args.num_epochs):
+        resilience.maybe_inject_fault(args, rank, epoch, watchdog)
+        if watchdog is not None:
+            try:
+                watchdog.check()
+            except PeerFailure as e:
+                resilience.fault_exit(e, rank, epoch)
         tic = time.time()
         t = dict(sample=0.0, fetch=0.0, pcie=0.0, fwd=0.0, bwd=0.0, upd=0.0, acct=0.0)
         n_seed = n_input = 0
         losses = []
         step_time = []
-        dataloader = loader.get_cur_dataloader(args, epoch)
-        start = time.time()
-        for step, (input_nodes, seeds, blocks) in enumerate(dataloader):
-            t0 = time.time()
-            t["sample"] += t0 - start
-            x = torch.zeros([input_nodes.shape[0], loader.in_feats], dtype=torch.float32)
-            loader.get_batch_input(x, input_nodes)
-            coverage = loader.get_coarse_count() if world > 1 else 1.0
-            labels = loader.get_batch_labels(seeds).long()
-            t1 = time.time()
-            t["fetch"] += t1 - t0
-            n_seed += len(seeds)
-            n_input += len(input_nodes)
-            t2 = time.time()
-            pred = model(blocks, x)
-            loss = F.cross_entropy(pred, labels)
-            t3 = time.time()
-            optimizer.zero_grad(set_to_none=True)
-            loss.backward()
-            coverage_all_reduce(list(model.parameters()), coverage, world)
-            t4 = time.time()
-            optimizer.step()
-            t5 = time.time()
-            t["fwd"] += t3 - t2
-            t["bwd"] += t4 - t3
-            t["upd"] += t5 - t4
-            step_time.append(t5 - t0)
-            iter_tput.append(len(seeds) / max(t5 - t0, 1e-9))
-            losses.append(float(loss.detach()))
-            if step % args.log_every == 0:
-                acc = compute_acc(pred.detach(), labels, loader.get_comm_dev())
-                rank_print("step_|epoch|{:04d}|step|{:04d}|part|{:04d}|loss|{:.4f}|train_acc|{:.4f}|sample_p_s|{:.2f}|"
-                           "gpu_mb|{:.1f}|step_time|{:.2f}|train:{:.1f},{:.1f}".format(
-                               epoch, step, rank, float(loss), float(acc[0] / max(acc[1], 1)),
-                               float(np.mean(iter_tput[3:])) if len(iter_tput) > 3 else 0.0, 0.0,
-                               float(np.sum(step_time[-args.log_every:])), float(acc[0]), float(acc[1])))
+        try:
+            dataloader = loader.get_cur_dataloader(args, epoch)
             start = time.time()
-            t["acct"] += start - t5
+            for step, (input_nodes, seeds, blocks) in enumerate(dataloader):
+                t0 = time.time()
+                t["sample"] += t0 - start
+                x = torch.zeros([input_nodes.shape[0], loader.in_feats], dtype=torch.float32)
+                loader.get_batch_input(x, input_nodes)
+                coverage = loader.get_coarse_count() if world > 1 else 1.0
+                labels = loader.get_batch_labels(seeds).long()
+                t1 = time.time()
+                t["fetch"] += t1 - t0
+                n_seed += len(seeds)
+                n_input += len(input_nodes)
+                t2 = time.time()
+                pred = model(blocks, x)
+                loss = F.cross_entropy(pred, labels)
+                t3 = time.time()
+                optimizer.zero_grad(set_to_none=True)
+                loss.backward()
+                coverage_all_reduce(list(model.parameters()), coverage, world)
+                t4 = time.time()
+                optimizer.step()
+                t5 = time.time()
+                t["fwd"] += t3 - t2
+                t["bwd"] += t4 - t3
+                t["upd"] += t5 - t4
+                step_time.append(t5 - t0)
+                iter_tput.append(len(seeds) / max(t5 - t0, 1e-9))
+                losses.append(float(loss.detach()))
+                if step % args.log_every == 0:
+                    acc = compute_acc(pred.detach(), labels, loader.get_comm_dev())
+                    rank_print("step_|epoch|{:04d}|step|{:04d}|part|{:04d}|loss|{:.4f}|train_acc|{:.4f}|sample_p_s|{:.2f}|"
+                               "gpu_mb|{:.1f}|step_time|{:.2f}|train:{:.1f},{:.1f}".format(
+                                   epoch, step, rank, float(loss), float(acc[0] / max(acc[1], 1)),
+                                   float(np.mean(iter_tput[3:])) if len(iter_tput) > 3 else 0.0, 0.0,
+                                   float(np.sum(step_time[-args.log_every:])), float(acc[0]), float(acc[1])))
+                start = time.time()
+                t["acct"] += start - t5
+        except Exception as e:  # a collective that timed out: name the silent peers if the watchdog can
+            if watchdog is not None:
+                try:
+                    watchdog.check()
+                except PeerFailure as pf:
+                    resilience.fault_exit(f"{pf} ({type(e).__name__} in epoch {epoch})", rank, epoch)
+            raise
         toc = time.time()
         epoch_loss.append(float(np.mean(losses)) if losses else 0.0)
         rank_print("epoch_|epoch|{:04d}|part|{:04d}|epoch_seconds|{:.4f}|sampling|{:.4f}|f_fetch|{:.4f}|pcie|{:.4f}|"
                    "forward|{:.4f}|backward|{:.4f}|update|{:.4f}|account|{:.4f}|n_seed|{:012d}|n_input|{:012d}".format(
                        epoch, rank, toc - tic, t["sample"], t["fetch"], t["pcie"], t["fwd"], t["bwd"], t["upd"],
                        t["acct"], n_seed, n_input))
+        resilience.periodic_checkpoint(args, epoch, rank, model, optimizer.state_dict, loss)
         if epoch != 0 and (epoch + 1) % args.eval_every == 0:
             c = run_infer(model, loader, device, args, subset_tag="valid")
             val_acc = float(c[1]) / max(float(c[4]), 1.0)
@@ -208,6 +228,8 @@ def run_cpu(args):
                 best["val_acc"] = val_acc
                 best["state_dict"] = deepcopy(model.state_dict_contiguous())
     summary = {"epochs": epoch + 1, "loss": epoch_loss, "val_acc": 0.0, "test_acc": 0.0, "train_acc": 0.0}
+    if watchdog is not None:
+        watchdog.stop()
     if best["state_dict"] is not None:
         t0 = time.time()
         model.load_state_dict(best["state_dict"])
@@ -236,8 +258,9 @@ def run_gpu(args):
     model = get_model(args.model, meta.n_dim, meta.n_label, num_hidden=args.num_hidden, num_layers=args.num_layers,
                       dropout=args.dropout)
     ckpt = None
-    if args.resume_path:
-        ckpt = torch.load(args.resume_path, weights_only=False)
+    resume = resilience.resolve_resume(args)
+    if resume:
+        ckpt = torch.load(resume, weights_only=False)
         model.load_state_dict(ckpt["state_dict"])
     own = partition_from_chunks(args.data_path, args.graph_name, args.part_method, args.n_part, rank, meta.n_dim,
                                 device)
@@ -249,16 +272,23 @@ def run_gpu(args):
         trainer.engine.load_optimizer_state_dict(ckpt["optimizer_state_dict"])
     first = int(ckpt["epoch"]) + 1 if ckpt is not None else 0
     trainer.warmup()
+    watchdog = resilience.start_watchdog(args)
+    trainer.watchdog = watchdog  # checked by train_epoch before the epoch's first collective
     best = {"val_acc": 0.0, "state_dict": None}
     epoch_loss = []
     epoch = first - 1
     for epoch in range(first, args.num_epochs):
+        resilience.maybe_inject_fault(args, rank, epoch, watchdog)
         tic = time.time()
-        loss = trainer.train_epoch(epoch, host_feed=True)
+        try:
+            loss = trainer.train_epoch(epoch, host_feed=True)
+        except PeerFailure as e:
+            resilience.fault_exit(e, rank, epoch)
         toc = time.time()
         epoch_loss.append(float(loss))
         rank_print("epoch_|epoch|{:04d}|part|{:04d}|epoch_seconds|{:.4f}|loss|{:.4f}|n_seed|{:012d}".format(
             epoch, rank, toc - tic, float(loss), int(trainer.train_ids.numel())))
+        resilience.periodic_checkpoint(args, epoch, rank, model, trainer.engine.optimizer_state_dict, float(loss))
         if epoch != 0 and (epoch + 1) % args.eval_every == 0:
             val_acc = trainer.evaluate_exact([own.val_mask])[0]
             rank_print(f"epoch={epoch}, val_acc={val_acc}")
@@ -266,6 +296,9 @@ def run_gpu(args):
                 best["val_acc"] = val_acc
                 best["state_dict"] = model.state_dict_contiguous()
     summary = {"epochs": epoch + 1, "loss": epoch_loss, "val_acc": 0.0, "test_acc": 0.0, "train_acc": 0.0}
+    if watchdog is not None:
+        watchdog.stop()
+        trainer.watchdog = None
     if best["state_dict"] is not None:
         t0 = time.time()
         trainer.load_state_dict(best["state_dict"])
@@ -285,7 +318,7 @@ def main(args, init_pg=True):
     print(socket.gethostname(), "Initializing", flush=True)
     if init_pg and not args.standalone:
         backend = args.backend if args.num_gpus != -1 else "gloo"
-        dist.init_process_group(backend=backend, timeout=datetime.timedelta(seconds=args.pg_timeout))
+        resilience.init_process_group(backend, datetime.timedelta(seconds=args.pg_timeout))
     set_metrics_sink(getattr(args, "metrics_jsonl", None))
     if args.num_gpus == -1:
         return run_cpu(args)
@@ -323,6 +356,10 @@ def build_parser():
     p.add_argument("--close_dd", action="store_true", help="native sampler (the only sampler of this framework)")
     p.add_argument("--seed", type=int, default=0, help="seed of sampling, shuffling and initialisation")
     p.add_argument("--pg_timeout", type=int, default=600, help="process group timeout in seconds")
+    p.add_argument("--heartbeat_limit", type=float, default=0.0,
+                   help="seconds without a peer's heartbeat before this rank stops with exit code 3 (0: off)")
+    p.add_argument("--inject_fault", type=str, default=None,
+                   help="RANK:EPOCH:{exit,hang} - that rank leaves at the start of that epoch (first attempt only)")
     p.add_argument("--metrics_jsonl", type=str, default=None,
                    help="also append the step_/epoch_/infer_ lines as JSON objects to this file ({rank}: one per rank)")
     return p
