@@ -460,9 +460,17 @@ PYBIND11_MODULE(_C, m) {
                if (ma.size() != x.n_part() * ids.size()) throw std::invalid_argument("mask shape");
                mp = ma.mutable_data();
              }
-             auto g = x.group_by_partition(ids.data(), static_cast<int64_t>(ids.size()), mp);
+             // numpy arrays left uninitialised: the parallel fill pass writes (and first
+             // touches) every entry
+             std::vector<py::array_t<int64_t>> arrs;
+             arrs.reserve(static_cast<size_t>(x.n_part()));
+             x.group_by_partition_into(ids.data(), static_cast<int64_t>(ids.size()), mp,
+                                       [&](int64_t, int64_t count) {
+                                         arrs.emplace_back(static_cast<py::ssize_t>(count));
+                                         return arrs.back().mutable_data();
+                                       });
              py::list out;
-             for (auto& v : g) out.append(to_py(std::move(v)));
+             for (auto& a : arrs) out.append(a);
              return out;
            },
            py::arg("ids"), py::arg("mask") = py::none())

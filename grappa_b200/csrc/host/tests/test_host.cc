@@ -13,6 +13,7 @@
 #include <sys/syscall.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <atomic>
 #include <chrono>
 #include <cstdio>
@@ -147,6 +148,35 @@ static void test_group_by_partition_large() {
   xb.mask_by_partition(ids.data(), n, mask2.data());
   CHECK(mask2 == mask);
   CHECK(xb.group_by_partition(ids.data(), n, nullptr) == want);
+}
+
+static void test_owner_lookup() {
+  // the bucket table, the linear count (table too large) and the binary search (more than
+  // 64 partitions, table too large) against std::upper_bound
+  auto oracle = [](const std::vector<int64_t>& ps, int64_t gid) -> int64_t {
+    if (gid < ps.front() || gid >= ps.back()) return -1;
+    return static_cast<int64_t>(std::upper_bound(ps.begin(), ps.end(), gid) - ps.begin()) - 1;
+  };
+  std::vector<std::vector<int64_t>> cases;
+  cases.push_back({5, 1005, 1005, 1006, 70000, 70000, 90000});   // empty partitions, one of size 1
+  cases.push_back({0, 1, 1000000000, 1000000001, 3000000000});   // size-1 partitions: no table
+  std::vector<int64_t> many = {0};
+  for (int p = 0; p < 100; ++p) many.push_back(many.back() + (p == 50 ? 1 : 40000000));  // > 64 parts
+  cases.push_back(many);
+  uint64_t x = 99;
+  for (const auto& ps : cases) {
+    XBorder xb(0, static_cast<int64_t>(ps.size()) - 1, ps);
+    bool ok = true;
+    for (int i = 0; i < 200000; ++i) {
+      x = x * 6364136223846793005ull + 1442695040888963407ull;
+      const int64_t span = ps.back() - ps.front() + 20;
+      const int64_t gid = ps.front() - 10 + static_cast<int64_t>((x >> 11) % static_cast<uint64_t>(span));
+      ok &= xb.owner(gid) == oracle(ps, gid);
+    }
+    for (int64_t b : ps)
+      for (int64_t d = -1; d <= 1; ++d) ok &= xb.owner(b + d) == oracle(ps, b + d);
+    CHECK(ok);
+  }
 }
 
 static void test_chunks() {
@@ -388,6 +418,7 @@ int main() {
   test_random_walk();
   test_xborder();
   test_group_by_partition_large();
+  test_owner_lookup();
   test_chunks();
   test_multilevel_partition();
   test_pipeline_order_and_depth();

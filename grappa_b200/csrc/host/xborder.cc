@@ -17,12 +17,50 @@ XBorder::XBorder(int64_t rank, int64_t n_part, std::vector<int64_t> prefix_sum)
   if (static_cast<int64_t>(prefix_sum_.size()) != n_part_ + 1)
     throw std::invalid_argument("XBorder: prefix_sum must have n_part + 1 entries");
   gid_lid_.resize(n_part_);
+  // bucket width 2^s <= the smallest non-empty partition: a bucket then holds at most one
+  // start of a non-empty partition, and owner() needs one table read and a compare or two
+  const int64_t range = prefix_sum_[n_part_] - prefix_sum_[0];
+  int64_t min_size = range;
+  for (int64_t p = 0; p < n_part_; ++p) {
+    const int64_t sz = prefix_sum_[p + 1] - prefix_sum_[p];
+    if (sz < 0) throw std::invalid_argument("XBorder: prefix_sum must not decrease");
+    if (sz > 0) min_size = std::min(min_size, sz);
+  }
+  if (range > 0 && n_part_ < (int64_t{1} << 31)) {
+    int s = 0;
+    while ((int64_t{2} << s) <= min_size) ++s;
+    const int64_t buckets = ((range - 1) >> s) + 1;
+    if (buckets <= (int64_t{1} << 22)) {
+      lut_shift_ = s;
+      lut_.resize(static_cast<size_t>(buckets));
+      int64_t p = 0;
+      for (int64_t b = 0; b < buckets; ++b) {
+        const int64_t gid = prefix_sum_[0] + (b << s);
+        while (p + 1 < n_part_ && gid >= prefix_sum_[p + 1]) ++p;
+        lut_[static_cast<size_t>(b)] = static_cast<int32_t>(p);
+      }
+    }
+  }
 }
 
 int64_t XBorder::owner(int64_t gid) const {
+  if (gid < prefix_sum_[0] || gid >= prefix_sum_[n_part_]) return -1;
+  if (!lut_.empty()) {
+    int64_t p = lut_[static_cast<size_t>((gid - prefix_sum_[0]) >> lut_shift_)];
+    while (gid >= prefix_sum_[p + 1]) ++p;  // past the one partition start inside the bucket
+    return p;
+  }
+  if (n_part_ <= 64) {
+    // count the partition starts at or below gid: no branches to mispredict on random
+    // ids (a binary search spent most of its time there); empty partitions are skipped
+    // as upper_bound skips them
+    const int64_t* ps = prefix_sum_.data();
+    int64_t p = 0;
+    for (int64_t q = 1; q < n_part_; ++q) p += gid >= ps[q];
+    return p;
+  }
   auto it = std::upper_bound(prefix_sum_.begin(), prefix_sum_.end(), gid);
-  const int64_t p = static_cast<int64_t>(it - prefix_sum_.begin()) - 1;
-  return (p < 0 || p >= n_part_) ? -1 : p;
+  return static_cast<int64_t>(it - prefix_sum_.begin()) - 1;
 }
 
 namespace {
@@ -46,10 +84,11 @@ void XBorder::mask_by_partition(const int64_t* ids, int64_t n, int8_t* mask) con
 }
 
 // Two passes over contiguous slices, one slice per thread: count each slice's ids per
-// owner (zeroing the slice's mask columns on the way), then write every id straight to
-// its place in its owner's list (slice order = input order) and set its mask entry.
-std::vector<std::vector<int64_t>> XBorder::group_by_partition(const int64_t* ids, int64_t n,
-                                                              int8_t* mask) const {
+// owner (zeroing the slice's mask columns on the way), then, once the caller has given
+// storage for every partition, write every id straight to its place in its owner's list
+// (slice order = input order) and set its mask entry.
+void XBorder::group_by_partition_into(const int64_t* ids, int64_t n, int8_t* mask,
+                                      const std::function<int64_t*(int64_t, int64_t)>& alloc) const {
   const int nt = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(team_size(), (n + 4095) / 4096)));
   const int64_t P = n_part_;
   std::vector<int64_t> cnt(static_cast<size_t>(nt) * P, 0);
@@ -70,17 +109,15 @@ std::vector<std::vector<int64_t>> XBorder::group_by_partition(const int64_t* ids
       if (p >= 0) ++c[p];
     }
   }
-  std::vector<std::vector<int64_t>> out(static_cast<size_t>(P));
+  std::vector<int64_t*> out(static_cast<size_t>(P));
   std::vector<int64_t> pos(static_cast<size_t>(nt) * P, 0);
-  // the lists are sized (and their pages zeroed) by the team, one list per iteration
-#pragma omp parallel for num_threads(nt) schedule(dynamic, 1)
   for (int64_t q = 0; q < P; ++q) {
     int64_t total = 0;
     for (int t = 0; t < nt; ++t) {
       pos[static_cast<size_t>(t) * P + q] = total;
       total += cnt[static_cast<size_t>(t) * P + q];
     }
-    out[static_cast<size_t>(q)].resize(static_cast<size_t>(total));
+    out[static_cast<size_t>(q)] = alloc(q, total);
   }
 #pragma omp parallel for num_threads(nt) schedule(static, 1)
   for (int t = 0; t < nt; ++t) {
@@ -90,10 +127,19 @@ std::vector<std::vector<int64_t>> XBorder::group_by_partition(const int64_t* ids
     for (int64_t i = b; i < e; ++i) {
       const int64_t p = owner(ids[i]);
       if (p < 0) continue;
-      out[static_cast<size_t>(p)][static_cast<size_t>(w[p]++)] = ids[i];
+      out[static_cast<size_t>(p)][w[p]++] = ids[i];
       if (mask) mask[p * n + i] = 1;
     }
   }
+}
+
+std::vector<std::vector<int64_t>> XBorder::group_by_partition(const int64_t* ids, int64_t n,
+                                                              int8_t* mask) const {
+  std::vector<std::vector<int64_t>> out(static_cast<size_t>(n_part_));
+  group_by_partition_into(ids, n, mask, [&](int64_t p, int64_t count) {
+    out[static_cast<size_t>(p)].resize(static_cast<size_t>(count));
+    return out[static_cast<size_t>(p)].data();
+  });
   return out;
 }
 

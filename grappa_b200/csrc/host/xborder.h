@@ -9,6 +9,7 @@
 // global->working id map built at repartition time.
 #pragma once
 #include <cstdint>
+#include <functional>
 #include <unordered_map>
 #include <vector>
 
@@ -20,6 +21,11 @@ class XBorder {
   XBorder(int64_t rank, int64_t n_part, std::vector<int64_t> prefix_sum);
 
   int64_t owner(int64_t gid) const;
+  // ids grouped by owner into storage that alloc(p, count) returns for each partition
+  // (called once per partition, in order, between the counting and the filling pass);
+  // mask (may be null) receives the [n_part, n] 0/1 owner mask
+  void group_by_partition_into(const int64_t* ids, int64_t n, int8_t* mask,
+                               const std::function<int64_t*(int64_t, int64_t)>& alloc) const;
   // ids grouped by owner (in input order) and a [n_part, n] 0/1 mask
   std::vector<std::vector<int64_t>> group_by_partition(const int64_t* ids, int64_t n,
                                                        int8_t* mask) const;
@@ -42,6 +48,11 @@ class XBorder {
   int64_t n_part() const { return n_part_; }
 
  private:
+  // owner lookup: lut_[(gid - prefix_sum_[0]) >> lut_shift_] is the owner of the first id
+  // of that bucket; buckets are no wider than the smallest partition (empty when the
+  // table would be too large; owner() searches then)
+  std::vector<int32_t> lut_;
+  int lut_shift_ = 0;
   int64_t rank_, n_part_, nbr_idx_;
   std::vector<int64_t> prefix_sum_;
   std::vector<std::unordered_map<int64_t, int64_t>> gid_lid_;
