@@ -62,7 +62,6 @@ class T10nDeviceAllocator:
                 return int(tok)
         return pci_numa_node(local_gid)
 
-
     def get_local_cpu_num(self):
         """Logical CPUs of this machine."""
         return os.cpu_count() or 1

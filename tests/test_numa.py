@@ -1,6 +1,7 @@
 """NUMA placement and bandwidth probes of the host engine (grappa_b200._C.numa): node and
 CPU lists, the preferred-node policy scope, the NUMA-placed host graph, the bandwidth
-matrix and its command line; one GPU test of the pinned copy probe."""
+matrix and its command line, the host-path benchmark's lines; one GPU test of the pinned
+copy probe."""
 import json
 
 import numpy as np
@@ -89,3 +90,13 @@ def test_pinned_copy_probe():
     assert buf.is_pinned() and seen in (-1, *N.nodes())
     r = numa_bench.copy_bandwidth(torch.device("cuda", 0), buf, reps=2)
     assert r["h2d_gbs"] > 1.0 and r["d2h_gbs"] > 1.0
+
+
+def test_host_bench_lines(capsys):
+    from grappa_b200.utils import bench_host
+
+    assert bench_host.main(["--graph", "tiny", "--parts", "2", "--only", "csc,sample,metis"]) == 0
+    recs = [json.loads(l) for l in capsys.readouterr().out.strip().splitlines()]
+    assert [r["bench"] for r in recs] == ["HostGraph", "sample_batch", "multilevel_partition"]
+    assert recs[0]["median_s"] > 0 and recs[1]["mean_ms"] > 0
+    assert 0 < recs[2]["edge_cut"] < recs[2]["undirected_edges"] and recs[2]["node_imbalance"] <= 1.05
