@@ -5,10 +5,10 @@
 #endif
 
 #include <algorithm>
+#include <cstdint>
 #include <cmath>
 #include <numeric>
 #include <stdexcept>
-#include <unordered_map>
 
 #include "grappa/rng.h"
 
@@ -84,6 +84,46 @@ void pick_offsets(uint64_t key, uint64_t nid, uint32_t d, uint32_t k, int64_t* o
   }
 }
 
+namespace {
+
+// Global id -> local id during compaction: open addressing with linear probing in a
+// power-of-two table at most half full (std::unordered_map's node allocations made the
+// compaction the larger part of a host sampling step).
+class IdMap {
+ public:
+  static constexpr int64_t kEmpty = INT64_MIN;
+  explicit IdMap(int64_t expected) {
+    size_t cap = 16;
+    while (cap < static_cast<size_t>(2 * expected)) cap <<= 1;
+    keys_.assign(cap, kEmpty);
+    vals_.resize(cap);
+    mask_ = cap - 1;
+  }
+  // the value of key; when absent, key is inserted with value v (first insert wins)
+  int64_t find_or_insert(int64_t key, int64_t v, bool* inserted) {
+    size_t h = static_cast<size_t>(grappa::mix64(static_cast<uint64_t>(key))) & mask_;
+    while (true) {
+      if (keys_[h] == key) {
+        *inserted = false;
+        return vals_[h];
+      }
+      if (keys_[h] == kEmpty) {
+        keys_[h] = key;
+        vals_[h] = v;
+        *inserted = true;
+        return v;
+      }
+      h = (h + 1) & mask_;
+    }
+  }
+
+ private:
+  std::vector<int64_t> keys_, vals_;
+  size_t mask_ = 0;
+};
+
+}  // namespace
+
 Block sample_hop(const CSC& g, const int64_t* dst_nid, const uint8_t* frontier, int64_t n_dst,
                  int64_t fanout, uint64_t key, const int64_t* gideg, double* cov_sum,
                  double* cov_n) {
@@ -125,21 +165,17 @@ Block sample_hop(const CSC& g, const int64_t* dst_nid, const uint8_t* frontier, 
     }
   }
   // compaction: dst nodes first, then new sources by first appearance
-  std::unordered_map<int64_t, int64_t> lid;
-  lid.reserve(static_cast<size_t>((n_dst + n_e) * 1.3) + 16);
+  IdMap lid(n_dst + n_e);
   b.src_nid.assign(dst_nid, dst_nid + n_dst);
-  for (int64_t i = 0; i < n_dst; ++i) lid.emplace(dst_nid[i], i);
+  b.src_nid.reserve(static_cast<size_t>(n_dst + n_e));
+  bool inserted;
+  for (int64_t i = 0; i < n_dst; ++i) lid.find_or_insert(dst_nid[i], i, &inserted);
   b.indices.resize(n_e);
   for (int64_t j = 0; j < n_e; ++j) {
-    auto it = lid.find(nbr[j]);
-    if (it == lid.end()) {
-      const int64_t id = static_cast<int64_t>(b.src_nid.size());
-      lid.emplace(nbr[j], id);
-      b.src_nid.push_back(nbr[j]);
-      b.indices[j] = id;
-    } else {
-      b.indices[j] = it->second;
-    }
+    const int64_t next = static_cast<int64_t>(b.src_nid.size());
+    const int64_t id = lid.find_or_insert(nbr[j], next, &inserted);
+    if (inserted) b.src_nid.push_back(nbr[j]);
+    b.indices[j] = id;
   }
   b.n_src = static_cast<int64_t>(b.src_nid.size());
   b.src_sampled.assign(b.n_src, 0);
@@ -187,25 +223,19 @@ Block random_walk_topk(const CSC& g, const int64_t* seeds, int64_t n_seeds, int 
   b.indptr.assign(n_seeds + 1, 0);
   for (int64_t i = 0; i < n_seeds; ++i) b.indptr[i + 1] = b.indptr[i] + static_cast<int64_t>(top[i].size());
   const int64_t n_e = b.indptr[n_seeds];
-  std::unordered_map<int64_t, int64_t> lid;
-  lid.reserve(static_cast<size_t>((n_seeds + n_e) * 1.3) + 16);
+  IdMap lid(n_seeds + n_e);
   b.src_nid.assign(seeds, seeds + n_seeds);
-  for (int64_t i = 0; i < n_seeds; ++i) lid.emplace(seeds[i], i);
+  bool inserted;
+  for (int64_t i = 0; i < n_seeds; ++i) lid.find_or_insert(seeds[i], i, &inserted);
   b.indices.resize(n_e);
   if (weights) weights->resize(n_e);
   for (int64_t i = 0; i < n_seeds; ++i)
     for (size_t k = 0; k < top[i].size(); ++k) {
       const int64_t e = b.indptr[i] + static_cast<int64_t>(k);
       const int64_t nid = top[i][k].second;
-      auto it = lid.find(nid);
-      if (it == lid.end()) {
-        const int64_t id = static_cast<int64_t>(b.src_nid.size());
-        lid.emplace(nid, id);
-        b.src_nid.push_back(nid);
-        b.indices[e] = id;
-      } else {
-        b.indices[e] = it->second;
-      }
+      const int64_t id = lid.find_or_insert(nid, static_cast<int64_t>(b.src_nid.size()), &inserted);
+      if (inserted) b.src_nid.push_back(nid);
+      b.indices[e] = id;
       if (weights) (*weights)[e] = static_cast<float>(top[i][k].first);
     }
   b.n_src = static_cast<int64_t>(b.src_nid.size());
