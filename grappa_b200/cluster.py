@@ -88,22 +88,46 @@ def slurm_script(n_tasks, sweep_file, *, job_name, gpus, cpus, mem, time_limit, 
 
 
 def write_slurm_job(args):
-    """Write ``{out}/sweep.txt`` (the commands) and ``{out}/{job_name}.sbatch``; returns the
-    script path."""
+    """Write ``{out}/sweep.txt`` (the commands) and ``{out}/{job_name}.sbatch``; with
+    ``--partition`` also ``{out}/partition.sbatch`` (the missing chunk sets, built once on
+    one node before the array runs) and ``{out}/submit.sh``, which submits both with the
+    array waiting for the partition job.  Returns the path to submit."""
     cmds = sweep_commands(args)
     os.makedirs(args.out, exist_ok=True)
+    log_dir = os.path.abspath(args.log_dir)
     sweep_file = os.path.abspath(os.path.join(args.out, "sweep.txt"))
     with open(sweep_file, "w") as f:
         for tag, cmd in cmds:
-            f.write(f"{cmd} > {shlex.quote(os.path.join(os.path.abspath(args.log_dir), tag + '_0.txt'))} 2>&1\n")
+            f.write(f"{cmd} > {shlex.quote(os.path.join(log_dir, tag + '_0.txt'))} 2>&1\n")
     script = slurm_script(len(cmds), sweep_file, job_name=args.job_name, gpus=args.nproc, cpus=args.cpus,
-                          mem=args.mem, time_limit=args.time, log_dir=os.path.abspath(args.log_dir),
-                          partition=args.partition, nodes=args.nodes)
+                          mem=args.mem, time_limit=args.time, log_dir=log_dir, partition=args.partition, nodes=args.nodes)
     path = os.path.join(args.out, f"{args.job_name}.sbatch")
     with open(path, "w") as f:
         f.write(script)
     os.chmod(path, 0o755)
-    return path
+    if not getattr(args, "partition_step", False):
+        return path
+    steps = list(launch.partition_commands(args))
+    lines = ["#!/bin/bash", f"#SBATCH --job-name={args.job_name}_partition", "#SBATCH --nodes=1",
+             "#SBATCH --ntasks-per-node=1", f"#SBATCH --cpus-per-task={args.cpus}", f"#SBATCH --mem={args.mem}",
+             f"#SBATCH --time={args.time}", f"#SBATCH --output={log_dir}/%x_%j.out",
+             f"#SBATCH --error={log_dir}/%x_%j.err"]
+    if args.partition:
+        lines.append(f"#SBATCH --partition={args.partition}")
+    lines += ["", "set -euo pipefail"]
+    lines += [f"{cmd} > {shlex.quote(os.path.join(log_dir, tag + '_0.txt'))} 2>&1" for tag, cmd in steps]
+    part = os.path.join(args.out, "partition.sbatch")
+    with open(part, "w") as f:
+        f.write("\n".join(lines + [""]))
+    os.chmod(part, 0o755)
+    submit = os.path.join(args.out, "submit.sh")
+    with open(submit, "w") as f:
+        f.write("\n".join(["#!/bin/bash", "set -euo pipefail",
+                           f"mkdir -p {shlex.quote(log_dir)}",
+                           f"jid=$(sbatch --parsable {shlex.quote(os.path.abspath(part))})",
+                           f"sbatch --dependency=afterok:$jid {shlex.quote(os.path.abspath(path))}", ""]))
+    os.chmod(submit, 0o755)
+    return submit
 
 
 def docker_command(image, cmd, *, data_path, workspace=None, name=None, shm="64g", gpus="all"):
@@ -168,6 +192,8 @@ def main(argv=None):
     sl.add_argument("--cpus", type=int, default=32)
     sl.add_argument("--mem", default="0")
     sl.add_argument("--time", default="1-00:00:00")
+    sl.add_argument("--partition_step", action="store_true",
+                    help="also write a job that builds the missing chunk sets first, and submit.sh chaining both")
     dk = sub.add_parser("docker", help="print (or run) one container per sweep configuration")
     _sweep_args(dk)
     dk.add_argument("--image", required=True)

@@ -65,3 +65,24 @@ def test_inline_command_on_every_host(tmp_path, monkeypatch, capsys):
                          "echo hello"]) == 0
     assert (log / "t_0.txt").read_text().strip() == "hello" and (log / "t_1.txt").read_text().strip() == "hello"
     assert cluster.main(["inline", "--host_file", str(hosts), "--log_dir", str(log), "--", "exit 3"]) == 1
+
+
+def test_slurm_partition_job_runs_first(tmp_path):
+    data = tmp_path / "data"
+    out = tmp_path / "jobs"
+    import argparse
+
+    path = cluster.write_slurm_job(argparse.Namespace(
+        out=str(out), job_name="sw", partition="gpu", nodes=1, cpus=16, mem="0", time="1:00:00",
+        log_dir=str(tmp_path / "log"), partition_step=True, script="t10n_train", data_path=str(data),
+        parts="hash,metis", graphs="tiny", models="sage", layers_fanouts="2:10,5", runs=1, nproc=2, num_gpus=2,
+        hidden=16, epochs=2, bs=256, eval_bs=1000, eval_every=1, repart=1, log_every=20, tag_prefix="t",
+        port=29600))
+    assert path.endswith("submit.sh") and os.access(path, os.X_OK)
+    submit = open(path).read()
+    assert "jid=$(sbatch --parsable" in submit and "--dependency=afterok:$jid" in submit
+    part = open(out / "partition.sbatch").read()
+    assert part.count("grappa_b200.dataset.partition generate") == 1  # one graph
+    assert part.count("grappa_b200.dataset.partition seq") == 2 and "--part_method metis" in part
+    assert "#SBATCH --partition=gpu" in part and "#SBATCH --gres" not in part
+    assert len(open(out / "sweep.txt").read().strip().splitlines()) == 2
