@@ -145,9 +145,12 @@ def docker_command(image, cmd, *, data_path, workspace=None, name=None, shm="64g
 
 
 def run_docker(args):
-    """Print (or with --execute run, one after another) one container per configuration."""
+    """Print (or with --execute run, one after another) one container per configuration;
+    with ``--partition_step`` the missing chunk sets are built first, one container per
+    step."""
     failed = 0
-    for tag, cmd in sweep_commands(args):
+    steps = list(launch.partition_commands(args)) if getattr(args, "partition_step", False) else []
+    for tag, cmd in steps + sweep_commands(args):
         argv = docker_command(args.image, cmd, data_path=os.path.abspath(args.data_path), workspace=args.workspace,
                               name=f"{args.tag_prefix}_{tag}"[:63], shm=args.shm)
         print(" ".join(shlex.quote(a) for a in argv), flush=True)
@@ -200,6 +203,7 @@ def main(argv=None):
     dk.add_argument("--workspace", default=None)
     dk.add_argument("--shm", default="64g")
     dk.add_argument("--execute", action="store_true")
+    dk.add_argument("--partition_step", action="store_true", help="build the missing chunk sets first")
     hs = sub.add_parser("hosts", help="print the (host, n_gpu) pairs of a hosts file")
     hs.add_argument("path")
     il = sub.add_parser("inline", help="run one shell command on every host of a hosts file over ssh")

@@ -86,3 +86,12 @@ def test_slurm_partition_job_runs_first(tmp_path):
     assert part.count("grappa_b200.dataset.partition seq") == 2 and "--part_method metis" in part
     assert "#SBATCH --partition=gpu" in part and "#SBATCH --gres" not in part
     assert len(open(out / "sweep.txt").read().strip().splitlines()) == 2
+
+
+def test_docker_partition_steps_come_first(tmp_path, capsys):
+    rc = cluster.main(["docker", "--image", "img:1", "--data_path", str(tmp_path / "d"), "--graphs", "tiny",
+                       "--nproc", "2", "--partition_step"])
+    assert rc == 0
+    lines = capsys.readouterr().out.strip().splitlines()
+    assert "dataset.partition generate" in lines[0] and "dataset.partition seq" in lines[1]
+    assert "grappa_b200.train.t10n_train" in lines[2] and all(l.startswith("docker run") for l in lines)
