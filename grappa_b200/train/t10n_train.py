@@ -128,8 +128,11 @@ def save_to_ckpt(args, epoch, rank, model, optimizer_state, loss):
     os.makedirs(args.checkpoint_path, exist_ok=True)
     name = f"{args.checkpoint_path}/epoch_{epoch:03d}.pt"
     state = model.state_dict_contiguous() if hasattr(model, "state_dict_contiguous") else model.state_dict()
+    # written under a temporary name and renamed: a rank stopped mid-save (a restart ends
+    # the attempt's processes) leaves no truncated epoch_NNN.pt for a resume to pick up
     torch.save({"epoch": epoch, "state_dict": state, "optimizer_state_dict": optimizer_state,
-                "loss": float(loss.detach() if torch.is_tensor(loss) else loss)}, name)
+                "loss": float(loss.detach() if torch.is_tensor(loss) else loss)}, name + ".tmp")
+    os.replace(name + ".tmp", name)
     return name
 
 
