@@ -363,11 +363,12 @@ PYBIND11_MODULE(_C, m) {
     return to_py(std::move(keys));
   });
   mg.def("hash_part", [](arr<int64_t> ids, uint64_t seed, int32_t n_part) {
+    if (n_part < 1) throw std::invalid_argument("n_part must be >= 1");
     std::vector<int64_t> out(ids.size());
     for (py::ssize_t i = 0; i < ids.size(); ++i)
       out[i] = grappa::hash_part(static_cast<uint64_t>(ids.data()[i]), seed, n_part);
     return to_py(std::move(out));
-  });
+  }, py::arg("ids"), py::arg("seed"), py::arg("n_part"));
 
   // Dropout keep-mask with the same Philox stream as the GPU kernels: element (r, c)
   // of a row-major buffer with row stride ld is kept iff byte (idx % 16) of the draw of
@@ -570,6 +571,8 @@ PYBIND11_MODULE(_C, m) {
   // node (csrc/python/py_dist_chunking.cc:13-24); the assignment here is a hash
   // of (node id, seed), so every process computes the same owner for a node.
   md.def("random_assign_pid", [](int64_t n, int64_t n_part, uint64_t seed) {
+    if (n_part < 1 || n_part > INT32_MAX) throw std::invalid_argument("n_part must be in [1, 2^31)");
+    if (n < 0) throw std::invalid_argument("n must be >= 0");
     std::vector<int64_t> out(n);
 #pragma omp parallel for
     for (int64_t i = 0; i < n; ++i) out[i] = grappa::hash_part(static_cast<uint64_t>(i), seed, static_cast<int32_t>(n_part));

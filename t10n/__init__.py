@@ -9,7 +9,9 @@ names resolve to the grappa_b200 modules of the same role, imported on first use
   t10n.dataset.{meta, io_dist, chunk_seq, chunk_dist, dgl_to_t10n}
                                                      -> grappa_b200.dataset.<same name>
   t10n.dgl_dsg.{sampler, compliant}                  -> grappa_b200.dgl_dsg
-  t10n._C.{graph, xborder, c_seq, c_dist}            -> grappa_b200._C (C++ host engine)
+  t10n._C.{graph, xborder, c_seq, c_dist}            -> grappa_b200._C (C++ host engine) with the
+                                                        reference's native signatures
+                                                        (grappa_b200.t10n_native)
 """
 import importlib
 import importlib.abc
@@ -48,15 +50,18 @@ class _AliasFinder(importlib.abc.MetaPathFinder, importlib.abc.Loader):
 
     def create_module(self, spec):
         if spec.name == "t10n._C":
-            # the pybind submodules (graph, xborder, c_seq, c_dist) become importable names
+            # the submodules (graph, xborder, c_seq, c_dist) with the reference's native
+            # signatures over the engine's (grappa_b200.t10n_native), importable by name
             import types
+
+            from grappa_b200.t10n_native import build_modules
 
             native = importlib.import_module("grappa_b200._C")
             mod = types.ModuleType("t10n._C", native.__doc__)
             mod.__path__ = []
-            for sub in ("graph", "xborder", "c_seq", "c_dist"):
-                setattr(mod, sub, getattr(native, sub))
-                sys.modules[f"t10n._C.{sub}"] = getattr(native, sub)
+            for sub, m in build_modules("t10n._C").items():
+                setattr(mod, sub, m)
+                sys.modules[f"t10n._C.{sub}"] = m
             sys.modules[spec.name] = mod
             return mod
         mod = importlib.import_module(_ALIASES[spec.name])

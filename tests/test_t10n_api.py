@@ -344,7 +344,7 @@ def test_t10n_alias_and_converters(tmp_path, tiny_chunks):
     assert cfg["num_edges"] == g.u.numel() + g.n_nodes and cfg["num_labels"] == 8
     e = np.load(cfg["edge_file_bin"])
     assert e.shape[0] == 2 * cfg["num_edges"]
-    hg = HostGraph(g.u.numpy(), g.v.numpy(), g.n_nodes)
+    hg = HostGraph(g.u.numpy(), g.v.numpy())  # the reference's signature: (u, v[, numa node])
     s = HostBatchSamplerWithCounter(hg, torch.arange(100), [3, 3], batch_size=50, target_nodes_gideg=torch.ones(100,
                                     dtype=torch.int64))
     n = sum(1 for _ in s)
