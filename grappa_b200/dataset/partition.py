@@ -41,7 +41,8 @@ def generate(graph_name, out):
 
 def chunk_info(path):
     """Per-partition counts of a chunk directory: nodes, intra edges (self-loops
-    included), outgoing and incoming bridge edges, training / validation / test nodes."""
+    included), outgoing and incoming bridge edges, distinct remote sources of the incoming
+    bridges (halo), training / validation / test nodes."""
     parts = sorted(int(m.group(1)) for f in glob.glob(os.path.join(path, "p*.oid.bin"))
                    if (m := re.search(r"p(\d+)\.oid\.bin$", f)))
     if not parts or parts != list(range(len(parts))):
@@ -56,12 +57,22 @@ def chunk_info(path):
         f = os.path.join(path, name)
         return int(np.fromfile(f, dtype=np.int8).astype(np.int64).sum()) if os.path.exists(f) else 0
 
+    def halo(i):
+        # distinct nodes of other partitions with an edge into partition i: the rows a
+        # working set holding partition i must fetch from elsewhere
+        n = 0
+        for j in range(k):
+            f = os.path.join(path, f"b{j}_{i}.u.bin")
+            if j != i and os.path.exists(f):
+                n += int(np.unique(np.fromfile(f, dtype=np.int64)).shape[0])
+        return n
+
     rows = []
     for i in range(k):
         out_b = sum(n64(f"b{i}_{j}.u.bin") for j in range(k) if j != i)
         in_b = sum(n64(f"b{j}_{i}.u.bin") for j in range(k) if j != i)
         rows.append({"part": i, "nodes": n64(f"p{i}.oid.bin"), "intra_edges": n64(f"p{i}.u.bin"),
-                     "bridge_out": out_b, "bridge_in": in_b, "train": n_set(f"p{i}.train.bin"),
+                     "bridge_out": out_b, "bridge_in": in_b, "halo_in": halo(i), "train": n_set(f"p{i}.train.bin"),
                      "valid": n_set(f"p{i}.valid.bin"), "test": n_set(f"p{i}.test.bin")})
     total_intra = sum(r["intra_edges"] - r["nodes"] for r in rows)  # without the self-loops
     total_bridge = sum(r["bridge_out"] for r in rows)
@@ -74,7 +85,7 @@ def chunk_info(path):
 
 
 def _table(summary, rows):
-    cols = ["part", "nodes", "intra_edges", "bridge_out", "bridge_in", "train", "valid", "test"]
+    cols = ["part", "nodes", "intra_edges", "bridge_out", "bridge_in", "halo_in", "train", "valid", "test"]
     out = ["| " + " | ".join(cols) + " |", "|" + "|".join(["---:"] * len(cols)) + "|"]
     out += ["| " + " | ".join(str(r[c]) for c in cols) + " |" for r in rows]
     out.append("")

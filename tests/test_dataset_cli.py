@@ -64,6 +64,12 @@ def test_seq_chunks_hold_the_graph(src, method, capsys):
     assert summary["n_part"] == 4 and summary["nodes"] == cfg["num_nodes"]
     assert summary["edges"] == len(pairs)
     assert sum(r["train"] for r in rows) == cfg["num_train_nodes"]
+    for r in rows:  # the halo: distinct sources of the edges that enter the partition from others
+        i = r["part"]
+        oid = [np.fromfile(pfile(path, j, "oid"), dtype=np.int64) for j in range(4)]
+        mine = set(oid[i].tolist())
+        want = {int(a) for a, b in pairs if int(b) in mine and int(a) not in mine}
+        assert r["halo_in"] == len(want)
     assert np.array_equal(_edges(path, 4), pairs)
     oid = np.concatenate([np.fromfile(pfile(path, i, "oid"), dtype=np.int64) for i in range(4)])
     assert np.array_equal(np.sort(oid), np.arange(cfg["num_nodes"]))
