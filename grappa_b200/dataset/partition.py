@@ -108,6 +108,7 @@ def main(argv=None):
         if name == "seq":
             p.add_argument("--part_method", default="hash", choices=["hash", "random", "metis", "lp"])
             p.add_argument("--n_part", type=int, required=True)
+            p.add_argument("--verbose", action="store_true", help="per-phase seconds of the metis partitioner")
         else:
             p.add_argument("--part_method", default="hash", choices=["hash", "random"])
             p.add_argument("--n_part", type=int, default=None, help="a multiple of the ranks (default: the ranks)")
@@ -124,6 +125,9 @@ def main(argv=None):
         return 0
     if a.cmd == "seq":
         from grappa_b200.dataset.chunk_seq import build_chunks_seq
+
+        if a.verbose:
+            os.environ["GRAPPA_MLPART_VERBOSE"] = "1"  # read by the partitioner at each call
 
         out, _ = build_chunks_seq(a.dest_path, a.graph_name, a.src_path, a.part_method, a.n_part, a.seed)
         print(_table(*chunk_info(out)))
